@@ -1,0 +1,385 @@
+"""decisive_b200: B200 (sm_100a) backend for decisive's quantised projection path.
+
+Two layers, both thin over the C ABI of libdecisive_b200.so (include/decisive_b200.h):
+
+* kernel level -- torch-tensor wrappers of the group-64 quantiser, weight packer, grouped GEMM
+  (tensor-core and GEMV paths), fused MLP, attention and dequantisation.  torch supplies device
+  memory and streams only; every computation runs in this library's CUDA kernels.
+* model level -- ``Model`` / ``Cache`` / ``Cancellation`` / ``Error`` mirroring the reference's
+  ``inference`` module (src/inference/mod.rs:17-273): ``predict`` and ``predict_batch`` with the
+  same error codes, cache ownership and cancellation rules.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import json
+from dataclasses import dataclass, field
+
+from . import _lib
+from ._lib import CudaError, check, load
+
+GROUP = 64
+CODES_NATURAL, CODES_GEMV, CODES_TC = 0, 1, 2
+DTYPES = {"float32": 0, "float16": 1, "bfloat16": 2}
+
+
+def _ptr(t):
+    return C.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def _stream(stream=None):
+    import torch
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return C.c_void_p(s.cuda_stream)
+
+
+def padded(k: int) -> int:
+    return (k + GROUP - 1) // GROUP * GROUP
+
+
+# ------------------------------------------------------------------ kernel level
+def quantize_activations(x, bits: int = 8, layout: int = CODES_TC, sums: bool = False, nonfinite=None):
+    """int8::Matrix::prepare (int8.rs:178-202) on the GPU -> (codes, scales [G, M], sums [G, M] | None)."""
+    import torch
+    assert x.is_cuda and x.dim() == 2
+    M, K = x.shape
+    Kp = padded(K)
+    G = Kp // GROUP
+    dt = torch.float16 if layout == CODES_TC else torch.int8
+    codes = torch.zeros((M, Kp), dtype=dt, device=x.device)
+    scales = torch.zeros((G, max(M, 1)), dtype=torch.float32, device=x.device)
+    s = torch.zeros((G, max(M, 1)), dtype=torch.int32, device=x.device) if sums else None
+    check(load().db_quantize_activations_g64(_ptr(x), DTYPES[str(x.dtype).split(".")[1]], x.stride(0), M, K, bits,
+                                             _ptr(codes), layout, Kp, _ptr(scales), _ptr(s), max(M, 1),
+                                             _ptr(nonfinite), _stream()))
+    return codes, scales, s
+
+
+def pack_weights(bf16, bits: int = 4):
+    """Absmax group-64 weight quantiser (int8.rs:51-152, packed.rs:31-56): bf16 [N, K] (as int16/uint16
+    bits or torch.bfloat16) -> (codes, scales [G, N])."""
+    import torch
+    N, K = bf16.shape
+    Kp = padded(K)
+    codes = torch.empty((N, Kp * bits // 8), dtype=torch.uint8, device=bf16.device)
+    scales = torch.empty((Kp // GROUP, N), dtype=torch.float32, device=bf16.device)
+    check(load().db_pack_weights_g64(_ptr(bf16), N, K, bits, _ptr(codes), _ptr(scales), _stream()))
+    return codes, scales
+
+
+def import_packed(packed, N: int, K: int, bits: int):
+    import torch
+    codes = torch.empty((N, K * bits // 8), dtype=torch.uint8, device=packed.device)
+    scales = torch.empty((K // GROUP, N), dtype=torch.float32, device=packed.device)
+    check(load().db_import_packed(_ptr(packed), N, K, bits, _ptr(codes), _ptr(scales), _stream()))
+    return codes, scales
+
+
+def export_packed(codes, scales, N: int, K: int, bits: int):
+    import torch
+    out = torch.empty(N * (K // GROUP) * (GROUP * bits // 8 + 4), dtype=torch.uint8, device=codes.device)
+    check(load().db_export_packed(_ptr(codes), _ptr(scales), N, K, bits, _ptr(out), _stream()))
+    return out
+
+
+def dequant_rows(codes, scales, N: int, K: int, bits: int, ids=None):
+    import torch
+    T = N if ids is None else ids.numel()
+    out = torch.empty((T, K), dtype=torch.float32, device=codes.device)
+    check(load().db_dequant_rows_g64(_ptr(codes), _ptr(scales), N, K, bits, _ptr(ids), T, _ptr(out), K, _stream()))
+    return out
+
+
+def gemm(a_codes, layout, sa, w_codes, sw, M, N, K, bits, fused=True, a_sums=None, residual=None, nonfinite=None):
+    """Matrix::apply_prepared (int8.rs:229-288) on prepared activations -> y f32 [M, N]."""
+    import torch
+    y = residual if residual is not None else torch.empty((M, N), dtype=torch.float32, device=w_codes.device)
+    check(load().db_gemm_g64(_ptr(a_codes), layout, a_codes.stride(0), _ptr(sa), _ptr(a_sums), sa.stride(0),
+                             _ptr(w_codes), _ptr(sw), M, N, K, bits, int(fused), int(residual is not None), _ptr(y),
+                             N, _ptr(nonfinite), _stream()))
+    return y
+
+
+def linear(x, w_codes, sw, N: int, weight_bits: int = 4, activation_bits: int = 8, fused: bool = True):
+    """Matrix::apply (int8.rs:166-176): quantise + grouped GEMM (GEMV path for small M)."""
+    import torch
+    M, K = x.shape
+    ws = torch.empty(load().db_linear_workspace_bytes(M, K), dtype=torch.uint8, device=x.device)
+    y = torch.empty((M, N), dtype=torch.float32, device=x.device)
+    check(load().db_linear_g64(_ptr(x), M, K, _ptr(w_codes), _ptr(sw), N, weight_bits, activation_bits, int(fused),
+                               _ptr(y), _ptr(ws), _stream()))
+    return y
+
+
+def project_packed(x, w_codes, sw, outputs: int, bits: int):
+    """packed::project (packed.rs:75-119) for one activation row."""
+    import torch
+    K = x.numel()
+    ws = torch.empty(load().db_linear_workspace_bytes(1, K), dtype=torch.uint8, device=x.device)
+    y = torch.empty(outputs, dtype=torch.float32, device=x.device)
+    check(load().db_project_packed(_ptr(x), K, _ptr(w_codes), _ptr(sw), outputs, bits, _ptr(y), _ptr(ws), _stream()))
+    return y
+
+
+def interleave_gate_up(gate_codes, gate_scales, up_codes, up_scales, F: int, K: int, bits: int):
+    import torch
+    codes = torch.empty((2 * F, gate_codes.shape[1]), dtype=torch.uint8, device=gate_codes.device)
+    scales = torch.empty((gate_scales.shape[0], 2 * F), dtype=torch.float32, device=gate_codes.device)
+    check(load().db_interleave_gate_up(_ptr(gate_codes), _ptr(gate_scales), _ptr(up_codes), _ptr(up_scales), F, K,
+                                       bits, _ptr(codes), _ptr(scales), _stream()))
+    return codes, scales
+
+
+def mlp(a_codes, sa, gu_codes, gu_scales, M: int, F: int, K: int, bits: int, fused: bool = True, nonfinite=None):
+    """Fused gate/up + SiLU*up + re-quantisation (grouped_q4_mlp.wgsl) -> (codes TC [M, F], scales [F/64, M])."""
+    import torch
+    codes = torch.zeros((M, F), dtype=torch.float16, device=a_codes.device)
+    scales = torch.zeros((F // GROUP, M), dtype=torch.float32, device=a_codes.device)
+    check(load().db_mlp_g64(_ptr(a_codes), a_codes.stride(0), _ptr(sa), sa.stride(0), _ptr(gu_codes), _ptr(gu_scales),
+                            M, F, K, bits, int(fused), _ptr(codes), F, _ptr(scales), M, _ptr(nonfinite), _stream()))
+    return codes, scales
+
+
+def attention(q16, k16, v16, q_heads: int, kv_heads: int, scale: float | None = None):
+    import torch
+    T = q16.shape[0]
+    out = torch.empty((T, q_heads * 128), dtype=torch.float32, device=q16.device)
+    s = (1.0 / 128 ** 0.5) if scale is None else scale
+    check(load().db_attention(_ptr(q16), _ptr(k16), _ptr(v16), T, q_heads, kv_heads, 128, s, _ptr(out),
+                              q_heads * 128, _stream()))
+    return out
+
+
+def synthetic_bf16(seed: int, tensor: int, shape, std: float, device="cuda"):
+    import torch
+    out = torch.empty(shape, dtype=torch.int16, device=device)
+    check(load().db_synthetic_bf16(seed, tensor, out.numel(), std, _ptr(out), _stream()))
+    return out
+
+
+def device_error_word() -> int:
+    return int(load().db_device_error_word())
+
+
+# ------------------------------------------------------------------ model level (inference API mirror)
+class Error(Exception):
+    """inference::Error {code, message} (src/inference/mod.rs:44-85)."""
+
+    def __init__(self, code: str, message: str):
+        super().__init__(f"{code}: {message}")
+        self.code, self.message = code, message
+
+    @staticmethod
+    def _from(e: _lib.DbError) -> "Error":
+        return Error(e.code.decode(), e.message.decode())
+
+
+class Cancellation:
+    """inference::Cancellation (mod.rs:87-100): a shared flag the library polls."""
+
+    def __init__(self):
+        self._flag = C.c_int32(0)
+
+    def cancel(self):
+        self._flag.value = 1
+
+    def check(self):
+        if self._flag.value:
+            raise Error("CANCELLED", "Inference was cancelled")
+
+    @property
+    def ptr(self):
+        return C.byref(self._flag)
+
+
+@dataclass
+class CacheOptions:
+    """inference::CacheOptions (mod.rs:102-115)."""
+    max_bytes: int = 64 * 1024 * 1024
+    require_prefix: bool = False
+
+
+@dataclass
+class PplxParameters:
+    """inference::PplxParameters (parameters.rs:81-103)."""
+    max_sequence_tokens: int = 1024
+
+
+@dataclass
+class EncoderConfig:
+    layers: int = 28
+    hidden: int = 1024
+    q_heads: int = 16
+    kv_heads: int = 8
+    head_dim: int = 128
+    ffn: int = 3072
+    vocab: int = 151936
+    weight_bits: int = 4
+    rope_theta: float = 1e6
+    eps: float = 1e-6
+    max_sequence_tokens: int = 1024
+    fused: bool = True
+
+    def c(self) -> _lib.EncoderConfig:
+        return _lib.EncoderConfig(self.layers, self.hidden, self.q_heads, self.kv_heads, self.head_dim, self.ffn,
+                                  self.vocab, self.weight_bits, self.rope_theta, self.eps, self.max_sequence_tokens,
+                                  int(self.fused))
+
+
+@dataclass
+class Response:
+    """inference::Response (mod.rs:127-132); `response` is the pooled embedding."""
+    response: object
+    model: str
+    backend: str
+
+
+@dataclass
+class Outcome:
+    """inference::Outcome (mod.rs:133-138)."""
+    status: str
+    result: Response | None = None
+    error: Error | None = None
+
+
+class Cache:
+    def __init__(self, handle, model):
+        self._h, self._model = handle, model
+
+    def __del__(self):
+        if getattr(self, "_h", None):
+            load().db_cache_destroy(self._h)
+            self._h = None
+
+
+class Model:
+    """inference::Model<B> (mod.rs:156-273) over the CUDA encoder backend."""
+
+    def __init__(self, handle, config: EncoderConfig):
+        self._h, self.config = handle, config
+        self.defaults = PplxParameters(config.max_sequence_tokens)
+
+    @classmethod
+    def synthetic(cls, config: EncoderConfig, seed: int = 0, std: float = 0.02, device: int = 0) -> "Model":
+        err = _lib.DbError()
+        cfg = config.c()
+        h = load().db_model_create_synthetic(device, C.byref(cfg), seed, std, C.byref(err))
+        if not h:
+            raise Error._from(err)
+        return cls(h, config)
+
+    @classmethod
+    def from_weights(cls, config: EncoderConfig, weights: dict, device: int = 0) -> "Model":
+        """weights: 'embedding' bf16 bits [vocab, hidden]; per-layer lists 'q','k','v','o','gate','up','down'
+        (bf16 bits [out, in]); per-layer f32 'input_norm','post_norm','q_norm','k_norm'; 'final_norm'."""
+        import numpy as np
+        keep = []
+
+        def arr(a, dt):
+            a = np.ascontiguousarray(a, dtype=dt)
+            keep.append(a)
+            return a.ctypes.data_as(C.POINTER(C.c_uint16 if dt == np.uint16 else C.c_float))
+
+        w = _lib.EncoderWeights()
+        w.embedding = arr(weights["embedding"], np.uint16)
+        L = config.layers
+        for n in ("q", "k", "v", "o", "gate", "up", "down"):
+            p = (C.POINTER(C.c_uint16) * L)(*[arr(t, np.uint16) for t in weights[n]])
+            keep.append(p)
+            setattr(w, n, C.cast(p, _lib._u16pp))
+        for n in ("input_norm", "post_norm", "q_norm", "k_norm"):
+            p = (C.POINTER(C.c_float) * L)(*[arr(t, np.float32) for t in weights[n]])
+            keep.append(p)
+            setattr(w, n, C.cast(p, _lib._fpp))
+        w.final_norm = arr(weights["final_norm"], np.float32)
+        err = _lib.DbError()
+        cfg = config.c()
+        h = load().db_model_create(device, C.byref(cfg), C.byref(w), C.byref(err))
+        if not h:
+            raise Error._from(err)
+        return cls(h, config)
+
+    def close(self):
+        if getattr(self, "_h", None):
+            load().db_model_destroy(self._h)
+            self._h = None
+
+    __del__ = close
+
+    def capabilities(self) -> dict:
+        buf = C.create_string_buffer(512)
+        check(load().db_model_capabilities(self._h, buf, 512))
+        return json.loads(buf.value.decode())
+
+    def synthetic_weight(self, name: str, layer: int = 0):
+        import numpy as np
+        n = load().db_model_synthetic_weight(self._h, name.encode(), layer, None, 0)
+        if n < 0:
+            raise CudaError(int(n))
+        out = np.empty(n, dtype=np.uint16)
+        got = load().db_model_synthetic_weight(self._h, name.encode(), layer, out.ctypes.data_as(C.c_void_p), n)
+        if got != n:
+            raise CudaError(int(got))
+        return out
+
+    def create_cache(self, options: CacheOptions | None = None) -> Cache:
+        o = options or CacheOptions()
+        err = _lib.DbError()
+        h = load().db_cache_create(self._h, o.max_bytes, int(o.require_prefix), C.byref(err))
+        if not h:
+            raise Error._from(err)
+        return Cache(h, self)
+
+    def clear_cache(self, cache: Cache):
+        err = _lib.DbError()
+        if load().db_cache_clear(self._h, cache._h, C.byref(err)):
+            raise Error._from(err)
+
+    def _params(self, parameters):
+        p = parameters or self.defaults
+        return _lib.Parameters(p.max_sequence_tokens)
+
+    def predict(self, ids, parameters: PplxParameters | None = None, cache: Cache | None = None,
+                cancellation: Cancellation | None = None, out=None) -> Response:
+        import numpy as np
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        out = np.empty(self.config.hidden, dtype=np.float32) if out is None else out
+        err = _lib.DbError()
+        p = self._params(parameters)
+        rc = load().db_predict(self._h, ids.ctypes.data_as(C.c_void_p), ids.size, C.byref(p),
+                               cache._h if cache else None, cancellation.ptr if cancellation else None,
+                               out.ctypes.data_as(C.c_void_p), C.byref(err))
+        if rc:
+            raise Error._from(err)
+        caps = self.capabilities()
+        return Response(out, caps["model"], caps["backend"])
+
+    def predict_batch(self, requests, parameters: PplxParameters | None = None, cache: Cache | None = None,
+                      cancellation: Cancellation | None = None) -> list[Outcome]:
+        import numpy as np
+        reqs = [np.ascontiguousarray(r, dtype=np.int32) for r in requests]
+        n = len(reqs)
+        ptrs = (C.c_void_p * max(n, 1))(*[r.ctypes.data_as(C.c_void_p).value for r in reqs])
+        lens = (C.c_size_t * max(n, 1))(*[r.size for r in reqs])
+        outs = np.zeros((max(n, 1), self.config.hidden), dtype=np.float32)
+        status = np.zeros(max(n, 1), dtype=np.int32)
+        errs = (_lib.DbError * max(n, 1))()
+        err = _lib.DbError()
+        p = self._params(parameters)
+        rc = load().db_predict_batch(self._h, ptrs, lens, n, C.byref(p), cache._h if cache else None,
+                                     cancellation.ptr if cancellation else None, outs.ctypes.data_as(C.c_void_p),
+                                     status.ctypes.data_as(C.c_void_p), errs, C.byref(err))
+        if rc:
+            raise Error._from(err)
+        caps = self.capabilities()
+        result = []
+        for i in range(n):
+            if status[i] == 0:
+                result.append(Outcome("success", result=Response(outs[i].copy(), caps["model"], caps["backend"])))
+            else:
+                result.append(Outcome("error", error=Error._from(errs[i])))
+        return result
+
+    def forward_device(self, ids_dev, out_dev, stream=None):
+        """Device-resident forward (no host synchronisation) used for device-timed measurement."""
+        check(load().db_forward_device(self._h, _ptr(ids_dev), ids_dev.numel(), _ptr(out_dev), _stream(stream)))

@@ -1,0 +1,212 @@
+// Non-causal GQA attention, head_dim 128, f16 operands with f32 accumulation and an online
+// softmax (the reference computes scale * q.k, softmax, then P.v per head in f32:
+// backbone.rs:560-600).  One CTA = 64 queries of one head, 4 warps x 16 query rows; K/V tiles
+// of 64 keys double-buffered in 128B-swizzled shared memory via cp.async.
+#include "common.cuh"
+#include "layer_ops.h"
+
+namespace db {
+
+constexpr int ATT_BQ = 64, ATT_BKV = 64, ATT_D = 128;
+constexpr int ATT_THREADS = 128;
+constexpr int ATT_TILE_BYTES = ATT_BKV * ATT_D * 2;  // 16 KB
+
+// byte offset of (row, 16-byte chunk) in a [64][128] f16 tile, chunk XOR-swizzled by row
+__device__ __forceinline__ uint32_t tile_off(int row, int chunk) {
+    return (uint32_t)(row * 256 + ((chunk ^ (row & 7)) << 4));
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, int src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// rows [t0, t0+64) of head h of a [T, H, 128] f16 tensor -> swizzled tile (rows >= T zero-filled)
+__device__ __forceinline__ void load_tile(uint32_t dst, const __half* base, int T, int H, int h, int t0, int tid) {
+#pragma unroll
+    for (int i = 0; i < (ATT_BKV * 16) / ATT_THREADS; ++i) {
+        const int idx = tid + i * ATT_THREADS;
+        const int row = idx >> 4, chunk = idx & 15;
+        const int t = t0 + row;
+        const __half* src = base + ((size_t)(t < T ? t : T - 1) * H + h) * ATT_D + chunk * 8;
+        cp_async16(dst + tile_off(row, chunk), src, t < T ? 16 : 0);
+    }
+}
+
+__global__ void __launch_bounds__(ATT_THREADS)
+    attention_kernel(const __half* __restrict__ q16, const __half* __restrict__ k16, const __half* __restrict__ v16,
+                     int T, int Hq, int Hk, float scale_log2, float* __restrict__ out, int64_t ldo) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const uint32_t sQ = smem_u32(smem);
+    const uint32_t sK[2] = {sQ + ATT_TILE_BYTES, sQ + 2 * ATT_TILE_BYTES};
+    const uint32_t sV[2] = {sQ + 3 * ATT_TILE_BYTES, sQ + 4 * ATT_TILE_BYTES};
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int h = blockIdx.y, kh = h / (Hq / Hk);
+    const int q0 = blockIdx.x * ATT_BQ;
+    const int tiles = (T + ATT_BKV - 1) / ATT_BKV;
+
+    load_tile(sQ, q16, T, Hq, h, q0, tid);
+    load_tile(sK[0], k16, T, Hk, kh, 0, tid);
+    load_tile(sV[0], v16, T, Hk, kh, 0, tid);
+    cp_async_commit();
+
+    uint32_t qf[8][4];
+    float o[16][4];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+    float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
+
+    for (int j = 0; j < tiles; ++j) {
+        if (j + 1 < tiles) {
+            load_tile(sK[(j + 1) & 1], k16, T, Hk, kh, (j + 1) * ATT_BKV, tid);
+            load_tile(sV[(j + 1) & 1], v16, T, Hk, kh, (j + 1) * ATT_BKV, tid);
+        }
+        cp_async_commit();
+        cp_async_wait<1>();
+        __syncthreads();
+        if (j == 0) {
+#pragma unroll
+            for (int s = 0; s < 8; ++s) {
+                const int row = warp * 16 + (lane & 15), chunk = 2 * s + (lane >> 4);
+                ldsm_x4(sQ + tile_off(row, chunk), qf[s][0], qf[s][1], qf[s][2], qf[s][3]);
+            }
+        }
+        const uint32_t kb = sK[j & 1], vb = sV[j & 1];
+        // S = Q K^T : 16 x 64 per warp
+        float sc[8][4];
+#pragma unroll
+        for (int n = 0; n < 8; ++n) sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.f;
+#pragma unroll
+        for (int s = 0; s < 8; ++s) {
+#pragma unroll
+            for (int n = 0; n < 8; n += 2) {
+                const int row = n * 8 + (lane & 7) + ((lane >> 4) << 3);
+                const int chunk = 2 * s + ((lane >> 3) & 1);
+                uint32_t b0, b1, b2, b3;
+                ldsm_x4(kb + tile_off(row, chunk), b0, b1, b2, b3);
+                mma16816(sc[n], qf[s], b0, b1);
+                mma16816(sc[n + 1], qf[s], b2, b3);
+            }
+        }
+        // mask keys beyond T, scale into the log2 domain
+        const int kv0 = j * ATT_BKV;
+        float mx[2] = {mrow[0], mrow[1]};
+#pragma unroll
+        for (int n = 0; n < 8; ++n) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int key = kv0 + n * 8 + 2 * (lane & 3) + (e & 1);
+                float v = key < T ? sc[n][e] * scale_log2 : -INFINITY;
+                sc[n][e] = v;
+                mx[e >> 1] = fmaxf(mx[e >> 1], v);
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+            mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+        }
+        float corr[2], rs[2] = {0.f, 0.f};
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            corr[r] = mrow[r] == -INFINITY ? 0.f : exp2f(mrow[r] - mx[r]);
+            mrow[r] = mx[r];
+        }
+#pragma unroll
+        for (int n = 0; n < 8; ++n) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float p = exp2f(sc[n][e] - mrow[e >> 1]);
+                sc[n][e] = p;
+                rs[e >> 1] += p;
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 1);
+            rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 2);
+            lrow[r] = lrow[r] * corr[r] + rs[r];
+        }
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            o[i][0] *= corr[0]; o[i][1] *= corr[0];
+            o[i][2] *= corr[1]; o[i][3] *= corr[1];
+        }
+        // O += P V
+#pragma unroll
+        for (int s = 0; s < 4; ++s) {
+            uint32_t pa[4];
+            pa[0] = pack_h2(sc[2 * s][0], sc[2 * s][1]);
+            pa[1] = pack_h2(sc[2 * s][2], sc[2 * s][3]);
+            pa[2] = pack_h2(sc[2 * s + 1][0], sc[2 * s + 1][1]);
+            pa[3] = pack_h2(sc[2 * s + 1][2], sc[2 * s + 1][3]);
+#pragma unroll
+            for (int n = 0; n < 16; n += 2) {
+                const int row = s * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
+                const int chunk = n + (lane >> 4);
+                uint32_t b0, b1, b2, b3;
+                ldsm_x4_t(vb + tile_off(row, chunk), b0, b1, b2, b3);
+                mma16816(o[n], pa, b0, b1);
+                mma16816(o[n + 1], pa, b2, b3);
+            }
+        }
+        __syncthreads();
+    }
+    // normalise and store
+    const float inv0 = 1.f / lrow[0], inv1 = 1.f / lrow[1];
+    const int r0 = q0 + warp * 16 + (lane >> 2);
+#pragma unroll
+    for (int n = 0; n < 16; ++n) {
+        const int d = n * 8 + 2 * (lane & 3);
+        if (r0 < T)
+            *reinterpret_cast<float2*>(out + (size_t)r0 * ldo + h * ATT_D + d) = make_float2(o[n][0] * inv0, o[n][1] * inv0);
+        if (r0 + 8 < T)
+            *reinterpret_cast<float2*>(out + (size_t)(r0 + 8) * ldo + h * ATT_D + d) =
+                make_float2(o[n][2] * inv1, o[n][3] * inv1);
+    }
+}
+
+}  // namespace db
+
+using namespace db;
+
+int db_launch_attention(const __half* q16, const __half* k16, const __half* v16, int T, int Hq, int Hk, float scale,
+                        float* out, int64_t ldo, cudaStream_t stream) {
+    if (T <= 0) return 0;
+    if (Hk <= 0 || Hq % Hk) return (int)cudaErrorInvalidValue;
+    const int smem = 5 * ATT_TILE_BYTES;
+    static bool configured = false;
+    if (!configured) {
+        cudaError_t e = cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return (int)e;
+        configured = true;
+    }
+    dim3 grid((T + ATT_BQ - 1) / ATT_BQ, Hq);
+    attention_kernel<<<grid, ATT_THREADS, smem, stream>>>(q16, k16, v16, T, Hq, Hk, scale * 1.4426950408889634f, out,
+                                                          ldo);
+    return (int)cudaGetLastError();
+}

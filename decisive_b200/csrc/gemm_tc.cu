@@ -1,0 +1,480 @@
+// Tensor-core grouped W4A8 / W8A8 GEMM with fused group dequantisation (sm_100a, tcgen05).
+//
+// Computes, for every output (m, n), the reference's grouped sum (int8.rs:526-585):
+//     acc = 0; for g ascending: acc = fma(float(dot_g), sw[n,g] * sa[m,g], acc)
+// where dot_g is the exact integer dot of 64 activation codes with 64 weight codes.
+//
+// The integer dots come from tcgen05.mma kind::f16 on integer-valued f16 operands: every code
+// is exact in f16, every product and every partial sum of one group (|sum| <= 64*127*127 < 2^24)
+// is an exact f32 integer, so the tensor core returns dot_g exactly.  Each 64-wide group is one
+// K-block; its dot lands in its own TMEM buffer (double buffered) and the epilogue warps fold it
+// into their register accumulators with the reference's rounding, in group order.
+//
+// Roles (448 threads, one CTA per SM, persistent over 128 x BN output tiles):
+//   warp 0      TMA producer: activation-code tiles (128 x 64 f16, 128B swizzle) and raw weight
+//               code tiles (BN rows x 32|64 bytes) into smem rings
+//   warp 1      TMEM owner + MMA issuer (one elected lane): 4 x (128 x BN x 16) MMAs per group
+//   warps 2-5   converters: weight nibbles/bytes -> f16 codes in the UMMA K-major SW128 layout
+//   warps 6-13  epilogue: TMEM -> registers, per-group scale fold, final store / fused SwiGLU
+//               re-quantisation (grouped_q4_mlp.wgsl:83-105 semantics)
+// Every mbarrier wait is bounded (DB_WAIT_LIMIT_NS); on expiry the CTA records an error in the
+// device error word, stops issuing work, and releases its tensor memory.
+#include <float.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace db {
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int A_STAGES = 4;
+constexpr int W_STAGES = 4;
+constexpr int B_STAGES = 3;
+constexpr int NUM_THREADS = 448;
+constexpr int CONVERTER_WARP0 = 2;
+constexpr int EPILOGUE_WARP0 = 6;
+constexpr int XCH_STRIDE = 65;  // floats per row of the SwiGLU exchange buffer (bank-conflict free)
+
+template <int BN, int BITS, int EPI>
+struct GemmSmem {
+    static constexpr int A_BYTES = BM * BK * 2;          // 16 KB
+    static constexpr int B_BYTES = BN * BK * 2;          // f16 codes
+    static constexpr int W_ROW = BK * BITS / 8;          // 32 or 64 bytes of raw codes per row
+    static constexpr int W_BYTES = BN * W_ROW;
+    static constexpr int XCH_BYTES = EPI == DB_EPI_SWIGLU_QUANT ? BM * XCH_STRIDE * 4 : 0;
+    static constexpr int OFF_A = 0;
+    static constexpr int OFF_B = OFF_A + A_STAGES * A_BYTES;
+    static constexpr int OFF_W = OFF_B + B_STAGES * B_BYTES;
+    static constexpr int OFF_X = OFF_W + W_STAGES * W_BYTES;
+    static constexpr int OFF_BAR = (OFF_X + XCH_BYTES + 15) / 16 * 16;
+    static constexpr int NUM_BARS = 2 * A_STAGES + 2 * W_STAGES + 2 * B_STAGES + 6;
+    static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
+    static constexpr int BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
+};
+
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err,
+                                          int code) {
+    bool ok = mbar_wait(bar, parity, abort_flag, err, code);
+    return __all_sync(0xffffffffu, ok);
+}
+
+// 8 weight nibbles (bytes of one row, k = 8c..8c+7) -> 8 f16 codes in the order 0,4,1,5,2,6,3,7.
+__device__ __forceinline__ uint4 nibbles_to_f16(uint32_t w) {
+    const uint32_t magic = 0x64006400u;
+    uint32_t t0 = (w & 0x000F000Fu) | magic;         // 1024+u(k0), 1024+u(k4)
+    uint32_t t1 = (w & 0x00F000F0u) | magic;         // 1024+16u(k1), 1024+16u(k5)
+    uint32_t w8 = w >> 8;
+    uint32_t t2 = (w8 & 0x000F000Fu) | magic;        // k2, k6
+    uint32_t t3 = (w8 & 0x00F000F0u) | magic;        // k3, k7
+    const __half2 bias = __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x6408));   // 1032
+    const __half2 sixteenth = __halves2half2(__ushort_as_half(0x2C00), __ushort_as_half(0x2C00));  // 1/16
+    const __half2 m72 = __halves2half2(__ushort_as_half(0xD480), __ushort_as_half(0xD480));        // -72
+    __half2 o0 = __hsub2(*reinterpret_cast<__half2*>(&t0), bias);
+    __half2 o1 = __hfma2(*reinterpret_cast<__half2*>(&t1), sixteenth, m72);
+    __half2 o2 = __hsub2(*reinterpret_cast<__half2*>(&t2), bias);
+    __half2 o3 = __hfma2(*reinterpret_cast<__half2*>(&t3), sixteenth, m72);
+    uint4 r;
+    r.x = *reinterpret_cast<uint32_t*>(&o0);
+    r.y = *reinterpret_cast<uint32_t*>(&o1);
+    r.z = *reinterpret_cast<uint32_t*>(&o2);
+    r.w = *reinterpret_cast<uint32_t*>(&o3);
+    return r;
+}
+
+// 8 int8 weight codes (k = 8c..8c+3 in w0, 8c+4..8c+7 in w1) -> f16 codes in order 0,4,1,5,2,6,3,7.
+__device__ __forceinline__ uint4 bytes_to_f16(uint32_t w0, uint32_t w1) {
+    uint32_t x0 = w0 ^ 0x80808080u, x1 = w1 ^ 0x80808080u;  // code + 128, unsigned
+    uint32_t p = __byte_perm(x0, x1, 0x5140);              // k0 k4 k1 k5
+    uint32_t q = __byte_perm(x0, x1, 0x7362);              // k2 k6 k3 k7
+    const uint32_t hi = 0x64646464u;
+    uint32_t t0 = __byte_perm(p, hi, 0x4140), t1 = __byte_perm(p, hi, 0x4342);
+    uint32_t t2 = __byte_perm(q, hi, 0x4140), t3 = __byte_perm(q, hi, 0x4342);
+    const __half2 bias = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));  // 1152
+    __half2 o0 = __hsub2(*reinterpret_cast<__half2*>(&t0), bias);
+    __half2 o1 = __hsub2(*reinterpret_cast<__half2*>(&t1), bias);
+    __half2 o2 = __hsub2(*reinterpret_cast<__half2*>(&t2), bias);
+    __half2 o3 = __hsub2(*reinterpret_cast<__half2*>(&t3), bias);
+    uint4 r;
+    r.x = *reinterpret_cast<uint32_t*>(&o0);
+    r.y = *reinterpret_cast<uint32_t*>(&o1);
+    r.z = *reinterpret_cast<uint32_t*>(&o2);
+    r.w = *reinterpret_cast<uint32_t*>(&o3);
+    return r;
+}
+
+__device__ __forceinline__ float silu_ref(float x) {
+    // cpu.rs:513-518: x * (1 / (1 + exp(-x)))
+    return __fmul_rn(x, __fdiv_rn(1.f, __fadd_rn(1.f, expf(-x))));
+}
+
+template <int BN, int BITS, int EPI, bool FUSED>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
+                   const float* __restrict__ sa, int64_t ldsa, const float* __restrict__ sw, int M, int N, int G,
+                   float* __restrict__ y, int64_t ldy, __half* __restrict__ out_codes, int64_t ldoc,
+                   float* __restrict__ out_scales, int64_t ldos, const int* __restrict__ nonfinite,
+                   int* __restrict__ dev_error) {
+    using S = GemmSmem<BN, BITS, EPI>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::OFF_BAR);
+    uint64_t* a_full = bars;
+    uint64_t* a_empty = a_full + A_STAGES;
+    uint64_t* w_full = a_empty + A_STAGES;
+    uint64_t* w_empty = w_full + W_STAGES;
+    uint64_t* b_full = w_empty + W_STAGES;
+    uint64_t* b_empty = b_full + B_STAGES;
+    uint64_t* acc_full = b_empty + B_STAGES;
+    uint64_t* acc_empty = acc_full + 2;
+    uint64_t* xch_full = acc_empty + 2;   // SwiGLU exchange: up half -> gate half
+    uint64_t* xch_empty = xch_full + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::OFF_MISC);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + S::OFF_MISC + 4);
+
+    const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+    const int m_tiles = (M + BM - 1) / BM, n_tiles = (N + BN - 1) / BN;
+    const int tiles = m_tiles * n_tiles;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < A_STAGES; ++i) { mbar_init(&a_full[i], 1); mbar_init(&a_empty[i], 1); }
+        for (int i = 0; i < W_STAGES; ++i) { mbar_init(&w_full[i], 1); mbar_init(&w_empty[i], 4); }
+        for (int i = 0; i < B_STAGES; ++i) { mbar_init(&b_full[i], 4); mbar_init(&b_empty[i], 1); }
+        for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], 8); }
+        mbar_init(xch_full, 4);
+        mbar_init(xch_empty, 4);
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmW);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, 2 * BN);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------------------------------------------------------- TMA producer
+        if (lane == 0) {
+            int ia = 0, iw = 0;
+            uint32_t pa = 0, pw = 0;
+            for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+                const int m0 = (tile % m_tiles) * BM, n0 = (tile / m_tiles) * BN;
+                for (int g = 0; g < G; ++g) {
+                    if (!mbar_wait(&a_empty[ia], pa ^ 1u, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_TMA)) goto done;
+                    mbar_arrive_expect_tx(&a_full[ia], S::A_BYTES);
+                    tma_load_2d(smem + S::OFF_A + ia * S::A_BYTES, &tmA, &a_full[ia], g * BK, m0);
+                    if (++ia == A_STAGES) { ia = 0; pa ^= 1u; }
+                    if (!mbar_wait(&w_empty[iw], pw ^ 1u, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_TMA)) goto done;
+                    mbar_arrive_expect_tx(&w_full[iw], S::W_BYTES);
+                    tma_load_2d(smem + S::OFF_W + iw * S::W_BYTES, &tmW, &w_full[iw], g * S::W_ROW, n0);
+                    if (++iw == W_STAGES) { iw = 0; pw ^= 1u; }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------------------------------------------------------- MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t IDESC = idesc_f16_f32(BM, BN);
+            int ia = 0, ib = 0, ic = 0;
+            uint32_t pa = 0, pb = 0, pc = 0;
+            const uint32_t a_base = smem_u32(smem + S::OFF_A), b_base = smem_u32(smem + S::OFF_B);
+            for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+                for (int g = 0; g < G; ++g) {
+                    if (!mbar_wait(&a_full[ia], pa, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_MMA)) goto done;
+                    if (!mbar_wait(&b_full[ib], pb, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_MMA)) goto done;
+                    if (!mbar_wait(&acc_empty[ic], pc ^ 1u, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_MMA)) goto done;
+                    tc_fence_after();
+                    const uint32_t d = tmem_base + (uint32_t)(ic * BN);
+                    const uint32_t a_addr = a_base + ia * S::A_BYTES, b_addr = b_base + ib * S::B_BYTES;
+#pragma unroll
+                    for (int kk = 0; kk < BK / 16; ++kk)
+                        umma_f16(d, sw128_desc(a_addr + kk * 32), sw128_desc(b_addr + kk * 32), IDESC, kk > 0);
+                    umma_commit(&a_empty[ia]);
+                    umma_commit(&b_empty[ib]);
+                    umma_commit(&acc_full[ic]);
+                    if (++ia == A_STAGES) { ia = 0; pa ^= 1u; }
+                    if (++ib == B_STAGES) { ib = 0; pb ^= 1u; }
+                    if (++ic == 2) { ic = 0; pc ^= 1u; }
+                }
+            }
+        }
+    } else if (warp < EPILOGUE_WARP0) {
+        // ---------------------------------------------------------------- converters
+        const int ct = threadIdx.x - CONVERTER_WARP0 * 32;  // 0..127
+        int iw = 0, ib = 0;
+        uint32_t pw = 0, pb = 0;
+        for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+            for (int g = 0; g < G; ++g) {
+                if (!warp_wait(&w_full[iw], pw, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_CVT)) goto done;
+                if (!warp_wait(&b_empty[ib], pb ^ 1u, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_CVT)) goto done;
+                const uint8_t* wsrc = smem + S::OFF_W + iw * S::W_BYTES;
+                uint8_t* bdst = smem + S::OFF_B + ib * S::B_BYTES;
+                for (int r = ct; r < BN; r += 128) {
+                    const uint4* src = reinterpret_cast<const uint4*>(wsrc + r * S::W_ROW);
+                    uint8_t* row = bdst + r * 128;
+                    const int sw = r & 7;
+                    if (BITS == 4) {
+                        uint4 v0 = src[0], v1 = src[1];
+                        uint32_t words[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+                        for (int c = 0; c < 8; ++c)
+                            *reinterpret_cast<uint4*>(row + ((c ^ sw) << 4)) = nibbles_to_f16(words[c]);
+                    } else {
+#pragma unroll
+                        for (int h = 0; h < 4; ++h) {
+                            uint4 v = src[h];
+                            *reinterpret_cast<uint4*>(row + (((2 * h) ^ sw) << 4)) = bytes_to_f16(v.x, v.y);
+                            *reinterpret_cast<uint4*>(row + (((2 * h + 1) ^ sw) << 4)) = bytes_to_f16(v.z, v.w);
+                        }
+                    }
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&b_full[ib]);
+                    mbar_arrive(&w_empty[iw]);
+                }
+                if (++iw == W_STAGES) { iw = 0; pw ^= 1u; }
+                if (++ib == B_STAGES) { ib = 0; pb ^= 1u; }
+            }
+        }
+    } else {
+        // ---------------------------------------------------------------- epilogue
+        constexpr int COLS = BN / 2;  // columns per thread
+        constexpr int CHUNKS = COLS / 32;
+        const int q = warp & 3;                        // TMEM lane quadrant this warp may access
+        const int half = (warp - EPILOGUE_WARP0) >> 2;  // which half of the tile's columns
+        const int r = q * 32 + lane;                   // row inside the tile
+        const int col0 = half * COLS;
+        const bool any_nonfinite = nonfinite != nullptr && *nonfinite != 0;
+        float* xch = reinterpret_cast<float*>(smem + S::OFF_X);
+        int ic = 0;
+        uint32_t pc = 0, px = 0;
+        for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+            const int m0 = (tile % m_tiles) * BM, n0 = (tile / m_tiles) * BN;
+            const int m = m0 + r;
+            const bool full_cols = (n0 + BN <= N) && ((N & 3) == 0);
+            float acc[COLS];
+#pragma unroll
+            for (int j = 0; j < COLS; ++j) acc[j] = 0.f;
+            for (int g = 0; g < G; ++g) {
+                if (!warp_wait(&acc_full[ic], pc, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_EPI)) goto done;
+                tc_fence_after();
+                const float s_a = m < M ? __ldg(sa + (size_t)g * ldsa + m) : 0.f;
+                const float* swp = sw + (size_t)g * N + n0 + col0;
+#pragma unroll
+                for (int c = 0; c < CHUNKS; ++c) {
+                    uint32_t v[32];
+                    tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ic * BN + col0 + c * 32), v);
+                    float swv[32];
+                    if (full_cols) {
+#pragma unroll
+                        for (int j = 0; j < 32; j += 4) {
+                            float4 t = __ldg(reinterpret_cast<const float4*>(swp + c * 32 + j));
+                            swv[j] = t.x; swv[j + 1] = t.y; swv[j + 2] = t.z; swv[j + 3] = t.w;
+                        }
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            swv[j] = (n0 + col0 + c * 32 + j < N) ? __ldg(swp + c * 32 + j) : 0.f;
+                    }
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const float d = __uint_as_float(v[j]);
+                        if (FUSED) acc[c * 32 + j] = __fmaf_rn(d, __fmul_rn(swv[j], s_a), acc[c * 32 + j]);
+                        else acc[c * 32 + j] = __fadd_rn(acc[c * 32 + j], __fmul_rn(d, __fmul_rn(s_a, swv[j])));
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&acc_empty[ic]);
+                if (++ic == 2) { ic = 0; pc ^= 1u; }
+            }
+            if (EPI == DB_EPI_SWIGLU_QUANT) {
+                // half 1 holds the up projection of the same 64 features: hand it to half 0.
+                if (half == 1) {
+                    if (!warp_wait(xch_empty, px ^ 1u, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_EPI)) goto done;
+#pragma unroll
+                    for (int j = 0; j < COLS; ++j) xch[r * XCH_STRIDE + j] = acc[j];
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(xch_full);
+                } else {
+                    if (!warp_wait(xch_full, px, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_EPI)) goto done;
+                    if (m < M) {
+                        float h[COLS];
+                        float amax = 0.f;
+#pragma unroll
+                        for (int j = 0; j < COLS; ++j) {
+                            h[j] = __fmul_rn(silu_ref(acc[j]), xch[r * XCH_STRIDE + j]);
+                            amax = fmaxf(amax, fabsf(h[j]));
+                        }
+                        const float scale = fmaxf(__fdiv_rn(amax, 127.f), FLT_MIN);
+                        const float inv = __fdiv_rn(1.f, scale);
+                        const int f0 = (n0 / BN) * 64;  // first output feature of this tile
+                        __half* dst = out_codes + (size_t)m * ldoc + f0;
+#pragma unroll
+                        for (int b = 0; b < COLS; b += 8) {
+                            const int order[8] = {0, 4, 1, 5, 2, 6, 3, 7};
+                            __half hv[8];
+#pragma unroll
+                            for (int p = 0; p < 8; ++p)
+                                hv[p] = __float2half_rn(
+                                    fminf(fmaxf(rintf(__fmul_rn(h[b + order[p]], inv)), -127.f), 127.f));
+                            *reinterpret_cast<uint4*>(dst + b) = *reinterpret_cast<uint4*>(hv);
+                        }
+                        out_scales[(size_t)(n0 / BN) * ldos + m] = scale;
+                    }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(xch_empty);
+                }
+                px ^= 1u;
+            } else if (m < M) {
+                float* dst = y + (size_t)m * ldy + n0 + col0;
+                const float nanv = __int_as_float(0x7fc00000);
+                if (full_cols && (ldy & 3) == 0) {
+#pragma unroll
+                    for (int j = 0; j < COLS; j += 4) {
+                        float4 o = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+                        if (EPI == DB_EPI_RESIDUAL) {
+                            float4 rr = *reinterpret_cast<const float4*>(dst + j);
+                            o.x = __fadd_rn(rr.x, o.x); o.y = __fadd_rn(rr.y, o.y);
+                            o.z = __fadd_rn(rr.z, o.z); o.w = __fadd_rn(rr.w, o.w);
+                        }
+                        if (any_nonfinite) o = make_float4(nanv, nanv, nanv, nanv);
+                        *reinterpret_cast<float4*>(dst + j) = o;
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < COLS; ++j) {
+                        if (n0 + col0 + j < N) {
+                            float o = acc[j];
+                            if (EPI == DB_EPI_RESIDUAL) o = __fadd_rn(dst[j], o);
+                            dst[j] = any_nonfinite ? nanv : o;
+                        }
+                    }
+                }
+            }
+        }
+    }
+done:
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, 2 * BN);
+    }
+}
+
+}  // namespace db
+
+using namespace db;
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        cudaDriverEntryPointQueryResult q;
+        void* p = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+int db_num_sms() {
+    static int sms = 0;
+    if (!sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (sms <= 0) sms = 148;
+    }
+    return sms;
+}
+
+template <int BN, int BITS, int EPI, bool FUSED>
+static int launch_variant(const DbGemmArgs& a, const CUtensorMap& tmA, const CUtensorMap& tmW, int G,
+                          cudaStream_t stream) {
+    using S = GemmSmem<BN, BITS, EPI>;
+    auto kernel = gemm_tc_kernel<BN, BITS, EPI, FUSED>;
+    static bool configured = false;
+    if (!configured) {
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S::BYTES);
+        if (e != cudaSuccess) return (int)e;
+        configured = true;
+    }
+    const int tiles = ((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN);
+    int ctas = a.max_ctas > 0 ? a.max_ctas : db_num_sms();
+    if (ctas > tiles) ctas = tiles;
+    kernel<<<ctas, NUM_THREADS, S::BYTES, stream>>>(tmA, tmW, a.sa, a.ldsa, a.sw, a.M, a.N, G, a.y, a.ldy,
+                                                    static_cast<__half*>(a.out_codes), a.ldoc, a.out_scales, a.ldos,
+                                                    a.nonfinite, a.dev_error);
+    return (int)cudaGetLastError();
+}
+
+template <int BN, int BITS>
+static int dispatch_epi(const DbGemmArgs& a, const CUtensorMap& tmA, const CUtensorMap& tmW, int G,
+                        cudaStream_t s) {
+    if (a.epilogue == DB_EPI_SWIGLU_QUANT) {
+        if (BN != 128) return (int)cudaErrorInvalidValue;
+        return a.fused ? launch_variant<BN, BITS, DB_EPI_SWIGLU_QUANT, true>(a, tmA, tmW, G, s)
+                       : launch_variant<BN, BITS, DB_EPI_SWIGLU_QUANT, false>(a, tmA, tmW, G, s);
+    }
+    if (a.epilogue == DB_EPI_RESIDUAL)
+        return a.fused ? launch_variant<BN, BITS, DB_EPI_RESIDUAL, true>(a, tmA, tmW, G, s)
+                       : launch_variant<BN, BITS, DB_EPI_RESIDUAL, false>(a, tmA, tmW, G, s);
+    return a.fused ? launch_variant<BN, BITS, DB_EPI_STORE, true>(a, tmA, tmW, G, s)
+                   : launch_variant<BN, BITS, DB_EPI_STORE, false>(a, tmA, tmW, G, s);
+}
+
+int db_launch_gemm_tc(const DbGemmArgs& a, cudaStream_t stream) {
+    if (a.M <= 0 || a.N <= 0) return 0;
+    if (a.K <= 0 || (a.bits != 4 && a.bits != 8)) return (int)cudaErrorInvalidValue;
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return (int)cudaErrorNotSupported;
+    const int G = (a.K + BK - 1) / BK, Kp = G * BK;
+    int bn = a.block_n ? a.block_n : 128;
+    if (a.epilogue == DB_EPI_SWIGLU_QUANT) bn = 128;
+    if (bn != 64 && bn != 128) return (int)cudaErrorInvalidValue;
+    if ((reinterpret_cast<uintptr_t>(a.a_codes) & 15) || (a.lda * 2) % 16 || a.lda < Kp ||
+        (reinterpret_cast<uintptr_t>(a.w_codes) & 15))
+        return (int)cudaErrorMisalignedAddress;
+    CUtensorMap tmA, tmW;
+    {
+        cuuint64_t dims[2] = {(cuuint64_t)Kp, (cuuint64_t)a.M};
+        cuuint64_t strides[1] = {(cuuint64_t)a.lda * 2};
+        cuuint32_t box[2] = {BK, BM};
+        cuuint32_t estr[2] = {1, 1};
+        if (enc(&tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(a.a_codes), dims, strides, box, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return (int)cudaErrorInvalidValue;
+    }
+    {
+        const cuuint64_t row_bytes = (cuuint64_t)Kp * a.bits / 8;
+        cuuint64_t dims[2] = {row_bytes, (cuuint64_t)a.N};
+        cuuint64_t strides[1] = {row_bytes};
+        cuuint32_t box[2] = {(cuuint32_t)(BK * a.bits / 8), (cuuint32_t)bn};
+        cuuint32_t estr[2] = {1, 1};
+        if (enc(&tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(a.w_codes), dims, strides, box, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return (int)cudaErrorInvalidValue;
+    }
+    if (bn == 64) return a.bits == 4 ? dispatch_epi<64, 4>(a, tmA, tmW, G, stream) : dispatch_epi<64, 8>(a, tmA, tmW, G, stream);
+    return a.bits == 4 ? dispatch_epi<128, 4>(a, tmA, tmW, G, stream) : dispatch_epi<128, 8>(a, tmA, tmW, G, stream);
+}

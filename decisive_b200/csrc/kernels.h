@@ -1,0 +1,75 @@
+// Host-side launchers of the device kernels (internal to libdecisive_b200.so).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+// element types of activation inputs
+enum { DB_F32 = 0, DB_F16 = 1, DB_BF16 = 2 };
+// activation code layouts
+enum { DB_CODES_NATURAL_I8 = 0, DB_CODES_GEMV_I8 = 1, DB_CODES_TC_F16 = 2 };
+// GEMM epilogues
+enum { DB_EPI_STORE = 0, DB_EPI_RESIDUAL = 1, DB_EPI_SWIGLU_QUANT = 2 };
+
+int db_launch_quantize_rows(const void* x, int dtype, int64_t ldx, int M, int K, int bits, void* codes, int layout,
+                            int64_t ldc, float* scales, int32_t* sums, int64_t lds, int* nonfinite,
+                            cudaStream_t stream);
+int db_launch_pack_weights(const uint16_t* w, int N, int K, int bits, uint8_t* codes, float* scales, int* bad,
+                           cudaStream_t stream);
+int db_launch_dequant_rows(const uint8_t* codes, const float* scales, int N, int K, int bits, const int32_t* ids,
+                           int T, float* out, int64_t ldo, int* bad, cudaStream_t stream);
+int db_launch_packed_convert(uint8_t* packed, uint8_t* codes, float* scales, int N, int K, int bits, int to_device,
+                             cudaStream_t stream);
+int db_launch_codes_to_natural(const void* codes, int layout, int64_t ldc, int M, int Kp, int8_t* out,
+                               cudaStream_t stream);
+
+// Tensor-core grouped GEMM.  A: f16 codes (tensor-core order) [M, lda], sa [G, ldsa];
+// W: device-layout codes [N, Kp*bits/8], sw [G, N].  Epilogue:
+//   DB_EPI_STORE     y[m, n] = acc
+//   DB_EPI_RESIDUAL  y[m, n] = y[m, n] + acc
+//   DB_EPI_SWIGLU_QUANT  columns come in blocks of 64 gate + 64 up rows of W; the activation
+//                    silu(gate) * up is quantised per 64 to f16 codes (tensor-core order) in
+//                    out_codes [M, ldoc] and scales out_scales [N/128, ldos].
+// fused = 1: sum = fma(dot, sw*sa, sum) (int8.rs:562-565); 0: sum += dot * (sa*sw) (int8.rs:276-278).
+struct DbGemmArgs {
+    const void* a_codes;
+    int64_t lda;  // elements
+    const float* sa;
+    int64_t ldsa;
+    const uint8_t* w_codes;
+    const float* sw;
+    int M, N, K, bits;
+    int fused;
+    int epilogue;
+    float* y;
+    int64_t ldy;
+    void* out_codes;
+    int64_t ldoc;
+    float* out_scales;
+    int64_t ldos;
+    const int* nonfinite;  // optional: when *nonfinite != 0 the outputs are NaN (int8.rs:170-173)
+    int* dev_error;        // device error word
+    int block_n;           // tile width (0 = default)
+    int max_ctas;          // persistent grid cap (0 = number of SMs)
+};
+int db_launch_gemm_tc(const DbGemmArgs& args, cudaStream_t stream);
+
+// Small-M path: int8 A codes (GEMV order) [M, lda] + sums [G, ldsa], sa [G, ldsa].
+struct DbGemvArgs {
+    const int8_t* a_codes;
+    int64_t lda;
+    const float* sa;
+    const int32_t* a_sums;
+    int64_t ldsa;
+    const uint8_t* w_codes;
+    const float* sw;
+    int M, N, K, bits;
+    int fused;
+    int residual;
+    float* y;
+    int64_t ldy;
+    const int* nonfinite;
+};
+int db_launch_gemv(const DbGemvArgs& args, cudaStream_t stream);
+int db_gemv_rows_limit();
+
+int db_num_sms();

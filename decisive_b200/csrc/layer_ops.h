@@ -1,0 +1,19 @@
+// Launchers of the layer kernels (internal to libdecisive_b200.so).
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+int db_launch_rms_quantize(const float* x, int64_t ldx, const float* w, int T, int D, float eps, int zero_centered,
+                           float* normed, int64_t ldn, void* codes, int layout, int64_t ldc, float* scales,
+                           int32_t* sums, int64_t lds, int* nonfinite, cudaStream_t stream);
+int db_launch_qk_norm_rope(const float* qkv, int64_t ld, int T, int Hq, int Hk, const float* qw, const float* kw,
+                           float eps, const float* cos_t, const float* sin_t, __half* q16, __half* k16, __half* v16,
+                           cudaStream_t stream);
+int db_launch_mean_pool(const float* x, int64_t ldx, int T, int D, float* out, cudaStream_t stream);
+int db_launch_fill_nan_if(float* y, int64_t n, const int* flag, cudaStream_t stream);
+
+// Non-causal GQA attention over head_dim 128: q16 [T, Hq, 128], k16/v16 [T, Hk, 128] (f16),
+// out f32 [T, Hq*128] with row stride ldo.  scale multiplies q.k before the softmax.
+int db_launch_attention(const __half* q16, const __half* k16, const __half* v16, int T, int Hq, int Hk, float scale,
+                        float* out, int64_t ldo, cudaStream_t stream);

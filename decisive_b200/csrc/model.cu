@@ -1,0 +1,513 @@
+// Model-level C ABI: the Pplx-shaped Q4/Q8 encoder on one device, behind a mirror of the
+// reference's inference API (src/inference/mod.rs:140-273):
+//   Model::create_cache / clear_cache / predict / predict_batch with cache ownership
+//   (CACHE_OWNER), cancellation (CANCELLED), parameter validation (INVALID_PARAMETERS),
+//   request validation (INVALID_REQUEST), the "never truncate" rule (INPUT_TOO_LONG,
+//   input.rs:261-269) and the finiteness check of the hidden state (backbone.rs:243-247).
+//
+// Forward of one sequence (pre-norm residual block, backbone.rs:197-249, Qwen3 attention mixer):
+//   x = embedding rows (quantized_rows.rs:89-110)
+//   per layer: n = rms(x); qkv = Wqkv n; q,k = rope(qknorm(q,k)); ctx = attn(q,k,v);
+//              x += Wo ctx; n = rms(x); h = silu(Wg n) * (Wu n); x += Wd h
+//   pooled = mean_t rms(x)
+// Every projection is the group-64 quantised GEMM; activations are quantised by the kernel
+// that produces them (rms_quantize, the SwiGLU epilogue) except the attention context.
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "../../include/decisive_b200.h"
+#include "capi_internal.h"
+#include "common.cuh"
+#include "kernels.h"
+#include "layer_ops.h"
+
+namespace {
+
+struct LayerW {
+    uint8_t *qkv_c = nullptr, *o_c = nullptr, *gu_c = nullptr, *dn_c = nullptr;
+    float *qkv_s = nullptr, *o_s = nullptr, *gu_s = nullptr, *dn_s = nullptr;
+    float *in_norm = nullptr, *post_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr;
+};
+
+void fill_error(db_error* err, const char* code, const std::string& msg) {
+    if (!err) return;
+    std::snprintf(err->code, sizeof err->code, "%s", code);
+    std::snprintf(err->message, sizeof err->message, "%s", msg.c_str());
+}
+
+}  // namespace
+
+struct db_model {
+    int device = 0;
+    db_encoder_config cfg{};
+    cudaStream_t stream = nullptr;
+    std::shared_ptr<char> identity = std::make_shared<char>(0);
+    bool synthetic = false;
+    uint64_t seed = 0;
+    float std = 0.f;
+    uint8_t* emb_c = nullptr;
+    float* emb_s = nullptr;
+    std::vector<LayerW> layers;
+    float* final_norm = nullptr;
+    std::vector<void*> allocations;
+    // workspace for up to cap_T tokens
+    int cap_T = 0;
+    std::vector<void*> ws_allocations;
+    float *x = nullptr, *qkv = nullptr, *ctx = nullptr, *normed = nullptr, *pooled = nullptr;
+    float *cos_t = nullptr, *sin_t = nullptr, *sa = nullptr, *sh = nullptr;
+    __half *acodes = nullptr, *hcodes = nullptr, *q16 = nullptr, *k16 = nullptr, *v16 = nullptr;
+    int32_t* ids = nullptr;
+    int* flag = nullptr;
+    int* dev_err = nullptr;
+
+    int D() const { return cfg.hidden; }
+    int Nq() const { return cfg.q_heads * cfg.head_dim; }
+    int Nk() const { return cfg.kv_heads * cfg.head_dim; }
+    int Nqkv() const { return Nq() + 2 * Nk(); }
+    int F() const { return cfg.ffn; }
+    int Kmax() const { return std::max(std::max(D(), Nq()), F()); }
+
+    template <class T>
+    cudaError_t alloc(T** p, size_t count, std::vector<void*>& into) {
+        cudaError_t e = cudaMalloc(reinterpret_cast<void**>(p), count * sizeof(T) + 256);
+        if (e == cudaSuccess) into.push_back(*p);
+        return e;
+    }
+    void free_all(std::vector<void*>& v) {
+        for (void* p : v) cudaFree(p);
+        v.clear();
+    }
+};
+
+struct db_cache {
+    std::shared_ptr<char> identity;
+    size_t max_bytes = 0;
+};
+
+namespace {
+
+enum { T_EMB = 0, T_Q, T_K, T_V, T_O, T_GATE, T_UP, T_DOWN };
+uint64_t tensor_id(int kind, int layer) { return kind == T_EMB ? 0 : 1 + 8ull * layer + (kind - 1); }
+
+int check_config(const db_encoder_config* c, db_error* err) {
+    if (!c || c->layers <= 0 || c->hidden <= 0 || c->hidden % 128 || c->hidden > 4096 || c->head_dim != 128 ||
+        c->q_heads <= 0 || c->kv_heads <= 0 || c->q_heads % c->kv_heads || c->ffn <= 0 || c->ffn % 64 ||
+        c->vocab <= 0 || (c->weight_bits != 4 && c->weight_bits != 8) || c->max_sequence_tokens <= 0) {
+        fill_error(err, "INVALID_PARAMETERS", "unsupported encoder configuration");
+        return -1;
+    }
+    return 0;
+}
+
+// Quantises a bf16 device tensor [N, K] into freshly allocated codes/scales.
+int pack(db_model* m, const uint16_t* bf16, int N, int K, uint8_t** codes, float** scales) {
+    const int G = (K + 63) / 64;
+    if (m->alloc(codes, (size_t)N * G * 64 * m->cfg.weight_bits / 8, m->allocations) ||
+        m->alloc(scales, (size_t)G * N, m->allocations))
+        return db_fail(DB_ERR_CUDA, "RESOURCE_LIMIT", "weight allocation exceeds device limits");
+    return db_pack_weights_g64(bf16, N, K, m->cfg.weight_bits, *codes, *scales, m->stream);
+}
+
+int upload_norm(db_model* m, const float* host, int n, float** out) {
+    if (m->alloc(out, n, m->allocations)) return db_fail(DB_ERR_CUDA, "RESOURCE_LIMIT", "norm allocation");
+    if (host) return db_cuda_status(cudaMemcpy(*out, host, n * sizeof(float), cudaMemcpyHostToDevice), "norm upload");
+    std::vector<float> ones(n, 1.f);
+    return db_cuda_status(cudaMemcpy(*out, ones.data(), n * sizeof(float), cudaMemcpyHostToDevice), "norm upload");
+}
+
+int ensure_workspace(db_model* m, int T) {
+    if (T <= m->cap_T) return 0;
+    cudaStreamSynchronize(m->stream);
+    m->free_all(m->ws_allocations);
+    m->cap_T = 0;
+    const int D = m->D(), F = m->F(), Kmax = m->Kmax();
+    const int Gmax = (Kmax + 63) / 64;
+    auto& v = m->ws_allocations;
+    if (m->alloc(&m->x, (size_t)T * D, v) || m->alloc(&m->qkv, (size_t)T * m->Nqkv(), v) ||
+        m->alloc(&m->ctx, (size_t)T * m->Nq(), v) || m->alloc(&m->normed, (size_t)T * D, v) ||
+        m->alloc(&m->pooled, D, v) || m->alloc(&m->cos_t, (size_t)T * 64, v) || m->alloc(&m->sin_t, (size_t)T * 64, v) ||
+        m->alloc(&m->sa, (size_t)Gmax * T, v) || m->alloc(&m->sh, (size_t)(F / 64) * T, v) ||
+        m->alloc(&m->acodes, (size_t)T * Kmax, v) || m->alloc(&m->hcodes, (size_t)T * F, v) ||
+        m->alloc(&m->q16, (size_t)T * m->Nq(), v) || m->alloc(&m->k16, (size_t)T * m->Nk(), v) ||
+        m->alloc(&m->v16, (size_t)T * m->Nk(), v) || m->alloc(&m->ids, T, v) || m->alloc(&m->flag, 4, v))
+        return db_fail(DB_ERR_CUDA, "RESOURCE_LIMIT", "workspace exceeds device limits");
+    // rotate-half RoPE table (backbone.rs:214-216, :471-483): angle = t * theta^(-2i/head_dim)
+    const int half = m->cfg.head_dim / 2;
+    std::vector<float> freq(half), c((size_t)T * 64), s((size_t)T * 64);
+    for (int i = 0; i < half; ++i) freq[i] = 1.f / powf(m->cfg.rope_theta, (float)(2 * i) / (float)m->cfg.head_dim);
+    for (int t = 0; t < T; ++t)
+        for (int i = 0; i < half; ++i) {
+            const float angle = (float)t * freq[i];
+            c[(size_t)t * 64 + i] = cosf(angle);
+            s[(size_t)t * 64 + i] = sinf(angle);
+        }
+    cudaMemcpy(m->cos_t, c.data(), c.size() * 4, cudaMemcpyHostToDevice);
+    cudaMemcpy(m->sin_t, s.data(), s.size() * 4, cudaMemcpyHostToDevice);
+    m->cap_T = T;
+    return 0;
+}
+
+int build(db_model* m, const db_encoder_weights* w) {
+    const int D = m->D(), L = m->cfg.layers, F = m->F(), Nq = m->Nq(), Nk = m->Nk();
+    cudaStream_t st = m->stream;
+    // scratch bf16 buffer big enough for any one projection block
+    const size_t big = std::max({(size_t)m->cfg.vocab * D, (size_t)m->Nqkv() * D, (size_t)F * D, (size_t)D * Nq});
+    uint16_t* scratch = nullptr;
+    if (cudaMalloc(&scratch, big * 2 + 256) != cudaSuccess)
+        return db_fail(DB_ERR_CUDA, "RESOURCE_LIMIT", "weight staging exceeds device limits");
+    auto fill = [&](int kind, int layer, const uint16_t* host, size_t n, uint16_t* dst) -> int {
+        if (m->synthetic) return db_synthetic_bf16(m->seed, tensor_id(kind, layer), (int64_t)n, m->std, dst, st);
+        return db_cuda_status(cudaMemcpyAsync(dst, host, n * 2, cudaMemcpyHostToDevice, st), "weight upload");
+    };
+    int rc = 0;
+    rc = fill(T_EMB, 0, w ? w->embedding : nullptr, (size_t)m->cfg.vocab * D, scratch);
+    if (!rc) rc = pack(m, scratch, m->cfg.vocab, D, &m->emb_c, &m->emb_s);
+    m->layers.resize(L);
+    for (int l = 0; l < L && !rc; ++l) {
+        LayerW& lw = m->layers[l];
+        rc = fill(T_Q, l, w ? w->q[l] : nullptr, (size_t)Nq * D, scratch);
+        if (!rc) rc = fill(T_K, l, w ? w->k[l] : nullptr, (size_t)Nk * D, scratch + (size_t)Nq * D);
+        if (!rc) rc = fill(T_V, l, w ? w->v[l] : nullptr, (size_t)Nk * D, scratch + (size_t)(Nq + Nk) * D);
+        if (!rc) rc = pack(m, scratch, m->Nqkv(), D, &lw.qkv_c, &lw.qkv_s);
+        if (!rc) rc = fill(T_O, l, w ? w->o[l] : nullptr, (size_t)D * Nq, scratch);
+        if (!rc) rc = pack(m, scratch, D, Nq, &lw.o_c, &lw.o_s);
+        uint8_t *gc = nullptr, *uc = nullptr;
+        float *gs = nullptr, *us = nullptr;
+        if (!rc) rc = fill(T_GATE, l, w ? w->gate[l] : nullptr, (size_t)F * D, scratch);
+        if (!rc) rc = pack(m, scratch, F, D, &gc, &gs);
+        if (!rc) rc = fill(T_UP, l, w ? w->up[l] : nullptr, (size_t)F * D, scratch);
+        if (!rc) rc = pack(m, scratch, F, D, &uc, &us);
+        if (!rc) {
+            const int G = (D + 63) / 64;
+            if (m->alloc(&lw.gu_c, (size_t)2 * F * G * 64 * m->cfg.weight_bits / 8, m->allocations) ||
+                m->alloc(&lw.gu_s, (size_t)G * 2 * F, m->allocations))
+                rc = db_fail(DB_ERR_CUDA, "RESOURCE_LIMIT", "weight allocation exceeds device limits");
+            if (!rc) rc = db_interleave_gate_up(gc, gs, uc, us, F, D, m->cfg.weight_bits, lw.gu_c, lw.gu_s, st);
+            cudaStreamSynchronize(st);
+        }
+        if (!rc) rc = fill(T_DOWN, l, w ? w->down[l] : nullptr, (size_t)D * F, scratch);
+        if (!rc) rc = pack(m, scratch, D, F, &lw.dn_c, &lw.dn_s);
+        if (!rc) rc = upload_norm(m, w ? w->input_norm[l] : nullptr, D, &lw.in_norm);
+        if (!rc) rc = upload_norm(m, w ? w->post_norm[l] : nullptr, D, &lw.post_norm);
+        if (!rc) rc = upload_norm(m, w ? w->q_norm[l] : nullptr, m->cfg.head_dim, &lw.q_norm);
+        if (!rc) rc = upload_norm(m, w ? w->k_norm[l] : nullptr, m->cfg.head_dim, &lw.k_norm);
+    }
+    if (!rc) rc = upload_norm(m, w ? w->final_norm : nullptr, D, &m->final_norm);
+    cudaStreamSynchronize(st);
+    cudaFree(scratch);
+    if (!rc) rc = ensure_workspace(m, m->cfg.max_sequence_tokens);
+    return rc;
+}
+
+db_model* create(int device, const db_encoder_config* cfg, const db_encoder_weights* w, bool synthetic,
+                 uint64_t seed, float stdv, db_error* err) {
+    if (check_config(cfg, err)) return nullptr;
+    if (device < 0 || device >= db_device_count() || cudaSetDevice(device) != cudaSuccess) {
+        fill_error(err, "GPU_UNAVAILABLE", "no CUDA device " + std::to_string(device));
+        return nullptr;
+    }
+    auto* m = new db_model();
+    m->device = device;
+    m->cfg = *cfg;
+    m->synthetic = synthetic;
+    m->seed = seed;
+    m->std = stdv;
+    m->dev_err = db_device_error_ptr();
+    cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking);
+    if (build(m, w)) {
+        fill_error(err, db_last_error_code(), db_last_error_message());
+        db_model_destroy(m);
+        return nullptr;
+    }
+    return m;
+}
+
+// Enqueues the forward of ids (device, T tokens) -> m->pooled.  Host-side cancellation is polled
+// between layers.  Returns 0, 1 when cancelled, or a negative status.
+int enqueue_forward(db_model* m, int T, const volatile int32_t* cancel) {
+    const auto& c = m->cfg;
+    const int D = c.hidden, Nq = m->Nq(), F = m->F(), Nqkv = m->Nqkv();
+    const int bits = c.weight_bits, fused = c.fused;
+    cudaStream_t st = m->stream;
+    const int64_t ld_codes = m->Kmax(), lds = m->cap_T;
+    int rc = 0;
+    cudaMemsetAsync(m->flag, 0, sizeof(int), st);
+    rc = db_launch_dequant_rows(m->emb_c, m->emb_s, c.vocab, D, bits, m->ids, T, m->x, D, m->flag, st);
+    auto gemm = [&](const void* a, const uint8_t* wc, const float* ws, const float* sa, int N, int K, int epi, float* y,
+                    int64_t ldy) {
+        DbGemmArgs g{};
+        g.a_codes = a;
+        g.lda = ld_codes;
+        g.sa = sa;
+        g.ldsa = lds;
+        g.w_codes = wc;
+        g.sw = ws;
+        g.M = T;
+        g.N = N;
+        g.K = K;
+        g.bits = bits;
+        g.fused = fused;
+        g.epilogue = epi;
+        g.y = y;
+        g.ldy = ldy;
+        g.out_codes = m->hcodes;
+        g.ldoc = F;
+        g.out_scales = m->sh;
+        g.ldos = lds;
+        g.nonfinite = m->flag;
+        g.dev_error = m->dev_err;
+        return db_launch_gemm_tc(g, st);
+    };
+    const float attn_scale = 1.f / sqrtf((float)c.head_dim);
+    for (int l = 0; l < c.layers && !rc; ++l) {
+        if (cancel && *cancel) return 1;
+        const LayerW& w = m->layers[l];
+        rc = db_launch_rms_quantize(m->x, D, w.in_norm, T, D, c.eps, 0, nullptr, 0, m->acodes, DB_CODES_TC, ld_codes,
+                                    m->sa, nullptr, lds, m->flag, st);
+        if (!rc) rc = gemm(m->acodes, w.qkv_c, w.qkv_s, m->sa, Nqkv, D, DB_EPI_STORE, m->qkv, Nqkv);
+        if (!rc)
+            rc = db_launch_qk_norm_rope(m->qkv, Nqkv, T, c.q_heads, c.kv_heads, w.q_norm, w.k_norm, c.eps, m->cos_t,
+                                        m->sin_t, m->q16, m->k16, m->v16, st);
+        if (!rc) rc = db_launch_attention(m->q16, m->k16, m->v16, T, c.q_heads, c.kv_heads, attn_scale, m->ctx, Nq, st);
+        if (!rc)
+            rc = db_launch_quantize_rows(m->ctx, DB_F32, Nq, T, Nq, 8, m->acodes, DB_CODES_TC, ld_codes, m->sa, nullptr,
+                                         lds, m->flag, st);
+        if (!rc) rc = gemm(m->acodes, w.o_c, w.o_s, m->sa, D, Nq, DB_EPI_RESIDUAL, m->x, D);
+        if (!rc)
+            rc = db_launch_rms_quantize(m->x, D, w.post_norm, T, D, c.eps, 0, nullptr, 0, m->acodes, DB_CODES_TC,
+                                        ld_codes, m->sa, nullptr, lds, m->flag, st);
+        if (!rc) rc = gemm(m->acodes, w.gu_c, w.gu_s, m->sa, 2 * F, D, DB_EPI_SWIGLU_QUANT, nullptr, 0);
+        if (!rc) {
+            DbGemmArgs g{};
+            g.a_codes = m->hcodes;
+            g.lda = F;
+            g.sa = m->sh;
+            g.ldsa = lds;
+            g.w_codes = w.dn_c;
+            g.sw = w.dn_s;
+            g.M = T;
+            g.N = D;
+            g.K = F;
+            g.bits = bits;
+            g.fused = fused;
+            g.epilogue = DB_EPI_RESIDUAL;
+            g.y = m->x;
+            g.ldy = D;
+            g.nonfinite = m->flag;
+            g.dev_error = m->dev_err;
+            rc = db_launch_gemm_tc(g, st);
+        }
+    }
+    if (!rc)
+        rc = db_launch_rms_quantize(m->x, D, m->final_norm, T, D, c.eps, 0, m->normed, D, nullptr, DB_CODES_TC, 0,
+                                    nullptr, nullptr, 0, m->flag, st);
+    if (!rc) rc = db_launch_mean_pool(m->normed, D, T, D, m->pooled, st);
+    return rc ? db_cuda_status(rc, "forward") : 0;
+}
+
+// Backend::predict for one request; errors use the reference's codes.
+int predict_one(db_model* m, const int32_t* ids, size_t n, const db_parameters* params, const volatile int32_t* cancel,
+                float* out, db_error* err) {
+    if (cancel && *cancel) {
+        fill_error(err, "CANCELLED", "Inference was cancelled");
+        return -1;
+    }
+    if (!ids || n == 0) {
+        fill_error(err, "INVALID_REQUEST", "a nonempty token sequence is required");
+        return -1;
+    }
+    const int limit = params ? params->max_sequence_tokens : m->cfg.max_sequence_tokens;
+    if (limit <= 0) {
+        fill_error(err, "INVALID_PARAMETERS", "maxSequenceTokens must be positive");
+        return -1;
+    }
+    if (n > (size_t)limit) {
+        fill_error(err, "INPUT_TOO_LONG", "single question exceeds token limit: " + std::to_string(n) + " > " +
+                                              std::to_string(limit) + "; inputs are never truncated");
+        return -1;
+    }
+    for (size_t i = 0; i < n; ++i)
+        if (ids[i] < 0 || ids[i] >= m->cfg.vocab) {
+            fill_error(err, "INVALID_REQUEST", "token id " + std::to_string(ids[i]) + " outside the vocabulary");
+            return -1;
+        }
+    cudaSetDevice(m->device);
+    if (ensure_workspace(m, (int)n)) {
+        fill_error(err, "RESOURCE_LIMIT", db_last_error_message());
+        return -1;
+    }
+    cudaMemcpyAsync(m->ids, ids, n * sizeof(int32_t), cudaMemcpyHostToDevice, m->stream);
+    int rc = enqueue_forward(m, (int)n, cancel);
+    if (rc == 1) {
+        cudaStreamSynchronize(m->stream);
+        fill_error(err, "CANCELLED", "Inference was cancelled");
+        return -1;
+    }
+    int flag = 0;
+    cudaMemcpyAsync(&flag, m->flag, sizeof(int), cudaMemcpyDeviceToHost, m->stream);
+    cudaMemcpyAsync(out, m->pooled, m->cfg.hidden * sizeof(float), cudaMemcpyDeviceToHost, m->stream);
+    const cudaError_t e = cudaStreamSynchronize(m->stream);
+    if (rc || e != cudaSuccess) {
+        fill_error(err, "INFERENCE_FAILED", rc ? db_last_error_message() : cudaGetErrorString(e));
+        return -1;
+    }
+    int word = 0;
+    cudaMemcpy(&word, m->dev_err, sizeof(int), cudaMemcpyDeviceToHost);
+    if (word) {
+        cudaMemset(m->dev_err, 0, sizeof(int));
+        fill_error(err, "INFERENCE_FAILED", "device wait expired (error word " + std::to_string(word) + ")");
+        return -1;
+    }
+    if (flag) {
+        fill_error(err, "INFERENCE_FAILED", "non-finite hidden state");
+        return -1;
+    }
+    if (cancel && *cancel) {
+        fill_error(err, "CANCELLED", "Inference was cancelled");
+        return -1;
+    }
+    return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+db_model* db_model_create(int device, const db_encoder_config* cfg, const db_encoder_weights* w, db_error* err) {
+    if (!w || !w->embedding || !w->q || !w->k || !w->v || !w->o || !w->gate || !w->up || !w->down || !w->final_norm) {
+        fill_error(err, "INVALID_PARAMETERS", "missing weights");
+        return nullptr;
+    }
+    return create(device, cfg, w, false, 0, 0.f, err);
+}
+
+db_model* db_model_create_synthetic(int device, const db_encoder_config* cfg, uint64_t seed, float stdv,
+                                    db_error* err) {
+    return create(device, cfg, nullptr, true, seed, stdv, err);
+}
+
+int64_t db_model_synthetic_weight(const db_model* m, const char* name, int layer, uint16_t* host_out, int64_t cap) {
+    if (!m || !m->synthetic || !name) return db_fail(DB_ERR_INVALID_ARGUMENT, "INVALID_ARGUMENT", "not synthetic");
+    const int D = m->D(), F = m->F(), Nq = m->Nq(), Nk = m->Nk();
+    static const char* names[] = {"embedding", "q", "k", "v", "o", "gate", "up", "down"};
+    int kind = -1;
+    for (int i = 0; i < 8; ++i)
+        if (!std::strcmp(name, names[i])) kind = i;
+    if (kind < 0 || layer < 0 || layer >= m->cfg.layers)
+        return db_fail(DB_ERR_INVALID_ARGUMENT, "INVALID_ARGUMENT", "unknown weight");
+    const int64_t sizes[8] = {(int64_t)m->cfg.vocab * D, (int64_t)Nq * D, (int64_t)Nk * D, (int64_t)Nk * D,
+                              (int64_t)D * Nq,          (int64_t)F * D,  (int64_t)F * D,  (int64_t)D * F};
+    const int64_t n = sizes[kind];
+    if (!host_out) return n;
+    if (cap < n) return db_fail(DB_ERR_INVALID_ARGUMENT, "INVALID_ARGUMENT", "buffer too small");
+    cudaSetDevice(m->device);
+    uint16_t* d = nullptr;
+    if (cudaMalloc(&d, n * 2) != cudaSuccess) return db_cuda_status(1, "weight export");
+    int rc = db_synthetic_bf16(m->seed, tensor_id(kind, layer), n, m->std, d, m->stream);
+    if (!rc) rc = db_cuda_status(cudaMemcpyAsync(host_out, d, n * 2, cudaMemcpyDeviceToHost, m->stream), "copy");
+    cudaStreamSynchronize(m->stream);
+    cudaFree(d);
+    return rc ? rc : n;
+}
+
+void db_model_destroy(db_model* m) {
+    if (!m) return;
+    cudaSetDevice(m->device);
+    if (m->stream) cudaStreamSynchronize(m->stream);
+    m->free_all(m->ws_allocations);
+    m->free_all(m->allocations);
+    if (m->stream) cudaStreamDestroy(m->stream);
+    delete m;
+}
+
+int db_model_capabilities(const db_model* m, char* json, size_t cap) {
+    if (!m || !json) return DB_ERR_INVALID_ARGUMENT;
+    // adapters.rs:167-176 (Pplx: no caches); backend is this library
+    int n = std::snprintf(json, cap,
+                          "{\"model\":\"pplx-flash\",\"backend\":\"cuda\",\"caches\":[],\"tuning\":\"heuristic\","
+                          "\"weightBits\":%d,\"layers\":%d,\"hidden\":%d}",
+                          m->cfg.weight_bits, m->cfg.layers, m->cfg.hidden);
+    return n < 0 || (size_t)n >= cap ? DB_ERR_INVALID_ARGUMENT : DB_OK;
+}
+
+db_cache* db_cache_create(db_model* m, size_t max_bytes, int require_prefix, db_error* err) {
+    if (!m) {
+        fill_error(err, "INVALID_PARAMETERS", "no model");
+        return nullptr;
+    }
+    if (require_prefix) {  // mod.rs:177-182: this model/backend has no prefix cache
+        fill_error(err, "UNSUPPORTED_CACHE", "This model/backend does not support prefix caching");
+        return nullptr;
+    }
+    auto* c = new db_cache();
+    c->identity = m->identity;
+    c->max_bytes = max_bytes;
+    return c;
+}
+
+int db_cache_clear(db_model* m, db_cache* c, db_error* err) {
+    if (!m || !c || c->identity != m->identity) {
+        fill_error(err, "CACHE_OWNER", "Cache belongs to another model instance");
+        return -1;
+    }
+    return 0;  // the Pplx backend keeps no cache state (adapters.rs:180-181)
+}
+
+void db_cache_destroy(db_cache* c) { delete c; }
+
+int db_predict(db_model* m, const int32_t* ids, size_t n, const db_parameters* params, db_cache* cache,
+               const volatile int32_t* cancel, float* out, db_error* err) {
+    if (!m || !out) {
+        fill_error(err, "INVALID_PARAMETERS", "null model or output");
+        return -1;
+    }
+    if (cache && cache->identity != m->identity) {
+        fill_error(err, "CACHE_OWNER", "Cache belongs to another model instance");
+        return -1;
+    }
+    return predict_one(m, ids, n, params, cancel, out, err);  // errors clear the (stateless) cache
+}
+
+int db_predict_batch(db_model* m, const int32_t* const* ids, const size_t* lens, size_t count,
+                     const db_parameters* params, db_cache* cache, const volatile int32_t* cancel, float* outs,
+                     int32_t* status, db_error* errs, db_error* err) {
+    if (!m || (count && (!ids || !lens || !outs || !status))) {
+        fill_error(err, "INVALID_PARAMETERS", "null batch arguments");
+        return -1;
+    }
+    if (cache && cache->identity != m->identity) {
+        fill_error(err, "CACHE_OWNER", "Cache belongs to another model instance");
+        return -1;
+    }
+    for (size_t i = 0; i < count; ++i)
+        status[i] = predict_one(m, ids[i], lens[i], params, cancel, outs + i * (size_t)m->cfg.hidden,
+                                errs ? &errs[i] : nullptr);
+    return 0;
+}
+
+int db_forward_device(db_model* m, const int32_t* ids_dev, int64_t n, float* out_dev, void* stream) {
+    if (!m || !ids_dev || n <= 0 || !out_dev)
+        return db_fail(DB_ERR_INVALID_ARGUMENT, "INVALID_ARGUMENT", "forward: bad arguments");
+    cudaSetDevice(m->device);
+    if (ensure_workspace(m, (int)n)) return DB_ERR_CUDA;
+    cudaStream_t caller = static_cast<cudaStream_t>(stream);
+    cudaEvent_t ev;
+    cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+    cudaEventRecord(ev, caller);
+    cudaStreamWaitEvent(m->stream, ev, 0);
+    cudaMemcpyAsync(m->ids, ids_dev, n * sizeof(int32_t), cudaMemcpyDeviceToDevice, m->stream);
+    int rc = enqueue_forward(m, (int)n, nullptr);
+    cudaMemcpyAsync(out_dev, m->pooled, m->cfg.hidden * sizeof(float), cudaMemcpyDeviceToDevice, m->stream);
+    cudaEventRecord(ev, m->stream);
+    cudaStreamWaitEvent(caller, ev, 0);
+    cudaEventDestroy(ev);
+    return rc;
+}
+
+}  // extern "C"

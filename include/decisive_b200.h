@@ -1,0 +1,213 @@
+/*
+ * decisive_b200 -- C ABI of the B200 (sm_100a) backend for decisive's quantised projection path.
+ *
+ * Two layers of entry points:
+ *   1. kernel level: device pointers + sizes + an optional cudaStream_t (passed as void*; NULL =
+ *      the calling thread's current-device default stream).  Each replaces one reference
+ *      function of src/models/pplx_flash/ (cited per entry).  Return 0 or a negative DB_ERR_*;
+ *      db_last_error_code()/db_last_error_message() describe the failure (thread-local).
+ *   2. model level: an opaque model handle mirroring `inference::Model<B: Backend>`
+ *      (src/inference/mod.rs:140-273) for the Pplx-shaped encoder, with per-request
+ *      {code, message} errors using the reference's error codes.
+ *
+ * Numerics: group-64 symmetric quantisation with f32 scales; activation codes in [-127, 127]
+ * (int8.rs:178-202); weight codes Q4 in [-7, 7] (or [-8, 7] when fitted) or Q8 in [-127, 127];
+ * per output sum = fma(float(dot_g), sw*sa, sum) over ascending groups (int8.rs:562-565) or the
+ * portable sum += dot*(sa*sw) (int8.rs:276-278) -- both bit-exact against the reference's CPU
+ * arithmetic.
+ *
+ * Device weight layout (see DB_LAYOUT comment below) differs from the reference's packed row
+ * format (packed.rs) only in where the scales live; db_import_packed/db_export_packed convert
+ * losslessly.
+ */
+#ifndef DECISIVE_B200_H
+#define DECISIVE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DB_ABI_VERSION 1
+
+/* ---- status codes ---- */
+#define DB_OK 0
+#define DB_ERR_INVALID_ARGUMENT (-1) /* bad shape / pointer / alignment */
+#define DB_ERR_CUDA (-2)             /* a CUDA runtime call failed */
+#define DB_ERR_DEVICE_TIMEOUT (-3)   /* a kernel's bounded wait expired (device error word set) */
+#define DB_ERR_NONFINITE (-4)        /* non-finite input where the reference rejects it */
+#define DB_ERR_UNSUPPORTED (-5)
+
+/* ---- element types and code layouts ---- */
+#define DB_DTYPE_F32 0
+#define DB_DTYPE_F16 1
+#define DB_DTYPE_BF16 2
+/* activation code layouts (int8 values in [-127,127]):
+ *   DB_CODES_NATURAL  int8 [M, Kp], k in order (reference Scratch::values, int8.rs:7-11)
+ *   DB_CODES_GEMV     int8 [M, Kp], inside each 8 consecutive k stored as k0,k2,k4,k6,k1,k3,k5,k7
+ *   DB_CODES_TC       f16  [M, Kp] integer-valued, inside each 8 stored as k0,k4,k1,k5,k2,k6,k3,k7
+ * Kp = ceil(K/64)*64; activation scales f32 [G, lds], sums int32 [G, lds], G = Kp/64.
+ * DB_LAYOUT: weight codes Q4 [N, Kp/2] bytes (low nibble = even k, nibble = code+8, i.e. the
+ * code bytes of packed.rs:22-28), Q8 [N, Kp] int8; weight scales f32 [G, N]. */
+#define DB_CODES_NATURAL 0
+#define DB_CODES_GEMV 1
+#define DB_CODES_TC 2
+
+int db_abi_version(void);
+const char *db_last_error_code(void);
+const char *db_last_error_message(void);
+int db_device_count(void);
+/* reads and clears the calling device's kernel error word (bounded-wait expiries) */
+int db_device_error_word(void);
+
+/* ---- kernel level ---- */
+
+/* Activation quantiser.  Replaces int8::Matrix::prepare (int8.rs:178-202) and the grouped
+ * WGSL quantiser `int8_input` (webgpu/grouped_q4.rs:3-25).  x [M, K] (row stride ldx elements)
+ * of dtype -> codes (layout, row stride ldc elements), scales [G, lds], sums [G, lds] (optional).
+ * bits 8 (limit 127) or 4 (limit 7).  *nonfinite (optional, device int) is OR-ed with 1 when any
+ * input is NaN/Inf. */
+int db_quantize_activations_g64(const void *x, int dtype, int64_t ldx, int64_t M, int64_t K, int bits,
+                                void *codes, int layout, int64_t ldc, float *scales, int32_t *sums, int64_t lds,
+                                int *nonfinite, void *stream);
+
+/* Weight quantiser, absmax.  Replaces int8::Matrix::from_bf16_optimized's absmax branch
+ * (int8.rs:51-152) and packed::pack (packed.rs:31-56): bf16 [N, K] ([output, input], the
+ * reference's weight order) -> codes/scales in DB_LAYOUT.  Returns DB_ERR_NONFINITE for a
+ * non-finite weight ("non-finite INT8 weight", int8.rs:99-102). */
+int db_pack_weights_g64(const uint16_t *bf16, int64_t N, int64_t K, int bits, uint8_t *codes, float *scales,
+                        void *stream);
+
+/* Reference packed rows (packed.rs:10-56: per (row, group) 32|64 code bytes then the f32
+ * scale; K % 64 == 0) <-> DB_LAYOUT, lossless. */
+int db_import_packed(const uint8_t *packed, int64_t N, int64_t K, int bits, uint8_t *codes, float *scales,
+                     void *stream);
+int db_export_packed(const uint8_t *codes, const float *scales, int64_t N, int64_t K, int bits, uint8_t *packed,
+                     void *stream);
+
+/* Row dequantisation: out[t, k] = code(row ids[t], k) * scale.  Replaces packed::unpack
+ * (packed.rs:59-73) and Embedding::append (quantized_rows.rs:89-110); ids may be NULL
+ * (rows 0..T-1).  An id outside [0, N) yields DB_ERR_INVALID_ARGUMENT. */
+int db_dequant_rows_g64(const uint8_t *codes, const float *scales, int64_t N, int64_t K, int bits,
+                        const int32_t *ids, int64_t T, float *out, int64_t ldo, void *stream);
+
+/* Grouped GEMM on prepared activations.  Replaces Matrix::apply_prepared (int8.rs:229-288)
+ * and the WGSL int8_gemm family (grouped_q4_tuned.wgsl): y[m, n] (+)= sum over groups.
+ * a_codes in DB_CODES_TC layout (M >= 1), or DB_CODES_GEMV when M <= db_gemv_max_rows();
+ * a_sums is required by the GEMV layout with Q4 weights.  fused: 1 = AVX2 numerics (fma),
+ * 0 = portable numerics.  residual: 1 adds into y.  nonfinite (optional): when *nonfinite != 0
+ * every output is NaN (int8.rs:170-173). */
+int db_gemm_g64(const void *a_codes, int layout, int64_t lda, const float *sa, const int32_t *a_sums, int64_t ldsa,
+                const uint8_t *w_codes, const float *sw, int64_t M, int64_t N, int64_t K, int bits, int fused,
+                int residual, float *y, int64_t ldy, const int *nonfinite, void *stream);
+int db_gemv_max_rows(void);
+
+/* Full projection: quantise x (f32 [M, K]) then GEMM, choosing the GEMV path for
+ * M <= db_gemv_max_rows() and the tensor-core path otherwise.  Replaces Matrix::apply
+ * (int8.rs:166-176) including its non-finite guard.  workspace: device bytes from
+ * db_linear_workspace_bytes(M, K). */
+size_t db_linear_workspace_bytes(int64_t M, int64_t K);
+int db_linear_g64(const float *x, int64_t M, int64_t K, const uint8_t *w_codes, const float *sw, int64_t N,
+                  int weight_bits, int activation_bits, int fused, float *y, void *workspace, void *stream);
+
+/* Readout GEMV on one activation row.  Replaces packed::project (packed.rs:75-119; portable
+ * numerics, activation 8-bit).  Returns DB_ERR_NONFINITE for a non-finite x. */
+int db_project_packed(const float *x, int64_t K, const uint8_t *w_codes, const float *sw, int64_t outputs,
+                      int bits, float *y, void *workspace, void *stream);
+
+/* Fused gate/up projection + SiLU(gate)*up + group-64 re-quantisation, the semantics of the
+ * reference's fused q4_mlp (grouped_q4_mlp.wgsl:1-105) == apply_pair + silu_mul + prepare
+ * (backbone.rs:229-236, cpu.rs:348-371, int8.rs:178-202).  w_gu: 2*F rows in blocks of
+ * 64 gate rows followed by the 64 matching up rows (db_interleave_gate_up builds it).
+ * Output: codes DB_CODES_TC [M, ldoc] and scales [F/64, ldos].  F % 64 == 0. */
+int db_mlp_g64(const void *a_codes, int64_t lda, const float *sa, int64_t ldsa, const uint8_t *w_gu_codes,
+               const float *w_gu_scales, int64_t M, int64_t F, int64_t K, int bits, int fused, void *out_codes,
+               int64_t ldoc, float *out_scales, int64_t ldos, const int *nonfinite, void *stream);
+/* gate/up [F, K] each (DB_LAYOUT) -> interleaved [2F, K] (DB_LAYOUT) for db_mlp_g64 */
+int db_interleave_gate_up(const uint8_t *gate_codes, const float *gate_scales, const uint8_t *up_codes,
+                          const float *up_scales, int64_t F, int64_t K, int bits, uint8_t *out_codes,
+                          float *out_scales, void *stream);
+
+/* Non-causal GQA attention (backbone.rs:485-615 without the output gate): q f16 [T, Hq, 128],
+ * k/v f16 [T, Hk, 128], out f32 [T, Hq*128] (row stride ldo); scale multiplies q.k. */
+int db_attention(const void *q16, const void *k16, const void *v16, int64_t T, int64_t q_heads, int64_t kv_heads,
+                 int64_t head_dim, float scale, float *out, int64_t ldo, void *stream);
+
+/* Deterministic synthetic bf16 tensor on the device: value_i = std * N(0,1) from a
+ * counter-based generator keyed by (seed, tensor). */
+int db_synthetic_bf16(uint64_t seed, uint64_t tensor, int64_t n, float std, uint16_t *out, void *stream);
+
+/* ---- model level: mirror of inference::Model / Backend (src/inference/mod.rs) ---- */
+
+typedef struct db_model db_model;
+typedef struct db_cache db_cache;
+
+/* {code, message} of inference::Error (mod.rs:44-85). */
+typedef struct {
+    char code[32];
+    char message[224];
+} db_error;
+
+/* Qwen3-shaped bidirectional encoder, Q4/Q8 group-64 projections. */
+typedef struct {
+    int32_t layers, hidden, q_heads, kv_heads, head_dim, ffn, vocab;
+    int32_t weight_bits;         /* 4 or 8 */
+    float rope_theta, eps;
+    int32_t max_sequence_tokens; /* PplxParameters default (parameters.rs:81-92) */
+    int32_t fused;               /* 1 = AVX2 numerics (default), 0 = portable */
+} db_encoder_config;
+
+/* PplxParameters (parameters.rs:81-103): max_sequence_tokens must be positive. */
+typedef struct {
+    int32_t max_sequence_tokens;
+} db_parameters;
+
+/* Host weights: bf16 [out, in] per projection per layer (q, k, v, o, gate, up, down),
+ * f32 norms, bf16 embedding [vocab, hidden]. */
+typedef struct {
+    const uint16_t *embedding;
+    const uint16_t *const *q, *const *k, *const *v, *const *o, *const *gate, *const *up, *const *down;
+    const float *const *input_norm, *const *post_norm, *const *q_norm, *const *k_norm;
+    const float *final_norm;
+} db_encoder_weights;
+
+db_model *db_model_create(int device, const db_encoder_config *cfg, const db_encoder_weights *w, db_error *err);
+/* random-init weights (N(0, std) via db_synthetic_bf16, norms = 1) generated on the device */
+db_model *db_model_create_synthetic(int device, const db_encoder_config *cfg, uint64_t seed, float std,
+                                    db_error *err);
+/* copies the bf16 weight `name` ("embedding", "q", ..., "down") of `layer` of a synthetic model
+ * into host memory (for the CPU oracle); returns elements copied or a negative status */
+int64_t db_model_synthetic_weight(const db_model *m, const char *name, int layer, uint16_t *host_out, int64_t cap);
+void db_model_destroy(db_model *m);
+/* Capabilities (mod.rs:118-125) as JSON: {"model":..., "backend":"cuda", "caches":[...], "tuning":...} */
+int db_model_capabilities(const db_model *m, char *json, size_t cap);
+
+/* Model::create_cache (mod.rs:176-189): require_prefix on a model without prefix caching ->
+ * NULL with code UNSUPPORTED_CACHE.  max_bytes excludes weights and scratch. */
+db_cache *db_cache_create(db_model *m, size_t max_bytes, int require_prefix, db_error *err);
+/* Model::clear_cache (mod.rs:190-194): a cache of another model -> CACHE_OWNER */
+int db_cache_clear(db_model *m, db_cache *c, db_error *err);
+void db_cache_destroy(db_cache *c);
+
+/* Model::predict (mod.rs:206-249): ids [n] -> pooled f32 [hidden].  params NULL = the model's
+ * defaults; cache NULL = an ephemeral cache; *cancel != 0 -> CANCELLED (checked before and
+ * after the forward, and between layers).  Returns 0, or -1 with *err filled. */
+int db_predict(db_model *m, const int32_t *ids, size_t n, const db_parameters *params, db_cache *cache,
+               const volatile int32_t *cancel, float *out, db_error *err);
+
+/* Model::predict_batch (mod.rs:250-273): ordered per-request outcomes; status[i] = 0 success
+ * (outs + i*hidden filled) or -1 (errs[i] filled).  A foreign cache fails the whole call. */
+int db_predict_batch(db_model *m, const int32_t *const *ids, const size_t *lens, size_t count,
+                     const db_parameters *params, db_cache *cache, const volatile int32_t *cancel, float *outs,
+                     int32_t *status, db_error *errs, db_error *err);
+
+/* Device-resident variant for throughput measurement: ids already on the device, output left on
+ * the device; no host synchronisation.  Used by bench.py's device-timed leg. */
+int db_forward_device(db_model *m, const int32_t *ids_dev, int64_t n, float *out_dev, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif
