@@ -1,0 +1,337 @@
+#!/usr/bin/env python
+"""Benchmark: Pplx-shaped Q4 encoder forward at 1024 tokens per GPU.
+
+One step = one 28-layer forward of one 1024-token sequence on every GPU (weak scaling; ranks
+process independent sequences, no collective on the data path).  `value` is device-timed with
+inputs resident in HBM; `e2e` goes through the public API (Model.predict) with host token ids in
+and the host embedding out.  Runs under torchrun for N > 1 (one process per GPU).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "Pplx Q4 tokens/s @1024 tok (1/2/4/8 B200) + GEMM % roofline vs host-CPU ref"
+CFG = dict(layers=28, hidden=1024, q_heads=16, kv_heads=8, head_dim=128, ffn=3072, vocab=151936, weight_bits=4)
+TOKENS = 1024
+SEED = 1234
+L2_BYTES = 126 * 2 ** 20
+
+
+def gemm_flops_per_token_layer(c):
+    nq, nk = c["q_heads"] * c["head_dim"], c["kv_heads"] * c["head_dim"]
+    d, f = c["hidden"], c["ffn"]
+    return {"gemm_qkv": 2 * d * (nq + 2 * nk), "gemm_o": 2 * nq * d, "gemm_mlp_swiglu": 2 * d * 2 * f,
+            "gemm_down": 2 * f * d}
+
+
+def q4_weight_bytes(c):
+    nq, nk = c["q_heads"] * c["head_dim"], c["kv_heads"] * c["head_dim"]
+    d, f = c["hidden"], c["ffn"]
+    params = c["layers"] * (d * (nq + 2 * nk) + nq * d + 2 * d * f + f * d)
+    return params * (0.5 + 4 / 64)
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d.get("bf16_tflops", 1590.0), d.get("hbm_gbs", 6650.0), "measured"
+    return 1590.0, 6650.0, "fallback"
+
+
+def ncu_traffic():
+    """DRAM bytes per GEMM launch from the committed ncu summary (profiles/), or None."""
+    p = os.path.join(ROOT, "profiles", "gemm_tc_c2_encoder.md")
+    if not os.path.exists(p):
+        return None
+    m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", open(p).read())
+    return float(m.group(1)) if m else None
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.rows = []
+        self.proc = None
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.gpu), "-lms", "100"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.reader = threading.Thread(target=self._read, daemon=True)
+            self.reader.start()
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([x.strip() for x in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.proc:
+            time.sleep(0.2)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        sm, mx, reasons = [], None, set()
+        for r in self.rows:
+            try:
+                sm.append(float(r[1]))
+                mx = float(r[2])
+                for i, n in enumerate(names):
+                    if r[5 + i].lower().startswith("active"):
+                        reasons.add(n)
+            except (ValueError, IndexError):
+                continue
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
+        load = [s for s in sm if s > 0.5 * max(sm)]
+        return {"sm_mhz": float(np.median(load)), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ CPU baseline (oracle, test infrastructure)
+_CPU_ENCODERS = {}
+
+
+def _cpu_encoder(layers: int, vocab: int):
+    """Oracle encoder with `layers` layers cycling through two distinct random layers (timing does
+    not depend on the weight values; generating 28 distinct layers would dominate the run)."""
+    from oracle import oracle
+    key = (layers, vocab)
+    if key not in _CPU_ENCODERS:
+        c = dict(CFG, layers=layers, vocab=vocab)
+        rng = np.random.default_rng(SEED)
+        d, f = c["hidden"], c["ffn"]
+        nq, nk = c["q_heads"] * 128, c["kv_heads"] * 128
+
+        def bf(shape):
+            return oracle.f32_to_bf16(rng.normal(0, 0.02, shape).astype(np.float32))
+
+        w = {"embedding": bf((vocab, d))}
+        for n, shape in (("q", (nq, d)), ("k", (nk, d)), ("v", (nk, d)), ("o", (d, nq)), ("gate", (f, d)),
+                         ("up", (f, d)), ("down", (d, f))):
+            two = [bf(shape) for _ in range(2)]
+            w[n] = [two[i % 2] for i in range(layers)]
+        for n, size in (("input_norm", d), ("post_norm", d), ("q_norm", 128), ("k_norm", 128)):
+            w[n] = [np.ones(size, np.float32) for _ in range(layers)]
+        w["final_norm"] = np.ones(d, np.float32)
+        _CPU_ENCODERS[key] = oracle.Encoder(c, w)
+    return _CPU_ENCODERS[key]
+
+
+def cpu_sample(threads: int = 0, layers: int = 2, vocab: int = 4096, full_budget_s: float = 0.0):
+    """Times the CPU restatement of the reference path (AVX2 rows<R,Q4> GEMMs, f32 attention) at
+    1024 tokens on `layers` of the 28 layers, scaled to 28; when full_budget_s > 0 and the scaled
+    estimate fits in it, times the full 28-layer forward instead.  Returns (tokens/s, info)."""
+    from oracle import oracle
+    if threads > 0:
+        oracle.set_threads(threads)
+    rng = np.random.default_rng(SEED + 1)
+    ids = rng.integers(0, vocab, TOKENS).astype(np.int32)
+    enc = _cpu_encoder(layers, vocab)
+    enc.forward(ids[:64], mode=2)  # thread-pool warm-up
+    t0 = time.perf_counter()
+    enc.forward(ids, mode=2)
+    dt = time.perf_counter() - t0
+    est_full = dt / layers * CFG["layers"]
+    if full_budget_s > 0 and est_full <= full_budget_s:
+        enc = _cpu_encoder(CFG["layers"], vocab)
+        t0 = time.perf_counter()
+        enc.forward(ids, mode=2)
+        dt = time.perf_counter() - t0
+        return TOKENS / dt, {"cores": oracle.num_threads(), "seconds": dt,
+                             "sample": "one full 28-layer 1024-token Q4 forward (oracle AVX2 path, f32 attention); "
+                                       f"vocab {vocab} embedding table"}
+    return TOKENS / est_full, {"cores": oracle.num_threads(), "seconds": dt,
+                               "sample": f"{layers} of 28 layers of the 1024-token Q4 forward (oracle AVX2 path, "
+                                         f"f32 attention), time scaled to 28 layers; vocab {vocab} embedding table"}
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    steps = []
+    info = {}
+    for i in range(args.warmup + args.steps):
+        v, info = cpu_sample(0, layers=args.cpu_layers)
+        if i >= args.warmup:
+            steps.append(v)
+    value = float(np.median(steps))
+    line = {"metric": METRIC, "value": value, "unit": "tokens/s", "impl": "reference", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": TOKENS / value * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "w4a8 int (f32 fma)",
+            "data": "synthetic", "config": config_json(),
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": info["cores"], "kind": "port",
+                             "sample": info["sample"]},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def config_json():
+    return {"workload": "pplx-q4-encoder-1024tok (BASELINE config 2)", **CFG, "tokens_per_step_per_gpu": TOKENS,
+            "group": 64, "weight_quant": "Q4 absmax g64 f32 scales", "activation_quant": "int8 g64 f32 scales",
+            "l2": f"inputs larger than L2: {q4_weight_bytes(CFG) / 1e6:.0f} MB of Q4 weights streamed per step "
+                  f"(L2 {L2_BYTES >> 20} MiB)"}
+
+
+# ------------------------------------------------------------------ GPU arm
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    import decisive_b200 as db
+
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local_rank))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    cfg = db.EncoderConfig(**CFG, max_sequence_tokens=TOKENS)
+    model = db.Model.synthetic(cfg, seed=SEED, std=0.02, device=local_rank)
+    rng = np.random.default_rng(SEED + rank)
+    ids_host = torch.from_numpy(rng.integers(0, CFG["vocab"], TOKENS).astype(np.int32)).pin_memory()
+    ids_dev = ids_host.cuda()
+    out_dev = torch.empty(CFG["hidden"], dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream()
+
+    for _ in range(args.warmup):
+        model.forward_device(ids_dev, out_dev)
+    torch.cuda.synchronize()
+
+    gpu_index = local_rank
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        parts = vis.split(",")
+        if local_rank < len(parts) and parts[local_rank].strip().isdigit():
+            gpu_index = int(parts[local_rank])
+
+    # ---- device-timed region: K forwards with inputs resident in HBM
+    model.profile(True)
+    model.profile_read(reset=True)
+    with ClockSampler(gpu_index) as clocks:
+        barrier()
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(args.steps):
+            model.forward_device(ids_dev, out_dev)
+        end.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+    ms = start.elapsed_time(end)
+    prof = model.profile_read(reset=True)
+    model.profile(False)
+    ms_max = max_over_ranks(ms)
+    assert np.all(np.isfinite(out_dev.cpu().numpy())), "non-finite embedding"
+    assert db.device_error_word() == 0, "device wait expired"
+    value = world * TOKENS * args.steps / (ms_max / 1e3)
+
+    # ---- end to end through the public API: host ids in (pinned), host embedding out
+    out_host = torch.empty(CFG["hidden"], dtype=torch.float32).pin_memory()
+    ids_np, out_np = ids_host.numpy(), out_host.numpy()
+    for _ in range(2):
+        model.predict(ids_np, out=out_np)
+    barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        model.predict(ids_np, out=out_np)
+    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    barrier()
+    e2e = world * TOKENS * args.steps / e2e_s
+
+    # ---- roofline of the dominant kernel (the grouped GEMM, all four projection shapes)
+    fl = gemm_flops_per_token_layer(CFG)
+    gemm_ms = sum(prof[k][0] for k in fl)
+    gemm_launches = sum(prof[k][1] for k in fl)
+    gemm_flops = sum(fl.values()) * TOKENS * CFG["layers"] * args.steps
+    achieved = gemm_flops / (gemm_ms / 1e3) / 1e12
+    peak_tf, _, peak_kind = measured_peaks()
+    traffic = ncu_traffic()
+    launches = sum(v[1] for v in prof.values())
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "w4a8 int (f16 MMA exact int dots, f32 fma)",
+                "data": "synthetic (seeded N(0,0.02) bf16 weights, uniform token ids)", "config": config_json(),
+                "clocks": clocks.summary(),
+                "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": TOKENS * 4,
+                        "d2h_bytes_per_step": CFG["hidden"] * 4},
+                "gpu_launches": launches,
+                "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
+                             "frac": achieved / peak_tf, "traffic": traffic,
+                             "kernel": "gemm_tc_kernel (all projection launches)",
+                             "peak_kind": f"{peak_kind} bf16 dense burst",
+                             "launches": gemm_launches, "avg_launch_us": gemm_ms / gemm_launches * 1e3,
+                             "flops_per_launch": gemm_flops / gemm_launches},
+                "kernel_ms_per_step": {k: v[0] / args.steps for k, v in prof.items()}}
+        if world == 1 and not args.no_cpu:
+            cpu_v, info = cpu_sample(0, layers=args.cpu_layers, full_budget_s=30.0)
+            line["cpu_baseline"] = {"value": cpu_v, "unit": "tokens/s", "cores": info["cores"], "kind": "port",
+                                    "sample": info["sample"]}
+        print(json.dumps(line), flush=True)
+    model.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-layers", type=int, default=2)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local_rank = int(os.environ.get("LOCAL_RANK", 0))
+    if args.impl == "reference":
+        run_reference(args, rank)
+    else:
+        run_ours(args, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    main()

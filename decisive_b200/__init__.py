@@ -380,6 +380,19 @@ class Model:
                 result.append(Outcome("error", error=Error._from(errs[i])))
         return result
 
+    def profile(self, enable: bool = True):
+        check(load().db_model_profile(self._h, int(enable)))
+
+    def profile_read(self, reset: bool = True) -> dict:
+        """{kernel kind: (total ms, launches)} accumulated since the last reset."""
+        import numpy as np
+        n = 11
+        ms = np.zeros(n, np.float64)
+        cnt = np.zeros(n, np.int64)
+        check(load().db_model_profile_read(self._h, ms.ctypes.data_as(C.c_void_p), cnt.ctypes.data_as(C.c_void_p), n,
+                                           int(reset)))
+        return {load().db_model_profile_name(k).decode(): (float(ms[k]), int(cnt[k])) for k in range(n)}
+
     def forward_device(self, ids_dev, out_dev, stream=None):
         """Device-resident forward (no host synchronisation) used for device-timed measurement."""
         check(load().db_forward_device(self._h, _ptr(ids_dev), ids_dev.numel(), _ptr(out_dev), _stream(stream)))

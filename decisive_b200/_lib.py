@@ -74,6 +74,9 @@ SIGNATURES = [
     ("db_predict_batch", _i32, [_vp, _vp, _vp, _sz, C.POINTER(Parameters), _vp, _vp, _vp, _vp, _vp,
                                 C.POINTER(DbError)]),
     ("db_forward_device", _i32, [_vp, _vp, _i64, _vp, _vp]),
+    ("db_model_profile", _i32, [_vp, _i32]),
+    ("db_model_profile_read", _i32, [_vp, _vp, _vp, _i32, _i32]),
+    ("db_model_profile_name", C.c_char_p, [_i32]),
 ]
 
 _lib = None

@@ -43,6 +43,10 @@ void fill_error(db_error* err, const char* code, const std::string& msg) {
 
 }  // namespace
 
+static const char* kProfNames[DB_PROF_KINDS] = {"dequant_rows", "rms_quantize", "gemm_qkv", "qk_norm_rope",
+                                                "attention", "quantize_rows", "gemm_o", "gemm_mlp_swiglu",
+                                                "gemm_down", "final_norm", "mean_pool"};
+
 struct db_model {
     int device = 0;
     db_encoder_config cfg{};
@@ -65,6 +69,23 @@ struct db_model {
     int32_t* ids = nullptr;
     int* flag = nullptr;
     int* dev_err = nullptr;
+    // per-launch CUDA-event profiling (mirror of the reference's projection_ms accounting,
+    // cpu.rs:8-16 / native.rs:229-258), enabled by db_model_profile
+    bool profile = false;
+    std::vector<cudaEvent_t> ev_pool;
+    size_t ev_next = 0;
+    struct Rec { int kind; cudaEvent_t a, b; };
+    std::vector<Rec> recs;
+    double prof_ms[DB_PROF_KINDS] = {};
+    int64_t prof_n[DB_PROF_KINDS] = {};
+    cudaEvent_t next_event() {
+        if (ev_next == ev_pool.size()) {
+            cudaEvent_t e;
+            cudaEventCreate(&e);
+            ev_pool.push_back(e);
+        }
+        return ev_pool[ev_next++];
+    }
 
     int D() const { return cfg.hidden; }
     int Nq() const { return cfg.q_heads * cfg.head_dim; }
@@ -237,8 +258,19 @@ int enqueue_forward(db_model* m, int T, const volatile int32_t* cancel) {
     cudaStream_t st = m->stream;
     const int64_t ld_codes = m->Kmax(), lds = m->cap_T;
     int rc = 0;
+    auto timed = [&](int kind, auto&& launch) -> int {
+        if (!m->profile) return launch();
+        cudaEvent_t a = m->next_event(), b = m->next_event();
+        cudaEventRecord(a, st);
+        const int r = launch();
+        cudaEventRecord(b, st);
+        m->recs.push_back({kind, a, b});
+        return r;
+    };
     cudaMemsetAsync(m->flag, 0, sizeof(int), st);
-    rc = db_launch_dequant_rows(m->emb_c, m->emb_s, c.vocab, D, bits, m->ids, T, m->x, D, m->flag, st);
+    rc = timed(0, [&] {
+        return db_launch_dequant_rows(m->emb_c, m->emb_s, c.vocab, D, bits, m->ids, T, m->x, D, m->flag, st);
+    });
     auto gemm = [&](const void* a, const uint8_t* wc, const float* ws, const float* sa, int N, int K, int epi, float* y,
                     int64_t ldy) {
         DbGemmArgs g{};
@@ -268,22 +300,34 @@ int enqueue_forward(db_model* m, int T, const volatile int32_t* cancel) {
     for (int l = 0; l < c.layers && !rc; ++l) {
         if (cancel && *cancel) return 1;
         const LayerW& w = m->layers[l];
-        rc = db_launch_rms_quantize(m->x, D, w.in_norm, T, D, c.eps, 0, nullptr, 0, m->acodes, DB_CODES_TC, ld_codes,
-                                    m->sa, nullptr, lds, m->flag, st);
-        if (!rc) rc = gemm(m->acodes, w.qkv_c, w.qkv_s, m->sa, Nqkv, D, DB_EPI_STORE, m->qkv, Nqkv);
+        rc = timed(1, [&] {
+            return db_launch_rms_quantize(m->x, D, w.in_norm, T, D, c.eps, 0, nullptr, 0, m->acodes, DB_CODES_TC,
+                                          ld_codes, m->sa, nullptr, lds, m->flag, st);
+        });
+        if (!rc) rc = timed(2, [&] { return gemm(m->acodes, w.qkv_c, w.qkv_s, m->sa, Nqkv, D, DB_EPI_STORE, m->qkv, Nqkv); });
         if (!rc)
-            rc = db_launch_qk_norm_rope(m->qkv, Nqkv, T, c.q_heads, c.kv_heads, w.q_norm, w.k_norm, c.eps, m->cos_t,
-                                        m->sin_t, m->q16, m->k16, m->v16, st);
-        if (!rc) rc = db_launch_attention(m->q16, m->k16, m->v16, T, c.q_heads, c.kv_heads, attn_scale, m->ctx, Nq, st);
+            rc = timed(3, [&] {
+                return db_launch_qk_norm_rope(m->qkv, Nqkv, T, c.q_heads, c.kv_heads, w.q_norm, w.k_norm, c.eps,
+                                              m->cos_t, m->sin_t, m->q16, m->k16, m->v16, st);
+            });
         if (!rc)
-            rc = db_launch_quantize_rows(m->ctx, DB_F32, Nq, T, Nq, 8, m->acodes, DB_CODES_TC, ld_codes, m->sa, nullptr,
-                                         lds, m->flag, st);
-        if (!rc) rc = gemm(m->acodes, w.o_c, w.o_s, m->sa, D, Nq, DB_EPI_RESIDUAL, m->x, D);
+            rc = timed(4, [&] {
+                return db_launch_attention(m->q16, m->k16, m->v16, T, c.q_heads, c.kv_heads, attn_scale, m->ctx, Nq, st);
+            });
         if (!rc)
-            rc = db_launch_rms_quantize(m->x, D, w.post_norm, T, D, c.eps, 0, nullptr, 0, m->acodes, DB_CODES_TC,
-                                        ld_codes, m->sa, nullptr, lds, m->flag, st);
-        if (!rc) rc = gemm(m->acodes, w.gu_c, w.gu_s, m->sa, 2 * F, D, DB_EPI_SWIGLU_QUANT, nullptr, 0);
-        if (!rc) {
+            rc = timed(5, [&] {
+                return db_launch_quantize_rows(m->ctx, DB_F32, Nq, T, Nq, 8, m->acodes, DB_CODES_TC, ld_codes, m->sa,
+                                               nullptr, lds, m->flag, st);
+            });
+        if (!rc) rc = timed(6, [&] { return gemm(m->acodes, w.o_c, w.o_s, m->sa, D, Nq, DB_EPI_RESIDUAL, m->x, D); });
+        if (!rc)
+            rc = timed(1, [&] {
+                return db_launch_rms_quantize(m->x, D, w.post_norm, T, D, c.eps, 0, nullptr, 0, m->acodes, DB_CODES_TC,
+                                              ld_codes, m->sa, nullptr, lds, m->flag, st);
+            });
+        if (!rc)
+            rc = timed(7, [&] { return gemm(m->acodes, w.gu_c, w.gu_s, m->sa, 2 * F, D, DB_EPI_SWIGLU_QUANT, nullptr, 0); });
+        if (!rc) rc = timed(8, [&] {
             DbGemmArgs g{};
             g.a_codes = m->hcodes;
             g.lda = F;
@@ -301,13 +345,15 @@ int enqueue_forward(db_model* m, int T, const volatile int32_t* cancel) {
             g.ldy = D;
             g.nonfinite = m->flag;
             g.dev_error = m->dev_err;
-            rc = db_launch_gemm_tc(g, st);
-        }
+            return db_launch_gemm_tc(g, st);
+        });
     }
     if (!rc)
-        rc = db_launch_rms_quantize(m->x, D, m->final_norm, T, D, c.eps, 0, m->normed, D, nullptr, DB_CODES_TC, 0,
-                                    nullptr, nullptr, 0, m->flag, st);
-    if (!rc) rc = db_launch_mean_pool(m->normed, D, T, D, m->pooled, st);
+        rc = timed(9, [&] {
+            return db_launch_rms_quantize(m->x, D, m->final_norm, T, D, c.eps, 0, m->normed, D, nullptr, DB_CODES_TC, 0,
+                                          nullptr, nullptr, 0, m->flag, st);
+        });
+    if (!rc) rc = timed(10, [&] { return db_launch_mean_pool(m->normed, D, T, D, m->pooled, st); });
     return rc ? db_cuda_status(rc, "forward") : 0;
 }
 
@@ -423,6 +469,7 @@ void db_model_destroy(db_model* m) {
     m->free_all(m->ws_allocations);
     m->free_all(m->allocations);
     if (m->stream) cudaStreamDestroy(m->stream);
+    for (cudaEvent_t e : m->ev_pool) cudaEventDestroy(e);
     delete m;
 }
 
@@ -490,6 +537,37 @@ int db_predict_batch(db_model* m, const int32_t* const* ids, const size_t* lens,
                                 errs ? &errs[i] : nullptr);
     return 0;
 }
+
+int db_model_profile(db_model* m, int enable) {
+    if (!m) return DB_ERR_INVALID_ARGUMENT;
+    m->profile = enable != 0;
+    return DB_OK;
+}
+
+int db_model_profile_read(db_model* m, double* ms, int64_t* counts, int n, int reset) {
+    if (!m || n < DB_PROF_KINDS) return DB_ERR_INVALID_ARGUMENT;
+    cudaSetDevice(m->device);
+    if (cudaStreamSynchronize(m->stream) != cudaSuccess) return db_cuda_status(1, "profile sync");
+    for (auto& r : m->recs) {
+        float t = 0.f;
+        cudaEventElapsedTime(&t, r.a, r.b);
+        m->prof_ms[r.kind] += t;
+        m->prof_n[r.kind] += 1;
+    }
+    m->recs.clear();
+    m->ev_next = 0;
+    for (int k = 0; k < DB_PROF_KINDS; ++k) {
+        if (ms) ms[k] = m->prof_ms[k];
+        if (counts) counts[k] = m->prof_n[k];
+        if (reset) {
+            m->prof_ms[k] = 0;
+            m->prof_n[k] = 0;
+        }
+    }
+    return DB_OK;
+}
+
+const char* db_model_profile_name(int kind) { return kind >= 0 && kind < DB_PROF_KINDS ? kProfNames[kind] : ""; }
 
 int db_forward_device(db_model* m, const int32_t* ids_dev, int64_t n, float* out_dev, void* stream) {
     if (!m || !ids_dev || n <= 0 || !out_dev)

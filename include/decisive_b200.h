@@ -203,6 +203,15 @@ int db_predict_batch(db_model *m, const int32_t *const *ids, const size_t *lens,
                      const db_parameters *params, db_cache *cache, const volatile int32_t *cancel, float *outs,
                      int32_t *status, db_error *errs, db_error *err);
 
+/* Per-launch CUDA-event timing of the forward's kernels (the reference's projection_ms
+ * accounting, cpu.rs:8-16).  Kinds 0..DB_PROF_KINDS-1, named by db_model_profile_name.
+ * db_model_profile_read synchronises the model's stream and returns accumulated ms and
+ * launch counts per kind. */
+#define DB_PROF_KINDS 11
+int db_model_profile(db_model *m, int enable);
+int db_model_profile_read(db_model *m, double *ms, int64_t *counts, int n, int reset);
+const char *db_model_profile_name(int kind);
+
 /* Device-resident variant for throughput measurement: ids already on the device, output left on
  * the device; no host synchronisation.  Used by bench.py's device-timed leg. */
 int db_forward_device(db_model *m, const int32_t *ids_dev, int64_t n, float *out_dev, void *stream);
