@@ -37,6 +37,11 @@ def padded(k: int) -> int:
     return (k + GROUP - 1) // GROUP * GROUP
 
 
+def scale_stride(n: int) -> int:
+    """Row stride of scale arrays: roundup(n, 128) (db_scale_row_stride)."""
+    return (n + 127) // 128 * 128
+
+
 # ------------------------------------------------------------------ kernel level
 def quantize_activations(x, bits: int = 8, layout: int = CODES_TC, sums: bool = False, nonfinite=None):
     """int8::Matrix::prepare (int8.rs:178-202) on the GPU -> (codes, scales [G, M], sums [G, M] | None)."""
@@ -47,10 +52,11 @@ def quantize_activations(x, bits: int = 8, layout: int = CODES_TC, sums: bool = 
     G = Kp // GROUP
     dt = torch.float16 if layout == CODES_TC else torch.int8
     codes = torch.zeros((M, Kp), dtype=dt, device=x.device)
-    scales = torch.zeros((G, max(M, 1)), dtype=torch.float32, device=x.device)
-    s = torch.zeros((G, max(M, 1)), dtype=torch.int32, device=x.device) if sums else None
+    lds = scale_stride(max(M, 1))
+    scales = torch.zeros((G, lds), dtype=torch.float32, device=x.device)
+    s = torch.zeros((G, lds), dtype=torch.int32, device=x.device) if sums else None
     check(load().db_quantize_activations_g64(_ptr(x), DTYPES[str(x.dtype).split(".")[1]], x.stride(0), M, K, bits,
-                                             _ptr(codes), layout, Kp, _ptr(scales), _ptr(s), max(M, 1),
+                                             _ptr(codes), layout, Kp, _ptr(scales), _ptr(s), lds,
                                              _ptr(nonfinite), _stream()))
     return codes, scales, s
 
@@ -62,7 +68,7 @@ def pack_weights(bf16, bits: int = 4):
     N, K = bf16.shape
     Kp = padded(K)
     codes = torch.empty((N, Kp * bits // 8), dtype=torch.uint8, device=bf16.device)
-    scales = torch.empty((Kp // GROUP, N), dtype=torch.float32, device=bf16.device)
+    scales = torch.empty((Kp // GROUP, scale_stride(N)), dtype=torch.float32, device=bf16.device)
     check(load().db_pack_weights_g64(_ptr(bf16), N, K, bits, _ptr(codes), _ptr(scales), _stream()))
     return codes, scales
 
@@ -70,7 +76,7 @@ def pack_weights(bf16, bits: int = 4):
 def import_packed(packed, N: int, K: int, bits: int):
     import torch
     codes = torch.empty((N, K * bits // 8), dtype=torch.uint8, device=packed.device)
-    scales = torch.empty((K // GROUP, N), dtype=torch.float32, device=packed.device)
+    scales = torch.empty((K // GROUP, scale_stride(N)), dtype=torch.float32, device=packed.device)
     check(load().db_import_packed(_ptr(packed), N, K, bits, _ptr(codes), _ptr(scales), _stream()))
     return codes, scales
 
@@ -124,7 +130,7 @@ def project_packed(x, w_codes, sw, outputs: int, bits: int):
 def interleave_gate_up(gate_codes, gate_scales, up_codes, up_scales, F: int, K: int, bits: int):
     import torch
     codes = torch.empty((2 * F, gate_codes.shape[1]), dtype=torch.uint8, device=gate_codes.device)
-    scales = torch.empty((gate_scales.shape[0], 2 * F), dtype=torch.float32, device=gate_codes.device)
+    scales = torch.empty((gate_scales.shape[0], scale_stride(2 * F)), dtype=torch.float32, device=gate_codes.device)
     check(load().db_interleave_gate_up(_ptr(gate_codes), _ptr(gate_scales), _ptr(up_codes), _ptr(up_scales), F, K,
                                        bits, _ptr(codes), _ptr(scales), _stream()))
     return codes, scales
@@ -134,9 +140,10 @@ def mlp(a_codes, sa, gu_codes, gu_scales, M: int, F: int, K: int, bits: int, fus
     """Fused gate/up + SiLU*up + re-quantisation (grouped_q4_mlp.wgsl) -> (codes TC [M, F], scales [F/64, M])."""
     import torch
     codes = torch.zeros((M, F), dtype=torch.float16, device=a_codes.device)
-    scales = torch.zeros((F // GROUP, M), dtype=torch.float32, device=a_codes.device)
+    scales = torch.zeros((F // GROUP, scale_stride(M)), dtype=torch.float32, device=a_codes.device)
     check(load().db_mlp_g64(_ptr(a_codes), a_codes.stride(0), _ptr(sa), sa.stride(0), _ptr(gu_codes), _ptr(gu_scales),
-                            M, F, K, bits, int(fused), _ptr(codes), F, _ptr(scales), M, _ptr(nonfinite), _stream()))
+                            M, F, K, bits, int(fused), _ptr(codes), F, _ptr(scales), scale_stride(M), _ptr(nonfinite),
+                            _stream()))
     return codes, scales
 
 

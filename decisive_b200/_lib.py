@@ -43,6 +43,7 @@ class EncoderWeights(C.Structure):
 
 SIGNATURES = [
     ("db_abi_version", _i32, []),
+    ("db_scale_row_stride", _i64, [_i64]),
     ("db_last_error_code", C.c_char_p, []),
     ("db_last_error_message", C.c_char_p, []),
     ("db_device_count", _i32, []),

@@ -172,8 +172,10 @@ int db_gemm_g64(const void* a_codes, int layout, int64_t lda, const float* sa, c
 size_t db_linear_workspace_bytes(int64_t M, int64_t K) {
     const int64_t G = groups_of(K), Kp = G * DB_GROUP;
     auto up = [](size_t b) { return (b + 255) / 256 * 256; };
-    return up((size_t)M * Kp * 2) + 2 * up((size_t)G * M * 4) + 256;
+    return up((size_t)M * Kp * 2) + 2 * up((size_t)G * db_scale_stride(M) * 4) + 256;
 }
+
+int64_t db_scale_row_stride(int64_t n) { return db_scale_stride(n); }
 
 int db_linear_g64(const float* x, int64_t M, int64_t K, const uint8_t* w_codes, const float* sw, int64_t N,
                   int weight_bits, int activation_bits, int fused, float* y, void* workspace, void* stream) {
@@ -185,16 +187,17 @@ int db_linear_g64(const float* x, int64_t M, int64_t K, const uint8_t* w_codes, 
     auto up = [](size_t b) { return (b + 255) / 256 * 256; };
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     void* codes = ws;
+    const int64_t lds = db_scale_stride(M);
     float* sa = reinterpret_cast<float*>(ws + up((size_t)M * Kp * 2));
-    int32_t* sums = reinterpret_cast<int32_t*>(ws + up((size_t)M * Kp * 2) + up((size_t)G * M * 4));
-    int* flag = reinterpret_cast<int*>(ws + up((size_t)M * Kp * 2) + 2 * up((size_t)G * M * 4));
+    int32_t* sums = reinterpret_cast<int32_t*>(ws + up((size_t)M * Kp * 2) + up((size_t)G * lds * 4));
+    int* flag = reinterpret_cast<int*>(ws + up((size_t)M * Kp * 2) + 2 * up((size_t)G * lds * 4));
     cudaMemsetAsync(flag, 0, sizeof(int), S(stream));
     const bool gemv = M <= db_gemv_rows_limit();
     const int layout = gemv ? DB_CODES_GEMV : DB_CODES_TC;
     int rc = db_quantize_activations_g64(x, DB_DTYPE_F32, K, M, K, activation_bits, codes, layout, Kp, sa,
-                                         gemv ? sums : nullptr, M, flag, stream);
+                                         gemv ? sums : nullptr, lds, flag, stream);
     if (rc) return rc;
-    return db_gemm_g64(codes, layout, Kp, sa, sums, M, w_codes, sw, M, N, K, weight_bits, fused, 0, y, N, flag,
+    return db_gemm_g64(codes, layout, Kp, sa, sums, lds, w_codes, sw, M, N, K, weight_bits, fused, 0, y, N, flag,
                        stream);
 }
 
@@ -207,7 +210,7 @@ int db_project_packed(const float* x, int64_t K, const uint8_t* w_codes, const f
     const int64_t G = K / DB_GROUP, Kp = K;
     auto up = [](size_t b) { return (b + 255) / 256 * 256; };
     const int* flag = reinterpret_cast<const int*>(static_cast<uint8_t*>(workspace) + up((size_t)Kp * 2) +
-                                                   2 * up((size_t)G * 4));
+                                                   2 * up((size_t)G * db_scale_stride(1) * 4));
     int h = 0;
     cudaMemcpyAsync(&h, flag, sizeof(int), cudaMemcpyDeviceToHost, S(stream));
     int e = (int)cudaStreamSynchronize(S(stream));
@@ -219,7 +222,8 @@ int db_project_packed(const float* x, int64_t K, const uint8_t* w_codes, const f
 int db_mlp_g64(const void* a_codes, int64_t lda, const float* sa, int64_t ldsa, const uint8_t* w_gu_codes,
                const float* w_gu_scales, int64_t M, int64_t F, int64_t K, int bits, int fused, void* out_codes,
                int64_t ldoc, float* out_scales, int64_t ldos, const int* nonfinite, void* stream) {
-    if (M < 0 || F <= 0 || F % DB_GROUP || K <= 0 || (bits != 4 && bits != 8) || ldoc < F || ldos < M)
+    if (M < 0 || F <= 0 || F % DB_GROUP || K <= 0 || (bits != 4 && bits != 8) || ldoc < F ||
+        ldos < db_scale_stride(M) || (ldos & 3))
         return db_fail(DB_ERR_INVALID_ARGUMENT, "INVALID_ARGUMENT", "mlp: bad shape");
     if (M == 0) return DB_OK;
     DbGemmArgs a{};
@@ -257,7 +261,7 @@ __global__ void interleave_kernel(const uint8_t* __restrict__ gc, const float* _
     const uint8_t* s = (is_up ? uc : gc) + (size_t)src * row_bytes;
     for (int i = threadIdx.x; i < row_bytes; i += blockDim.x) oc[(size_t)row * row_bytes + i] = s[i];
     for (int g = threadIdx.x; g < G; g += blockDim.x)
-        os[(size_t)g * 2 * F + row] = (is_up ? us : gs)[(size_t)g * F + src];
+        os[(size_t)g * db_scale_stride(2 * F) + row] = (is_up ? us : gs)[(size_t)g * db_scale_stride(F) + src];
 }
 
 __device__ __forceinline__ uint64_t mix64(uint64_t x) {
@@ -289,6 +293,7 @@ int db_interleave_gate_up(const uint8_t* gate_codes, const float* gate_scales, c
     if (F <= 0 || F % DB_GROUP || K <= 0 || (bits != 4 && bits != 8))
         return db_fail(DB_ERR_INVALID_ARGUMENT, "INVALID_ARGUMENT", "interleave: F must be a multiple of 64");
     const int G = (int)groups_of(K), row_bytes = G * DB_GROUP * bits / 8;
+    cudaMemsetAsync(out_scales, 0, (size_t)G * db_scale_stride(2 * F) * sizeof(float), S(stream));
     interleave_kernel<<<(unsigned)(2 * F), 128, 0, S(stream)>>>(gate_codes, gate_scales, up_codes, up_scales, (int)F,
                                                                   G, row_bytes, out_codes, out_scales);
     return db_cuda_status((int)cudaGetLastError(), "interleave");

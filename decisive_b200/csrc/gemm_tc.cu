@@ -33,6 +33,8 @@ constexpr int BK = 64;
 constexpr int A_STAGES = 4;
 constexpr int W_STAGES = 4;
 constexpr int B_STAGES = 3;
+constexpr int S_STAGES = 6;   // per-group scale vectors (sa: 128 rows, sw: BN columns)
+constexpr int NUM_ACC = 4;    // TMEM accumulator buffers (4 x BN columns <= 512)
 constexpr int NUM_THREADS = 448;
 constexpr int CONVERTER_WARP0 = 2;
 constexpr int EPILOGUE_WARP0 = 6;
@@ -45,12 +47,14 @@ struct GemmSmem {
     static constexpr int W_ROW = BK * BITS / 8;          // 32 or 64 bytes of raw codes per row
     static constexpr int W_BYTES = BN * W_ROW;
     static constexpr int XCH_BYTES = EPI == DB_EPI_SWIGLU_QUANT ? BM * XCH_STRIDE * 4 : 0;
+    static constexpr int S_BYTES = (BM + BN) * 4;        // sa then sw of one group
     static constexpr int OFF_A = 0;
     static constexpr int OFF_B = OFF_A + A_STAGES * A_BYTES;
     static constexpr int OFF_W = OFF_B + B_STAGES * B_BYTES;
-    static constexpr int OFF_X = OFF_W + W_STAGES * W_BYTES;
+    static constexpr int OFF_S = OFF_W + W_STAGES * W_BYTES;
+    static constexpr int OFF_X = OFF_S + S_STAGES * S_BYTES;
     static constexpr int OFF_BAR = (OFF_X + XCH_BYTES + 15) / 16 * 16;
-    static constexpr int NUM_BARS = 2 * A_STAGES + 2 * W_STAGES + 2 * B_STAGES + 6;
+    static constexpr int NUM_BARS = 2 * A_STAGES + 2 * W_STAGES + 2 * B_STAGES + 2 * S_STAGES + 2 * NUM_ACC + 2;
     static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
     static constexpr int BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
 };
@@ -113,7 +117,8 @@ __device__ __forceinline__ float silu_ref(float x) {
 template <int BN, int BITS, int EPI, bool FUSED>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
-                   const float* __restrict__ sa, int64_t ldsa, const float* __restrict__ sw, int M, int N, int G,
+                   const float* __restrict__ sa, int64_t ldsa, const float* __restrict__ sw, int64_t ldsw, int M,
+                   int N, int G,
                    float* __restrict__ y, int64_t ldy, __half* __restrict__ out_codes, int64_t ldoc,
                    float* __restrict__ out_scales, int64_t ldos, const int* __restrict__ nonfinite,
                    int* __restrict__ dev_error) {
@@ -127,9 +132,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     uint64_t* w_empty = w_full + W_STAGES;
     uint64_t* b_full = w_empty + W_STAGES;
     uint64_t* b_empty = b_full + B_STAGES;
-    uint64_t* acc_full = b_empty + B_STAGES;
-    uint64_t* acc_empty = acc_full + 2;
-    uint64_t* xch_full = acc_empty + 2;   // SwiGLU exchange: up half -> gate half
+    uint64_t* s_full = b_empty + B_STAGES;
+    uint64_t* s_empty = s_full + S_STAGES;
+    uint64_t* acc_full = s_empty + S_STAGES;
+    uint64_t* acc_empty = acc_full + NUM_ACC;
+    uint64_t* xch_full = acc_empty + NUM_ACC;   // SwiGLU exchange: up half -> gate half
     uint64_t* xch_empty = xch_full + 1;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::OFF_MISC);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + S::OFF_MISC + 4);
@@ -142,7 +149,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         for (int i = 0; i < A_STAGES; ++i) { mbar_init(&a_full[i], 1); mbar_init(&a_empty[i], 1); }
         for (int i = 0; i < W_STAGES; ++i) { mbar_init(&w_full[i], 1); mbar_init(&w_empty[i], 4); }
         for (int i = 0; i < B_STAGES; ++i) { mbar_init(&b_full[i], 4); mbar_init(&b_empty[i], 1); }
-        for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], 8); }
+        for (int i = 0; i < S_STAGES; ++i) { mbar_init(&s_full[i], 1); mbar_init(&s_empty[i], 8); }
+        for (int i = 0; i < NUM_ACC; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], 8); }
         mbar_init(xch_full, 4);
         mbar_init(xch_empty, 4);
         *abort_flag = 0;
@@ -153,7 +161,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tma_prefetch_desc(&tmW);
     }
     if (warp == 1) {
-        tmem_alloc(tmem_slot, 2 * BN);
+        tmem_alloc(tmem_slot, NUM_ACC * BN);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -164,11 +172,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (warp == 0) {
         // ---------------------------------------------------------------- TMA producer
         if (lane == 0) {
-            int ia = 0, iw = 0;
-            uint32_t pa = 0, pw = 0;
+            int ia = 0, iw = 0, is = 0;
+            uint32_t pa = 0, pw = 0, ps = 0;
             for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
                 const int m0 = (tile % m_tiles) * BM, n0 = (tile / m_tiles) * BN;
                 for (int g = 0; g < G; ++g) {
+                    if (!mbar_wait(&s_empty[is], ps ^ 1u, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_TMA)) goto done;
+                    mbar_arrive_expect_tx(&s_full[is], S::S_BYTES);
+                    {
+                        uint8_t* slot = smem + S::OFF_S + is * S::S_BYTES;
+                        bulk_load(slot, sa + (size_t)g * ldsa + m0, BM * 4, &s_full[is]);
+                        bulk_load(slot + BM * 4, sw + (size_t)g * ldsw + n0, BN * 4, &s_full[is]);
+                    }
+                    if (++is == S_STAGES) { is = 0; ps ^= 1u; }
                     if (!mbar_wait(&a_empty[ia], pa ^ 1u, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_TMA)) goto done;
                     mbar_arrive_expect_tx(&a_full[ia], S::A_BYTES);
                     tma_load_2d(smem + S::OFF_A + ia * S::A_BYTES, &tmA, &a_full[ia], g * BK, m0);
@@ -203,7 +219,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     umma_commit(&acc_full[ic]);
                     if (++ia == A_STAGES) { ia = 0; pa ^= 1u; }
                     if (++ib == B_STAGES) { ib = 0; pb ^= 1u; }
-                    if (++ic == 2) { ic = 0; pc ^= 1u; }
+                    if (++ic == NUM_ACC) { ic = 0; pc ^= 1u; }
                 }
             }
         }
@@ -257,35 +273,31 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int col0 = half * COLS;
         const bool any_nonfinite = nonfinite != nullptr && *nonfinite != 0;
         float* xch = reinterpret_cast<float*>(smem + S::OFF_X);
-        int ic = 0;
-        uint32_t pc = 0, px = 0;
+        int ic = 0, is = 0;
+        uint32_t pc = 0, ps = 0, px = 0;
         for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
             const int m0 = (tile % m_tiles) * BM, n0 = (tile / m_tiles) * BN;
             const int m = m0 + r;
-            const bool full_cols = (n0 + BN <= N) && ((N & 3) == 0);
+            const bool full_cols = n0 + BN <= N;
             float acc[COLS];
 #pragma unroll
             for (int j = 0; j < COLS; ++j) acc[j] = 0.f;
             for (int g = 0; g < G; ++g) {
+                if (!warp_wait(&s_full[is], ps, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_EPI)) goto done;
                 if (!warp_wait(&acc_full[ic], pc, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_EPI)) goto done;
                 tc_fence_after();
-                const float s_a = m < M ? __ldg(sa + (size_t)g * ldsa + m) : 0.f;
-                const float* swp = sw + (size_t)g * N + n0 + col0;
+                const float* slot = reinterpret_cast<const float*>(smem + S::OFF_S + is * S::S_BYTES);
+                const float s_a = slot[r];
+                const float* swp = slot + BM + col0;
 #pragma unroll
                 for (int c = 0; c < CHUNKS; ++c) {
                     uint32_t v[32];
                     tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ic * BN + col0 + c * 32), v);
                     float swv[32];
-                    if (full_cols) {
 #pragma unroll
-                        for (int j = 0; j < 32; j += 4) {
-                            float4 t = __ldg(reinterpret_cast<const float4*>(swp + c * 32 + j));
-                            swv[j] = t.x; swv[j + 1] = t.y; swv[j + 2] = t.z; swv[j + 3] = t.w;
-                        }
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < 32; ++j)
-                            swv[j] = (n0 + col0 + c * 32 + j < N) ? __ldg(swp + c * 32 + j) : 0.f;
+                    for (int j = 0; j < 32; j += 4) {
+                        const float4 t = *reinterpret_cast<const float4*>(swp + c * 32 + j);
+                        swv[j] = t.x; swv[j + 1] = t.y; swv[j + 2] = t.z; swv[j + 3] = t.w;
                     }
                     tmem_wait_ld();
 #pragma unroll
@@ -297,8 +309,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 }
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&acc_empty[ic]);
-                if (++ic == 2) { ic = 0; pc ^= 1u; }
+                if (lane == 0) {
+                    mbar_arrive(&acc_empty[ic]);
+                    mbar_arrive(&s_empty[is]);
+                }
+                if (++ic == NUM_ACC) { ic = 0; pc ^= 1u; }
+                if (++is == S_STAGES) { is = 0; ps ^= 1u; }
             }
             if (EPI == DB_EPI_SWIGLU_QUANT) {
                 // half 1 holds the up projection of the same 64 features: hand it to half 0.
@@ -341,7 +357,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             } else if (m < M) {
                 float* dst = y + (size_t)m * ldy + n0 + col0;
                 const float nanv = __int_as_float(0x7fc00000);
-                if (full_cols && (ldy & 3) == 0) {
+                if (full_cols && (ldy & 3) == 0 && (N & 3) == 0) {
 #pragma unroll
                     for (int j = 0; j < COLS; j += 4) {
                         float4 o = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
@@ -370,7 +386,7 @@ done:
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, 2 * BN);
+        tmem_dealloc(tmem_base, NUM_ACC * BN);
     }
 }
 
@@ -420,7 +436,8 @@ static int launch_variant(const DbGemmArgs& a, const CUtensorMap& tmA, const CUt
     const int tiles = ((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN);
     int ctas = a.max_ctas > 0 ? a.max_ctas : db_num_sms();
     if (ctas > tiles) ctas = tiles;
-    kernel<<<ctas, NUM_THREADS, S::BYTES, stream>>>(tmA, tmW, a.sa, a.ldsa, a.sw, a.M, a.N, G, a.y, a.ldy,
+    kernel<<<ctas, NUM_THREADS, S::BYTES, stream>>>(tmA, tmW, a.sa, a.ldsa, a.sw, db_scale_stride(a.N), a.M, a.N, G,
+                                                    a.y, a.ldy,
                                                     static_cast<__half*>(a.out_codes), a.ldoc, a.out_scales, a.ldos,
                                                     a.nonfinite, a.dev_error);
     return (int)cudaGetLastError();
@@ -451,7 +468,8 @@ int db_launch_gemm_tc(const DbGemmArgs& a, cudaStream_t stream) {
     if (a.epilogue == DB_EPI_SWIGLU_QUANT) bn = 128;
     if (bn != 64 && bn != 128) return (int)cudaErrorInvalidValue;
     if ((reinterpret_cast<uintptr_t>(a.a_codes) & 15) || (a.lda * 2) % 16 || a.lda < Kp ||
-        (reinterpret_cast<uintptr_t>(a.w_codes) & 15))
+        (reinterpret_cast<uintptr_t>(a.w_codes) & 15) || (reinterpret_cast<uintptr_t>(a.sa) & 15) ||
+        (reinterpret_cast<uintptr_t>(a.sw) & 15) || a.ldsa < db_scale_stride(a.M) || (a.ldsa & 3))
         return (int)cudaErrorMisalignedAddress;
     CUtensorMap tmA, tmW;
     {

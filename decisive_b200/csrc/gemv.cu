@@ -113,7 +113,7 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32)
         for (int g = 0; g < G; ++g) {
             const float d = (float)dots[warp][r][g];
             const float s_a = __ldg(sa + (size_t)g * ldsa + r);
-            const float s_w = __ldg(sw + (size_t)g * N + n);
+            const float s_w = __ldg(sw + (size_t)g * db_scale_stride(N) + n);
             if (FUSED) acc = __fmaf_rn(d, __fmul_rn(s_w, s_a), acc);
             else acc = __fadd_rn(acc, __fmul_rn(d, __fmul_rn(s_a, s_w)));
         }

@@ -3,6 +3,10 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+// Scale vectors are stored with a row stride padded to 128 entries ([G, db_scale_stride(N)]) so
+// that every 128-wide tile of one group is a 16-byte aligned, in-bounds bulk copy.
+__host__ __device__ inline int64_t db_scale_stride(int64_t n) { return (n + 127) / 128 * 128; }
+
 // element types of activation inputs
 enum { DB_F32 = 0, DB_F16 = 1, DB_BF16 = 2 };
 // activation code layouts

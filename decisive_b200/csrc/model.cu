@@ -130,7 +130,7 @@ int check_config(const db_encoder_config* c, db_error* err) {
 int pack(db_model* m, const uint16_t* bf16, int N, int K, uint8_t** codes, float** scales) {
     const int G = (K + 63) / 64;
     if (m->alloc(codes, (size_t)N * G * 64 * m->cfg.weight_bits / 8, m->allocations) ||
-        m->alloc(scales, (size_t)G * N, m->allocations))
+        m->alloc(scales, (size_t)G * db_scale_stride(N), m->allocations))
         return db_fail(DB_ERR_CUDA, "RESOURCE_LIMIT", "weight allocation exceeds device limits");
     return db_pack_weights_g64(bf16, N, K, m->cfg.weight_bits, *codes, *scales, m->stream);
 }
@@ -153,7 +153,7 @@ int ensure_workspace(db_model* m, int T) {
     if (m->alloc(&m->x, (size_t)T * D, v) || m->alloc(&m->qkv, (size_t)T * m->Nqkv(), v) ||
         m->alloc(&m->ctx, (size_t)T * m->Nq(), v) || m->alloc(&m->normed, (size_t)T * D, v) ||
         m->alloc(&m->pooled, D, v) || m->alloc(&m->cos_t, (size_t)T * 64, v) || m->alloc(&m->sin_t, (size_t)T * 64, v) ||
-        m->alloc(&m->sa, (size_t)Gmax * T, v) || m->alloc(&m->sh, (size_t)(F / 64) * T, v) ||
+        m->alloc(&m->sa, (size_t)Gmax * db_scale_stride(T), v) || m->alloc(&m->sh, (size_t)(F / 64) * db_scale_stride(T), v) ||
         m->alloc(&m->acodes, (size_t)T * Kmax, v) || m->alloc(&m->hcodes, (size_t)T * F, v) ||
         m->alloc(&m->q16, (size_t)T * m->Nq(), v) || m->alloc(&m->k16, (size_t)T * m->Nk(), v) ||
         m->alloc(&m->v16, (size_t)T * m->Nk(), v) || m->alloc(&m->ids, T, v) || m->alloc(&m->flag, 4, v))
@@ -207,7 +207,7 @@ int build(db_model* m, const db_encoder_weights* w) {
         if (!rc) {
             const int G = (D + 63) / 64;
             if (m->alloc(&lw.gu_c, (size_t)2 * F * G * 64 * m->cfg.weight_bits / 8, m->allocations) ||
-                m->alloc(&lw.gu_s, (size_t)G * 2 * F, m->allocations))
+                m->alloc(&lw.gu_s, (size_t)G * db_scale_stride(2 * F), m->allocations))
                 rc = db_fail(DB_ERR_CUDA, "RESOURCE_LIMIT", "weight allocation exceeds device limits");
             if (!rc) rc = db_interleave_gate_up(gc, gs, uc, us, F, D, m->cfg.weight_bits, lw.gu_c, lw.gu_s, st);
             cudaStreamSynchronize(st);
@@ -256,7 +256,7 @@ int enqueue_forward(db_model* m, int T, const volatile int32_t* cancel) {
     const int D = c.hidden, Nq = m->Nq(), F = m->F(), Nqkv = m->Nqkv();
     const int bits = c.weight_bits, fused = c.fused;
     cudaStream_t st = m->stream;
-    const int64_t ld_codes = m->Kmax(), lds = m->cap_T;
+    const int64_t ld_codes = m->Kmax(), lds = db_scale_stride(m->cap_T);
     int rc = 0;
     auto timed = [&](int kind, auto&& launch) -> int {
         if (!m->profile) return launch();

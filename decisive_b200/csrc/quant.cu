@@ -4,12 +4,14 @@
 //   weight codes  Q4: [N, Kp/2] bytes, row n holds k = 0..Kp-1, low nibble = even k, nibble = code+8
 //                      (the code bytes of reference packed.rs:22-28, without the interleaved scale)
 //                 Q8: [N, Kp] int8
-//   weight scales f32 [G, N]  (group-major so a tile of N columns of one group is contiguous)
+//   weight scales f32 [G, Ns], Ns = db_scale_stride(N) = roundup(N, 128), padding zero (group-major so
+//                 that one group's scales for a tile of columns are one aligned bulk copy)
 //   activation codes, tensor-core order: f16 integer values [M, Kp]; inside every 8 consecutive k
 //                 the stored order is k = 0,4,1,5,2,6,3,7 (matches the nibble extraction of the GEMM)
 //   activation codes, GEMV order: int8 [M, Kp]; inside every 8 consecutive k: 0,2,4,6,1,3,5,7
 //   activation codes, natural order: int8 [M, Kp] (reference Scratch::values, int8.rs:7-11)
-//   activation scales f32 [G, lds] and code sums int32 [G, lds]
+//   activation scales f32 [G, lds] and code sums int32 [G, lds]; the tensor-core GEMM needs
+//                 lds >= roundup(M, 128) and lds % 4 == 0 (bulk-copied per 128-row tile)
 // Kp = ceil(K/64)*64; padding codes are 0 (nibble 8).
 #include <float.h>
 
@@ -102,7 +104,7 @@ __global__ void pack_weights_kernel(const uint16_t* __restrict__ w, int N, int K
         codes[(size_t)n * Kp + k0] = (uint8_t)(int8_t)c0;
         codes[(size_t)n * Kp + k0 + 1] = (uint8_t)(int8_t)c1;
     }
-    if (lane == 0) scales[(size_t)g * N + n] = scale;
+    if (lane == 0) scales[(size_t)g * db_scale_stride(N) + n] = scale;
 }
 
 // packed.rs:59-73 / quantized_rows.rs:89-110: out[t, k] = code(ids[t], k) * scale(ids[t], g).
@@ -122,7 +124,7 @@ __global__ void dequant_rows_kernel(const uint8_t* __restrict__ codes, const flo
     int code;
     if (bits == 4) code = (int)((codes[(size_t)row * (Kp / 2) + k / 2] >> ((k & 1) * 4)) & 15) - 8;
     else code = (int)(int8_t)codes[(size_t)row * Kp + k];
-    out[(size_t)t * ldo + k] = __fmul_rn((float)code, scales[(size_t)(k / DB_GROUP) * N + row]);
+    out[(size_t)t * ldo + k] = __fmul_rn((float)code, scales[(size_t)(k / DB_GROUP) * db_scale_stride(N) + row]);
 }
 
 // Reference packed rows (packed.rs:10-28: per (row, group) 32|64 code bytes then f32 scale) <-> device layout.
@@ -139,10 +141,10 @@ __global__ void packed_convert_kernel(uint8_t* __restrict__ packed, uint8_t* __r
         for (int j = 0; j < cb; ++j) c[j] = p[j];
         float s;
         memcpy(&s, p + cb, 4);
-        scales[(size_t)g * N + n] = s;
+        scales[(size_t)g * db_scale_stride(N) + n] = s;
     } else {
         for (int j = 0; j < cb; ++j) p[j] = c[j];
-        float s = scales[(size_t)g * N + n];
+        float s = scales[(size_t)g * db_scale_stride(N) + n];
         memcpy(p + cb, &s, 4);
     }
 }
@@ -183,6 +185,7 @@ int db_launch_pack_weights(const uint16_t* w, int N, int K, int bits, uint8_t* c
     int Kp = G * DB_GROUP;
     size_t code_bytes = (size_t)N * Kp * bits / 8;
     cudaMemsetAsync(codes, bits == 4 ? 0x88 : 0, code_bytes, stream);  // padding codes = 0
+    cudaMemsetAsync(scales, 0, (size_t)G * db_scale_stride(N) * sizeof(float), stream);  // padding scales = 0
     int64_t warps = (int64_t)N * G;
     pack_weights_kernel<<<blocks_for(warps, 8), 256, 0, stream>>>(w, N, K, bits, codes, scales, bad);
     return (int)cudaGetLastError();
@@ -199,6 +202,7 @@ int db_launch_dequant_rows(const uint8_t* codes, const float* scales, int N, int
 int db_launch_packed_convert(uint8_t* packed, uint8_t* codes, float* scales, int N, int K, int bits, int to_device,
                              cudaStream_t stream) {
     int64_t n = (int64_t)N * (K / DB_GROUP);
+    if (to_device) cudaMemsetAsync(scales, 0, (size_t)(K / DB_GROUP) * db_scale_stride(N) * sizeof(float), stream);
     packed_convert_kernel<<<blocks_for(n, 256), 256, 0, stream>>>(packed, codes, scales, N, K, bits, to_device);
     return (int)cudaGetLastError();
 }

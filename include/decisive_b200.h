@@ -50,12 +50,16 @@ extern "C" {
  *   DB_CODES_TC       f16  [M, Kp] integer-valued, inside each 8 stored as k0,k4,k1,k5,k2,k6,k3,k7
  * Kp = ceil(K/64)*64; activation scales f32 [G, lds], sums int32 [G, lds], G = Kp/64.
  * DB_LAYOUT: weight codes Q4 [N, Kp/2] bytes (low nibble = even k, nibble = code+8, i.e. the
- * code bytes of packed.rs:22-28), Q8 [N, Kp] int8; weight scales f32 [G, N]. */
+ * code bytes of packed.rs:22-28), Q8 [N, Kp] int8; weight scales f32 [G, Ns] with
+ * Ns = db_scale_row_stride(N) = roundup(N, 128), entries n >= N zero.  Activation scales passed
+ * to the tensor-core path need lds >= db_scale_row_stride(M) (and lds % 4 == 0). */
 #define DB_CODES_NATURAL 0
 #define DB_CODES_GEMV 1
 #define DB_CODES_TC 2
 
 int db_abi_version(void);
+/* row stride (elements) of a scale array with n columns: roundup(n, 128) */
+int64_t db_scale_row_stride(int64_t n);
 const char *db_last_error_code(void);
 const char *db_last_error_message(void);
 int db_device_count(void);
@@ -121,7 +125,8 @@ int db_project_packed(const float *x, int64_t K, const uint8_t *w_codes, const f
  * reference's fused q4_mlp (grouped_q4_mlp.wgsl:1-105) == apply_pair + silu_mul + prepare
  * (backbone.rs:229-236, cpu.rs:348-371, int8.rs:178-202).  w_gu: 2*F rows in blocks of
  * 64 gate rows followed by the 64 matching up rows (db_interleave_gate_up builds it).
- * Output: codes DB_CODES_TC [M, ldoc] and scales [F/64, ldos].  F % 64 == 0. */
+ * Output: codes DB_CODES_TC [M, ldoc] and scales [F/64, ldos] (ldos >= db_scale_row_stride(M)
+ * so they can feed the down projection directly).  F % 64 == 0. */
 int db_mlp_g64(const void *a_codes, int64_t lda, const float *sa, int64_t ldsa, const uint8_t *w_gu_codes,
                const float *w_gu_scales, int64_t M, int64_t F, int64_t K, int bits, int fused, void *out_codes,
                int64_t ldoc, float *out_scales, int64_t ldos, const int *nonfinite, void *stream);

@@ -75,8 +75,8 @@ def test_activation_quantiser_matches_oracle(db, oracle, bits, m, k):
             natural[:, b + perm] = c[:, b:b + 8]
         del nat
         assert np.array_equal(natural.reshape(-1), values.astype(np.int64)), layout
-        assert bits_equal(sc.cpu().numpy().T.reshape(-1), scales)
-        assert np.array_equal(s.cpu().numpy().T.reshape(-1), sums)
+        assert bits_equal(sc.cpu().numpy()[:, :m].T.reshape(-1), scales)
+        assert np.array_equal(s.cpu().numpy()[:, :m].T.reshape(-1), sums)
 
 
 def test_activation_rounding_at_ties(db, oracle):
@@ -92,7 +92,7 @@ def test_activation_rounding_at_ties(db, oracle):
         w = oracle.Matrix(np.zeros(64, np.uint16), 64, 1)
         values, scales, _ = w.prepare(x)
         assert np.array_equal(codes.cpu().numpy().reshape(-1), values)
-        assert bits_equal(sc.cpu().numpy().T.reshape(-1), scales)
+        assert bits_equal(sc.cpu().numpy()[:, :x.shape[0]].T.reshape(-1), scales)
 
 
 # ------------------------------------------------------------------ weights
@@ -128,7 +128,8 @@ def test_weight_packer_ragged_k_matches_matrix_layout(db, oracle, bits):
         else:
             dense = c.view(np.int8).astype(np.int64)
         assert np.array_equal(dense, mat.weight_codes().astype(np.int64))
-        assert bits_equal(scales.cpu().numpy().T, mat.weight_scales())
+        assert bits_equal(scales.cpu().numpy()[:, :n].T, mat.weight_scales())
+        assert np.all(scales.cpu().numpy()[:, n:] == 0)
 
 
 def test_embedding_rows_match_append(db, oracle):
@@ -263,7 +264,7 @@ def test_fused_mlp_matches_unfused_oracle(db, oracle, bits, m, f, k):
     diff = np.abs(natural.reshape(-1) - values.astype(np.int64))
     # exp() of CUDA and libm differ by <= 2 ulp; a code may flip only at a rounding boundary
     assert diff.max() <= 1 and np.count_nonzero(diff) <= max(2, diff.size // 10000)
-    rel = np.abs(scales.cpu().numpy().T.reshape(-1) - ref_scales) / ref_scales
+    rel = np.abs(scales.cpu().numpy()[:, :m].T.reshape(-1) - ref_scales) / ref_scales
     assert rel.max() <= 4e-7
 
 
