@@ -33,8 +33,14 @@ constexpr int BK = 64;
 constexpr int A_STAGES = 4;
 constexpr int W_STAGES = 4;
 constexpr int B_STAGES = 3;
-constexpr int S_STAGES = 6;   // per-group scale vectors (sa: 128 rows, sw: BN columns)
-constexpr int NUM_ACC = 4;    // TMEM accumulator buffers (4 x BN columns <= 512)
+#ifndef DB_GEMM_S_STAGES
+#define DB_GEMM_S_STAGES 6
+#endif
+#ifndef DB_GEMM_NUM_ACC
+#define DB_GEMM_NUM_ACC 4
+#endif
+constexpr int S_STAGES = DB_GEMM_S_STAGES;  // per-group scale vectors (sa: 128 rows, sw: BN columns)
+constexpr int NUM_ACC = DB_GEMM_NUM_ACC;    // TMEM accumulator buffers (NUM_ACC x BN columns <= 512)
 constexpr int NUM_THREADS = 448;
 constexpr int CONVERTER_WARP0 = 2;
 constexpr int EPILOGUE_WARP0 = 6;
@@ -299,7 +305,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         const float4 t = *reinterpret_cast<const float4*>(swp + c * 32 + j);
                         swv[j] = t.x; swv[j + 1] = t.y; swv[j + 2] = t.z; swv[j + 3] = t.w;
                     }
-                    tmem_wait_ld();
+                    tmem_wait_ld(v);
 #pragma unroll
                     for (int j = 0; j < 32; ++j) {
                         const float d = __uint_as_float(v[j]);
@@ -308,6 +314,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     }
                 }
                 tc_fence_before();
+                // the slot's next fill is an async-proxy (bulk copy) write: order this warp's
+                // generic-proxy reads of it before the release
+                fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) {
                     mbar_arrive(&acc_empty[ic]);
