@@ -320,6 +320,44 @@ def run_ours(args, rank, world, local_rank):
         dist.destroy_process_group()
 
 
+def run_gemm(args, local_rank):
+    """Single grouped GEMM (BASELINE config 1 by default: M=1024, K=1024, N=3072, W4A8 g64): K
+    device-timed launches on prepared activations, L2 flushed between launches."""
+    import torch
+
+    import decisive_b200 as db
+    from oracle import oracle
+    torch.cuda.set_device(local_rank)
+    m, k, n = (int(v) for v in args.gemm_shape.split(","))
+    rng = np.random.default_rng(1)
+    w = oracle.f32_to_bf16(rng.normal(0, 0.02, (n, k)).astype(np.float32))
+    x = np.random.default_rng(0).normal(0, 1, (m, k)).astype(np.float16)
+    codes, scales = db.pack_weights(torch.from_numpy(w.view(np.int16)).cuda(), args.bits)
+    xt = torch.from_numpy(x).cuda()
+    a, sa, _ = db.quantize_activations(xt, bits=8, layout=db.CODES_TC)
+    y = torch.empty((m, n), dtype=torch.float32, device="cuda")
+    flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device="cuda")
+    for _ in range(args.warmup):
+        db.gemm(a, db.CODES_TC, sa, codes, scales, m, n, k, args.bits, residual=y)
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(args.steps):
+        flush.zero_()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        db.gemm(a, db.CODES_TC, sa, codes, scales, m, n, k, args.bits, residual=y)
+        e.record()
+        torch.cuda.synchronize()
+        times.append(s.elapsed_time(e))
+    us = float(np.mean(times)) * 1e3
+    flops = 2.0 * m * n * k
+    peak_tf, peak_gbs, kind = measured_peaks()
+    out = {"workload": f"gemm W{args.bits}A8 g64 M={m} K={k} N={n}", "us_per_launch": us,
+           "tflops": flops / us / 1e6, "frac_of_bf16_peak": flops / us / 1e6 / peak_tf, "peak_kind": kind,
+           "launches": args.steps, "l2": "flushed between launches"}
+    print(json.dumps(out), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -328,11 +366,16 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-layers", type=int, default=2)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--workload", default="encoder", choices=["encoder", "gemm"])
+    ap.add_argument("--gemm-shape", default="1024,1024,3072", help="M,K,N for --workload gemm")
+    ap.add_argument("--bits", type=int, default=4)
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local_rank = int(os.environ.get("LOCAL_RANK", 0))
-    if args.impl == "reference":
+    if args.workload == "gemm":
+        run_gemm(args, local_rank)
+    elif args.impl == "reference":
         run_reference(args, rank)
     else:
         run_ours(args, rank, world, local_rank)

@@ -56,6 +56,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
+// As above, but the hardware may park the thread (up to the hint, 1 ms) until the phase
+// completes, instead of returning at once: waiting warps then stop competing for issue slots.
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u)
+        : "memory");
+    return ok != 0;
+}
 
 // Bounded wait.  Returns false when the CTA was aborted (by this or another thread) or the
 // limit expired; in the latter case the abort flag and the device error word are set.
@@ -64,8 +77,8 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     if (mbar_try_wait(bar, parity)) return true;
     uint64_t start = globaltimer();
     for (uint32_t i = 1;; ++i) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 255u) == 0) {
+        if (mbar_try_wait_suspend(bar, parity)) return true;
+        if ((i & 15u) == 0) {
             if (*abort_flag) return false;
             if (globaltimer() - start > DB_WAIT_LIMIT_NS) {
                 *abort_flag = 1;

@@ -41,9 +41,12 @@ constexpr int B_STAGES = 3;
 #endif
 constexpr int S_STAGES = DB_GEMM_S_STAGES;  // per-group scale vectors (sa: 128 rows, sw: BN columns)
 constexpr int NUM_ACC = DB_GEMM_NUM_ACC;    // TMEM accumulator buffers (NUM_ACC x BN columns <= 512)
-constexpr int NUM_THREADS = 448;
+// Warp roles: warpgroup 0 = {TMA producer, MMA issuer, 2 converters}; warpgroups 1-2 = epilogue.
 constexpr int CONVERTER_WARP0 = 2;
-constexpr int EPILOGUE_WARP0 = 6;
+constexpr int CONVERTER_WARPS = 2;
+constexpr int EPILOGUE_WARP0 = 4;
+constexpr int EPILOGUE_WARPS = 8;
+constexpr int NUM_THREADS = 384;
 constexpr int XCH_STRIDE = 65;  // floats per row of the SwiGLU exchange buffer (bank-conflict free)
 
 template <int BN, int BITS, int EPI>
@@ -120,12 +123,56 @@ __device__ __forceinline__ float silu_ref(float x) {
     return __fmul_rn(x, __fdiv_rn(1.f, __fadd_rn(1.f, expf(-x))));
 }
 
+// Epilogue helpers: one warp owns 32 rows (its TMEM lane quadrant) x COLS columns of the tile.
+template <int COLS>
+__device__ __forceinline__ void tmem_load_cols(uint32_t taddr, uint32_t (&v)[COLS]) {
+#pragma unroll
+    for (int c = 0; c < COLS / 32; ++c)
+        tmem_ld_32x32b_x32(taddr + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&v[c * 32]));
+}
+template <int COLS>
+__device__ __forceinline__ void tmem_wait_cols(uint32_t (&v)[COLS]) {
+    tmem_wait_ld(*reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+#pragma unroll
+    for (int c = 1; c < COLS / 32; ++c) {
+        uint32_t(&w)[32] = *reinterpret_cast<uint32_t(*)[32]>(&v[c * 32]);
+        asm volatile(""
+                     : "+r"(w[0]), "+r"(w[1]), "+r"(w[2]), "+r"(w[3]), "+r"(w[4]), "+r"(w[5]), "+r"(w[6]),
+                       "+r"(w[7]), "+r"(w[8]), "+r"(w[9]), "+r"(w[10]), "+r"(w[11]), "+r"(w[12]), "+r"(w[13]),
+                       "+r"(w[14]), "+r"(w[15]), "+r"(w[16]), "+r"(w[17]), "+r"(w[18]), "+r"(w[19]), "+r"(w[20]),
+                       "+r"(w[21]), "+r"(w[22]), "+r"(w[23]), "+r"(w[24]), "+r"(w[25]), "+r"(w[26]), "+r"(w[27]),
+                       "+r"(w[28]), "+r"(w[29]), "+r"(w[30]), "+r"(w[31]));
+    }
+}
+// acc[j] = fma(d[j], sw[j]*sa, acc[j]) (fused) or acc[j] + d[j]*(sa*sw[j]) (portable), in f32x2 pairs;
+// each lane of the packed ops rounds exactly like the scalar instruction.
+template <int COLS, bool FUSED>
+__device__ __forceinline__ void fold_group(float2 (&acc)[COLS / 2], const uint32_t (&v)[COLS], const float* swp,
+                                           float s_a) {
+    const float2 sa2 = make_float2(s_a, s_a);
+#pragma unroll
+    for (int j = 0; j < COLS; j += 4) {
+        const float4 w4 = *reinterpret_cast<const float4*>(swp + j);
+        const float2 d0 = make_float2(__uint_as_float(v[j]), __uint_as_float(v[j + 1]));
+        const float2 d1 = make_float2(__uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]));
+        if (FUSED) {
+            acc[j / 2] = __ffma2_rn(d0, __fmul2_rn(make_float2(w4.x, w4.y), sa2), acc[j / 2]);
+            acc[j / 2 + 1] = __ffma2_rn(d1, __fmul2_rn(make_float2(w4.z, w4.w), sa2), acc[j / 2 + 1]);
+        } else {
+            // two roundings per step (int8.rs:276-278); scalar _rn ops are never contracted to fma
+            acc[j / 2].x = __fadd_rn(acc[j / 2].x, __fmul_rn(d0.x, __fmul_rn(s_a, w4.x)));
+            acc[j / 2].y = __fadd_rn(acc[j / 2].y, __fmul_rn(d0.y, __fmul_rn(s_a, w4.y)));
+            acc[j / 2 + 1].x = __fadd_rn(acc[j / 2 + 1].x, __fmul_rn(d1.x, __fmul_rn(s_a, w4.z)));
+            acc[j / 2 + 1].y = __fadd_rn(acc[j / 2 + 1].y, __fmul_rn(d1.y, __fmul_rn(s_a, w4.w)));
+        }
+    }
+}
+
 template <int BN, int BITS, int EPI, bool FUSED>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                    const float* __restrict__ sa, int64_t ldsa, const float* __restrict__ sw, int64_t ldsw, int M,
-                   int N, int G,
-                   float* __restrict__ y, int64_t ldy, __half* __restrict__ out_codes, int64_t ldoc,
+                   int N, int G, float* __restrict__ y, int64_t ldy, __half* __restrict__ out_codes, int64_t ldoc,
                    float* __restrict__ out_scales, int64_t ldos, const int* __restrict__ nonfinite,
                    int* __restrict__ dev_error) {
     using S = GemmSmem<BN, BITS, EPI>;
@@ -142,7 +189,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     uint64_t* s_empty = s_full + S_STAGES;
     uint64_t* acc_full = s_empty + S_STAGES;
     uint64_t* acc_empty = acc_full + NUM_ACC;
-    uint64_t* xch_full = acc_empty + NUM_ACC;   // SwiGLU exchange: up half -> gate half
+    uint64_t* xch_full = acc_empty + NUM_ACC;  // SwiGLU exchange: up half -> gate half
     uint64_t* xch_empty = xch_full + 1;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::OFF_MISC);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + S::OFF_MISC + 4);
@@ -153,10 +200,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < A_STAGES; ++i) { mbar_init(&a_full[i], 1); mbar_init(&a_empty[i], 1); }
-        for (int i = 0; i < W_STAGES; ++i) { mbar_init(&w_full[i], 1); mbar_init(&w_empty[i], 4); }
-        for (int i = 0; i < B_STAGES; ++i) { mbar_init(&b_full[i], 4); mbar_init(&b_empty[i], 1); }
-        for (int i = 0; i < S_STAGES; ++i) { mbar_init(&s_full[i], 1); mbar_init(&s_empty[i], 8); }
-        for (int i = 0; i < NUM_ACC; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], 8); }
+        for (int i = 0; i < W_STAGES; ++i) { mbar_init(&w_full[i], 1); mbar_init(&w_empty[i], CONVERTER_WARPS); }
+        for (int i = 0; i < B_STAGES; ++i) { mbar_init(&b_full[i], CONVERTER_WARPS); mbar_init(&b_empty[i], 1); }
+        for (int i = 0; i < S_STAGES; ++i) { mbar_init(&s_full[i], 1); mbar_init(&s_empty[i], EPILOGUE_WARPS); }
+        for (int i = 0; i < NUM_ACC; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], EPILOGUE_WARPS); }
         mbar_init(xch_full, 4);
         mbar_init(xch_empty, 4);
         *abort_flag = 0;
@@ -229,9 +276,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 }
             }
         }
-    } else if (warp < EPILOGUE_WARP0) {
+    } else if (warp < 4) {
         // ---------------------------------------------------------------- converters
-        const int ct = threadIdx.x - CONVERTER_WARP0 * 32;  // 0..127
+        const int ct = threadIdx.x - CONVERTER_WARP0 * 32;  // 0..63
         int iw = 0, ib = 0;
         uint32_t pw = 0, pb = 0;
         for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
@@ -240,22 +287,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 if (!warp_wait(&b_empty[ib], pb ^ 1u, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_CVT)) goto done;
                 const uint8_t* wsrc = smem + S::OFF_W + iw * S::W_BYTES;
                 uint8_t* bdst = smem + S::OFF_B + ib * S::B_BYTES;
-                for (int r = ct; r < BN; r += 128) {
+#pragma unroll
+                for (int r = ct; r < BN; r += CONVERTER_WARPS * 32) {
                     const uint4* src = reinterpret_cast<const uint4*>(wsrc + r * S::W_ROW);
                     uint8_t* row = bdst + r * 128;
-                    const int sw = r & 7;
+                    const int swz = r & 7;
                     if (BITS == 4) {
-                        uint4 v0 = src[0], v1 = src[1];
-                        uint32_t words[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+                        const uint4 v0 = src[0], v1 = src[1];
+                        const uint32_t words[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
 #pragma unroll
                         for (int c = 0; c < 8; ++c)
-                            *reinterpret_cast<uint4*>(row + ((c ^ sw) << 4)) = nibbles_to_f16(words[c]);
+                            *reinterpret_cast<uint4*>(row + ((c ^ swz) << 4)) = nibbles_to_f16(words[c]);
                     } else {
 #pragma unroll
                         for (int h = 0; h < 4; ++h) {
-                            uint4 v = src[h];
-                            *reinterpret_cast<uint4*>(row + (((2 * h) ^ sw) << 4)) = bytes_to_f16(v.x, v.y);
-                            *reinterpret_cast<uint4*>(row + (((2 * h + 1) ^ sw) << 4)) = bytes_to_f16(v.z, v.w);
+                            const uint4 v = src[h];
+                            *reinterpret_cast<uint4*>(row + (((2 * h) ^ swz) << 4)) = bytes_to_f16(v.x, v.y);
+                            *reinterpret_cast<uint4*>(row + (((2 * h + 1) ^ swz) << 4)) = bytes_to_f16(v.z, v.w);
                         }
                     }
                 }
@@ -271,12 +319,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
     } else {
         // ---------------------------------------------------------------- epilogue
+        // Software pipeline over 32-column chunks: the TMEM load of the next chunk (of this group
+        // or of the next group) is in flight while the current chunk is folded; a TMEM buffer is
+        // released as soon as all of its chunks sit in registers.
         constexpr int COLS = BN / 2;  // columns per thread
         constexpr int CHUNKS = COLS / 32;
-        const int q = warp & 3;                        // TMEM lane quadrant this warp may access
+        const int q = warp & 3;                         // TMEM lane quadrant this warp may access
         const int half = (warp - EPILOGUE_WARP0) >> 2;  // which half of the tile's columns
-        const int r = q * 32 + lane;                   // row inside the tile
+        const int r = q * 32 + lane;                    // row inside the tile
         const int col0 = half * COLS;
+        const uint32_t tlane = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)col0;
         const bool any_nonfinite = nonfinite != nullptr && *nonfinite != 0;
         float* xch = reinterpret_cast<float*>(smem + S::OFF_X);
         int ic = 0, is = 0;
@@ -285,52 +337,59 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const int m0 = (tile % m_tiles) * BM, n0 = (tile / m_tiles) * BN;
             const int m = m0 + r;
             const bool full_cols = n0 + BN <= N;
-            float acc[COLS];
+            float2 acc[COLS / 2];
 #pragma unroll
-            for (int j = 0; j < COLS; ++j) acc[j] = 0.f;
+            for (int j = 0; j < COLS / 2; ++j) acc[j] = make_float2(0.f, 0.f);
+            uint32_t va[32], vb[32];
+            // prologue: chunk 0 of group 0
+            if (!warp_wait(&acc_full[ic], pc, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_EPI)) goto done;
+            tc_fence_after();
+            tmem_ld_32x32b_x32(tlane + (uint32_t)(ic * BN), va);
+            tmem_wait_ld(va);
             for (int g = 0; g < G; ++g) {
                 if (!warp_wait(&s_full[is], ps, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_EPI)) goto done;
-                if (!warp_wait(&acc_full[ic], pc, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_EPI)) goto done;
-                tc_fence_after();
                 const float* slot = reinterpret_cast<const float*>(smem + S::OFF_S + is * S::S_BYTES);
                 const float s_a = slot[r];
                 const float* swp = slot + BM + col0;
-#pragma unroll
-                for (int c = 0; c < CHUNKS; ++c) {
-                    uint32_t v[32];
-                    tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ic * BN + col0 + c * 32), v);
-                    float swv[32];
-#pragma unroll
-                    for (int j = 0; j < 32; j += 4) {
-                        const float4 t = *reinterpret_cast<const float4*>(swp + c * 32 + j);
-                        swv[j] = t.x; swv[j + 1] = t.y; swv[j + 2] = t.z; swv[j + 3] = t.w;
-                    }
-                    tmem_wait_ld(v);
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const float d = __uint_as_float(v[j]);
-                        if (FUSED) acc[c * 32 + j] = __fmaf_rn(d, __fmul_rn(swv[j], s_a), acc[c * 32 + j]);
-                        else acc[c * 32 + j] = __fadd_rn(acc[c * 32 + j], __fmul_rn(d, __fmul_rn(s_a, swv[j])));
-                    }
+                if (CHUNKS == 2) {
+                    tmem_ld_32x32b_x32(tlane + (uint32_t)(ic * BN + 32), vb);  // chunk 1 of g
+                    fold_group<32, FUSED>(*reinterpret_cast<float2(*)[16]>(&acc[0]), va, swp, s_a);
+                    tmem_wait_ld(vb);
+                } else {
+                    vb[0] = vb[0];
                 }
+                // every chunk of group g is in registers: release its TMEM buffer
                 tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&acc_empty[ic]);
+                if (++ic == NUM_ACC) { ic = 0; pc ^= 1u; }
+                const bool next = g + 1 < G;
+                if (next) {
+                    if (!warp_wait(&acc_full[ic], pc, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_EPI)) goto done;
+                    tc_fence_after();
+                    if (CHUNKS == 2) tmem_ld_32x32b_x32(tlane + (uint32_t)(ic * BN), va);  // chunk 0 of g+1
+                }
+                if (CHUNKS == 2) {
+                    fold_group<32, FUSED>(*reinterpret_cast<float2(*)[16]>(&acc[16]), vb, swp + 32, s_a);
+                } else {
+                    fold_group<32, FUSED>(*reinterpret_cast<float2(*)[16]>(&acc[0]), va, swp, s_a);
+                    if (next) tmem_ld_32x32b_x32(tlane + (uint32_t)(ic * BN), va);
+                }
                 // the slot's next fill is an async-proxy (bulk copy) write: order this warp's
                 // generic-proxy reads of it before the release
                 fence_proxy_async_smem();
                 __syncwarp();
-                if (lane == 0) {
-                    mbar_arrive(&acc_empty[ic]);
-                    mbar_arrive(&s_empty[is]);
-                }
-                if (++ic == NUM_ACC) { ic = 0; pc ^= 1u; }
+                if (lane == 0) mbar_arrive(&s_empty[is]);
                 if (++is == S_STAGES) { is = 0; ps ^= 1u; }
+                if (next) tmem_wait_ld(va);
             }
+            float* accf = reinterpret_cast<float*>(acc);
             if (EPI == DB_EPI_SWIGLU_QUANT) {
                 // half 1 holds the up projection of the same 64 features: hand it to half 0.
                 if (half == 1) {
                     if (!warp_wait(xch_empty, px ^ 1u, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_EPI)) goto done;
 #pragma unroll
-                    for (int j = 0; j < COLS; ++j) xch[r * XCH_STRIDE + j] = acc[j];
+                    for (int j = 0; j < COLS; ++j) xch[r * XCH_STRIDE + j] = accf[j];
                     __syncwarp();
                     if (lane == 0) mbar_arrive(xch_full);
                 } else {
@@ -340,7 +399,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         float amax = 0.f;
 #pragma unroll
                         for (int j = 0; j < COLS; ++j) {
-                            h[j] = __fmul_rn(silu_ref(acc[j]), xch[r * XCH_STRIDE + j]);
+                            h[j] = __fmul_rn(silu_ref(accf[j]), xch[r * XCH_STRIDE + j]);
                             amax = fmaxf(amax, fabsf(h[j]));
                         }
                         const float scale = fmaxf(__fdiv_rn(amax, 127.f), FLT_MIN);
@@ -369,9 +428,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 if (full_cols && (ldy & 3) == 0 && (N & 3) == 0) {
 #pragma unroll
                     for (int j = 0; j < COLS; j += 4) {
-                        float4 o = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+                        float4 o = make_float4(accf[j], accf[j + 1], accf[j + 2], accf[j + 3]);
                         if (EPI == DB_EPI_RESIDUAL) {
-                            float4 rr = *reinterpret_cast<const float4*>(dst + j);
+                            const float4 rr = *reinterpret_cast<const float4*>(dst + j);
                             o.x = __fadd_rn(rr.x, o.x); o.y = __fadd_rn(rr.y, o.y);
                             o.z = __fadd_rn(rr.z, o.z); o.w = __fadd_rn(rr.w, o.w);
                         }
@@ -382,7 +441,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
                     for (int j = 0; j < COLS; ++j) {
                         if (n0 + col0 + j < N) {
-                            float o = acc[j];
+                            float o = accf[j];
                             if (EPI == DB_EPI_RESIDUAL) o = __fadd_rn(dst[j], o);
                             dst[j] = any_nonfinite ? nanv : o;
                         }
