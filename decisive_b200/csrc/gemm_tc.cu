@@ -30,42 +30,43 @@ namespace db {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
-constexpr int A_STAGES = 4;
-constexpr int W_STAGES = 4;
-constexpr int B_STAGES = 3;
-#ifndef DB_GEMM_S_STAGES
-#define DB_GEMM_S_STAGES 6
+constexpr int B_STAGES = 3;   // converted f16 weight tiles (converter -> MMA)
+constexpr int NUM_ACC = 4;    // TMEM accumulator buffers (NUM_ACC x BN columns <= 512)
+// Warp roles: 0 = TMA producer, 1 = MMA issuer, then the converters, then 8 epilogue warps.
+#ifndef DB_GEMM_CONVERTER_WARPS
+#define DB_GEMM_CONVERTER_WARPS 2
 #endif
-#ifndef DB_GEMM_NUM_ACC
-#define DB_GEMM_NUM_ACC 4
-#endif
-constexpr int S_STAGES = DB_GEMM_S_STAGES;  // per-group scale vectors (sa: 128 rows, sw: BN columns)
-constexpr int NUM_ACC = DB_GEMM_NUM_ACC;    // TMEM accumulator buffers (NUM_ACC x BN columns <= 512)
-// Warp roles: warpgroup 0 = {TMA producer, MMA issuer, 2 converters}; warpgroups 1-2 = epilogue.
 constexpr int CONVERTER_WARP0 = 2;
-constexpr int CONVERTER_WARPS = 2;
-constexpr int EPILOGUE_WARP0 = 4;
+constexpr int CONVERTER_WARPS = DB_GEMM_CONVERTER_WARPS;
+constexpr int EPILOGUE_WARP0 = CONVERTER_WARP0 + CONVERTER_WARPS;
 constexpr int EPILOGUE_WARPS = 8;
-constexpr int NUM_THREADS = 384;
+constexpr int NUM_THREADS = 32 * (EPILOGUE_WARP0 + EPILOGUE_WARPS);
 constexpr int XCH_STRIDE = 65;  // floats per row of the SwiGLU exchange buffer (bank-conflict free)
 
+// One pipeline stage per 64-wide K group holds everything the group needs: the activation-code
+// tile, the raw weight-code tile and the group's scale vectors.  The epilogue is the last
+// consumer of every part, so it alone releases the stage; the producer issues one wait, one
+// expect-tx and four copies per group.
 template <int BN, int BITS, int EPI>
 struct GemmSmem {
+    static constexpr int STAGES = BITS == 4 ? 6 : 5;
     static constexpr int A_BYTES = BM * BK * 2;          // 16 KB
-    static constexpr int B_BYTES = BN * BK * 2;          // f16 codes
     static constexpr int W_ROW = BK * BITS / 8;          // 32 or 64 bytes of raw codes per row
     static constexpr int W_BYTES = BN * W_ROW;
+    static constexpr int SC_BYTES = (BM + BN) * 4;       // sa then sw of the group
+    static constexpr int ST_A = 0, ST_W = A_BYTES, ST_S = A_BYTES + W_BYTES;
+    static constexpr int STAGE_BYTES = (ST_S + SC_BYTES + 1023) / 1024 * 1024;
+    static constexpr int TX_BYTES = A_BYTES + W_BYTES + SC_BYTES;
+    static constexpr int B_BYTES = BN * BK * 2;          // f16 codes
     static constexpr int XCH_BYTES = EPI == DB_EPI_SWIGLU_QUANT ? BM * XCH_STRIDE * 4 : 0;
-    static constexpr int S_BYTES = (BM + BN) * 4;        // sa then sw of one group
-    static constexpr int OFF_A = 0;
-    static constexpr int OFF_B = OFF_A + A_STAGES * A_BYTES;
-    static constexpr int OFF_W = OFF_B + B_STAGES * B_BYTES;
-    static constexpr int OFF_S = OFF_W + W_STAGES * W_BYTES;
-    static constexpr int OFF_X = OFF_S + S_STAGES * S_BYTES;
+    static constexpr int OFF_STAGE = 0;
+    static constexpr int OFF_B = OFF_STAGE + STAGES * STAGE_BYTES;
+    static constexpr int OFF_X = OFF_B + B_STAGES * B_BYTES;
     static constexpr int OFF_BAR = (OFF_X + XCH_BYTES + 15) / 16 * 16;
-    static constexpr int NUM_BARS = 2 * A_STAGES + 2 * W_STAGES + 2 * B_STAGES + 2 * S_STAGES + 2 * NUM_ACC + 2;
+    static constexpr int NUM_BARS = 2 * STAGES + 2 * B_STAGES + 2 * NUM_ACC + 2;
     static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
     static constexpr int BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
+    static_assert(BYTES <= 232448, "shared memory budget");
 };
 
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err,
@@ -144,26 +145,21 @@ __device__ __forceinline__ void tmem_wait_cols(uint32_t (&v)[COLS]) {
                        "+r"(w[28]), "+r"(w[29]), "+r"(w[30]), "+r"(w[31]));
     }
 }
-// acc[j] = fma(d[j], sw[j]*sa, acc[j]) (fused) or acc[j] + d[j]*(sa*sw[j]) (portable), in f32x2 pairs;
-// each lane of the packed ops rounds exactly like the scalar instruction.
+// acc[j] = fma(d[j], sw[j]*sa, acc[j]) (fused) or acc[j] + d[j]*(sa*sw[j]) (portable).  Scalar
+// FMUL/FFMA: on this part the packed f32x2 forms run at a lower element rate than scalar FFMA.
 template <int COLS, bool FUSED>
 __device__ __forceinline__ void fold_group(float2 (&acc)[COLS / 2], const uint32_t (&v)[COLS], const float* swp,
                                            float s_a) {
-    const float2 sa2 = make_float2(s_a, s_a);
 #pragma unroll
     for (int j = 0; j < COLS; j += 4) {
         const float4 w4 = *reinterpret_cast<const float4*>(swp + j);
-        const float2 d0 = make_float2(__uint_as_float(v[j]), __uint_as_float(v[j + 1]));
-        const float2 d1 = make_float2(__uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]));
-        if (FUSED) {
-            acc[j / 2] = __ffma2_rn(d0, __fmul2_rn(make_float2(w4.x, w4.y), sa2), acc[j / 2]);
-            acc[j / 2 + 1] = __ffma2_rn(d1, __fmul2_rn(make_float2(w4.z, w4.w), sa2), acc[j / 2 + 1]);
-        } else {
-            // two roundings per step (int8.rs:276-278); scalar _rn ops are never contracted to fma
-            acc[j / 2].x = __fadd_rn(acc[j / 2].x, __fmul_rn(d0.x, __fmul_rn(s_a, w4.x)));
-            acc[j / 2].y = __fadd_rn(acc[j / 2].y, __fmul_rn(d0.y, __fmul_rn(s_a, w4.y)));
-            acc[j / 2 + 1].x = __fadd_rn(acc[j / 2 + 1].x, __fmul_rn(d1.x, __fmul_rn(s_a, w4.z)));
-            acc[j / 2 + 1].y = __fadd_rn(acc[j / 2 + 1].y, __fmul_rn(d1.y, __fmul_rn(s_a, w4.w)));
+        const float w[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            float& a = (e & 1) ? acc[(j + e) / 2].y : acc[(j + e) / 2].x;
+            const float d = __uint_as_float(v[j + e]);
+            if (FUSED) a = __fmaf_rn(d, __fmul_rn(w[e], s_a), a);
+            else a = __fadd_rn(a, __fmul_rn(d, __fmul_rn(s_a, w[e])));
         }
     }
 }
@@ -179,15 +175,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::OFF_BAR);
-    uint64_t* a_full = bars;
-    uint64_t* a_empty = a_full + A_STAGES;
-    uint64_t* w_full = a_empty + A_STAGES;
-    uint64_t* w_empty = w_full + W_STAGES;
-    uint64_t* b_full = w_empty + W_STAGES;
-    uint64_t* b_empty = b_full + B_STAGES;
-    uint64_t* s_full = b_empty + B_STAGES;
-    uint64_t* s_empty = s_full + S_STAGES;
-    uint64_t* acc_full = s_empty + S_STAGES;
+    uint64_t* full = bars;                   // stage loaded (TMA tx)
+    uint64_t* empty = full + S::STAGES;      // stage released by the epilogue warps
+    uint64_t* b_full = empty + S::STAGES;    // converted weight tile ready
+    uint64_t* b_empty = b_full + B_STAGES;   // converted tile consumed by the MMA
+    uint64_t* acc_full = b_empty + B_STAGES;
     uint64_t* acc_empty = acc_full + NUM_ACC;
     uint64_t* xch_full = acc_empty + NUM_ACC;  // SwiGLU exchange: up half -> gate half
     uint64_t* xch_empty = xch_full + 1;
@@ -199,10 +191,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int tiles = m_tiles * n_tiles;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < A_STAGES; ++i) { mbar_init(&a_full[i], 1); mbar_init(&a_empty[i], 1); }
-        for (int i = 0; i < W_STAGES; ++i) { mbar_init(&w_full[i], 1); mbar_init(&w_empty[i], CONVERTER_WARPS); }
+        for (int i = 0; i < S::STAGES; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], EPILOGUE_WARPS); }
         for (int i = 0; i < B_STAGES; ++i) { mbar_init(&b_full[i], CONVERTER_WARPS); mbar_init(&b_empty[i], 1); }
-        for (int i = 0; i < S_STAGES; ++i) { mbar_init(&s_full[i], 1); mbar_init(&s_empty[i], EPILOGUE_WARPS); }
         for (int i = 0; i < NUM_ACC; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], EPILOGUE_WARPS); }
         mbar_init(xch_full, 4);
         mbar_init(xch_empty, 4);
@@ -225,27 +215,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (warp == 0) {
         // ---------------------------------------------------------------- TMA producer
         if (lane == 0) {
-            int ia = 0, iw = 0, is = 0;
-            uint32_t pa = 0, pw = 0, ps = 0;
+            int is = 0;
+            uint32_t ps = 0;
             for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
                 const int m0 = (tile % m_tiles) * BM, n0 = (tile / m_tiles) * BN;
                 for (int g = 0; g < G; ++g) {
-                    if (!mbar_wait(&s_empty[is], ps ^ 1u, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_TMA)) goto done;
-                    mbar_arrive_expect_tx(&s_full[is], S::S_BYTES);
-                    {
-                        uint8_t* slot = smem + S::OFF_S + is * S::S_BYTES;
-                        bulk_load(slot, sa + (size_t)g * ldsa + m0, BM * 4, &s_full[is]);
-                        bulk_load(slot + BM * 4, sw + (size_t)g * ldsw + n0, BN * 4, &s_full[is]);
-                    }
-                    if (++is == S_STAGES) { is = 0; ps ^= 1u; }
-                    if (!mbar_wait(&a_empty[ia], pa ^ 1u, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_TMA)) goto done;
-                    mbar_arrive_expect_tx(&a_full[ia], S::A_BYTES);
-                    tma_load_2d(smem + S::OFF_A + ia * S::A_BYTES, &tmA, &a_full[ia], g * BK, m0);
-                    if (++ia == A_STAGES) { ia = 0; pa ^= 1u; }
-                    if (!mbar_wait(&w_empty[iw], pw ^ 1u, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_TMA)) goto done;
-                    mbar_arrive_expect_tx(&w_full[iw], S::W_BYTES);
-                    tma_load_2d(smem + S::OFF_W + iw * S::W_BYTES, &tmW, &w_full[iw], g * S::W_ROW, n0);
-                    if (++iw == W_STAGES) { iw = 0; pw ^= 1u; }
+                    if (!mbar_wait(&empty[is], ps ^ 1u, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_TMA)) goto done;
+                    uint8_t* st = smem + S::OFF_STAGE + is * S::STAGE_BYTES;
+                    mbar_arrive_expect_tx(&full[is], S::TX_BYTES);
+                    tma_load_2d(st + S::ST_A, &tmA, &full[is], g * BK, m0);
+                    tma_load_2d(st + S::ST_W, &tmW, &full[is], g * S::W_ROW, n0);
+                    bulk_load(st + S::ST_S, sa + (size_t)g * ldsa + m0, BM * 4, &full[is]);
+                    bulk_load(st + S::ST_S + BM * 4, sw + (size_t)g * ldsw + n0, BN * 4, &full[is]);
+                    if (++is == S::STAGES) { is = 0; ps ^= 1u; }
                 }
             }
         }
@@ -253,39 +235,38 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         // ---------------------------------------------------------------- MMA issuer
         if (lane == 0) {
             constexpr uint32_t IDESC = idesc_f16_f32(BM, BN);
-            int ia = 0, ib = 0, ic = 0;
-            uint32_t pa = 0, pb = 0, pc = 0;
-            const uint32_t a_base = smem_u32(smem + S::OFF_A), b_base = smem_u32(smem + S::OFF_B);
+            int is = 0, ib = 0, ic = 0;
+            uint32_t ps = 0, pb = 0, pc = 0;
+            const uint32_t st_base = smem_u32(smem + S::OFF_STAGE), b_base = smem_u32(smem + S::OFF_B);
             for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
                 for (int g = 0; g < G; ++g) {
-                    if (!mbar_wait(&a_full[ia], pa, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_MMA)) goto done;
+                    if (!mbar_wait(&full[is], ps, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_MMA)) goto done;
                     if (!mbar_wait(&b_full[ib], pb, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_MMA)) goto done;
                     if (!mbar_wait(&acc_empty[ic], pc ^ 1u, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_MMA)) goto done;
                     tc_fence_after();
                     const uint32_t d = tmem_base + (uint32_t)(ic * BN);
-                    const uint32_t a_addr = a_base + ia * S::A_BYTES, b_addr = b_base + ib * S::B_BYTES;
+                    const uint32_t a_addr = st_base + is * S::STAGE_BYTES + S::ST_A, b_addr = b_base + ib * S::B_BYTES;
 #pragma unroll
                     for (int kk = 0; kk < BK / 16; ++kk)
                         umma_f16(d, sw128_desc(a_addr + kk * 32), sw128_desc(b_addr + kk * 32), IDESC, kk > 0);
-                    umma_commit(&a_empty[ia]);
                     umma_commit(&b_empty[ib]);
                     umma_commit(&acc_full[ic]);
-                    if (++ia == A_STAGES) { ia = 0; pa ^= 1u; }
+                    if (++is == S::STAGES) { is = 0; ps ^= 1u; }
                     if (++ib == B_STAGES) { ib = 0; pb ^= 1u; }
                     if (++ic == NUM_ACC) { ic = 0; pc ^= 1u; }
                 }
             }
         }
-    } else if (warp < 4) {
+    } else if (warp < EPILOGUE_WARP0) {
         // ---------------------------------------------------------------- converters
-        const int ct = threadIdx.x - CONVERTER_WARP0 * 32;  // 0..63
-        int iw = 0, ib = 0;
-        uint32_t pw = 0, pb = 0;
+        const int ct = threadIdx.x - CONVERTER_WARP0 * 32;
+        int is = 0, ib = 0;
+        uint32_t ps = 0, pb = 0;
         for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
             for (int g = 0; g < G; ++g) {
-                if (!warp_wait(&w_full[iw], pw, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_CVT)) goto done;
+                if (!warp_wait(&full[is], ps, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_CVT)) goto done;
                 if (!warp_wait(&b_empty[ib], pb ^ 1u, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_CVT)) goto done;
-                const uint8_t* wsrc = smem + S::OFF_W + iw * S::W_BYTES;
+                const uint8_t* wsrc = smem + S::OFF_STAGE + is * S::STAGE_BYTES + S::ST_W;
                 uint8_t* bdst = smem + S::OFF_B + ib * S::B_BYTES;
 #pragma unroll
                 for (int r = ct; r < BN; r += CONVERTER_WARPS * 32) {
@@ -307,13 +288,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         }
                     }
                 }
+                // generic writes of the B tile become MMA (async proxy) reads
                 fence_proxy_async_smem();
                 __syncwarp();
-                if (lane == 0) {
-                    mbar_arrive(&b_full[ib]);
-                    mbar_arrive(&w_empty[iw]);
-                }
-                if (++iw == W_STAGES) { iw = 0; pw ^= 1u; }
+                if (lane == 0) mbar_arrive(&b_full[ib]);
+                if (++is == S::STAGES) { is = 0; ps ^= 1u; }
                 if (++ib == B_STAGES) { ib = 0; pb ^= 1u; }
             }
         }
@@ -347,8 +326,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             tmem_ld_32x32b_x32(tlane + (uint32_t)(ic * BN), va);
             tmem_wait_ld(va);
             for (int g = 0; g < G; ++g) {
-                if (!warp_wait(&s_full[is], ps, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_EPI)) goto done;
-                const float* slot = reinterpret_cast<const float*>(smem + S::OFF_S + is * S::S_BYTES);
+                if (!warp_wait(&full[is], ps, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_EPI)) goto done;
+                const float* slot = reinterpret_cast<const float*>(smem + S::OFF_STAGE + is * S::STAGE_BYTES + S::ST_S);
                 const float s_a = slot[r];
                 const float* swp = slot + BM + col0;
                 if (CHUNKS == 2) {
@@ -375,12 +354,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     fold_group<32, FUSED>(*reinterpret_cast<float2(*)[16]>(&acc[0]), va, swp, s_a);
                     if (next) tmem_ld_32x32b_x32(tlane + (uint32_t)(ic * BN), va);
                 }
-                // the slot's next fill is an async-proxy (bulk copy) write: order this warp's
-                // generic-proxy reads of it before the release
+                // the stage's next fill is an async-proxy (TMA / bulk copy) write: order this warp's
+                // generic-proxy reads of it before releasing the stage
                 fence_proxy_async_smem();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&s_empty[is]);
-                if (++is == S_STAGES) { is = 0; ps ^= 1u; }
+                if (lane == 0) mbar_arrive(&empty[is]);
+                if (++is == S::STAGES) { is = 0; ps ^= 1u; }
                 if (next) tmem_wait_ld(va);
             }
             float* accf = reinterpret_cast<float*>(acc);
