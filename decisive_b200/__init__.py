@@ -117,6 +117,19 @@ def linear(x, w_codes, sw, N: int, weight_bits: int = 4, activation_bits: int = 
     return y
 
 
+def linear_noalloc(x, w_codes, sw, N: int, weight_bits: int = 4, activation_bits: int = 8, fused: bool = True,
+                   out=None):
+    """Matrix::apply without any device allocation by the library: for hosts that forbid it.  Uses
+    the library's fixed scratch array (db_linear_noalloc_scratch_bytes()); see the C header for the
+    sharing rules."""
+    import torch
+    M, K = x.shape
+    y = torch.empty((M, N), dtype=torch.float32, device=x.device) if out is None else out
+    check(load().db_linear_g64_noalloc(_ptr(x), M, K, _ptr(w_codes), _ptr(sw), N, weight_bits, activation_bits,
+                                       int(fused), _ptr(y), _stream()))
+    return y
+
+
 def project_packed(x, w_codes, sw, outputs: int, bits: int):
     """packed::project (packed.rs:75-119) for one activation row."""
     import torch

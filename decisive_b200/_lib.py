@@ -58,6 +58,8 @@ SIGNATURES = [
     ("db_gemv_max_rows", _i32, []),
     ("db_linear_workspace_bytes", _sz, [_i64, _i64]),
     ("db_linear_g64", _i32, [_vp, _i64, _i64, _vp, _vp, _i64, _i32, _i32, _i32, _vp, _vp, _vp]),
+    ("db_linear_noalloc_scratch_bytes", _sz, []),
+    ("db_linear_g64_noalloc", _i32, [_vp, _i64, _i64, _vp, _vp, _i64, _i32, _i32, _i32, _vp, _vp]),
     ("db_project_packed", _i32, [_vp, _i64, _vp, _vp, _i64, _i32, _vp, _vp, _vp]),
     ("db_mlp_g64", _i32, [_vp, _i64, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _i32, _i32, _vp, _i64, _vp, _i64, _vp, _vp]),
     ("db_interleave_gate_up", _i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i32, _vp, _vp, _vp]),

@@ -116,6 +116,21 @@ size_t db_linear_workspace_bytes(int64_t M, int64_t K);
 int db_linear_g64(const float *x, int64_t M, int64_t K, const uint8_t *w_codes, const float *sw, int64_t N,
                   int weight_bits, int activation_bits, int fused, float *y, void *workspace, void *stream);
 
+/* Allocation-free variant of db_linear_g64 -- this entry point has no counterpart in the
+ * reference.  For hosts that pass device pointers but do not let the library allocate device
+ * memory (a fixed device-memory budget owned by the host, or a latency-critical caller that must
+ * never reach cudaMalloc and its implicit synchronisation) and that cannot size a workspace up
+ * front.  Its scratch is one array of DB_NOALLOC_SCRATCH_BYTES compiled into the library, held
+ * by every GPU that loads it until the process exits; larger shapes are rejected with code
+ * SCRATCH_LIMIT.  The first call on a device looks up the array's device address, so make it
+ * before any stream capture.  All calls on a device share the array (the entry point clears what
+ * must start at zero); calls that overlap on the GPU race on it and must be serialised by the
+ * caller.  No cudaMalloc, cudaFree or allocating library routine is called. */
+#define DB_NOALLOC_SCRATCH_BYTES (8u << 20)
+size_t db_linear_noalloc_scratch_bytes(void);
+int db_linear_g64_noalloc(const float *x, int64_t M, int64_t K, const uint8_t *w_codes, const float *sw, int64_t N,
+                          int weight_bits, int activation_bits, int fused, float *y, void *stream);
+
 /* Readout GEMV on one activation row.  Replaces packed::project (packed.rs:75-119; portable
  * numerics, activation 8-bit).  Returns DB_ERR_NONFINITE for a non-finite x. */
 int db_project_packed(const float *x, int64_t K, const uint8_t *w_codes, const float *sw, int64_t outputs,
