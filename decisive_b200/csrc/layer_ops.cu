@@ -21,123 +21,155 @@ __device__ __forceinline__ int gemv_pos(int k) {
     return b + ((j & 1) << 2) + (j >> 1);  // stored order 0,2,4,6,1,3,5,7
 }
 
-// One warp per row; D % 128 == 0 and D <= 4096.  Each lane owns float4 columns 4l + 128j.
-template <int VEC>
+// One CTA per row, one float4 per thread (blockDim = D/4, D % 128 == 0, D <= 4096): short
+// per-thread dependency chains and enough CTAs in flight to cover memory latency.
+// normalize = 0 skips the RMSNorm (plain group-64 activation quantiser of int8.rs:178-202).
+// Each warp covers 128 columns = two 64-groups (lanes 0-15, 16-31).  Code stores: lanes 2b and
+// 2b+1 hold the two halves (k0..k3, k4..k7) of one 8-code block; they swap halves with one
+// shuffle so each lane writes its part of the block's stored order with a single 8-byte
+// (tensor-core f16 order) or 4-byte (GEMV int8 order) store.
 __global__ void rms_quantize_kernel(const float* __restrict__ x, int64_t ldx, const float* __restrict__ w, int T,
-                                    int D, float eps, int zero_centered, float* __restrict__ normed,
+                                    int D, float eps, int zero_centered, int normalize, float* __restrict__ normed,
                                     int64_t ldn, void* __restrict__ codes, int layout, int64_t ldc,
                                     float* __restrict__ scales, int32_t* __restrict__ sums, int64_t lds,
                                     int* __restrict__ nonfinite) {
-    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-    if (warp >= T) return;
-    const int t = warp;
-    const int J = D / 128;
-    float4 v[VEC];
-    float ss = 0.f;
-    bool bad = false;
-#pragma unroll
-    for (int j = 0; j < VEC; ++j) {
-        if (j < J) {
-            v[j] = *reinterpret_cast<const float4*>(x + (size_t)t * ldx + 4 * lane + 128 * j);
-            bad |= !(isfinite(v[j].x) && isfinite(v[j].y) && isfinite(v[j].z) && isfinite(v[j].w));
-            ss = __fadd_rn(ss, __fmul_rn(v[j].x, v[j].x));
-            ss = __fadd_rn(ss, __fmul_rn(v[j].y, v[j].y));
-            ss = __fadd_rn(ss, __fmul_rn(v[j].z, v[j].z));
-            ss = __fadd_rn(ss, __fmul_rn(v[j].w, v[j].w));
-        }
-    }
-#pragma unroll
-    for (int o = 16; o; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+    __shared__ float partial[32];
+    const int t = blockIdx.x, lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    const int c = 4 * threadIdx.x;
+    const float4 v = *reinterpret_cast<const float4*>(x + (size_t)t * ldx + c);
+    const bool bad = !(isfinite(v.x) && isfinite(v.y) && isfinite(v.z) && isfinite(v.w));
     if (__any_sync(0xffffffffu, bad) && lane == 0 && nonfinite) atomicOr(nonfinite, 1);
-    const float scale = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), eps)));
+    float scale = 1.f;
+    if (normalize) {
+        float ss = __fadd_rn(__fadd_rn(__fmul_rn(v.x, v.x), __fmul_rn(v.y, v.y)),
+                             __fadd_rn(__fmul_rn(v.z, v.z), __fmul_rn(v.w, v.w)));
 #pragma unroll
-    for (int j = 0; j < VEC; ++j) {
-        if (j >= J) continue;
-        const int c = 4 * lane + 128 * j;
+        for (int o = 16; o; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+        if (lane == 0) partial[wid] = ss;
+        __syncthreads();
+        if (wid == 0) {
+            float tot = lane < (int)(blockDim.x >> 5) ? partial[lane] : 0.f;
+#pragma unroll
+            for (int o = 16; o; o >>= 1) tot = __fadd_rn(tot, __shfl_xor_sync(0xffffffffu, tot, o));
+            if (lane == 0) partial[0] = tot;
+        }
+        __syncthreads();
+        scale = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(partial[0], (float)D), eps)));
+    }
+    float o[4] = {v.x, v.y, v.z, v.w};
+    if (normalize) {
         const float4 wv = *reinterpret_cast<const float4*>(w + c);
-        float o[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
         const float ww[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
         for (int i = 0; i < 4; ++i)
             o[i] = __fmul_rn(__fmul_rn(o[i], scale), zero_centered ? __fadd_rn(1.f, ww[i]) : ww[i]);
-        if (normed) *reinterpret_cast<float4*>(normed + (size_t)t * ldn + c) = make_float4(o[0], o[1], o[2], o[3]);
-        if (codes) {
-            // group 2j (lanes 0-15) or 2j+1 (lanes 16-31): absmax over 16 lanes
-            float amax = fmaxf(fmaxf(fabsf(o[0]), fabsf(o[1])), fmaxf(fabsf(o[2]), fabsf(o[3])));
+    }
+    if (normed) *reinterpret_cast<float4*>(normed + (size_t)t * ldn + c) = make_float4(o[0], o[1], o[2], o[3]);
+    if (!codes) return;
+    float amax = fmaxf(fmaxf(fabsf(o[0]), fabsf(o[1])), fmaxf(fabsf(o[2]), fabsf(o[3])));
 #pragma unroll
-            for (int s = 8; s; s >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, s));
-            const float gs = fmaxf(__fdiv_rn(amax, 127.f), FLT_MIN);
-            const float inv = __fdiv_rn(1.f, gs);
-            int qs = 0;
-            int qv[4];
+    for (int s2 = 8; s2; s2 >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, s2));
+    const float gs = fmaxf(__fdiv_rn(amax, 127.f), FLT_MIN);
+    const float inv = __fdiv_rn(1.f, gs);
+    int q[4], p[4];
+    int qs = 0;
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                qv[i] = (int)fminf(fmaxf(rintf(__fmul_rn(o[i], inv)), -127.f), 127.f);
-                qs += qv[i];
-            }
-            const int g = c / DB_GROUP;
-            if (layout == DB_CODES_TC_F16) {
-                __half* dst = static_cast<__half*>(codes) + (size_t)t * ldc;
+    for (int i = 0; i < 4; ++i) {
+        q[i] = (int)fminf(fmaxf(rintf(__fmul_rn(o[i], inv)), -127.f), 127.f);
+        qs += q[i];
+    }
 #pragma unroll
-                for (int i = 0; i < 4; ++i) dst[tc_pos(c + i)] = __int2half_rn(qv[i]);
-            } else {
-                int8_t* dst = static_cast<int8_t*>(codes) + (size_t)t * ldc;
+    for (int i = 0; i < 4; ++i) p[i] = __shfl_xor_sync(0xffffffffu, q[i], 1);
+    const bool odd = lane & 1;
+    const int* lo = odd ? p : q;  // codes k0..k3 of the 8-code block
+    const int* hi = odd ? q : p;  // codes k4..k7
+    const int b8 = c & ~7;
+    if (layout == DB_CODES_TC_F16) {
+        // stored order k0,k4,k1,k5 | k2,k6,k3,k7
+        const int e0 = odd ? 2 : 0;
+        __half2 h0 = __halves2half2(__int2half_rn(lo[e0]), __int2half_rn(hi[e0]));
+        __half2 h1 = __halves2half2(__int2half_rn(lo[e0 + 1]), __int2half_rn(hi[e0 + 1]));
+        uint2 pk;
+        pk.x = *reinterpret_cast<uint32_t*>(&h0);
+        pk.y = *reinterpret_cast<uint32_t*>(&h1);
+        *reinterpret_cast<uint2*>(static_cast<__half*>(codes) + (size_t)t * ldc + b8 + (odd ? 4 : 0)) = pk;
+    } else if (layout == DB_CODES_GEMV_I8) {
+        // stored order k0,k2,k4,k6 | k1,k3,k5,k7
+        const int e = odd ? 1 : 0;
+        const uint32_t word = (uint32_t)(lo[e] & 255) | ((uint32_t)(lo[e + 2] & 255) << 8) |
+                              ((uint32_t)(hi[e] & 255) << 16) | ((uint32_t)(hi[e + 2] & 255) << 24);
+        *reinterpret_cast<uint32_t*>(static_cast<int8_t*>(codes) + (size_t)t * ldc + b8 + (odd ? 4 : 0)) = word;
+    } else {
+        const uint32_t word = (uint32_t)(q[0] & 255) | ((uint32_t)(q[1] & 255) << 8) |
+                              ((uint32_t)(q[2] & 255) << 16) | ((uint32_t)(q[3] & 255) << 24);
+        *reinterpret_cast<uint32_t*>(static_cast<int8_t*>(codes) + (size_t)t * ldc + c) = word;
+    }
 #pragma unroll
-                for (int i = 0; i < 4; ++i)
-                    dst[layout == DB_CODES_GEMV_I8 ? gemv_pos(c + i) : c + i] = (int8_t)qv[i];
-            }
-#pragma unroll
-            for (int s = 8; s; s >>= 1) qs += __shfl_xor_sync(0xffffffffu, qs, s);
-            if ((lane & 15) == 0) {
-                scales[(size_t)g * lds + t] = gs;
-                if (sums) sums[(size_t)g * lds + t] = qs;
-            }
-        }
+    for (int s2 = 8; s2; s2 >>= 1) qs += __shfl_xor_sync(0xffffffffu, qs, s2);
+    if ((lane & 15) == 0) {
+        const int g = c / DB_GROUP;
+        scales[(size_t)g * lds + t] = gs;
+        if (sums) sums[(size_t)g * lds + t] = qs;
     }
 }
 
-// One warp per (token, head) of q or k; head_dim 128.  qkv row: [q heads | k heads | v heads].
-// RoPE pairs (i, i+64); lane l holds dims 4l..4l+3, lanes 0-15 the first half.
+// One warp per (token, 4 consecutive heads); head_dim 128.  qkv row: [q heads | k heads | v heads].
+// RoPE pairs (i, i+64); lane l holds dims 4l..4l+3 of a head, lanes 0-15 the first half.
+constexpr int QK_HEADS_PER_WARP = 4;
 __global__ void qk_norm_rope_kernel(const float* __restrict__ qkv, int64_t ld, int T, int Hq, int Hk,
                                     const float* __restrict__ qw, const float* __restrict__ kw, float eps,
                                     const float* __restrict__ cos_t, const float* __restrict__ sin_t,
                                     __half* __restrict__ q16, __half* __restrict__ k16, __half* __restrict__ v16) {
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     const int heads = Hq + 2 * Hk;
-    if (warp >= T * heads) return;
-    const int t = warp / heads, h = warp % heads;
-    const float* src = qkv + (size_t)t * ld + h * 128;
-    float4 v = *reinterpret_cast<const float4*>(src + 4 * lane);
-    if (h >= Hq + Hk) {  // value head: convert only
-        __half* dst = v16 + ((size_t)t * Hk + (h - Hq - Hk)) * 128 + 4 * lane;
-        *reinterpret_cast<__half2*>(dst) = __floats2half2_rn(v.x, v.y);
-        *reinterpret_cast<__half2*>(dst + 2) = __floats2half2_rn(v.z, v.w);
-        return;
-    }
-    const bool is_q = h < Hq;
-    const float* w = is_q ? qw : kw;
-    float ss = __fadd_rn(__fadd_rn(__fmul_rn(v.x, v.x), __fmul_rn(v.y, v.y)),
-                         __fadd_rn(__fmul_rn(v.z, v.z), __fmul_rn(v.w, v.w)));
+    const int units = (heads + QK_HEADS_PER_WARP - 1) / QK_HEADS_PER_WARP;
+    if (warp >= T * units) return;
+    const int t = warp / units, h0 = (warp % units) * QK_HEADS_PER_WARP;
+    float4 v[QK_HEADS_PER_WARP];
 #pragma unroll
-    for (int o = 16; o; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
-    const float scale = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, 128.f), eps)));
-    const float4 wv = *reinterpret_cast<const float4*>(w + 4 * lane);
-    float o[4] = {__fmul_rn(__fmul_rn(v.x, scale), wv.x), __fmul_rn(__fmul_rn(v.y, scale), wv.y),
-                  __fmul_rn(__fmul_rn(v.z, scale), wv.z), __fmul_rn(__fmul_rn(v.w, scale), wv.w)};
-    float p[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) p[i] = __shfl_xor_sync(0xffffffffu, o[i], 16);  // partner dims +-64
+    for (int u = 0; u < QK_HEADS_PER_WARP; ++u)
+        if (h0 + u < heads) v[u] = *reinterpret_cast<const float4*>(qkv + (size_t)t * ld + (h0 + u) * 128 + 4 * lane);
     const int i0 = (4 * lane) & 63;
-    float r[4];
+    const float4 cs = *reinterpret_cast<const float4*>(cos_t + (size_t)t * 64 + i0);
+    const float4 sn = *reinterpret_cast<const float4*>(sin_t + (size_t)t * 64 + i0);
+    const float cc[4] = {cs.x, cs.y, cs.z, cs.w}, ssn[4] = {sn.x, sn.y, sn.z, sn.w};
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const float c = cos_t[(size_t)t * 64 + i0 + i], s = sin_t[(size_t)t * 64 + i0 + i];
-        if (lane < 16) r[i] = __fsub_rn(__fmul_rn(o[i], c), __fmul_rn(p[i], s));  // a*c - b*s
-        else r[i] = __fadd_rn(__fmul_rn(o[i], c), __fmul_rn(p[i], s));           // b*c + a*s
+    for (int u = 0; u < QK_HEADS_PER_WARP; ++u) {
+        const int h = h0 + u;
+        if (h >= heads) break;
+        if (h >= Hq + Hk) {  // value head: convert only
+            __half* dst = v16 + ((size_t)t * Hk + (h - Hq - Hk)) * 128 + 4 * lane;
+            __half2 a = __floats2half2_rn(v[u].x, v[u].y), b2 = __floats2half2_rn(v[u].z, v[u].w);
+            uint2 pk;
+            pk.x = *reinterpret_cast<uint32_t*>(&a);
+            pk.y = *reinterpret_cast<uint32_t*>(&b2);
+            *reinterpret_cast<uint2*>(dst) = pk;
+            continue;
+        }
+        const bool is_q = h < Hq;
+        const float* w = is_q ? qw : kw;
+        float ss = __fadd_rn(__fadd_rn(__fmul_rn(v[u].x, v[u].x), __fmul_rn(v[u].y, v[u].y)),
+                             __fadd_rn(__fmul_rn(v[u].z, v[u].z), __fmul_rn(v[u].w, v[u].w)));
+#pragma unroll
+        for (int o = 16; o; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+        const float scale = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, 128.f), eps)));
+        const float4 wv = *reinterpret_cast<const float4*>(w + 4 * lane);
+        float o[4] = {__fmul_rn(__fmul_rn(v[u].x, scale), wv.x), __fmul_rn(__fmul_rn(v[u].y, scale), wv.y),
+                      __fmul_rn(__fmul_rn(v[u].z, scale), wv.z), __fmul_rn(__fmul_rn(v[u].w, scale), wv.w)};
+        float r[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float p = __shfl_xor_sync(0xffffffffu, o[i], 16);  // partner dims +-64
+            if (lane < 16) r[i] = __fsub_rn(__fmul_rn(o[i], cc[i]), __fmul_rn(p, ssn[i]));  // a*c - b*s
+            else r[i] = __fadd_rn(__fmul_rn(o[i], cc[i]), __fmul_rn(p, ssn[i]));           // b*c + a*s
+        }
+        __half* dst = is_q ? q16 + ((size_t)t * Hq + h) * 128 : k16 + ((size_t)t * Hk + (h - Hq)) * 128;
+        __half2 a = __floats2half2_rn(r[0], r[1]), b2 = __floats2half2_rn(r[2], r[3]);
+        uint2 pk;
+        pk.x = *reinterpret_cast<uint32_t*>(&a);
+        pk.y = *reinterpret_cast<uint32_t*>(&b2);
+        *reinterpret_cast<uint2*>(dst + 4 * lane) = pk;
     }
-    __half* dst = is_q ? q16 + ((size_t)t * Hq + h) * 128 : k16 + ((size_t)t * Hk + (h - Hq)) * 128;
-    *reinterpret_cast<__half2*>(dst + 4 * lane) = __floats2half2_rn(r[0], r[1]);
-    *reinterpret_cast<__half2*>(dst + 4 * lane + 2) = __floats2half2_rn(r[2], r[3]);
 }
 
 // pooled[d] = (sum over t, in order, of x[t, d]) / T
@@ -145,6 +177,7 @@ __global__ void mean_pool_kernel(const float* __restrict__ x, int64_t ldx, int T
     const int d = blockIdx.x * blockDim.x + threadIdx.x;
     if (d >= D) return;
     float s = 0.f;
+#pragma unroll 16
     for (int t = 0; t < T; ++t) s = __fadd_rn(s, x[(size_t)t * ldx + d]);
     out[d] = __fdiv_rn(s, (float)T);
 }
@@ -160,17 +193,11 @@ using namespace db;
 
 int db_launch_rms_quantize(const float* x, int64_t ldx, const float* w, int T, int D, float eps, int zero_centered,
                            float* normed, int64_t ldn, void* codes, int layout, int64_t ldc, float* scales,
-                           int32_t* sums, int64_t lds, int* nonfinite, cudaStream_t stream) {
+                           int32_t* sums, int64_t lds, int* nonfinite, cudaStream_t stream, int normalize) {
     if (T <= 0) return 0;
     if (D % 128 || D > 4096) return (int)cudaErrorInvalidValue;
-    const unsigned blocks = (unsigned)((T + 7) / 8);
-    const int J = D / 128;
-    if (J <= 8)
-        rms_quantize_kernel<8><<<blocks, 256, 0, stream>>>(x, ldx, w, T, D, eps, zero_centered, normed, ldn, codes,
-                                                           layout, ldc, scales, sums, lds, nonfinite);
-    else
-        rms_quantize_kernel<32><<<blocks, 256, 0, stream>>>(x, ldx, w, T, D, eps, zero_centered, normed, ldn, codes,
-                                                            layout, ldc, scales, sums, lds, nonfinite);
+    rms_quantize_kernel<<<T, D / 4, 0, stream>>>(x, ldx, w, T, D, eps, zero_centered, normalize, normed, ldn, codes,
+                                                 layout, ldc, scales, sums, lds, nonfinite);
     return (int)cudaGetLastError();
 }
 
@@ -178,8 +205,8 @@ int db_launch_qk_norm_rope(const float* qkv, int64_t ld, int T, int Hq, int Hk, 
                            float eps, const float* cos_t, const float* sin_t, __half* q16, __half* k16, __half* v16,
                            cudaStream_t stream) {
     if (T <= 0) return 0;
-    const int64_t warps = (int64_t)T * (Hq + 2 * Hk);
-    qk_norm_rope_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, stream>>>(qkv, ld, T, Hq, Hk, qw, kw, eps, cos_t,
+    const int64_t warps = (int64_t)T * ((Hq + 2 * Hk + QK_HEADS_PER_WARP - 1) / QK_HEADS_PER_WARP);
+    qk_norm_rope_kernel<<<(unsigned)((warps + 3) / 4), 128, 0, stream>>>(qkv, ld, T, Hq, Hk, qw, kw, eps, cos_t,
                                                                           sin_t, q16, k16, v16);
     return (int)cudaGetLastError();
 }

@@ -6,7 +6,7 @@
 
 int db_launch_rms_quantize(const float* x, int64_t ldx, const float* w, int T, int D, float eps, int zero_centered,
                            float* normed, int64_t ldn, void* codes, int layout, int64_t ldc, float* scales,
-                           int32_t* sums, int64_t lds, int* nonfinite, cudaStream_t stream);
+                           int32_t* sums, int64_t lds, int* nonfinite, cudaStream_t stream, int normalize = 1);
 int db_launch_qk_norm_rope(const float* qkv, int64_t ld, int T, int Hq, int Hk, const float* qw, const float* kw,
                            float eps, const float* cos_t, const float* sin_t, __half* q16, __half* k16, __half* v16,
                            cudaStream_t stream);

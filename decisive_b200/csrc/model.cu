@@ -316,8 +316,8 @@ int enqueue_forward(db_model* m, int T, const volatile int32_t* cancel) {
             });
         if (!rc)
             rc = timed(5, [&] {
-                return db_launch_quantize_rows(m->ctx, DB_F32, Nq, T, Nq, 8, m->acodes, DB_CODES_TC, ld_codes, m->sa,
-                                               nullptr, lds, m->flag, st);
+                return db_launch_rms_quantize(m->ctx, Nq, nullptr, T, Nq, 0.f, 0, nullptr, 0, m->acodes, DB_CODES_TC,
+                                              ld_codes, m->sa, nullptr, lds, m->flag, st, /*normalize=*/0);
             });
         if (!rc) rc = timed(6, [&] { return gemm(m->acodes, w.o_c, w.o_s, m->sa, D, Nq, DB_EPI_RESIDUAL, m->x, D); });
         if (!rc)
