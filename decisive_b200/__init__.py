@@ -96,13 +96,22 @@ def dequant_rows(codes, scales, N: int, K: int, bits: int, ids=None):
     return out
 
 
-def gemm(a_codes, layout, sa, w_codes, sw, M, N, K, bits, fused=True, a_sums=None, residual=None, nonfinite=None):
-    """Matrix::apply_prepared (int8.rs:229-288) on prepared activations -> y f32 [M, N]."""
+class GemmConfig(C.Structure):
+    """db_gemm_config: tile width (0 = default, 64, 128), persistent grid cap (0 = all SMs) and
+    CTA pairing (1 = clusters of two CTAs with M = 256 MMAs).  The tuner's candidate space."""
+    _fields_ = [("block_n", C.c_int), ("max_ctas", C.c_int), ("pair_ctas", C.c_int)]
+
+
+def gemm(a_codes, layout, sa, w_codes, sw, M, N, K, bits, fused=True, a_sums=None, residual=None, nonfinite=None,
+         config=None):
+    """Matrix::apply_prepared (int8.rs:229-288) on prepared activations -> y f32 [M, N].
+    config: optional GemmConfig (tile configuration of the tensor-core path)."""
     import torch
     y = residual if residual is not None else torch.empty((M, N), dtype=torch.float32, device=w_codes.device)
-    check(load().db_gemm_g64(_ptr(a_codes), layout, a_codes.stride(0), _ptr(sa), _ptr(a_sums), sa.stride(0),
-                             _ptr(w_codes), _ptr(sw), M, N, K, bits, int(fused), int(residual is not None), _ptr(y),
-                             N, _ptr(nonfinite), _stream()))
+    cfg = C.byref(config) if config is not None else None
+    check(load().db_gemm_g64_config(_ptr(a_codes), layout, a_codes.stride(0), _ptr(sa), _ptr(a_sums), sa.stride(0),
+                                    _ptr(w_codes), _ptr(sw), M, N, K, bits, int(fused), int(residual is not None),
+                                    _ptr(y), N, _ptr(nonfinite), cfg, _stream()))
     return y
 
 

@@ -55,6 +55,8 @@ SIGNATURES = [
     ("db_dequant_rows_g64", _i32, [_vp, _vp, _i64, _i64, _i32, _vp, _i64, _vp, _i64, _vp]),
     ("db_gemm_g64", _i32, [_vp, _i32, _i64, _vp, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _i32, _i32, _i32, _vp, _i64,
                            _vp, _vp]),
+    ("db_gemm_g64_config", _i32, [_vp, _i32, _i64, _vp, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _i32, _i32, _i32, _vp,
+                                  _i64, _vp, _vp, _vp]),
     ("db_gemv_max_rows", _i32, []),
     ("db_linear_workspace_bytes", _sz, [_i64, _i64]),
     ("db_linear_g64", _i32, [_vp, _i64, _i64, _vp, _vp, _i64, _i32, _i32, _i32, _vp, _vp, _vp]),

@@ -137,6 +137,17 @@ int db_gemv_max_rows(void) { return db_gemv_rows_limit(); }
 int db_gemm_g64(const void* a_codes, int layout, int64_t lda, const float* sa, const int32_t* a_sums, int64_t ldsa,
                 const uint8_t* w_codes, const float* sw, int64_t M, int64_t N, int64_t K, int bits, int fused,
                 int residual, float* y, int64_t ldy, const int* nonfinite, void* stream) {
+    return db_gemm_g64_config(a_codes, layout, lda, sa, a_sums, ldsa, w_codes, sw, M, N, K, bits, fused, residual, y,
+                              ldy, nonfinite, nullptr, stream);
+}
+
+int db_gemm_g64_config(const void* a_codes, int layout, int64_t lda, const float* sa, const int32_t* a_sums,
+                       int64_t ldsa, const uint8_t* w_codes, const float* sw, int64_t M, int64_t N, int64_t K,
+                       int bits, int fused, int residual, float* y, int64_t ldy, const int* nonfinite,
+                       const db_gemm_config* config, void* stream) {
+    if (config && ((config->block_n != 0 && config->block_n != 64 && config->block_n != 128) || config->max_ctas < 0 ||
+                   (config->pair_ctas != 0 && config->pair_ctas != 1)))
+        return db_fail(DB_ERR_INVALID_ARGUMENT, "INVALID_ARGUMENT", "gemm: bad tile configuration");
     if (M < 0 || N <= 0 || K <= 0 || (bits != 4 && bits != 8) || ldy < N || ldsa < M)
         return db_fail(DB_ERR_INVALID_ARGUMENT, "INVALID_ARGUMENT", "gemm: bad shape");
     if (M == 0) return DB_OK;
@@ -166,6 +177,11 @@ int db_gemm_g64(const void* a_codes, int layout, int64_t lda, const float* sa, c
     a.ldy = ldy;
     a.nonfinite = nonfinite;
     a.dev_error = db_device_error_ptr();
+    if (config) {
+        a.block_n = config->block_n;
+        a.max_ctas = config->max_ctas;
+        a.pair_ctas = config->pair_ctas;
+    }
     return db_cuda_status(db_launch_gemm_tc(a, S(stream)), "gemm");
 }
 

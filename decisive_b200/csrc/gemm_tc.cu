@@ -7,19 +7,25 @@
 // The integer dots come from tcgen05.mma kind::f16 on integer-valued f16 operands: every code
 // is exact in f16, every product and every partial sum of one group (|sum| <= 64*127*127 < 2^24)
 // is an exact f32 integer, so the tensor core returns dot_g exactly.  Each 64-wide group is one
-// K-block; its dot lands in its own TMEM buffer (double buffered) and the epilogue warps fold it
-// into their register accumulators with the reference's rounding, in group order.
+// K-block; its dot lands in its own TMEM buffer (four buffers) and the epilogue warps fold it into
+// their register accumulators with the reference's rounding, in group order.
 //
-// Roles (448 threads, one CTA per SM, persistent over 128 x BN output tiles):
-//   warp 0      TMA producer: activation-code tiles (128 x 64 f16, 128B swizzle) and raw weight
-//               code tiles (BN rows x 32|64 bytes) into smem rings
-//   warp 1      TMEM owner + MMA issuer (one elected lane): 4 x (128 x BN x 16) MMAs per group
-//   warps 2-5   converters: weight nibbles/bytes -> f16 codes in the UMMA K-major SW128 layout
-//   warps 6-13  epilogue: TMEM -> registers, per-group scale fold, final store / fused SwiGLU
-//               re-quantisation (grouped_q4_mlp.wgsl:83-105 semantics)
+// Roles (512 threads, one CTA per SM, persistent over 128 x BN output tiles):
+//   warp 0      TMA producer: one stage per pair of K groups, loaded by a single three-lane TMA
+//               instruction (activation tiles of both groups, 128 x 64 f16 with 128B swizzle, and
+//               the raw weight codes of both groups, BN rows)
+//   warp 1      TMEM owner + MMA issuer (one elected lane): 4 x (128 x BN x 16) MMAs per group;
+//               its commit releases the stage once both groups of the pair are multiplied
+//   warps 2-5   converters (one per SM sub-partition): weight nibbles/bytes -> f16 codes in the
+//               UMMA K-major SW128 layout, one B tile per group (warps 6-7 idle)
+//   warps 8-15  epilogue (192 registers each through setmaxnreg): per-group scale vectors prefetched with cp.async a few groups ahead,
+//               TMEM -> registers, f32x2 scale fold, final store / fused SwiGLU re-quantisation
+//               (grouped_q4_mlp.wgsl:83-105 semantics)
 // Every mbarrier wait is bounded (DB_WAIT_LIMIT_NS); on expiry the CTA records an error in the
-// device error word, stops issuing work, and releases its tensor memory.
+// device error word, stops issuing work, lets its own copies and MMAs land, and releases its
+// tensor memory.
 #include <float.h>
+#include <string.h>
 
 #include <mutex>
 
@@ -30,49 +36,76 @@ namespace db {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
-constexpr int B_STAGES = 3;   // converted f16 weight tiles (converter -> MMA)
-constexpr int NUM_ACC = 4;    // TMEM accumulator buffers (NUM_ACC x BN columns <= 512)
-// Warp roles: 0 = TMA producer, 1 = MMA issuer, then the converters, then 8 epilogue warps.
-#ifndef DB_GEMM_CONVERTER_WARPS
-#define DB_GEMM_CONVERTER_WARPS 2
-#endif
+constexpr int NUM_ACC = 4;         // TMEM accumulator buffers (NUM_ACC x BN columns <= 512)
 constexpr int CONVERTER_WARP0 = 2;
-constexpr int CONVERTER_WARPS = DB_GEMM_CONVERTER_WARPS;
-constexpr int EPILOGUE_WARP0 = CONVERTER_WARP0 + CONVERTER_WARPS;
+constexpr int CONVERTER_WARPS = 4;  // warps 2-5; warps 6-7 only fill their warpgroup
+constexpr int EPILOGUE_WARP0 = 8;   // warps 8-15: warpgroups 2 and 3
 constexpr int EPILOGUE_WARPS = 8;
-constexpr int NUM_THREADS = 32 * (EPILOGUE_WARP0 + EPILOGUE_WARPS);
-constexpr int XCH_STRIDE = 65;  // floats per row of the SwiGLU exchange buffer (bank-conflict free)
+constexpr int NUM_THREADS = 32 * (EPILOGUE_WARP0 + EPILOGUE_WARPS);  // 512
+// Register split (setmaxnreg, per warpgroup): the launch gives every thread 65536 / 512 = 128;
+// warpgroups 0-1 (producer, MMA, converters) drop to 64 and warpgroups 2-3 (epilogue) rise to
+// 192, so 2 * 128 * 64 + 2 * 128 * 192 = 65536 stays within the launch's allocation.
+constexpr int REGS_CONTROL = 64;
+constexpr int REGS_EPILOGUE = 192;
+static_assert(2 * 128 * REGS_CONTROL + 2 * 128 * REGS_EPILOGUE == 65536, "register split");
+constexpr int SC_DEPTH = 6;        // groups of scale vectors each epilogue warp keeps in flight
+constexpr int XCH_STRIDE = 33;     // floats per row of the SwiGLU exchange buffers (bank-conflict free)
+constexpr uint64_t DRAIN_NS = 100000000ull;  // wind-down wait for in-flight copies / MMAs
 
-// One pipeline stage per 64-wide K group holds everything the group needs: the activation-code
-// tile, the raw weight-code tile and the group's scale vectors.  The epilogue is the last
-// consumer of every part, so it alone releases the stage; the producer issues one wait, one
-// expect-tx and four copies per group.
-template <int BN, int BITS, int EPI>
+template <int BN, int BITS, int EPI, bool PAIR>
 struct GemmSmem {
-    static constexpr int STAGES = BITS == 4 ? 6 : 5;
-    static constexpr int A_BYTES = BM * BK * 2;          // 16 KB
-    static constexpr int W_ROW = BK * BITS / 8;          // 32 or 64 bytes of raw codes per row
-    static constexpr int W_BYTES = BN * W_ROW;
-    static constexpr int SC_BYTES = (BM + BN) * 4;       // sa then sw of the group
-    static constexpr int ST_A = 0, ST_W = A_BYTES, ST_S = A_BYTES + W_BYTES;
-    static constexpr int STAGE_BYTES = (ST_S + SC_BYTES + 1023) / 1024 * 1024;
-    static constexpr int TX_BYTES = A_BYTES + W_BYTES + SC_BYTES;
-    static constexpr int B_BYTES = BN * BK * 2;          // f16 codes
-    static constexpr int XCH_BYTES = EPI == DB_EPI_SWIGLU_QUANT ? BM * XCH_STRIDE * 4 : 0;
+    static constexpr int WR = PAIR ? BN / 2 : BN;          // weight rows held by this CTA
+    static constexpr int A_BYTES = BM * BK * 2;            // one group of activation codes, 16 KB
+    static constexpr int W_ROW = BK * BITS / 8;            // raw weight-code bytes per row and group
+    static constexpr int WP_BYTES = WR * 2 * W_ROW;        // raw weight codes of a group pair
+    static constexpr int STAGE_BYTES = (2 * A_BYTES + WP_BYTES + 1023) / 1024 * 1024;
+    static constexpr int TX_BYTES = 2 * A_BYTES + WP_BYTES;  // full boxes, also for a lone tail group
+    static constexpr int B_BYTES = WR * BK * 2;            // converted f16 weight tile of one group
+    static constexpr int COLS = BN / 2;                    // accumulator columns per epilogue thread
+    static constexpr int SC_SLOT = (32 + COLS) * 4;        // sa of a warp's 32 rows + sw of its columns
+    static constexpr int SC_BYTES = EPILOGUE_WARPS * SC_DEPTH * SC_SLOT;
+    // SwiGLU exchange: 32 gate and 32 up columns per row, plus each half's row maxima
+    static constexpr int XCH_BYTES = EPI == DB_EPI_SWIGLU_QUANT ? 2 * BM * XCH_STRIDE * 4 + 2 * BM * 4 : 0;
+    // output staging for the TMA store: per epilogue warp two buffers of 32 rows x 16 f32 columns
+    static constexpr int Y_CHUNK = 32 * 16 * 4;
+    static constexpr int Y_BYTES = EPI == DB_EPI_SWIGLU_QUANT ? 0 : EPILOGUE_WARPS * 2 * Y_CHUNK;
+    static constexpr int BUDGET = 232448 - 1024 - 512;     // opt-in limit - alignment slack - barriers
+    static constexpr bool fits(int st, int b) {
+        return SC_BYTES + XCH_BYTES + Y_BYTES + st * STAGE_BYTES + b * B_BYTES <= BUDGET;
+    }
+    static constexpr int B_STAGES = fits(3, 8) ? 8 : fits(3, 6) ? 6 : fits(3, 4) ? 4 : 3;
+    static constexpr int STAGES = fits(4, B_STAGES) ? 4 : fits(3, B_STAGES) ? 3 : 2;
     static constexpr int OFF_STAGE = 0;
     static constexpr int OFF_B = OFF_STAGE + STAGES * STAGE_BYTES;
-    static constexpr int OFF_X = OFF_B + B_STAGES * B_BYTES;
-    static constexpr int OFF_BAR = (OFF_X + XCH_BYTES + 15) / 16 * 16;
-    static constexpr int NUM_BARS = 2 * STAGES + 2 * B_STAGES + 2 * NUM_ACC + 2;
+    static constexpr int OFF_SC = OFF_B + B_STAGES * B_BYTES;
+    static constexpr int OFF_X = OFF_SC + SC_BYTES;
+    static constexpr int OFF_Y = OFF_X + XCH_BYTES;
+    static constexpr int OFF_BAR = (OFF_Y + Y_BYTES + 15) / 16 * 16;
+    static constexpr int NUM_BARS = 3 * STAGES + 2 * B_STAGES + 2 * NUM_ACC + 4;
     static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
-    static constexpr int BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
-    static_assert(BYTES <= 232448, "shared memory budget");
+    static constexpr int BYTES = OFF_MISC + 16 + 1024;     // + alignment slack
+    static_assert(fits(STAGES, B_STAGES) && BYTES <= 232448, "shared memory budget");
+    static_assert(STAGE_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "SW128 tiles need 1024-byte alignment");
 };
 
+// Warp-wide bounded wait.  Only lane 0 polls the barrier (32 pollers per warp would flood the
+// shared-memory barrier unit that every role's waits go through); the other lanes are released by
+// the __syncwarp, which also orders their later accesses after lane 0's acquire.
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err,
                                           int code) {
-    bool ok = mbar_wait(bar, parity, abort_flag, err, code);
-    return __all_sync(0xffffffffu, ok);
+    int ok = 1;
+    if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, abort_flag, err, code);
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    __syncwarp();
+    return ok != 0;
+}
+__device__ __forceinline__ bool warp_wait_backoff(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                                  int* err, int code) {
+    int ok = 1;
+    if ((threadIdx.x & 31) == 0) ok = mbar_wait_backoff(bar, parity, abort_flag, err, code);
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    __syncwarp();
+    return ok != 0;
 }
 
 // 8 weight nibbles (bytes of one row, k = 8c..8c+7) -> 8 f16 codes in the order 0,4,1,5,2,6,3,7.
@@ -120,82 +153,94 @@ __device__ __forceinline__ uint4 bytes_to_f16(uint32_t w0, uint32_t w1) {
 }
 
 __device__ __forceinline__ float silu_ref(float x) {
-    // cpu.rs:513-518: x * (1 / (1 + exp(-x)))
-    return __fmul_rn(x, __fdiv_rn(1.f, __fadd_rn(1.f, expf(-x))));
+    // cpu.rs:513-518: x * (1 / (1 + exp(-x))); the correctly rounded reciprocal is exactly the
+    // correctly rounded quotient 1 / y
+    return __fmul_rn(x, __frcp_rn(__fadd_rn(1.f, expf(-x))));
 }
 
-// Epilogue helpers: one warp owns 32 rows (its TMEM lane quadrant) x COLS columns of the tile.
-template <int COLS>
-__device__ __forceinline__ void tmem_load_cols(uint32_t taddr, uint32_t (&v)[COLS]) {
+// Folds one group's 16 columns into 8 packed accumulator pairs:
+//   fused:    acc = fma(d, sw * sa, acc)     (AVX2 path, int8.rs:566-572)
+//   portable: acc = acc + d * (sa * sw)      (int8.rs:259-287)
+// w holds the 16 weight scales of these columns (the same for every lane).
+template <bool FUSED>
+__device__ __forceinline__ void fold16(uint64_t* acc, const uint32_t (&v)[16], const uint4 (&w)[4], float s_a) {
+    const uint64_t sa2 = f2_pack(__float_as_uint(s_a), __float_as_uint(s_a));
 #pragma unroll
-    for (int c = 0; c < COLS / 32; ++c)
-        tmem_ld_32x32b_x32(taddr + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&v[c * 32]));
-}
-template <int COLS>
-__device__ __forceinline__ void tmem_wait_cols(uint32_t (&v)[COLS]) {
-    tmem_wait_ld(*reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+    for (int i = 0; i < 4; ++i) {
+        const int j = 4 * i;
+        if (FUSED) {
+            acc[j / 2] = f2_fma(f2_pack(v[j], v[j + 1]), f2_mul(f2_pack(w[i].x, w[i].y), sa2), acc[j / 2]);
+            acc[j / 2 + 1] = f2_fma(f2_pack(v[j + 2], v[j + 3]), f2_mul(f2_pack(w[i].z, w[i].w), sa2), acc[j / 2 + 1]);
+        } else {
+            // scalar: the packed add/mul pair does not reproduce the reference's rounding here
+            const uint32_t ww[4] = {w[i].x, w[i].y, w[i].z, w[i].w};
 #pragma unroll
-    for (int c = 1; c < COLS / 32; ++c) {
-        uint32_t(&w)[32] = *reinterpret_cast<uint32_t(*)[32]>(&v[c * 32]);
-        asm volatile(""
-                     : "+r"(w[0]), "+r"(w[1]), "+r"(w[2]), "+r"(w[3]), "+r"(w[4]), "+r"(w[5]), "+r"(w[6]),
-                       "+r"(w[7]), "+r"(w[8]), "+r"(w[9]), "+r"(w[10]), "+r"(w[11]), "+r"(w[12]), "+r"(w[13]),
-                       "+r"(w[14]), "+r"(w[15]), "+r"(w[16]), "+r"(w[17]), "+r"(w[18]), "+r"(w[19]), "+r"(w[20]),
-                       "+r"(w[21]), "+r"(w[22]), "+r"(w[23]), "+r"(w[24]), "+r"(w[25]), "+r"(w[26]), "+r"(w[27]),
-                       "+r"(w[28]), "+r"(w[29]), "+r"(w[30]), "+r"(w[31]));
-    }
-}
-// acc[j] = fma(d[j], sw[j]*sa, acc[j]) (fused) or acc[j] + d[j]*(sa*sw[j]) (portable).  Scalar
-// FMUL/FFMA: on this part the packed f32x2 forms run at a lower element rate than scalar FFMA.
-template <int COLS, bool FUSED>
-__device__ __forceinline__ void fold_group(float2 (&acc)[COLS / 2], const uint32_t (&v)[COLS], const float* swp,
-                                           float s_a) {
-#pragma unroll
-    for (int j = 0; j < COLS; j += 4) {
-        const float4 w4 = *reinterpret_cast<const float4*>(swp + j);
-        const float w[4] = {w4.x, w4.y, w4.z, w4.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            float& a = (e & 1) ? acc[(j + e) / 2].y : acc[(j + e) / 2].x;
-            const float d = __uint_as_float(v[j + e]);
-            if (FUSED) a = __fmaf_rn(d, __fmul_rn(w[e], s_a), a);
-            else a = __fadd_rn(a, __fmul_rn(d, __fmul_rn(s_a, w[e])));
+            for (int e = 0; e < 4; e += 2) {
+                uint64_t& a = acc[(j + e) / 2];
+                const float lo = __fadd_rn(f2_lo(a), __fmul_rn(__uint_as_float(v[j + e]),
+                                                               __fmul_rn(s_a, __uint_as_float(ww[e]))));
+                const float hi = __fadd_rn(f2_hi(a), __fmul_rn(__uint_as_float(v[j + e + 1]),
+                                                               __fmul_rn(s_a, __uint_as_float(ww[e + 1]))));
+                a = f2_pack(__float_as_uint(lo), __float_as_uint(hi));
+            }
         }
     }
 }
 
-template <int BN, int BITS, int EPI, bool FUSED>
+template <int BN, int BITS, int EPI, bool FUSED, bool PAIR>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
+                   const __grid_constant__ CUtensorMap tmY, int y_tma,
                    const float* __restrict__ sa, int64_t ldsa, const float* __restrict__ sw, int64_t ldsw, int M,
                    int N, int G, float* __restrict__ y, int64_t ldy, __half* __restrict__ out_codes, int64_t ldoc,
                    float* __restrict__ out_scales, int64_t ldos, const int* __restrict__ nonfinite,
                    int* __restrict__ dev_error) {
-    using S = GemmSmem<BN, BITS, EPI>;
+    using S = GemmSmem<BN, BITS, EPI, PAIR>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::OFF_BAR);
     uint64_t* full = bars;                   // stage loaded (TMA tx)
-    uint64_t* empty = full + S::STAGES;      // stage released by the epilogue warps
-    uint64_t* b_full = empty + S::STAGES;    // converted weight tile ready
-    uint64_t* b_empty = b_full + B_STAGES;   // converted tile consumed by the MMA
-    uint64_t* acc_full = b_empty + B_STAGES;
+    uint64_t* empty = full + S::STAGES;      // stage released by the MMA commit
+    uint64_t* b_full = empty + S::STAGES;    // converted weight tile ready (4 converter warps)
+    uint64_t* b_empty = b_full + S::B_STAGES;  // converted tile consumed by the MMA
+    uint64_t* acc_full = b_empty + S::B_STAGES;
     uint64_t* acc_empty = acc_full + NUM_ACC;
-    uint64_t* xch_full = acc_empty + NUM_ACC;  // SwiGLU exchange: up half -> gate half
-    uint64_t* xch_empty = xch_full + 1;
+    uint64_t* xch_full = acc_empty + NUM_ACC;  // SwiGLU exchange: both halves' columns published
+    uint64_t* xch_empty = xch_full + 1;        // every epilogue warp is done with this tile's exchange
+    uint64_t* xch_amax = xch_empty + 1;        // both halves' row maxima published
+    uint64_t* mma_done = xch_amax + 1;         // final commit of the MMA issuer
+    uint64_t* wfull = mma_done + 1;            // pair mode: this CTA's raw weight codes loaded
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::OFF_MISC);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + S::OFF_MISC + 4);
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
-    const int m_tiles = (M + BM - 1) / BM, n_tiles = (N + BN - 1) / BN;
+    // Pair mode: a cluster of two CTAs computes 256 x BN tiles; CTA `rank` owns rows 128*rank.. of
+    // the tile and weight rows (BN/2)*rank.. of it, the even CTA issues the M = 256 MMAs.
+    const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+    const bool leader = rank == 0;
+    constexpr int MT = PAIR ? 2 * BM : BM;    // tile rows
+    const int m_tiles = (M + MT - 1) / MT, n_tiles = (N + BN - 1) / BN;
     const int tiles = m_tiles * n_tiles;
+    const int tile0 = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+    const int tstride = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+    const int row_off = (int)rank * BM, wrow_off = (int)rank * S::WR;
+    // barrier addresses as the pair sees them (rank-0 copies for the leader-counted barriers)
+    auto at_leader = [&](uint64_t* b) { return PAIR ? mapa_shared(smem_u32(b), 0) : smem_u32(b); };
+    auto at_peer = [&](uint64_t* b) { return mapa_shared(smem_u32(b), 1); };
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < S::STAGES; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], EPILOGUE_WARPS); }
-        for (int i = 0; i < B_STAGES; ++i) { mbar_init(&b_full[i], CONVERTER_WARPS); mbar_init(&b_empty[i], 1); }
-        for (int i = 0; i < NUM_ACC; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], EPILOGUE_WARPS); }
-        mbar_init(xch_full, 4);
-        mbar_init(xch_empty, 4);
+        constexpr int NC = PAIR ? 2 : 1;  // leader-counted barriers hear from both CTAs
+        for (int i = 0; i < S::STAGES; ++i) {
+            mbar_init(&full[i], NC);
+            mbar_init(&empty[i], 1);
+            mbar_init(&wfull[i], 1);
+        }
+        for (int i = 0; i < S::B_STAGES; ++i) { mbar_init(&b_full[i], NC * CONVERTER_WARPS); mbar_init(&b_empty[i], 1); }
+        for (int i = 0; i < NUM_ACC; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], NC * EPILOGUE_WARPS); }
+        mbar_init(xch_full, EPILOGUE_WARPS);
+        mbar_init(xch_empty, EPILOGUE_WARPS);
+        mbar_init(xch_amax, EPILOGUE_WARPS);
+        mbar_init(mma_done, 1);
         *abort_flag = 0;
         fence_barrier_init();
     }
@@ -204,210 +249,375 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tma_prefetch_desc(&tmW);
     }
     if (warp == 1) {
-        tmem_alloc(tmem_slot, NUM_ACC * BN);
-        tmem_relinquish();
+        if (PAIR) {
+            tmem_alloc_pair(tmem_slot, NUM_ACC * BN);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(tmem_slot, NUM_ACC * BN);
+            tmem_relinquish();
+        }
     }
     tc_fence_before();
     __syncthreads();
+    if (PAIR) cluster_sync_all();  // the peer's barriers are initialised before any remote arrive
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
-
+    if (warp < EPILOGUE_WARP0) {
+    // warpgroups 0-1 give registers back; one instruction, executed by all eight warps
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REGS_CONTROL));
     if (warp == 0) {
         // ---------------------------------------------------------------- TMA producer
-        if (lane == 0) {
-            int is = 0;
-            uint32_t ps = 0;
-            for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
-                const int m0 = (tile % m_tiles) * BM, n0 = (tile / m_tiles) * BN;
-                for (int g = 0; g < G; ++g) {
-                    if (!mbar_wait(&empty[is], ps ^ 1u, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_TMA)) goto done;
-                    uint8_t* st = smem + S::OFF_STAGE + is * S::STAGE_BYTES;
-                    mbar_arrive_expect_tx(&full[is], S::TX_BYTES);
-                    tma_load_2d(st + S::ST_A, &tmA, &full[is], g * BK, m0);
-                    tma_load_2d(st + S::ST_W, &tmW, &full[is], g * S::W_ROW, n0);
-                    bulk_load(st + S::ST_S, sa + (size_t)g * ldsa + m0, BM * 4, &full[is]);
-                    bulk_load(st + S::ST_S + BM * 4, sw + (size_t)g * ldsw + n0, BN * 4, &full[is]);
-                    if (++is == S::STAGES) { is = 0; ps ^= 1u; }
+        int is = 0, issued = 0;
+        uint32_t ps = 0;
+        for (int tile = tile0; tile < tiles; tile += tstride) {
+            const int m0 = (tile % m_tiles) * MT + row_off, n0 = (tile / m_tiles) * BN + wrow_off;
+            for (int g = 0; g < G; g += 2) {
+                if (!warp_wait_backoff(&empty[is], ps ^ 1u, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_TMA)) goto drain;
+                uint8_t* st = smem + S::OFF_STAGE + is * S::STAGE_BYTES;
+                if (PAIR) {
+                    // activation tiles count on the leader's barrier (both CTAs' bytes); this CTA's
+                    // weight codes on its own barrier, read by its converters
+                    if (lane == 0) {
+                        mbar_arrive_expect_tx_cluster(at_leader(&full[is]), 2 * S::A_BYTES);
+                        mbar_arrive_expect_tx(&wfull[is], S::WP_BYTES);
+                    }
+                    __syncwarp();
+                    if (lane < 2) tma_load_2d_pair(st + lane * S::A_BYTES, &tmA, at_leader(&full[is]), (g + lane) * BK, m0);
+                    else if (lane == 2) tma_load_2d(st + 2 * S::A_BYTES, &tmW, &wfull[is], g * S::W_ROW, n0);
+                } else {
+                    if (lane == 0) mbar_arrive_expect_tx(&full[is], S::TX_BYTES);
+                    __syncwarp();
+                    // lanes 0, 1: activation tiles of groups g, g+1 (past K the box reads zeros);
+                    // lane 2: raw weight codes of both groups.  One instruction, three copies.
+                    if (lane < 3) {
+                        const bool is_a = lane < 2;
+                        tma_load_2d(st + (is_a ? lane * S::A_BYTES : 2 * S::A_BYTES), is_a ? &tmA : &tmW,
+                                    &full[is], is_a ? (g + lane) * BK : g * S::W_ROW, is_a ? m0 : n0);
+                    }
                 }
+                ++issued;
+                if (++is == S::STAGES) { is = 0; ps ^= 1u; }
+            }
+        }
+        goto done;
+    drain:
+        // after an abort: let the stages this warp issued land before the CTA winds down
+        if (lane == 0) {
+            for (int k = 0; k < issued && k < S::STAGES; ++k) {
+                if (is == 0) { is = S::STAGES - 1; ps ^= 1u; } else --is;
+                if (PAIR) mbar_wait_drain(&wfull[is], ps, DRAIN_NS);
+                if (leader) mbar_wait_drain(&full[is], ps, DRAIN_NS);
             }
         }
     } else if (warp == 1) {
         // ---------------------------------------------------------------- MMA issuer
-        if (lane == 0) {
-            constexpr uint32_t IDESC = idesc_f16_f32(BM, BN);
-            int is = 0, ib = 0, ic = 0;
-            uint32_t ps = 0, pb = 0, pc = 0;
-            const uint32_t st_base = smem_u32(smem + S::OFF_STAGE), b_base = smem_u32(smem + S::OFF_B);
-            for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
-                for (int g = 0; g < G; ++g) {
-                    if (!mbar_wait(&full[is], ps, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_MMA)) goto done;
-                    if (!mbar_wait(&b_full[ib], pb, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_MMA)) goto done;
-                    if (!mbar_wait(&acc_empty[ic], pc ^ 1u, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_MMA)) goto done;
-                    tc_fence_after();
-                    const uint32_t d = tmem_base + (uint32_t)(ic * BN);
-                    const uint32_t a_addr = st_base + is * S::STAGE_BYTES + S::ST_A, b_addr = b_base + ib * S::B_BYTES;
-#pragma unroll
-                    for (int kk = 0; kk < BK / 16; ++kk)
-                        umma_f16(d, sw128_desc(a_addr + kk * 32), sw128_desc(b_addr + kk * 32), IDESC, kk > 0);
-                    umma_commit(&b_empty[ib]);
-                    umma_commit(&acc_full[ic]);
-                    if (++is == S::STAGES) { is = 0; ps ^= 1u; }
-                    if (++ib == B_STAGES) { ib = 0; pb ^= 1u; }
-                    if (++ic == NUM_ACC) { ic = 0; pc ^= 1u; }
-                }
-            }
-        }
-    } else if (warp < EPILOGUE_WARP0) {
-        // ---------------------------------------------------------------- converters
-        const int ct = threadIdx.x - CONVERTER_WARP0 * 32;
-        int is = 0, ib = 0;
-        uint32_t ps = 0, pb = 0;
-        for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+        // The whole warp runs the loop (lane 0 polls the barriers and issues), so the warp stays
+        // converged instead of idling 31 lanes at the CTA barrier.
+        constexpr uint32_t IDESC = idesc_f16_f32(MT, BN);
+        int is = 0, ib = 0, ic = 0;
+        uint32_t ps = 0, pb = 0, pc = 0;
+        const uint32_t st_base = smem_u32(smem + S::OFF_STAGE), b_base = smem_u32(smem + S::OFF_B);
+        if (!leader) goto mma_peer;  // the even CTA issues the pair's MMAs
+        for (int tile = tile0; tile < tiles; tile += tstride) {
             for (int g = 0; g < G; ++g) {
-                if (!warp_wait(&full[is], ps, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_CVT)) goto done;
-                if (!warp_wait(&b_empty[ib], pb ^ 1u, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_CVT)) goto done;
-                const uint8_t* wsrc = smem + S::OFF_STAGE + is * S::STAGE_BYTES + S::ST_W;
-                uint8_t* bdst = smem + S::OFF_B + ib * S::B_BYTES;
+                if (!(g & 1) && !warp_wait(&full[is], ps, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_MMA)) goto mma_end;
+                if (!warp_wait(&b_full[ib], pb, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_MMA)) goto mma_end;
+                if (!warp_wait(&acc_empty[ic], pc ^ 1u, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_MMA)) goto mma_end;
+                tc_fence_after();
+                if (lane == 0) {
+                    const uint32_t d = tmem_base + (uint32_t)(ic * BN);
+                    const uint32_t a_addr = st_base + is * S::STAGE_BYTES + (g & 1) * S::A_BYTES;
+                    const uint32_t b_addr = b_base + ib * S::B_BYTES;
+                    if (PAIR) {
 #pragma unroll
-                for (int r = ct; r < BN; r += CONVERTER_WARPS * 32) {
-                    const uint4* src = reinterpret_cast<const uint4*>(wsrc + r * S::W_ROW);
-                    uint8_t* row = bdst + r * 128;
-                    const int swz = r & 7;
-                    if (BITS == 4) {
-                        const uint4 v0 = src[0], v1 = src[1];
-                        const uint32_t words[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-#pragma unroll
-                        for (int c = 0; c < 8; ++c)
-                            *reinterpret_cast<uint4*>(row + ((c ^ swz) << 4)) = nibbles_to_f16(words[c]);
+                        for (int kk = 0; kk < BK / 16; ++kk)
+                            umma_f16_pair(d, sw128_desc(a_addr + kk * 32), sw128_desc(b_addr + kk * 32), IDESC, kk > 0);
+                        // completion signals go to both CTAs of the pair
+                        umma_commit_pair(smem_u32(&b_empty[ib]));
+                        umma_commit_pair(at_peer(&b_empty[ib]));
+                        umma_commit_pair(smem_u32(&acc_full[ic]));
+                        umma_commit_pair(at_peer(&acc_full[ic]));
+                        if ((g & 1) || g == G - 1) {
+                            umma_commit_pair(smem_u32(&empty[is]));
+                            umma_commit_pair(at_peer(&empty[is]));
+                        }
                     } else {
 #pragma unroll
-                        for (int h = 0; h < 4; ++h) {
-                            const uint4 v = src[h];
-                            *reinterpret_cast<uint4*>(row + (((2 * h) ^ swz) << 4)) = bytes_to_f16(v.x, v.y);
-                            *reinterpret_cast<uint4*>(row + (((2 * h + 1) ^ swz) << 4)) = bytes_to_f16(v.z, v.w);
-                        }
+                        for (int kk = 0; kk < BK / 16; ++kk)
+                            umma_f16(d, sw128_desc(a_addr + kk * 32), sw128_desc(b_addr + kk * 32), IDESC, kk > 0);
+                        umma_commit(&b_empty[ib]);
+                        umma_commit(&acc_full[ic]);
+                        if ((g & 1) || g == G - 1) umma_commit(&empty[is]);  // both groups of the stage are multiplied
                     }
                 }
-                // generic writes of the B tile become MMA (async proxy) reads
-                fence_proxy_async_smem();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&b_full[ib]);
-                if (++is == S::STAGES) { is = 0; ps ^= 1u; }
-                if (++ib == B_STAGES) { ib = 0; pb ^= 1u; }
+                if ((g & 1) || g == G - 1) {
+                    if (++is == S::STAGES) { is = 0; ps ^= 1u; }
+                }
+                if (++ib == S::B_STAGES) { ib = 0; pb ^= 1u; }
+                if (++ic == NUM_ACC) { ic = 0; pc ^= 1u; }
             }
         }
-    } else {
-        // ---------------------------------------------------------------- epilogue
-        // Software pipeline over 32-column chunks: the TMEM load of the next chunk (of this group
-        // or of the next group) is in flight while the current chunk is folded; a TMEM buffer is
-        // released as soon as all of its chunks sit in registers.
-        constexpr int COLS = BN / 2;  // columns per thread
-        constexpr int CHUNKS = COLS / 32;
-        const int q = warp & 3;                         // TMEM lane quadrant this warp may access
-        const int half = (warp - EPILOGUE_WARP0) >> 2;  // which half of the tile's columns
-        const int r = q * 32 + lane;                    // row inside the tile
-        const int col0 = half * COLS;
-        const uint32_t tlane = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)col0;
-        const bool any_nonfinite = nonfinite != nullptr && *nonfinite != 0;
-        float* xch = reinterpret_cast<float*>(smem + S::OFF_X);
-        int ic = 0, is = 0;
-        uint32_t pc = 0, ps = 0, px = 0;
-        for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
-            const int m0 = (tile % m_tiles) * BM, n0 = (tile / m_tiles) * BN;
-            const int m = m0 + r;
-            const bool full_cols = n0 + BN <= N;
-            float2 acc[COLS / 2];
-#pragma unroll
-            for (int j = 0; j < COLS / 2; ++j) acc[j] = make_float2(0.f, 0.f);
-            uint32_t va[32], vb[32];
-            // prologue: chunk 0 of group 0
-            if (!warp_wait(&acc_full[ic], pc, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_EPI)) goto done;
-            tc_fence_after();
-            tmem_ld_32x32b_x32(tlane + (uint32_t)(ic * BN), va);
-            tmem_wait_ld(va);
+    mma_end:
+        // every MMA this warp issued has completed before the CTA releases tensor memory
+        if (lane == 0) {
+            if (PAIR) {
+                umma_commit_pair(smem_u32(mma_done));
+                umma_commit_pair(at_peer(mma_done));
+            } else {
+                umma_commit(mma_done);
+            }
+            mbar_wait_drain(mma_done, 0, DRAIN_NS);
+        }
+        __syncwarp();
+        goto done;
+    mma_peer:
+        // the peer CTA's tensor memory is written by the leader's MMAs: wait for their last commit
+        if (lane == 0) mbar_wait_drain(mma_done, 0, DRAIN_NS);
+        __syncwarp();
+    } else if (warp < CONVERTER_WARP0 + CONVERTER_WARPS) {
+        // ---------------------------------------------------------------- converters
+        constexpr int TPR = 128 / S::WR;           // threads per weight row (1 or 2)
+        constexpr int WORDS = S::W_ROW / 4;        // raw 32-bit words per row and group (8 or 16)
+        constexpr int WPT = WORDS / TPR;           // words per thread
+        constexpr int CPT = 8 / TPR;               // 16-byte f16 chunks written per thread
+        const int ct = threadIdx.x - CONVERTER_WARP0 * 32;
+        const int row = ct / TPR, part = ct % TPR, swz = row & 7;
+        const uint32_t st_base = smem_u32(smem + S::OFF_STAGE), b_base = smem_u32(smem + S::OFF_B);
+        int is = 0, ib = 0;
+        uint32_t ps = 0, pb = 0;
+        for (int tile = tile0; tile < tiles; tile += tstride) {
             for (int g = 0; g < G; ++g) {
-                if (!warp_wait(&full[is], ps, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_EPI)) goto done;
-                const float* slot = reinterpret_cast<const float*>(smem + S::OFF_STAGE + is * S::STAGE_BYTES + S::ST_S);
-                const float s_a = slot[r];
-                const float* swp = slot + BM + col0;
-                if (CHUNKS == 2) {
-                    tmem_ld_32x32b_x32(tlane + (uint32_t)(ic * BN + 32), vb);  // chunk 1 of g
-                    fold_group<32, FUSED>(*reinterpret_cast<float2(*)[16]>(&acc[0]), va, swp, s_a);
-                    tmem_wait_ld(vb);
-                } else {
-                    vb[0] = vb[0];
+                if (!(g & 1) &&
+                    !warp_wait_backoff(PAIR ? &wfull[is] : &full[is], ps, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_CVT))
+                    goto done;
+                if (!warp_wait_backoff(&b_empty[ib], pb ^ 1u, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_CVT)) goto done;
+                const uint32_t src = st_base + is * S::STAGE_BYTES + 2 * S::A_BYTES + row * (2 * S::W_ROW) +
+                                     (g & 1) * S::W_ROW + part * WPT * 4;
+                const uint32_t dst = b_base + ib * S::B_BYTES + row * 128;
+                uint32_t words[WPT];
+#pragma unroll
+                for (int i = 0; i < WPT / 4; ++i) {
+                    const uint4 v = lds128(src + i * 16);
+                    words[4 * i] = v.x; words[4 * i + 1] = v.y; words[4 * i + 2] = v.z; words[4 * i + 3] = v.w;
                 }
-                // every chunk of group g is in registers: release its TMEM buffer
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&acc_empty[ic]);
-                if (++ic == NUM_ACC) { ic = 0; pc ^= 1u; }
-                const bool next = g + 1 < G;
-                if (next) {
-                    if (!warp_wait(&acc_full[ic], pc, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_EPI)) goto done;
-                    tc_fence_after();
-                    if (CHUNKS == 2) tmem_ld_32x32b_x32(tlane + (uint32_t)(ic * BN), va);  // chunk 0 of g+1
+#pragma unroll
+                for (int c = 0; c < CPT; ++c) {
+                    const int chunk = part * CPT + c;
+                    const uint4 h = BITS == 4 ? nibbles_to_f16(words[c]) : bytes_to_f16(words[2 * c], words[2 * c + 1]);
+                    sts128(dst + ((chunk ^ swz) << 4), h);
                 }
-                if (CHUNKS == 2) {
-                    fold_group<32, FUSED>(*reinterpret_cast<float2(*)[16]>(&acc[16]), vb, swp + 32, s_a);
-                } else {
-                    fold_group<32, FUSED>(*reinterpret_cast<float2(*)[16]>(&acc[0]), va, swp, s_a);
-                    if (next) tmem_ld_32x32b_x32(tlane + (uint32_t)(ic * BN), va);
-                }
-                // the stage's next fill is an async-proxy (TMA / bulk copy) write: order this warp's
-                // generic-proxy reads of it before releasing the stage
+                // generic writes of the B tile become MMA (async proxy) reads; the generic reads of
+                // the raw codes are ordered before the stage's next TMA fill as well
                 fence_proxy_async_smem();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&empty[is]);
-                if (++is == S::STAGES) { is = 0; ps ^= 1u; }
-                if (next) tmem_wait_ld(va);
-            }
-            float* accf = reinterpret_cast<float*>(acc);
-            if (EPI == DB_EPI_SWIGLU_QUANT) {
-                // half 1 holds the up projection of the same 64 features: hand it to half 0.
-                if (half == 1) {
-                    if (!warp_wait(xch_empty, px ^ 1u, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_EPI)) goto done;
-#pragma unroll
-                    for (int j = 0; j < COLS; ++j) xch[r * XCH_STRIDE + j] = accf[j];
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(xch_full);
-                } else {
-                    if (!warp_wait(xch_full, px, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_EPI)) goto done;
-                    if (m < M) {
-                        float h[COLS];
-                        float amax = 0.f;
-#pragma unroll
-                        for (int j = 0; j < COLS; ++j) {
-                            h[j] = __fmul_rn(silu_ref(accf[j]), xch[r * XCH_STRIDE + j]);
-                            amax = fmaxf(amax, fabsf(h[j]));
-                        }
-                        const float scale = fmaxf(__fdiv_rn(amax, 127.f), FLT_MIN);
-                        const float inv = __fdiv_rn(1.f, scale);
-                        const int f0 = (n0 / BN) * 64;  // first output feature of this tile
-                        __half* dst = out_codes + (size_t)m * ldoc + f0;
-#pragma unroll
-                        for (int b = 0; b < COLS; b += 8) {
-                            const int order[8] = {0, 4, 1, 5, 2, 6, 3, 7};
-                            __half hv[8];
-#pragma unroll
-                            for (int p = 0; p < 8; ++p)
-                                hv[p] = __float2half_rn(
-                                    fminf(fmaxf(rintf(__fmul_rn(h[b + order[p]], inv)), -127.f), 127.f));
-                            *reinterpret_cast<uint4*>(dst + b) = *reinterpret_cast<uint4*>(hv);
-                        }
-                        out_scales[(size_t)(n0 / BN) * ldos + m] = scale;
-                    }
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(xch_empty);
+                if (lane == 0) {
+                    if (PAIR) mbar_arrive_cluster(at_leader(&b_full[ib]));
+                    else mbar_arrive(&b_full[ib]);
                 }
+                if ((g & 1) || g == G - 1) {
+                    if (++is == S::STAGES) { is = 0; ps ^= 1u; }
+                }
+                if (++ib == S::B_STAGES) { ib = 0; pb ^= 1u; }
+            }
+        }
+    }
+    } else {
+        // ---------------------------------------------------------------- epilogue
+        // warpgroups 2-3 take the registers the control warpgroups released
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REGS_EPILOGUE));
+        constexpr int COLS = S::COLS;  // columns per thread: 64 (BN 128) or 32 (BN 64)
+        constexpr int CHUNKS = COLS / 32;
+        const int ew = warp - EPILOGUE_WARP0;
+        const int q = warp & 3;          // TMEM lane quadrant this warp may access
+        const int half = ew >> 2;        // which half of the tile's columns
+        const int r = q * 32 + lane;     // row inside the tile
+        const int col0 = half * COLS;
+        const uint32_t tlane = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)col0;
+        const uint32_t sc_base = smem_u32(smem + S::OFF_SC) + ew * SC_DEPTH * S::SC_SLOT;
+        const bool any_nonfinite = nonfinite != nullptr && *nonfinite != 0;
+        float* xch = reinterpret_cast<float*>(smem + S::OFF_X);
+        // Scale vectors of one job (one group of one tile) go to the next ring slot: lanes 0-7
+        // fetch the sa of this warp's 32 rows, lanes 8.. the sw of its COLS columns (16 bytes
+        // each).  The prefetch cursor walks this CTA's jobs in order, SC_DEPTH jobs ahead.
+        int pf_tile = tile0, pf_g = 0, pf_slot = 0;
+        const float* pf_src = nullptr;
+        auto pf_tile_start = [&]() {
+            if (pf_tile < tiles) {
+                const int m0 = (pf_tile % m_tiles) * MT + row_off, n0 = (pf_tile / m_tiles) * BN;
+                pf_src = lane < 8 ? sa + m0 + q * 32 + lane * 4 : sw + n0 + col0 + (lane - 8) * 4;
+            }
+        };
+        const int64_t pf_ld = lane < 8 ? ldsa : ldsw;
+        const bool pf_lane = lane < 8 + COLS / 4;
+        const uint32_t pf_dst = lane < 8 ? lane * 16 : 128 + (lane - 8) * 16;
+        auto prefetch = [&]() {
+            if (pf_tile < tiles) {
+                if (pf_lane) cp_async16(sc_base + pf_slot * S::SC_SLOT + pf_dst, pf_src);
+                pf_src += pf_ld;
+                if (++pf_g == G) {
+                    pf_g = 0;
+                    pf_tile += tstride;
+                    pf_tile_start();
+                }
+            }
+            cp_async_commit();
+            if (++pf_slot == SC_DEPTH) pf_slot = 0;
+        };
+        pf_tile_start();
+        for (int j = 0; j < SC_DEPTH; ++j) prefetch();
+        int ic = 0, slot_i = 0, ybuf = 0;
+        uint32_t pc = 0, px = 0;
+        bool refill = false;  // the slot consumed by the previous job is free to refill
+        cp_async_wait<SC_DEPTH - 1>();
+        __syncwarp();
+        float s_a_next = lds_f32(sc_base + lane * 4);
+        for (int tile = tile0; tile < tiles; tile += tstride) {
+            const int m0 = (tile % m_tiles) * MT + row_off, n0 = (tile / m_tiles) * BN;
+            const int m = m0 + r;
+            const bool full_cols = n0 + BN <= N;
+            uint64_t acc[COLS / 2];
+#pragma unroll
+            for (int j = 0; j < COLS / 2; ++j) acc[j] = 0ull;
+            for (int g = 0; g < G; ++g) {
+                // This job's scale vectors landed before its s_a was read (end of the previous
+                // iteration).  Refill the slot the previous job used: every lane has finished reading
+                // it (the __syncwarp that ended the previous iteration).
+                if (refill) prefetch();
+                refill = true;
+                const uint32_t slot = sc_base + slot_i * S::SC_SLOT;
+                const float s_a = s_a_next;
+                if (!warp_wait(&acc_full[ic], pc, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_EPI)) goto done;
+                tc_fence_after();
+#pragma unroll
+                for (int c = 0; c < COLS / 16; ++c) {
+                    uint32_t v[16];
+                    uint4 w[4];
+                    tmem_ld_32x32b_x16(tlane + (uint32_t)(ic * BN + c * 16), v);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) w[i] = lds128(slot + 128 + c * 64 + i * 16);
+                    tmem_wait_ld(v);
+                    if (c == COLS / 16 - 1) {
+                        // every column of this group is in registers: release its TMEM buffer
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) {
+                            if (PAIR) mbar_arrive_cluster(at_leader(&acc_empty[ic]));
+                            else mbar_arrive(&acc_empty[ic]);
+                        }
+                    }
+                    fold16<FUSED>(&acc[c * 8], v, w, s_a);
+                }
+                if (++ic == NUM_ACC) { ic = 0; pc ^= 1u; }
+                if (++slot_i == SC_DEPTH) slot_i = 0;
+                // the next job's scale vectors: its commit group is the oldest but SC_DEPTH - 2
+                cp_async_wait<SC_DEPTH - 2>();
+                __syncwarp();
+                s_a_next = lds_f32(sc_base + slot_i * S::SC_SLOT + lane * 4);
+            }
+            if (EPI == DB_EPI_SWIGLU_QUANT) {
+                // Half 0 holds the gate projection of this tile's 64 features, half 1 the up
+                // projection of the same features.  Each half finishes 32 features: half 0 takes
+                // features 0-31 (needs up 0-31), half 1 features 32-63 (needs gate 32-63).  The row's
+                // absmax over all 64 features is combined through shared memory before quantising.
+                float* xg = xch;                       // gate columns 32..63, written by half 0
+                float* xu = xch + BM * XCH_STRIDE;     // up columns 0..31, written by half 1
+                float* xm = xch + 2 * BM * XCH_STRIDE; // [2][BM] row maxima of each half
+                if (!warp_wait(xch_empty, px ^ 1u, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_EPI)) goto done;
+                // (separate branches keep every accumulator index a compile-time constant)
+                if (half == 0) {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        xg[r * XCH_STRIDE + 2 * j] = f2_lo(acc[16 + j]);
+                        xg[r * XCH_STRIDE + 2 * j + 1] = f2_hi(acc[16 + j]);
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        xu[r * XCH_STRIDE + 2 * j] = f2_lo(acc[j]);
+                        xu[r * XCH_STRIDE + 2 * j + 1] = f2_hi(acc[j]);
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(xch_full);
+                if (!warp_wait(xch_full, px, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_EPI)) goto done;
+                float h[32];
+                float amax = 0.f;
+                if (half == 0) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const float gate = (j & 1) ? f2_hi(acc[j / 2]) : f2_lo(acc[j / 2]);
+                        h[j] = __fmul_rn(silu_ref(gate), xu[r * XCH_STRIDE + j]);
+                        amax = fmaxf(amax, fabsf(h[j]));
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const float up = (j & 1) ? f2_hi(acc[16 + j / 2]) : f2_lo(acc[16 + j / 2]);
+                        h[j] = __fmul_rn(silu_ref(xg[r * XCH_STRIDE + j]), up);
+                        amax = fmaxf(amax, fabsf(h[j]));
+                    }
+                }
+                xm[half * BM + r] = amax;
+                __syncwarp();
+                if (lane == 0) mbar_arrive(xch_amax);
+                if (!warp_wait(xch_amax, px, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_EPI)) goto done;
+                amax = fmaxf(xm[r], xm[BM + r]);
+                if (m < M) {
+                    const float scale = fmaxf(__fdiv_rn(amax, 127.f), FLT_MIN);
+                    const float inv = __fdiv_rn(1.f, scale);
+                    const int f0 = (n0 / BN) * 64 + half * 32;  // first output feature of this half
+                    __half* dst = out_codes + (size_t)m * ldoc + f0;
+#pragma unroll
+                    for (int b = 0; b < 32; b += 8) {
+                        const int order[8] = {0, 4, 1, 5, 2, 6, 3, 7};
+                        __half hv[8];
+#pragma unroll
+                        for (int p = 0; p < 8; ++p)
+                            hv[p] = __float2half_rn(fminf(fmaxf(rintf(__fmul_rn(h[b + order[p]], inv)), -127.f), 127.f));
+                        *reinterpret_cast<uint4*>(dst + b) = *reinterpret_cast<uint4*>(hv);
+                    }
+                    if (half == 0) out_scales[(size_t)(n0 / BN) * ldos + m] = scale;
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(xch_empty);  // this warp is done reading the exchange
                 px ^= 1u;
+            } else if (y_tma) {
+                // Stage 32 rows x 16 columns per chunk in shared memory and hand them to the TMA:
+                // a coalesced store (y = acc) or an in-L2 reduce-add (y = y + acc, round to nearest,
+                // so y is never read here).  Rows/columns past M/N are clipped by the TMA.
+                const float nanv = __int_as_float(0x7fc00000);
+                const uint32_t ystage = smem_u32(smem + S::OFF_Y) + ew * 2 * S::Y_CHUNK;
+#pragma unroll
+                for (int c = 0; c < COLS / 16; ++c) {
+                    const uint32_t buf = ystage + ybuf * S::Y_CHUNK;
+                    if (lane == 0) bulk_wait_group_read<1>();  // this buffer's previous store has read it
+                    __syncwarp();
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const uint64_t p0 = acc[c * 8 + 2 * i], p1 = acc[c * 8 + 2 * i + 1];
+                        uint4 o = make_uint4((uint32_t)p0, (uint32_t)(p0 >> 32), (uint32_t)p1, (uint32_t)(p1 >> 32));
+                        if (any_nonfinite) o = make_uint4(__float_as_uint(nanv), __float_as_uint(nanv),
+                                                          __float_as_uint(nanv), __float_as_uint(nanv));
+                        sts128(buf + lane * 64 + i * 16, o);
+                    }
+                    fence_proxy_async_smem();  // generic writes of the staging buffer -> TMA reads
+                    __syncwarp();
+                    if (lane == 0) {
+                        if (EPI == DB_EPI_RESIDUAL) tma_reduce_add_2d(&tmY, buf, n0 + col0 + c * 16, m0 + q * 32);
+                        else tma_store_2d(&tmY, buf, n0 + col0 + c * 16, m0 + q * 32);
+                        bulk_commit_group();
+                    }
+                    ybuf ^= 1;
+                }
             } else if (m < M) {
                 float* dst = y + (size_t)m * ldy + n0 + col0;
                 const float nanv = __int_as_float(0x7fc00000);
                 if (full_cols && (ldy & 3) == 0 && (N & 3) == 0) {
 #pragma unroll
                     for (int j = 0; j < COLS; j += 4) {
-                        float4 o = make_float4(accf[j], accf[j + 1], accf[j + 2], accf[j + 3]);
+                        float4 o = make_float4(f2_lo(acc[j / 2]), f2_hi(acc[j / 2]), f2_lo(acc[j / 2 + 1]),
+                                               f2_hi(acc[j / 2 + 1]));
                         if (EPI == DB_EPI_RESIDUAL) {
                             const float4 rr = *reinterpret_cast<const float4*>(dst + j);
                             o.x = __fadd_rn(rr.x, o.x); o.y = __fadd_rn(rr.y, o.y);
@@ -420,7 +630,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
                     for (int j = 0; j < COLS; ++j) {
                         if (n0 + col0 + j < N) {
-                            float o = accf[j];
+                            float o = (j & 1) ? f2_hi(acc[j / 2]) : f2_lo(acc[j / 2]);
                             if (EPI == DB_EPI_RESIDUAL) o = __fadd_rn(dst[j], o);
                             dst[j] = any_nonfinite ? nanv : o;
                         }
@@ -430,10 +640,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
     }
 done:
+    cp_async_wait_all();
+    bulk_wait_all();  // output stores issued by this thread have completed
     __syncthreads();
+    // neither CTA of a pair leaves while the other may still arrive on its barriers or have its
+    // shared memory read by the pair's MMAs (every wait above is bounded, so both get here)
+    if (PAIR) cluster_sync_all();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, NUM_ACC * BN);
+        if (PAIR) tmem_dealloc_pair(tmem_base, NUM_ACC * BN);
+        else tmem_dealloc(tmem_base, NUM_ACC * BN);
     }
 }
 
@@ -469,40 +685,64 @@ int db_num_sms() {
     return sms;
 }
 
-template <int BN, int BITS, int EPI, bool FUSED>
-static int launch_variant(const DbGemmArgs& a, const CUtensorMap& tmA, const CUtensorMap& tmW, int G,
-                          cudaStream_t stream) {
-    using S = GemmSmem<BN, BITS, EPI>;
-    auto kernel = gemm_tc_kernel<BN, BITS, EPI, FUSED>;
+template <int BN, int BITS, int EPI, bool FUSED, bool PAIR>
+static int launch_variant(const DbGemmArgs& a, const CUtensorMap& tmA, const CUtensorMap& tmW,
+                          const CUtensorMap& tmY, int y_tma, int G, cudaStream_t stream) {
+    using S = GemmSmem<BN, BITS, EPI, PAIR>;
+    auto kernel = gemm_tc_kernel<BN, BITS, EPI, FUSED, PAIR>;
     static bool configured = false;
     if (!configured) {
         cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S::BYTES);
         if (e != cudaSuccess) return (int)e;
         configured = true;
     }
-    const int tiles = ((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN);
-    int ctas = a.max_ctas > 0 ? a.max_ctas : db_num_sms();
-    if (ctas > tiles) ctas = tiles;
-    kernel<<<ctas, NUM_THREADS, S::BYTES, stream>>>(tmA, tmW, a.sa, a.ldsa, a.sw, db_scale_stride(a.N), a.M, a.N, G,
-                                                    a.y, a.ldy,
-                                                    static_cast<__half*>(a.out_codes), a.ldoc, a.out_scales, a.ldos,
-                                                    a.nonfinite, a.dev_error);
-    return (int)cudaGetLastError();
+    constexpr int MT = PAIR ? 2 * BM : BM;
+    const int tiles = ((a.M + MT - 1) / MT) * ((a.N + BN - 1) / BN);
+    int units = a.max_ctas > 0 ? a.max_ctas : db_num_sms();  // CTAs available
+    if (PAIR) units /= 2;                                      // pairs available
+    if (units < 1) units = 1;
+    if (units > tiles) units = tiles;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(PAIR ? 2 * units : units));
+    cfg.blockDim = dim3(NUM_THREADS);
+    cfg.dynamicSmemBytes = S::BYTES;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = PAIR ? 2 : 1;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, tmA, tmW, tmY, y_tma, a.sa, a.ldsa, a.sw,
+                                             (int64_t)db_scale_stride(a.N), a.M, a.N, G, a.y, a.ldy,
+                                             static_cast<__half*>(a.out_codes), a.ldoc, a.out_scales, a.ldos,
+                                             a.nonfinite, a.dev_error);
+    return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
+}
+
+template <int BN, int BITS, int EPI, bool FUSED>
+static int launch_pairing(const DbGemmArgs& a, bool pair, const CUtensorMap& tmA, const CUtensorMap& tmW,
+                          const CUtensorMap& tmY, int y_tma, int G, cudaStream_t s) {
+    if constexpr (BN == 128) {
+        if (pair) return launch_variant<BN, BITS, EPI, FUSED, true>(a, tmA, tmW, tmY, y_tma, G, s);
+    }
+    return launch_variant<BN, BITS, EPI, FUSED, false>(a, tmA, tmW, tmY, y_tma, G, s);
 }
 
 template <int BN, int BITS>
-static int dispatch_epi(const DbGemmArgs& a, const CUtensorMap& tmA, const CUtensorMap& tmW, int G,
-                        cudaStream_t s) {
+static int dispatch_epi(const DbGemmArgs& a, bool pair, const CUtensorMap& tmA, const CUtensorMap& tmW,
+                        const CUtensorMap& tmY, int y_tma, int G, cudaStream_t s) {
     if (a.epilogue == DB_EPI_SWIGLU_QUANT) {
         if (BN != 128) return (int)cudaErrorInvalidValue;
-        return a.fused ? launch_variant<BN, BITS, DB_EPI_SWIGLU_QUANT, true>(a, tmA, tmW, G, s)
-                       : launch_variant<BN, BITS, DB_EPI_SWIGLU_QUANT, false>(a, tmA, tmW, G, s);
+        return a.fused ? launch_pairing<BN, BITS, DB_EPI_SWIGLU_QUANT, true>(a, pair, tmA, tmW, tmY, y_tma, G, s)
+                       : launch_pairing<BN, BITS, DB_EPI_SWIGLU_QUANT, false>(a, pair, tmA, tmW, tmY, y_tma, G, s);
     }
     if (a.epilogue == DB_EPI_RESIDUAL)
-        return a.fused ? launch_variant<BN, BITS, DB_EPI_RESIDUAL, true>(a, tmA, tmW, G, s)
-                       : launch_variant<BN, BITS, DB_EPI_RESIDUAL, false>(a, tmA, tmW, G, s);
-    return a.fused ? launch_variant<BN, BITS, DB_EPI_STORE, true>(a, tmA, tmW, G, s)
-                   : launch_variant<BN, BITS, DB_EPI_STORE, false>(a, tmA, tmW, G, s);
+        return a.fused ? launch_pairing<BN, BITS, DB_EPI_RESIDUAL, true>(a, pair, tmA, tmW, tmY, y_tma, G, s)
+                       : launch_pairing<BN, BITS, DB_EPI_RESIDUAL, false>(a, pair, tmA, tmW, tmY, y_tma, G, s);
+    return a.fused ? launch_pairing<BN, BITS, DB_EPI_STORE, true>(a, pair, tmA, tmW, tmY, y_tma, G, s)
+                   : launch_pairing<BN, BITS, DB_EPI_STORE, false>(a, pair, tmA, tmW, tmY, y_tma, G, s);
 }
 
 int db_launch_gemm_tc(const DbGemmArgs& a, cudaStream_t stream) {
@@ -514,6 +754,8 @@ int db_launch_gemm_tc(const DbGemmArgs& a, cudaStream_t stream) {
     int bn = a.block_n ? a.block_n : 128;
     if (a.epilogue == DB_EPI_SWIGLU_QUANT) bn = 128;
     if (bn != 64 && bn != 128) return (int)cudaErrorInvalidValue;
+    // CTA pairs (M = 256 MMAs) for 128-wide tiles when asked for and there are rows for both CTAs
+    const bool pair = bn == 128 && a.M > BM && a.pair_ctas;
     if ((reinterpret_cast<uintptr_t>(a.a_codes) & 15) || (a.lda * 2) % 16 || a.lda < Kp ||
         (reinterpret_cast<uintptr_t>(a.w_codes) & 15) || (reinterpret_cast<uintptr_t>(a.sa) & 15) ||
         (reinterpret_cast<uintptr_t>(a.sw) & 15) || a.ldsa < db_scale_stride(a.M) || (a.ldsa & 3))
@@ -533,13 +775,28 @@ int db_launch_gemm_tc(const DbGemmArgs& a, cudaStream_t stream) {
         const cuuint64_t row_bytes = (cuuint64_t)Kp * a.bits / 8;
         cuuint64_t dims[2] = {row_bytes, (cuuint64_t)a.N};
         cuuint64_t strides[1] = {row_bytes};
-        cuuint32_t box[2] = {(cuuint32_t)(BK * a.bits / 8), (cuuint32_t)bn};
+        // a pair of K groups; in pair mode each CTA loads half of the tile's weight rows
+        cuuint32_t box[2] = {(cuuint32_t)(2 * BK * a.bits / 8), (cuuint32_t)(pair ? bn / 2 : bn)};
         cuuint32_t estr[2] = {1, 1};
         if (enc(&tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(a.w_codes), dims, strides, box, estr,
                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
             return (int)cudaErrorInvalidValue;
     }
-    if (bn == 64) return a.bits == 4 ? dispatch_epi<64, 4>(a, tmA, tmW, G, stream) : dispatch_epi<64, 8>(a, tmA, tmW, G, stream);
-    return a.bits == 4 ? dispatch_epi<128, 4>(a, tmA, tmW, G, stream) : dispatch_epi<128, 8>(a, tmA, tmW, G, stream);
+    // output tensor map for the TMA store / reduce-add (fallback: plain per-thread stores)
+    CUtensorMap tmY;
+    memset(&tmY, 0, sizeof(tmY));
+    int y_tma = 0;
+    if (a.epilogue != DB_EPI_SWIGLU_QUANT && a.y && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0 && a.ldy % 4 == 0 &&
+        a.ldy >= a.N) {
+        cuuint64_t dims[2] = {(cuuint64_t)a.N, (cuuint64_t)a.M};
+        cuuint64_t strides[1] = {(cuuint64_t)a.ldy * 4};
+        cuuint32_t box[2] = {16, 32};
+        cuuint32_t estr[2] = {1, 1};
+        y_tma = enc(&tmY, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, a.y, dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    }
+    if (bn == 64) return a.bits == 4 ? dispatch_epi<64, 4>(a, pair, tmA, tmW, tmY, y_tma, G, stream) : dispatch_epi<64, 8>(a, pair, tmA, tmW, tmY, y_tma, G, stream);
+    return a.bits == 4 ? dispatch_epi<128, 4>(a, pair, tmA, tmW, tmY, y_tma, G, stream) : dispatch_epi<128, 8>(a, pair, tmA, tmW, tmY, y_tma, G, stream);
 }

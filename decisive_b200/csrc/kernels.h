@@ -54,6 +54,7 @@ struct DbGemmArgs {
     int* dev_error;        // device error word
     int block_n;           // tile width (0 = default)
     int max_ctas;          // persistent grid cap (0 = number of SMs)
+    int pair_ctas;         // 1 = CTA pairs with M = 256 MMAs (used for 128-wide tiles when M > 128)
 };
 int db_launch_gemm_tc(const DbGemmArgs& args, cudaStream_t stream);
 

@@ -106,6 +106,25 @@ int db_dequant_rows_g64(const uint8_t *codes, const float *scales, int64_t N, in
 int db_gemm_g64(const void *a_codes, int layout, int64_t lda, const float *sa, const int32_t *a_sums, int64_t ldsa,
                 const uint8_t *w_codes, const float *sw, int64_t M, int64_t N, int64_t K, int bits, int fused,
                 int residual, float *y, int64_t ldy, const int *nonfinite, void *stream);
+
+/* Tile configuration of the tensor-core GEMM: the candidate space of the kernel-selection tuner
+ * (checkpoint.rs:279-294, 428-563 select among kernel variants; a candidate is accepted only when
+ * its output is bitwise equal to the baseline's).  Every configuration computes the same
+ * per-group fold in the same order, so all are bitwise equal by construction.
+ *   block_n    output columns per tile: 0 (default 128), 64 or 128
+ *   max_ctas   persistent grid cap: 0 = one CTA per SM
+ *   pair_ctas  1 = clusters of two CTAs issue M = 256 MMAs (128-wide tiles, M > 128); 0 = off
+ * No counterpart in the reference's CPU path (its tuner picks WGSL variants). */
+typedef struct db_gemm_config {
+    int block_n;
+    int max_ctas;
+    int pair_ctas;
+} db_gemm_config;
+/* db_gemm_g64 with an explicit tile configuration (NULL = defaults).  GEMV-layout inputs ignore it. */
+int db_gemm_g64_config(const void *a_codes, int layout, int64_t lda, const float *sa, const int32_t *a_sums,
+                       int64_t ldsa, const uint8_t *w_codes, const float *sw, int64_t M, int64_t N, int64_t K,
+                       int bits, int fused, int residual, float *y, int64_t ldy, const int *nonfinite,
+                       const db_gemm_config *config, void *stream);
 int db_gemv_max_rows(void);
 
 /* Full projection: quantise x (f32 [M, K]) then GEMM, choosing the GEMV path for

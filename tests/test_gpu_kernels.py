@@ -186,6 +186,35 @@ def test_tensor_core_gemm_bit_exact(db, oracle, wb, ab, m, k, n):
     assert bits_equal(y, ref), f"max |d| = {np.max(np.abs(y - ref))}"
 
 
+TILE_CONFIGS = [(0, 0, 0), (64, 0, 0), (128, 0, 1), (128, 16, 0), (128, 7, 1), (64, 3, 0)]
+
+
+@pytest.mark.parametrize("m,k,n", [(200, 1000, 300), (1024, 1024, 3072), (257, 130, 129), (384, 2048, 256)])
+@pytest.mark.parametrize("wb", [4, 8])
+def test_tile_configurations_are_bitwise_equal(db, oracle, m, k, n, wb):
+    """The tuner's candidate space (checkpoint.rs:279-294): every tile configuration -- tile width,
+    persistent grid cap, CTA pairs with M = 256 MMAs -- gives the same bits, equal to the oracle."""
+    x = ref_x(m, k, kind="normal")
+    bf = oracle.f32_to_bf16(np.random.default_rng(k + n).normal(0, 0.02, (n, k)).astype(np.float32))
+    codes, scales = db.pack_weights(torch.from_numpy(bf.view(np.int16)).cuda(), wb)
+    a, sa, _ = db.quantize_activations(torch.from_numpy(x.reshape(m, k)).cuda(), bits=8, layout=db.CODES_TC)
+    ref = oracle.Matrix(bf.reshape(-1), k, n, wb, 8).apply(x, mode=0)
+    base = torch.randn(m, n, device="cuda")
+    outs = []
+    for bn, cap, pair in TILE_CONFIGS:
+        cfg = db.GemmConfig(bn, cap, pair)
+        y = db.gemm(a, db.CODES_TC, sa, codes, scales, m, n, k, wb, True, config=cfg)
+        r = db.gemm(a, db.CODES_TC, sa, codes, scales, m, n, k, wb, True, residual=base.clone(), config=cfg)
+        torch.cuda.synchronize()
+        assert db.device_error_word() == 0
+        outs.append((y.cpu().numpy(), r.cpu().numpy()))
+    assert bits_equal(outs[0][0], ref)
+    expect_res = (base.cpu().numpy() + ref).astype(np.float32)
+    for (y, r), c in zip(outs, TILE_CONFIGS):
+        assert bits_equal(y, outs[0][0]), f"store epilogue differs for config {c}"
+        assert bits_equal(r, expect_res), f"residual epilogue differs for config {c}"
+
+
 @pytest.mark.parametrize("m,k,n", [(7, 65, 9), (65, 256, 33), (256, 1024, 512)])
 def test_tensor_core_gemm_portable_mode_bit_exact(db, oracle, m, k, n):
     x = ref_x(m, k)
