@@ -187,6 +187,35 @@ __device__ __forceinline__ void fold16(uint64_t* acc, const uint32_t (&v)[16], c
     }
 }
 
+// SwiGLU finish, in slices.  pend holds a thread's 32 own values of a tile (gate for half 0, up
+// for half 1) and receives h = silu(gate) * up in place; other_row holds the other half's values.
+template <int B>
+__device__ __forceinline__ void swiglu_silu4(uint64_t (&pend)[16], const float* other_row, int half, float& amax) {
+#pragma unroll
+    for (int j = B; j < B + 4; ++j) {
+        uint64_t& p = pend[j / 2];
+        const float own = (j & 1) ? f2_hi(p) : f2_lo(p);
+        const float oth = other_row[j];
+        const float h = __fmul_rn(silu_ref(half == 0 ? own : oth), half == 0 ? oth : own);
+        p = (j & 1) ? f2_pack(__float_as_uint(f2_lo(p)), __float_as_uint(h))
+                    : f2_pack(__float_as_uint(h), __float_as_uint(f2_hi(p)));
+        amax = fmaxf(amax, fabsf(h));
+    }
+}
+// int8 codes (as f16, TC order 0,4,1,5,2,6,3,7) of features B..B+7.
+template <int B>
+__device__ __forceinline__ void swiglu_store8(const uint64_t (&pend)[16], float inv, __half* dst) {
+    const int order[8] = {0, 4, 1, 5, 2, 6, 3, 7};
+    __half hv[8];
+#pragma unroll
+    for (int p = 0; p < 8; ++p) {
+        const int j = B + order[p];
+        const float h = (j & 1) ? f2_hi(pend[j / 2]) : f2_lo(pend[j / 2]);
+        hv[p] = __float2half_rn(fminf(fmaxf(rintf(__fmul_rn(h, inv)), -127.f), 127.f));
+    }
+    *reinterpret_cast<uint4*>(dst + B) = *reinterpret_cast<uint4*>(hv);
+}
+
 template <int BN, int BITS, int EPI, bool FUSED, bool PAIR>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
@@ -427,7 +456,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         // warpgroups 2-3 take the registers the control warpgroups released
         asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REGS_EPILOGUE));
         constexpr int COLS = S::COLS;  // columns per thread: 64 (BN 128) or 32 (BN 64)
-        constexpr int CHUNKS = COLS / 32;
         const int ew = warp - EPILOGUE_WARP0;
         const int q = warp & 3;          // TMEM lane quadrant this warp may access
         const int half = ew >> 2;        // which half of the tile's columns
@@ -467,11 +495,69 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         pf_tile_start();
         for (int j = 0; j < SC_DEPTH; ++j) prefetch();
         int ic = 0, slot_i = 0, ybuf = 0;
-        uint32_t pc = 0, px = 0;
+        uint32_t pc = 0;
         bool refill = false;  // the slot consumed by the previous job is free to refill
         cp_async_wait<SC_DEPTH - 1>();
         __syncwarp();
         float s_a_next = lds_f32(sc_base + lane * 4);
+        // ---- SwiGLU: a tile's finish (exchange, silu * up, row absmax, re-quantisation) is spread
+        // over the groups of the next tile, where the fold leaves the epilogue warps idle time.
+        // Half 0 holds the gate projection of the tile's 64 features, half 1 the up projection;
+        // half 0 finishes features 0-31, half 1 features 32-63 (grouped_q4_mlp.wgsl:83-105).
+        float* xg = xch;                        // gate columns 32..63, written by half 0
+        float* xu = xch + BM * XCH_STRIDE;      // up columns 0..31, written by half 1
+        float* xm = xch + 2 * BM * XCH_STRIDE;  // [2][BM] row maxima of each half
+        uint64_t pend[16];                      // own 32 values of the pending tile, then h
+        int pstep = -1, p_m = 0, p_n0 = 0, xc = 0;
+        uint32_t p_par = 0;
+        float p_amax = 0.f, p_scale = 0.f, p_inv = 0.f;
+        auto swiglu_step = [&]() -> bool {
+            const float* other_row = (half == 0 ? xu : xg) + r * XCH_STRIDE;
+            switch (pstep) {
+                case 0:
+                    if (!warp_wait(xch_full, p_par, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_EPI)) return false;
+                    swiglu_silu4<0>(pend, other_row, half, p_amax);
+                    break;
+                case 1: swiglu_silu4<4>(pend, other_row, half, p_amax); break;
+                case 2: swiglu_silu4<8>(pend, other_row, half, p_amax); break;
+                case 3: swiglu_silu4<12>(pend, other_row, half, p_amax); break;
+                case 4: swiglu_silu4<16>(pend, other_row, half, p_amax); break;
+                case 5: swiglu_silu4<20>(pend, other_row, half, p_amax); break;
+                case 6: swiglu_silu4<24>(pend, other_row, half, p_amax); break;
+                case 7:
+                    swiglu_silu4<28>(pend, other_row, half, p_amax);
+                    xm[half * BM + r] = p_amax;
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(xch_amax);
+                    break;
+                case 8: {
+                    if (!warp_wait(xch_amax, p_par, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_EPI)) return false;
+                    const float amax = fmaxf(xm[r], xm[BM + r]);
+                    p_scale = fmaxf(__fdiv_rn(amax, 127.f), FLT_MIN);
+                    p_inv = __fdiv_rn(1.f, p_scale);
+                    if (p_m < M) {
+                        __half* dst = out_codes + (size_t)p_m * ldoc + (p_n0 / BN) * 64 + half * 32;
+                        swiglu_store8<0>(pend, p_inv, dst);
+                        swiglu_store8<8>(pend, p_inv, dst);
+                    }
+                    break;
+                }
+                default: {
+                    if (p_m < M) {
+                        __half* dst = out_codes + (size_t)p_m * ldoc + (p_n0 / BN) * 64 + half * 32;
+                        swiglu_store8<16>(pend, p_inv, dst);
+                        swiglu_store8<24>(pend, p_inv, dst);
+                        if (half == 0) out_scales[(size_t)(p_n0 / BN) * ldos + p_m] = p_scale;
+                    }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(xch_empty);  // this warp is done reading the exchange
+                    pstep = -2;
+                    break;
+                }
+            }
+            ++pstep;
+            return true;
+        };
         for (int tile = tile0; tile < tiles; tile += tstride) {
             const int m0 = (tile % m_tiles) * MT + row_off, n0 = (tile / m_tiles) * BN;
             const int m = m0 + r;
@@ -514,74 +600,40 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 cp_async_wait<SC_DEPTH - 2>();
                 __syncwarp();
                 s_a_next = lds_f32(sc_base + slot_i * S::SC_SLOT + lane * 4);
+                if (EPI == DB_EPI_SWIGLU_QUANT && pstep >= 0 && !swiglu_step()) goto done;
             }
             if (EPI == DB_EPI_SWIGLU_QUANT) {
-                // Half 0 holds the gate projection of this tile's 64 features, half 1 the up
-                // projection of the same features.  Each half finishes 32 features: half 0 takes
-                // features 0-31 (needs up 0-31), half 1 features 32-63 (needs gate 32-63).  The row's
-                // absmax over all 64 features is combined through shared memory before quantising.
-                float* xg = xch;                       // gate columns 32..63, written by half 0
-                float* xu = xch + BM * XCH_STRIDE;     // up columns 0..31, written by half 1
-                float* xm = xch + 2 * BM * XCH_STRIDE; // [2][BM] row maxima of each half
-                if (!warp_wait(xch_empty, px ^ 1u, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_EPI)) goto done;
+                // finish the previous tile if this one was too short to absorb it
+                while (pstep >= 0)
+                    if (!swiglu_step()) goto done;
+                // publish the columns the other half needs, once every warp is done with the
+                // previous tile's exchange; keep this thread's own 32 values pending
+                if (!warp_wait(xch_empty, (uint32_t)(xc & 1) ^ 1u, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_EPI))
+                    goto done;
                 // (separate branches keep every accumulator index a compile-time constant)
                 if (half == 0) {
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
                         xg[r * XCH_STRIDE + 2 * j] = f2_lo(acc[16 + j]);
                         xg[r * XCH_STRIDE + 2 * j + 1] = f2_hi(acc[16 + j]);
+                        pend[j] = acc[j];
                     }
                 } else {
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
                         xu[r * XCH_STRIDE + 2 * j] = f2_lo(acc[j]);
                         xu[r * XCH_STRIDE + 2 * j + 1] = f2_hi(acc[j]);
+                        pend[j] = acc[16 + j];
                     }
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(xch_full);
-                if (!warp_wait(xch_full, px, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_EPI)) goto done;
-                float h[32];
-                float amax = 0.f;
-                if (half == 0) {
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const float gate = (j & 1) ? f2_hi(acc[j / 2]) : f2_lo(acc[j / 2]);
-                        h[j] = __fmul_rn(silu_ref(gate), xu[r * XCH_STRIDE + j]);
-                        amax = fmaxf(amax, fabsf(h[j]));
-                    }
-                } else {
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const float up = (j & 1) ? f2_hi(acc[16 + j / 2]) : f2_lo(acc[16 + j / 2]);
-                        h[j] = __fmul_rn(silu_ref(xg[r * XCH_STRIDE + j]), up);
-                        amax = fmaxf(amax, fabsf(h[j]));
-                    }
-                }
-                xm[half * BM + r] = amax;
-                __syncwarp();
-                if (lane == 0) mbar_arrive(xch_amax);
-                if (!warp_wait(xch_amax, px, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_EPI)) goto done;
-                amax = fmaxf(xm[r], xm[BM + r]);
-                if (m < M) {
-                    const float scale = fmaxf(__fdiv_rn(amax, 127.f), FLT_MIN);
-                    const float inv = __fdiv_rn(1.f, scale);
-                    const int f0 = (n0 / BN) * 64 + half * 32;  // first output feature of this half
-                    __half* dst = out_codes + (size_t)m * ldoc + f0;
-#pragma unroll
-                    for (int b = 0; b < 32; b += 8) {
-                        const int order[8] = {0, 4, 1, 5, 2, 6, 3, 7};
-                        __half hv[8];
-#pragma unroll
-                        for (int p = 0; p < 8; ++p)
-                            hv[p] = __float2half_rn(fminf(fmaxf(rintf(__fmul_rn(h[b + order[p]], inv)), -127.f), 127.f));
-                        *reinterpret_cast<uint4*>(dst + b) = *reinterpret_cast<uint4*>(hv);
-                    }
-                    if (half == 0) out_scales[(size_t)(n0 / BN) * ldos + m] = scale;
-                }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(xch_empty);  // this warp is done reading the exchange
-                px ^= 1u;
+                p_m = m;
+                p_n0 = n0;
+                p_par = (uint32_t)(xc & 1);
+                p_amax = 0.f;
+                pstep = 0;
+                ++xc;
             } else if (y_tma) {
                 // Stage 32 rows x 16 columns per chunk in shared memory and hand them to the TMA:
                 // a coalesced store (y = acc) or an in-L2 reduce-add (y = y + acc, round to nearest,
@@ -638,6 +690,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 }
             }
         }
+        // the last tile's pending SwiGLU finish
+        if (EPI == DB_EPI_SWIGLU_QUANT)
+            while (pstep >= 0)
+                if (!swiglu_step()) goto done;
     }
 done:
     cp_async_wait_all();
@@ -734,9 +790,13 @@ template <int BN, int BITS>
 static int dispatch_epi(const DbGemmArgs& a, bool pair, const CUtensorMap& tmA, const CUtensorMap& tmW,
                         const CUtensorMap& tmY, int y_tma, int G, cudaStream_t s) {
     if (a.epilogue == DB_EPI_SWIGLU_QUANT) {
-        if (BN != 128) return (int)cudaErrorInvalidValue;
-        return a.fused ? launch_pairing<BN, BITS, DB_EPI_SWIGLU_QUANT, true>(a, pair, tmA, tmW, tmY, y_tma, G, s)
-                       : launch_pairing<BN, BITS, DB_EPI_SWIGLU_QUANT, false>(a, pair, tmA, tmW, tmY, y_tma, G, s);
+        // the SwiGLU epilogue pairs the 64 gate and 64 up rows of a 128-wide tile
+        if constexpr (BN != 128) {
+            return (int)cudaErrorInvalidValue;
+        } else {
+            return a.fused ? launch_pairing<BN, BITS, DB_EPI_SWIGLU_QUANT, true>(a, pair, tmA, tmW, tmY, y_tma, G, s)
+                           : launch_pairing<BN, BITS, DB_EPI_SWIGLU_QUANT, false>(a, pair, tmA, tmW, tmY, y_tma, G, s);
+        }
     }
     if (a.epilogue == DB_EPI_RESIDUAL)
         return a.fused ? launch_pairing<BN, BITS, DB_EPI_RESIDUAL, true>(a, pair, tmA, tmW, tmY, y_tma, G, s)
