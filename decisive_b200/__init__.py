@@ -207,7 +207,7 @@ class Cancellation:
     """inference::Cancellation (mod.rs:87-100): a shared flag the library polls."""
 
     def __init__(self):
-        self._flag = C.c_int32(0)
+        self._flag = C.c_uint8(0)  # the layout of Rust's AtomicBool
 
     def cancel(self):
         self._flag.value = 1

@@ -251,7 +251,7 @@ db_model* create(int device, const db_encoder_config* cfg, const db_encoder_weig
 
 // Enqueues the forward of ids (device, T tokens) -> m->pooled.  Host-side cancellation is polled
 // between layers.  Returns 0, 1 when cancelled, or a negative status.
-int enqueue_forward(db_model* m, int T, const volatile int32_t* cancel) {
+int enqueue_forward(db_model* m, int T, const volatile uint8_t* cancel) {
     const auto& c = m->cfg;
     const int D = c.hidden, Nq = m->Nq(), F = m->F(), Nqkv = m->Nqkv();
     const int bits = c.weight_bits, fused = c.fused;
@@ -358,7 +358,7 @@ int enqueue_forward(db_model* m, int T, const volatile int32_t* cancel) {
 }
 
 // Backend::predict for one request; errors use the reference's codes.
-int predict_one(db_model* m, const int32_t* ids, size_t n, const db_parameters* params, const volatile int32_t* cancel,
+int predict_one(db_model* m, const int32_t* ids, size_t n, const db_parameters* params, const volatile uint8_t* cancel,
                 float* out, db_error* err) {
     if (cancel && *cancel) {
         fill_error(err, "CANCELLED", "Inference was cancelled");
@@ -509,7 +509,7 @@ int db_cache_clear(db_model* m, db_cache* c, db_error* err) {
 void db_cache_destroy(db_cache* c) { delete c; }
 
 int db_predict(db_model* m, const int32_t* ids, size_t n, const db_parameters* params, db_cache* cache,
-               const volatile int32_t* cancel, float* out, db_error* err) {
+               const volatile uint8_t* cancel, float* out, db_error* err) {
     if (!m || !out) {
         fill_error(err, "INVALID_PARAMETERS", "null model or output");
         return -1;
@@ -522,7 +522,7 @@ int db_predict(db_model* m, const int32_t* ids, size_t n, const db_parameters* p
 }
 
 int db_predict_batch(db_model* m, const int32_t* const* ids, const size_t* lens, size_t count,
-                     const db_parameters* params, db_cache* cache, const volatile int32_t* cancel, float* outs,
+                     const db_parameters* params, db_cache* cache, const volatile uint8_t* cancel, float* outs,
                      int32_t* status, db_error* errs, db_error* err) {
     if (!m || (count && (!ids || !lens || !outs || !status))) {
         fill_error(err, "INVALID_PARAMETERS", "null batch arguments");

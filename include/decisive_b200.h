@@ -232,14 +232,16 @@ void db_cache_destroy(db_cache *c);
 
 /* Model::predict (mod.rs:206-249): ids [n] -> pooled f32 [hidden].  params NULL = the model's
  * defaults; cache NULL = an ephemeral cache; *cancel != 0 -> CANCELLED (checked before and
- * after the forward, and between layers).  Returns 0, or -1 with *err filled. */
+ * after the forward, and between layers).  cancel is one byte so that the reference's
+ * Cancellation(Arc<AtomicBool>) (mod.rs:87-100) can be passed as-is.  Returns 0, or -1 with
+ * *err filled. */
 int db_predict(db_model *m, const int32_t *ids, size_t n, const db_parameters *params, db_cache *cache,
-               const volatile int32_t *cancel, float *out, db_error *err);
+               const volatile uint8_t *cancel, float *out, db_error *err);
 
 /* Model::predict_batch (mod.rs:250-273): ordered per-request outcomes; status[i] = 0 success
  * (outs + i*hidden filled) or -1 (errs[i] filled).  A foreign cache fails the whole call. */
 int db_predict_batch(db_model *m, const int32_t *const *ids, const size_t *lens, size_t count,
-                     const db_parameters *params, db_cache *cache, const volatile int32_t *cancel, float *outs,
+                     const db_parameters *params, db_cache *cache, const volatile uint8_t *cancel, float *outs,
                      int32_t *status, db_error *errs, db_error *err);
 
 /* Per-launch CUDA-event timing of the forward's kernels (the reference's projection_ms
