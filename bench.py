@@ -343,6 +343,7 @@ def run_gemm(args, local_rank):
     times = []
     for _ in range(args.steps):
         flush.zero_()
+        torch.cuda._sleep(200_000)  # the launch is queued before the start event fires
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
         db.gemm(a, db.CODES_TC, sa, codes, scales, m, n, k, args.bits, residual=y)
@@ -358,6 +359,55 @@ def run_gemm(args, local_rank):
     print(json.dumps(out), flush=True)
 
 
+def run_gemv(args, local_rank):
+    """Small-M grouped GEMV (decode / scoring steps; C5-shaped layers: hidden 2560, 32q/8kv x 128,
+    FF 9728, Q4 g64): HBM-bound, so the roofline is the weight (+ scale) bytes streamed from HBM
+    per launch over the measured copy bandwidth.  L2 is flushed before every launch, so the
+    weights come from HBM; device-timed with CUDA events, K launches per shape."""
+    import torch
+
+    import decisive_b200 as db
+    from oracle import oracle
+    torch.cuda.set_device(local_rank)
+    hid, ff = 2560, 9728
+    shapes = [("qkv", hid, 32 * 128 + 2 * 8 * 128), ("o", 32 * 128, hid), ("gate_up", hid, 2 * ff), ("down", ff, hid)]
+    rows = [int(v) for v in args.gemv_rows.split(",")]
+    flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device="cuda")
+    _, peak_gbs, kind = measured_peaks()
+    results = []
+    for name, k, n in shapes:
+        rng = np.random.default_rng(k * 7 + n)
+        w = oracle.f32_to_bf16(rng.normal(0, 0.02, (n, k)).astype(np.float32))
+        codes, scales = db.pack_weights(torch.from_numpy(w.view(np.int16)).cuda(), args.bits)
+        wbytes = codes.numel() * codes.element_size() + (k // 64) * n * 4
+        for m in rows:
+            x = torch.from_numpy(rng.normal(0, 1, (m, k)).astype(np.float32)).cuda()
+            a, sa, sums = db.quantize_activations(x, bits=8, layout=db.CODES_GEMV, sums=True)
+            y = torch.empty((m, n), dtype=torch.float32, device="cuda")
+            for _ in range(args.warmup):
+                db.gemm(a, db.CODES_GEMV, sa, codes, scales, m, n, k, args.bits, a_sums=sums, residual=y)
+            torch.cuda.synchronize()
+            times = []
+            for _ in range(args.steps):
+                flush.zero_()
+                # a few microseconds of GPU sleep so the launch below is queued before the start
+                # event fires (the host-side call must not be inside the measured interval)
+                torch.cuda._sleep(200_000)
+                s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s.record()
+                db.gemm(a, db.CODES_GEMV, sa, codes, scales, m, n, k, args.bits, a_sums=sums, residual=y)
+                e.record()
+                torch.cuda.synchronize()
+                times.append(s.elapsed_time(e))
+            us = float(np.median(times)) * 1e3
+            gbs = wbytes / us / 1e3
+            results.append({"layer": name, "M": m, "K": k, "N": n, "weight_bytes": wbytes, "us": us,
+                            "GB/s": gbs, "frac_of_hbm": gbs / peak_gbs})
+    print(json.dumps({"workload": f"gemv Q{args.bits} g64 C5-shaped layers", "peak_hbm_gbs": peak_gbs,
+                      "peak_kind": kind, "l2": "flushed before every launch", "launches_per_case": args.steps,
+                      "cases": results}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -366,7 +416,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-layers", type=int, default=2)
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--workload", default="encoder", choices=["encoder", "gemm"])
+    ap.add_argument("--workload", default="encoder", choices=["encoder", "gemm", "gemv"])
+    ap.add_argument("--gemv-rows", default="1,4,8", help="activation rows (M) for --workload gemv")
     ap.add_argument("--gemm-shape", default="1024,1024,3072", help="M,K,N for --workload gemm")
     ap.add_argument("--bits", type=int, default=4)
     args = ap.parse_args()
@@ -375,6 +426,8 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", 0))
     if args.workload == "gemm":
         run_gemm(args, local_rank)
+    elif args.workload == "gemv":
+        run_gemv(args, local_rank)
     elif args.impl == "reference":
         run_reference(args, rank)
     else:
