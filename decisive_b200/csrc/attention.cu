@@ -2,6 +2,8 @@
 // softmax (the reference computes scale * q.k, softmax, then P.v per head in f32:
 // backbone.rs:560-600).  One CTA = 64 queries of one head, 4 warps x 16 query rows; K/V tiles
 // of 64 keys double-buffered in 128B-swizzled shared memory via cp.async.
+#include <float.h>
+
 #include "common.cuh"
 #include "layer_ops.h"
 
@@ -55,9 +57,16 @@ __device__ __forceinline__ void load_tile(uint32_t dst, const __half* base, int 
     }
 }
 
+// QUANT: instead of the f32 context, write what the output projection consumes -- the context
+// quantised per 64-wide group with the activation quantiser (int8.rs:178-202, 305-391): f16 codes
+// in tensor-core order [T, ldc] and scales [groups, lds] -- and raise *nonfinite on a non-finite
+// value (the NaN guard of Matrix::apply, int8.rs:170-173).
+template <bool QUANT>
 __global__ void __launch_bounds__(ATT_THREADS)
     attention_kernel(const __half* __restrict__ q16, const __half* __restrict__ k16, const __half* __restrict__ v16,
-                     int T, int Hq, int Hk, float scale_log2, float* __restrict__ out, int64_t ldo) {
+                     int T, int Hq, int Hk, float scale_log2, float* __restrict__ out, int64_t ldo,
+                     __half* __restrict__ codes, int64_t ldc, float* __restrict__ scales, int64_t lds,
+                     int* __restrict__ nonfinite) {
     extern __shared__ __align__(128) uint8_t smem[];
     const uint32_t sQ = smem_u32(smem);
     const uint32_t sK[2] = {sQ + ATT_TILE_BYTES, sQ + 2 * ATT_TILE_BYTES};
@@ -177,6 +186,60 @@ __global__ void __launch_bounds__(ATT_THREADS)
     // normalise and store
     const float inv0 = 1.f / lrow[0], inv1 = 1.f / lrow[1];
     const int r0 = q0 + warp * 16 + (lane >> 2);
+    if constexpr (QUANT) {
+        // Rows r0 and r0 + 8 of this warp: 16 values per 64-wide group per thread, the rest of the
+        // group on the other three lanes of the quad.  Codes go through shared memory (the Q tile,
+        // free after the last iteration's barrier) in the tensor-core order k0,k4,k1,k5,k2,k6,k3,k7
+        // of every 8 consecutive features, then out as 16-byte rows.
+        const int q = lane & 3;
+        const int pos0 = (q < 2) ? 4 * q : 4 * (q - 2) + 1;  // stored position of feature 2q in its 8-block
+        bool bad = false;
+#pragma unroll
+        for (int grp = 0; grp < 2; ++grp) {
+#pragma unroll
+            for (int rr = 0; rr < 2; ++rr) {
+                const float inv = rr ? inv1 : inv0;
+                float v[16];
+                float amax = 0.f;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    v[2 * i] = o[grp * 8 + i][2 * rr] * inv;
+                    v[2 * i + 1] = o[grp * 8 + i][2 * rr + 1] * inv;
+                    amax = fmaxf(amax, fmaxf(fabsf(v[2 * i]), fabsf(v[2 * i + 1])));
+                    bad |= !isfinite(v[2 * i]) || !isfinite(v[2 * i + 1]);
+                }
+                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+                // group_scale (int8.rs:305-313) and pack_bits (int8.rs:347-360)
+                const float scale = fmaxf(__fdiv_rn(amax, 127.f), FLT_MIN);
+                const float rinv = __fdiv_rn(1.f, scale);
+                const int row = warp * 16 + (lane >> 2) + 8 * rr;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const int col = grp * 64 + i * 8 + pos0;  // feature grp*64 + 8i + 2q and its neighbour
+                    const __half c0 = __float2half_rn(fminf(fmaxf(rintf(__fmul_rn(v[2 * i], rinv)), -127.f), 127.f));
+                    const __half c1 = __float2half_rn(fminf(fmaxf(rintf(__fmul_rn(v[2 * i + 1], rinv)), -127.f), 127.f));
+                    reinterpret_cast<__half*>(smem)[row * ATT_D + col] = c0;
+                    reinterpret_cast<__half*>(smem)[row * ATT_D + col + 2] = c1;
+                }
+                const int t = q0 + row;
+                if (q == 0 && t < T) scales[(size_t)(h * 2 + grp) * lds + t] = scale;
+            }
+        }
+        if (bad) atomicOr(nonfinite, 1);
+        __syncthreads();
+        // 64 rows x 256 bytes: 16-byte chunks, 16 per row
+#pragma unroll
+        for (int i = 0; i < (ATT_BQ * 16) / ATT_THREADS; ++i) {
+            const int idx = tid + i * ATT_THREADS;
+            const int row = idx >> 4, chunk = idx & 15;
+            const int t = q0 + row;
+            if (t < T)
+                *reinterpret_cast<uint4*>(codes + (size_t)t * ldc + h * ATT_D + chunk * 8) =
+                    reinterpret_cast<const uint4*>(smem)[row * 16 + chunk];
+        }
+        return;
+    }
 #pragma unroll
     for (int n = 0; n < 16; ++n) {
         const int d = n * 8 + 2 * (lane & 3);
@@ -199,12 +262,30 @@ int db_launch_attention(const __half* q16, const __half* k16, const __half* v16,
     const int smem = 5 * ATT_TILE_BYTES;
     static bool configured = false;
     if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        cudaError_t e = cudaFuncSetAttribute(attention_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return (int)e;
         configured = true;
     }
     dim3 grid((T + ATT_BQ - 1) / ATT_BQ, Hq);
-    attention_kernel<<<grid, ATT_THREADS, smem, stream>>>(q16, k16, v16, T, Hq, Hk, scale * 1.4426950408889634f, out,
-                                                          ldo);
+    attention_kernel<false><<<grid, ATT_THREADS, smem, stream>>>(q16, k16, v16, T, Hq, Hk, scale * 1.4426950408889634f,
+                                                                 out, ldo, nullptr, 0, nullptr, 0, nullptr);
+    return (int)cudaGetLastError();
+}
+
+int db_launch_attention_quant(const __half* q16, const __half* k16, const __half* v16, int T, int Hq, int Hk,
+                              float scale, __half* codes, int64_t ldc, float* scales, int64_t lds, int* nonfinite,
+                              cudaStream_t stream) {
+    if (T <= 0) return 0;
+    if (Hk <= 0 || Hq % Hk || !codes || !scales || !nonfinite || (ldc & 7)) return (int)cudaErrorInvalidValue;
+    const int smem = 5 * ATT_TILE_BYTES;
+    static bool configured = false;
+    if (!configured) {
+        cudaError_t e = cudaFuncSetAttribute(attention_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return (int)e;
+        configured = true;
+    }
+    dim3 grid((T + ATT_BQ - 1) / ATT_BQ, Hq);
+    attention_kernel<true><<<grid, ATT_THREADS, smem, stream>>>(q16, k16, v16, T, Hq, Hk, scale * 1.4426950408889634f,
+                                                                nullptr, 0, codes, ldc, scales, lds, nonfinite);
     return (int)cudaGetLastError();
 }

@@ -17,3 +17,9 @@ int db_launch_fill_nan_if(float* y, int64_t n, const int* flag, cudaStream_t str
 // out f32 [T, Hq*128] with row stride ldo.  scale multiplies q.k before the softmax.
 int db_launch_attention(const __half* q16, const __half* k16, const __half* v16, int T, int Hq, int Hk, float scale,
                         float* out, int64_t ldo, cudaStream_t stream);
+// Same attention, writing the context already quantised for the output projection: f16 codes in
+// tensor-core order [T, ldc] (head h occupies features 128h..128h+127), per-64 scales [2*Hq, lds];
+// *nonfinite is raised when a context value is not finite.
+int db_launch_attention_quant(const __half* q16, const __half* k16, const __half* v16, int T, int Hq, int Hk,
+                              float scale, __half* codes, int64_t ldc, float* scales, int64_t lds, int* nonfinite,
+                              cudaStream_t stream);

@@ -310,14 +310,11 @@ int enqueue_forward(db_model* m, int T, const volatile uint8_t* cancel) {
                 return db_launch_qk_norm_rope(m->qkv, Nqkv, T, c.q_heads, c.kv_heads, w.q_norm, w.k_norm, c.eps,
                                               m->cos_t, m->sin_t, m->q16, m->k16, m->v16, st);
             });
+        // attention writes the context already quantised for the output projection
         if (!rc)
             rc = timed(4, [&] {
-                return db_launch_attention(m->q16, m->k16, m->v16, T, c.q_heads, c.kv_heads, attn_scale, m->ctx, Nq, st);
-            });
-        if (!rc)
-            rc = timed(5, [&] {
-                return db_launch_rms_quantize(m->ctx, Nq, nullptr, T, Nq, 0.f, 0, nullptr, 0, m->acodes, DB_CODES_TC,
-                                              ld_codes, m->sa, nullptr, lds, m->flag, st, /*normalize=*/0);
+                return db_launch_attention_quant(m->q16, m->k16, m->v16, T, c.q_heads, c.kv_heads, attn_scale,
+                                                 static_cast<__half*>(m->acodes), ld_codes, m->sa, lds, m->flag, st);
             });
         if (!rc) rc = timed(6, [&] { return gemm(m->acodes, w.o_c, w.o_s, m->sa, D, Nq, DB_EPI_RESIDUAL, m->x, D); });
         if (!rc)
