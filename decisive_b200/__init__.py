@@ -115,6 +115,21 @@ def gemm(a_codes, layout, sa, w_codes, sw, M, N, K, bits, fused=True, a_sums=Non
     return y
 
 
+EPILOGUE_STORE, EPILOGUE_RESIDUAL, EPILOGUE_SWIGLU = 0, 1, 2
+
+
+def tune_gemm(M: int, N: int, K: int, bits: int, epilogue: int = EPILOGUE_STORE, cache_path: str | None = None):
+    """Kernel-selection tuner for one GEMM shape (the reference's rule, webgpu/checkpoint.rs:420-565):
+    the fastest tile configuration bitwise equal to the default and >= 1 % faster.  Returns
+    (GemmConfig, report dict)."""
+    import json
+    choice = GemmConfig()
+    buf = C.create_string_buffer(16384)
+    path = cache_path.encode() if cache_path else None
+    check(load().db_gemm_tune(M, N, K, bits, epilogue, path, C.byref(choice), buf, len(buf)))
+    return choice, json.loads(buf.value.decode())
+
+
 def linear(x, w_codes, sw, N: int, weight_bits: int = 4, activation_bits: int = 8, fused: bool = True):
     """Matrix::apply (int8.rs:166-176): quantise + grouped GEMM (GEMV path for small M)."""
     import torch
@@ -421,6 +436,18 @@ class Model:
         check(load().db_model_profile_read(self._h, ms.ctypes.data_as(C.c_void_p), cnt.ctypes.data_as(C.c_void_p), n,
                                            int(reset)))
         return {load().db_model_profile_name(k).decode(): (float(ms[k]), int(cnt[k])) for k in range(n)}
+
+    def tune(self, tokens: int | None = None, cache_path: str | None = None) -> dict:
+        """Tunes the four projection GEMMs at `tokens` rows (default: max_sequence_tokens) and uses
+        the choices from then on; returns the per-projection reports."""
+        import json
+        err = _lib.DbError()
+        buf = C.create_string_buffer(65536)
+        n = tokens if tokens is not None else self.config.max_sequence_tokens
+        rc = load().db_model_tune(self._h, n, cache_path.encode() if cache_path else None, buf, len(buf), C.byref(err))
+        if rc:
+            raise Error._from(err)
+        return json.loads(buf.value.decode())
 
     def forward_device(self, ids_dev, out_dev, stream=None):
         """Device-resident forward (no host synchronisation) used for device-timed measurement."""

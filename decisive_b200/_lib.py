@@ -58,6 +58,7 @@ SIGNATURES = [
     ("db_gemm_g64_config", _i32, [_vp, _i32, _i64, _vp, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _i32, _i32, _i32, _vp,
                                   _i64, _vp, _vp, _vp]),
     ("db_gemv_max_rows", _i32, []),
+    ("db_gemm_tune", _i32, [_i64, _i64, _i64, _i32, _i32, C.c_char_p, _vp, C.c_char_p, _sz]),
     ("db_linear_workspace_bytes", _sz, [_i64, _i64]),
     ("db_linear_g64", _i32, [_vp, _i64, _i64, _vp, _vp, _i64, _i32, _i32, _i32, _vp, _vp, _vp]),
     ("db_linear_noalloc_scratch_bytes", _sz, []),
@@ -80,6 +81,7 @@ SIGNATURES = [
                                 C.POINTER(DbError)]),
     ("db_forward_device", _i32, [_vp, _vp, _i64, _vp, _vp]),
     ("db_model_profile", _i32, [_vp, _i32]),
+    ("db_model_tune", _i32, [_vp, _i64, C.c_char_p, C.c_char_p, _sz, C.POINTER(DbError)]),
     ("db_model_profile_read", _i32, [_vp, _vp, _vp, _i32, _i32]),
     ("db_model_profile_name", C.c_char_p, [_i32]),
 ]

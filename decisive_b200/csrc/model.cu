@@ -69,6 +69,8 @@ struct db_model {
     int32_t* ids = nullptr;
     int* flag = nullptr;
     int* dev_err = nullptr;
+    // tile configurations chosen by db_model_tune for qkv, o, gate/up, down (zero = defaults)
+    db_gemm_config tuned[4] = {};
     // per-launch CUDA-event profiling (mirror of the reference's projection_ms accounting,
     // cpu.rs:8-16 / native.rs:229-258), enabled by db_model_profile
     bool profile = false;
@@ -271,8 +273,8 @@ int enqueue_forward(db_model* m, int T, const volatile uint8_t* cancel) {
     rc = timed(0, [&] {
         return db_launch_dequant_rows(m->emb_c, m->emb_s, c.vocab, D, bits, m->ids, T, m->x, D, m->flag, st);
     });
-    auto gemm = [&](const void* a, const uint8_t* wc, const float* ws, const float* sa, int N, int K, int epi, float* y,
-                    int64_t ldy) {
+    auto gemm = [&](int proj, const void* a, const uint8_t* wc, const float* ws, const float* sa, int N, int K, int epi,
+                    float* y, int64_t ldy) {
         DbGemmArgs g{};
         g.a_codes = a;
         g.lda = ld_codes;
@@ -294,6 +296,9 @@ int enqueue_forward(db_model* m, int T, const volatile uint8_t* cancel) {
         g.ldos = lds;
         g.nonfinite = m->flag;
         g.dev_error = m->dev_err;
+        g.block_n = m->tuned[proj].block_n;
+        g.max_ctas = m->tuned[proj].max_ctas;
+        g.pair_ctas = m->tuned[proj].pair_ctas;
         return db_launch_gemm_tc(g, st);
     };
     const float attn_scale = 1.f / sqrtf((float)c.head_dim);
@@ -304,7 +309,7 @@ int enqueue_forward(db_model* m, int T, const volatile uint8_t* cancel) {
             return db_launch_rms_quantize(m->x, D, w.in_norm, T, D, c.eps, 0, nullptr, 0, m->acodes, DB_CODES_TC,
                                           ld_codes, m->sa, nullptr, lds, m->flag, st);
         });
-        if (!rc) rc = timed(2, [&] { return gemm(m->acodes, w.qkv_c, w.qkv_s, m->sa, Nqkv, D, DB_EPI_STORE, m->qkv, Nqkv); });
+        if (!rc) rc = timed(2, [&] { return gemm(0, m->acodes, w.qkv_c, w.qkv_s, m->sa, Nqkv, D, DB_EPI_STORE, m->qkv, Nqkv); });
         if (!rc)
             rc = timed(3, [&] {
                 return db_launch_qk_norm_rope(m->qkv, Nqkv, T, c.q_heads, c.kv_heads, w.q_norm, w.k_norm, c.eps,
@@ -316,14 +321,14 @@ int enqueue_forward(db_model* m, int T, const volatile uint8_t* cancel) {
                 return db_launch_attention_quant(m->q16, m->k16, m->v16, T, c.q_heads, c.kv_heads, attn_scale,
                                                  static_cast<__half*>(m->acodes), ld_codes, m->sa, lds, m->flag, st);
             });
-        if (!rc) rc = timed(6, [&] { return gemm(m->acodes, w.o_c, w.o_s, m->sa, D, Nq, DB_EPI_RESIDUAL, m->x, D); });
+        if (!rc) rc = timed(6, [&] { return gemm(1, m->acodes, w.o_c, w.o_s, m->sa, D, Nq, DB_EPI_RESIDUAL, m->x, D); });
         if (!rc)
             rc = timed(1, [&] {
                 return db_launch_rms_quantize(m->x, D, w.post_norm, T, D, c.eps, 0, nullptr, 0, m->acodes, DB_CODES_TC,
                                               ld_codes, m->sa, nullptr, lds, m->flag, st);
             });
         if (!rc)
-            rc = timed(7, [&] { return gemm(m->acodes, w.gu_c, w.gu_s, m->sa, 2 * F, D, DB_EPI_SWIGLU_QUANT, nullptr, 0); });
+            rc = timed(7, [&] { return gemm(2, m->acodes, w.gu_c, w.gu_s, m->sa, 2 * F, D, DB_EPI_SWIGLU_QUANT, nullptr, 0); });
         if (!rc) rc = timed(8, [&] {
             DbGemmArgs g{};
             g.a_codes = m->hcodes;
@@ -342,6 +347,9 @@ int enqueue_forward(db_model* m, int T, const volatile uint8_t* cancel) {
             g.ldy = D;
             g.nonfinite = m->flag;
             g.dev_error = m->dev_err;
+            g.block_n = m->tuned[3].block_n;
+            g.max_ctas = m->tuned[3].max_ctas;
+            g.pair_ctas = m->tuned[3].pair_ctas;
             return db_launch_gemm_tc(g, st);
         });
     }
@@ -565,6 +573,37 @@ int db_model_profile_read(db_model* m, double* ms, int64_t* counts, int n, int r
 }
 
 const char* db_model_profile_name(int kind) { return kind >= 0 && kind < DB_PROF_KINDS ? kProfNames[kind] : ""; }
+
+int db_model_tune(db_model* m, int64_t tokens, const char* cache_path, char* report_json, size_t cap, db_error* err) {
+    if (!m || tokens <= 0 || tokens > m->cfg.max_sequence_tokens) {
+        fill_error(err, "INVALID_PARAMETERS", "tune: tokens must be in [1, max_sequence_tokens]");
+        return DB_ERR_INVALID_ARGUMENT;
+    }
+    cudaSetDevice(m->device);
+    const int D = m->D(), F = m->F();
+    // the four projections of a layer: {N, K, epilogue}
+    const int64_t shapes[4][3] = {{m->Nqkv(), D, DB_EPI_STORE},
+                                  {D, m->Nq(), DB_EPI_RESIDUAL},
+                                  {2 * F, D, DB_EPI_SWIGLU_QUANT},
+                                  {D, F, DB_EPI_RESIDUAL}};
+    static const char* names[4] = {"qkv", "o", "gate_up", "down"};
+    db_gemm_config chosen[4] = {};
+    std::string all = "{";
+    for (int p = 0; p < 4; ++p) {
+        std::string rep;
+        const int rc = db_tune_gemm_shape(tokens, shapes[p][0], shapes[p][1], m->cfg.weight_bits, (int)shapes[p][2],
+                                          cache_path, &chosen[p], &rep, m->stream);
+        if (rc) {
+            fill_error(err, db_last_error_code(), db_last_error_message());
+            return rc;
+        }
+        all += std::string(p ? "," : "") + "\"" + names[p] + "\":" + rep;
+    }
+    all += "}";
+    for (int p = 0; p < 4; ++p) m->tuned[p] = chosen[p];
+    if (report_json && cap) std::snprintf(report_json, cap, "%s", all.c_str());
+    return DB_OK;
+}
 
 int db_forward_device(db_model* m, const int32_t* ids_dev, int64_t n, float* out_dev, void* stream) {
     if (!m || !ids_dev || n <= 0 || !out_dev)

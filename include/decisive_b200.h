@@ -127,6 +127,19 @@ int db_gemm_g64_config(const void *a_codes, int layout, int64_t lda, const float
                        const db_gemm_config *config, void *stream);
 int db_gemv_max_rows(void);
 
+/* Kernel-selection tuner for one tensor-core GEMM shape, with the reference's rule
+ * (webgpu/checkpoint.rs:420-565, the int8_gemm candidate selection): each candidate tile
+ * configuration runs on synthetic inputs; the fastest candidate whose output is bitwise equal to
+ * the default configuration's and that is at least 1 % faster (best of 10 timed launches) is
+ * chosen, else the default.  cache_path (NULL = no cache): a text file of tuned choices keyed by
+ * a hash of the device name, SM count, compute capability, driver version, library build and
+ * shape (the reference keys by adapter, user agent, weight bits and kernel sources,
+ * checkpoint.rs:279-294); a cached choice is only checked for equality again.  epilogue:
+ * 0 store, 1 residual add, 2 SwiGLU re-quantisation (N = 2F, N % 128 == 0).  report_json
+ * (optional): the candidates, their equality and best times, and the choice. */
+int db_gemm_tune(int64_t M, int64_t N, int64_t K, int bits, int epilogue, const char *cache_path,
+                 db_gemm_config *choice, char *report_json, size_t cap);
+
 /* Full projection: quantise x (f32 [M, K]) then GEMM, choosing the GEMV path for
  * M <= db_gemv_max_rows() and the tensor-core path otherwise.  Replaces Matrix::apply
  * (int8.rs:166-176) including its non-finite guard.  workspace: device bytes from
@@ -252,6 +265,12 @@ int db_predict_batch(db_model *m, const int32_t *const *ids, const size_t *lens,
 int db_model_profile(db_model *m, int enable);
 int db_model_profile_read(db_model *m, double *ms, int64_t *counts, int n, int reset);
 const char *db_model_profile_name(int kind);
+
+/* Tunes the model's four projection GEMMs (qkv, o, gate/up + SwiGLU, down) at `tokens` rows with
+ * db_gemm_tune's rule and uses the choices in every later forward.  Every configuration is
+ * bitwise equal, so only speed changes.  report_json: one object per projection. */
+int db_model_tune(db_model *m, int64_t tokens, const char *cache_path, char *report_json, size_t cap,
+                  db_error *err);
 
 /* Device-resident variant for throughput measurement: ids already on the device, output left on
  * the device; no host synchronisation.  Used by bench.py's device-timed leg. */
