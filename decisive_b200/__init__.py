@@ -97,7 +97,7 @@ def dequant_rows(codes, scales, N: int, K: int, bits: int, ids=None):
 
 
 class GemmConfig(C.Structure):
-    """db_gemm_config: tile width (0 = default, 64, 128), persistent grid cap (0 = all SMs) and
+    """db_gemm_config: tile width (0 = default, 64, 128, 256), persistent grid cap (0 = all SMs) and
     CTA pairing (1 = clusters of two CTAs with M = 256 MMAs).  The tuner's candidate space."""
     _fields_ = [("block_n", C.c_int), ("max_ctas", C.c_int), ("pair_ctas", C.c_int)]
 

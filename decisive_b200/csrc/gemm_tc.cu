@@ -7,19 +7,22 @@
 // The integer dots come from tcgen05.mma kind::f16 on integer-valued f16 operands: every code
 // is exact in f16, every product and every partial sum of one group (|sum| <= 64*127*127 < 2^24)
 // is an exact f32 integer, so the tensor core returns dot_g exactly.  Each 64-wide group is one
-// K-block; its dot lands in its own TMEM buffer (four buffers) and the epilogue warps fold it into
-// their register accumulators with the reference's rounding, in group order.
+// K-block; its dot lands in its own TMEM buffer (512 / BN buffers, at most eight) and the epilogue
+// warps fold it into their register accumulators with the reference's rounding, in group order.
 //
-// Roles (512 threads, one CTA per SM, persistent over 128 x BN output tiles):
+// Roles (512 threads, one CTA per SM, persistent over 128 x BN output tiles, BN = 64, 128 or 256;
+// the pipeline hands work over in jobs of two K groups, one for BN = 256):
 //   warp 0      TMA producer: one stage per pair of K groups, loaded by a single three-lane TMA
 //               instruction (activation tiles of both groups, 128 x 64 f16 with 128B swizzle, and
 //               the raw weight codes of both groups, BN rows)
-//   warp 1      TMEM owner + MMA issuer (one elected lane): 4 x (128 x BN x 16) MMAs per group;
-//               its commit releases the stage once both groups of the pair are multiplied
+//   warp 1      TMEM owner + MMA issuer (one elected lane): 4 x (128 x BN x 16) MMAs per group,
+//               one combined wait (three polling lanes) and one commit per job plus the stage's
 //   warps 2-5   converters (one per SM sub-partition): weight nibbles/bytes -> f16 codes in the
 //               UMMA K-major SW128 layout, one B tile per group (warps 6-7 idle)
-//   warps 8-15  epilogue (192 registers each through setmaxnreg): per-group scale vectors prefetched with cp.async a few groups ahead,
-//               TMEM -> registers, f32x2 scale fold, final store / fused SwiGLU re-quantisation
+//   warps 8-15  epilogue (192 registers each through setmaxnreg): one warp polls the job barrier
+//               while the others sleep in a hardware barrier; per-group scale vectors prefetched
+//               with cp.async a few groups ahead, a group's TMEM columns loaded under one wait,
+//               f32x2 scale fold, final store / fused SwiGLU re-quantisation
 //               (grouped_q4_mlp.wgsl:83-105 semantics)
 // Every mbarrier wait is bounded (DB_WAIT_LIMIT_NS); on expiry the CTA records an error in the
 // device error word, stops issuing work, lets its own copies and MMAs land, and releases its
@@ -36,7 +39,6 @@ namespace db {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
-constexpr int NUM_ACC = 4;         // TMEM accumulator buffers (NUM_ACC x BN columns <= 512)
 constexpr int CONVERTER_WARP0 = 2;
 constexpr int CONVERTER_WARPS = 4;  // warps 2-5; warps 6-7 only fill their warpgroup
 constexpr int EPILOGUE_WARP0 = 8;   // warps 8-15: warpgroups 2 and 3
@@ -48,44 +50,58 @@ constexpr int NUM_THREADS = 32 * (EPILOGUE_WARP0 + EPILOGUE_WARPS);  // 512
 constexpr int REGS_CONTROL = 64;
 constexpr int REGS_EPILOGUE = 192;
 static_assert(2 * 128 * REGS_CONTROL + 2 * 128 * REGS_EPILOGUE == 65536, "register split");
-constexpr int SC_DEPTH = 6;        // groups of scale vectors each epilogue warp keeps in flight
 constexpr int XCH_STRIDE = 33;     // floats per row of the SwiGLU exchange buffers (bank-conflict free)
 constexpr uint64_t DRAIN_NS = 100000000ull;  // wind-down wait for in-flight copies / MMAs
 
+// The pipeline moves in jobs of GPJ K-groups (two for tiles up to 128 wide, one for 256): one
+// combined wait and one or two tcgen05.commits per job in the MMA issuer, whose instruction stream
+// (an MMA issue costs ~60 cycles, a commit ~100-170, a satisfied wait ~165) otherwise sets the pace.
+// JS job slots hold the converted weight tiles and the TMEM accumulators of a job; one MMA commit
+// per job ("done") tells both the converters (weight slot free) and the epilogue (accumulators
+// ready).  A phase of done[js] cannot be skipped by any waiter: the job JS later needs the same
+// weight slot and accumulator buffers, which those waiters release first.
 template <int BN, int BITS, int EPI, bool PAIR>
 struct GemmSmem {
+    static constexpr int GPJ = BN <= 128 ? 2 : 1;          // K groups per job
+    static constexpr int BUFS = 512 / BN > 8 ? 8 : 512 / BN;  // TMEM accumulator buffers (BUFS x BN <= 512 columns)
+    static constexpr int JS = BUFS / GPJ;                   // job slots: 4 (BN 64), 2 (BN 128, 256)
+    static constexpr int SC_DEPTH = BN >= 256 ? 3 : 6;      // groups of scale vectors each epilogue warp keeps in flight
     static constexpr int WR = PAIR ? BN / 2 : BN;          // weight rows held by this CTA
     static constexpr int A_BYTES = BM * BK * 2;            // one group of activation codes, 16 KB
     static constexpr int W_ROW = BK * BITS / 8;            // raw weight-code bytes per row and group
     static constexpr int WP_BYTES = WR * 2 * W_ROW;        // raw weight codes of a group pair
     static constexpr int STAGE_BYTES = (2 * A_BYTES + WP_BYTES + 1023) / 1024 * 1024;
     static constexpr int TX_BYTES = 2 * A_BYTES + WP_BYTES;  // full boxes, also for a lone tail group
-    static constexpr int B_BYTES = WR * BK * 2;            // converted f16 weight tile of one group
+    static constexpr int BG_BYTES = WR * BK * 2;           // converted f16 weight tile of one group
+    static constexpr int B_SLOT = GPJ * BG_BYTES;          // converted weight tiles of one job
     static constexpr int COLS = BN / 2;                    // accumulator columns per epilogue thread
     static constexpr int SC_SLOT = (32 + COLS) * 4;        // sa of a warp's 32 rows + sw of its columns
     static constexpr int SC_BYTES = EPILOGUE_WARPS * SC_DEPTH * SC_SLOT;
     // SwiGLU exchange: 32 gate and 32 up columns per row, plus each half's row maxima
     static constexpr int XCH_BYTES = EPI == DB_EPI_SWIGLU_QUANT ? 2 * BM * XCH_STRIDE * 4 + 2 * BM * 4 : 0;
-    // output staging for the TMA store: per epilogue warp two buffers of 32 rows x 16 f32 columns
+    // output staging for the TMA store: per epilogue warp one or two buffers of 32 rows x 16 f32 columns
     static constexpr int Y_CHUNK = 32 * 16 * 4;
-    static constexpr int Y_BYTES = EPI == DB_EPI_SWIGLU_QUANT ? 0 : EPILOGUE_WARPS * 2 * Y_CHUNK;
     static constexpr int BUDGET = 232448 - 1024 - 512;     // opt-in limit - alignment slack - barriers
-    static constexpr bool fits(int st, int b) {
-        return SC_BYTES + XCH_BYTES + Y_BYTES + st * STAGE_BYTES + b * B_BYTES <= BUDGET;
+    static constexpr bool fits(int st, int ybufs) {
+        return SC_BYTES + XCH_BYTES + (EPI == DB_EPI_SWIGLU_QUANT ? 0 : EPILOGUE_WARPS * ybufs * Y_CHUNK) +
+                   st * STAGE_BYTES + JS * B_SLOT <= BUDGET;
     }
-    static constexpr int B_STAGES = fits(3, 8) ? 8 : fits(3, 6) ? 6 : fits(3, 4) ? 4 : 3;
-    static constexpr int STAGES = fits(4, B_STAGES) ? 4 : fits(3, B_STAGES) ? 3 : 2;
+    // preference: stages (TMA lookahead) first, then double-buffered output staging
+    static constexpr int STAGES = fits(4, 2) ? 4 : fits(3, 1) ? 3 : 2;
+    static constexpr int Y_BUFS = fits(STAGES, 2) ? 2 : 1;
+    static constexpr int Y_BYTES = EPI == DB_EPI_SWIGLU_QUANT ? 0 : EPILOGUE_WARPS * Y_BUFS * Y_CHUNK;
     static constexpr int OFF_STAGE = 0;
     static constexpr int OFF_B = OFF_STAGE + STAGES * STAGE_BYTES;
-    static constexpr int OFF_SC = OFF_B + B_STAGES * B_BYTES;
+    static constexpr int OFF_SC = OFF_B + JS * B_SLOT;
     static constexpr int OFF_X = OFF_SC + SC_BYTES;
     static constexpr int OFF_Y = OFF_X + XCH_BYTES;
     static constexpr int OFF_BAR = (OFF_Y + Y_BYTES + 15) / 16 * 16;
-    static constexpr int NUM_BARS = 3 * STAGES + 2 * B_STAGES + 2 * NUM_ACC + 4;
+    static constexpr int NUM_BARS = 3 * STAGES + 3 * JS + 4;
     static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
     static constexpr int BYTES = OFF_MISC + 16 + 1024;     // + alignment slack
-    static_assert(fits(STAGES, B_STAGES) && BYTES <= 232448, "shared memory budget");
-    static_assert(STAGE_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "SW128 tiles need 1024-byte alignment");
+    static_assert(fits(STAGES, Y_BUFS) && BYTES <= 232448, "shared memory budget");
+    static_assert(STAGE_BYTES % 1024 == 0 && BG_BYTES % 1024 == 0, "SW128 tiles need 1024-byte alignment");
+    static_assert(JS >= 2, "job slots must double-buffer");
 };
 
 // Warp-wide bounded wait.  Only lane 0 polls the barrier (32 pollers per warp would flood the
@@ -158,15 +174,15 @@ __device__ __forceinline__ float silu_ref(float x) {
     return __fmul_rn(x, __frcp_rn(__fadd_rn(1.f, expf(-x))));
 }
 
-// Folds one group's 16 columns into 8 packed accumulator pairs:
+// Folds NC columns of one group into NC / 2 packed accumulator pairs:
 //   fused:    acc = fma(d, sw * sa, acc)     (AVX2 path, int8.rs:566-572)
 //   portable: acc = acc + d * (sa * sw)      (int8.rs:259-287)
 // w holds the 16 weight scales of these columns (the same for every lane).
-template <bool FUSED>
-__device__ __forceinline__ void fold16(uint64_t* acc, const uint32_t (&v)[16], const uint4 (&w)[4], float s_a) {
+template <bool FUSED, int NC>
+__device__ __forceinline__ void fold_cols(uint64_t* acc, const uint32_t (&v)[NC], const uint4 (&w)[NC / 4], float s_a) {
     const uint64_t sa2 = f2_pack(__float_as_uint(s_a), __float_as_uint(s_a));
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < NC / 4; ++i) {
         const int j = 4 * i;
         if (FUSED) {
             acc[j / 2] = f2_fma(f2_pack(v[j], v[j + 1]), f2_mul(f2_pack(w[i].x, w[i].y), sa2), acc[j / 2]);
@@ -230,15 +246,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::OFF_BAR);
     uint64_t* full = bars;                   // stage loaded (TMA tx)
     uint64_t* empty = full + S::STAGES;      // stage released by the MMA commit
-    uint64_t* b_full = empty + S::STAGES;    // converted weight tile ready (4 converter warps)
-    uint64_t* b_empty = b_full + S::B_STAGES;  // converted tile consumed by the MMA
-    uint64_t* acc_full = b_empty + S::B_STAGES;
-    uint64_t* acc_empty = acc_full + NUM_ACC;
-    uint64_t* xch_full = acc_empty + NUM_ACC;  // SwiGLU exchange: both halves' columns published
-    uint64_t* xch_empty = xch_full + 1;        // every epilogue warp is done with this tile's exchange
-    uint64_t* xch_amax = xch_empty + 1;        // both halves' row maxima published
-    uint64_t* mma_done = xch_amax + 1;         // final commit of the MMA issuer
-    uint64_t* wfull = mma_done + 1;            // pair mode: this CTA's raw weight codes loaded
+    uint64_t* wfull = empty + S::STAGES;     // pair mode: this CTA's raw weight codes loaded
+    uint64_t* b_full = wfull + S::STAGES;    // job slot: converted weight tiles ready (4 converter warps)
+    uint64_t* done = b_full + S::JS;         // job slot: the job's MMAs completed (weights free, accumulators ready)
+    uint64_t* acc_empty = done + S::JS;      // job slot: the epilogue has read the accumulators
+    uint64_t* xch_full = acc_empty + S::JS;  // SwiGLU exchange: both halves' columns published
+    uint64_t* xch_empty = xch_full + 1;      // every epilogue warp is done with this tile's exchange
+    uint64_t* xch_amax = xch_empty + 1;      // both halves' row maxima published
+    uint64_t* mma_done = xch_amax + 1;       // final commit of the MMA issuer
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::OFF_MISC);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + S::OFF_MISC + 4);
 
@@ -264,8 +279,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             mbar_init(&empty[i], 1);
             mbar_init(&wfull[i], 1);
         }
-        for (int i = 0; i < S::B_STAGES; ++i) { mbar_init(&b_full[i], NC * CONVERTER_WARPS); mbar_init(&b_empty[i], 1); }
-        for (int i = 0; i < NUM_ACC; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], NC * EPILOGUE_WARPS); }
+        for (int i = 0; i < S::JS; ++i) {
+            mbar_init(&b_full[i], NC * CONVERTER_WARPS);
+            mbar_init(&done[i], 1);
+            mbar_init(&acc_empty[i], NC * EPILOGUE_WARPS);
+        }
         mbar_init(xch_full, EPILOGUE_WARPS);
         mbar_init(xch_empty, EPILOGUE_WARPS);
         mbar_init(xch_amax, EPILOGUE_WARPS);
@@ -279,10 +297,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     if (warp == 1) {
         if (PAIR) {
-            tmem_alloc_pair(tmem_slot, NUM_ACC * BN);
+            tmem_alloc_pair(tmem_slot, S::BUFS * BN);
             tmem_relinquish_pair();
         } else {
-            tmem_alloc(tmem_slot, NUM_ACC * BN);
+            tmem_alloc(tmem_slot, S::BUFS * BN);
             tmem_relinquish();
         }
     }
@@ -343,48 +361,59 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         // The whole warp runs the loop (lane 0 polls the barriers and issues), so the warp stays
         // converged instead of idling 31 lanes at the CTA barrier.
         constexpr uint32_t IDESC = idesc_f16_f32(MT, BN);
-        int is = 0, ib = 0, ic = 0;
-        uint32_t ps = 0, pb = 0, pc = 0;
+        constexpr int GPJ = S::GPJ;
+        int is = 0, js = 0;
+        uint32_t ps = 0, pj = 0;
         const uint32_t st_base = smem_u32(smem + S::OFF_STAGE), b_base = smem_u32(smem + S::OFF_B);
         if (!leader) goto mma_peer;  // the even CTA issues the pair's MMAs
         for (int tile = tile0; tile < tiles; tile += tstride) {
-            for (int g = 0; g < G; ++g) {
-                if (!(g & 1) && !warp_wait(&full[is], ps, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_MMA)) goto mma_end;
-                if (!warp_wait(&b_full[ib], pb, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_MMA)) goto mma_end;
-                if (!warp_wait(&acc_empty[ic], pc ^ 1u, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_MMA)) goto mma_end;
+            for (int g = 0; g < G; g += GPJ) {
+                const int ng = (GPJ == 2 && g + 1 < G) ? 2 : 1;  // a lone last group past an odd G
+                const bool ends_stage = ((g + ng - 1) & 1) || g + ng - 1 == G - 1;
+                {
+                    // lanes 0-2 poll the stage, the job slot's weight tiles and its accumulator
+                    // buffers at the same time
+                    const bool need = (lane == 0 && !(g & 1)) || lane == 1 || lane == 2;
+                    uint64_t* bar = lane == 0 ? &full[is] : lane == 1 ? &b_full[js] : &acc_empty[js];
+                    const uint32_t par = lane == 0 ? ps : lane == 1 ? pj : (pj ^ 1u);
+                    const int ok = need ? (int)mbar_wait(bar, par, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_MMA) : 1;
+                    const bool all_ok = __all_sync(0xffffffffu, ok) != 0;
+                    __syncwarp();  // orders the pollers' acquires before lane 0's MMAs
+                    if (!all_ok) goto mma_end;
+                }
                 tc_fence_after();
                 if (lane == 0) {
-                    const uint32_t d = tmem_base + (uint32_t)(ic * BN);
-                    const uint32_t a_addr = st_base + is * S::STAGE_BYTES + (g & 1) * S::A_BYTES;
-                    const uint32_t b_addr = b_base + ib * S::B_BYTES;
-                    if (PAIR) {
 #pragma unroll
-                        for (int kk = 0; kk < BK / 16; ++kk)
-                            umma_f16_pair(d, sw128_desc(a_addr + kk * 32), sw128_desc(b_addr + kk * 32), IDESC, kk > 0);
-                        // completion signals go to both CTAs of the pair
-                        umma_commit_pair(smem_u32(&b_empty[ib]));
-                        umma_commit_pair(at_peer(&b_empty[ib]));
-                        umma_commit_pair(smem_u32(&acc_full[ic]));
-                        umma_commit_pair(at_peer(&acc_full[ic]));
-                        if ((g & 1) || g == G - 1) {
+                    for (int h = 0; h < GPJ; ++h) {
+                        if (h < ng) {
+                            const uint32_t d = tmem_base + (uint32_t)((js * GPJ + h) * BN);
+                            const uint32_t a_addr = st_base + is * S::STAGE_BYTES + ((g + h) & 1) * S::A_BYTES;
+                            const uint32_t b_addr = b_base + js * S::B_SLOT + h * S::BG_BYTES;
+#pragma unroll
+                            for (int kk = 0; kk < BK / 16; ++kk) {
+                                if (PAIR) umma_f16_pair(d, sw128_desc(a_addr + kk * 32), sw128_desc(b_addr + kk * 32), IDESC, kk > 0);
+                                else umma_f16(d, sw128_desc(a_addr + kk * 32), sw128_desc(b_addr + kk * 32), IDESC, kk > 0);
+                            }
+                        }
+                    }
+                    // one completion signal per job (both CTAs of a pair hear it), plus the stage's
+                    if (PAIR) {
+                        umma_commit_pair(smem_u32(&done[js]));
+                        umma_commit_pair(at_peer(&done[js]));
+                        if (ends_stage) {
                             umma_commit_pair(smem_u32(&empty[is]));
                             umma_commit_pair(at_peer(&empty[is]));
                         }
                     } else {
-#pragma unroll
-                        for (int kk = 0; kk < BK / 16; ++kk)
-                            umma_f16(d, sw128_desc(a_addr + kk * 32), sw128_desc(b_addr + kk * 32), IDESC, kk > 0);
-                        umma_commit(&b_empty[ib]);
-                        umma_commit(&acc_full[ic]);
-                        if ((g & 1) || g == G - 1) umma_commit(&empty[is]);  // both groups of the stage are multiplied
+                        umma_commit(&done[js]);
+                        if (ends_stage) umma_commit(&empty[is]);
                     }
                 }
                 __syncwarp();
-                if ((g & 1) || g == G - 1) {
+                if (ends_stage) {
                     if (++is == S::STAGES) { is = 0; ps ^= 1u; }
                 }
-                if (++ib == S::B_STAGES) { ib = 0; pb ^= 1u; }
-                if (++ic == NUM_ACC) { ic = 0; pc ^= 1u; }
+                if (++js == S::JS) { js = 0; pj ^= 1u; }
             }
         }
     mma_end:
@@ -406,48 +435,61 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         __syncwarp();
     } else if (warp < CONVERTER_WARP0 + CONVERTER_WARPS) {
         // ---------------------------------------------------------------- converters
-        constexpr int TPR = 128 / S::WR;           // threads per weight row (1 or 2)
+        constexpr int TPR = S::WR >= 128 ? 1 : 128 / S::WR;  // threads per weight row (1 or 2)
+        constexpr int RPT = S::WR > 128 ? S::WR / 128 : 1;   // weight rows per thread (1 or 2)
         constexpr int WORDS = S::W_ROW / 4;        // raw 32-bit words per row and group (8 or 16)
-        constexpr int WPT = WORDS / TPR;           // words per thread
-        constexpr int CPT = 8 / TPR;               // 16-byte f16 chunks written per thread
+        constexpr int WPT = WORDS / TPR;           // words per thread and row
+        constexpr int CPT = 8 / TPR;               // 16-byte f16 chunks written per thread and row
         const int ct = threadIdx.x - CONVERTER_WARP0 * 32;
-        const int row = ct / TPR, part = ct % TPR, swz = row & 7;
+        const int row0 = ct / TPR, part = ct % TPR, swz = row0 & 7;  // rows row0 + 128 i share the swizzle
         const uint32_t st_base = smem_u32(smem + S::OFF_STAGE), b_base = smem_u32(smem + S::OFF_B);
-        int is = 0, ib = 0;
-        uint32_t ps = 0, pb = 0;
+        int is = 0, js = 0;
+        uint32_t ps = 0, pj = 0;
         for (int tile = tile0; tile < tiles; tile += tstride) {
-            for (int g = 0; g < G; ++g) {
+            for (int g = 0; g < G; g += S::GPJ) {
+                const int ng = (S::GPJ == 2 && g + 1 < G) ? 2 : 1;
                 if (!(g & 1) &&
                     !warp_wait_backoff(PAIR ? &wfull[is] : &full[is], ps, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_CVT))
                     goto done;
-                if (!warp_wait_backoff(&b_empty[ib], pb ^ 1u, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_CVT)) goto done;
-                const uint32_t src = st_base + is * S::STAGE_BYTES + 2 * S::A_BYTES + row * (2 * S::W_ROW) +
-                                     (g & 1) * S::W_ROW + part * WPT * 4;
-                const uint32_t dst = b_base + ib * S::B_BYTES + row * 128;
-                uint32_t words[WPT];
+                // the job slot's previous job (JS jobs back) has been multiplied
+                if (!warp_wait_backoff(&done[js], pj ^ 1u, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_CVT)) goto done;
 #pragma unroll
-                for (int i = 0; i < WPT / 4; ++i) {
-                    const uint4 v = lds128(src + i * 16);
-                    words[4 * i] = v.x; words[4 * i + 1] = v.y; words[4 * i + 2] = v.z; words[4 * i + 3] = v.w;
-                }
+                for (int h = 0; h < S::GPJ; ++h) {
+                    if (h < ng) {
 #pragma unroll
-                for (int c = 0; c < CPT; ++c) {
-                    const int chunk = part * CPT + c;
-                    const uint4 h = BITS == 4 ? nibbles_to_f16(words[c]) : bytes_to_f16(words[2 * c], words[2 * c + 1]);
-                    sts128(dst + ((chunk ^ swz) << 4), h);
+                        for (int rr = 0; rr < RPT; ++rr) {
+                            const int row = row0 + rr * 128;
+                            const uint32_t src = st_base + is * S::STAGE_BYTES + 2 * S::A_BYTES + row * (2 * S::W_ROW) +
+                                                 ((g + h) & 1) * S::W_ROW + part * WPT * 4;
+                            const uint32_t dst = b_base + js * S::B_SLOT + h * S::BG_BYTES + row * 128;
+                            uint32_t words[WPT];
+#pragma unroll
+                            for (int i = 0; i < WPT / 4; ++i) {
+                                const uint4 v = lds128(src + i * 16);
+                                words[4 * i] = v.x; words[4 * i + 1] = v.y; words[4 * i + 2] = v.z; words[4 * i + 3] = v.w;
+                            }
+#pragma unroll
+                            for (int c = 0; c < CPT; ++c) {
+                                const int chunk = part * CPT + c;
+                                const uint4 hv =
+                                    BITS == 4 ? nibbles_to_f16(words[c]) : bytes_to_f16(words[2 * c], words[2 * c + 1]);
+                                sts128(dst + ((chunk ^ swz) << 4), hv);
+                            }
+                        }
+                    }
                 }
-                // generic writes of the B tile become MMA (async proxy) reads; the generic reads of
+                // generic writes of the B tiles become MMA (async proxy) reads; the generic reads of
                 // the raw codes are ordered before the stage's next TMA fill as well
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) {
-                    if (PAIR) mbar_arrive_cluster(at_leader(&b_full[ib]));
-                    else mbar_arrive(&b_full[ib]);
+                    if (PAIR) mbar_arrive_cluster(at_leader(&b_full[js]));
+                    else mbar_arrive(&b_full[js]);
                 }
-                if ((g & 1) || g == G - 1) {
+                if (((g + ng - 1) & 1) || g + ng - 1 == G - 1) {
                     if (++is == S::STAGES) { is = 0; ps ^= 1u; }
                 }
-                if (++ib == S::B_STAGES) { ib = 0; pb ^= 1u; }
+                if (++js == S::JS) { js = 0; pj ^= 1u; }
             }
         }
     }
@@ -455,34 +497,57 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         // ---------------------------------------------------------------- epilogue
         // warpgroups 2-3 take the registers the control warpgroups released
         asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REGS_EPILOGUE));
-        constexpr int COLS = S::COLS;  // columns per thread: 64 (BN 128) or 32 (BN 64)
+        constexpr int COLS = S::COLS;  // columns per thread: 128 (BN 256), 64 (BN 128) or 32 (BN 64)
+        constexpr int LDC = BN >= 256 ? 8 : 16;  // columns per TMEM load (fewer live registers at BN 256)
+        // TMEM loads per wait: a whole group's columns where the registers allow (not beside 128
+        // accumulators or the SwiGLU epilogue's pending values)
+        constexpr int LDN = (BN >= 256 || EPI == DB_EPI_SWIGLU_QUANT) ? 1 : COLS / LDC;
         const int ew = warp - EPILOGUE_WARP0;
         const int q = warp & 3;          // TMEM lane quadrant this warp may access
         const int half = ew >> 2;        // which half of the tile's columns
         const int r = q * 32 + lane;     // row inside the tile
         const int col0 = half * COLS;
         const uint32_t tlane = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)col0;
-        const uint32_t sc_base = smem_u32(smem + S::OFF_SC) + ew * SC_DEPTH * S::SC_SLOT;
+        const uint32_t sc_base = smem_u32(smem + S::OFF_SC) + ew * S::SC_DEPTH * S::SC_SLOT;
         const bool any_nonfinite = nonfinite != nullptr && *nonfinite != 0;
         float* xch = reinterpret_cast<float*>(smem + S::OFF_X);
+        // The SwiGLU epilogue has further bounded waits inside the job loop, after which a warp may
+        // leave on its own; a hardware barrier there could then wait for a warp that has left.
+        constexpr bool ONE_POLLER = EPI != DB_EPI_SWIGLU_QUANT;
+        volatile int* epi_go = reinterpret_cast<volatile int*>(smem + S::OFF_MISC + 8);
+        int jn = 0;
         // Scale vectors of one job (one group of one tile) go to the next ring slot: lanes 0-7
         // fetch the sa of this warp's 32 rows, lanes 8.. the sw of its COLS columns (16 bytes
         // each).  The prefetch cursor walks this CTA's jobs in order, SC_DEPTH jobs ahead.
+        // Chunk ch = lane (and lane + 32 where 8 + COLS / 4 > 32): 0-7 sa, 8.. sw.  Weight-scale
+        // chunks at or past the padded row length ldsw (columns past N in a 256-wide tile) are
+        // not fetched; their columns are never stored.
+        constexpr int PF_CHUNKS = 8 + COLS / 4;
         int pf_tile = tile0, pf_g = 0, pf_slot = 0;
-        const float* pf_src = nullptr;
+        const float* pf_src[2] = {nullptr, nullptr};
+        bool pf_on[2] = {false, false};
         auto pf_tile_start = [&]() {
             if (pf_tile < tiles) {
                 const int m0 = (pf_tile % m_tiles) * MT + row_off, n0 = (pf_tile / m_tiles) * BN;
-                pf_src = lane < 8 ? sa + m0 + q * 32 + lane * 4 : sw + n0 + col0 + (lane - 8) * 4;
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int ch = lane + 32 * h;
+                    const int n = n0 + col0 + (ch - 8) * 4;
+                    pf_src[h] = ch < 8 ? sa + m0 + q * 32 + ch * 4 : sw + n;
+                    pf_on[h] = ch < PF_CHUNKS && (ch < 8 || n < ldsw);
+                }
             }
         };
-        const int64_t pf_ld = lane < 8 ? ldsa : ldsw;
-        const bool pf_lane = lane < 8 + COLS / 4;
-        const uint32_t pf_dst = lane < 8 ? lane * 16 : 128 + (lane - 8) * 16;
+        const int64_t pf_ld[2] = {lane < 8 ? ldsa : ldsw, ldsw};
+        const uint32_t pf_dst[2] = {lane < 8 ? (uint32_t)lane * 16u : 128u + (uint32_t)(lane - 8) * 16u,
+                                    128u + (uint32_t)(lane + 24) * 16u};
         auto prefetch = [&]() {
             if (pf_tile < tiles) {
-                if (pf_lane) cp_async16(sc_base + pf_slot * S::SC_SLOT + pf_dst, pf_src);
-                pf_src += pf_ld;
+#pragma unroll
+                for (int h = 0; h < (PF_CHUNKS > 32 ? 2 : 1); ++h) {
+                    if (pf_on[h]) cp_async16(sc_base + pf_slot * S::SC_SLOT + pf_dst[h], pf_src[h]);
+                    pf_src[h] += pf_ld[h];
+                }
                 if (++pf_g == G) {
                     pf_g = 0;
                     pf_tile += tstride;
@@ -490,14 +555,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 }
             }
             cp_async_commit();
-            if (++pf_slot == SC_DEPTH) pf_slot = 0;
+            if (++pf_slot == S::SC_DEPTH) pf_slot = 0;
         };
         pf_tile_start();
-        for (int j = 0; j < SC_DEPTH; ++j) prefetch();
-        int ic = 0, slot_i = 0, ybuf = 0;
-        uint32_t pc = 0;
-        bool refill = false;  // the slot consumed by the previous job is free to refill
-        cp_async_wait<SC_DEPTH - 1>();
+        for (int j = 0; j < S::SC_DEPTH; ++j) prefetch();
+        int js = 0, slot_i = 0, ybuf = 0;
+        uint32_t pj = 0;
+        bool refill = false;  // the scale slot consumed by the previous group is free to refill
+        cp_async_wait<S::SC_DEPTH - 1>();
         __syncwarp();
         float s_a_next = lds_f32(sc_base + lane * 4);
         // ---- SwiGLU: a tile's finish (exchange, silu * up, row absmax, re-quantisation) is spread
@@ -565,42 +630,69 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             uint64_t acc[COLS / 2];
 #pragma unroll
             for (int j = 0; j < COLS / 2; ++j) acc[j] = 0ull;
-            for (int g = 0; g < G; ++g) {
-                // This job's scale vectors landed before its s_a was read (end of the previous
-                // iteration).  Refill the slot the previous job used: every lane has finished reading
-                // it (the __syncwarp that ended the previous iteration).
-                if (refill) prefetch();
-                refill = true;
-                const uint32_t slot = sc_base + slot_i * S::SC_SLOT;
-                const float s_a = s_a_next;
-                if (!warp_wait(&acc_full[ic], pc, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_EPI)) goto done;
+            for (int g = 0; g < G; g += S::GPJ) {
+                const int ng = (S::GPJ == 2 && g + 1 < G) ? 2 : 1;
+                if (ONE_POLLER) {
+                    // one warp polls the job's barrier; the other seven sleep in a hardware
+                    // barrier.  The decision goes through shared memory (two slots, alternating by
+                    // job) so that every epilogue warp leaves on the same job.
+                    if (ew == 0) {
+                        const bool ok = warp_wait(&done[js], pj, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_EPI);
+                        if (lane == 0) epi_go[jn & 1] = ok && !*abort_flag;
+                    }
+                    named_barrier_sync(1, 32 * EPILOGUE_WARPS);
+                    if (!epi_go[jn & 1]) goto done;
+                    ++jn;
+                } else if (!warp_wait(&done[js], pj, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_EPI)) {
+                    goto done;
+                }
                 tc_fence_after();
 #pragma unroll
-                for (int c = 0; c < COLS / 16; ++c) {
-                    uint32_t v[16];
-                    uint4 w[4];
-                    tmem_ld_32x32b_x16(tlane + (uint32_t)(ic * BN + c * 16), v);
+                for (int h = 0; h < S::GPJ; ++h) {
+                    if (h < ng) {
+                        // This group's scale vectors landed before its s_a was read (end of the
+                        // previous group).  Refill the slot the previous group used: every lane has
+                        // finished reading it (the __syncwarp that ended the previous group).
+                        if (refill) prefetch();
+                        refill = true;
+                        const uint32_t slot = sc_base + slot_i * S::SC_SLOT;
+                        const float s_a = s_a_next;
+                        const uint32_t tbuf = tlane + (uint32_t)((js * S::GPJ + h) * BN);
+                        // LDN TMEM loads in flight per wait; each chunk's weight scales are read
+                        // from shared memory just before its fold
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) w[i] = lds128(slot + 128 + c * 64 + i * 16);
-                    tmem_wait_ld(v);
-                    if (c == COLS / 16 - 1) {
-                        // every column of this group is in registers: release its TMEM buffer
-                        tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) {
-                            if (PAIR) mbar_arrive_cluster(at_leader(&acc_empty[ic]));
-                            else mbar_arrive(&acc_empty[ic]);
+                        for (int c = 0; c < COLS / LDC; c += LDN) {
+                            uint32_t v[LDN][LDC];
+#pragma unroll
+                            for (int u = 0; u < LDN; ++u) tmem_ld_32x32b(tbuf + (uint32_t)((c + u) * LDC), v[u]);
+#pragma unroll
+                            for (int u = 0; u < LDN; ++u) tmem_wait_ld(v[u]);
+                            if (h == ng - 1 && c + LDN == COLS / LDC) {
+                                // every accumulator of this job is in registers: release its buffers
+                                tc_fence_before();
+                                __syncwarp();
+                                if (lane == 0) {
+                                    if (PAIR) mbar_arrive_cluster(at_leader(&acc_empty[js]));
+                                    else mbar_arrive(&acc_empty[js]);
+                                }
+                            }
+#pragma unroll
+                            for (int u = 0; u < LDN; ++u) {
+                                uint4 w[LDC / 4];
+#pragma unroll
+                                for (int i = 0; i < LDC / 4; ++i) w[i] = lds128(slot + 128 + (c + u) * LDC * 4 + i * 16);
+                                fold_cols<FUSED, LDC>(&acc[(c + u) * LDC / 2], v[u], w, s_a);
+                            }
                         }
+                        if (++slot_i == S::SC_DEPTH) slot_i = 0;
+                        // the next group's scale vectors: its commit group is the oldest but SC_DEPTH - 2
+                        cp_async_wait<S::SC_DEPTH - 2>();
+                        __syncwarp();
+                        s_a_next = lds_f32(sc_base + slot_i * S::SC_SLOT + lane * 4);
+                        if (EPI == DB_EPI_SWIGLU_QUANT && pstep >= 0 && !swiglu_step()) goto done;
                     }
-                    fold16<FUSED>(&acc[c * 8], v, w, s_a);
                 }
-                if (++ic == NUM_ACC) { ic = 0; pc ^= 1u; }
-                if (++slot_i == SC_DEPTH) slot_i = 0;
-                // the next job's scale vectors: its commit group is the oldest but SC_DEPTH - 2
-                cp_async_wait<SC_DEPTH - 2>();
-                __syncwarp();
-                s_a_next = lds_f32(sc_base + slot_i * S::SC_SLOT + lane * 4);
-                if (EPI == DB_EPI_SWIGLU_QUANT && pstep >= 0 && !swiglu_step()) goto done;
+                if (++js == S::JS) { js = 0; pj ^= 1u; }
             }
             if (EPI == DB_EPI_SWIGLU_QUANT) {
                 // finish the previous tile if this one was too short to absorb it
@@ -639,11 +731,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 // a coalesced store (y = acc) or an in-L2 reduce-add (y = y + acc, round to nearest,
                 // so y is never read here).  Rows/columns past M/N are clipped by the TMA.
                 const float nanv = __int_as_float(0x7fc00000);
-                const uint32_t ystage = smem_u32(smem + S::OFF_Y) + ew * 2 * S::Y_CHUNK;
+                const uint32_t ystage = smem_u32(smem + S::OFF_Y) + ew * S::Y_BUFS * S::Y_CHUNK;
 #pragma unroll
                 for (int c = 0; c < COLS / 16; ++c) {
                     const uint32_t buf = ystage + ybuf * S::Y_CHUNK;
-                    if (lane == 0) bulk_wait_group_read<1>();  // this buffer's previous store has read it
+                    if (lane == 0) bulk_wait_group_read<S::Y_BUFS - 1>();  // this buffer's previous store has read it
                     __syncwarp();
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
@@ -660,7 +752,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         else tma_store_2d(&tmY, buf, n0 + col0 + c * 16, m0 + q * 32);
                         bulk_commit_group();
                     }
-                    ybuf ^= 1;
+                    if (++ybuf == S::Y_BUFS) ybuf = 0;
                 }
             } else if (m < M) {
                 float* dst = y + (size_t)m * ldy + n0 + col0;
@@ -704,8 +796,8 @@ done:
     if (PAIR) cluster_sync_all();
     if (warp == 1) {
         tc_fence_after();
-        if (PAIR) tmem_dealloc_pair(tmem_base, NUM_ACC * BN);
-        else tmem_dealloc(tmem_base, NUM_ACC * BN);
+        if (PAIR) tmem_dealloc_pair(tmem_base, S::BUFS * BN);
+        else tmem_dealloc(tmem_base, S::BUFS * BN);
     }
 }
 
@@ -813,7 +905,7 @@ int db_launch_gemm_tc(const DbGemmArgs& a, cudaStream_t stream) {
     const int G = (a.K + BK - 1) / BK, Kp = G * BK;
     int bn = a.block_n ? a.block_n : 128;
     if (a.epilogue == DB_EPI_SWIGLU_QUANT) bn = 128;
-    if (bn != 64 && bn != 128) return (int)cudaErrorInvalidValue;
+    if (bn != 64 && bn != 128 && bn != 256) return (int)cudaErrorInvalidValue;
     // CTA pairs (M = 256 MMAs) for 128-wide tiles when asked for and there are rows for both CTAs
     const bool pair = bn == 128 && a.M > BM && a.pair_ctas;
     if ((reinterpret_cast<uintptr_t>(a.a_codes) & 15) || (a.lda * 2) % 16 || a.lda < Kp ||
@@ -858,5 +950,6 @@ int db_launch_gemm_tc(const DbGemmArgs& a, cudaStream_t stream) {
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
     }
     if (bn == 64) return a.bits == 4 ? dispatch_epi<64, 4>(a, pair, tmA, tmW, tmY, y_tma, G, stream) : dispatch_epi<64, 8>(a, pair, tmA, tmW, tmY, y_tma, G, stream);
+    if (bn == 256) return a.bits == 4 ? dispatch_epi<256, 4>(a, pair, tmA, tmW, tmY, y_tma, G, stream) : dispatch_epi<256, 8>(a, pair, tmA, tmW, tmY, y_tma, G, stream);
     return a.bits == 4 ? dispatch_epi<128, 4>(a, pair, tmA, tmW, tmY, y_tma, G, stream) : dispatch_epi<128, 8>(a, pair, tmA, tmW, tmY, y_tma, G, stream);
 }

@@ -64,7 +64,7 @@ bool cache_lookup(const char* path, const std::string& key, db_gemm_config* out)
     db_gemm_config c{};
     bool found = false;
     while (f >> k >> c.block_n >> c.max_ctas >> c.pair_ctas)
-        if (k == key && (c.block_n == 0 || c.block_n == 64 || c.block_n == 128) && c.max_ctas >= 0 &&
+        if (k == key && (c.block_n == 0 || c.block_n == 64 || c.block_n == 128 || c.block_n == 256) && c.max_ctas >= 0 &&
             (c.pair_ctas == 0 || c.pair_ctas == 1)) {  // malformed entries are ignored
             *out = c;
             found = true;  // the last entry for a key wins
@@ -209,7 +209,10 @@ int db_tune_gemm_shape(int64_t M, int64_t N, int64_t K, int bits, int epilogue, 
         return db_cuda_status(rc, what);
     };
     std::vector<db_gemm_config> cands = {{128, 0, 0}};  // baseline first
-    if (!swiglu) cands.push_back({64, 0, 0});
+    if (!swiglu) {
+        cands.push_back({64, 0, 0});
+        cands.push_back({256, 0, 0});
+    }
     if (M > 128) cands.push_back({128, 0, 1});
     std::vector<uint8_t> want, got;
     int rc = run(cands[0]);

@@ -111,7 +111,7 @@ int db_gemm_g64(const void *a_codes, int layout, int64_t lda, const float *sa, c
  * (checkpoint.rs:279-294, 428-563 select among kernel variants; a candidate is accepted only when
  * its output is bitwise equal to the baseline's).  Every configuration computes the same
  * per-group fold in the same order, so all are bitwise equal by construction.
- *   block_n    output columns per tile: 0 (default 128), 64 or 128
+ *   block_n    output columns per tile: 0 (default 128), 64, 128 or 256 (not for SwiGLU)
  *   max_ctas   persistent grid cap: 0 = one CTA per SM
  *   pair_ctas  1 = clusters of two CTAs issue M = 256 MMAs (128-wide tiles, M > 128); 0 = off
  * No counterpart in the reference's CPU path (its tuner picks WGSL variants). */

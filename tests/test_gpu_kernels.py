@@ -186,7 +186,7 @@ def test_tensor_core_gemm_bit_exact(db, oracle, wb, ab, m, k, n):
     assert bits_equal(y, ref), f"max |d| = {np.max(np.abs(y - ref))}"
 
 
-TILE_CONFIGS = [(0, 0, 0), (64, 0, 0), (128, 0, 1), (128, 16, 0), (128, 7, 1), (64, 3, 0)]
+TILE_CONFIGS = [(0, 0, 0), (64, 0, 0), (128, 0, 1), (128, 16, 0), (128, 7, 1), (64, 3, 0), (256, 0, 0), (256, 5, 0)]
 
 
 @pytest.mark.parametrize("m,k,n", [(200, 1000, 300), (1024, 1024, 3072), (257, 130, 129), (384, 2048, 256)])
