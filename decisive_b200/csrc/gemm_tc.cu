@@ -383,14 +383,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 }
                 tc_fence_after();
                 if (lane == 0) {
+                    // MMAs that accumulate into the same TMEM buffer run one after another (~160
+                    // cycles each, whatever N); the job's groups use separate buffers, so their
+                    // K steps are interleaved and the two accumulation chains overlap
 #pragma unroll
-                    for (int h = 0; h < GPJ; ++h) {
-                        if (h < ng) {
-                            const uint32_t d = tmem_base + (uint32_t)((js * GPJ + h) * BN);
-                            const uint32_t a_addr = st_base + is * S::STAGE_BYTES + ((g + h) & 1) * S::A_BYTES;
-                            const uint32_t b_addr = b_base + js * S::B_SLOT + h * S::BG_BYTES;
+                    for (int kk = 0; kk < BK / 16; ++kk) {
 #pragma unroll
-                            for (int kk = 0; kk < BK / 16; ++kk) {
+                        for (int h = 0; h < GPJ; ++h) {
+                            if (h < ng) {
+                                const uint32_t d = tmem_base + (uint32_t)((js * GPJ + h) * BN);
+                                const uint32_t a_addr = st_base + is * S::STAGE_BYTES + ((g + h) & 1) * S::A_BYTES;
+                                const uint32_t b_addr = b_base + js * S::B_SLOT + h * S::BG_BYTES;
                                 if (PAIR) umma_f16_pair(d, sw128_desc(a_addr + kk * 32), sw128_desc(b_addr + kk * 32), IDESC, kk > 0);
                                 else umma_f16(d, sw128_desc(a_addr + kk * 32), sw128_desc(b_addr + kk * 32), IDESC, kk > 0);
                             }
