@@ -115,6 +115,43 @@ def gemm(a_codes, layout, sa, w_codes, sw, M, N, K, bits, fused=True, a_sums=Non
     return y
 
 
+def decima_quantize_weights(w, block: int = 32):
+    """decima::int8::Matrix::new (W8, decima/int8.rs:106-151): f32 [N, K] device tensor ->
+    (codes uint8 [N, Kp], scales f32 [ceil(K/block), scale_stride(N)])."""
+    import torch
+    N, K = w.shape
+    Kp = -(-K // GROUP) * GROUP
+    codes = torch.zeros((N, Kp), dtype=torch.uint8, device=w.device)
+    scales = torch.empty((-(-K // block), scale_stride(N)), dtype=torch.float32, device=w.device)
+    check(load().db_decima_quantize_weights(_ptr(w), N, K, block, _ptr(codes), _ptr(scales), _stream()))
+    return codes, scales
+
+
+def decima_quantize_activations(x, block: int = 32, layout: int = CODES_TC):
+    """The activation fill of decima Matrix::apply_with_rows: f32 [M, K] -> (codes, scales, nonfinite flag)."""
+    import torch
+    M, K = x.shape
+    Kp = -(-K // GROUP) * GROUP
+    dt = torch.float16 if layout == CODES_TC else torch.int8
+    codes = torch.zeros((M, Kp), dtype=dt, device=x.device)
+    scales = torch.empty((-(-K // block), scale_stride(M)), dtype=torch.float32, device=x.device)
+    flag = torch.zeros(1, dtype=torch.int32, device=x.device)
+    check(load().db_decima_quantize_activations(_ptr(x), M, K, block, _ptr(codes), layout, Kp, _ptr(scales),
+                                                scales.stride(0), _ptr(flag), _stream()))
+    return codes, scales, flag
+
+
+def decima_linear(x, w_codes, w_scales, N: int, block: int = 32, fused: bool = True, bias=None):
+    """decima Matrix::apply_with_rows, WeightsActivations mode: y [M, N] = W8A8 grouped GEMM + bias."""
+    import torch
+    M, K = x.shape
+    ws = torch.empty(load().db_decima_workspace_bytes(M, K, block), dtype=torch.uint8, device=x.device)
+    y = torch.empty((M, N), dtype=torch.float32, device=x.device)
+    check(load().db_decima_linear(_ptr(x), M, K, _ptr(w_codes), _ptr(w_scales), N, block, int(fused), _ptr(bias),
+                                  _ptr(y), _ptr(ws), _stream()))
+    return y
+
+
 EPILOGUE_STORE, EPILOGUE_RESIDUAL, EPILOGUE_SWIGLU = 0, 1, 2
 
 

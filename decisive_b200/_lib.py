@@ -58,6 +58,10 @@ SIGNATURES = [
     ("db_gemm_g64_config", _i32, [_vp, _i32, _i64, _vp, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _i32, _i32, _i32, _vp,
                                   _i64, _vp, _vp, _vp]),
     ("db_gemv_max_rows", _i32, []),
+    ("db_decima_quantize_weights", _i32, [_vp, _i64, _i64, _i32, _vp, _vp, _vp]),
+    ("db_decima_quantize_activations", _i32, [_vp, _i64, _i64, _i32, _vp, _i32, _i64, _vp, _i64, _vp, _vp]),
+    ("db_decima_workspace_bytes", _sz, [_i64, _i64, _i32]),
+    ("db_decima_linear", _i32, [_vp, _i64, _i64, _vp, _vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp]),
     ("db_gemm_tune", _i32, [_i64, _i64, _i64, _i32, _i32, C.c_char_p, _vp, C.c_char_p, _sz]),
     ("db_linear_workspace_bytes", _sz, [_i64, _i64]),
     ("db_linear_g64", _i32, [_vp, _i64, _i64, _vp, _vp, _i64, _i32, _i32, _i32, _vp, _vp, _vp]),

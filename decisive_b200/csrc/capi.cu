@@ -218,6 +218,91 @@ int db_linear_g64(const float* x, int64_t M, int64_t K, const uint8_t* w_codes, 
                        stream);
 }
 
+// ---- Decima int8 (decima/int8.rs): blocks of 32 or 64, round half away from zero of x / scale
+static inline bool decima_block_ok(int block) { return block == 16 || block == 32 || block == 64 || block == 128; }
+
+int db_decima_quantize_weights(const float* w, int64_t N, int64_t K, int block, uint8_t* codes, float* scales,
+                               void* stream) {
+    if (N <= 0 || K <= 0 || !decima_block_ok(block) || !w || !codes || !scales)
+        return db_fail(DB_ERR_INVALID_ARGUMENT, "INVALID_ARGUMENT",
+                       "INT8 block must be 16, 32, 64 or 128 and the shape positive");
+    const int64_t Kp = groups_of(K) * DB_GROUP, GS = (K + block - 1) / block, ldw = db_scale_stride(N);
+    int* bad = nullptr;
+    if (cudaMallocAsync(&bad, sizeof(int), S(stream)) != cudaSuccess) return db_cuda_status(1, "quantize alloc");
+    cudaMemsetAsync(bad, 0, sizeof(int), S(stream));
+    cudaMemsetAsync(scales, 0, (size_t)GS * ldw * sizeof(float), S(stream));  // padding columns: scale 0
+    int rc = db_launch_decima_quantize(w, K, (int)N, (int)K, block, codes, DB_CODES_NATURAL_I8, Kp, scales, ldw, 0,
+                                       bad, S(stream));
+    int h = 0;
+    cudaMemcpyAsync(&h, bad, sizeof(int), cudaMemcpyDeviceToHost, S(stream));
+    cudaFreeAsync(bad, S(stream));
+    int e = (int)cudaStreamSynchronize(S(stream));
+    if (rc) return db_cuda_status(rc, "decima quantize weights");
+    if (e) return db_cuda_status(e, "decima quantize weights");
+    if (h) return db_fail(DB_ERR_NONFINITE, "INVALID_WEIGHTS", "non-finite INT8 weights");
+    return DB_OK;
+}
+
+int db_decima_quantize_activations(const float* x, int64_t M, int64_t K, int block, void* codes, int layout,
+                                   int64_t ldc, float* scales, int64_t lds, int* nonfinite, void* stream) {
+    const int64_t Kp = groups_of(K) * DB_GROUP;
+    if (M < 0 || K <= 0 || !decima_block_ok(block) || ldc < Kp ||
+        (layout != DB_CODES_TC && layout != DB_CODES_NATURAL) || lds < M)
+        return db_fail(DB_ERR_INVALID_ARGUMENT, "INVALID_ARGUMENT", "decima quantize: bad shape or layout");
+    if (M == 0) return DB_OK;
+    return db_cuda_status(db_launch_decima_quantize(x, K, (int)M, (int)K, block, codes,
+                                                    layout == DB_CODES_TC ? DB_CODES_TC_F16 : DB_CODES_NATURAL_I8,
+                                                    ldc, scales, lds, 0, nonfinite, S(stream)),
+                          "decima quantize activations");
+}
+
+size_t db_decima_workspace_bytes(int64_t M, int64_t K, int block) {
+    if (M < 0 || K <= 0 || !decima_block_ok(block)) return 0;
+    const int64_t Kp = groups_of(K) * DB_GROUP, GS = (K + block - 1) / block;
+    auto up = [](size_t b) { return (b + 255) / 256 * 256; };
+    return up((size_t)M * Kp * 2) + up((size_t)GS * db_scale_stride(M) * 4) + 256;
+}
+
+int db_decima_linear(const float* x, int64_t M, int64_t K, const uint8_t* w_codes, const float* sw, int64_t N,
+                     int block, int fused, const float* bias, float* y, void* workspace, void* stream) {
+    if (M < 0 || K <= 0 || N <= 0 || !decima_block_ok(block) || !workspace || !w_codes || !sw || !y)
+        return db_fail(DB_ERR_INVALID_ARGUMENT, "INVALID_ARGUMENT", "decima linear: bad shape");
+    if (block != 32 && block != 64)
+        return db_fail(DB_ERR_UNSUPPORTED, "UNSUPPORTED", "decima linear: the GPU GEMM takes blocks of 32 or 64");
+    if (M == 0) return DB_OK;
+    const int64_t Kp = groups_of(K) * DB_GROUP, GS = (K + block - 1) / block, lds = db_scale_stride(M);
+    auto up = [](size_t b) { return (b + 255) / 256 * 256; };
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    void* codes = ws;
+    float* sa = reinterpret_cast<float*>(ws + up((size_t)M * Kp * 2));
+    int* flag = reinterpret_cast<int*>(ws + up((size_t)M * Kp * 2) + up((size_t)GS * lds * 4));
+    cudaMemsetAsync(flag, 0, sizeof(int), S(stream));
+    int rc = db_launch_decima_quantize(x, K, (int)M, (int)K, block, codes, DB_CODES_TC_F16, Kp, sa, lds, 0, flag,
+                                       S(stream));
+    if (rc) return db_cuda_status(rc, "decima quantize activations");
+    DbGemmArgs a{};
+    a.a_codes = codes;
+    a.lda = Kp;
+    a.sa = sa;
+    a.ldsa = lds;
+    a.w_codes = w_codes;
+    a.sw = sw;
+    a.M = (int)M;
+    a.N = (int)N;
+    a.K = (int)K;
+    a.bits = 8;
+    a.fused = fused;
+    a.epilogue = DB_EPI_STORE;
+    a.y = y;
+    a.ldy = N;
+    a.nonfinite = flag;  // a non-finite x gives all-NaN y (decima/int8.rs:186-190)
+    a.dev_error = db_device_error_ptr();
+    a.block = block;
+    a.bias = bias;
+    a.add_bias = 1;
+    return db_cuda_status(db_launch_gemm_tc(a, S(stream)), "decima gemm");
+}
+
 int db_project_packed(const float* x, int64_t K, const uint8_t* w_codes, const float* sw, int64_t outputs, int bits,
                       float* y, void* workspace, void* stream) {
     if (K <= 0 || K % DB_GROUP || outputs <= 0 || !workspace)

@@ -60,11 +60,11 @@ constexpr uint64_t DRAIN_NS = 100000000ull;  // wind-down wait for in-flight cop
 // per job ("done") tells both the converters (weight slot free) and the epilogue (accumulators
 // ready).  A phase of done[js] cannot be skipped by any waiter: the job JS later needs the same
 // weight slot and accumulator buffers, which those waiters release first.
-template <int BN, int BITS, int EPI, bool PAIR>
+template <int BN, int BITS, int EPI, bool PAIR, int SUB = 1>
 struct GemmSmem {
-    static constexpr int GPJ = BN <= 128 ? 2 : 1;          // K groups per job
+    static constexpr int GPJ = BN <= 128 ? 2 : 1;          // 64-wide K slabs per job
     static constexpr int BUFS = 512 / BN > 8 ? 8 : 512 / BN;  // TMEM accumulator buffers (BUFS x BN <= 512 columns)
-    static constexpr int JS = BUFS / GPJ;                   // job slots: 4 (BN 64), 2 (BN 128, 256)
+    static constexpr int JS = BUFS / (GPJ * SUB);           // job slots: 4 (BN 64), 2 (BN 128, 256; BN 64 with SUB 2)
     static constexpr int SC_DEPTH = BN >= 256 ? 3 : 6;      // groups of scale vectors each epilogue warp keeps in flight
     static constexpr int WR = PAIR ? BN / 2 : BN;          // weight rows held by this CTA
     static constexpr int A_BYTES = BM * BK * 2;            // one group of activation codes, 16 KB
@@ -232,15 +232,15 @@ __device__ __forceinline__ void swiglu_store8(const uint64_t (&pend)[16], float 
     *reinterpret_cast<uint4*>(dst + B) = *reinterpret_cast<uint4*>(hv);
 }
 
-template <int BN, int BITS, int EPI, bool FUSED, bool PAIR>
+template <int BN, int BITS, int EPI, bool FUSED, bool PAIR, int SUB>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                    const __grid_constant__ CUtensorMap tmY, int y_tma,
                    const float* __restrict__ sa, int64_t ldsa, const float* __restrict__ sw, int64_t ldsw, int M,
-                   int N, int G, float* __restrict__ y, int64_t ldy, __half* __restrict__ out_codes, int64_t ldoc,
+                   int N, int G, int GS, float* __restrict__ y, int64_t ldy, __half* __restrict__ out_codes, int64_t ldoc,
                    float* __restrict__ out_scales, int64_t ldos, const int* __restrict__ nonfinite,
-                   int* __restrict__ dev_error) {
-    using S = GemmSmem<BN, BITS, EPI, PAIR>;
+                   const float* __restrict__ bias, int add_bias, int* __restrict__ dev_error) {
+    using S = GemmSmem<BN, BITS, EPI, PAIR, SUB>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::OFF_BAR);
@@ -391,11 +391,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
                         for (int h = 0; h < GPJ; ++h) {
                             if (h < ng) {
-                                const uint32_t d = tmem_base + (uint32_t)((js * GPJ + h) * BN);
+                                // K steps 0..4/SUB-1 of a slab go to its first scale group's buffer
+                                constexpr int KPS = (BK / 16) / SUB;  // K steps per scale group
+                                const uint32_t d = tmem_base + (uint32_t)((((js * GPJ + h) * SUB) + kk / KPS) * BN);
                                 const uint32_t a_addr = st_base + is * S::STAGE_BYTES + ((g + h) & 1) * S::A_BYTES;
                                 const uint32_t b_addr = b_base + js * S::B_SLOT + h * S::BG_BYTES;
-                                if (PAIR) umma_f16_pair(d, sw128_desc(a_addr + kk * 32), sw128_desc(b_addr + kk * 32), IDESC, kk > 0);
-                                else umma_f16(d, sw128_desc(a_addr + kk * 32), sw128_desc(b_addr + kk * 32), IDESC, kk > 0);
+                                const uint32_t acc_in = (kk % KPS) > 0;
+                                if (PAIR) umma_f16_pair(d, sw128_desc(a_addr + kk * 32), sw128_desc(b_addr + kk * 32), IDESC, acc_in);
+                                else umma_f16(d, sw128_desc(a_addr + kk * 32), sw128_desc(b_addr + kk * 32), IDESC, acc_in);
                             }
                         }
                     }
@@ -551,7 +554,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     if (pf_on[h]) cp_async16(sc_base + pf_slot * S::SC_SLOT + pf_dst[h], pf_src[h]);
                     pf_src[h] += pf_ld[h];
                 }
-                if (++pf_g == G) {
+                if (++pf_g == GS) {
                     pf_g = 0;
                     pf_tile += tstride;
                     pf_tile_start();
@@ -651,8 +654,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 }
                 tc_fence_after();
 #pragma unroll
-                for (int h = 0; h < S::GPJ; ++h) {
-                    if (h < ng) {
+                for (int hs = 0; hs < S::GPJ * SUB; ++hs) {
+                    const int h = hs / SUB, gi = (g + h) * SUB + hs % SUB;  // slab, scale group
+                    if (h < ng && gi < GS) {
+                        // the job's last scale group (past K, the last slab may hold only one)
+                        const bool last = h == ng - 1 && (hs % SUB == SUB - 1 || gi + 1 == GS);
                         // This group's scale vectors landed before its s_a was read (end of the
                         // previous group).  Refill the slot the previous group used: every lane has
                         // finished reading it (the __syncwarp that ended the previous group).
@@ -660,7 +666,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         refill = true;
                         const uint32_t slot = sc_base + slot_i * S::SC_SLOT;
                         const float s_a = s_a_next;
-                        const uint32_t tbuf = tlane + (uint32_t)((js * S::GPJ + h) * BN);
+                        const uint32_t tbuf = tlane + (uint32_t)((js * S::GPJ * SUB + hs) * BN);
                         // LDN TMEM loads in flight per wait; each chunk's weight scales are read
                         // from shared memory just before its fold
 #pragma unroll
@@ -670,7 +676,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                             for (int u = 0; u < LDN; ++u) tmem_ld_32x32b(tbuf + (uint32_t)((c + u) * LDC), v[u]);
 #pragma unroll
                             for (int u = 0; u < LDN; ++u) tmem_wait_ld(v[u]);
-                            if (h == ng - 1 && c + LDN == COLS / LDC) {
+                            if (last && c + LDN == COLS / LDC) {
                                 // every accumulator of this job is in registers: release its buffers
                                 tc_fence_before();
                                 __syncwarp();
@@ -744,6 +750,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     for (int i = 0; i < 4; ++i) {
                         const uint64_t p0 = acc[c * 8 + 2 * i], p1 = acc[c * 8 + 2 * i + 1];
                         uint4 o = make_uint4((uint32_t)p0, (uint32_t)(p0 >> 32), (uint32_t)p1, (uint32_t)(p1 >> 32));
+                        if (add_bias) {
+                            // y = sum + bias[n] (or + 0), decima/int8.rs:492-496
+                            const int nb = n0 + col0 + c * 16 + 4 * i;
+                            o.x = __float_as_uint(__fadd_rn(__uint_as_float(o.x), bias && nb < N ? __ldg(bias + nb) : 0.f));
+                            o.y = __float_as_uint(__fadd_rn(__uint_as_float(o.y), bias && nb + 1 < N ? __ldg(bias + nb + 1) : 0.f));
+                            o.z = __float_as_uint(__fadd_rn(__uint_as_float(o.z), bias && nb + 2 < N ? __ldg(bias + nb + 2) : 0.f));
+                            o.w = __float_as_uint(__fadd_rn(__uint_as_float(o.w), bias && nb + 3 < N ? __ldg(bias + nb + 3) : 0.f));
+                        }
                         if (any_nonfinite) o = make_uint4(__float_as_uint(nanv), __float_as_uint(nanv),
                                                           __float_as_uint(nanv), __float_as_uint(nanv));
                         sts128(buf + lane * 64 + i * 16, o);
@@ -765,6 +779,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     for (int j = 0; j < COLS; j += 4) {
                         float4 o = make_float4(f2_lo(acc[j / 2]), f2_hi(acc[j / 2]), f2_lo(acc[j / 2 + 1]),
                                                f2_hi(acc[j / 2 + 1]));
+                        if (add_bias) {
+                            const int nb = n0 + col0 + j;
+                            o.x = __fadd_rn(o.x, bias ? __ldg(bias + nb) : 0.f);
+                            o.y = __fadd_rn(o.y, bias ? __ldg(bias + nb + 1) : 0.f);
+                            o.z = __fadd_rn(o.z, bias ? __ldg(bias + nb + 2) : 0.f);
+                            o.w = __fadd_rn(o.w, bias ? __ldg(bias + nb + 3) : 0.f);
+                        }
                         if (EPI == DB_EPI_RESIDUAL) {
                             const float4 rr = *reinterpret_cast<const float4*>(dst + j);
                             o.x = __fadd_rn(rr.x, o.x); o.y = __fadd_rn(rr.y, o.y);
@@ -778,6 +799,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     for (int j = 0; j < COLS; ++j) {
                         if (n0 + col0 + j < N) {
                             float o = (j & 1) ? f2_hi(acc[j / 2]) : f2_lo(acc[j / 2]);
+                            if (add_bias) o = __fadd_rn(o, bias ? __ldg(bias + n0 + col0 + j) : 0.f);
                             if (EPI == DB_EPI_RESIDUAL) o = __fadd_rn(dst[j], o);
                             dst[j] = any_nonfinite ? nanv : o;
                         }
@@ -836,11 +858,11 @@ int db_num_sms() {
     return sms;
 }
 
-template <int BN, int BITS, int EPI, bool FUSED, bool PAIR>
+template <int BN, int BITS, int EPI, bool FUSED, bool PAIR, int SUB>
 static int launch_variant(const DbGemmArgs& a, const CUtensorMap& tmA, const CUtensorMap& tmW,
                           const CUtensorMap& tmY, int y_tma, int G, cudaStream_t stream) {
-    using S = GemmSmem<BN, BITS, EPI, PAIR>;
-    auto kernel = gemm_tc_kernel<BN, BITS, EPI, FUSED, PAIR>;
+    using S = GemmSmem<BN, BITS, EPI, PAIR, SUB>;
+    auto kernel = gemm_tc_kernel<BN, BITS, EPI, FUSED, PAIR, SUB>;
     static bool configured = false;
     if (!configured) {
         cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S::BYTES);
@@ -865,10 +887,11 @@ static int launch_variant(const DbGemmArgs& a, const CUtensorMap& tmA, const CUt
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    const int GS = (a.K + 64 / SUB - 1) / (64 / SUB);  // scale groups (blocks of 64 / SUB)
     const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, tmA, tmW, tmY, y_tma, a.sa, a.ldsa, a.sw,
-                                             (int64_t)db_scale_stride(a.N), a.M, a.N, G, a.y, a.ldy,
+                                             (int64_t)db_scale_stride(a.N), a.M, a.N, G, GS, a.y, a.ldy,
                                              static_cast<__half*>(a.out_codes), a.ldoc, a.out_scales, a.ldos,
-                                             a.nonfinite, a.dev_error);
+                                             a.nonfinite, a.bias, a.add_bias, a.dev_error);
     return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }
 
@@ -876,9 +899,14 @@ template <int BN, int BITS, int EPI, bool FUSED>
 static int launch_pairing(const DbGemmArgs& a, bool pair, const CUtensorMap& tmA, const CUtensorMap& tmW,
                           const CUtensorMap& tmY, int y_tma, int G, cudaStream_t s) {
     if constexpr (BN == 128) {
-        if (pair) return launch_variant<BN, BITS, EPI, FUSED, true>(a, tmA, tmW, tmY, y_tma, G, s);
+        if (pair) return launch_variant<BN, BITS, EPI, FUSED, true, 1>(a, tmA, tmW, tmY, y_tma, G, s);
     }
-    return launch_variant<BN, BITS, EPI, FUSED, false>(a, tmA, tmW, tmY, y_tma, G, s);
+    if constexpr (BN == 64 && BITS == 8 && EPI != DB_EPI_SWIGLU_QUANT) {
+        // scale blocks of 32 (Decima int8): two scale groups per 64-wide K slab, 64-wide tiles only
+        if (a.block == 32) return launch_variant<BN, BITS, EPI, FUSED, false, 2>(a, tmA, tmW, tmY, y_tma, G, s);
+    }
+    if (a.block == 32) return (int)cudaErrorInvalidValue;
+    return launch_variant<BN, BITS, EPI, FUSED, false, 1>(a, tmA, tmW, tmY, y_tma, G, s);
 }
 
 template <int BN, int BITS>
@@ -908,6 +936,8 @@ int db_launch_gemm_tc(const DbGemmArgs& a, cudaStream_t stream) {
     const int G = (a.K + BK - 1) / BK, Kp = G * BK;
     int bn = a.block_n ? a.block_n : 128;
     if (a.epilogue == DB_EPI_SWIGLU_QUANT) bn = 128;
+    if (a.block != 0 && a.block != 64 && a.block != 32) return (int)cudaErrorInvalidValue;
+    if (a.block == 32) bn = 64;  // scale blocks of 32 need eight TMEM buffers of 64 columns
     if (bn != 64 && bn != 128 && bn != 256) return (int)cudaErrorInvalidValue;
     // CTA pairs (M = 256 MMAs) for 128-wide tiles when asked for and there are rows for both CTAs
     const bool pair = bn == 128 && a.M > BM && a.pair_ctas;

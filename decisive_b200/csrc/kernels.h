@@ -17,6 +17,12 @@ enum { DB_EPI_STORE = 0, DB_EPI_RESIDUAL = 1, DB_EPI_SWIGLU_QUANT = 2 };
 int db_launch_quantize_rows(const void* x, int dtype, int64_t ldx, int M, int K, int bits, void* codes, int layout,
                             int64_t ldc, float* scales, int32_t* sums, int64_t lds, int* nonfinite,
                             cudaStream_t stream);
+// Decima int8 quantiser (blocks of 16/32/64/128, round half away from zero of x / scale).  Weights
+// use it with layout DB_CODES_NATURAL_I8 into the Q8 device layout and group-major scales
+// [G, lds]; activations with DB_CODES_TC_F16.  row_major_scales = 1 writes scales [M, lds].
+int db_launch_decima_quantize(const float* x, int64_t ldx, int M, int K, int block, void* codes, int layout,
+                              int64_t ldc, float* scales, int64_t lds, int row_major_scales, int* nonfinite,
+                              cudaStream_t stream);
 int db_launch_pack_weights(const uint16_t* w, int N, int K, int bits, uint8_t* codes, float* scales, int* bad,
                            cudaStream_t stream);
 int db_launch_dequant_rows(const uint8_t* codes, const float* scales, int N, int K, int bits, const int32_t* ids,
@@ -55,6 +61,9 @@ struct DbGemmArgs {
     int block_n;           // tile width (0 = default)
     int max_ctas;          // persistent grid cap (0 = number of SMs)
     int pair_ctas;         // 1 = CTA pairs with M = 256 MMAs (used for 128-wide tiles when M > 128)
+    int block;             // K values per scale group: 0 or 64 (group 64), 32 (Decima int8 blocks, Q8 only)
+    const float* bias;     // add_bias = 1: y = acc + bias[n] (bias == nullptr: y = acc + 0)
+    int add_bias;
 };
 int db_launch_gemm_tc(const DbGemmArgs& args, cudaStream_t stream);
 

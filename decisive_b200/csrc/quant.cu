@@ -162,11 +162,74 @@ __global__ void codes_to_natural_kernel(const void* __restrict__ codes, int layo
         out[i] = static_cast<const int8_t*>(codes)[(size_t)m * ldc + p];
 }
 
+// Decima int8 quantiser (decima/int8.rs:413-418, used for weights by Matrix::new :106-151 and for
+// activations by the per-row fill :239-253): blocks of `block` values (16/32/64/128, the last one
+// partial), scale = max(max|x| / 127, MIN_POSITIVE), code = round-half-away-from-zero(x / scale)
+// with a correctly rounded division, clamped to +-127.  One warp per (row, block).  Codes of the
+// row's padding up to Kp = ceil(K/64)*64 are written as 0 by the warp of the last block.
+// out_layout: DB_CODES_TC_F16 (f16 codes, tensor-core order) or DB_CODES_NATURAL_I8 (int8).
+__global__ void decima_quantize_rows_kernel(const float* __restrict__ x, int64_t ldx, int M, int K, int block,
+                                            void* __restrict__ codes, int layout, int64_t ldc,
+                                            float* __restrict__ scales, int64_t lds, bool row_major_scales,
+                                            int* __restrict__ nonfinite) {
+    const int G = (K + block - 1) / block, Kp = (K + DB_GROUP - 1) / DB_GROUP * DB_GROUP;
+    const int64_t warp = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (warp >= (int64_t)M * G) return;
+    const int m = (int)(warp / G), g = (int)(warp % G);
+    const int k0 = g * block, per = (block + 31) / 32;  // values per lane (1..4)
+    float v[4];
+    float amax = 0.f;
+    bool bad = false;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int k = k0 + lane + 32 * i;
+        v[i] = (i < per && lane + 32 * i < block && k < K) ? x[(size_t)m * ldx + k] : 0.f;
+        bad |= !isfinite(v[i]);
+        amax = fmaxf(amax, fabsf(v[i]));
+    }
+    if (__any_sync(0xffffffffu, bad) && lane == 0 && nonfinite) atomicOr(nonfinite, 1);
+    amax = warp_max(amax);
+    const float scale = fmaxf(__fdiv_rn(amax, 127.f), FLT_MIN);
+    auto put = [&](int k, float c) {
+        if (layout == DB_CODES_TC_F16)
+            static_cast<__half*>(codes)[(size_t)m * ldc + code_position(layout, k)] = __float2half_rn(c);
+        else
+            static_cast<int8_t*>(codes)[(size_t)m * ldc + k] = (int8_t)(int)c;
+    };
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int k = k0 + lane + 32 * i;
+        if (i < per && lane + 32 * i < block && k < Kp) {
+            const float c = k < K ? fminf(fmaxf(roundf(__fdiv_rn(v[i], scale)), -127.f), 127.f) : 0.f;
+            put(k, c);
+        }
+    }
+    if (g == G - 1)
+        for (int k = G * block + lane; k < Kp; k += 32) put(k, 0.f);
+    if (lane == 0) {
+        if (row_major_scales) scales[(size_t)m * lds + g] = scale;
+        else scales[(size_t)g * lds + m] = scale;
+    }
+}
+
 }  // namespace db
 
 using namespace db;
 
 static inline unsigned blocks_for(int64_t n, int per) { return (unsigned)((n + per - 1) / per); }
+
+int db_launch_decima_quantize(const float* x, int64_t ldx, int M, int K, int block, void* codes, int layout,
+                              int64_t ldc, float* scales, int64_t lds, int row_major_scales, int* nonfinite,
+                              cudaStream_t stream) {
+    if (M <= 0 || K <= 0) return 0;
+    if (block != 16 && block != 32 && block != 64 && block != 128) return (int)cudaErrorInvalidValue;
+    const int64_t warps = (int64_t)M * ((K + block - 1) / block);
+    decima_quantize_rows_kernel<<<blocks_for(warps, 8), 256, 0, stream>>>(x, ldx, M, K, block, codes, layout, ldc,
+                                                                            scales, lds, row_major_scales != 0,
+                                                                            nonfinite);
+    return (int)cudaGetLastError();
+}
 
 int db_launch_quantize_rows(const void* x, int dtype, int64_t ldx, int M, int K, int bits, void* codes, int layout,
                             int64_t ldc, float* scales, int32_t* sums, int64_t lds, int* nonfinite,

@@ -168,6 +168,29 @@ int db_linear_g64_noalloc(const float *x, int64_t M, int64_t K, const uint8_t *w
 int db_project_packed(const float *x, int64_t K, const uint8_t *w_codes, const float *sw, int64_t outputs,
                       int bits, float *y, void *workspace, void *stream);
 
+/* ---- Decima int8 (C4 scheme, src/models/decima/int8.rs): weights and activations quantised in
+ * blocks of 16/32/64/128 values, scale = max(max|x| / 127, FLT_MIN), code = round-half-away-from-
+ * zero(x / scale) with a correctly rounded division, clamped to +-127 (int8.rs:413-418).
+ *
+ * Weights: Matrix::new (int8.rs:106-151) from f32 [N, K] (row-major, [output, input]) into the Q8
+ * device layout codes [N, Kp] and group-major scales [ceil(K/block), db_scale_row_stride(N)];
+ * DB_ERR_NONFINITE for a non-finite weight (the reference rejects them). */
+int db_decima_quantize_weights(const float *w, int64_t N, int64_t K, int block, uint8_t *codes, float *scales,
+                               void *stream);
+/* The activation fill of Matrix::apply_with_rows (int8.rs:239-253, pack_x86.rs:4-56): f32 [M, K]
+ * -> codes (DB_CODES_TC f16 or DB_CODES_NATURAL int8, [M, ldc], ldc >= Kp) and scales
+ * [ceil(K/block), lds]; *nonfinite is set for a non-finite x. */
+int db_decima_quantize_activations(const float *x, int64_t M, int64_t K, int block, void *codes, int layout,
+                                   int64_t ldc, float *scales, int64_t lds, int *nonfinite, void *stream);
+/* Matrix::apply_with_rows in WeightsActivations mode (W8A8): quantise x, grouped GEMM in blocks of
+ * 32 or 64 (16 and 128 give DB_ERR_UNSUPPORTED), y [M, N] = sum + bias[n] (bias NULL: + 0).
+ * fused = 1 follows the AVX2 order sums = fma(float(dot), sw*sa, sums) (int8.rs:459-498), 0 the
+ * portable sum += float(dot) * (sw*sa) (int8.rs:380-420).  A non-finite x gives all-NaN y.
+ * workspace: device bytes from db_decima_workspace_bytes(M, K, block). */
+size_t db_decima_workspace_bytes(int64_t M, int64_t K, int block);
+int db_decima_linear(const float *x, int64_t M, int64_t K, const uint8_t *w_codes, const float *sw, int64_t N,
+                     int block, int fused, const float *bias, float *y, void *workspace, void *stream);
+
 /* Fused gate/up projection + SiLU(gate)*up + group-64 re-quantisation, the semantics of the
  * reference's fused q4_mlp (grouped_q4_mlp.wgsl:1-105) == apply_pair + silu_mul + prepare
  * (backbone.rs:229-236, cpu.rs:348-371, int8.rs:178-202).  w_gu: 2*F rows in blocks of

@@ -912,6 +912,76 @@ int oracle_encoder_forward(void *p, const int32_t *ids, size_t T, int layers_lim
     return 0;
 }
 
+/* ---------------------------------------------------------------- Decima int8 */
+
+/* decima/int8.rs:413-415: (max over |x| starting at 0) / 127, at least f32::MIN_POSITIVE. */
+float oracle_decima_scale(const float *x, size_t n) {
+    float m = 0.f;
+    for (size_t i = 0; i < n; ++i) {
+        const float a = fabsf(x[i]);
+        m = a > m ? a : m;  /* Rust f32::max; inputs are finite here */
+    }
+    const float s = m / 127.f;
+    return s > FLT_MIN ? s : FLT_MIN;
+}
+
+/* decima/int8.rs:416-418: (x / s).round() -- half away from zero -- clamped to [-127, 127]. */
+int8_t oracle_decima_quantize(float x, float scale) {
+    float q = roundf(x / scale);
+    if (q < -127.f) q = -127.f;
+    if (q > 127.f) q = 127.f;
+    return (int8_t)q;
+}
+
+/* decima/int8.rs:106-151 (Matrix::new) and :239-253 (the activation fill): each row in blocks,
+ * the last block partial; codes past cols stay 0. */
+void oracle_decima_quantize_rows(const float *x, size_t rows, size_t cols, size_t block, int8_t *codes,
+                                 float *scales) {
+    const size_t groups = (cols + block - 1) / block;
+    for (size_t r = 0; r < rows; ++r) {
+        int8_t *row = codes + r * groups * block;
+        memset(row, 0, groups * block);
+        for (size_t g = 0; g < groups; ++g) {
+            const size_t s0 = g * block, len = (s0 + block < cols ? s0 + block : cols) - s0;
+            const float *v = x + r * cols + s0;
+            const float sc = oracle_decima_scale(v, len);
+            scales[r * groups + g] = sc;
+            for (size_t k = 0; k < len; ++k) row[s0 + k] = oracle_decima_quantize(v[k], sc);
+        }
+    }
+}
+
+void oracle_decima_apply_w8a8(const int8_t *w_codes, const float *w_scales, size_t rows, size_t cols,
+                              size_t block, const float *x, size_t m, const float *bias, int mode, float *y) {
+    const size_t groups = (cols + block - 1) / block;
+    for (size_t i = 0; i < m * cols; ++i)
+        if (!isfinite(x[i])) {
+            for (size_t j = 0; j < m * rows; ++j) y[j] = NAN;
+            return;
+        }
+    int8_t *a = malloc(m * groups * block);
+    float *sa = malloc(m * groups * sizeof(float));
+    oracle_decima_quantize_rows(x, m, cols, block, a, sa);
+#pragma omp parallel for schedule(static)
+    for (long long i = 0; i < (long long)m; ++i) {
+        for (size_t n = 0; n < rows; ++n) {
+            float sum = 0.f;
+            for (size_t g = 0; g < groups; ++g) {
+                const int8_t *qa = a + ((size_t)i * groups + g) * block;
+                const int8_t *qw = w_codes + (n * groups + g) * block;
+                int32_t dot = 0;
+                for (size_t k = 0; k < block; ++k) dot += (int32_t)qa[k] * (int32_t)qw[k];
+                const float s = w_scales[n * groups + g] * sa[(size_t)i * groups + g];
+                if (mode == 0) sum = fmaf((float)dot, s, sum);
+                else sum = sum + (float)dot * s;
+            }
+            y[(size_t)i * rows + n] = sum + (bias ? bias[n] : 0.f);
+        }
+    }
+    free(a);
+    free(sa);
+}
+
 int oracle_num_threads(void) {
 #ifdef _OPENMP
     return omp_get_max_threads();

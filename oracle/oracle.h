@@ -116,6 +116,21 @@ void oracle_encoder_destroy(void *enc);
 int oracle_encoder_forward(void *enc, const int32_t *ids, size_t tokens, int layers_limit,
                            int mode, float *pooled, float *hidden_out);
 
+/* ---- Decima int8 (src/models/decima/int8.rs): blocks of 16/32/64/128, scale = max|x|/127
+ * (min f32::MIN_POSITIVE), code = round-half-away(x / scale) clamped to +-127 (true division).
+ * Codes are row-major [rows, groups*block] with zeros past cols; scales [rows, groups]. */
+float oracle_decima_scale(const float *x, size_t n);
+int8_t oracle_decima_quantize(float x, float scale);
+/* Matrix::new quantiser for weights and the per-row activation packer (int8.rs:106-151, 239-253). */
+void oracle_decima_quantize_rows(const float *x, size_t rows, size_t cols, size_t block, int8_t *codes,
+                                 float *scales);
+/* Matrix::apply_with_rows in WeightsActivations mode: quantise x, then per output
+ * mode 0 (AVX2, int8.rs:459-498): sums = fma(float(dot_g), sw*sa, sums) over ascending g;
+ * mode 1 (portable, int8.rs:380-420): sum += float(dot_g) * (sw*sa);
+ * then y = sum + (bias ? bias[n] : 0).  A non-finite x gives all-NaN y (int8.rs:186-190). */
+void oracle_decima_apply_w8a8(const int8_t *w_codes, const float *w_scales, size_t rows, size_t cols,
+                              size_t block, const float *x, size_t m, const float *bias, int mode, float *y);
+
 int oracle_num_threads(void);
 void oracle_set_threads(int n);
 int oracle_has_avx2(void);

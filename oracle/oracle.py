@@ -87,6 +87,12 @@ def _declare(l):
     l.oracle_encoder_destroy.argtypes = [C.c_void_p]
     l.oracle_encoder_forward.restype = C.c_int
     l.oracle_encoder_forward.argtypes = [C.c_void_p, _i32, _sz, C.c_int, C.c_int, _f, _f]
+    l.oracle_decima_scale.restype = C.c_float
+    l.oracle_decima_scale.argtypes = [_f, _sz]
+    l.oracle_decima_quantize.restype = C.c_int8
+    l.oracle_decima_quantize.argtypes = [C.c_float, C.c_float]
+    l.oracle_decima_quantize_rows.argtypes = [_f, _sz, _sz, _sz, _i8, _f]
+    l.oracle_decima_apply_w8a8.argtypes = [_i8, _f, _sz, _sz, _sz, _f, _sz, _f, C.c_int, _f]
     l.oracle_num_threads.restype = C.c_int
     l.oracle_set_threads.argtypes = [C.c_int]
     l.oracle_has_avx2.restype = C.c_int
@@ -418,3 +424,35 @@ def num_threads() -> int:
 
 def set_threads(n: int) -> None:
     lib().oracle_set_threads(n)
+
+
+# ------------------------------------------------------------------ Decima int8 (decima/int8.rs)
+def decima_quantize_rows(x, block: int):
+    """[rows, cols] f32 -> (codes int8 [rows, groups*block], scales f32 [rows, groups])."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    rows, cols = x.shape
+    groups = -(-cols // block)
+    codes = np.zeros((rows, groups * block), np.int8)
+    scales = np.zeros((rows, groups), np.float32)
+    lib().oracle_decima_quantize_rows(_p(x, _f), rows, cols, block, _p(codes, _i8), _p(scales, _f))
+    return codes, scales
+
+
+class DecimaMatrix:
+    """decima::int8::Matrix in WeightsActivations mode (W8A8), weights f32 [rows, cols]."""
+
+    def __init__(self, weights, block: int):
+        w = np.ascontiguousarray(weights, dtype=np.float32)
+        if block not in (16, 32, 64, 128) or not np.all(np.isfinite(w)):
+            raise ValueError("INT8 block must be 16, 32, 64 or 128 and weights finite")
+        self.rows, self.cols = w.shape
+        self.block = block
+        self.codes, self.scales = decima_quantize_rows(w, block)
+
+    def apply(self, x, bias=None, mode: int = 0):
+        x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, self.cols)
+        y = np.zeros((x.shape[0], self.rows), np.float32)
+        b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+        lib().oracle_decima_apply_w8a8(_p(self.codes, _i8), _p(self.scales, _f), self.rows, self.cols,
+                                       self.block, _p(x, _f), x.shape[0], _p(b, _f), mode, _p(y, _f))
+        return y
