@@ -411,6 +411,49 @@ def run_gemv(args, local_rank):
                       "cases": results}), flush=True)
 
 
+def run_decima(args, local_rank):
+    """Decima int8 (C4 scheme: W8A8, blocks of 32, round-half-away division, bias) projections of a
+    C4-shaped layer (D=768, FF=3072) on one request's tokens (8 sequences x 416 = 3328 rows):
+    quantise + grouped GEMM + bias through db_decima_linear, device-timed, L2 flushed before every
+    launch.  Reports microseconds and TFLOP/s per projection and the layer's linear time."""
+    import torch
+
+    import decisive_b200 as db
+    torch.cuda.set_device(local_rank)
+    m, d, ff, block = 3328, 768, 3072, 32
+    shapes = [("qkv", d, 3 * d), ("o", d, d), ("ffn_in", d, ff), ("ffn_out", ff, d)]
+    flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device="cuda")
+    peak_tf, _, kind = measured_peaks()
+    cases, total_us = [], 0.0
+    for name, k, n in shapes:
+        rng = np.random.default_rng(k * 3 + n)
+        w = torch.from_numpy(rng.normal(0, 0.02, (n, k)).astype(np.float32)).cuda()
+        codes, scales = db.decima_quantize_weights(w, block)
+        x = torch.from_numpy(rng.normal(0, 1, (m, k)).astype(np.float32)).cuda()
+        bias = torch.from_numpy(rng.normal(0, 0.1, n).astype(np.float32)).cuda()
+        for _ in range(args.warmup):
+            db.decima_linear(x, codes, scales, n, block, True, bias)
+        torch.cuda.synchronize()
+        times = []
+        for _ in range(args.steps):
+            flush.zero_()
+            torch.cuda._sleep(200_000)
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            db.decima_linear(x, codes, scales, n, block, True, bias)
+            e.record()
+            torch.cuda.synchronize()
+            times.append(s.elapsed_time(e))
+        us = float(np.median(times)) * 1e3
+        total_us += us
+        tf = 2.0 * m * n * k / us / 1e6
+        cases.append({"projection": name, "M": m, "K": k, "N": n, "us": us, "tflops": tf, "frac_of_bf16_peak": tf / peak_tf})
+    print(json.dumps({"workload": f"decima W8A8 block {block} C4-shaped layer projections (quantise + GEMM + bias)",
+                      "tokens": m, "layer_linear_us": total_us, "linear_tokens_per_s_per_layer": m / total_us * 1e6,
+                      "peak_kind": kind, "l2": "flushed before every launch", "launches_per_case": args.steps,
+                      "cases": cases}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -420,7 +463,7 @@ def main():
     ap.add_argument("--cpu-layers", type=int, default=2)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-tune", action="store_true", help="skip kernel selection (default tile configurations)")
-    ap.add_argument("--workload", default="encoder", choices=["encoder", "gemm", "gemv"])
+    ap.add_argument("--workload", default="encoder", choices=["encoder", "gemm", "gemv", "decima"])
     ap.add_argument("--gemv-rows", default="1,4,8", help="activation rows (M) for --workload gemv")
     ap.add_argument("--gemm-shape", default="1024,1024,3072", help="M,K,N for --workload gemm")
     ap.add_argument("--bits", type=int, default=4)
@@ -432,6 +475,8 @@ def main():
         run_gemm(args, local_rank)
     elif args.workload == "gemv":
         run_gemv(args, local_rank)
+    elif args.workload == "decima":
+        run_decima(args, local_rank)
     elif args.impl == "reference":
         run_reference(args, rank)
     else:

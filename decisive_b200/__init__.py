@@ -474,6 +474,25 @@ class Model:
                                            int(reset)))
         return {load().db_model_profile_name(k).decode(): (float(ms[k]), int(cnt[k])) for k in range(n)}
 
+    @classmethod
+    def from_packed(cls, config: EncoderConfig, manifest_path: str, verify: bool = True, device: int = 0) -> "Model":
+        """Loads a packed checkpoint directory (packed-q4-e4.json / packed-q8-e8.json manifest, the
+        reference's export_packed.rs format); verify checks every file's SHA-256."""
+        err = _lib.DbError()
+        cfg = config.c()
+        h = load().db_model_create_packed(device, C.byref(cfg), manifest_path.encode(), int(verify), C.byref(err))
+        if not h:
+            raise Error._from(err)
+        return cls(h, config)
+
+    def export_packed(self, directory: str) -> str:
+        """Writes this model's weights as a packed checkpoint into directory; returns the manifest path."""
+        import os
+        err = _lib.DbError()
+        if load().db_model_export_packed(self._h, directory.encode(), C.byref(err)):
+            raise Error._from(err)
+        return os.path.join(directory, f"packed-q{self.config.weight_bits}-e{self.config.weight_bits}.json")
+
     def tune(self, tokens: int | None = None, cache_path: str | None = None) -> dict:
         """Tunes the four projection GEMMs at `tokens` rows (default: max_sequence_tokens) and uses
         the choices from then on; returns the per-projection reports."""

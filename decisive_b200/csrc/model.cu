@@ -26,6 +26,7 @@
 #include "common.cuh"
 #include "kernels.h"
 #include "layer_ops.h"
+#include "packed_io.h"
 
 namespace {
 
@@ -428,6 +429,143 @@ int predict_one(db_model* m, const int32_t* ids, size_t n, const db_parameters* 
 
 }  // namespace
 
+namespace {
+
+// ---- packed checkpoints (the reference's export_packed.rs:13-103 manifest and file layout)
+const char* kLayerTensors[11] = {"self_attn.q_proj.weight",  "self_attn.k_proj.weight", "self_attn.v_proj.weight",
+                                 "self_attn.o_proj.weight",  "mlp.gate_proj.weight",    "mlp.up_proj.weight",
+                                 "mlp.down_proj.weight",     "input_layernorm.weight",  "post_attention_layernorm.weight",
+                                 "self_attn.q_norm.weight",  "self_attn.k_norm.weight"};
+
+inline size_t group_bytes(int bits) { return bits == 4 ? 36 : 68; }  // packed.rs:10-20
+inline uint16_t f32_to_bf16_rne(float f) {
+    uint32_t u;
+    std::memcpy(&u, &f, 4);
+    if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((u >> 16) | 0x40);  // quiet NaN
+    return (uint16_t)((u + 0x7fffu + ((u >> 16) & 1u)) >> 16);
+}
+inline float bf16_to_f32(uint16_t b) {
+    const uint32_t u = (uint32_t)b << 16;
+    float f;
+    std::memcpy(&f, &u, 4);
+    return f;
+}
+
+// device layout [N, K] -> packed row-group bytes on the host
+int export_matrix(db_model* m, const uint8_t* codes, const float* scales, int N, int K, uint8_t* dev_stage,
+                  std::vector<uint8_t>* out) {
+    const size_t bytes = (size_t)N * (K / 64) * group_bytes(m->cfg.weight_bits);
+    int rc = db_export_packed(codes, scales, N, K, m->cfg.weight_bits, dev_stage, m->stream);
+    out->resize(bytes);
+    if (!rc) rc = db_cuda_status(cudaMemcpyAsync(out->data(), dev_stage, bytes, cudaMemcpyDeviceToHost, m->stream),
+                                 "export copy");
+    if (!rc) rc = db_cuda_status(cudaStreamSynchronize(m->stream), "export");
+    return rc;
+}
+std::vector<uint8_t> norm_bytes(const float* dev, int n) {
+    std::vector<float> h(n);
+    cudaMemcpy(h.data(), dev, n * 4, cudaMemcpyDeviceToHost);
+    std::vector<uint8_t> b(2 * n);
+    for (int i = 0; i < n; ++i) {
+        const uint16_t v = f32_to_bf16_rne(h[i]);
+        b[2 * i] = (uint8_t)v;
+        b[2 * i + 1] = (uint8_t)(v >> 8);
+    }
+    return b;
+}
+
+// packed row-group bytes (host) -> freshly allocated device codes/scales
+int import_matrix(db_model* m, const uint8_t* packed, int N, int K, uint8_t* dev_stage, uint8_t** codes,
+                  float** scales) {
+    const int G = K / 64, bits = m->cfg.weight_bits;
+    if (m->alloc(codes, (size_t)N * G * 64 * bits / 8, m->allocations) ||
+        m->alloc(scales, (size_t)G * db_scale_stride(N), m->allocations))
+        return db_fail(DB_ERR_CUDA, "RESOURCE_LIMIT", "weight allocation exceeds device limits");
+    cudaMemsetAsync(*scales, 0, (size_t)G * db_scale_stride(N) * 4, m->stream);
+    const size_t bytes = (size_t)N * G * group_bytes(bits);
+    int rc = db_cuda_status(cudaMemcpyAsync(dev_stage, packed, bytes, cudaMemcpyHostToDevice, m->stream), "upload");
+    if (!rc) rc = db_import_packed(dev_stage, N, K, bits, *codes, *scales, m->stream);
+    if (!rc) rc = db_cuda_status(cudaStreamSynchronize(m->stream), "import");
+    return rc;
+}
+
+int norm_from_bytes(db_model* m, const uint8_t* p, int n, float** out) {
+    std::vector<float> h(n);
+    for (int i = 0; i < n; ++i) h[i] = bf16_to_f32((uint16_t)(p[2 * i] | (p[2 * i + 1] << 8)));
+    return upload_norm(m, h.data(), n, out);
+}
+
+int build_packed(db_model* m, const dbio::Manifest& man, const std::string& dir, bool verify) {
+    const int D = m->D(), L = m->cfg.layers, F = m->F(), Nq = m->Nq(), Nk = m->Nk(), bits = m->cfg.weight_bits;
+    const size_t gb = group_bytes(bits);
+    std::string err;
+    if (man.bits != bits) return db_fail(DB_ERR_INVALID_ARGUMENT, "INVALID_WEIGHTS", "manifest scheme is not Q" + std::to_string(bits));
+    if ((int)man.layers.size() < L) return db_fail(DB_ERR_INVALID_ARGUMENT, "INVALID_WEIGHTS", "manifest has too few layers");
+    const size_t big = std::max({(size_t)m->cfg.vocab * D, (size_t)m->Nqkv() * D, (size_t)F * D, (size_t)D * Nq}) / 64 * gb;
+    uint8_t* stage = nullptr;
+    if (cudaMalloc(&stage, big + 256) != cudaSuccess)
+        return db_fail(DB_ERR_CUDA, "RESOURCE_LIMIT", "weight staging exceeds device limits");
+    auto bad = [&](const std::string& what) { return db_fail(DB_ERR_INVALID_ARGUMENT, "INVALID_WEIGHTS", what); };
+    int rc = 0;
+    std::vector<uint8_t> bytes;
+    if (!dbio::read_checked(dir, man.embedding, man, verify, &bytes, &err)) rc = bad(err);
+    else if (bytes.size() != (size_t)m->cfg.vocab * (D / 64) * gb) rc = bad("embedding size does not match the configuration");
+    if (!rc) rc = import_matrix(m, bytes.data(), m->cfg.vocab, D, stage, &m->emb_c, &m->emb_s);
+    m->layers.resize(L);
+    for (int l = 0; l < L && !rc; ++l) {
+        const dbio::LayerEntry& le = man.layers[l];
+        if (!dbio::read_checked(dir, le.file, man, verify, &bytes, &err)) { rc = bad(err); break; }
+        const dbio::TensorEntry* t[11];
+        const int64_t rows[11] = {Nq, Nk, Nk, D, F, F, D, D, D, m->cfg.head_dim, m->cfg.head_dim};
+        const int64_t cols[11] = {D, D, D, Nq, D, D, F, 0, 0, 0, 0};
+        for (int i = 0; i < 11 && !rc; ++i) {
+            t[i] = le.find_suffix(std::string("layers.") + std::to_string(l) + "." + kLayerTensors[i]);
+            if (!t[i]) { rc = bad(le.file + ": missing " + kLayerTensors[i]); break; }
+            const bool mat = cols[i] > 0;
+            const size_t want = mat ? (size_t)rows[i] * (cols[i] / 64) * gb : (size_t)rows[i] * 2;
+            const bool shape_ok = mat ? (t[i]->shape.size() == 2 && t[i]->shape[0] == rows[i] && t[i]->shape[1] == cols[i])
+                                      : (t[i]->shape.size() == 1 && t[i]->shape[0] == rows[i]);
+            if (!shape_ok || t[i]->end - t[i]->start != want || t[i]->end > bytes.size())
+                rc = bad(t[i]->name + ": shape or byte range does not match the configuration");
+        }
+        if (rc) break;
+        LayerW& lw = m->layers[l];
+        // q, k and v rows one after another are the packed form of the concatenated projection
+        std::vector<uint8_t> qkv;
+        for (int i = 0; i < 3; ++i) qkv.insert(qkv.end(), bytes.begin() + t[i]->start, bytes.begin() + t[i]->end);
+        rc = import_matrix(m, qkv.data(), m->Nqkv(), D, stage, &lw.qkv_c, &lw.qkv_s);
+        if (!rc) rc = import_matrix(m, bytes.data() + t[3]->start, D, Nq, stage, &lw.o_c, &lw.o_s);
+        uint8_t *gc = nullptr, *uc = nullptr;
+        float *gs = nullptr, *us = nullptr;
+        if (!rc) rc = import_matrix(m, bytes.data() + t[4]->start, F, D, stage, &gc, &gs);
+        if (!rc) rc = import_matrix(m, bytes.data() + t[5]->start, F, D, stage, &uc, &us);
+        if (!rc) {
+            const int G = D / 64;
+            if (m->alloc(&lw.gu_c, (size_t)2 * F * G * 64 * bits / 8, m->allocations) ||
+                m->alloc(&lw.gu_s, (size_t)G * db_scale_stride(2 * F), m->allocations))
+                rc = db_fail(DB_ERR_CUDA, "RESOURCE_LIMIT", "weight allocation exceeds device limits");
+            if (!rc) rc = db_interleave_gate_up(gc, gs, uc, us, F, D, bits, lw.gu_c, lw.gu_s, m->stream);
+            cudaStreamSynchronize(m->stream);
+        }
+        if (!rc) rc = import_matrix(m, bytes.data() + t[6]->start, D, F, stage, &lw.dn_c, &lw.dn_s);
+        if (!rc) rc = norm_from_bytes(m, bytes.data() + t[7]->start, D, &lw.in_norm);
+        if (!rc) rc = norm_from_bytes(m, bytes.data() + t[8]->start, D, &lw.post_norm);
+        if (!rc) rc = norm_from_bytes(m, bytes.data() + t[9]->start, m->cfg.head_dim, &lw.q_norm);
+        if (!rc) rc = norm_from_bytes(m, bytes.data() + t[10]->start, m->cfg.head_dim, &lw.k_norm);
+    }
+    if (!rc) {
+        if (!dbio::read_checked(dir, man.norm, man, verify, &bytes, &err)) rc = bad(err);
+        else if (bytes.size() != (size_t)D * 2) rc = bad("final norm size does not match the configuration");
+        else rc = norm_from_bytes(m, bytes.data(), D, &m->final_norm);
+    }
+    cudaStreamSynchronize(m->stream);
+    cudaFree(stage);
+    if (!rc) rc = ensure_workspace(m, m->cfg.max_sequence_tokens);
+    return rc;
+}
+
+}  // namespace
+
 extern "C" {
 
 db_model* db_model_create(int device, const db_encoder_config* cfg, const db_encoder_weights* w, db_error* err) {
@@ -622,6 +760,130 @@ int db_forward_device(db_model* m, const int32_t* ids_dev, int64_t n, float* out
     cudaStreamWaitEvent(caller, ev, 0);
     cudaEventDestroy(ev);
     return rc;
+}
+
+int db_model_export_packed(db_model* m, const char* directory, db_error* err) {
+    if (!m || !directory) {
+        fill_error(err, "INVALID_PARAMETERS", "null model or directory");
+        return DB_ERR_INVALID_ARGUMENT;
+    }
+    cudaSetDevice(m->device);
+    const int D = m->D(), L = m->cfg.layers, F = m->F(), Nq = m->Nq(), Nk = m->Nk(), bits = m->cfg.weight_bits;
+    const size_t gb = group_bytes(bits);
+    const std::string dir = directory, prefix = bits == 4 ? "q4-e4" : "q8-e8";
+    const size_t big = std::max({(size_t)m->cfg.vocab * D, (size_t)m->Nqkv() * D, (size_t)2 * F * D, (size_t)D * Nq}) / 64 * gb;
+    uint8_t* stage = nullptr;
+    if (cudaMalloc(&stage, big + 256) != cudaSuccess) {
+        fill_error(err, "RESOURCE_LIMIT", "export staging exceeds device limits");
+        return DB_ERR_CUDA;
+    }
+    std::string e, files = "{", layers = "[";
+    int rc = 0;
+    uint64_t decoder_bytes = 0;
+    auto put = [&](const std::string& name, const std::vector<uint8_t>& b) {
+        if (!dbio::write_file(dir + "/" + name, b.data(), b.size(), &e)) return false;
+        files += std::string(files.size() > 1 ? "," : "") + dbio::json_quote(name) + ":{\"bytes\":" +
+                 std::to_string(b.size()) + ",\"sha256\":" + dbio::json_quote(dbio::sha256_hex(b.data(), b.size())) + "}";
+        return true;
+    };
+    for (int l = 0; l < L && !rc; ++l) {
+        const LayerW& lw = m->layers[l];
+        std::vector<uint8_t> qkv, o, gu, dn;
+        rc = export_matrix(m, lw.qkv_c, lw.qkv_s, m->Nqkv(), D, stage, &qkv);
+        if (!rc) rc = export_matrix(m, lw.o_c, lw.o_s, D, Nq, stage, &o);
+        if (!rc) rc = export_matrix(m, lw.gu_c, lw.gu_s, 2 * F, D, stage, &gu);
+        if (!rc) rc = export_matrix(m, lw.dn_c, lw.dn_s, D, F, stage, &dn);
+        if (rc) break;
+        const size_t row_q = (size_t)(D / 64) * gb, row_o = (size_t)(Nq / 64) * gb, row_d = (size_t)(F / 64) * gb;
+        // gate and up rows come interleaved in blocks of 64 in the device layout
+        std::vector<uint8_t> gate, up;
+        for (int b = 0; b < 2 * F / 64; ++b)
+            (b % 2 ? up : gate).insert((b % 2 ? up : gate).end(), gu.begin() + (size_t)b * 64 * row_q,
+                                       gu.begin() + (size_t)(b + 1) * 64 * row_q);
+        std::vector<std::vector<uint8_t>> parts = {
+            std::vector<uint8_t>(qkv.begin(), qkv.begin() + (size_t)Nq * row_q),
+            std::vector<uint8_t>(qkv.begin() + (size_t)Nq * row_q, qkv.begin() + (size_t)(Nq + Nk) * row_q),
+            std::vector<uint8_t>(qkv.begin() + (size_t)(Nq + Nk) * row_q, qkv.end()),
+            o, gate, up, dn, norm_bytes(lw.in_norm, D), norm_bytes(lw.post_norm, D),
+            norm_bytes(lw.q_norm, m->cfg.head_dim), norm_bytes(lw.k_norm, m->cfg.head_dim)};
+        (void)row_o;
+        (void)row_d;
+        const std::vector<std::vector<int64_t>> shapes = {{Nq, D}, {Nk, D}, {Nk, D}, {D, Nq}, {F, D}, {F, D}, {D, F},
+                                                          {D}, {D}, {m->cfg.head_dim}, {m->cfg.head_dim}};
+        std::vector<uint8_t> file;
+        std::string tensors = "[";
+        for (int i = 0; i < 11; ++i) {
+            std::string shape = "[";
+            for (size_t d = 0; d < shapes[i].size(); ++d) shape += (d ? "," : "") + std::to_string(shapes[i][d]);
+            tensors += std::string(i ? "," : "") + "{\"name\":" +
+                       dbio::json_quote("language_model.layers." + std::to_string(l) + "." + kLayerTensors[i]) +
+                       ",\"shape\":" + shape + "],\"start\":" + std::to_string(file.size()) +
+                       ",\"end\":" + std::to_string(file.size() + parts[i].size()) + "}";
+            file.insert(file.end(), parts[i].begin(), parts[i].end());
+        }
+        char name[64];
+        std::snprintf(name, sizeof name, "%s-layer-%02d.bin", prefix.c_str(), l);
+        if (!put(name, file)) { rc = DB_ERR_INVALID_ARGUMENT; break; }
+        layers += std::string(l ? "," : "") + "{\"file\":" + dbio::json_quote(name) + ",\"bytes\":" +
+                  std::to_string(file.size()) + ",\"tensors\":" + tensors + "]}";
+        decoder_bytes += file.size();
+    }
+    std::vector<uint8_t> emb;
+    if (!rc) rc = export_matrix(m, m->emb_c, m->emb_s, m->cfg.vocab, D, stage, &emb);
+    if (!rc && !put(prefix + "-embedding.bin", emb)) rc = DB_ERR_INVALID_ARGUMENT;
+    if (!rc && !put(prefix + "-norm.bin", norm_bytes(m->final_norm, D))) rc = DB_ERR_INVALID_ARGUMENT;
+    cudaFree(stage);
+    if (!rc) {
+        const std::string manifest =
+            "{\"schema_version\":1,\"revision\":\"decisive-b200\",\"scheme\":\"q" + std::to_string(bits) + "-w" +
+            std::to_string(bits) + "a8-e" + std::to_string(bits) + "-r" + std::to_string(bits) +
+            "-g64\",\"group_size\":64,\"group_bytes\":" + std::to_string(gb) + ",\"embedding_row_bytes\":" +
+            std::to_string((size_t)(D / 64) * gb) + ",\"layers\":" + layers + "],\"headers\":[],\"embedding\":" +
+            dbio::json_quote(prefix + "-embedding.bin") + ",\"readout\":null,\"norm\":" +
+            dbio::json_quote(prefix + "-norm.bin") + ",\"decoder_bytes\":" + std::to_string(decoder_bytes) +
+            ",\"files\":" + files + "}}";
+        if (!dbio::write_file(dir + "/packed-" + prefix + ".json", manifest.data(), manifest.size(), &e))
+            rc = DB_ERR_INVALID_ARGUMENT;
+    }
+    if (rc) {
+        fill_error(err, rc == DB_ERR_INVALID_ARGUMENT ? "IO_ERROR" : db_last_error_code(),
+                   rc == DB_ERR_INVALID_ARGUMENT ? e : std::string(db_last_error_message()));
+        return rc;
+    }
+    return DB_OK;
+}
+
+db_model* db_model_create_packed(int device, const db_encoder_config* cfg, const char* manifest_path, int verify,
+                                 db_error* err) {
+    if (!manifest_path) {
+        fill_error(err, "INVALID_PARAMETERS", "null manifest path");
+        return nullptr;
+    }
+    if (check_config(cfg, err)) return nullptr;
+    dbio::Manifest man;
+    std::string e;
+    if (!dbio::read_manifest(manifest_path, &man, &e)) {
+        fill_error(err, "INVALID_WEIGHTS", e);
+        return nullptr;
+    }
+    if (device < 0 || device >= db_device_count() || cudaSetDevice(device) != cudaSuccess) {
+        fill_error(err, "GPU_UNAVAILABLE", "no CUDA device " + std::to_string(device));
+        return nullptr;
+    }
+    std::string path = manifest_path, dir = ".";
+    const size_t slash = path.find_last_of('/');
+    if (slash != std::string::npos) dir = path.substr(0, slash);
+    auto* m = new db_model();
+    m->device = device;
+    m->cfg = *cfg;
+    m->dev_err = db_device_error_ptr();
+    cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking);
+    if (build_packed(m, man, dir, verify != 0)) {
+        fill_error(err, db_last_error_code(), db_last_error_message());
+        db_model_destroy(m);
+        return nullptr;
+    }
+    return m;
 }
 
 }  // extern "C"

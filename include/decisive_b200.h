@@ -295,7 +295,20 @@ const char *db_model_profile_name(int kind);
 int db_model_tune(db_model *m, int64_t tokens, const char *cache_path, char *report_json, size_t cap,
                   db_error *err);
 
-/* Device-resident variant for throughput measurement: ids already on the device, output left on
+/* Packed checkpoints in the reference's export format (export_packed.rs:13-103): a directory
+ * holding packed-q4-e4.json (or packed-q8-e8.json) -- schema_version 1, scheme, group_size 64,
+ * layers[{file, bytes, tensors[{name, shape, start, end}]}], embedding, norm, files{name: {bytes,
+ * sha256}} -- and one file per layer (Qwen3 tensor names, 2-D tensors in the packed row-group
+ * format of packed.rs:10-56, 1-D tensors raw bf16), the embedding and the final norm.  The encoder
+ * has no readout ("readout": null).  db_model_export_packed writes one from a model's weights;
+ * db_model_create_packed loads one (verify = 1 checks every file's SHA-256), failing with
+ * INVALID_WEIGHTS on a missing tensor, a shape or size that does not match cfg, or a digest
+ * mismatch. */
+int db_model_export_packed(db_model *m, const char *directory, db_error *err);
+db_model *db_model_create_packed(int device, const db_encoder_config *cfg, const char *manifest_path, int verify,
+                                 db_error *err);
+
+/* Device-resident variant for throughput measurement/* Device-resident variant for throughput measurement: ids already on the device, output left on
  * the device; no host synchronisation.  Used by bench.py's device-timed leg. */
 int db_forward_device(db_model *m, const int32_t *ids_dev, int64_t n, float *out_dev, void *stream);
 
