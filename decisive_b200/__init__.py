@@ -300,11 +300,12 @@ class EncoderConfig:
     eps: float = 1e-6
     max_sequence_tokens: int = 1024
     fused: bool = True
+    causal: bool = False  # True: decoder (causal attention, prefix caches)
 
     def c(self) -> _lib.EncoderConfig:
         return _lib.EncoderConfig(self.layers, self.hidden, self.q_heads, self.kv_heads, self.head_dim, self.ffn,
                                   self.vocab, self.weight_bits, self.rope_theta, self.eps, self.max_sequence_tokens,
-                                  int(self.fused))
+                                  int(self.fused), int(self.causal))
 
 
 @dataclass
@@ -326,6 +327,12 @@ class Outcome:
 class Cache:
     def __init__(self, handle, model):
         self._h, self._model = handle, model
+
+    def stats(self) -> dict:
+        """Prefix reuse counters (kev/mod.rs Stats): hits, prefix tokens reused / computed."""
+        v = (C.c_int64 * 3)()
+        check(load().db_cache_stats(self._h, C.byref(v, 0), C.byref(v, 8), C.byref(v, 16)))
+        return {"hits": v[0], "prefix_tokens_reused": v[1], "prefix_tokens_computed": v[2]}
 
     def __del__(self):
         if getattr(self, "_h", None):
@@ -434,6 +441,26 @@ class Model:
             raise Error._from(err)
         caps = self.capabilities()
         return Response(out, caps["model"], caps["backend"])
+
+    def predict_continuations(self, prefix, continuations, cache: Cache | None = None,
+                              cancellation: Cancellation | None = None):
+        """Causal models: the final-normed hidden states [count, tokens, hidden] of each continuation
+        (equal-length token lists) after a shared prefix, whose per-layer keys and values are
+        computed once or reused from the cache (kev/mod.rs:163-300)."""
+        import numpy as np
+        pre = np.ascontiguousarray(prefix, dtype=np.int32)
+        cont = np.ascontiguousarray(continuations, dtype=np.int32)
+        if cont.ndim != 2:
+            raise ValueError("continuations must be equal-length token lists")
+        out = np.empty((cont.shape[0], cont.shape[1], self.config.hidden), dtype=np.float32)
+        err = _lib.DbError()
+        rc = load().db_predict_continuations(self._h, cache._h if cache else None, pre.ctypes.data_as(C.c_void_p),
+                                             pre.size, cont.ctypes.data_as(C.c_void_p), cont.shape[0], cont.shape[1],
+                                             cancellation.ptr if cancellation else None,
+                                             out.ctypes.data_as(C.c_void_p), C.byref(err))
+        if rc:
+            raise Error._from(err)
+        return out
 
     def predict_batch(self, requests, parameters: PplxParameters | None = None, cache: Cache | None = None,
                       cancellation: Cancellation | None = None) -> list[Outcome]:

@@ -23,7 +23,7 @@ class EncoderConfig(C.Structure):
     _fields_ = [("layers", C.c_int32), ("hidden", C.c_int32), ("q_heads", C.c_int32), ("kv_heads", C.c_int32),
                 ("head_dim", C.c_int32), ("ffn", C.c_int32), ("vocab", C.c_int32), ("weight_bits", C.c_int32),
                 ("rope_theta", C.c_float), ("eps", C.c_float), ("max_sequence_tokens", C.c_int32),
-                ("fused", C.c_int32)]
+                ("fused", C.c_int32), ("causal", C.c_int32)]
 
 
 class Parameters(C.Structure):
@@ -84,6 +84,8 @@ SIGNATURES = [
     ("db_predict_batch", _i32, [_vp, _vp, _vp, _sz, C.POINTER(Parameters), _vp, _vp, _vp, _vp, _vp,
                                 C.POINTER(DbError)]),
     ("db_forward_device", _i32, [_vp, _vp, _i64, _vp, _vp]),
+    ("db_predict_continuations", _i32, [_vp, _vp, _vp, _sz, _vp, _sz, _sz, _vp, _vp, C.POINTER(DbError)]),
+    ("db_cache_stats", _i32, [_vp, _vp, _vp, _vp]),
     ("db_model_profile", _i32, [_vp, _i32]),
     ("db_model_export_packed", _i32, [_vp, C.c_char_p, C.POINTER(DbError)]),
     ("db_model_create_packed", _vp, [_i32, C.POINTER(EncoderConfig), C.c_char_p, _i32, C.POINTER(DbError)]),

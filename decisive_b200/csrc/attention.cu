@@ -66,7 +66,8 @@ __global__ void __launch_bounds__(ATT_THREADS)
     attention_kernel(const __half* __restrict__ q16, const __half* __restrict__ k16, const __half* __restrict__ v16,
                      int T, int Hq, int Hk, float scale_log2, float* __restrict__ out, int64_t ldo,
                      __half* __restrict__ codes, int64_t ldc, float* __restrict__ scales, int64_t lds,
-                     int* __restrict__ nonfinite) {
+                     int* __restrict__ nonfinite, const __half* __restrict__ kp, const __half* __restrict__ vp, int P,
+                     int causal) {
     extern __shared__ __align__(128) uint8_t smem[];
     const uint32_t sQ = smem_u32(smem);
     const uint32_t sK[2] = {sQ + ATT_TILE_BYTES, sQ + 2 * ATT_TILE_BYTES};
@@ -74,11 +75,28 @@ __global__ void __launch_bounds__(ATT_THREADS)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int h = blockIdx.y, kh = h / (Hq / Hk);
     const int q0 = blockIdx.x * ATT_BQ;
-    const int tiles = (T + ATT_BKV - 1) / ATT_BKV;
+    // item blockIdx.z of a batch: its rows follow the previous items' in every row-indexed tensor
+    const int64_t rb = (int64_t)blockIdx.z * T;
+    q16 += rb * Hq * ATT_D;
+    k16 += rb * Hk * ATT_D;
+    v16 += rb * Hk * ATT_D;
+    // key tiles: the P cached prefix keys first, then the item's own T keys (causal: only the
+    // tiles that reach this query tile)
+    const int tiles_p = (P + ATT_BKV - 1) / ATT_BKV, tiles_own_all = (T + ATT_BKV - 1) / ATT_BKV;
+    const int tiles_own = causal ? min(tiles_own_all, (q0 + ATT_BQ + ATT_BKV - 1) / ATT_BKV) : tiles_own_all;
+    const int tiles = tiles_p + tiles_own;
+    auto load_kv = [&](int buf, int j) {
+        if (j < tiles_p) {
+            load_tile(sK[buf], kp, P, Hk, kh, j * ATT_BKV, tid);
+            load_tile(sV[buf], vp, P, Hk, kh, j * ATT_BKV, tid);
+        } else {
+            load_tile(sK[buf], k16, T, Hk, kh, (j - tiles_p) * ATT_BKV, tid);
+            load_tile(sV[buf], v16, T, Hk, kh, (j - tiles_p) * ATT_BKV, tid);
+        }
+    };
 
     load_tile(sQ, q16, T, Hq, h, q0, tid);
-    load_tile(sK[0], k16, T, Hk, kh, 0, tid);
-    load_tile(sV[0], v16, T, Hk, kh, 0, tid);
+    load_kv(0, 0);
     cp_async_commit();
 
     uint32_t qf[8][4];
@@ -88,10 +106,7 @@ __global__ void __launch_bounds__(ATT_THREADS)
     float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
 
     for (int j = 0; j < tiles; ++j) {
-        if (j + 1 < tiles) {
-            load_tile(sK[(j + 1) & 1], k16, T, Hk, kh, (j + 1) * ATT_BKV, tid);
-            load_tile(sV[(j + 1) & 1], v16, T, Hk, kh, (j + 1) * ATT_BKV, tid);
-        }
+        if (j + 1 < tiles) load_kv((j + 1) & 1, j + 1);
         cp_async_commit();
         cp_async_wait<1>();
         __syncthreads();
@@ -119,15 +134,18 @@ __global__ void __launch_bounds__(ATT_THREADS)
                 mma16816(sc[n + 1], qf[s], b2, b3);
             }
         }
-        // mask keys beyond T, scale into the log2 domain
-        const int kv0 = j * ATT_BKV;
+        // mask keys past the segment's end (and, causal, past the query), scale into the log2 domain
+        const bool seg_p = j < tiles_p;
+        const int kv0 = (seg_p ? j : j - tiles_p) * ATT_BKV, kend = seg_p ? P : T;
+        const int qrow = q0 + warp * 16 + (lane >> 2);
         float mx[2] = {mrow[0], mrow[1]};
 #pragma unroll
         for (int n = 0; n < 8; ++n) {
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
                 const int key = kv0 + n * 8 + 2 * (lane & 3) + (e & 1);
-                float v = key < T ? sc[n][e] * scale_log2 : -INFINITY;
+                const bool ok = key < kend && (seg_p || !causal || key <= qrow + ((e >> 1) << 3));
+                float v = ok ? sc[n][e] * scale_log2 : -INFINITY;
                 sc[n][e] = v;
                 mx[e >> 1] = fmaxf(mx[e >> 1], v);
             }
@@ -223,7 +241,7 @@ __global__ void __launch_bounds__(ATT_THREADS)
                     reinterpret_cast<__half*>(smem)[row * ATT_D + col + 2] = c1;
                 }
                 const int t = q0 + row;
-                if (q == 0 && t < T) scales[(size_t)(h * 2 + grp) * lds + t] = scale;
+                if (q == 0 && t < T) scales[(size_t)(h * 2 + grp) * lds + rb + t] = scale;
             }
         }
         if (bad) atomicOr(nonfinite, 1);
@@ -235,7 +253,7 @@ __global__ void __launch_bounds__(ATT_THREADS)
             const int row = idx >> 4, chunk = idx & 15;
             const int t = q0 + row;
             if (t < T)
-                *reinterpret_cast<uint4*>(codes + (size_t)t * ldc + h * ATT_D + chunk * 8) =
+                *reinterpret_cast<uint4*>(codes + (size_t)(rb + t) * ldc + h * ATT_D + chunk * 8) =
                     reinterpret_cast<const uint4*>(smem)[row * 16 + chunk];
         }
         return;
@@ -244,9 +262,9 @@ __global__ void __launch_bounds__(ATT_THREADS)
     for (int n = 0; n < 16; ++n) {
         const int d = n * 8 + 2 * (lane & 3);
         if (r0 < T)
-            *reinterpret_cast<float2*>(out + (size_t)r0 * ldo + h * ATT_D + d) = make_float2(o[n][0] * inv0, o[n][1] * inv0);
+            *reinterpret_cast<float2*>(out + (size_t)(rb + r0) * ldo + h * ATT_D + d) = make_float2(o[n][0] * inv0, o[n][1] * inv0);
         if (r0 + 8 < T)
-            *reinterpret_cast<float2*>(out + (size_t)(r0 + 8) * ldo + h * ATT_D + d) =
+            *reinterpret_cast<float2*>(out + (size_t)(rb + r0 + 8) * ldo + h * ATT_D + d) =
                 make_float2(o[n][2] * inv1, o[n][3] * inv1);
     }
 }
@@ -268,7 +286,8 @@ int db_launch_attention(const __half* q16, const __half* k16, const __half* v16,
     }
     dim3 grid((T + ATT_BQ - 1) / ATT_BQ, Hq);
     attention_kernel<false><<<grid, ATT_THREADS, smem, stream>>>(q16, k16, v16, T, Hq, Hk, scale * 1.4426950408889634f,
-                                                                 out, ldo, nullptr, 0, nullptr, 0, nullptr);
+                                                                 out, ldo, nullptr, 0, nullptr, 0, nullptr, nullptr,
+                                                                 nullptr, 0, 0);
     return (int)cudaGetLastError();
 }
 
@@ -286,6 +305,29 @@ int db_launch_attention_quant(const __half* q16, const __half* k16, const __half
     }
     dim3 grid((T + ATT_BQ - 1) / ATT_BQ, Hq);
     attention_kernel<true><<<grid, ATT_THREADS, smem, stream>>>(q16, k16, v16, T, Hq, Hk, scale * 1.4426950408889634f,
-                                                                nullptr, 0, codes, ldc, scales, lds, nonfinite);
+                                                                nullptr, 0, codes, ldc, scales, lds, nonfinite, nullptr,
+                                                                nullptr, 0, 0);
+    return (int)cudaGetLastError();
+}
+
+int db_launch_attention_prefix_quant(const __half* q16, const __half* k16, const __half* v16, int B, int T,
+                                     const __half* kp, const __half* vp, int P, int causal, int Hq, int Hk,
+                                     float scale, __half* codes, int64_t ldc, float* scales, int64_t lds,
+                                     int* nonfinite, cudaStream_t stream) {
+    if (T <= 0 || B <= 0) return 0;
+    if (Hk <= 0 || Hq % Hk || !codes || !scales || !nonfinite || (ldc & 7) || P < 0 || (P > 0 && (!kp || !vp)) ||
+        B > 65535)
+        return (int)cudaErrorInvalidValue;
+    const int smem = 5 * ATT_TILE_BYTES;
+    static bool configured = false;
+    if (!configured) {
+        cudaError_t e = cudaFuncSetAttribute(attention_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return (int)e;
+        configured = true;
+    }
+    dim3 grid((T + ATT_BQ - 1) / ATT_BQ, Hq, B);
+    attention_kernel<true><<<grid, ATT_THREADS, smem, stream>>>(q16, k16, v16, T, Hq, Hk, scale * 1.4426950408889634f,
+                                                                nullptr, 0, codes, ldc, scales, lds, nonfinite, kp, vp,
+                                                                P, causal);
     return (int)cudaGetLastError();
 }

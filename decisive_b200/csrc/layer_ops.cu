@@ -119,7 +119,8 @@ constexpr int QK_HEADS_PER_WARP = 4;
 __global__ void qk_norm_rope_kernel(const float* __restrict__ qkv, int64_t ld, int T, int Hq, int Hk,
                                     const float* __restrict__ qw, const float* __restrict__ kw, float eps,
                                     const float* __restrict__ cos_t, const float* __restrict__ sin_t,
-                                    __half* __restrict__ q16, __half* __restrict__ k16, __half* __restrict__ v16) {
+                                    __half* __restrict__ q16, __half* __restrict__ k16, __half* __restrict__ v16,
+                                    int pos0, int seq_len) {
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     const int heads = Hq + 2 * Hk;
     const int units = (heads + QK_HEADS_PER_WARP - 1) / QK_HEADS_PER_WARP;
@@ -130,8 +131,10 @@ __global__ void qk_norm_rope_kernel(const float* __restrict__ qkv, int64_t ld, i
     for (int u = 0; u < QK_HEADS_PER_WARP; ++u)
         if (h0 + u < heads) v[u] = *reinterpret_cast<const float4*>(qkv + (size_t)t * ld + (h0 + u) * 128 + 4 * lane);
     const int i0 = (4 * lane) & 63;
-    const float4 cs = *reinterpret_cast<const float4*>(cos_t + (size_t)t * 64 + i0);
-    const float4 sn = *reinterpret_cast<const float4*>(sin_t + (size_t)t * 64 + i0);
+    // rows are seq_len-token items placed one after another, each starting at position pos0
+    const size_t pos = (size_t)(pos0 + t % seq_len);
+    const float4 cs = *reinterpret_cast<const float4*>(cos_t + pos * 64 + i0);
+    const float4 sn = *reinterpret_cast<const float4*>(sin_t + pos * 64 + i0);
     const float cc[4] = {cs.x, cs.y, cs.z, cs.w}, ssn[4] = {sn.x, sn.y, sn.z, sn.w};
 #pragma unroll
     for (int u = 0; u < QK_HEADS_PER_WARP; ++u) {
@@ -203,11 +206,12 @@ int db_launch_rms_quantize(const float* x, int64_t ldx, const float* w, int T, i
 
 int db_launch_qk_norm_rope(const float* qkv, int64_t ld, int T, int Hq, int Hk, const float* qw, const float* kw,
                            float eps, const float* cos_t, const float* sin_t, __half* q16, __half* k16, __half* v16,
-                           cudaStream_t stream) {
+                           cudaStream_t stream, int pos0, int seq_len) {
     if (T <= 0) return 0;
     const int64_t warps = (int64_t)T * ((Hq + 2 * Hk + QK_HEADS_PER_WARP - 1) / QK_HEADS_PER_WARP);
     qk_norm_rope_kernel<<<(unsigned)((warps + 3) / 4), 128, 0, stream>>>(qkv, ld, T, Hq, Hk, qw, kw, eps, cos_t,
-                                                                          sin_t, q16, k16, v16);
+                                                                          sin_t, q16, k16, v16, pos0,
+                                                                          seq_len > 0 ? seq_len : T);
     return (int)cudaGetLastError();
 }
 

@@ -7,9 +7,11 @@
 int db_launch_rms_quantize(const float* x, int64_t ldx, const float* w, int T, int D, float eps, int zero_centered,
                            float* normed, int64_t ldn, void* codes, int layout, int64_t ldc, float* scales,
                            int32_t* sums, int64_t lds, int* nonfinite, cudaStream_t stream, int normalize = 1);
+// Rows are items of seq_len tokens (0 = T) one after another; row t gets RoPE position
+// pos0 + t % seq_len (a continuation after a cached prefix of pos0 tokens).
 int db_launch_qk_norm_rope(const float* qkv, int64_t ld, int T, int Hq, int Hk, const float* qw, const float* kw,
                            float eps, const float* cos_t, const float* sin_t, __half* q16, __half* k16, __half* v16,
-                           cudaStream_t stream);
+                           cudaStream_t stream, int pos0 = 0, int seq_len = 0);
 int db_launch_mean_pool(const float* x, int64_t ldx, int T, int D, float* out, cudaStream_t stream);
 int db_launch_fill_nan_if(float* y, int64_t n, const int* flag, cudaStream_t stream);
 
@@ -23,3 +25,11 @@ int db_launch_attention(const __half* q16, const __half* k16, const __half* v16,
 int db_launch_attention_quant(const __half* q16, const __half* k16, const __half* v16, int T, int Hq, int Hk,
                               float scale, __half* codes, int64_t ldc, float* scales, int64_t lds, int* nonfinite,
                               cudaStream_t stream);
+// Decoder form of the quantising attention: B items of T rows each (q16/k16/v16 and the outputs
+// hold the items one after another); every item's keys are the P cached prefix keys kp/vp
+// [P, Hk, 128] (shared by the items; P = 0: none) followed by its own T keys, which are causal
+// (row i sees own keys 0..i) when causal != 0.
+int db_launch_attention_prefix_quant(const __half* q16, const __half* k16, const __half* v16, int B, int T,
+                                     const __half* kp, const __half* vp, int P, int causal, int Hq, int Hk,
+                                     float scale, __half* codes, int64_t ldc, float* scales, int64_t lds,
+                                     int* nonfinite, cudaStream_t stream);

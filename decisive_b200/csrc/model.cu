@@ -64,6 +64,11 @@ struct db_model {
     // workspace for up to cap_T tokens
     int cap_T = 0;
     std::vector<void*> ws_allocations;
+    int rope_T = 0;  // positions covered by the RoPE tables
+    std::vector<void*> rope_allocations;
+    // per-layer prefix keys/values of a continuation call whose cache cannot keep them
+    std::vector<__half*> tmp_k, tmp_v;
+    int tmp_cap = 0;
     float *x = nullptr, *qkv = nullptr, *ctx = nullptr, *normed = nullptr, *pooled = nullptr;
     float *cos_t = nullptr, *sin_t = nullptr, *sa = nullptr, *sh = nullptr;
     __half *acodes = nullptr, *hcodes = nullptr, *q16 = nullptr, *k16 = nullptr, *v16 = nullptr;
@@ -112,6 +117,23 @@ struct db_model {
 struct db_cache {
     std::shared_ptr<char> identity;
     size_t max_bytes = 0;
+    bool prefix_cache = false;
+    // the kept prefix: its ids and, per layer, keys and values [cap_P, Hk, 128] f16
+    int device = 0;
+    std::vector<int32_t> ids;
+    int cap_P = 0;
+    std::vector<__half*> k, v;
+    int64_t hits = 0, reused = 0, computed = 0;
+    void release() {
+        if (!k.empty()) cudaSetDevice(device);
+        for (__half* p : k) cudaFree(p);
+        for (__half* p : v) cudaFree(p);
+        k.clear();
+        v.clear();
+        ids.clear();
+        cap_P = 0;
+    }
+    ~db_cache() { release(); }
 };
 
 namespace {
@@ -145,6 +167,31 @@ int upload_norm(db_model* m, const float* host, int n, float** out) {
     return db_cuda_status(cudaMemcpy(*out, ones.data(), n * sizeof(float), cudaMemcpyHostToDevice), "norm upload");
 }
 
+// rotate-half RoPE table for positions 0..n-1 (backbone.rs:214-216, :471-483):
+// angle = t * theta^(-2i/head_dim)
+int ensure_rope(db_model* m, int n) {
+    if (n <= m->rope_T) return 0;
+    cudaStreamSynchronize(m->stream);
+    m->free_all(m->rope_allocations);
+    m->rope_T = 0;
+    if (m->alloc(&m->cos_t, (size_t)n * 64, m->rope_allocations) ||
+        m->alloc(&m->sin_t, (size_t)n * 64, m->rope_allocations))
+        return db_fail(DB_ERR_CUDA, "RESOURCE_LIMIT", "RoPE table exceeds device limits");
+    const int half = m->cfg.head_dim / 2;
+    std::vector<float> freq(half), c((size_t)n * 64), s((size_t)n * 64);
+    for (int i = 0; i < half; ++i) freq[i] = 1.f / powf(m->cfg.rope_theta, (float)(2 * i) / (float)m->cfg.head_dim);
+    for (int t = 0; t < n; ++t)
+        for (int i = 0; i < half; ++i) {
+            const float angle = (float)t * freq[i];
+            c[(size_t)t * 64 + i] = cosf(angle);
+            s[(size_t)t * 64 + i] = sinf(angle);
+        }
+    cudaMemcpy(m->cos_t, c.data(), c.size() * 4, cudaMemcpyHostToDevice);
+    cudaMemcpy(m->sin_t, s.data(), s.size() * 4, cudaMemcpyHostToDevice);
+    m->rope_T = n;
+    return 0;
+}
+
 int ensure_workspace(db_model* m, int T) {
     if (T <= m->cap_T) return 0;
     cudaStreamSynchronize(m->stream);
@@ -155,26 +202,14 @@ int ensure_workspace(db_model* m, int T) {
     auto& v = m->ws_allocations;
     if (m->alloc(&m->x, (size_t)T * D, v) || m->alloc(&m->qkv, (size_t)T * m->Nqkv(), v) ||
         m->alloc(&m->ctx, (size_t)T * m->Nq(), v) || m->alloc(&m->normed, (size_t)T * D, v) ||
-        m->alloc(&m->pooled, D, v) || m->alloc(&m->cos_t, (size_t)T * 64, v) || m->alloc(&m->sin_t, (size_t)T * 64, v) ||
+        m->alloc(&m->pooled, D, v) ||
         m->alloc(&m->sa, (size_t)Gmax * db_scale_stride(T), v) || m->alloc(&m->sh, (size_t)(F / 64) * db_scale_stride(T), v) ||
         m->alloc(&m->acodes, (size_t)T * Kmax, v) || m->alloc(&m->hcodes, (size_t)T * F, v) ||
         m->alloc(&m->q16, (size_t)T * m->Nq(), v) || m->alloc(&m->k16, (size_t)T * m->Nk(), v) ||
         m->alloc(&m->v16, (size_t)T * m->Nk(), v) || m->alloc(&m->ids, T, v) || m->alloc(&m->flag, 4, v))
         return db_fail(DB_ERR_CUDA, "RESOURCE_LIMIT", "workspace exceeds device limits");
-    // rotate-half RoPE table (backbone.rs:214-216, :471-483): angle = t * theta^(-2i/head_dim)
-    const int half = m->cfg.head_dim / 2;
-    std::vector<float> freq(half), c((size_t)T * 64), s((size_t)T * 64);
-    for (int i = 0; i < half; ++i) freq[i] = 1.f / powf(m->cfg.rope_theta, (float)(2 * i) / (float)m->cfg.head_dim);
-    for (int t = 0; t < T; ++t)
-        for (int i = 0; i < half; ++i) {
-            const float angle = (float)t * freq[i];
-            c[(size_t)t * 64 + i] = cosf(angle);
-            s[(size_t)t * 64 + i] = sinf(angle);
-        }
-    cudaMemcpy(m->cos_t, c.data(), c.size() * 4, cudaMemcpyHostToDevice);
-    cudaMemcpy(m->sin_t, s.data(), s.size() * 4, cudaMemcpyHostToDevice);
     m->cap_T = T;
-    return 0;
+    return ensure_rope(m, T);
 }
 
 int build(db_model* m, const db_encoder_weights* w) {
@@ -252,9 +287,24 @@ db_model* create(int device, const db_encoder_config* cfg, const db_encoder_weig
     return m;
 }
 
+// A decoder pass over `items` sequences of T tokens each: RoPE positions start at `prefix`, the
+// attention of every item also sees the cached prefix keys/values pk[l], pv[l] (P = prefix rows);
+// sk/sv (a prefix pass) receive each layer's own keys and values; pool: mean-pool into m->pooled.
+struct Pass {
+    int items = 1;
+    int prefix = 0;
+    __half* const* pk = nullptr;
+    __half* const* pv = nullptr;
+    __half* const* sk = nullptr;
+    __half* const* sv = nullptr;
+    bool pool = true;
+};
+
 // Enqueues the forward of ids (device, T tokens) -> m->pooled.  Host-side cancellation is polled
 // between layers.  Returns 0, 1 when cancelled, or a negative status.
-int enqueue_forward(db_model* m, int T, const volatile uint8_t* cancel) {
+int enqueue_forward(db_model* m, int T, const volatile uint8_t* cancel, const Pass* pass = nullptr) {
+    // rows: `items` token sequences of T tokens one after another
+    const int items = pass ? pass->items : 1, R = items * T, P = pass ? pass->prefix : 0;
     const auto& c = m->cfg;
     const int D = c.hidden, Nq = m->Nq(), F = m->F(), Nqkv = m->Nqkv();
     const int bits = c.weight_bits, fused = c.fused;
@@ -272,7 +322,7 @@ int enqueue_forward(db_model* m, int T, const volatile uint8_t* cancel) {
     };
     cudaMemsetAsync(m->flag, 0, sizeof(int), st);
     rc = timed(0, [&] {
-        return db_launch_dequant_rows(m->emb_c, m->emb_s, c.vocab, D, bits, m->ids, T, m->x, D, m->flag, st);
+        return db_launch_dequant_rows(m->emb_c, m->emb_s, c.vocab, D, bits, m->ids, R, m->x, D, m->flag, st);
     });
     auto gemm = [&](int proj, const void* a, const uint8_t* wc, const float* ws, const float* sa, int N, int K, int epi,
                     float* y, int64_t ldy) {
@@ -283,7 +333,7 @@ int enqueue_forward(db_model* m, int T, const volatile uint8_t* cancel) {
         g.ldsa = lds;
         g.w_codes = wc;
         g.sw = ws;
-        g.M = T;
+        g.M = R;
         g.N = N;
         g.K = K;
         g.bits = bits;
@@ -303,29 +353,39 @@ int enqueue_forward(db_model* m, int T, const volatile uint8_t* cancel) {
         return db_launch_gemm_tc(g, st);
     };
     const float attn_scale = 1.f / sqrtf((float)c.head_dim);
+    auto own_k = [&](int l) { return pass && pass->sk ? pass->sk[l] : m->k16; };
+    auto own_v = [&](int l) { return pass && pass->sv ? pass->sv[l] : m->v16; };
     for (int l = 0; l < c.layers && !rc; ++l) {
         if (cancel && *cancel) return 1;
         const LayerW& w = m->layers[l];
         rc = timed(1, [&] {
-            return db_launch_rms_quantize(m->x, D, w.in_norm, T, D, c.eps, 0, nullptr, 0, m->acodes, DB_CODES_TC,
+            return db_launch_rms_quantize(m->x, D, w.in_norm, R, D, c.eps, 0, nullptr, 0, m->acodes, DB_CODES_TC,
                                           ld_codes, m->sa, nullptr, lds, m->flag, st);
         });
         if (!rc) rc = timed(2, [&] { return gemm(0, m->acodes, w.qkv_c, w.qkv_s, m->sa, Nqkv, D, DB_EPI_STORE, m->qkv, Nqkv); });
         if (!rc)
             rc = timed(3, [&] {
-                return db_launch_qk_norm_rope(m->qkv, Nqkv, T, c.q_heads, c.kv_heads, w.q_norm, w.k_norm, c.eps,
-                                              m->cos_t, m->sin_t, m->q16, m->k16, m->v16, st);
+                // a prefix pass stores this layer's keys and values straight into the cache
+                return db_launch_qk_norm_rope(m->qkv, Nqkv, R, c.q_heads, c.kv_heads, w.q_norm, w.k_norm, c.eps,
+                                              m->cos_t, m->sin_t, m->q16, own_k(l), own_v(l), st, P, T);
             });
         // attention writes the context already quantised for the output projection
         if (!rc)
             rc = timed(4, [&] {
-                return db_launch_attention_quant(m->q16, m->k16, m->v16, T, c.q_heads, c.kv_heads, attn_scale,
-                                                 static_cast<__half*>(m->acodes), ld_codes, m->sa, lds, m->flag, st);
+                if (!c.causal && !pass)
+                    return db_launch_attention_quant(m->q16, m->k16, m->v16, T, c.q_heads, c.kv_heads, attn_scale,
+                                                     static_cast<__half*>(m->acodes), ld_codes, m->sa, lds, m->flag, st);
+                return db_launch_attention_prefix_quant(m->q16, own_k(l), own_v(l), items, T,
+                                                        pass && pass->pk ? pass->pk[l] : nullptr,
+                                                        pass && pass->pv ? pass->pv[l] : nullptr, P, c.causal,
+                                                        c.q_heads, c.kv_heads, attn_scale,
+                                                        static_cast<__half*>(m->acodes), ld_codes, m->sa, lds, m->flag,
+                                                        st);
             });
         if (!rc) rc = timed(6, [&] { return gemm(1, m->acodes, w.o_c, w.o_s, m->sa, D, Nq, DB_EPI_RESIDUAL, m->x, D); });
         if (!rc)
             rc = timed(1, [&] {
-                return db_launch_rms_quantize(m->x, D, w.post_norm, T, D, c.eps, 0, nullptr, 0, m->acodes, DB_CODES_TC,
+                return db_launch_rms_quantize(m->x, D, w.post_norm, R, D, c.eps, 0, nullptr, 0, m->acodes, DB_CODES_TC,
                                               ld_codes, m->sa, nullptr, lds, m->flag, st);
             });
         if (!rc)
@@ -338,7 +398,7 @@ int enqueue_forward(db_model* m, int T, const volatile uint8_t* cancel) {
             g.ldsa = lds;
             g.w_codes = w.dn_c;
             g.sw = w.dn_s;
-            g.M = T;
+            g.M = R;
             g.N = D;
             g.K = F;
             g.bits = bits;
@@ -356,10 +416,10 @@ int enqueue_forward(db_model* m, int T, const volatile uint8_t* cancel) {
     }
     if (!rc)
         rc = timed(9, [&] {
-            return db_launch_rms_quantize(m->x, D, m->final_norm, T, D, c.eps, 0, m->normed, D, nullptr, DB_CODES_TC, 0,
+            return db_launch_rms_quantize(m->x, D, m->final_norm, R, D, c.eps, 0, m->normed, D, nullptr, DB_CODES_TC, 0,
                                           nullptr, nullptr, 0, m->flag, st);
         });
-    if (!rc) rc = timed(10, [&] { return db_launch_mean_pool(m->normed, D, T, D, m->pooled, st); });
+    if (!rc && (!pass || pass->pool)) rc = timed(10, [&] { return db_launch_mean_pool(m->normed, D, T, D, m->pooled, st); });
     return rc ? db_cuda_status(rc, "forward") : 0;
 }
 
@@ -610,7 +670,10 @@ void db_model_destroy(db_model* m) {
     cudaSetDevice(m->device);
     if (m->stream) cudaStreamSynchronize(m->stream);
     m->free_all(m->ws_allocations);
+    m->free_all(m->rope_allocations);
     m->free_all(m->allocations);
+    for (__half* p : m->tmp_k) cudaFree(p);
+    for (__half* p : m->tmp_v) cudaFree(p);
     if (m->stream) cudaStreamDestroy(m->stream);
     for (cudaEvent_t e : m->ev_pool) cudaEventDestroy(e);
     delete m;
@@ -620,8 +683,9 @@ int db_model_capabilities(const db_model* m, char* json, size_t cap) {
     if (!m || !json) return DB_ERR_INVALID_ARGUMENT;
     // adapters.rs:167-176 (Pplx: no caches); backend is this library
     int n = std::snprintf(json, cap,
-                          "{\"model\":\"pplx-flash\",\"backend\":\"cuda\",\"caches\":[],\"tuning\":\"heuristic\","
+                          "{\"model\":\"%s\",\"backend\":\"cuda\",\"caches\":[%s],\"tuning\":\"tiles\","
                           "\"weightBits\":%d,\"layers\":%d,\"hidden\":%d}",
+                          m->cfg.causal ? "decoder" : "pplx-flash", m->cfg.causal ? "\"prefix\"" : "",
                           m->cfg.weight_bits, m->cfg.layers, m->cfg.hidden);
     return n < 0 || (size_t)n >= cap ? DB_ERR_INVALID_ARGUMENT : DB_OK;
 }
@@ -631,13 +695,15 @@ db_cache* db_cache_create(db_model* m, size_t max_bytes, int require_prefix, db_
         fill_error(err, "INVALID_PARAMETERS", "no model");
         return nullptr;
     }
-    if (require_prefix) {  // mod.rs:177-182: this model/backend has no prefix cache
+    if (require_prefix && !m->cfg.causal) {  // mod.rs:177-182: the encoder has no prefix cache
         fill_error(err, "UNSUPPORTED_CACHE", "This model/backend does not support prefix caching");
         return nullptr;
     }
     auto* c = new db_cache();
     c->identity = m->identity;
     c->max_bytes = max_bytes;
+    c->prefix_cache = m->cfg.causal != 0;
+    c->device = m->device;
     return c;
 }
 
@@ -646,7 +712,8 @@ int db_cache_clear(db_model* m, db_cache* c, db_error* err) {
         fill_error(err, "CACHE_OWNER", "Cache belongs to another model instance");
         return -1;
     }
-    return 0;  // the Pplx backend keeps no cache state (adapters.rs:180-181)
+    c->release();  // encoders keep no state (adapters.rs:180-181); decoders drop the prefix
+    return 0;
 }
 
 void db_cache_destroy(db_cache* c) { delete c; }
@@ -884,6 +951,154 @@ db_model* db_model_create_packed(int device, const db_encoder_config* cfg, const
         return nullptr;
     }
     return m;
+}
+
+}  // extern "C"
+
+namespace {
+// (re)allocates per-layer key/value buffers for cap rows of Hk heads
+int ensure_kv(std::vector<__half*>& k, std::vector<__half*>& v, int& cap, int rows, int layers, int Hk) {
+    if (rows <= cap && (int)k.size() == layers) return 0;
+    for (__half* p : k) cudaFree(p);
+    for (__half* p : v) cudaFree(p);
+    k.assign(layers, nullptr);
+    v.assign(layers, nullptr);
+    cap = 0;
+    for (int l = 0; l < layers; ++l)
+        if (cudaMalloc(&k[l], (size_t)rows * Hk * 128 * 2) != cudaSuccess ||
+            cudaMalloc(&v[l], (size_t)rows * Hk * 128 * 2) != cudaSuccess)
+            return db_fail(DB_ERR_CUDA, "RESOURCE_LIMIT", "prefix state exceeds device limits");
+    cap = rows;
+    return 0;
+}
+}  // namespace
+
+extern "C" {
+
+int db_predict_continuations(db_model* m, db_cache* cache, const int32_t* prefix, size_t prefix_len,
+                             const int32_t* continuations, size_t count, size_t tokens,
+                             const volatile uint8_t* cancel, float* hidden, db_error* err) {
+    if (!m || !hidden || !prefix || !continuations) {
+        fill_error(err, "INVALID_PARAMETERS", "null model, ids or output");
+        return -1;
+    }
+    if (!m->cfg.causal) {
+        fill_error(err, "UNSUPPORTED_CACHE", "continuations need a causal (decoder) model");
+        return -1;
+    }
+    if (cache && cache->identity != m->identity) {
+        fill_error(err, "CACHE_OWNER", "Cache belongs to another model instance");
+        return -1;
+    }
+    if (cancel && *cancel) {
+        fill_error(err, "CANCELLED", "Inference was cancelled");
+        return -1;
+    }
+    if (prefix_len == 0 || count == 0 || tokens == 0) {
+        fill_error(err, "INVALID_REQUEST", "a nonempty prefix and nonempty continuations are required");
+        return -1;
+    }
+    if (prefix_len + tokens > (size_t)m->cfg.max_sequence_tokens || count > 65535) {
+        fill_error(err, "INPUT_TOO_LONG", "prefix + continuation exceeds token limit: " +
+                                              std::to_string(prefix_len + tokens) + " > " +
+                                              std::to_string(m->cfg.max_sequence_tokens) + "; inputs are never truncated");
+        return -1;
+    }
+    for (size_t i = 0; i < prefix_len + count * tokens; ++i) {
+        const int32_t id = i < prefix_len ? prefix[i] : continuations[i - prefix_len];
+        if (id < 0 || id >= m->cfg.vocab) {
+            fill_error(err, "INVALID_REQUEST", "token id " + std::to_string(id) + " outside the vocabulary");
+            return -1;
+        }
+    }
+    cudaSetDevice(m->device);
+    const int P = (int)prefix_len, T = (int)tokens, B = (int)count, L = m->cfg.layers, Hk = m->cfg.kv_heads;
+    if (ensure_workspace(m, std::max(P, B * T)) || ensure_rope(m, P + T)) {
+        fill_error(err, "RESOURCE_LIMIT", db_last_error_message());
+        return -1;
+    }
+    auto failed = [&](int rc) {
+        cudaStreamSynchronize(m->stream);
+        if (rc == 1) fill_error(err, "CANCELLED", "Inference was cancelled");
+        else fill_error(err, "INFERENCE_FAILED", db_last_error_message());
+        return -1;
+    };
+    // the prefix state: reused from the cache, or computed by a causal pass that stores every
+    // layer's keys and values (into the cache when its byte budget holds them, kev/mod.rs:186-236)
+    const bool reuse = cache && cache->prefix_cache && (int)cache->ids.size() == P &&
+                       std::equal(prefix, prefix + P, cache->ids.begin()) && (int)cache->k.size() == L;
+    std::vector<__half*>* pk = &m->tmp_k;
+    std::vector<__half*>* pv = &m->tmp_v;
+    if (reuse) {
+        pk = &cache->k;
+        pv = &cache->v;
+        cache->hits += 1;
+        cache->reused += P;
+    } else {
+        const size_t state_bytes = (size_t)L * P * Hk * 128 * 2 * 2;
+        const bool keep = cache && cache->prefix_cache && state_bytes <= cache->max_bytes;
+        int rc = 0;
+        if (keep) {
+            cache->ids.clear();
+            rc = ensure_kv(cache->k, cache->v, cache->cap_P, P, L, Hk);
+            pk = &cache->k;
+            pv = &cache->v;
+        } else {
+            rc = ensure_kv(m->tmp_k, m->tmp_v, m->tmp_cap, P, L, Hk);
+        }
+        if (rc) {
+            fill_error(err, "RESOURCE_LIMIT", db_last_error_message());
+            return -1;
+        }
+        cudaMemcpyAsync(m->ids, prefix, (size_t)P * sizeof(int32_t), cudaMemcpyHostToDevice, m->stream);
+        Pass pass;
+        pass.sk = pk->data();
+        pass.sv = pv->data();
+        pass.pool = false;
+        rc = enqueue_forward(m, P, cancel, &pass);
+        if (rc) return failed(rc);
+        if (cache && cache->prefix_cache) cache->computed += P;
+        if (keep) cache->ids.assign(prefix, prefix + P);
+    }
+    // all continuations in one batched pass after the prefix
+    cudaMemcpyAsync(m->ids, continuations, (size_t)B * T * sizeof(int32_t), cudaMemcpyHostToDevice, m->stream);
+    Pass pass;
+    pass.items = B;
+    pass.prefix = P;
+    pass.pk = pk->data();
+    pass.pv = pv->data();
+    pass.pool = false;
+    int rc = enqueue_forward(m, T, cancel, &pass);
+    if (rc) return failed(rc);
+    int flag = 0;
+    cudaMemcpyAsync(&flag, m->flag, sizeof(int), cudaMemcpyDeviceToHost, m->stream);
+    cudaMemcpyAsync(hidden, m->normed, (size_t)B * T * m->cfg.hidden * sizeof(float), cudaMemcpyDeviceToHost,
+                    m->stream);
+    const cudaError_t e = cudaStreamSynchronize(m->stream);
+    if (e != cudaSuccess) {
+        fill_error(err, "INFERENCE_FAILED", cudaGetErrorString(e));
+        return -1;
+    }
+    int word = 0;
+    cudaMemcpy(&word, m->dev_err, sizeof(int), cudaMemcpyDeviceToHost);
+    if (word) {
+        cudaMemset(m->dev_err, 0, sizeof(int));
+        fill_error(err, "INFERENCE_FAILED", "device wait expired (error word " + std::to_string(word) + ")");
+        return -1;
+    }
+    if (flag) {
+        fill_error(err, "INFERENCE_FAILED", "non-finite hidden state");
+        return -1;
+    }
+    return 0;
+}
+
+int db_cache_stats(const db_cache* c, int64_t* hits, int64_t* reused_tokens, int64_t* computed_tokens) {
+    if (!c) return DB_ERR_INVALID_ARGUMENT;
+    if (hits) *hits = c->hits;
+    if (reused_tokens) *reused_tokens = c->reused;
+    if (computed_tokens) *computed_tokens = c->computed;
+    return DB_OK;
 }
 
 }  // extern "C"

@@ -232,6 +232,7 @@ typedef struct {
     float rope_theta, eps;
     int32_t max_sequence_tokens; /* PplxParameters default (parameters.rs:81-92) */
     int32_t fused;               /* 1 = AVX2 numerics (default), 0 = portable */
+    int32_t causal;              /* 1 = decoder (causal attention; prefix caches, C5), 0 = encoder */
 } db_encoder_config;
 
 /* PplxParameters (parameters.rs:81-103): max_sequence_tokens must be positive. */
@@ -279,6 +280,22 @@ int db_predict(db_model *m, const int32_t *ids, size_t n, const db_parameters *p
 int db_predict_batch(db_model *m, const int32_t *const *ids, const size_t *lens, size_t count,
                      const db_parameters *params, db_cache *cache, const volatile uint8_t *cancel, float *outs,
                      int32_t *status, db_error *errs, db_error *err);
+
+/* Prefix-state cache and continuation batching for causal models (C5; the reference's Kev prefix
+ * reuse, kev/mod.rs:163-240, and per-question continuation from a clone of the prefix state,
+ * :245-300).  A cache made with require_prefix = 1 (causal models only; encoders answer
+ * UNSUPPORTED_CACHE) keeps the per-layer keys and values of the last prefix whose state fits in
+ * max_bytes.  db_predict_continuations runs `count` continuations of `tokens` tokens each after
+ * the prefix, batched in one pass (every continuation sees the prefix and, causally, its own
+ * tokens; the prefix is computed once, or reused when the cache holds the same ids), and writes
+ * the final-normed hidden states [count, tokens, hidden] (the Kev query/key heads on top of them
+ * are not part of this library).  prefix_len + tokens must not exceed max_sequence_tokens
+ * (INPUT_TOO_LONG).  cache may be NULL (nothing is kept). */
+int db_predict_continuations(db_model *m, db_cache *cache, const int32_t *prefix, size_t prefix_len,
+                             const int32_t *continuations, size_t count, size_t tokens,
+                             const volatile uint8_t *cancel, float *hidden, db_error *err);
+/* hits / prefix tokens reused / prefix tokens computed (kev/mod.rs Stats) */
+int db_cache_stats(const db_cache *c, int64_t *hits, int64_t *reused_tokens, int64_t *computed_tokens);
 
 /* Per-launch CUDA-event timing of the forward's kernels (the reference's projection_ms
  * accounting, cpu.rs:8-16).  Kinds 0..DB_PROF_KINDS-1, named by db_model_profile_name.

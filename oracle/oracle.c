@@ -746,6 +746,11 @@ void oracle_rope(float *x, size_t tokens, size_t heads, size_t head_dim, size_t 
 /* backbone.rs:560-600: per head, scores = scale * q k^T, softmax, P v (non-causal) */
 void oracle_attention(const float *q, const float *k, const float *v, size_t tokens, size_t q_heads,
                       size_t kv_heads, size_t head_dim, float scale, float *out) {
+    oracle_attention_masked(q, k, v, tokens, q_heads, kv_heads, head_dim, scale, 0, out);
+}
+
+void oracle_attention_masked(const float *q, const float *k, const float *v, size_t tokens, size_t q_heads,
+                             size_t kv_heads, size_t head_dim, float scale, int causal, float *out) {
     size_t per = q_heads / kv_heads;
 #pragma omp parallel
     {
@@ -755,16 +760,17 @@ void oracle_attention(const float *q, const float *k, const float *v, size_t tok
         for (size_t h = 0; h < q_heads; ++h)
             for (size_t i = 0; i < tokens; ++i) {
                 size_t kh = h / per;
+                const size_t keys = causal ? i + 1 : tokens;
                 const float *qi = q + (i * q_heads + h) * head_dim;
-                for (size_t j = 0; j < tokens; ++j) {
+                for (size_t j = 0; j < keys; ++j) {
                     const float *kj = k + (j * kv_heads + kh) * head_dim;
                     float dot = 0.f;
                     for (size_t d = 0; d < head_dim; ++d) dot = fmaf(qi[d], kj[d], dot);
                     scores[j] = scale * dot;
                 }
-                oracle_softmax(scores, tokens);
+                oracle_softmax(scores, keys);
                 for (size_t d = 0; d < head_dim; ++d) acc[d] = 0.f;
-                for (size_t j = 0; j < tokens; ++j) {
+                for (size_t j = 0; j < keys; ++j) {
                     const float *vj = v + (j * kv_heads + kh) * head_dim;
                     for (size_t d = 0; d < head_dim; ++d) acc[d] = fmaf(scores[j], vj[d], acc[d]);
                 }
@@ -891,7 +897,7 @@ int oracle_encoder_forward(void *p, const int32_t *ids, size_t T, int layers_lim
         oracle_rms(k, k, T * Hk, Dh, e->k_norm[l], c->eps, 0);
         oracle_rope(q, T, Hq, Dh, Dh, 0, c->rope_theta);
         oracle_rope(k, T, Hk, Dh, Dh, 0, c->rope_theta);
-        oracle_attention(q, k, v, T, Hq, Hk, Dh, scale, ctx);
+        oracle_attention_masked(q, k, v, T, Hq, Hk, Dh, scale, e->cfg.causal, ctx);
         project(&e->o[l], bits, abits, ctx, T, mode, proj);
         for (size_t i = 0; i < T * D; ++i) x[i] = x[i] + proj[i];
         oracle_rms(x, n, T, D, e->post_norm[l], c->eps, 0);

@@ -91,12 +91,17 @@ void oracle_rope(float *x, size_t tokens, size_t heads, size_t head_dim, size_t 
 /* non-causal GQA attention: q [T, Hq*D], k/v [T, Hkv*D] -> out [T, Hq*D] */
 void oracle_attention(const float *q, const float *k, const float *v, size_t tokens,
                       size_t q_heads, size_t kv_heads, size_t head_dim, float scale, float *out);
+/* the same with causal = 1: token i attends keys 0..i (a decoder's prefill; the continuation
+ * of a cached prefix is the tail of a causal pass over prefix + continuation) */
+void oracle_attention_masked(const float *q, const float *k, const float *v, size_t tokens, size_t q_heads,
+                             size_t kv_heads, size_t head_dim, float scale, int causal, float *out);
 
 /* ---- composed Qwen3-shaped Q4 encoder (composition of the above) ---- */
 typedef struct {
     int layers, hidden, q_heads, kv_heads, head_dim, ffn, vocab;
     int weight_bits, activation_bits;
     float rope_theta, eps;
+    int causal; /* 1: decoder (causal attention) */
 } oracle_encoder_config;
 
 /* Weights as bf16 [out,in] per projection (reference "[output,input]" order).  Per layer:

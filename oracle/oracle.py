@@ -82,6 +82,7 @@ def _declare(l):
     l.oracle_softmax.argtypes = [_f, _sz]
     l.oracle_rope.argtypes = [_f, _sz, _sz, _sz, _sz, _sz, C.c_float]
     l.oracle_attention.argtypes = [_f, _f, _f, _sz, _sz, _sz, _sz, C.c_float, _f]
+    l.oracle_attention_masked.argtypes = [_f, _f, _f, _sz, _sz, _sz, _sz, C.c_float, C.c_int, _f]
     l.oracle_encoder_create.restype = C.c_void_p
     l.oracle_encoder_create.argtypes = [C.c_void_p, C.c_void_p]
     l.oracle_encoder_destroy.argtypes = [C.c_void_p]
@@ -355,7 +356,7 @@ def attention(q, k, v, q_heads, kv_heads, head_dim, scale=None):
 class _Cfg(C.Structure):
     _fields_ = [("layers", C.c_int), ("hidden", C.c_int), ("q_heads", C.c_int), ("kv_heads", C.c_int),
                 ("head_dim", C.c_int), ("ffn", C.c_int), ("vocab", C.c_int), ("weight_bits", C.c_int),
-                ("activation_bits", C.c_int), ("rope_theta", C.c_float), ("eps", C.c_float)]
+                ("activation_bits", C.c_int), ("rope_theta", C.c_float), ("eps", C.c_float), ("causal", C.c_int)]
 
 
 class _W(C.Structure):
@@ -377,7 +378,7 @@ class Encoder:
         self.cfg = cfg
         c = _Cfg(cfg["layers"], cfg["hidden"], cfg["q_heads"], cfg["kv_heads"], cfg["head_dim"], cfg["ffn"],
                  cfg["vocab"], cfg.get("weight_bits", 4), cfg.get("activation_bits", 8),
-                 cfg.get("rope_theta", 1e6), cfg.get("eps", 1e-6))
+                 cfg.get("rope_theta", 1e6), cfg.get("eps", 1e-6), int(cfg.get("causal", 0)))
         keep = []
 
         def arr(a, dt):
