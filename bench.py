@@ -454,6 +454,45 @@ def run_decima(args, local_rank):
                       "cases": cases}), flush=True)
 
 
+def run_c5(args, local_rank):
+    """C5 (Qwen3-4B-shaped decoder: 36 layers, D=2560, 32q/8kv x 128, FF 9728, Q4 g64, synthetic
+    weights): requests of a 512-token prefix and 4 continuations of 32 tokens.  Each request runs
+    the causal prefix pass once (keys/values kept per layer) and the 4 continuations batched after
+    it, through the public db_predict_continuations call (host ids in, host hidden states out).
+    Requests have distinct prefixes, so nothing is reused across them; a second timing repeats one
+    prefix to show the cached path."""
+    import torch
+
+    import decisive_b200 as db
+    torch.cuda.set_device(local_rank)
+    cfg = db.EncoderConfig(layers=36, hidden=2560, q_heads=32, kv_heads=8, head_dim=128, ffn=9728, vocab=151936,
+                           weight_bits=4, max_sequence_tokens=1024, causal=True)
+    model = db.Model.synthetic(cfg, seed=SEED, std=0.02, device=local_rank)
+    rng = np.random.default_rng(5)
+    n_req = max(args.steps, 1)
+    prefixes = rng.integers(0, cfg.vocab, (n_req + args.warmup, 512)).astype(np.int32)
+    conts = rng.integers(0, cfg.vocab, (n_req + args.warmup, 4, 32)).astype(np.int32)
+    cache = model.create_cache(db.CacheOptions(max_bytes=256 << 20, require_prefix=True))
+    for i in range(args.warmup):
+        model.predict_continuations(prefixes[n_req + i], conts[n_req + i], cache=cache)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for i in range(n_req):
+        model.predict_continuations(prefixes[i], conts[i], cache=cache)
+    dt = time.perf_counter() - t0
+    t1 = time.perf_counter()
+    for i in range(n_req):
+        model.predict_continuations(prefixes[0], conts[i], cache=cache)  # same prefix: reused
+    dt_hit = time.perf_counter() - t1
+    tokens = 512 + 4 * 32
+    print(json.dumps({"workload": "C5 decoder Q4 (36L, D=2560, 32q/8kv, FF 9728): 512-token prefix + 4 x 32 continuations",
+                      "requests": n_req, "requests_per_s": n_req / dt, "tokens_per_s": n_req * tokens / dt,
+                      "ms_per_request": dt / n_req * 1e3, "ms_per_request_prefix_cached": dt_hit / n_req * 1e3,
+                      "cache": cache.stats(), "timing": "host wall clock around the public call (ids in, hidden out)",
+                      "data": "synthetic (seeded N(0,0.02) bf16 weights, uniform token ids)"}), flush=True)
+    model.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -463,7 +502,7 @@ def main():
     ap.add_argument("--cpu-layers", type=int, default=2)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-tune", action="store_true", help="skip kernel selection (default tile configurations)")
-    ap.add_argument("--workload", default="encoder", choices=["encoder", "gemm", "gemv", "decima"])
+    ap.add_argument("--workload", default="encoder", choices=["encoder", "gemm", "gemv", "decima", "c5"])
     ap.add_argument("--gemv-rows", default="1,4,8", help="activation rows (M) for --workload gemv")
     ap.add_argument("--gemm-shape", default="1024,1024,3072", help="M,K,N for --workload gemm")
     ap.add_argument("--bits", type=int, default=4)
@@ -477,6 +516,8 @@ def main():
         run_gemv(args, local_rank)
     elif args.workload == "decima":
         run_decima(args, local_rank)
+    elif args.workload == "c5":
+        run_c5(args, local_rank)
     elif args.impl == "reference":
         run_reference(args, rank)
     else:
