@@ -5,6 +5,7 @@
 #include <float.h>
 
 #include "common.cuh"
+#include "kernels.h"
 #include "layer_ops.h"
 
 namespace db {
@@ -278,11 +279,9 @@ int db_launch_attention(const __half* q16, const __half* k16, const __half* v16,
     if (T <= 0) return 0;
     if (Hk <= 0 || Hq % Hk) return (int)cudaErrorInvalidValue;
     const int smem = 5 * ATT_TILE_BYTES;
-    static bool configured = false;
-    if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(attention_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    {
+        const cudaError_t e = db_set_max_smem(reinterpret_cast<const void*>(attention_kernel<false>), smem);
         if (e != cudaSuccess) return (int)e;
-        configured = true;
     }
     dim3 grid((T + ATT_BQ - 1) / ATT_BQ, Hq);
     attention_kernel<false><<<grid, ATT_THREADS, smem, stream>>>(q16, k16, v16, T, Hq, Hk, scale * 1.4426950408889634f,
@@ -297,11 +296,9 @@ int db_launch_attention_quant(const __half* q16, const __half* k16, const __half
     if (T <= 0) return 0;
     if (Hk <= 0 || Hq % Hk || !codes || !scales || !nonfinite || (ldc & 7)) return (int)cudaErrorInvalidValue;
     const int smem = 5 * ATT_TILE_BYTES;
-    static bool configured = false;
-    if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(attention_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    {
+        const cudaError_t e = db_set_max_smem(reinterpret_cast<const void*>(attention_kernel<true>), smem);
         if (e != cudaSuccess) return (int)e;
-        configured = true;
     }
     dim3 grid((T + ATT_BQ - 1) / ATT_BQ, Hq);
     attention_kernel<true><<<grid, ATT_THREADS, smem, stream>>>(q16, k16, v16, T, Hq, Hk, scale * 1.4426950408889634f,
@@ -319,11 +316,9 @@ int db_launch_attention_prefix_quant(const __half* q16, const __half* k16, const
         B > 65535)
         return (int)cudaErrorInvalidValue;
     const int smem = 5 * ATT_TILE_BYTES;
-    static bool configured = false;
-    if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(attention_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    {
+        const cudaError_t e = db_set_max_smem(reinterpret_cast<const void*>(attention_kernel<true>), smem);
         if (e != cudaSuccess) return (int)e;
-        configured = true;
     }
     dim3 grid((T + ATT_BQ - 1) / ATT_BQ, Hq, B);
     attention_kernel<true><<<grid, ATT_THREADS, smem, stream>>>(q16, k16, v16, T, Hq, Hk, scale * 1.4426950408889634f,

@@ -30,6 +30,19 @@ int db_cuda_status(int e, const char* what) {
     return db_fail(DB_ERR_CUDA, "CUDA_ERROR", std::string(what) + ": " + cudaGetErrorString((cudaError_t)e));
 }
 
+cudaError_t db_set_max_smem(const void* kernel, int bytes) {
+    static std::mutex mu;
+    static std::vector<std::pair<const void*, int>> done;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lock(mu);
+    for (const auto& d : done)
+        if (d.first == kernel && d.second == dev) return cudaSuccess;
+    const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess) done.emplace_back(kernel, dev);
+    return e;
+}
+
 int* db_device_error_ptr() {
     static std::mutex mu;
     static std::vector<int*> words;

@@ -863,11 +863,9 @@ static int launch_variant(const DbGemmArgs& a, const CUtensorMap& tmA, const CUt
                           const CUtensorMap& tmY, int y_tma, int G, cudaStream_t stream) {
     using S = GemmSmem<BN, BITS, EPI, PAIR, SUB>;
     auto kernel = gemm_tc_kernel<BN, BITS, EPI, FUSED, PAIR, SUB>;
-    static bool configured = false;
-    if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S::BYTES);
+    {
+        const cudaError_t e = db_set_max_smem(reinterpret_cast<const void*>(kernel), S::BYTES);
         if (e != cudaSuccess) return (int)e;
-        configured = true;
     }
     constexpr int MT = PAIR ? 2 * BM : BM;
     const int tiles = ((a.M + MT - 1) / MT) * ((a.N + BN - 1) / BN);

@@ -186,12 +186,10 @@ __global__ void __launch_bounds__(GEMV_MAX_THREADS)
 template <int BITS, int MR, bool FUSED, bool RESIDUAL>
 static int launch_mr(const DbGemvArgs& a, int G, cudaStream_t s) {
     auto kernel = gemv_kernel<BITS, MR, FUSED, RESIDUAL>;
-    static bool configured = false;
-    if (!configured) {
+    {
         const int max_bytes = (GEMV_ROWS * MR + GEMV_ROWS + 2 * MR) * GEMV_MAX_GROUPS * 4;
-        const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, max_bytes);
+        const cudaError_t e = db_set_max_smem(reinterpret_cast<const void*>(kernel), max_bytes);
         if (e != cudaSuccess) return (int)e;
-        configured = true;
     }
     const size_t bytes = (size_t)(GEMV_ROWS * MR + GEMV_ROWS + 2 * MR) * G * 4;
     dim3 grid((a.N + GEMV_ROWS - 1) / GEMV_ROWS);

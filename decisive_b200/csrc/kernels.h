@@ -87,3 +87,7 @@ int db_launch_gemv(const DbGemvArgs& args, cudaStream_t stream);
 int db_gemv_rows_limit();
 
 int db_num_sms();
+// Raises a kernel's dynamic shared-memory limit once per (kernel, device): function attributes
+// belong to a device's context, so a process that drives several GPUs sets them on each.
+// Thread-safe.
+cudaError_t db_set_max_smem(const void* kernel, int bytes);

@@ -148,3 +148,18 @@ def test_predictions_are_deterministic(db, small_model):
     a = small_model.predict(ids).response
     b = small_model.predict(ids).response
     assert np.array_equal(a, b)
+
+
+def test_models_on_two_devices_in_one_process(db):
+    """One model per device from one process (the multi-GPU integration without collectives):
+    every kernel's launch settings are made per device."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    cfg = db.EncoderConfig(**SMALL, weight_bits=4, max_sequence_tokens=256)
+    a = db.Model.synthetic(cfg, seed=4, device=0)
+    b = db.Model.synthetic(cfg, seed=4, device=1)
+    ids = np.random.default_rng(0).integers(0, SMALL["vocab"], 200).astype(np.int32)
+    ra, rb = np.asarray(a.predict(ids).response), np.asarray(b.predict(ids).response)
+    assert np.array_equal(ra.view(np.uint32), rb.view(np.uint32))
+    a.close()
+    b.close()
