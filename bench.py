@@ -229,6 +229,8 @@ def run_ours(args, rank, world, local_rank):
     model = db.Model.synthetic(cfg, seed=SEED, std=0.02, device=local_rank)
     # kernel selection (bitwise-equal tile configurations, fastest by >= 1 %), before any timing
     tuning = None if args.no_tune else {k: v["choice"] for k, v in model.tune(TOKENS).items()}
+    if args.stream:
+        model.set_streaming(True)  # weights in pinned host memory, two layers on the device
     rng = np.random.default_rng(SEED + rank)
     ids_host = torch.from_numpy(rng.integers(0, CFG["vocab"], TOKENS).astype(np.int32)).pin_memory()
     ids_dev = ids_host.cuda()
@@ -312,6 +314,7 @@ def run_ours(args, rank, world, local_rank):
                              "launches": gemm_launches, "avg_launch_us": gemm_ms / gemm_launches * 1e3,
                              "flops_per_launch": gemm_flops / gemm_launches},
                 "kernel_ms_per_step": {k: v[0] / args.steps for k, v in prof.items()},
+                "weights": "streamed: pinned host memory -> two device banks" if args.stream else "resident in HBM",
                 "tile_configs": tuning}
         if world == 1 and not args.no_cpu:
             cpu_v, info = cpu_sample(0, layers=args.cpu_layers, full_budget_s=30.0)
@@ -502,6 +505,8 @@ def main():
     ap.add_argument("--cpu-layers", type=int, default=2)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-tune", action="store_true", help="skip kernel selection (default tile configurations)")
+    ap.add_argument("--stream", action="store_true",
+                    help="stream layer weights from pinned host memory through two device banks")
     ap.add_argument("--workload", default="encoder", choices=["encoder", "gemm", "gemv", "decima", "c5"])
     ap.add_argument("--gemv-rows", default="1,4,8", help="activation rows (M) for --workload gemv")
     ap.add_argument("--gemm-shape", default="1024,1024,3072", help="M,K,N for --workload gemm")

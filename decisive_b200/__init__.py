@@ -512,6 +512,12 @@ class Model:
             raise Error._from(err)
         return cls(h, config)
 
+    def set_streaming(self, enable: bool = True):
+        """Two-bank layer streaming: weights in pinned host memory, two layers on the device."""
+        err = _lib.DbError()
+        if load().db_model_set_streaming(self._h, int(enable), C.byref(err)):
+            raise Error._from(err)
+
     def export_packed(self, directory: str) -> str:
         """Writes this model's weights as a packed checkpoint into directory; returns the manifest path."""
         import os

@@ -88,6 +88,7 @@ SIGNATURES = [
     ("db_cache_stats", _i32, [_vp, _vp, _vp, _vp]),
     ("db_model_profile", _i32, [_vp, _i32]),
     ("db_model_export_packed", _i32, [_vp, C.c_char_p, C.POINTER(DbError)]),
+    ("db_model_set_streaming", _i32, [_vp, _i32, C.POINTER(DbError)]),
     ("db_model_create_packed", _vp, [_i32, C.POINTER(EncoderConfig), C.c_char_p, _i32, C.POINTER(DbError)]),
     ("db_model_tune", _i32, [_vp, _i64, C.c_char_p, C.c_char_p, _sz, C.POINTER(DbError)]),
     ("db_model_profile_read", _i32, [_vp, _vp, _vp, _i32, _i32]),

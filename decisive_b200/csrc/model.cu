@@ -66,6 +66,17 @@ struct db_model {
     std::vector<void*> ws_allocations;
     int rope_T = 0;  // positions covered by the RoPE tables
     std::vector<void*> rope_allocations;
+    // layer streaming (the reference's two-bank scheme, webgpu/streaming.rs): the projection weights
+    // of every layer live in pinned host memory and are copied into one of two device banks on a
+    // copy stream while the other bank's layer computes
+    bool streaming = false;
+    struct Span { size_t off, bytes; };
+    std::vector<uint8_t*> host_layers;   // pinned, one block per layer
+    std::vector<Span> spans;              // qkv_c, qkv_s, o_c, o_s, gu_c, gu_s, dn_c, dn_s inside a block
+    size_t layer_bytes = 0;
+    uint8_t* banks[2] = {nullptr, nullptr};
+    cudaStream_t copy_stream = nullptr;
+    cudaEvent_t uploaded[2] = {nullptr, nullptr}, consumed[2] = {nullptr, nullptr};
     // per-layer prefix keys/values of a continuation call whose cache cannot keep them
     std::vector<__half*> tmp_k, tmp_v;
     int tmp_cap = 0;
@@ -355,9 +366,36 @@ int enqueue_forward(db_model* m, int T, const volatile uint8_t* cancel, const Pa
     const float attn_scale = 1.f / sqrtf((float)c.head_dim);
     auto own_k = [&](int l) { return pass && pass->sk ? pass->sk[l] : m->k16; };
     auto own_v = [&](int l) { return pass && pass->sv ? pass->sv[l] : m->v16; };
+    // streaming: layer l computes from bank l % 2; the upload of layer l + 2 into that bank waits
+    // for layer l's last kernel (the copy stream and the compute stream meet only at events)
+    auto upload = [&](int l) {
+        const int b = l & 1;
+        cudaStreamWaitEvent(m->copy_stream, m->consumed[b], 0);
+        cudaMemcpyAsync(m->banks[b], m->host_layers[l], m->layer_bytes, cudaMemcpyHostToDevice, m->copy_stream);
+        cudaEventRecord(m->uploaded[b], m->copy_stream);
+    };
+    auto bank_layer = [&](int l) {
+        LayerW w = m->layers[l];  // norms stay resident
+        uint8_t* base = m->banks[l & 1];
+        auto at = [&](int i) { return base + m->spans[i].off; };
+        w.qkv_c = at(0);
+        w.qkv_s = reinterpret_cast<float*>(at(1));
+        w.o_c = at(2);
+        w.o_s = reinterpret_cast<float*>(at(3));
+        w.gu_c = at(4);
+        w.gu_s = reinterpret_cast<float*>(at(5));
+        w.dn_c = at(6);
+        w.dn_s = reinterpret_cast<float*>(at(7));
+        return w;
+    };
+    if (m->streaming) {
+        upload(0);
+        if (c.layers > 1) upload(1);
+    }
     for (int l = 0; l < c.layers && !rc; ++l) {
         if (cancel && *cancel) return 1;
-        const LayerW& w = m->layers[l];
+        if (m->streaming) cudaStreamWaitEvent(st, m->uploaded[l & 1], 0);
+        const LayerW w = m->streaming ? bank_layer(l) : m->layers[l];
         rc = timed(1, [&] {
             return db_launch_rms_quantize(m->x, D, w.in_norm, R, D, c.eps, 0, nullptr, 0, m->acodes, DB_CODES_TC,
                                           ld_codes, m->sa, nullptr, lds, m->flag, st);
@@ -413,6 +451,10 @@ int enqueue_forward(db_model* m, int T, const volatile uint8_t* cancel, const Pa
             g.pair_ctas = m->tuned[3].pair_ctas;
             return db_launch_gemm_tc(g, st);
         });
+        if (m->streaming) {
+            cudaEventRecord(m->consumed[l & 1], st);
+            if (l + 2 < c.layers) upload(l + 2);
+        }
     }
     if (!rc)
         rc = timed(9, [&] {
@@ -672,6 +714,13 @@ void db_model_destroy(db_model* m) {
     m->free_all(m->ws_allocations);
     m->free_all(m->rope_allocations);
     m->free_all(m->allocations);
+    for (uint8_t* h : m->host_layers) cudaFreeHost(h);
+    for (uint8_t* b : m->banks) cudaFree(b);
+    for (int i = 0; i < 2; ++i) {
+        if (m->uploaded[i]) cudaEventDestroy(m->uploaded[i]);
+        if (m->consumed[i]) cudaEventDestroy(m->consumed[i]);
+    }
+    if (m->copy_stream) cudaStreamDestroy(m->copy_stream);
     for (__half* p : m->tmp_k) cudaFree(p);
     for (__half* p : m->tmp_v) cudaFree(p);
     if (m->stream) cudaStreamDestroy(m->stream);
@@ -834,6 +883,10 @@ int db_model_export_packed(db_model* m, const char* directory, db_error* err) {
         fill_error(err, "INVALID_PARAMETERS", "null model or directory");
         return DB_ERR_INVALID_ARGUMENT;
     }
+    if (m->streaming) {
+        fill_error(err, "INVALID_PARAMETERS", "export needs resident weights (streaming is on)");
+        return DB_ERR_INVALID_ARGUMENT;
+    }
     cudaSetDevice(m->device);
     const int D = m->D(), L = m->cfg.layers, F = m->F(), Nq = m->Nq(), Nk = m->Nk(), bits = m->cfg.weight_bits;
     const size_t gb = group_bytes(bits);
@@ -951,6 +1004,91 @@ db_model* db_model_create_packed(int device, const db_encoder_config* cfg, const
         return nullptr;
     }
     return m;
+}
+
+int db_model_set_streaming(db_model* m, int enable, db_error* err) {
+    if (!m) {
+        fill_error(err, "INVALID_PARAMETERS", "null model");
+        return DB_ERR_INVALID_ARGUMENT;
+    }
+    cudaSetDevice(m->device);
+    cudaStreamSynchronize(m->stream);
+    if ((enable != 0) == m->streaming) return DB_OK;
+    const int L = m->cfg.layers, D = m->D(), F = m->F(), Nq = m->Nq(), bits = m->cfg.weight_bits;
+    const size_t G = (size_t)D / 64;
+    // the eight projection buffers of a layer, in bank order
+    const size_t sizes[8] = {(size_t)m->Nqkv() * D * bits / 8, G * db_scale_stride(m->Nqkv()) * 4,
+                             (size_t)D * Nq * bits / 8,           (size_t)(Nq / 64) * db_scale_stride(D) * 4,
+                             (size_t)2 * F * D * bits / 8,        G * db_scale_stride(2 * F) * 4,
+                             (size_t)D * F * bits / 8,            (size_t)(F / 64) * db_scale_stride(D) * 4};
+    auto fail = [&](const char* what) {
+        fill_error(err, "RESOURCE_LIMIT", what);
+        return DB_ERR_CUDA;
+    };
+    if (enable) {
+        m->spans.clear();
+        size_t off = 0;
+        for (size_t b : sizes) {
+            m->spans.push_back({off, b});
+            off += (b + 1023) / 1024 * 1024;
+        }
+        m->layer_bytes = off;
+        if (cudaMalloc(&m->banks[0], off) != cudaSuccess || cudaMalloc(&m->banks[1], off) != cudaSuccess)
+            return fail("streaming banks exceed device limits");
+        if (!m->copy_stream && cudaStreamCreateWithFlags(&m->copy_stream, cudaStreamNonBlocking) != cudaSuccess)
+            return fail("copy stream");
+        for (int i = 0; i < 2; ++i) {
+            if (!m->uploaded[i]) cudaEventCreateWithFlags(&m->uploaded[i], cudaEventDisableTiming);
+            if (!m->consumed[i]) cudaEventCreateWithFlags(&m->consumed[i], cudaEventDisableTiming);
+            cudaEventRecord(m->consumed[i], m->stream);  // the banks start free
+        }
+        m->host_layers.assign(L, nullptr);
+        for (int l = 0; l < L; ++l) {
+            if (cudaMallocHost(&m->host_layers[l], off) != cudaSuccess) return fail("pinned host memory");
+            LayerW& w = m->layers[l];
+            const void* src[8] = {w.qkv_c, w.qkv_s, w.o_c, w.o_s, w.gu_c, w.gu_s, w.dn_c, w.dn_s};
+            for (int i = 0; i < 8; ++i)
+                cudaMemcpy(m->host_layers[l] + m->spans[i].off, src[i], sizes[i], cudaMemcpyDeviceToHost);
+        }
+        // release the resident copies: only the two banks stay on the device
+        for (int l = 0; l < L; ++l) {
+            LayerW& w = m->layers[l];
+            void* ptrs[8] = {w.qkv_c, w.qkv_s, w.o_c, w.o_s, w.gu_c, w.gu_s, w.dn_c, w.dn_s};
+            for (void* p : ptrs) {
+                auto it = std::find(m->allocations.begin(), m->allocations.end(), p);
+                if (it != m->allocations.end()) {
+                    cudaFree(p);
+                    m->allocations.erase(it);
+                }
+            }
+            w.qkv_c = w.o_c = w.gu_c = w.dn_c = nullptr;
+            w.qkv_s = w.o_s = w.gu_s = w.dn_s = nullptr;
+        }
+        m->streaming = true;
+        return DB_OK;
+    }
+    // back to resident weights
+    for (int l = 0; l < L; ++l) {
+        LayerW& w = m->layers[l];
+        uint8_t* dst[8];
+        for (int i = 0; i < 8; ++i) {
+            if (m->alloc(&dst[i], sizes[i], m->allocations)) return fail("weight allocation exceeds device limits");
+            cudaMemcpy(dst[i], m->host_layers[l] + m->spans[i].off, sizes[i], cudaMemcpyHostToDevice);
+        }
+        w.qkv_c = dst[0]; w.qkv_s = reinterpret_cast<float*>(dst[1]);
+        w.o_c = dst[2];   w.o_s = reinterpret_cast<float*>(dst[3]);
+        w.gu_c = dst[4];  w.gu_s = reinterpret_cast<float*>(dst[5]);
+        w.dn_c = dst[6];  w.dn_s = reinterpret_cast<float*>(dst[7]);
+    }
+    cudaStreamSynchronize(m->copy_stream);
+    for (uint8_t* h : m->host_layers) cudaFreeHost(h);
+    m->host_layers.clear();
+    for (uint8_t*& b : m->banks) {
+        cudaFree(b);
+        b = nullptr;
+    }
+    m->streaming = false;
+    return DB_OK;
 }
 
 }  // extern "C"

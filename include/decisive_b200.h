@@ -325,6 +325,14 @@ int db_model_export_packed(db_model *m, const char *directory, db_error *err);
 db_model *db_model_create_packed(int device, const db_encoder_config *cfg, const char *manifest_path, int verify,
                                  db_error *err);
 
+/* Layer streaming (the reference's two-bank scheme, webgpu/streaming.rs): with enable = 1 every
+ * layer's projection weights move to pinned host memory and only two device banks remain; each
+ * forward copies layer l + 2 into the bank of layer l on a copy stream as soon as layer l's last
+ * kernel has run, so uploads overlap compute and at most two layers are on the device.  Results
+ * are bit-identical to resident weights.  enable = 0 makes the weights resident again.  Export
+ * needs resident weights. */
+int db_model_set_streaming(db_model *m, int enable, db_error *err);
+
 /* Device-resident variant for throughput measurement/* Device-resident variant for throughput measurement: ids already on the device, output left on
  * the device; no host synchronisation.  Used by bench.py's device-timed leg. */
 int db_forward_device(db_model *m, const int32_t *ids_dev, int64_t n, float *out_dev, void *stream);

@@ -103,3 +103,26 @@ def test_corrupt_or_mismatched_checkpoints_are_rejected(db, tmp_path):
     assert e.value.code == "INVALID_WEIGHTS"
     with pytest.raises(db.Error):
         db.Model.from_packed(cfg, str(tmp_path / "missing.json"))
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+def test_layer_streaming_is_bit_identical(db, tmp_path, bits):
+    """Two-bank layer streaming (webgpu/streaming.rs scheme): weights in pinned host memory, each
+    layer copied on a copy stream while the previous one computes; outputs equal resident ones."""
+    cfg = db.EncoderConfig(layers=5, hidden=256, q_heads=4, kv_heads=2, head_dim=128, ffn=512, vocab=1000,
+                           weight_bits=bits, max_sequence_tokens=256)
+    m = db.Model.synthetic(cfg, seed=21)
+    rng = np.random.default_rng(3)
+    reqs = [rng.integers(0, 1000, n).tolist() for n in (1, 64, 256, 77)]
+    want = [np.asarray(m.predict(r).response).copy() for r in reqs]
+    m.set_streaming(True)
+    for _ in range(2):  # consecutive forwards reuse the banks
+        got = [np.asarray(m.predict(r).response).copy() for r in reqs]
+        for a, b in zip(want, got):
+            assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    with pytest.raises(db.Error):
+        m.export_packed(str(tmp_path))
+    m.set_streaming(False)
+    got = np.asarray(m.predict(reqs[2]).response)
+    assert np.array_equal(want[2].view(np.uint32), got.view(np.uint32))
+    m.close()
