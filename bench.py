@@ -496,6 +496,35 @@ def run_c5(args, local_rank):
     model.close()
 
 
+def run_c4(args, local_rank):
+    """C4 (Decima-shaped BERT encoder: 12 layers, D=768, 12 heads, FF 3072, vocab 128100, W8A8 in
+    blocks of 32, synthetic weights): sequences of 384 + U(16..48) tokens (8 per request), one
+    db_bert_predict call each (host ids in, pooled state out), host wall clock."""
+    import torch
+
+    import decisive_b200 as db
+    torch.cuda.set_device(local_rank)
+    cfg = db.BertConfig(layers=12, hidden=768, heads=12, ffn=3072, vocab=128100, max_positions=512, block=32)
+    model = db.BertModel(cfg, seed=SEED, std=0.02, device=local_rank)
+    rng = np.random.default_rng(4)
+    n_seq = 8 * max(args.steps, 1)
+    seqs = [rng.integers(0, cfg.vocab, 384 + int(rng.integers(16, 49))).astype(np.int32) for _ in range(n_seq)]
+    for s_ in seqs[:max(args.warmup, 1)]:
+        model.predict(s_)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for s_ in seqs:
+        model.predict(s_)
+    dt = time.perf_counter() - t0
+    tokens = sum(len(s_) for s_ in seqs)
+    print(json.dumps({"workload": "C4 Decima-shaped encoder (12L, D=768, FF 3072), W8A8 block 32, 8 x (384 + U(16..48)) tokens per request",
+                      "sequences": n_seq, "tokens_per_s": tokens / dt, "requests_per_s": n_seq / 8 / dt,
+                      "ms_per_sequence": dt / n_seq * 1e3,
+                      "timing": "host wall clock around the public call (ids in, pooled state out)",
+                      "data": "synthetic (seeded N(0,0.02) bf16 weights, uniform token ids)"}), flush=True)
+    model.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -507,7 +536,7 @@ def main():
     ap.add_argument("--no-tune", action="store_true", help="skip kernel selection (default tile configurations)")
     ap.add_argument("--stream", action="store_true",
                     help="stream layer weights from pinned host memory through two device banks")
-    ap.add_argument("--workload", default="encoder", choices=["encoder", "gemm", "gemv", "decima", "c5"])
+    ap.add_argument("--workload", default="encoder", choices=["encoder", "gemm", "gemv", "decima", "c5", "c4"])
     ap.add_argument("--gemv-rows", default="1,4,8", help="activation rows (M) for --workload gemv")
     ap.add_argument("--gemm-shape", default="1024,1024,3072", help="M,K,N for --workload gemm")
     ap.add_argument("--bits", type=int, default=4)
@@ -523,6 +552,8 @@ def main():
         run_decima(args, local_rank)
     elif args.workload == "c5":
         run_c5(args, local_rank)
+    elif args.workload == "c4":
+        run_c4(args, local_rank)
     elif args.impl == "reference":
         run_reference(args, rank)
     else:

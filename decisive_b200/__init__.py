@@ -541,3 +541,54 @@ class Model:
     def forward_device(self, ids_dev, out_dev, stream=None):
         """Device-resident forward (no host synchronisation) used for device-timed measurement."""
         check(load().db_forward_device(self._h, _ptr(ids_dev), ids_dev.numel(), _ptr(out_dev), _stream(stream)))
+
+
+@dataclass
+class BertConfig:
+    """C4: the Decima-shaped (BERT) encoder on the Decima int8 kernels (db_bert_*)."""
+    layers: int = 12
+    hidden: int = 768
+    heads: int = 12
+    ffn: int = 3072
+    vocab: int = 128100
+    max_positions: int = 512
+    block: int = 32
+    eps: float = 1e-12
+    fused: bool = True
+
+    def c(self) -> _lib.BertConfig:
+        return _lib.BertConfig(self.layers, self.hidden, self.heads, self.ffn, self.vocab, self.max_positions,
+                               self.block, self.eps, int(self.fused))
+
+
+class BertModel:
+    """Synthetic-weight C4 encoder; predict returns (mean-pooled [hidden], states [n, hidden])."""
+
+    def __init__(self, config: BertConfig, seed: int = 0, std: float = 0.02, device: int = 0):
+        err = _lib.DbError()
+        cfg = config.c()
+        self._h = load().db_bert_create_synthetic(device, C.byref(cfg), seed, std, C.byref(err))
+        if not self._h:
+            raise Error._from(err)
+        self.config, self.seed, self.std = config, seed, std
+
+    def predict(self, ids, hidden: bool = False):
+        import numpy as np
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        pooled = np.empty(self.config.hidden, np.float32)
+        h = np.empty((ids.size, self.config.hidden), np.float32) if hidden else None
+        err = _lib.DbError()
+        rc = load().db_bert_predict(self._h, ids.ctypes.data_as(C.c_void_p), ids.size,
+                                    pooled.ctypes.data_as(C.c_void_p),
+                                    h.ctypes.data_as(C.c_void_p) if h is not None else None, C.byref(err))
+        if rc:
+            raise Error._from(err)
+        return (pooled, h) if hidden else pooled
+
+    def close(self):
+        if getattr(self, "_h", None):
+            load().db_bert_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()

@@ -26,6 +26,12 @@ class EncoderConfig(C.Structure):
                 ("fused", C.c_int32), ("causal", C.c_int32)]
 
 
+class BertConfig(C.Structure):
+    _fields_ = [("layers", C.c_int32), ("hidden", C.c_int32), ("heads", C.c_int32), ("ffn", C.c_int32),
+                ("vocab", C.c_int32), ("max_positions", C.c_int32), ("block", C.c_int32), ("eps", C.c_float),
+                ("fused", C.c_int32)]
+
+
 class Parameters(C.Structure):
     _fields_ = [("max_sequence_tokens", C.c_int32)]
 
@@ -84,6 +90,9 @@ SIGNATURES = [
     ("db_predict_batch", _i32, [_vp, _vp, _vp, _sz, C.POINTER(Parameters), _vp, _vp, _vp, _vp, _vp,
                                 C.POINTER(DbError)]),
     ("db_forward_device", _i32, [_vp, _vp, _i64, _vp, _vp]),
+    ("db_bert_create_synthetic", _vp, [_i32, C.POINTER(BertConfig), C.c_uint64, _f, C.POINTER(DbError)]),
+    ("db_bert_destroy", None, [_vp]),
+    ("db_bert_predict", _i32, [_vp, _vp, _sz, _vp, _vp, C.POINTER(DbError)]),
     ("db_predict_continuations", _i32, [_vp, _vp, _vp, _sz, _vp, _sz, _sz, _vp, _vp, C.POINTER(DbError)]),
     ("db_cache_stats", _i32, [_vp, _vp, _vp, _vp]),
     ("db_model_profile", _i32, [_vp, _i32]),

@@ -281,6 +281,24 @@ int db_predict_batch(db_model *m, const int32_t *const *ids, const size_t *lens,
                      const db_parameters *params, db_cache *cache, const volatile uint8_t *cancel, float *outs,
                      int32_t *status, db_error *errs, db_error *err);
 
+/* ---- C4: the Decima-shaped (BERT) encoder on the Decima int8 kernels (decima/mod.rs:492-556):
+ * x = LN(word[id] + type[0] + pos[p]); per layer x = LN(x + Wo attn(qkv) + bo),
+ * x = LN(x + W2 gelu(W1 x + b1) + b2); every projection W8A8 in blocks of `block` (32 or 64) with
+ * the Decima quantiser; heads of hidden/heads <= 128 dims, non-causal attention scaled by
+ * 1/sqrt(head dim); erf GELU; LayerNorm eps `eps`.  Synthetic weights (db_synthetic_bf16 keys:
+ * word 0, pos 1, type 2; layer l: 16 + 16 l + {q 0, k 1, v 2, o 3, ff1 4, ff2 5, bq 6, bk 7, bv 8,
+ * bo 9, b1 10, b2 11}; LayerNorm weights 1, biases 0).  db_bert_predict writes the mean-pooled
+ * state [hidden] and, when hidden != NULL, the final states [n, hidden]. */
+typedef struct {
+    int32_t layers, hidden, heads, ffn, vocab, max_positions, block;
+    float eps;
+    int32_t fused; /* 1 = AVX2 accumulation order (default), 0 = portable */
+} db_bert_config;
+typedef struct db_bert db_bert;
+db_bert *db_bert_create_synthetic(int device, const db_bert_config *cfg, uint64_t seed, float std, db_error *err);
+void db_bert_destroy(db_bert *m);
+int db_bert_predict(db_bert *m, const int32_t *ids, size_t n, float *pooled, float *hidden, db_error *err);
+
 /* Prefix-state cache and continuation batching for causal models (C5; the reference's Kev prefix
  * reuse, kev/mod.rs:163-240, and per-question continuation from a clone of the prefix state,
  * :245-300).  A cache made with require_prefix = 1 (causal models only; encoders answer

@@ -988,6 +988,24 @@ void oracle_decima_apply_w8a8(const int8_t *w_codes, const float *w_scales, size
     free(sa);
 }
 
+void oracle_layer_norm(float *x, size_t rows, size_t d, const float *w, const float *b, float eps) {
+    for (size_t r = 0; r < rows; ++r) {
+        float *row = x + r * d;
+        float sum = 0.f;
+        for (size_t i = 0; i < d; ++i) sum += row[i];
+        const float mean = sum / (float)d;
+        float var = 0.f;
+        for (size_t i = 0; i < d; ++i) var += (row[i] - mean) * (row[i] - mean);
+        var /= (float)d;
+        const float inv = 1.f / sqrtf(var + eps);
+        for (size_t i = 0; i < d; ++i) row[i] = (row[i] - mean) * inv * w[i] + b[i];
+    }
+}
+
+void oracle_gelu(float *x, size_t n) {
+    for (size_t i = 0; i < n; ++i) x[i] = 0.5f * x[i] * (1.f + erff(x[i] * 0.70710678118654752440f));
+}
+
 int oracle_num_threads(void) {
 #ifdef _OPENMP
     return omp_get_max_threads();

@@ -136,6 +136,11 @@ void oracle_decima_quantize_rows(const float *x, size_t rows, size_t cols, size_
 void oracle_decima_apply_w8a8(const int8_t *w_codes, const float *w_scales, size_t rows, size_t cols,
                               size_t block, const float *x, size_t m, const float *bias, int mode, float *y);
 
+/* Decima encoder pieces (decima/cpu.rs): LayerNorm with sequential f32 sums (:529-539) and the
+ * erf GELU (:542-556); the composed C4 forward lives in oracle.py (bert_forward). */
+void oracle_layer_norm(float *x, size_t rows, size_t d, const float *w, const float *b, float eps);
+void oracle_gelu(float *x, size_t n);
+
 int oracle_num_threads(void);
 void oracle_set_threads(int n);
 int oracle_has_avx2(void);

@@ -94,6 +94,8 @@ def _declare(l):
     l.oracle_decima_quantize.argtypes = [C.c_float, C.c_float]
     l.oracle_decima_quantize_rows.argtypes = [_f, _sz, _sz, _sz, _i8, _f]
     l.oracle_decima_apply_w8a8.argtypes = [_i8, _f, _sz, _sz, _sz, _f, _sz, _f, C.c_int, _f]
+    l.oracle_layer_norm.argtypes = [_f, _sz, _sz, _f, _f, C.c_float]
+    l.oracle_gelu.argtypes = [_f, _sz]
     l.oracle_num_threads.restype = C.c_int
     l.oracle_set_threads.argtypes = [C.c_int]
     l.oracle_has_avx2.restype = C.c_int
@@ -457,3 +459,41 @@ class DecimaMatrix:
         lib().oracle_decima_apply_w8a8(_p(self.codes, _i8), _p(self.scales, _f), self.rows, self.cols,
                                        self.block, _p(x, _f), x.shape[0], _p(b, _f), mode, _p(y, _f))
         return y
+
+
+def layer_norm(x, w, b, eps):
+    x = np.array(x, dtype=np.float32, copy=True)
+    rows, d = x.reshape(-1, x.shape[-1]).shape
+    lib().oracle_layer_norm(_p(x, _f), rows, d, _p(np.ascontiguousarray(w, np.float32), _f),
+                            _p(np.ascontiguousarray(b, np.float32), _f), eps)
+    return x
+
+
+def gelu(x):
+    x = np.array(x, dtype=np.float32, copy=True)
+    lib().oracle_gelu(_p(x, _f), x.size)
+    return x
+
+
+def bert_forward(cfg: dict, w: dict, ids, mode: int = 0):
+    """Composed Decima (BERT-shaped, decima/mod.rs:492-556) encoder forward with W8A8 block
+    projections: x = LN(word[id] + type[0] + pos[p]); per layer x = LN(x + o(attn(q, k, v)));
+    x = LN(x + ff2(gelu(ff1(x)))).  Returns (mean-pooled, hidden [T, D])."""
+    D, H, block, eps = cfg["hidden"], cfg["heads"], cfg["block"], cfg["eps"]
+    hd = D // H
+    ids = np.asarray(ids)
+    T = ids.size
+    x = ((w["word"][ids] + w["type"][0][None, :]).astype(np.float32) + w["pos"][:T]).astype(np.float32)
+    x = layer_norm(x, w["emb_ln_w"], w["emb_ln_b"], eps)
+    for l in range(cfg["layers"]):
+        L = w["layers"][l]
+        q = DecimaMatrix(L["q"], block).apply(x, bias=L["bq"], mode=mode)
+        k = DecimaMatrix(L["k"], block).apply(x, bias=L["bk"], mode=mode)
+        v = DecimaMatrix(L["v"], block).apply(x, bias=L["bv"], mode=mode)
+        ctx = attention(q, k, v, H, H, hd, scale=1.0 / np.sqrt(hd))
+        o = DecimaMatrix(L["o"], block).apply(ctx, bias=L["bo"], mode=mode)
+        x = layer_norm((x + o).astype(np.float32), L["ln1_w"], L["ln1_b"], eps)
+        h = gelu(DecimaMatrix(L["ff1"], block).apply(x, bias=L["b1"], mode=mode))
+        o2 = DecimaMatrix(L["ff2"], block).apply(h, bias=L["b2"], mode=mode)
+        x = layer_norm((x + o2).astype(np.float32), L["ln2_w"], L["ln2_b"], eps)
+    return x.mean(axis=0, dtype=np.float32), x
