@@ -488,6 +488,10 @@ class Model:
                 result.append(Outcome("error", error=Error._from(errs[i])))
         return result
 
+    def use_graphs(self, enable: bool = True):
+        """Forward as a captured CUDA graph per token count (default on); bit-identical either way."""
+        check(load().db_model_use_graphs(self._h, int(enable)))
+
     def profile(self, enable: bool = True):
         check(load().db_model_profile(self._h, int(enable)))
 

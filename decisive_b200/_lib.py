@@ -96,6 +96,7 @@ SIGNATURES = [
     ("db_predict_continuations", _i32, [_vp, _vp, _vp, _sz, _vp, _sz, _sz, _vp, _vp, C.POINTER(DbError)]),
     ("db_cache_stats", _i32, [_vp, _vp, _vp, _vp]),
     ("db_model_profile", _i32, [_vp, _i32]),
+    ("db_model_use_graphs", _i32, [_vp, _i32]),
     ("db_model_export_packed", _i32, [_vp, C.c_char_p, C.POINTER(DbError)]),
     ("db_model_set_streaming", _i32, [_vp, _i32, C.POINTER(DbError)]),
     ("db_model_create_packed", _vp, [_i32, C.POINTER(EncoderConfig), C.c_char_p, _i32, C.POINTER(DbError)]),

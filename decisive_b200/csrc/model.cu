@@ -86,6 +86,15 @@ struct db_model {
     int32_t* ids = nullptr;
     int* flag = nullptr;
     int* dev_err = nullptr;
+    // one CUDA graph per token count for the plain forward (captured on the second call for a T)
+    bool use_graphs = true;
+    std::map<int, cudaGraphExec_t> graphs;
+    std::map<int, int> graph_calls;
+    void drop_graphs() {
+        for (auto& g : graphs) cudaGraphExecDestroy(g.second);
+        graphs.clear();
+        graph_calls.clear();
+    }
     // tile configurations chosen by db_model_tune for qkv, o, gate/up, down (zero = defaults)
     db_gemm_config tuned[4] = {};
     // per-launch CUDA-event profiling (mirror of the reference's projection_ms accounting,
@@ -183,6 +192,7 @@ int upload_norm(db_model* m, const float* host, int n, float** out) {
 int ensure_rope(db_model* m, int n) {
     if (n <= m->rope_T) return 0;
     cudaStreamSynchronize(m->stream);
+    m->drop_graphs();
     m->free_all(m->rope_allocations);
     m->rope_T = 0;
     if (m->alloc(&m->cos_t, (size_t)n * 64, m->rope_allocations) ||
@@ -206,6 +216,7 @@ int ensure_rope(db_model* m, int n) {
 int ensure_workspace(db_model* m, int T) {
     if (T <= m->cap_T) return 0;
     cudaStreamSynchronize(m->stream);
+    m->drop_graphs();  // captured graphs hold the old buffers
     m->free_all(m->ws_allocations);
     m->cap_T = 0;
     const int D = m->D(), F = m->F(), Kmax = m->Kmax();
@@ -465,6 +476,41 @@ int enqueue_forward(db_model* m, int T, const volatile uint8_t* cancel, const Pa
     return rc ? db_cuda_status(rc, "forward") : 0;
 }
 
+// Runs the plain forward of T tokens.  From the second call for a T on, it runs as one CUDA graph
+// (captured then), which removes the per-launch gaps of ~230 kernels; the layer-by-layer path is
+// kept when a cancellation flag must be polled between layers (as the reference does), when
+// per-kernel profiling is on, while weights stream, or when graphs are switched off.
+int run_forward(db_model* m, int T, const volatile uint8_t* cancel) {
+    if (cancel || m->profile || m->streaming || !m->use_graphs) return enqueue_forward(m, T, cancel);
+    auto it = m->graphs.find(T);
+    if (it == m->graphs.end()) {
+        if (m->graph_calls[T]++ == 0) return enqueue_forward(m, T, nullptr);  // first call: eager
+        cudaGraph_t g = nullptr;
+        if (cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+            cudaGetLastError();
+            return enqueue_forward(m, T, nullptr);
+        }
+        const int rc = enqueue_forward(m, T, nullptr);
+        const cudaError_t e = cudaStreamEndCapture(m->stream, &g);
+        if (rc || e != cudaSuccess || !g) {
+            if (g) cudaGraphDestroy(g);
+            cudaGetLastError();
+            m->use_graphs = false;  // capture failed: stay eager
+            return enqueue_forward(m, T, nullptr);
+        }
+        cudaGraphExec_t exec = nullptr;
+        const cudaError_t ie = cudaGraphInstantiate(&exec, g, 0);
+        cudaGraphDestroy(g);
+        if (ie != cudaSuccess) {
+            cudaGetLastError();
+            m->use_graphs = false;
+            return enqueue_forward(m, T, nullptr);
+        }
+        it = m->graphs.emplace(T, exec).first;
+    }
+    return db_cuda_status((int)cudaGraphLaunch(it->second, m->stream), "graph launch");
+}
+
 // Backend::predict for one request; errors use the reference's codes.
 int predict_one(db_model* m, const int32_t* ids, size_t n, const db_parameters* params, const volatile uint8_t* cancel,
                 float* out, db_error* err) {
@@ -497,7 +543,7 @@ int predict_one(db_model* m, const int32_t* ids, size_t n, const db_parameters* 
         return -1;
     }
     cudaMemcpyAsync(m->ids, ids, n * sizeof(int32_t), cudaMemcpyHostToDevice, m->stream);
-    int rc = enqueue_forward(m, (int)n, cancel);
+    int rc = run_forward(m, (int)n, cancel);
     if (rc == 1) {
         cudaStreamSynchronize(m->stream);
         fill_error(err, "CANCELLED", "Inference was cancelled");
@@ -711,6 +757,7 @@ void db_model_destroy(db_model* m) {
     if (!m) return;
     cudaSetDevice(m->device);
     if (m->stream) cudaStreamSynchronize(m->stream);
+    m->drop_graphs();
     m->free_all(m->ws_allocations);
     m->free_all(m->rope_allocations);
     m->free_all(m->allocations);
@@ -797,6 +844,15 @@ int db_predict_batch(db_model* m, const int32_t* const* ids, const size_t* lens,
     return 0;
 }
 
+int db_model_use_graphs(db_model* m, int enable) {
+    if (!m) return DB_ERR_INVALID_ARGUMENT;
+    cudaSetDevice(m->device);
+    cudaStreamSynchronize(m->stream);
+    m->drop_graphs();
+    m->use_graphs = enable != 0;
+    return DB_OK;
+}
+
 int db_model_profile(db_model* m, int enable) {
     if (!m) return DB_ERR_INVALID_ARGUMENT;
     m->profile = enable != 0;
@@ -855,6 +911,7 @@ int db_model_tune(db_model* m, int64_t tokens, const char* cache_path, char* rep
     }
     all += "}";
     for (int p = 0; p < 4; ++p) m->tuned[p] = chosen[p];
+    m->drop_graphs();  // captured graphs hold the previous tile choices
     if (report_json && cap) std::snprintf(report_json, cap, "%s", all.c_str());
     return DB_OK;
 }
@@ -870,7 +927,7 @@ int db_forward_device(db_model* m, const int32_t* ids_dev, int64_t n, float* out
     cudaEventRecord(ev, caller);
     cudaStreamWaitEvent(m->stream, ev, 0);
     cudaMemcpyAsync(m->ids, ids_dev, n * sizeof(int32_t), cudaMemcpyDeviceToDevice, m->stream);
-    int rc = enqueue_forward(m, (int)n, nullptr);
+    int rc = run_forward(m, (int)n, nullptr);
     cudaMemcpyAsync(out_dev, m->pooled, m->cfg.hidden * sizeof(float), cudaMemcpyDeviceToDevice, m->stream);
     cudaEventRecord(ev, m->stream);
     cudaStreamWaitEvent(caller, ev, 0);
@@ -1014,6 +1071,7 @@ int db_model_set_streaming(db_model* m, int enable, db_error* err) {
     cudaSetDevice(m->device);
     cudaStreamSynchronize(m->stream);
     if ((enable != 0) == m->streaming) return DB_OK;
+    m->drop_graphs();  // the weight buffers move
     const int L = m->cfg.layers, D = m->D(), F = m->F(), Nq = m->Nq(), bits = m->cfg.weight_bits;
     const size_t G = (size_t)D / 64;
     // the eight projection buffers of a layer, in bank order

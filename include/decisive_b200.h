@@ -319,6 +319,11 @@ int db_cache_stats(const db_cache *c, int64_t *hits, int64_t *reused_tokens, int
  * accounting, cpu.rs:8-16).  Kinds 0..DB_PROF_KINDS-1, named by db_model_profile_name.
  * db_model_profile_read synchronises the model's stream and returns accumulated ms and
  * launch counts per kind. */
+/* The plain forward of a token count runs as one captured CUDA graph from its second call on
+ * (1 = on, the default); a cancellation flag, per-kernel profiling or streaming keeps the
+ * layer-by-layer path.  0 switches graphs off (results are bit-identical either way). */
+int db_model_use_graphs(db_model *m, int enable);
+
 #define DB_PROF_KINDS 11
 int db_model_profile(db_model *m, int enable);
 int db_model_profile_read(db_model *m, double *ms, int64_t *counts, int n, int reset);

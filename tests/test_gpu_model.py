@@ -163,3 +163,20 @@ def test_models_on_two_devices_in_one_process(db):
     assert np.array_equal(ra.view(np.uint32), rb.view(np.uint32))
     a.close()
     b.close()
+
+
+def test_graph_forward_is_bit_identical(db):
+    """The plain forward runs as a captured CUDA graph from its second call for a token count on;
+    graph and layer-by-layer results are identical, also after the workspace grows."""
+    cfg = db.EncoderConfig(**SMALL, weight_bits=4, max_sequence_tokens=128)
+    m = db.Model.synthetic(cfg, seed=8)
+    rng = np.random.default_rng(5)
+    reqs = [rng.integers(0, SMALL["vocab"], n).astype(np.int32) for n in (64, 64, 64, 17, 17, 17, 200, 200)]
+    m.use_graphs(False)
+    want = [np.asarray(m.predict(r, parameters=db.PplxParameters(256)).response).copy() for r in reqs]
+    m.use_graphs(True)
+    for _ in range(2):
+        got = [np.asarray(m.predict(r, parameters=db.PplxParameters(256)).response).copy() for r in reqs]
+        for a, b in zip(want, got):
+            assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    m.close()
