@@ -1,7 +1,9 @@
-// Non-causal GQA attention, head_dim 128, f16 operands with f32 accumulation and an online
-// softmax (the reference computes scale * q.k, softmax, then P.v per head in f32:
-// backbone.rs:560-600).  One CTA = 64 queries of one head, 4 warps x 16 query rows; K/V tiles
-// of 64 keys double-buffered in 128B-swizzled shared memory via cp.async.
+// GQA attention with cached prefix keys and/or causal own keys (the decoder forms), head_dim 128,
+// f16 operands with f32 accumulation and an online softmax (the reference computes scale * q.k,
+// softmax, then P.v per head in f32: backbone.rs:560-600).  One CTA = 64 queries of one head,
+// 4 warps x 16 query rows on mma.sync; K/V tiles of 64 keys double-buffered in 128B-swizzled
+// shared memory via cp.async.  The plain non-causal calls run on the tcgen05 kernel of
+// attention_tc.cu.
 #include <float.h>
 
 #include "common.cuh"
@@ -58,16 +60,13 @@ __device__ __forceinline__ void load_tile(uint32_t dst, const __half* base, int 
     }
 }
 
-// QUANT: instead of the f32 context, write what the output projection consumes -- the context
-// quantised per 64-wide group with the activation quantiser (int8.rs:178-202, 305-391): f16 codes
+// The context leaves as what the output projection consumes: quantised per 64-wide group with the activation quantiser (int8.rs:178-202, 305-391): f16 codes
 // in tensor-core order [T, ldc] and scales [groups, lds] -- and raise *nonfinite on a non-finite
 // value (the NaN guard of Matrix::apply, int8.rs:170-173).
-template <bool QUANT>
 __global__ void __launch_bounds__(ATT_THREADS)
     attention_kernel(const __half* __restrict__ q16, const __half* __restrict__ k16, const __half* __restrict__ v16,
-                     int T, int Hq, int Hk, float scale_log2, float* __restrict__ out, int64_t ldo,
-                     __half* __restrict__ codes, int64_t ldc, float* __restrict__ scales, int64_t lds,
-                     int* __restrict__ nonfinite, const __half* __restrict__ kp, const __half* __restrict__ vp, int P,
+                     int T, int Hq, int Hk, float scale_log2, __half* __restrict__ codes, int64_t ldc,
+                     float* __restrict__ scales, int64_t lds, int* __restrict__ nonfinite, const __half* __restrict__ kp, const __half* __restrict__ vp, int P,
                      int causal) {
     extern __shared__ __align__(128) uint8_t smem[];
     const uint32_t sQ = smem_u32(smem);
@@ -204,8 +203,7 @@ __global__ void __launch_bounds__(ATT_THREADS)
     }
     // normalise and store
     const float inv0 = 1.f / lrow[0], inv1 = 1.f / lrow[1];
-    const int r0 = q0 + warp * 16 + (lane >> 2);
-    if constexpr (QUANT) {
+    {
         // Rows r0 and r0 + 8 of this warp: 16 values per 64-wide group per thread, the rest of the
         // group on the other three lanes of the quad.  Codes go through shared memory (the Q tile,
         // free after the last iteration's barrier) in the tensor-core order k0,k4,k1,k5,k2,k6,k3,k7
@@ -257,16 +255,6 @@ __global__ void __launch_bounds__(ATT_THREADS)
                 *reinterpret_cast<uint4*>(codes + (size_t)(rb + t) * ldc + h * ATT_D + chunk * 8) =
                     reinterpret_cast<const uint4*>(smem)[row * 16 + chunk];
         }
-        return;
-    }
-#pragma unroll
-    for (int n = 0; n < 16; ++n) {
-        const int d = n * 8 + 2 * (lane & 3);
-        if (r0 < T)
-            *reinterpret_cast<float2*>(out + (size_t)(rb + r0) * ldo + h * ATT_D + d) = make_float2(o[n][0] * inv0, o[n][1] * inv0);
-        if (r0 + 8 < T)
-            *reinterpret_cast<float2*>(out + (size_t)(rb + r0 + 8) * ldo + h * ATT_D + d) =
-                make_float2(o[n][2] * inv1, o[n][3] * inv1);
     }
 }
 
@@ -276,35 +264,16 @@ using namespace db;
 
 int db_launch_attention(const __half* q16, const __half* k16, const __half* v16, int T, int Hq, int Hk, float scale,
                         float* out, int64_t ldo, cudaStream_t stream) {
-    if (T <= 0) return 0;
-    if (Hk <= 0 || Hq % Hk) return (int)cudaErrorInvalidValue;
-    const int smem = 5 * ATT_TILE_BYTES;
-    {
-        const cudaError_t e = db_set_max_smem(reinterpret_cast<const void*>(attention_kernel<false>), smem);
-        if (e != cudaSuccess) return (int)e;
-    }
-    dim3 grid((T + ATT_BQ - 1) / ATT_BQ, Hq);
-    attention_kernel<false><<<grid, ATT_THREADS, smem, stream>>>(q16, k16, v16, T, Hq, Hk, scale * 1.4426950408889634f,
-                                                                 out, ldo, nullptr, 0, nullptr, 0, nullptr, nullptr,
-                                                                 nullptr, 0, 0);
-    return (int)cudaGetLastError();
+    return db_launch_attention_tc(q16, k16, v16, 1, T, Hq, Hk, scale, out, ldo, nullptr, 0, nullptr, 0, nullptr,
+                                  stream);
 }
 
 int db_launch_attention_quant(const __half* q16, const __half* k16, const __half* v16, int T, int Hq, int Hk,
                               float scale, __half* codes, int64_t ldc, float* scales, int64_t lds, int* nonfinite,
                               cudaStream_t stream) {
-    if (T <= 0) return 0;
-    if (Hk <= 0 || Hq % Hk || !codes || !scales || !nonfinite || (ldc & 7)) return (int)cudaErrorInvalidValue;
-    const int smem = 5 * ATT_TILE_BYTES;
-    {
-        const cudaError_t e = db_set_max_smem(reinterpret_cast<const void*>(attention_kernel<true>), smem);
-        if (e != cudaSuccess) return (int)e;
-    }
-    dim3 grid((T + ATT_BQ - 1) / ATT_BQ, Hq);
-    attention_kernel<true><<<grid, ATT_THREADS, smem, stream>>>(q16, k16, v16, T, Hq, Hk, scale * 1.4426950408889634f,
-                                                                nullptr, 0, codes, ldc, scales, lds, nonfinite, nullptr,
-                                                                nullptr, 0, 0);
-    return (int)cudaGetLastError();
+    if (!codes) return (int)cudaErrorInvalidValue;
+    return db_launch_attention_tc(q16, k16, v16, 1, T, Hq, Hk, scale, nullptr, 0, codes, ldc, scales, lds, nonfinite,
+                                  stream);
 }
 
 int db_launch_attention_prefix_quant(const __half* q16, const __half* k16, const __half* v16, int B, int T,
@@ -317,12 +286,11 @@ int db_launch_attention_prefix_quant(const __half* q16, const __half* k16, const
         return (int)cudaErrorInvalidValue;
     const int smem = 5 * ATT_TILE_BYTES;
     {
-        const cudaError_t e = db_set_max_smem(reinterpret_cast<const void*>(attention_kernel<true>), smem);
+        const cudaError_t e = db_set_max_smem(reinterpret_cast<const void*>(attention_kernel), smem);
         if (e != cudaSuccess) return (int)e;
     }
     dim3 grid((T + ATT_BQ - 1) / ATT_BQ, Hq, B);
-    attention_kernel<true><<<grid, ATT_THREADS, smem, stream>>>(q16, k16, v16, T, Hq, Hk, scale * 1.4426950408889634f,
-                                                                nullptr, 0, codes, ldc, scales, lds, nonfinite, kp, vp,
-                                                                P, causal);
+    attention_kernel<<<grid, ATT_THREADS, smem, stream>>>(q16, k16, v16, T, Hq, Hk, scale * 1.4426950408889634f,
+                                                          codes, ldc, scales, lds, nonfinite, kp, vp, P, causal);
     return (int)cudaGetLastError();
 }

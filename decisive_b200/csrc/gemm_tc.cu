@@ -830,19 +830,15 @@ done:
 
 using namespace db;
 
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiledFn encode_fn() {
-    static EncodeTiledFn fn = nullptr;
+DbEncodeTiledFn db_encode_tiled() {
+    static DbEncodeTiledFn fn = nullptr;
     static std::once_flag once;
     std::call_once(once, [] {
         cudaDriverEntryPointQueryResult q;
         void* p = nullptr;
         if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
             q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<EncodeTiledFn>(p);
+            fn = reinterpret_cast<DbEncodeTiledFn>(p);
     });
     return fn;
 }
@@ -929,7 +925,7 @@ static int dispatch_epi(const DbGemmArgs& a, bool pair, const CUtensorMap& tmA, 
 int db_launch_gemm_tc(const DbGemmArgs& a, cudaStream_t stream) {
     if (a.M <= 0 || a.N <= 0) return 0;
     if (a.K <= 0 || (a.bits != 4 && a.bits != 8)) return (int)cudaErrorInvalidValue;
-    EncodeTiledFn enc = encode_fn();
+    DbEncodeTiledFn enc = db_encode_tiled();
     if (!enc) return (int)cudaErrorNotSupported;
     const int G = (a.K + BK - 1) / BK, Kp = G * BK;
     int bn = a.block_n ? a.block_n : 128;

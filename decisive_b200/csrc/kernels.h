@@ -1,5 +1,6 @@
 // Host-side launchers of the device kernels (internal to libdecisive_b200.so).
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -87,6 +88,11 @@ int db_launch_gemv(const DbGemvArgs& args, cudaStream_t stream);
 int db_gemv_rows_limit();
 
 int db_num_sms();
+// cuTensorMapEncodeTiled, reached through the runtime's driver entry point (null when absent).
+typedef CUresult (*DbEncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+DbEncodeTiledFn db_encode_tiled();
 // Raises a kernel's dynamic shared-memory limit once per (kernel, device): function attributes
 // belong to a device's context, so a process that drives several GPUs sets them on each.
 // Thread-safe.

@@ -25,6 +25,12 @@ int db_launch_attention(const __half* q16, const __half* k16, const __half* v16,
 int db_launch_attention_quant(const __half* q16, const __half* k16, const __half* v16, int T, int Hq, int Hk,
                               float scale, __half* codes, int64_t ldc, float* scales, int64_t lds, int* nonfinite,
                               cudaStream_t stream);
+// The tensor-core (tcgen05) attention behind the two calls above: B items of T rows each
+// (q16/k16/v16 and the outputs hold the items one after another, 16-byte aligned), non-causal;
+// the context goes to out (f32) when codes is null, else quantised as above.
+int db_launch_attention_tc(const __half* q16, const __half* k16, const __half* v16, int B, int T, int Hq, int Hk,
+                           float scale, float* out, int64_t ldo, __half* codes, int64_t ldc, float* scales,
+                           int64_t lds, int* nonfinite, cudaStream_t stream);
 // Decoder form of the quantising attention: B items of T rows each (q16/k16/v16 and the outputs
 // hold the items one after another); every item's keys are the P cached prefix keys kp/vp
 // [P, Hk, 128] (shared by the items; P = 0: none) followed by its own T keys, which are causal

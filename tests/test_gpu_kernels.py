@@ -298,14 +298,20 @@ def test_fused_mlp_matches_unfused_oracle(db, oracle, bits, m, f, k):
 
 
 # ------------------------------------------------------------------ attention
-@pytest.mark.parametrize("t,hq,hk", [(1, 2, 1), (65, 4, 2), (200, 4, 4), (1024, 16, 8)])
-def test_attention_matches_oracle(db, oracle, t, hq, hk):
+# Key-tile counts 1 to 8 (tiles of 128 keys: even and odd counts, ragged last tiles), GQA ratios
+# 1, 2 and 4, and sharper softmaxes (scale 0.25: scores with a standard deviation of ~2.8).
+@pytest.mark.parametrize("t,hq,hk,scale", [(1, 2, 1, None), (65, 4, 2, None), (128, 2, 2, None),
+                                           (129, 2, 1, None), (200, 4, 4, None), (300, 8, 2, None),
+                                           (300, 4, 1, 0.25), (1024, 16, 8, None), (1000, 4, 2, 0.25)])
+def test_attention_matches_oracle(db, oracle, t, hq, hk, scale):
     rng = np.random.default_rng(t)
     q = rng.normal(0, 1, (t, hq, 128)).astype(np.float16)
     k = rng.normal(0, 1, (t, hk, 128)).astype(np.float16)
     v = rng.normal(0, 1, (t, hk, 128)).astype(np.float16)
-    out = db.attention(torch.from_numpy(q).cuda(), torch.from_numpy(k).cuda(), torch.from_numpy(v).cuda(), hq, hk)
-    ref = oracle.attention(q.astype(np.float32), k.astype(np.float32), v.astype(np.float32), hq, hk, 128)
+    out = db.attention(torch.from_numpy(q).cuda(), torch.from_numpy(k).cuda(), torch.from_numpy(v).cuda(), hq, hk,
+                       scale)
+    assert db.device_error_word() == 0
+    ref = oracle.attention(q.astype(np.float32), k.astype(np.float32), v.astype(np.float32), hq, hk, 128, scale)
     o = out.cpu().numpy().reshape(-1)
     r = ref.reshape(-1)
     # f16 probabilities (11-bit mantissa) into an f32 accumulator: error ~1e-3 of the output RMS
