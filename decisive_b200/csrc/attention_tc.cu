@@ -208,11 +208,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    // Register split: the launch gives every thread 168; warpgroup 0 (producer, MMA issuer, two
-    // idle warps) keeps 64 and the softmax warpgroups take 216 (64*128 + 216*256 <= 168*384).  Each
-    // setmaxnreg sits inside its role's branch, so the compiler budgets each region separately.
     if (warp < AT_SOFTMAX_WARP0) {
-        asm volatile("setmaxnreg.dec.sync.aligned.u32 64;");
         if (warp == 0) {
             // ---------------------------------------------------------------- TMA producer
             // Load order = consumption order: the K tiles of pair p, then the V tiles of pair p-1, ...,
@@ -270,33 +266,49 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
             int st = 0;
             uint32_t ph = 0;
             uint32_t su[2] = {0u, 0u}, pu[2] = {0u, 0u};  // uses of S buffer / P tile b so far
-            auto take_stage = [&](int& slot) -> bool {
-                slot = st;
-                if (!warp_wait_at(&bars[BAR_KV_FULL + st], ph, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_MMA))
-                    return false;
-                if (++st == AT_STAGES) {
-                    st = 0;
-                    ph ^= 1u;
+            // descriptors of the tiles' first K step; a K step adds a constant (addresses < 256 KB,
+            // so the 14-bit start field never carries)
+            const uint64_t dQ = sw128_desc(sQ), dP = sw128_desc(sP), dKV = sw128_desc(sKV),
+                           dV = sw128_mn_desc(sKV);
+            auto kstep = [](int kk) -> uint64_t { return (uint64_t)(((kk >> 2) * AT_HALF + (kk & 3) * 32) >> 4); };
+            // The pair's n tiles take the next n ring stages.  Lanes 2t and 2t+1 poll tile t's stage
+            // and its S buffer (or P tile) at the same time; the warp proceeds when all have passed.
+            auto wait_pair = [&](int n, int (&slot)[2], int second, const uint32_t (&par)[2]) -> bool {
+                uint64_t* bar = nullptr;
+                uint32_t parity = 0;
+                for (int t = 0; t < n; ++t) {
+                    slot[t] = st;
+                    if (lane == 2 * t) {
+                        bar = &bars[BAR_KV_FULL + st];
+                        parity = ph;
+                    } else if (lane == 2 * t + 1) {
+                        bar = &bars[second + t];
+                        parity = par[t];
+                    }
+                    if (++st == AT_STAGES) {
+                        st = 0;
+                        ph ^= 1u;
+                    }
                 }
-                return true;
+                const int ok = bar ? (int)mbar_spin(bar, parity, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_MMA) : 1;
+                const bool all = __all_sync(0xffffffffu, ok) != 0;
+                __syncwarp();  // orders the pollers' acquires before lane 0's MMAs
+                return all;
             };
             // S_t = Q K_{2p+t}^T for the pair's tiles, K steps of the two chains interleaved
             auto s_pair = [&](int p) -> bool {
                 const int n = min(2, nt - 2 * p);
                 int slot[2] = {0, 0};
-                for (int t = 0; t < n; ++t) {
-                    if (!take_stage(slot[t])) return false;
-                    if (!warp_wait_at(&bars[BAR_S_EMPTY + t], (su[t] & 1u) ^ 1u, abort_flag, dev_error,
-                                      DB_DEV_ERR_TIMEOUT_MMA))
-                        return false;
-                }
+                const uint32_t par[2] = {(su[0] & 1u) ^ 1u, (su[1] & 1u) ^ 1u};  // S buffer free
+                if (!wait_pair(n, slot, BAR_S_EMPTY, par)) return false;
                 tc_fence_after();
                 if (lane == 0) {
+                    const uint64_t dK[2] = {dKV + (uint64_t)((slot[0] * AT_TILE) >> 4),
+                                            dKV + (uint64_t)((slot[1] * AT_TILE) >> 4)};
 #pragma unroll
                     for (int kk = 0; kk < AT_D / 16; ++kk)
                         for (int t = 0; t < n; ++t)
-                            umma_f16(tmem + TM_S + 128u * t, sw128_desc(kmajor_step(sQ, kk)),
-                                     sw128_desc(kmajor_step(sKV + (uint32_t)(slot[t] * AT_TILE), kk)), IDESC_S, kk > 0);
+                            umma_f16(tmem + TM_S + 128u * t, dQ + kstep(kk), dK[t] + kstep(kk), IDESC_S, kk > 0);
                     for (int t = 0; t < n; ++t) {
                         umma_commit(&bars[BAR_KV_EMPTY + slot[t]]);
                         umma_commit(&bars[BAR_S_FULL + t]);
@@ -310,19 +322,17 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
             auto pv_pair = [&](int p) -> bool {
                 const int n = min(2, nt - 2 * p);
                 int slot[2] = {0, 0};
-                for (int t = 0; t < n; ++t) {
-                    if (!take_stage(slot[t])) return false;
-                    if (!warp_wait_at(&bars[BAR_P_FULL + t], pu[t] & 1u, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_MMA))
-                        return false;
-                }
+                const uint32_t par[2] = {pu[0] & 1u, pu[1] & 1u};  // P tile written
+                if (!wait_pair(n, slot, BAR_P_FULL, par)) return false;
                 tc_fence_after();
                 if (lane == 0) {
+                    const uint64_t dVt[2] = {dV + (uint64_t)((slot[0] * AT_TILE) >> 4),
+                                             dV + (uint64_t)((slot[1] * AT_TILE) >> 4)};
 #pragma unroll
                     for (int kk = 0; kk < AT_KT / 16; ++kk)
                         for (int t = 0; t < n; ++t)
-                            umma_f16(tmem + TM_O + 128u * t, sw128_desc(kmajor_step(sP + (uint32_t)(t * AT_TILE), kk)),
-                                     sw128_mn_desc(sKV + (uint32_t)(slot[t] * AT_TILE + kk * 2048)), IDESC_PV,
-                                     p > 0 || kk > 0);
+                            umma_f16(tmem + TM_O + 128u * t, dP + (uint64_t)((t * AT_TILE) >> 4) + kstep(kk),
+                                     dVt[t] + (uint64_t)(kk * (2048 >> 4)), IDESC_PV, p > 0 || kk > 0);
                     for (int t = 0; t < n; ++t) {
                         umma_commit(&bars[BAR_KV_EMPTY + slot[t]]);
                         umma_commit(&bars[BAR_P_EMPTY + t]);
@@ -348,7 +358,6 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
             __syncwarp();
         }
     } else {
-        asm volatile("setmaxnreg.inc.sync.aligned.u32 216;");
         // ---------------------------------------------------------------- softmax + epilogue
         const int b = (warp - AT_SOFTMAX_WARP0) >> 2;  // 0: even tiles, 1: odd tiles
         const int qw = warp & 3;                       // TMEM lane quarter this warp may access
@@ -378,15 +387,22 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(&bars[BAR_S_EMPTY + b]);
             ++su;
+            // keys past the sequence end (only in a ragged last tile) score -inf: 2^(-inf) = 0
             const int kv0 = j * AT_KT;
-            const bool whole = kv0 + AT_KT <= T;
-            float mt = -INFINITY;  // key kv0 < T: at least one valid key
+            if (kv0 + AT_KT > T) {
+                const int lim = T - kv0;
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+#pragma unroll
+                    for (int i = 0; i < 32; ++i)
+                        if (32 * c + i >= lim) r[c][i] = __float_as_uint(-INFINITY);
+            }
+            float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // four independent chains
 #pragma unroll
             for (int c = 0; c < 4; ++c)
 #pragma unroll
-                for (int i = 0; i < 32; ++i)
-                    if (whole || kv0 + 32 * c + i < T) mt = fmaxf(mt, __uint_as_float(r[c][i]));
-            mt *= scale_log2;
+                for (int i = 0; i < 32; ++i) mx[i & 3] = fmaxf(mx[i & 3], __uint_as_float(r[c][i]));
+            const float mt = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * scale_log2;  // key kv0 < T
             float factor = 1.f;
             if (p == 0) {
                 m = mt;
@@ -397,20 +413,18 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
             }
             const bool rescale = __any_sync(0xffffffffu, factor != 1.f);
             uint32_t pk[64];
+            float ls[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
             for (int c = 0; c < 4; ++c)
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
-                    float p0 = ex2(fmaf(__uint_as_float(r[c][2 * i]), scale_log2, -m));
-                    float p1 = ex2(fmaf(__uint_as_float(r[c][2 * i + 1]), scale_log2, -m));
-                    if (!whole) {
-                        if (kv0 + 32 * c + 2 * i >= T) p0 = 0.f;
-                        if (kv0 + 32 * c + 2 * i + 1 >= T) p1 = 0.f;
-                    }
-                    l += p0;
-                    l += p1;
+                    const float p0 = ex2(fmaf(__uint_as_float(r[c][2 * i]), scale_log2, -m));
+                    const float p1 = ex2(fmaf(__uint_as_float(r[c][2 * i + 1]), scale_log2, -m));
+                    ls[2 * (i & 1)] += p0;
+                    ls[2 * (i & 1) + 1] += p1;
                     pk[16 * c + i] = pack_f16x2(p0, p1);
                 }
+            l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
             // the previous P.V into this warpgroup's accumulator has completed: the P tile is free
             // and O is stable
             if (!(ok = warp_wait_at(&bars[BAR_P_EMPTY + b], (pu & 1u) ^ 1u, abort_flag, dev_error,
