@@ -56,7 +56,8 @@ constexpr int BAR_P_EMPTY = BAR_P_FULL + 2;             // P tile b read by its 
 constexpr int BAR_XCH = BAR_P_EMPTY + 2;                // (m, l) exchange between the warpgroups (8 warps)
 constexpr int BAR_O_FULL = BAR_XCH + 1;                 // last P.V accumulated
 constexpr int BAR_MMA_DONE = BAR_O_FULL + 1;            // every MMA issued has completed
-constexpr int NUM_BARS = BAR_MMA_DONE + 1;
+constexpr int BAR_END = BAR_MMA_DONE + 1;               // every warp is done with tensor memory
+constexpr int NUM_BARS = BAR_END + 1;
 constexpr int OFF_MISC = OFF_BAR + ((NUM_BARS * 8 + 15) / 16) * 16;  // TMEM address, abort flag
 constexpr int AT_SMEM = OFF_MISC + 16 + 1024;                         // + 1024-byte alignment slack
 static_assert(AT_SMEM <= 232448, "shared memory budget");
@@ -192,6 +193,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         mbar_init(&bars[BAR_XCH], 8);
         mbar_init(&bars[BAR_O_FULL], 1);
         mbar_init(&bars[BAR_MMA_DONE], 1);
+        mbar_init(&bars[BAR_END], AT_THREADS / 32);
         *abort_flag = 0;
         fence_barrier_init();
     }
@@ -525,8 +527,15 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
             }
         }
     }
-    __syncthreads();
+    // Teardown through an mbarrier, not __syncthreads: a hardware CTA barrier reached from the
+    // different role branches was measured (clock64 per warp) to release warps 0-3 long before the
+    // softmax warps arrived, which would free tensor memory under their last reads.
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&bars[BAR_END]);
     if (warp == 1) {
+        if (lane == 0) mbar_wait_drain(&bars[BAR_END], 0, DRAIN_NS);
+        __syncwarp();
         tc_fence_after();
         tmem_dealloc(tmem, 512);
     }

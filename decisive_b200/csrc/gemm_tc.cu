@@ -96,7 +96,7 @@ struct GemmSmem {
     static constexpr int OFF_X = OFF_SC + SC_BYTES;
     static constexpr int OFF_Y = OFF_X + XCH_BYTES;
     static constexpr int OFF_BAR = (OFF_Y + Y_BYTES + 15) / 16 * 16;
-    static constexpr int NUM_BARS = 3 * STAGES + 3 * JS + 4;
+    static constexpr int NUM_BARS = 3 * STAGES + 3 * JS + 6;
     static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
     static constexpr int BYTES = OFF_MISC + 16 + 1024;     // + alignment slack
     static_assert(fits(STAGES, Y_BUFS) && BYTES <= 232448, "shared memory budget");
@@ -254,6 +254,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     uint64_t* xch_empty = xch_full + 1;      // every epilogue warp is done with this tile's exchange
     uint64_t* xch_amax = xch_empty + 1;      // both halves' row maxima published
     uint64_t* mma_done = xch_amax + 1;       // final commit of the MMA issuer
+    uint64_t* end_local = mma_done + 1;      // every warp of this CTA is done (tensor memory, copies)
+    uint64_t* end_peer = end_local + 1;      // pair mode: the other CTA of the pair is done
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::OFF_MISC);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + S::OFF_MISC + 4);
 
@@ -288,6 +290,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         mbar_init(xch_empty, EPILOGUE_WARPS);
         mbar_init(xch_amax, EPILOGUE_WARPS);
         mbar_init(mma_done, 1);
+        mbar_init(end_local, NUM_THREADS / 32);
+        mbar_init(end_peer, 1);
         *abort_flag = 0;
         fence_barrier_init();
     }
@@ -815,11 +819,24 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 done:
     cp_async_wait_all();
     bulk_wait_all();  // output stores issued by this thread have completed
-    __syncthreads();
-    // neither CTA of a pair leaves while the other may still arrive on its barriers or have its
-    // shared memory read by the pair's MMAs (every wait above is bounded, so both get here)
-    if (PAIR) cluster_sync_all();
+    // Teardown through mbarriers, not __syncthreads / barrier.cluster: a hardware barrier reached
+    // from the different role branches was measured (clock64 per warp) to release some warps long
+    // before the others arrived.  Warp 1 frees tensor memory once every warp has arrived; in pair
+    // mode it first trades a signal with the other CTA's warp 1, so neither CTA leaves while the
+    // other may still arrive on its barriers or have its shared memory read by the pair's MMAs.
+    // Every wait above is bounded, so all warps get here.
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(end_local);
     if (warp == 1) {
+        if (lane == 0) {
+            mbar_wait_drain(end_local, 0, DRAIN_NS);
+            if (PAIR) {
+                mbar_arrive_cluster(mapa_shared(smem_u32(end_peer), rank ^ 1u));
+                mbar_wait_drain(end_peer, 0, DRAIN_NS);
+            }
+        }
+        __syncwarp();
         tc_fence_after();
         if (PAIR) tmem_dealloc_pair(tmem_base, S::BUFS * BN);
         else tmem_dealloc(tmem_base, S::BUFS * BN);
