@@ -254,8 +254,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     uint64_t* xch_empty = xch_full + 1;      // every epilogue warp is done with this tile's exchange
     uint64_t* xch_amax = xch_empty + 1;      // both halves' row maxima published
     uint64_t* mma_done = xch_amax + 1;       // final commit of the MMA issuer
-    uint64_t* end_local = mma_done + 1;      // every warp of this CTA is done (tensor memory, copies)
-    uint64_t* end_peer = end_local + 1;      // pair mode: the other CTA of the pair is done
+    // the last two barriers (teardown): every warp of this CTA is done with tensor memory and its
+    // copies; pair mode: the other CTA of the pair is done.  Addressed from the shared-memory base
+    // where used, so no register holds them through the main loops.
+    auto end_bar = [&](int i) { return reinterpret_cast<uint64_t*>(smem + S::OFF_BAR) + (S::NUM_BARS - 2 + i); };
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::OFF_MISC);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + S::OFF_MISC + 4);
 
@@ -290,8 +292,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         mbar_init(xch_empty, EPILOGUE_WARPS);
         mbar_init(xch_amax, EPILOGUE_WARPS);
         mbar_init(mma_done, 1);
-        mbar_init(end_local, NUM_THREADS / 32);
-        mbar_init(end_peer, 1);
+        mbar_init(end_bar(0), NUM_THREADS / 32);
+        mbar_init(end_bar(1), 1);
         *abort_flag = 0;
         fence_barrier_init();
     }
@@ -826,14 +828,17 @@ done:
     // other may still arrive on its barriers or have its shared memory read by the pair's MMAs.
     // Every wait above is bounded, so all warps get here.
     tc_fence_before();
+    // Not relied on for ordering (see above); kept because without it the compiler lays the role
+    // branches out differently and the 256-wide epilogue spills three times as much.
+    __syncthreads();
     __syncwarp();
-    if (lane == 0) mbar_arrive(end_local);
+    if (lane == 0) mbar_arrive(end_bar(0));
     if (warp == 1) {
         if (lane == 0) {
-            mbar_wait_drain(end_local, 0, DRAIN_NS);
+            mbar_wait_drain(end_bar(0), 0, DRAIN_NS);
             if (PAIR) {
-                mbar_arrive_cluster(mapa_shared(smem_u32(end_peer), rank ^ 1u));
-                mbar_wait_drain(end_peer, 0, DRAIN_NS);
+                mbar_arrive_cluster(mapa_shared(smem_u32(end_bar(1)), cluster_ctarank() ^ 1u));
+                mbar_wait_drain(end_bar(1), 0, DRAIN_NS);
             }
         }
         __syncwarp();
