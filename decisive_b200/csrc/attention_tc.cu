@@ -166,6 +166,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
                         float* __restrict__ out, int64_t ldo, __half* __restrict__ codes, int64_t ldc,
                         float* __restrict__ scales, int64_t lds, int* __restrict__ nonfinite,
                         int* __restrict__ dev_error) {
+    pdl_wait();
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
@@ -589,7 +590,7 @@ int db_launch_attention_tc(const __half* q16, const __half* k16, const __half* v
         if (e != cudaSuccess) return (int)e;
     }
     const dim3 grid((unsigned)((T + AT_Q - 1) / AT_Q), (unsigned)Hq, (unsigned)B);
-    kernel<<<grid, AT_THREADS, AT_SMEM, stream>>>(tmQ, tmK, tmV, T, Hq, Hk, scale * 1.4426950408889634f, out, ldo,
-                                                  codes, ldc, scales, lds, nonfinite, err);
-    return (int)cudaGetLastError();
+    const cudaError_t e = db_launch_pdl(kernel, grid, dim3(AT_THREADS), AT_SMEM, stream, tmQ, tmK, tmV, T, Hq, Hk,
+                                        scale * 1.4426950408889634f, out, ldo, codes, ldc, scales, lds, nonfinite, err);
+    return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }

@@ -98,6 +98,12 @@ __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity, 
     return true;
 }
 
+// Programmatic dependent launch: a kernel launched with the programmatic-serialization attribute
+// (db_launch_pdl) may be scheduled while the previous kernel in its stream is still finishing; it
+// waits here, before touching anything, until that kernel has completed and its writes are
+// visible.  Returns at once for a launch without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // Hardware named barrier among `count` threads (a multiple of 32); barrier 0 is __syncthreads.
 __device__ __forceinline__ void named_barrier_sync(int id, int count) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");

@@ -241,6 +241,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                    float* __restrict__ out_scales, int64_t ldos, const int* __restrict__ nonfinite,
                    const float* __restrict__ bias, int add_bias, int* __restrict__ dev_error) {
     using S = GemmSmem<BN, BITS, EPI, PAIR, SUB>;
+    pdl_wait();
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::OFF_BAR);
@@ -896,13 +897,16 @@ static int launch_variant(const DbGemmArgs& a, const CUtensorMap& tmA, const CUt
     cfg.blockDim = dim3(NUM_THREADS);
     cfg.dynamicSmemBytes = S::BYTES;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = PAIR ? 2 : 1;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    // CTAs may start on SMs the previous kernel has released; the kernel waits (pdl_wait) first
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     const int GS = (a.K + 64 / SUB - 1) / (64 / SUB);  // scale groups (blocks of 64 / SUB)
     const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, tmA, tmW, tmY, y_tma, a.sa, a.ldsa, a.sw,
                                              (int64_t)db_scale_stride(a.N), a.M, a.N, G, GS, a.y, a.ldy,

@@ -88,6 +88,24 @@ int db_launch_gemv(const DbGemvArgs& args, cudaStream_t stream);
 int db_gemv_rows_limit();
 
 int db_num_sms();
+// Launches `kernel` with the programmatic-serialization attribute: its CTAs may start on SMs the
+// previous kernel in the stream has released, before that kernel completes.  Only for kernels
+// that call pdl_wait() before their first access to memory.
+template <typename... KArgs, typename... Args>
+cudaError_t db_launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                          Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
 // cuTensorMapEncodeTiled, reached through the runtime's driver entry point (null when absent).
 typedef CUresult (*DbEncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                     const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,

@@ -34,6 +34,7 @@ __global__ void rms_quantize_kernel(const float* __restrict__ x, int64_t ldx, co
                                     float* __restrict__ scales, int32_t* __restrict__ sums, int64_t lds,
                                     int* __restrict__ nonfinite) {
     __shared__ float partial[32];
+    pdl_wait();
     const int t = blockIdx.x, lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     const int c = 4 * threadIdx.x;
     const float4 v = *reinterpret_cast<const float4*>(x + (size_t)t * ldx + c);
@@ -121,6 +122,7 @@ __global__ void qk_norm_rope_kernel(const float* __restrict__ qkv, int64_t ld, i
                                     const float* __restrict__ cos_t, const float* __restrict__ sin_t,
                                     __half* __restrict__ q16, __half* __restrict__ k16, __half* __restrict__ v16,
                                     int pos0, int seq_len) {
+    pdl_wait();
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     const int heads = Hq + 2 * Hk;
     const int units = (heads + QK_HEADS_PER_WARP - 1) / QK_HEADS_PER_WARP;
@@ -177,6 +179,7 @@ __global__ void qk_norm_rope_kernel(const float* __restrict__ qkv, int64_t ld, i
 
 // pooled[d] = (sum over t, in order, of x[t, d]) / T
 __global__ void mean_pool_kernel(const float* __restrict__ x, int64_t ldx, int T, int D, float* __restrict__ out) {
+    pdl_wait();
     const int d = blockIdx.x * blockDim.x + threadIdx.x;
     if (d >= D) return;
     float s = 0.f;
@@ -199,9 +202,10 @@ int db_launch_rms_quantize(const float* x, int64_t ldx, const float* w, int T, i
                            int32_t* sums, int64_t lds, int* nonfinite, cudaStream_t stream, int normalize) {
     if (T <= 0) return 0;
     if (D % 128 || D > 4096) return (int)cudaErrorInvalidValue;
-    rms_quantize_kernel<<<T, D / 4, 0, stream>>>(x, ldx, w, T, D, eps, zero_centered, normalize, normed, ldn, codes,
-                                                 layout, ldc, scales, sums, lds, nonfinite);
-    return (int)cudaGetLastError();
+    const cudaError_t e = db_launch_pdl(rms_quantize_kernel, dim3(T), dim3(D / 4), 0, stream, x, ldx, w, T, D, eps,
+                                        zero_centered, normalize, normed, ldn, codes, layout, ldc, scales, sums, lds,
+                                        nonfinite);
+    return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }
 
 int db_launch_qk_norm_rope(const float* qkv, int64_t ld, int T, int Hq, int Hk, const float* qw, const float* kw,
@@ -209,15 +213,15 @@ int db_launch_qk_norm_rope(const float* qkv, int64_t ld, int T, int Hq, int Hk, 
                            cudaStream_t stream, int pos0, int seq_len) {
     if (T <= 0) return 0;
     const int64_t warps = (int64_t)T * ((Hq + 2 * Hk + QK_HEADS_PER_WARP - 1) / QK_HEADS_PER_WARP);
-    qk_norm_rope_kernel<<<(unsigned)((warps + 3) / 4), 128, 0, stream>>>(qkv, ld, T, Hq, Hk, qw, kw, eps, cos_t,
-                                                                          sin_t, q16, k16, v16, pos0,
-                                                                          seq_len > 0 ? seq_len : T);
-    return (int)cudaGetLastError();
+    const cudaError_t e = db_launch_pdl(qk_norm_rope_kernel, dim3((unsigned)((warps + 3) / 4)), dim3(128), 0, stream,
+                                        qkv, ld, T, Hq, Hk, qw, kw, eps, cos_t, sin_t, q16, k16, v16, pos0,
+                                        seq_len > 0 ? seq_len : T);
+    return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }
 
 int db_launch_mean_pool(const float* x, int64_t ldx, int T, int D, float* out, cudaStream_t stream) {
-    mean_pool_kernel<<<(D + 127) / 128, 128, 0, stream>>>(x, ldx, T, D, out);
-    return (int)cudaGetLastError();
+    const cudaError_t e = db_launch_pdl(mean_pool_kernel, dim3((D + 127) / 128), dim3(128), 0, stream, x, ldx, T, D, out);
+    return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }
 
 int db_launch_fill_nan_if(float* y, int64_t n, const int* flag, cudaStream_t stream) {
