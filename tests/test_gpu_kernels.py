@@ -298,11 +298,12 @@ def test_fused_mlp_matches_unfused_oracle(db, oracle, bits, m, f, k):
 
 
 # ------------------------------------------------------------------ attention
-# Key-tile counts 1 to 8 (tiles of 128 keys: even and odd counts, ragged last tiles), GQA ratios
+# Key-tile counts 1 to 16 (tiles of 128 keys: even and odd counts, ragged last tiles), GQA ratios
 # 1, 2 and 4, and sharper softmaxes (scale 0.25: scores with a standard deviation of ~2.8).
 @pytest.mark.parametrize("t,hq,hk,scale", [(1, 2, 1, None), (65, 4, 2, None), (128, 2, 2, None),
                                            (129, 2, 1, None), (200, 4, 4, None), (300, 8, 2, None),
-                                           (300, 4, 1, 0.25), (1024, 16, 8, None), (1000, 4, 2, 0.25)])
+                                           (300, 4, 1, 0.25), (1024, 16, 8, None), (1000, 4, 2, 0.25),
+                                           (2048, 4, 1, 0.25)])
 def test_attention_matches_oracle(db, oracle, t, hq, hk, scale):
     rng = np.random.default_rng(t)
     q = rng.normal(0, 1, (t, hq, 128)).astype(np.float16)
