@@ -73,6 +73,7 @@ SIGNATURES = [
     ("db_linear_g64", _i32, [_vp, _i64, _i64, _vp, _vp, _i64, _i32, _i32, _i32, _vp, _vp, _vp]),
     ("db_linear_noalloc_scratch_bytes", _sz, []),
     ("db_linear_g64_noalloc", _i32, [_vp, _i64, _i64, _vp, _vp, _i64, _i32, _i32, _i32, _vp, _vp]),
+    ("db_linear_noalloc_error_word", _i32, []),
     ("db_project_packed", _i32, [_vp, _i64, _vp, _vp, _i64, _i32, _vp, _vp, _vp]),
     ("db_mlp_g64", _i32, [_vp, _i64, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _i32, _i32, _vp, _i64, _vp, _i64, _vp, _vp]),
     ("db_interleave_gate_up", _i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i32, _vp, _vp, _vp]),

@@ -153,15 +153,22 @@ int db_linear_g64(const float *x, int64_t M, int64_t K, const uint8_t *w_codes, 
  * memory (a fixed device-memory budget owned by the host, or a latency-critical caller that must
  * never reach cudaMalloc and its implicit synchronisation) and that cannot size a workspace up
  * front.  Its scratch is one array of DB_NOALLOC_SCRATCH_BYTES compiled into the library, held
- * by every GPU that loads it until the process exits; larger shapes are rejected with code
- * SCRATCH_LIMIT.  The first call on a device looks up the array's device address, so make it
- * before any stream capture.  All calls on a device share the array (the entry point clears what
+ * by every GPU that loads it until the process exits.  A call needs up256(M*Kp*2) +
+ * 2*up256(G*roundup(M,128)*4) + 256 bytes of it (up256 rounds up to 256; e.g. M = 1024 fits up
+ * to K = 3840, M = 4096 up to K = 960); larger shapes are rejected with code SCRATCH_LIMIT.
+ * The first call on a device looks up the array's device address, so make it before any stream
+ * capture.  All calls on a device share the array (the entry point clears what
  * must start at zero); calls that overlap on the GPU race on it and must be serialised by the
  * caller.  No cudaMalloc, cudaFree or allocating library routine is called. */
 #define DB_NOALLOC_SCRATCH_BYTES (8u << 20)
 size_t db_linear_noalloc_scratch_bytes(void);
 int db_linear_g64_noalloc(const float *x, int64_t M, int64_t K, const uint8_t *w_codes, const float *sw, int64_t N,
                           int weight_bits, int activation_bits, int fused, float *y, void *stream);
+/* The allocation-free entry point's own device error word (its GEMM's bounded-wait expiries; the
+ * word behind db_device_error_word() is allocated, so this path cannot use it): reads and clears
+ * it for the calling device, synchronously.  0 = no expiry since the last read; -1 = CUDA error.
+ * Like db_device_error_word(), read it after synchronising the stream of the calls it covers. */
+int db_linear_noalloc_error_word(void);
 
 /* Readout GEMV on one activation row.  Replaces packed::project (packed.rs:75-119; portable
  * numerics, activation 8-bit).  Returns DB_ERR_NONFINITE for a non-finite x. */
@@ -356,7 +363,7 @@ db_model *db_model_create_packed(int device, const db_encoder_config *cfg, const
  * needs resident weights. */
 int db_model_set_streaming(db_model *m, int enable, db_error *err);
 
-/* Device-resident variant for throughput measurement/* Device-resident variant for throughput measurement: ids already on the device, output left on
+/* Device-resident variant for throughput measurement: ids already on the device, output left on
  * the device; no host synchronisation.  Used by bench.py's device-timed leg. */
 int db_forward_device(db_model *m, const int32_t *ids_dev, int64_t n, float *out_dev, void *stream);
 

@@ -5,8 +5,9 @@ device-memory budget, or a latency-critical caller that must never reach cudaMal
 implicit device synchronisation.  For them the library offers a variant of the full projection
 whose scratch is a fixed array compiled into the library.  This file checks it through the C ABI
 against the allocating entry point (db_linear_g64), bit for bit, on consecutive calls that reuse
-the shared array, and checks that oversized shapes are refused.  It runs alone in a fresh process
-and after the rest of the suite (it is collected last on purpose).
+the shared array, at the largest shape the array holds and one past it, and checks that calls
+after the first allocate no device memory and leave the entry point's own error word clear.  The
+file is collected last on purpose; it also passes when run on its own.
 """
 import ctypes as C
 
@@ -78,3 +79,60 @@ def test_noalloc_rejects_shapes_beyond_its_scratch(db):
                                    C.c_void_p(x.data_ptr()), n, 4, 8, 1, C.c_void_p(x.data_ptr()), None)
     assert rc == -1
     assert lib.db_last_error_code().decode() == "SCRATCH_LIMIT"
+
+
+CODE_BYTES = 2  # bytes per activation code in the tensor-core layout the entry point quantises into
+
+
+def _need(m, k):
+    """Scratch bytes of one call, as the header documents the carve: codes, scales, sums, flag."""
+    up = lambda b: (b + 255) // 256 * 256
+    g = (k + 63) // 64
+    lds = (m + 127) // 128 * 128
+    return up(m * g * 64 * CODE_BYTES) + 2 * up(g * lds * 4) + 256
+
+
+def test_noalloc_at_the_end_of_its_scratch(db):
+    lib = db.load()
+    cap = lib.db_linear_noalloc_scratch_bytes()
+    k, n = 960, 256
+    m = 4096
+    while _need(m + 128, k) <= cap:
+        m += 128
+    assert _need(m, k) <= cap < _need(m + 128, k)
+    codes, scales = _weights(db, n, k, 4, seed=9)
+    x = torch.from_numpy(np.random.default_rng(9).normal(0, 1, (m, k)).astype(np.float32)).cuda()
+    a, b = _both(db, x, codes, scales, n, 4)
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    # the first shape past the array is refused
+    m2 = m + 1
+    while _need(m2, k) <= cap:
+        m2 += 1
+    x2 = torch.zeros((m2, k), device="cuda")
+    y2 = torch.zeros((m2, n), device="cuda")
+    rc = lib.db_linear_g64_noalloc(C.c_void_p(x2.data_ptr()), m2, k, C.c_void_p(codes.data_ptr()),
+                                   C.c_void_p(scales.data_ptr()), n, 4, 8, 1, C.c_void_p(y2.data_ptr()), None)
+    assert rc == -1 and lib.db_last_error_code().decode() == "SCRATCH_LIMIT"
+
+
+def test_noalloc_allocates_nothing_after_the_first_call_and_reports_no_expiry(db):
+    lib = db.load()
+    m, k, n = 512, 1024, 1024
+    codes, scales = _weights(db, n, k, 8, seed=4)
+    x = torch.randn(m, k, device="cuda")
+    y = torch.empty((m, n), device="cuda")
+    stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+    def call():
+        rc = lib.db_linear_g64_noalloc(C.c_void_p(x.data_ptr()), m, k, C.c_void_p(codes.data_ptr()),
+                                       C.c_void_p(scales.data_ptr()), n, 8, 8, 1, C.c_void_p(y.data_ptr()), stream)
+        assert rc == 0, db._lib.last_error()
+
+    call()  # set-up: looks up the array's address on this device
+    torch.cuda.synchronize()
+    free_before = torch.cuda.mem_get_info()[0]
+    for _ in range(5):
+        call()
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info()[0] == free_before
+    assert lib.db_linear_noalloc_error_word() == 0
