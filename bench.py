@@ -362,11 +362,13 @@ def run_gemm(args, local_rank):
     x = np.random.default_rng(0).normal(0, 1, (m, k)).astype(np.float16)
     codes, scales = db.pack_weights(torch.from_numpy(w.view(np.int16)).cuda(), args.bits)
     xt = torch.from_numpy(x).cuda()
-    a, sa, _ = db.quantize_activations(xt, bits=8, layout=db.CODES_TC)
+    layout = db.CODES_TC if args.layout == "tc" else db.CODES_NATURAL
+    a, sa, _ = db.quantize_activations(xt, bits=8, layout=layout)
     y = torch.empty((m, n), dtype=torch.float32, device="cuda")
     flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device="cuda")
+    cfg = db.GemmConfig(*(int(v) for v in args.gemm_config.split(","))) if args.gemm_config else None
     for _ in range(args.warmup):
-        db.gemm(a, db.CODES_TC, sa, codes, scales, m, n, k, args.bits, residual=y)
+        db.gemm(a, layout, sa, codes, scales, m, n, k, args.bits, residual=y, config=cfg)
     torch.cuda.synchronize()
     times = []
     for _ in range(args.steps):
@@ -374,14 +376,15 @@ def run_gemm(args, local_rank):
         torch.cuda._sleep(200_000)  # the launch is queued before the start event fires
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
-        db.gemm(a, db.CODES_TC, sa, codes, scales, m, n, k, args.bits, residual=y)
+        db.gemm(a, layout, sa, codes, scales, m, n, k, args.bits, residual=y, config=cfg)
         e.record()
         torch.cuda.synchronize()
         times.append(s.elapsed_time(e))
     us = float(np.mean(times)) * 1e3
     flops = 2.0 * m * n * k
     peak_tf, peak_gbs, kind = measured_peaks()
-    out = {"workload": f"gemm W{args.bits}A8 g64 M={m} K={k} N={n}", "us_per_launch": us,
+    out = {"workload": f"gemm W{args.bits}A8 g64 M={m} K={k} N={n}", "layout": args.layout,
+           "config": args.gemm_config or "default", "us_per_launch": us,
            "tflops": flops / us / 1e6, "frac_of_bf16_peak": flops / us / 1e6 / peak_tf, "peak_kind": kind,
            "launches": args.steps, "l2": "flushed between launches"}
     print(json.dumps(out), flush=True)
@@ -562,6 +565,9 @@ def main():
     ap.add_argument("--gemv-rows", default="1,4,8", help="activation rows (M) for --workload gemv")
     ap.add_argument("--gemm-shape", default="1024,1024,3072", help="M,K,N for --workload gemm")
     ap.add_argument("--bits", type=int, default=4)
+    ap.add_argument("--layout", default="i8", choices=["i8", "tc"],
+                    help="activation codes of --workload gemm: int8 (kind::i8 kernel) or f16 (kind::f16 kernel)")
+    ap.add_argument("--gemm-config", default="", help="block_n,max_ctas,pair_ctas for --workload gemm")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))

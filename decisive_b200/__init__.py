@@ -211,13 +211,16 @@ def interleave_gate_up(gate_codes, gate_scales, up_codes, up_scales, F: int, K: 
 
 
 def mlp(a_codes, sa, gu_codes, gu_scales, M: int, F: int, K: int, bits: int, fused: bool = True, nonfinite=None):
-    """Fused gate/up + SiLU*up + re-quantisation (grouped_q4_mlp.wgsl) -> (codes TC [M, F], scales [F/64, M])."""
+    """Fused gate/up + SiLU*up + re-quantisation (grouped_q4_mlp.wgsl) -> (codes [M, F], scales [F/64, M]).
+    The code layout follows a_codes: f16 tensor-core codes (db_mlp_g64) or int8 natural codes
+    (db_mlp_g64_natural, the kind::i8 path)."""
     import torch
-    codes = torch.zeros((M, F), dtype=torch.float16, device=a_codes.device)
+    natural = a_codes.dtype == torch.int8
+    codes = torch.zeros((M, F), dtype=torch.int8 if natural else torch.float16, device=a_codes.device)
     scales = torch.zeros((F // GROUP, scale_stride(M)), dtype=torch.float32, device=a_codes.device)
-    check(load().db_mlp_g64(_ptr(a_codes), a_codes.stride(0), _ptr(sa), sa.stride(0), _ptr(gu_codes), _ptr(gu_scales),
-                            M, F, K, bits, int(fused), _ptr(codes), F, _ptr(scales), scale_stride(M), _ptr(nonfinite),
-                            _stream()))
+    fn = load().db_mlp_g64_natural if natural else load().db_mlp_g64
+    check(fn(_ptr(a_codes), a_codes.stride(0), _ptr(sa), sa.stride(0), _ptr(gu_codes), _ptr(gu_scales),
+             M, F, K, bits, int(fused), _ptr(codes), F, _ptr(scales), scale_stride(M), _ptr(nonfinite), _stream()))
     return codes, scales
 
 
@@ -491,6 +494,11 @@ class Model:
     def use_graphs(self, enable: bool = True):
         """Forward as a captured CUDA graph per token count (default on); bit-identical either way."""
         check(load().db_model_use_graphs(self._h, int(enable)))
+
+    def set_code_layout(self, layout: int):
+        """CODES_NATURAL (int8 codes, kind::i8 GEMM; default) or CODES_TC (f16 codes, kind::f16 GEMM);
+        bit-identical outputs either way."""
+        check(load().db_model_set_code_layout(self._h, int(layout)))
 
     def profile(self, enable: bool = True):
         check(load().db_model_profile(self._h, int(enable)))

@@ -76,6 +76,7 @@ SIGNATURES = [
     ("db_linear_noalloc_error_word", _i32, []),
     ("db_project_packed", _i32, [_vp, _i64, _vp, _vp, _i64, _i32, _vp, _vp, _vp]),
     ("db_mlp_g64", _i32, [_vp, _i64, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _i32, _i32, _vp, _i64, _vp, _i64, _vp, _vp]),
+    ("db_mlp_g64_natural", _i32, [_vp, _i64, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _i32, _i32, _vp, _i64, _vp, _i64, _vp, _vp]),
     ("db_interleave_gate_up", _i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i32, _vp, _vp, _vp]),
     ("db_attention", _i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _f, _vp, _i64, _vp]),
     ("db_synthetic_bf16", _i32, [C.c_uint64, C.c_uint64, _i64, _f, _vp, _vp]),
@@ -97,6 +98,7 @@ SIGNATURES = [
     ("db_predict_continuations", _i32, [_vp, _vp, _vp, _sz, _vp, _sz, _sz, _vp, _vp, C.POINTER(DbError)]),
     ("db_cache_stats", _i32, [_vp, _vp, _vp, _vp]),
     ("db_model_profile", _i32, [_vp, _i32]),
+    ("db_model_set_code_layout", _i32, [_vp, _i32]),
     ("db_model_use_graphs", _i32, [_vp, _i32]),
     ("db_model_export_packed", _i32, [_vp, C.c_char_p, C.POINTER(DbError)]),
     ("db_model_set_streaming", _i32, [_vp, _i32, C.POINTER(DbError)]),

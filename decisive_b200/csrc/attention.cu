@@ -65,9 +65,9 @@ __device__ __forceinline__ void load_tile(uint32_t dst, const __half* base, int 
 // value (the NaN guard of Matrix::apply, int8.rs:170-173).
 __global__ void __launch_bounds__(ATT_THREADS)
     attention_kernel(const __half* __restrict__ q16, const __half* __restrict__ k16, const __half* __restrict__ v16,
-                     int T, int Hq, int Hk, float scale_log2, __half* __restrict__ codes, int64_t ldc,
-                     float* __restrict__ scales, int64_t lds, int* __restrict__ nonfinite, const __half* __restrict__ kp, const __half* __restrict__ vp, int P,
-                     int causal) {
+                     int T, int Hq, int Hk, float scale_log2, void* __restrict__ codes, int64_t ldc,
+                     float* __restrict__ scales, int64_t lds, int* __restrict__ nonfinite, const __half* __restrict__ kp,
+                     const __half* __restrict__ vp, int P, int causal, int codes_i8) {
     extern __shared__ __align__(128) uint8_t smem[];
     const uint32_t sQ = smem_u32(smem);
     const uint32_t sK[2] = {sQ + ATT_TILE_BYTES, sQ + 2 * ATT_TILE_BYTES};
@@ -206,10 +206,13 @@ __global__ void __launch_bounds__(ATT_THREADS)
     {
         // Rows r0 and r0 + 8 of this warp: 16 values per 64-wide group per thread, the rest of the
         // group on the other three lanes of the quad.  Codes go through shared memory (the Q tile,
-        // free after the last iteration's barrier) in the tensor-core order k0,k4,k1,k5,k2,k6,k3,k7
-        // of every 8 consecutive features, then out as 16-byte rows.
+        // free after the last iteration's barrier) -- f16 codes in the tensor-core order
+        // k0,k4,k1,k5,k2,k6,k3,k7 of every 8 consecutive features, or int8 codes in natural order
+        // (codes_i8) -- then out as 16-byte rows.
         const int q = lane & 3;
-        const int pos0 = (q < 2) ? 4 * q : 4 * (q - 2) + 1;  // stored position of feature 2q in its 8-block
+        // stored position of feature 2q in its 8-block, and the step to feature 2q + 1
+        const int pos0 = codes_i8 ? 2 * q : (q < 2) ? 4 * q : 4 * (q - 2) + 1;
+        const int pos1 = codes_i8 ? 1 : 2;
         bool bad = false;
 #pragma unroll
         for (int grp = 0; grp < 2; ++grp) {
@@ -234,10 +237,15 @@ __global__ void __launch_bounds__(ATT_THREADS)
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
                     const int col = grp * 64 + i * 8 + pos0;  // feature grp*64 + 8i + 2q and its neighbour
-                    const __half c0 = __float2half_rn(fminf(fmaxf(rintf(__fmul_rn(v[2 * i], rinv)), -127.f), 127.f));
-                    const __half c1 = __float2half_rn(fminf(fmaxf(rintf(__fmul_rn(v[2 * i + 1], rinv)), -127.f), 127.f));
-                    reinterpret_cast<__half*>(smem)[row * ATT_D + col] = c0;
-                    reinterpret_cast<__half*>(smem)[row * ATT_D + col + 2] = c1;
+                    const float c0 = fminf(fmaxf(rintf(__fmul_rn(v[2 * i], rinv)), -127.f), 127.f);
+                    const float c1 = fminf(fmaxf(rintf(__fmul_rn(v[2 * i + 1], rinv)), -127.f), 127.f);
+                    if (codes_i8) {
+                        reinterpret_cast<int8_t*>(smem)[row * ATT_D + col] = (int8_t)(int)c0;
+                        reinterpret_cast<int8_t*>(smem)[row * ATT_D + col + pos1] = (int8_t)(int)c1;
+                    } else {
+                        reinterpret_cast<__half*>(smem)[row * ATT_D + col] = __float2half_rn(c0);
+                        reinterpret_cast<__half*>(smem)[row * ATT_D + col + pos1] = __float2half_rn(c1);
+                    }
                 }
                 const int t = q0 + row;
                 if (q == 0 && t < T) scales[(size_t)(h * 2 + grp) * lds + rb + t] = scale;
@@ -245,15 +253,27 @@ __global__ void __launch_bounds__(ATT_THREADS)
         }
         if (bad) atomicOr(nonfinite, 1);
         __syncthreads();
-        // 64 rows x 256 bytes: 16-byte chunks, 16 per row
+        // 64 rows x 256 bytes (f16) or 128 bytes (int8): 16-byte chunks, 16 or 8 per row
+        if (codes_i8) {
 #pragma unroll
-        for (int i = 0; i < (ATT_BQ * 16) / ATT_THREADS; ++i) {
-            const int idx = tid + i * ATT_THREADS;
-            const int row = idx >> 4, chunk = idx & 15;
-            const int t = q0 + row;
-            if (t < T)
-                *reinterpret_cast<uint4*>(codes + (size_t)(rb + t) * ldc + h * ATT_D + chunk * 8) =
-                    reinterpret_cast<const uint4*>(smem)[row * 16 + chunk];
+            for (int i = 0; i < (ATT_BQ * 8) / ATT_THREADS; ++i) {
+                const int idx = tid + i * ATT_THREADS;
+                const int row = idx >> 3, chunk = idx & 7;
+                const int t = q0 + row;
+                if (t < T)
+                    *reinterpret_cast<uint4*>(static_cast<int8_t*>(codes) + (size_t)(rb + t) * ldc + h * ATT_D +
+                                              chunk * 16) = reinterpret_cast<const uint4*>(smem)[row * 8 + chunk];
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < (ATT_BQ * 16) / ATT_THREADS; ++i) {
+                const int idx = tid + i * ATT_THREADS;
+                const int row = idx >> 4, chunk = idx & 15;
+                const int t = q0 + row;
+                if (t < T)
+                    *reinterpret_cast<uint4*>(static_cast<__half*>(codes) + (size_t)(rb + t) * ldc + h * ATT_D +
+                                              chunk * 8) = reinterpret_cast<const uint4*>(smem)[row * 16 + chunk];
+            }
         }
     }
 }
@@ -269,20 +289,20 @@ int db_launch_attention(const __half* q16, const __half* k16, const __half* v16,
 }
 
 int db_launch_attention_quant(const __half* q16, const __half* k16, const __half* v16, int T, int Hq, int Hk,
-                              float scale, __half* codes, int64_t ldc, float* scales, int64_t lds, int* nonfinite,
-                              cudaStream_t stream) {
+                              float scale, void* codes, int64_t ldc, float* scales, int64_t lds, int* nonfinite,
+                              cudaStream_t stream, int codes_i8) {
     if (!codes) return (int)cudaErrorInvalidValue;
     return db_launch_attention_tc(q16, k16, v16, 1, T, Hq, Hk, scale, nullptr, 0, codes, ldc, scales, lds, nonfinite,
-                                  stream);
+                                  stream, codes_i8);
 }
 
 int db_launch_attention_prefix_quant(const __half* q16, const __half* k16, const __half* v16, int B, int T,
                                      const __half* kp, const __half* vp, int P, int causal, int Hq, int Hk,
-                                     float scale, __half* codes, int64_t ldc, float* scales, int64_t lds,
-                                     int* nonfinite, cudaStream_t stream) {
+                                     float scale, void* codes, int64_t ldc, float* scales, int64_t lds,
+                                     int* nonfinite, cudaStream_t stream, int codes_i8) {
     if (T <= 0 || B <= 0) return 0;
-    if (Hk <= 0 || Hq % Hk || !codes || !scales || !nonfinite || (ldc & 7) || P < 0 || (P > 0 && (!kp || !vp)) ||
-        B > 65535)
+    if (Hk <= 0 || Hq % Hk || !codes || !scales || !nonfinite || (ldc & (codes_i8 ? 15 : 7)) || P < 0 ||
+        (P > 0 && (!kp || !vp)) || B > 65535)
         return (int)cudaErrorInvalidValue;
     const int smem = 5 * ATT_TILE_BYTES;
     {
@@ -291,6 +311,7 @@ int db_launch_attention_prefix_quant(const __half* q16, const __half* k16, const
     }
     dim3 grid((T + ATT_BQ - 1) / ATT_BQ, Hq, B);
     attention_kernel<<<grid, ATT_THREADS, smem, stream>>>(q16, k16, v16, T, Hq, Hk, scale * 1.4426950408889634f,
-                                                          codes, ldc, scales, lds, nonfinite, kp, vp, P, causal);
+                                                          codes, ldc, scales, lds, nonfinite, kp, vp, P, causal,
+                                                          codes_i8);
     return (int)cudaGetLastError();
 }

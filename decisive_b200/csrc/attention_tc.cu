@@ -163,9 +163,9 @@ template <bool QUANT>
 __global__ void __launch_bounds__(AT_THREADS, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV, int T, int Hq, int Hk, float scale_log2,
-                        float* __restrict__ out, int64_t ldo, __half* __restrict__ codes, int64_t ldc,
+                        float* __restrict__ out, int64_t ldo, void* __restrict__ codes, int64_t ldc,
                         float* __restrict__ scales, int64_t lds, int* __restrict__ nonfinite,
-                        int* __restrict__ dev_error) {
+                        int* __restrict__ dev_error, int codes_i8) {
     pdl_wait();
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -505,16 +505,36 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
                     }
                     const float scale = fmaxf(__fdiv_rn(amax, 127.f), FLT_MIN);
                     const float rinv = __fdiv_rn(1.f, scale);
-                    __half* dst = codes + orow * ldc + h * AT_D + 64 * b;
+                    if (codes_i8) {
+                        // int8 codes in natural order
+                        int8_t* dst = static_cast<int8_t*>(codes) + orow * ldc + h * AT_D + 64 * b;
 #pragma unroll
-                    for (int g8 = 0; g8 < 8; ++g8) {
-                        float c8[8];
+                        for (int g16 = 0; g16 < 4; ++g16) {
+                            uint32_t wd[4];
 #pragma unroll
-                        for (int e = 0; e < 8; ++e)
-                            c8[e] = fminf(fmaxf(rintf(__fmul_rn(v[8 * g8 + e], rinv)), -127.f), 127.f);
-                        const uint4 w = make_uint4(pack_f16x2(c8[0], c8[4]), pack_f16x2(c8[1], c8[5]),
-                                                   pack_f16x2(c8[2], c8[6]), pack_f16x2(c8[3], c8[7]));
-                        *reinterpret_cast<uint4*>(dst + 8 * g8) = w;
+                            for (int wq = 0; wq < 4; ++wq) {
+                                uint32_t word = 0;
+#pragma unroll
+                                for (int e = 0; e < 4; ++e) {
+                                    const float c = fminf(fmaxf(rintf(__fmul_rn(v[16 * g16 + 4 * wq + e], rinv)), -127.f), 127.f);
+                                    word |= ((uint32_t)(int)c & 0xFFu) << (8 * e);
+                                }
+                                wd[wq] = word;
+                            }
+                            *reinterpret_cast<uint4*>(dst + 16 * g16) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+                        }
+                    } else {
+                        __half* dst = static_cast<__half*>(codes) + orow * ldc + h * AT_D + 64 * b;
+#pragma unroll
+                        for (int g8 = 0; g8 < 8; ++g8) {
+                            float c8[8];
+#pragma unroll
+                            for (int e = 0; e < 8; ++e)
+                                c8[e] = fminf(fmaxf(rintf(__fmul_rn(v[8 * g8 + e], rinv)), -127.f), 127.f);
+                            const uint4 w = make_uint4(pack_f16x2(c8[0], c8[4]), pack_f16x2(c8[1], c8[5]),
+                                                       pack_f16x2(c8[2], c8[6]), pack_f16x2(c8[3], c8[7]));
+                            *reinterpret_cast<uint4*>(dst + 8 * g8) = w;
+                        }
                     }
                     scales[(size_t)(h * 2 + b) * lds + orow] = scale;
                     if (bad) atomicOr(nonfinite, 1);
@@ -565,11 +585,12 @@ using namespace db;
 // q16 [B*T, Hq, 128], k16/v16 [B*T, Hk, 128] (f16, 16-byte aligned); either out (f32, row stride
 // ldo) or codes/scales/nonfinite (quantised for the output projection) receives the context.
 int db_launch_attention_tc(const __half* q16, const __half* k16, const __half* v16, int B, int T, int Hq, int Hk,
-                           float scale, float* out, int64_t ldo, __half* codes, int64_t ldc, float* scales,
-                           int64_t lds, int* nonfinite, cudaStream_t stream) {
+                           float scale, float* out, int64_t ldo, void* codes, int64_t ldc, float* scales,
+                           int64_t lds, int* nonfinite, cudaStream_t stream, int codes_i8) {
     if (T <= 0 || B <= 0) return 0;
     const bool quant = codes != nullptr;
-    if (Hk <= 0 || Hq % Hk || Hq > 65535 || B > 65535 || (quant && (!scales || !nonfinite || (ldc & 7))) ||
+    if (Hk <= 0 || Hq % Hk || Hq > 65535 || B > 65535 ||
+        (quant && (!scales || !nonfinite || (ldc & (codes_i8 ? 15 : 7)))) ||
         (!quant && (!out || (ldo & 3))))
         return (int)cudaErrorInvalidValue;
     if ((reinterpret_cast<uintptr_t>(q16) | reinterpret_cast<uintptr_t>(k16) | reinterpret_cast<uintptr_t>(v16)) & 15)
@@ -591,6 +612,7 @@ int db_launch_attention_tc(const __half* q16, const __half* k16, const __half* v
     }
     const dim3 grid((unsigned)((T + AT_Q - 1) / AT_Q), (unsigned)Hq, (unsigned)B);
     const cudaError_t e = db_launch_pdl(kernel, grid, dim3(AT_THREADS), AT_SMEM, stream, tmQ, tmK, tmV, T, Hq, Hk,
-                                        scale * 1.4426950408889634f, out, ldo, codes, ldc, scales, lds, nonfinite, err);
+                                        scale * 1.4426950408889634f, out, ldo, codes, ldc, scales, lds, nonfinite, err,
+                                        codes_i8);
     return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }

@@ -172,8 +172,8 @@ int db_gemm_g64_config(const void* a_codes, int layout, int64_t lda, const float
                      bits, fused, residual, y, ldy, nonfinite};
         return db_cuda_status(db_launch_gemv(g, S(stream)), "gemv");
     }
-    if (layout != DB_CODES_TC)
-        return db_fail(DB_ERR_INVALID_ARGUMENT, "INVALID_ARGUMENT", "gemm: natural layout is not a GEMM input");
+    if (layout != DB_CODES_TC && layout != DB_CODES_NATURAL)
+        return db_fail(DB_ERR_INVALID_ARGUMENT, "INVALID_ARGUMENT", "gemm: unknown code layout");
     DbGemmArgs a{};
     a.a_codes = a_codes;
     a.lda = lda;
@@ -196,8 +196,46 @@ int db_gemm_g64_config(const void* a_codes, int layout, int64_t lda, const float
         a.max_ctas = config->max_ctas;
         a.pair_ctas = config->pair_ctas;
     }
+    if (layout == DB_CODES_NATURAL) {
+        if (!config) {
+            const db_gemm_config d = db_gemm_i8_default_config(M, N, a.epilogue);
+            a.block_n = d.block_n;
+            a.pair_ctas = d.pair_ctas;
+        }
+        return db_cuda_status(db_launch_gemm_i8(a, S(stream)), "gemm");
+    }
     return db_cuda_status(db_launch_gemm_tc(a, S(stream)), "gemm");
 }
+
+}  // extern "C"
+
+// Tile configuration of the int8 tensor-core GEMM when none is given: the widest tile (and CTA
+// pairs) that still occupies the SMs -- each candidate is scored by the fraction of the last
+// wave of CTAs that has work, with a small preference for wide tiles (fewer re-reads of A per
+// output) and for pairs (half of the weight tile per CTA).
+db_gemm_config db_gemm_i8_default_config(int64_t M, int64_t N, int epilogue) {
+    const int sms = db_num_sms();
+    const int cands[6][2] = {{256, 1}, {128, 1}, {64, 1}, {256, 0}, {128, 0}, {64, 0}};
+    double best = -1.0;
+    db_gemm_config out{256, 0, M > 128 ? 1 : 0};
+    for (const auto& c : cands) {
+        const int bn = c[0], pair = c[1];
+        if (pair && M <= 128) continue;
+        if (epilogue == DB_EPI_SWIGLU_QUANT && bn == 64) continue;
+        const int64_t mt = pair ? 256 : 128;
+        const int64_t ctas = ((M + mt - 1) / mt) * ((N + bn - 1) / bn) * (pair ? 2 : 1);
+        const int64_t waves = (ctas + sms - 1) / sms;
+        const double fill = (double)ctas / (double)(waves * sms);
+        const double score = fill * (bn == 256 ? 1.0 : bn == 128 ? 0.93 : 0.85) * (pair ? 1.0 : 0.97);
+        if (score > best + 1e-9) {
+            best = score;
+            out = db_gemm_config{bn, 0, pair};
+        }
+    }
+    return out;
+}
+
+extern "C" {
 
 size_t db_linear_workspace_bytes(int64_t M, int64_t K) {
     const int64_t G = groups_of(K), Kp = G * DB_GROUP;
@@ -361,6 +399,38 @@ int db_mlp_g64(const void* a_codes, int64_t lda, const float* sa, int64_t ldsa, 
     a.nonfinite = nonfinite;
     a.dev_error = db_device_error_ptr();
     return db_cuda_status(db_launch_gemm_tc(a, S(stream)), "mlp");
+}
+
+int db_mlp_g64_natural(const void* a_codes, int64_t lda, const float* sa, int64_t ldsa, const uint8_t* w_gu_codes,
+                       const float* w_gu_scales, int64_t M, int64_t F, int64_t K, int bits, int fused, void* out_codes,
+                       int64_t ldoc, float* out_scales, int64_t ldos, const int* nonfinite, void* stream) {
+    if (M < 0 || F <= 0 || F % DB_GROUP || K <= 0 || (bits != 4 && bits != 8) || ldoc < F || (ldoc & 15) ||
+        ldos < db_scale_stride(M) || (ldos & 3))
+        return db_fail(DB_ERR_INVALID_ARGUMENT, "INVALID_ARGUMENT", "mlp: bad shape");
+    if (M == 0) return DB_OK;
+    DbGemmArgs a{};
+    a.a_codes = a_codes;
+    a.lda = lda;
+    a.sa = sa;
+    a.ldsa = ldsa;
+    a.w_codes = w_gu_codes;
+    a.sw = w_gu_scales;
+    a.M = (int)M;
+    a.N = (int)(2 * F);
+    a.K = (int)K;
+    a.bits = bits;
+    a.fused = fused;
+    a.epilogue = DB_EPI_SWIGLU_QUANT;
+    a.out_codes = out_codes;
+    a.ldoc = ldoc;
+    a.out_scales = out_scales;
+    a.ldos = ldos;
+    a.nonfinite = nonfinite;
+    a.dev_error = db_device_error_ptr();
+    const db_gemm_config d = db_gemm_i8_default_config(M, 2 * F, DB_EPI_SWIGLU_QUANT);
+    a.block_n = d.block_n;
+    a.pair_ctas = d.pair_ctas;
+    return db_cuda_status(db_launch_gemm_i8(a, S(stream)), "mlp");
 }
 
 }  // extern "C"

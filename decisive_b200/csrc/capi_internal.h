@@ -12,4 +12,6 @@ int* db_device_error_ptr();
 #include <stdint.h>
 #include "../../include/decisive_b200.h"
 int db_tune_gemm_shape(int64_t M, int64_t N, int64_t K, int bits, int epilogue, const char* cache_path,
-                       db_gemm_config* choice, std::string* report, cudaStream_t stream);
+                       db_gemm_config* choice, std::string* report, cudaStream_t stream, bool i8);
+// Default tile configuration of the int8 (kind::i8) tensor-core GEMM for an M x N output.
+db_gemm_config db_gemm_i8_default_config(int64_t M, int64_t N, int epilogue);

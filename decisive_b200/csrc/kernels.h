@@ -67,6 +67,11 @@ struct DbGemmArgs {
     int add_bias;
 };
 int db_launch_gemm_tc(const DbGemmArgs& args, cudaStream_t stream);
+// The same GEMM on int8 activation codes in natural order (DB_CODES_NATURAL_I8, a_codes [M, lda]
+// bytes, lda % 16 == 0) with tcgen05 kind::i8 MMAs (gemm_i8.cuh).  Tile widths 64/128/256
+// (default 256; the SwiGLU epilogue always 256, writing int8 natural codes to out_codes),
+// optional CTA pairs (M = 256 MMAs), scale blocks of 64 or (Q8 only) 32.
+int db_launch_gemm_i8(const DbGemmArgs& args, cudaStream_t stream);
 
 // Small-M path: int8 A codes (GEMV order) [M, lda] + sums [G, ldsa], sa [G, ldsa].
 struct DbGemvArgs {

@@ -20,22 +20,23 @@ int db_launch_fill_nan_if(float* y, int64_t n, const int* flag, cudaStream_t str
 int db_launch_attention(const __half* q16, const __half* k16, const __half* v16, int T, int Hq, int Hk, float scale,
                         float* out, int64_t ldo, cudaStream_t stream);
 // Same attention, writing the context already quantised for the output projection: f16 codes in
-// tensor-core order [T, ldc] (head h occupies features 128h..128h+127), per-64 scales [2*Hq, lds];
-// *nonfinite is raised when a context value is not finite.
+// tensor-core order [T, ldc], or with codes_i8 int8 codes in natural order [T, ldc] (ldc % 16 == 0)
+// (head h occupies features 128h..128h+127), per-64 scales [2*Hq, lds]; *nonfinite is raised
+// when a context value is not finite.
 int db_launch_attention_quant(const __half* q16, const __half* k16, const __half* v16, int T, int Hq, int Hk,
-                              float scale, __half* codes, int64_t ldc, float* scales, int64_t lds, int* nonfinite,
-                              cudaStream_t stream);
+                              float scale, void* codes, int64_t ldc, float* scales, int64_t lds, int* nonfinite,
+                              cudaStream_t stream, int codes_i8 = 0);
 // The tensor-core (tcgen05) attention behind the two calls above: B items of T rows each
 // (q16/k16/v16 and the outputs hold the items one after another, 16-byte aligned), non-causal;
 // the context goes to out (f32) when codes is null, else quantised as above.
 int db_launch_attention_tc(const __half* q16, const __half* k16, const __half* v16, int B, int T, int Hq, int Hk,
-                           float scale, float* out, int64_t ldo, __half* codes, int64_t ldc, float* scales,
-                           int64_t lds, int* nonfinite, cudaStream_t stream);
+                           float scale, float* out, int64_t ldo, void* codes, int64_t ldc, float* scales,
+                           int64_t lds, int* nonfinite, cudaStream_t stream, int codes_i8 = 0);
 // Decoder form of the quantising attention: B items of T rows each (q16/k16/v16 and the outputs
 // hold the items one after another); every item's keys are the P cached prefix keys kp/vp
 // [P, Hk, 128] (shared by the items; P = 0: none) followed by its own T keys, which are causal
 // (row i sees own keys 0..i) when causal != 0.
 int db_launch_attention_prefix_quant(const __half* q16, const __half* k16, const __half* v16, int B, int T,
                                      const __half* kp, const __half* vp, int P, int causal, int Hq, int Hk,
-                                     float scale, __half* codes, int64_t ldc, float* scales, int64_t lds,
-                                     int* nonfinite, cudaStream_t stream);
+                                     float scale, void* codes, int64_t ldc, float* scales, int64_t lds,
+                                     int* nonfinite, cudaStream_t stream, int codes_i8 = 0);

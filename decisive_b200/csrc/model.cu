@@ -97,6 +97,9 @@ struct db_model {
     }
     // tile configurations chosen by db_model_tune for qkv, o, gate/up, down (zero = defaults)
     db_gemm_config tuned[4] = {};
+    // activation codes of the projections: int8 natural order through the kind::i8 GEMM (default),
+    // or f16 codes through the kind::f16 GEMM (db_model_set_code_layout)
+    bool i8 = true;
     // per-launch CUDA-event profiling (mirror of the reference's projection_ms accounting,
     // cpu.rs:8-16 / native.rs:229-258), enabled by db_model_profile
     bool profile = false;
@@ -346,6 +349,20 @@ int enqueue_forward(db_model* m, int T, const volatile uint8_t* cancel, const Pa
     rc = timed(0, [&] {
         return db_launch_dequant_rows(m->emb_c, m->emb_s, c.vocab, D, bits, m->ids, R, m->x, D, m->flag, st);
     });
+    const int code_layout = m->i8 ? DB_CODES_NATURAL_I8 : DB_CODES_TC_F16;
+    // one projection; the tuned tile configuration, else the i8 path's default for the shape
+    auto launch = [&](int proj, DbGemmArgs& g) {
+        g.block_n = m->tuned[proj].block_n;
+        g.max_ctas = m->tuned[proj].max_ctas;
+        g.pair_ctas = m->tuned[proj].pair_ctas;
+        if (!m->i8) return db_launch_gemm_tc(g, st);
+        if (g.block_n == 0) {
+            const db_gemm_config d = db_gemm_i8_default_config(g.M, g.N, g.epilogue);
+            g.block_n = d.block_n;
+            g.pair_ctas = d.pair_ctas;
+        }
+        return db_launch_gemm_i8(g, st);
+    };
     auto gemm = [&](int proj, const void* a, const uint8_t* wc, const float* ws, const float* sa, int N, int K, int epi,
                     float* y, int64_t ldy) {
         DbGemmArgs g{};
@@ -369,10 +386,7 @@ int enqueue_forward(db_model* m, int T, const volatile uint8_t* cancel, const Pa
         g.ldos = lds;
         g.nonfinite = m->flag;
         g.dev_error = m->dev_err;
-        g.block_n = m->tuned[proj].block_n;
-        g.max_ctas = m->tuned[proj].max_ctas;
-        g.pair_ctas = m->tuned[proj].pair_ctas;
-        return db_launch_gemm_tc(g, st);
+        return launch(proj, g);
     };
     const float attn_scale = 1.f / sqrtf((float)c.head_dim);
     auto own_k = [&](int l) { return pass && pass->sk ? pass->sk[l] : m->k16; };
@@ -408,7 +422,7 @@ int enqueue_forward(db_model* m, int T, const volatile uint8_t* cancel, const Pa
         if (m->streaming) cudaStreamWaitEvent(st, m->uploaded[l & 1], 0);
         const LayerW w = m->streaming ? bank_layer(l) : m->layers[l];
         rc = timed(1, [&] {
-            return db_launch_rms_quantize(m->x, D, w.in_norm, R, D, c.eps, 0, nullptr, 0, m->acodes, DB_CODES_TC,
+            return db_launch_rms_quantize(m->x, D, w.in_norm, R, D, c.eps, 0, nullptr, 0, m->acodes, code_layout,
                                           ld_codes, m->sa, nullptr, lds, m->flag, st);
         });
         if (!rc) rc = timed(2, [&] { return gemm(0, m->acodes, w.qkv_c, w.qkv_s, m->sa, Nqkv, D, DB_EPI_STORE, m->qkv, Nqkv); });
@@ -423,18 +437,17 @@ int enqueue_forward(db_model* m, int T, const volatile uint8_t* cancel, const Pa
             rc = timed(4, [&] {
                 if (!c.causal && !pass)
                     return db_launch_attention_quant(m->q16, m->k16, m->v16, T, c.q_heads, c.kv_heads, attn_scale,
-                                                     static_cast<__half*>(m->acodes), ld_codes, m->sa, lds, m->flag, st);
+                                                     m->acodes, ld_codes, m->sa, lds, m->flag, st, m->i8);
                 return db_launch_attention_prefix_quant(m->q16, own_k(l), own_v(l), items, T,
                                                         pass && pass->pk ? pass->pk[l] : nullptr,
                                                         pass && pass->pv ? pass->pv[l] : nullptr, P, c.causal,
                                                         c.q_heads, c.kv_heads, attn_scale,
-                                                        static_cast<__half*>(m->acodes), ld_codes, m->sa, lds, m->flag,
-                                                        st);
+                                                        m->acodes, ld_codes, m->sa, lds, m->flag, st, m->i8);
             });
         if (!rc) rc = timed(6, [&] { return gemm(1, m->acodes, w.o_c, w.o_s, m->sa, D, Nq, DB_EPI_RESIDUAL, m->x, D); });
         if (!rc)
             rc = timed(1, [&] {
-                return db_launch_rms_quantize(m->x, D, w.post_norm, R, D, c.eps, 0, nullptr, 0, m->acodes, DB_CODES_TC,
+                return db_launch_rms_quantize(m->x, D, w.post_norm, R, D, c.eps, 0, nullptr, 0, m->acodes, code_layout,
                                               ld_codes, m->sa, nullptr, lds, m->flag, st);
             });
         if (!rc)
@@ -457,10 +470,7 @@ int enqueue_forward(db_model* m, int T, const volatile uint8_t* cancel, const Pa
             g.ldy = D;
             g.nonfinite = m->flag;
             g.dev_error = m->dev_err;
-            g.block_n = m->tuned[3].block_n;
-            g.max_ctas = m->tuned[3].max_ctas;
-            g.pair_ctas = m->tuned[3].pair_ctas;
-            return db_launch_gemm_tc(g, st);
+            return launch(3, g);
         });
         if (m->streaming) {
             cudaEventRecord(m->consumed[l & 1], st);
@@ -844,6 +854,16 @@ int db_predict_batch(db_model* m, const int32_t* const* ids, const size_t* lens,
     return 0;
 }
 
+int db_model_set_code_layout(db_model* m, int layout) {
+    if (!m || (layout != DB_CODES_NATURAL && layout != DB_CODES_TC)) return DB_ERR_INVALID_ARGUMENT;
+    cudaSetDevice(m->device);
+    cudaStreamSynchronize(m->stream);
+    m->drop_graphs();
+    for (auto& t : m->tuned) t = db_gemm_config{0, 0, 0};  // tile choices belong to one kernel
+    m->i8 = layout == DB_CODES_NATURAL;
+    return DB_OK;
+}
+
 int db_model_use_graphs(db_model* m, int enable) {
     if (!m) return DB_ERR_INVALID_ARGUMENT;
     cudaSetDevice(m->device);
@@ -902,7 +922,7 @@ int db_model_tune(db_model* m, int64_t tokens, const char* cache_path, char* rep
     for (int p = 0; p < 4; ++p) {
         std::string rep;
         const int rc = db_tune_gemm_shape(tokens, shapes[p][0], shapes[p][1], m->cfg.weight_bits, (int)shapes[p][2],
-                                          cache_path, &chosen[p], &rep, m->stream);
+                                          cache_path, &chosen[p], &rep, m->stream, m->i8);
         if (rc) {
             fill_error(err, db_last_error_code(), db_last_error_message());
             return rc;

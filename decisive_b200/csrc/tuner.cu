@@ -36,6 +36,10 @@ __global__ void fill_codes_f16(__half* a, int64_t n, uint64_t seed) {
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
         a[i] = __int2half_rn((int)(mix32(seed + i) % 255u) - 127);
 }
+__global__ void fill_codes_i8(int8_t* a, int64_t n, uint64_t seed) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        a[i] = (int8_t)((int)(mix32(seed + i) % 255u) - 127);
+}
 __global__ void fill_bytes(uint8_t* w, int64_t n, uint64_t seed) {
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
         w[i] = (uint8_t)mix32(seed + i);
@@ -95,7 +99,7 @@ struct Buffers {
 
 }  // namespace
 
-std::string db_tuning_key(int64_t M, int64_t N, int64_t K, int bits, int epilogue) {
+std::string db_tuning_key(int64_t M, int64_t N, int64_t K, int bits, int epilogue, bool i8) {
     int dev = 0;
     cudaGetDevice(&dev);
     cudaDeviceProp p{};
@@ -105,33 +109,40 @@ std::string db_tuning_key(int64_t M, int64_t N, int64_t K, int bits, int epilogu
     std::ostringstream s;
     s << "decisive-b200-tuning-v1|" << p.name << '|' << p.multiProcessorCount << '|' << p.major << '.' << p.minor
       << '|' << driver << "|build " << __DATE__ << ' ' << __TIME__ << '|' << M << 'x' << N << 'x' << K << "|q"
-      << bits << "|epi" << epilogue;
+      << bits << "|epi" << epilogue << (i8 ? "|i8" : "|f16");
     char hex[17];
     std::snprintf(hex, sizeof hex, "%016llx", (unsigned long long)fnv1a(s.str()));
     return hex;
 }
 
-// Tunes one GEMM shape.  epilogue: DB_EPI_STORE, DB_EPI_RESIDUAL or DB_EPI_SWIGLU_QUANT.
+// Tunes one GEMM shape.  epilogue: DB_EPI_STORE, DB_EPI_RESIDUAL or DB_EPI_SWIGLU_QUANT.  i8: the
+// kind::i8 kernel on int8 codes (baseline: its default configuration for the shape), else the
+// kind::f16 kernel on f16 codes (baseline: 128-wide tiles).
 int db_tune_gemm_shape(int64_t M, int64_t N, int64_t K, int bits, int epilogue, const char* cache_path,
-                       db_gemm_config* choice, std::string* report, cudaStream_t s) {
+                       db_gemm_config* choice, std::string* report, cudaStream_t s, bool i8) {
     *choice = db_gemm_config{0, 0, 0};
     const int64_t G = (K + DB_GROUP - 1) / DB_GROUP, Kp = G * DB_GROUP;
     const int64_t lds = db_scale_stride(M), ldw = db_scale_stride(N);
     const bool swiglu = epilogue == DB_EPI_SWIGLU_QUANT;
     Buffers b;
-    __half* a = b.get<__half>((size_t)M * Kp);
+    void* a = i8 ? (void*)b.get<int8_t>((size_t)M * Kp) : (void*)b.get<__half>((size_t)M * Kp);
     float* sa = b.get<float>((size_t)G * lds);
     uint8_t* w = b.get<uint8_t>((size_t)N * Kp * bits / 8);
     float* sw = b.get<float>((size_t)G * ldw);
     float* y0 = b.get<float>((size_t)M * N);  // residual start values
     float* y = b.get<float>((size_t)M * N);
-    __half* oc = swiglu ? b.get<__half>((size_t)M * (N / 2)) : nullptr;
+    const size_t oc_bytes = swiglu ? (size_t)M * (N / 2) * (i8 ? 1 : 2) : 0;
+    void* oc = swiglu ? b.get<uint8_t>(oc_bytes) : nullptr;
     float* os = swiglu ? b.get<float>((size_t)(N / 128) * lds) : nullptr;
     int* flag = b.get<int>(64);
     int* err = b.get<int>(64);
     if (!a || !sa || !w || !sw || !y0 || !y || !flag || !err || (swiglu && (!oc || !os)))
         return db_fail(DB_ERR_CUDA, "RESOURCE_LIMIT", "tuner: device allocation failed");
-    fill_codes_f16<<<256, 256, 0, s>>>(a, M * Kp, 1);
+    auto fill_a = [&]() {
+        if (i8) fill_codes_i8<<<256, 256, 0, s>>>(static_cast<int8_t*>(a), M * Kp, 1);
+        else fill_codes_f16<<<256, 256, 0, s>>>(static_cast<__half*>(a), M * Kp, 1);
+    };
+    fill_a();
     fill_bytes<<<256, 256, 0, s>>>(w, N * Kp * bits / 8, 2);
     fill_scales<<<64, 256, 0, s>>>(sa, G * lds, 3);
     fill_scales<<<64, 256, 0, s>>>(sw, G * ldw, 4);
@@ -170,7 +181,7 @@ int db_tune_gemm_shape(int64_t M, int64_t N, int64_t K, int bits, int epilogue, 
         g.block_n = c.block_n;
         g.max_ctas = c.max_ctas;
         g.pair_ctas = c.pair_ctas;
-        return db_launch_gemm_tc(g, s);
+        return i8 ? db_launch_gemm_i8(g, s) : db_launch_gemm_tc(g, s);
     };
     // one launch on a fresh copy of the residual input (the output the bitwise check reads)
     auto run = [&](const db_gemm_config& c) -> int {
@@ -179,7 +190,7 @@ int db_tune_gemm_shape(int64_t M, int64_t N, int64_t K, int bits, int epilogue, 
     };
     // the bytes a candidate must reproduce
     auto snapshot = [&](std::vector<uint8_t>& out) -> int {
-        const size_t ny = swiglu ? 0 : (size_t)M * N * 4, nc = swiglu ? (size_t)M * (N / 2) * 2 : 0,
+        const size_t ny = swiglu ? 0 : (size_t)M * N * 4, nc = oc_bytes,
                      ns = swiglu ? (size_t)(N / 128) * lds * 4 : 0;
         out.resize(ny + nc + ns);
         if (ny) cudaMemcpyAsync(out.data(), y, ny, cudaMemcpyDeviceToHost, s);
@@ -202,7 +213,7 @@ int db_tune_gemm_shape(int64_t M, int64_t N, int64_t K, int bits, int epilogue, 
         int rc = 0;
         for (int r = 0; r < reps + 1 && !rc; ++r) {
             if (flush) cudaMemsetAsync(flush, r & 0xff, FLUSH_BYTES, s);
-            fill_codes_f16<<<256, 256, 0, s>>>(a, M * Kp, 1);  // same values as before
+            fill_a();  // same values as before
             if (epilogue == DB_EPI_RESIDUAL) cudaMemcpyAsync(y, y0, (size_t)M * N * 4, cudaMemcpyDeviceToDevice, s);
             cudaEventRecord(e0, s);
             rc = launch(c);
@@ -224,18 +235,29 @@ int db_tune_gemm_shape(int64_t M, int64_t N, int64_t K, int bits, int epilogue, 
                            std::string(what) + ": device wait ran out, error word " + std::to_string(-rc));
         return db_cuda_status(rc, what);
     };
-    std::vector<db_gemm_config> cands = {{128, 0, 0}};  // baseline first
-    if (!swiglu) {
-        cands.push_back({64, 0, 0});
-        cands.push_back({256, 0, 0});
+    std::vector<db_gemm_config> cands;  // baseline first
+    if (i8) {
+        cands.push_back(db_gemm_i8_default_config(M, N, epilogue));
+        for (int bn : {256, 128, 64})
+            for (int pair : {1, 0}) {
+                if ((pair && M <= 128) || (swiglu && bn == 64)) continue;
+                if (bn == cands[0].block_n && pair == cands[0].pair_ctas) continue;
+                cands.push_back({bn, 0, pair});
+            }
+    } else {
+        cands.push_back({128, 0, 0});
+        if (!swiglu) {
+            cands.push_back({64, 0, 0});
+            cands.push_back({256, 0, 0});
+        }
+        if (M > 128) cands.push_back({128, 0, 1});
     }
-    if (M > 128) cands.push_back({128, 0, 1});
     std::vector<uint8_t> want, got;
     int rc = run(cands[0]);
     if (!rc) rc = snapshot(want);
     if (rc) return fail(rc, "tuner baseline");
 
-    const std::string key = db_tuning_key(M, N, K, bits, epilogue);
+    const std::string key = db_tuning_key(M, N, K, bits, epilogue, i8);
     std::ostringstream rep;
     rep << "{\"key\":\"" << key << "\",\"shape\":[" << M << ',' << N << ',' << K << "],\"bits\":" << bits
         << ",\"epilogue\":" << epilogue;
@@ -256,7 +278,8 @@ int db_tune_gemm_shape(int64_t M, int64_t N, int64_t K, int bits, int epilogue, 
     float base_ms = 0.f;
     rc = time_best(cands[0], 8, &base_ms);
     if (rc) return db_cuda_status(rc, "tuner timing");
-    rep << ",\"cached\":false,\"candidates\":[{\"config\":[128,0,0],\"equal\":true,\"ms\":" << base_ms << "}";
+    rep << ",\"cached\":false,\"candidates\":[{\"config\":[" << cands[0].block_n << ',' << cands[0].max_ctas << ','
+        << cands[0].pair_ctas << "],\"equal\":true,\"ms\":" << base_ms << "}";
     float best_ms = base_ms;
     db_gemm_config best = cands[0];
     for (size_t i = 1; i < cands.size(); ++i) {
@@ -290,7 +313,7 @@ extern "C" int db_gemm_tune(int64_t M, int64_t N, int64_t K, int bits, int epilo
         (epilogue == DB_EPI_SWIGLU_QUANT && N % 128))
         return db_fail(DB_ERR_INVALID_ARGUMENT, "INVALID_ARGUMENT", "tune: bad shape or epilogue");
     std::string rep;
-    const int rc = db_tune_gemm_shape(M, N, K, bits, epilogue, cache_path, choice, &rep, nullptr);
+    const int rc = db_tune_gemm_shape(M, N, K, bits, epilogue, cache_path, choice, &rep, nullptr, true);
     if (report_json && cap) std::snprintf(report_json, cap, "%s", rep.c_str());
     return rc;
 }

@@ -99,7 +99,9 @@ int db_dequant_rows_g64(const uint8_t *codes, const float *scales, int64_t N, in
 
 /* Grouped GEMM on prepared activations.  Replaces Matrix::apply_prepared (int8.rs:229-288)
  * and the WGSL int8_gemm family (grouped_q4_tuned.wgsl): y[m, n] (+)= sum over groups.
- * a_codes in DB_CODES_TC layout (M >= 1), or DB_CODES_GEMV when M <= db_gemv_max_rows();
+ * a_codes in DB_CODES_NATURAL layout (int8, lda % 16 == 0; the kind::i8 tensor-core kernel) or
+ * DB_CODES_TC layout (f16 codes; the kind::f16 kernel), M >= 1, or DB_CODES_GEMV when
+ * M <= db_gemv_max_rows();
  * a_sums is required by the GEMV layout with Q4 weights.  fused: 1 = AVX2 numerics (fma),
  * 0 = portable numerics.  residual: 1 adds into y.  nonfinite (optional): when *nonfinite != 0
  * every output is NaN (int8.rs:170-173). */
@@ -111,9 +113,12 @@ int db_gemm_g64(const void *a_codes, int layout, int64_t lda, const float *sa, c
  * (checkpoint.rs:279-294, 428-563 select among kernel variants; a candidate is accepted only when
  * its output is bitwise equal to the baseline's).  Every configuration computes the same
  * per-group fold in the same order, so all are bitwise equal by construction.
- *   block_n    output columns per tile: 0 (default 128), 64, 128 or 256 (not for SwiGLU)
+ *   block_n    output columns per tile: 0 (default: 128 for DB_CODES_TC, 256 for DB_CODES_NATURAL),
+ *              64, 128 or 256 (the SwiGLU epilogue fixes it: 128 for DB_CODES_TC, 256 otherwise)
  *   max_ctas   persistent grid cap: 0 = one CTA per SM
- *   pair_ctas  1 = clusters of two CTAs issue M = 256 MMAs (128-wide tiles, M > 128); 0 = off
+ *   pair_ctas  1 = clusters of two CTAs issue M = 256 MMAs (M > 128; DB_CODES_TC: 128-wide tiles
+ *              only); 0 = off
+ * A NULL configuration on DB_CODES_NATURAL inputs picks the widest tile that still fills the SMs.
  * No counterpart in the reference's CPU path (its tuner picks WGSL variants). */
 typedef struct db_gemm_config {
     int block_n;
@@ -207,6 +212,13 @@ int db_decima_linear(const float *x, int64_t M, int64_t K, const uint8_t *w_code
 int db_mlp_g64(const void *a_codes, int64_t lda, const float *sa, int64_t ldsa, const uint8_t *w_gu_codes,
                const float *w_gu_scales, int64_t M, int64_t F, int64_t K, int bits, int fused, void *out_codes,
                int64_t ldoc, float *out_scales, int64_t ldos, const int *nonfinite, void *stream);
+/* db_mlp_g64 on int8 activation codes in DB_CODES_NATURAL layout (the kind::i8 tensor-core path,
+ * half the operand bytes of DB_CODES_TC): a_codes int8 [M, lda] (lda % 16 == 0), out_codes int8
+ * natural [M, ldoc] (ldoc % 16 == 0), out_scales as db_mlp_g64.  Same numerics. */
+int db_mlp_g64_natural(const void *a_codes, int64_t lda, const float *sa, int64_t ldsa, const uint8_t *w_gu_codes,
+                       const float *w_gu_scales, int64_t M, int64_t F, int64_t K, int bits, int fused,
+                       void *out_codes, int64_t ldoc, float *out_scales, int64_t ldos, const int *nonfinite,
+                       void *stream);
 /* gate/up [F, K] each (DB_LAYOUT) -> interleaved [2F, K] (DB_LAYOUT) for db_mlp_g64 */
 int db_interleave_gate_up(const uint8_t *gate_codes, const float *gate_scales, const uint8_t *up_codes,
                           const float *up_scales, int64_t F, int64_t K, int bits, uint8_t *out_codes,
@@ -330,6 +342,12 @@ int db_cache_stats(const db_cache *c, int64_t *hits, int64_t *reused_tokens, int
  * (1 = on, the default); a cancellation flag, per-kernel profiling or streaming keeps the
  * layer-by-layer path.  0 switches graphs off (results are bit-identical either way). */
 int db_model_use_graphs(db_model *m, int enable);
+
+/* Activation codes of the model's projections: DB_CODES_NATURAL (int8 codes, the kind::i8
+ * tensor-core GEMM; the default) or DB_CODES_TC (f16 codes, the kind::f16 GEMM).  Both compute
+ * the same per-group integer dots and fold them in the same order, so outputs are bit-identical;
+ * only speed differs.  Resets tuned tile choices (they belong to one kernel). */
+int db_model_set_code_layout(db_model *m, int layout);
 
 #define DB_PROF_KINDS 11
 int db_model_profile(db_model *m, int enable);

@@ -169,21 +169,53 @@ def _gpu_gemm(db, oracle, x, m, k, n, wbits, abits, fused, path):
     if path == "linear":
         y = db.linear(xt, codes, scales, n, wbits, abits, fused)
     else:
-        a, sa, s = db.quantize_activations(xt, bits=abits, layout=db.CODES_TC)
-        y = db.gemm(a, db.CODES_TC, sa, codes, scales, m, n, k, wbits, fused)
+        layout = db.CODES_NATURAL if path == "i8" else db.CODES_TC
+        a, sa, s = db.quantize_activations(xt, bits=abits, layout=layout)
+        y = db.gemm(a, layout, sa, codes, scales, m, n, k, wbits, fused)
     torch.cuda.synchronize()
     assert db.device_error_word() == 0
     mat = oracle.Matrix(bf.reshape(-1), k, n, wbits, abits)
     return y.cpu().numpy(), mat
 
 
+@pytest.mark.parametrize("path", ["tc", "i8"])
 @pytest.mark.parametrize("wb,ab", [(4, 8), (8, 8), (4, 4)])
 @pytest.mark.parametrize("m,k,n", SHAPES)
-def test_tensor_core_gemm_bit_exact(db, oracle, wb, ab, m, k, n):
+def test_tensor_core_gemm_bit_exact(db, oracle, wb, ab, m, k, n, path):
     x = ref_x(m, k, kind="ramp" if m * k < 100000 else "normal")
-    y, mat = _gpu_gemm(db, oracle, x, m, k, n, wb, ab, True, "tc")
+    y, mat = _gpu_gemm(db, oracle, x, m, k, n, wb, ab, True, path)
     ref = mat.apply(x, mode=2 if m * n * k > 10 ** 7 else 0)
     assert bits_equal(y, ref), f"max |d| = {np.max(np.abs(y - ref))}"
+
+
+I8_CONFIGS = [(256, 0, 1), (256, 0, 0), (128, 0, 1), (128, 0, 0), (64, 0, 1), (64, 0, 0), (256, 5, 1), (64, 3, 0),
+              (128, 7, 1)]
+
+
+@pytest.mark.parametrize("m,k,n", [(200, 1000, 300), (1024, 1024, 3072), (257, 130, 129), (384, 2048, 256),
+                                   (300, 64, 64), (129, 3072, 1024)])
+@pytest.mark.parametrize("wb", [4, 8])
+def test_i8_tile_configurations_are_bitwise_equal(db, oracle, m, k, n, wb):
+    """kind::i8 path: every tile width / pairing / grid cap gives the oracle's bits, for the store
+    and the residual (TMA reduce-add) epilogues and both accumulation orders."""
+    x = ref_x(m, k, kind="normal")
+    bf = oracle.f32_to_bf16(np.random.default_rng(k + n).normal(0, 0.02, (n, k)).astype(np.float32))
+    codes, scales = db.pack_weights(torch.from_numpy(bf.view(np.int16)).cuda(), wb)
+    a, sa, _ = db.quantize_activations(torch.from_numpy(x.reshape(m, k)).cuda(), bits=8, layout=db.CODES_NATURAL)
+    mat = oracle.Matrix(bf.reshape(-1), k, n, wb, 8)
+    ref, ref_p = mat.apply(x, mode=0), mat.apply(x, mode=1)
+    base = torch.randn(m, n, device="cuda")
+    expect_res = (base.cpu().numpy() + ref).astype(np.float32)
+    for bn, cap, pair in I8_CONFIGS:
+        cfg = db.GemmConfig(bn, cap, pair)
+        y = db.gemm(a, db.CODES_NATURAL, sa, codes, scales, m, n, k, wb, True, config=cfg)
+        r = db.gemm(a, db.CODES_NATURAL, sa, codes, scales, m, n, k, wb, True, residual=base.clone(), config=cfg)
+        p = db.gemm(a, db.CODES_NATURAL, sa, codes, scales, m, n, k, wb, False, config=cfg)
+        torch.cuda.synchronize()
+        assert db.device_error_word() == 0
+        assert bits_equal(y.cpu().numpy(), ref), f"store epilogue differs for config {(bn, cap, pair)}"
+        assert bits_equal(r.cpu().numpy(), expect_res), f"residual epilogue differs for config {(bn, cap, pair)}"
+        assert bits_equal(p.cpu().numpy(), ref_p), f"portable numerics differ for config {(bn, cap, pair)}"
 
 
 TILE_CONFIGS = [(0, 0, 0), (64, 0, 0), (128, 0, 1), (128, 16, 0), (128, 7, 1), (64, 3, 0), (256, 0, 0), (256, 5, 0)]
@@ -266,7 +298,8 @@ def test_project_packed_matches_packed_project(db, oracle):
 # ------------------------------------------------------------------ fused MLP
 @pytest.mark.parametrize("bits", [4, 8])
 @pytest.mark.parametrize("m,f,k", [(67, 192, 256), (256, 512, 1024), (1024, 3072, 1024)])
-def test_fused_mlp_matches_unfused_oracle(db, oracle, bits, m, f, k):
+@pytest.mark.parametrize("layout", ["tc", "i8"])
+def test_fused_mlp_matches_unfused_oracle(db, oracle, bits, m, f, k, layout):
     # webgpu/grouped_q4.rs:313-354 shape and generators for the first case
     def weight(seed):
         i = np.arange(f * k)
@@ -277,7 +310,8 @@ def test_fused_mlp_matches_unfused_oracle(db, oracle, bits, m, f, k):
     gc, gs = db.pack_weights(dg, bits)
     uc, us = db.pack_weights(du, bits)
     guc, gus = db.interleave_gate_up(gc, gs, uc, us, f, k, bits)
-    a, sa, _ = db.quantize_activations(torch.from_numpy(x.reshape(m, k)).cuda(), bits=8, layout=db.CODES_TC)
+    lay = db.CODES_NATURAL if layout == "i8" else db.CODES_TC
+    a, sa, _ = db.quantize_activations(torch.from_numpy(x.reshape(m, k)).cuda(), bits=8, layout=lay)
     codes, scales = db.mlp(a, sa, guc, gus, m, f, k, bits)
     torch.cuda.synchronize()
     assert db.device_error_word() == 0
@@ -286,10 +320,13 @@ def test_fused_mlp_matches_unfused_oracle(db, oracle, bits, m, f, k):
     h = oracle.silu_mul(g, u)
     values, ref_scales, _ = oracle.Matrix(np.zeros(f, np.uint16), f, 1).prepare(h)
     c = codes.cpu().numpy().astype(np.int64)
-    perm = np.array([0, 4, 1, 5, 2, 6, 3, 7])
-    natural = np.zeros_like(c)
-    for b in range(0, f, 8):
-        natural[:, b + perm] = c[:, b:b + 8]
+    if layout == "i8":
+        natural = c
+    else:
+        perm = np.array([0, 4, 1, 5, 2, 6, 3, 7])
+        natural = np.zeros_like(c)
+        for b in range(0, f, 8):
+            natural[:, b + perm] = c[:, b:b + 8]
     diff = np.abs(natural.reshape(-1) - values.astype(np.int64))
     # exp() of CUDA and libm differ by <= 2 ulp; a code may flip only at a rounding boundary
     assert diff.max() <= 1 and np.count_nonzero(diff) <= max(2, diff.size // 10000)

@@ -180,3 +180,19 @@ def test_graph_forward_is_bit_identical(db):
         for a, b in zip(want, got):
             assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
     m.close()
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+def test_code_layouts_are_bit_identical(db, oracle, bits):
+    """int8 codes through the kind::i8 GEMM and f16 codes through the kind::f16 GEMM compute the
+    same integer dots and fold them in the same order: the encoder's outputs agree bit for bit."""
+    cfg = dict(SMALL, weight_bits=bits)
+    model = db.Model.from_weights(db.EncoderConfig(**cfg, max_sequence_tokens=512), random_weights(oracle, cfg, 3))
+    ids = np.random.default_rng(9).integers(0, cfg["vocab"], 300).astype(np.int32)
+    a = np.asarray(model.predict(ids).response)
+    model.set_code_layout(db.CODES_TC)
+    b = np.asarray(model.predict(ids).response)
+    model.set_code_layout(db.CODES_NATURAL)
+    c = np.asarray(model.predict(ids).response)
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32)) and np.array_equal(a.view(np.uint32), c.view(np.uint32))
+    model.close()
