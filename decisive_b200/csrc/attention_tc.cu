@@ -165,7 +165,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
                         const __grid_constant__ CUtensorMap tmV, int T, int Hq, int Hk, float scale_log2,
                         float* __restrict__ out, int64_t ldo, void* __restrict__ codes, int64_t ldc,
                         float* __restrict__ scales, int64_t lds, int* __restrict__ nonfinite,
-                        int* __restrict__ dev_error, int codes_i8) {
+                        int* __restrict__ dev_error, int codes_i8, const int* __restrict__ cu_seqlens) {
     pdl_wait();
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -173,8 +173,20 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_MISC);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + OFF_MISC + 4);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int h = blockIdx.y, kh = h / (Hq / Hk), item = blockIdx.z;
+    const int h = blockIdx.y, kh = h / (Hq / Hk);
     const int q0 = blockIdx.x * AT_Q;
+    // Equal items: item blockIdx.z of T rows (4-D maps [B][T][H][D]).  Ragged items (cu_seqlens):
+    // sequence blockIdx.z holds rows cu[z]..cu[z+1]-1 of the packed rows (maps [1][R][H][D]); its
+    // keys are its own rows only.  A CTA whose query tile lies past its sequence has no work.
+    int item = blockIdx.z, row0 = 0;
+    int64_t obase = (int64_t)blockIdx.z * T;
+    if (cu_seqlens) {
+        row0 = cu_seqlens[blockIdx.z];
+        T = cu_seqlens[blockIdx.z + 1] - row0;
+        obase = row0;
+        item = 0;
+        if (q0 >= T) return;
+    }
     const int nt = (T + AT_KT - 1) / AT_KT;  // key tiles
     const int np = (nt + 1) / 2;             // pairs of tiles (even, odd)
     const uint32_t sQ = smem_u32(smem + OFF_Q), sP = smem_u32(smem + OFF_P), sKV = smem_u32(smem + OFF_KV);
@@ -225,8 +237,8 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
                 if (lane == 0) {
                     const uint32_t dst = sKV + (uint32_t)(st * AT_TILE);
                     mbar_arrive_expect_tx(&bars[BAR_KV_FULL + st], AT_TILE);
-                    tma_load_4d(dst, map, &bars[BAR_KV_FULL + st], 0, kh, tile * AT_KT, item);
-                    tma_load_4d(dst + AT_HALF, map, &bars[BAR_KV_FULL + st], 64, kh, tile * AT_KT, item);
+                    tma_load_4d(dst, map, &bars[BAR_KV_FULL + st], 0, kh, row0 + tile * AT_KT, item);
+                    tma_load_4d(dst + AT_HALF, map, &bars[BAR_KV_FULL + st], 64, kh, row0 + tile * AT_KT, item);
                 }
                 __syncwarp();
                 ++issued;
@@ -238,8 +250,8 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
             };
             if (lane == 0) {
                 mbar_arrive_expect_tx(&bars[BAR_Q], AT_TILE);
-                tma_load_4d(sQ, &tmQ, &bars[BAR_Q], 0, h, q0, item);
-                tma_load_4d(sQ + AT_HALF, &tmQ, &bars[BAR_Q], 64, h, q0, item);
+                tma_load_4d(sQ, &tmQ, &bars[BAR_Q], 0, h, row0 + q0, item);
+                tma_load_4d(sQ + AT_HALF, &tmQ, &bars[BAR_Q], 64, h, row0 + q0, item);
             }
             __syncwarp();
             for (int p = 0; p <= np && ok; ++p) {
@@ -491,7 +503,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
             }
             tc_fence_before();
             const int t = q0 + row;
-            const int64_t orow = (int64_t)item * T + t;
+            const int64_t orow = obase + t;
             if (t < T) {
                 if constexpr (QUANT) {
                     // group_scale (int8.rs:305-313) and pack_bits (int8.rs:347-360) over this row's
@@ -613,6 +625,43 @@ int db_launch_attention_tc(const __half* q16, const __half* k16, const __half* v
     const dim3 grid((unsigned)((T + AT_Q - 1) / AT_Q), (unsigned)Hq, (unsigned)B);
     const cudaError_t e = db_launch_pdl(kernel, grid, dim3(AT_THREADS), AT_SMEM, stream, tmQ, tmK, tmV, T, Hq, Hk,
                                         scale * 1.4426950408889634f, out, ldo, codes, ldc, scales, lds, nonfinite, err,
-                                        codes_i8);
+                                        codes_i8, static_cast<const int*>(nullptr));
+    return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
+}
+
+// Ragged items packed one after another: R rows in total, sequence i holds rows
+// cu_seqlens[i]..cu_seqlens[i+1]-1 (device array of nseq + 1 ints, cu_seqlens[nseq] = R) and attends
+// to its own rows only; max_len bounds the longest sequence (sizes the grid).  Outputs as
+// db_launch_attention_tc, row-indexed by the packed row.
+int db_launch_attention_varlen(const __half* q16, const __half* k16, const __half* v16, const int* cu_seqlens,
+                               int nseq, int max_len, int R, int Hq, int Hk, float scale, float* out, int64_t ldo,
+                               void* codes, int64_t ldc, float* scales, int64_t lds, int* nonfinite,
+                               cudaStream_t stream, int codes_i8) {
+    if (nseq <= 0 || R <= 0 || max_len <= 0) return 0;
+    const bool quant = codes != nullptr;
+    if (!cu_seqlens || Hk <= 0 || Hq % Hk || Hq > 65535 || nseq > 65535 ||
+        (quant && (!scales || !nonfinite || (ldc & (codes_i8 ? 15 : 7)))) || (!quant && (!out || (ldo & 3))))
+        return (int)cudaErrorInvalidValue;
+    if ((reinterpret_cast<uintptr_t>(q16) | reinterpret_cast<uintptr_t>(k16) | reinterpret_cast<uintptr_t>(v16)) & 15)
+        return (int)cudaErrorMisalignedAddress;
+    if (!quant && (reinterpret_cast<uintptr_t>(out) & 15)) return (int)cudaErrorMisalignedAddress;
+    if (quant && (reinterpret_cast<uintptr_t>(codes) & 15)) return (int)cudaErrorMisalignedAddress;
+    DbEncodeTiledFn enc = db_encode_tiled();
+    if (!enc) return (int)cudaErrorNotSupported;
+    CUtensorMap tmQ, tmK, tmV;
+    if (make_head_map(enc, &tmQ, q16, Hq, R, 1) || make_head_map(enc, &tmK, k16, Hk, R, 1) ||
+        make_head_map(enc, &tmV, v16, Hk, R, 1))
+        return (int)cudaErrorInvalidValue;
+    int* err = db_device_error_ptr();
+    if (!err) return (int)cudaErrorMemoryAllocation;
+    auto kernel = quant ? attention_tc_kernel<true> : attention_tc_kernel<false>;
+    {
+        const cudaError_t e = db_set_max_smem(reinterpret_cast<const void*>(kernel), AT_SMEM);
+        if (e != cudaSuccess) return (int)e;
+    }
+    const dim3 grid((unsigned)((max_len + AT_Q - 1) / AT_Q), (unsigned)Hq, (unsigned)nseq);
+    const cudaError_t e = db_launch_pdl(kernel, grid, dim3(AT_THREADS), AT_SMEM, stream, tmQ, tmK, tmV, max_len, Hq,
+                                        Hk, scale * 1.4426950408889634f, out, ldo, codes, ldc, scales, lds, nonfinite,
+                                        err, codes_i8, cu_seqlens);
     return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }

@@ -109,6 +109,27 @@ __device__ __forceinline__ bool mbar_spin(uint64_t* bar, uint32_t parity, volati
     }
 }
 
+// The same poll with a short sleep after every failed test: for waiters that share their SM
+// sub-partition with a latency-critical warp (the MMA issuer), so that polling does not take its
+// issue slots.
+__device__ __forceinline__ bool mbar_spin_polite(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err,
+                                                 int code) {
+    if (mbar_test_wait(bar, parity)) return true;
+    const uint64_t start = globaltimer();
+    for (uint32_t i = 1;; ++i) {
+        __nanosleep(32);
+        if (mbar_test_wait(bar, parity)) return true;
+        if ((i & 15u) == 0) {
+            if (*abort_flag) return false;
+            if (globaltimer() - start > DB_WAIT_LIMIT_NS) {
+                *abort_flag = 1;
+                atomicOr(err, code);
+                return false;
+            }
+        }
+    }
+}
+
 // Bounded wait that ignores the abort flag: used while winding down after an abort, to let this
 // thread's own asynchronous copies or MMAs land before the CTA releases its memory.
 __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {

@@ -25,7 +25,7 @@
 //   warp 1      TMEM owner + MMA issuer (lane 0; in pair mode the even CTA issues M = 256 MMAs
 //               for both CTAs of the cluster, each CTA holding 128 rows of A and BN/2 rows of W)
 //   warps 2-3   Q4 weight converters (idle for Q8)
-//   warps 4-11  epilogue (224 registers each through setmaxnreg): warp w reads TMEM lanes
+//   warps 4-11  epilogue (216 registers each through setmaxnreg): warp w reads TMEM lanes
 //               32 (w % 4).. and half of the tile's columns; per job: bias-subtract, scale fold
 //               in f32 (packed f32x2 operations, each an IEEE operation), bias write-back; per
 //               tile: TMA store / reduce-add of the outputs, or SwiGLU + re-quantisation
@@ -50,10 +50,10 @@ constexpr int EPI_WARPS = 8;
 constexpr int NUM_THREADS = 32 * (EPI_WARP0 + EPI_WARPS);  // 384
 // Register split (setmaxnreg): __launch_bounds__(384, 1) gives every thread 168 registers at
 // launch (65536 / 384, rounded down to a multiple of 8); warpgroup 0 (producer, MMA, converters)
-// drops to 56 and warpgroups 1-2 (epilogue) rise to 224: 128 * 56 + 256 * 224 = 168 * 384.
+// drops to 64 and warpgroups 1-2 (epilogue) rise to 216: 128 * 64 + 256 * 216 <= 168 * 384.
 constexpr int REGS_LAUNCH = 65536 / NUM_THREADS / 8 * 8;
-constexpr int REGS_CONTROL = 56;
-constexpr int REGS_EPI = 224;
+constexpr int REGS_CONTROL = 64;
+constexpr int REGS_EPI = 216;
 static_assert(128 * REGS_CONTROL + 256 * REGS_EPI <= REGS_LAUNCH * NUM_THREADS, "register split");
 constexpr uint32_t DOT_BIAS = 0x4B400000u;  // bits of 12582912.0f
 constexpr float DOT_BIAS_F = 12582912.0f;
@@ -353,45 +353,40 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             __syncwarp();
         } else if (warp == 1) {
             // ------------------------------------------------------------ MMA issuer
+            // Lane 0 alone runs the issue loop (no warp-wide handshakes per job); descriptors are
+            // built once and advanced by the stage / k offsets (start address field, in 16-byte
+            // units: shared memory is below 256 KB, so the 14-bit field never carries).
             constexpr uint32_t IDESC = idesc_s8_s32(MT, BN);
             constexpr int KPJ = 2 / SUB;  // K = 32 MMAs per job
             constexpr int JB = 64 / SUB;  // k bytes per job
-            int st = 0, jn = 0;
-            uint32_t ps = 0;
-            const uint32_t st_base = smem_u32(smem + S::OFF_STAGE), cb_base = smem_u32(smem + S::OFF_CB);
-            if (!leader) goto mma_peer;
-            for (int tile = tile0; tile < tiles; tile += tstride) {
-                for (int s = 0; s < NS; ++s) {
-                    {
-                        int ok = 1;
-                        if (lane == 0) {
-                            ok = mbar_spin(&full[st], ps, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_MMA);
-                            if (ok && BITS == 4) ok = mbar_spin(&cbf[st], ps, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_MMA);
-                        }
-                        ok = __shfl_sync(0xffffffffu, ok, 0);
-                        __syncwarp();
-                        if (!ok) goto mma_end;
-                    }
-                    const uint32_t a_addr = st_base + st * S::STAGE_BYTES;
-                    const uint32_t b_addr = BITS == 8 ? a_addr + S::A_BYTES : cb_base + st * S::CB_BYTES;
-                    const int j0 = s * 2 * SUB, j1 = min(j0 + 2 * SUB, GS);
-                    for (int j = j0; j < j1; ++j, ++jn) {
-                        const int b = jn % S::NBUF;
-                        const uint32_t par = (uint32_t)(jn / S::NBUF) & 1u;
-                        int ok = 1;
-                        if (lane == 0) ok = mbar_spin(&acc_empty[b], par, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_MMA);
-                        ok = __shfl_sync(0xffffffffu, ok, 0);
-                        __syncwarp();
-                        if (!ok) goto mma_end;
-                        tc_fence_after();
-                        if (lane == 0) {
+            if (leader && lane == 0) {
+                const uint32_t st_base = smem_u32(smem + S::OFF_STAGE), cb_base = smem_u32(smem + S::OFF_CB);
+                const uint64_t a_desc0 = sw128_desc(st_base);
+                const uint64_t b_desc0 = sw128_desc(BITS == 8 ? st_base + S::A_BYTES : cb_base);
+                constexpr int B_STRIDE = BITS == 8 ? S::STAGE_BYTES : S::CB_BYTES;
+                int st = 0, jn = 0;
+                uint32_t ps = 0;
+                for (int tile = tile0; tile < tiles; tile += tstride) {
+                    for (int s = 0; s < NS; ++s) {
+                        if (!mbar_spin(&full[st], ps, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_MMA)) goto mma_end;
+                        if (BITS == 4 && !mbar_spin(&cbf[st], ps, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_MMA))
+                            goto mma_end;
+                        const uint64_t ad = a_desc0 + (uint64_t)((st * S::STAGE_BYTES) >> 4);
+                        const uint64_t bd = b_desc0 + (uint64_t)((st * B_STRIDE) >> 4);
+                        const int j0 = s * 2 * SUB, j1 = min(j0 + 2 * SUB, GS);
+                        for (int j = j0; j < j1; ++j, ++jn) {
+                            const int b = jn % S::NBUF;
+                            if (!mbar_spin(&acc_empty[b], (uint32_t)(jn / S::NBUF) & 1u, abort_flag, dev_error,
+                                           DB_DEV_ERR_TIMEOUT_MMA))
+                                goto mma_end;
+                            tc_fence_after();
                             const uint32_t d = tmem_base + (uint32_t)(b * BN);
 #pragma unroll
                             for (int kk = 0; kk < KPJ; ++kk) {
-                                const uint32_t off = (uint32_t)((j - j0) * JB + kk * 32);
+                                const uint64_t off = (uint64_t)(((j - j0) * JB + kk * 32) >> 4);
                                 // accumulate onto the bias the epilogue left in the buffer
-                                if (PAIR) umma_i8_pair(d, sw128_desc(a_addr + off), sw128_desc(b_addr + off), IDESC, 1u);
-                                else umma_i8(d, sw128_desc(a_addr + off), sw128_desc(b_addr + off), IDESC, 1u);
+                                if (PAIR) umma_i8_pair(d, ad + off, bd + off, IDESC, 1u);
+                                else umma_i8(d, ad + off, bd + off, IDESC, 1u);
                             }
                             if (PAIR) {
                                 umma_commit_pair(smem_u32(&done[b]));
@@ -400,23 +395,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                                 umma_commit(&done[b]);
                             }
                         }
-                        __syncwarp();
-                    }
-                    if (lane == 0) {
                         if (PAIR) {
                             umma_commit_pair(smem_u32(&empty[st]));
                             umma_commit_pair(at_peer(&empty[st]));
                         } else {
                             umma_commit(&empty[st]);
                         }
+                        if (++st == S::STAGES) { st = 0; ps ^= 1u; }
                     }
-                    __syncwarp();
-                    if (++st == S::STAGES) { st = 0; ps ^= 1u; }
                 }
-            }
-        mma_end:
-            // every MMA this warp issued has completed before the CTA releases tensor memory
-            if (lane == 0) {
+            mma_end:
+                // every MMA this thread issued has completed before the CTA releases tensor memory
                 if (PAIR) {
                     umma_commit_pair(smem_u32(mma_done));
                     umma_commit_pair(at_peer(mma_done));
@@ -424,13 +413,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     umma_commit(mma_done);
                 }
                 mbar_wait_drain(mma_done, 0, DRAIN_NS);
+            } else if (!leader && lane == 0) {
+                // the peer CTA's tensor memory is written by the leader's MMAs: wait for their last
+                // commit (a wait as long as the whole launch, so bounded by the launch-wide limit)
+                mbar_wait_drain(mma_done, 0, DB_WAIT_LIMIT_NS);
             }
-            __syncwarp();
-            goto ctl_done;
-        mma_peer:
-            // the peer CTA's tensor memory is written by the leader's MMAs: wait for their last
-            // commit (a wait as long as the whole launch, so bounded by the launch-wide limit)
-            if (lane == 0) mbar_wait_drain(mma_done, 0, DB_WAIT_LIMIT_NS);
             __syncwarp();
         } else if (BITS == 4 && warp < CONV_WARP0 + CONV_WARPS) {
             // ------------------------------------------------------------ Q4 converters
@@ -498,12 +485,22 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         auto wait_job = [&](int jn) -> bool {
             int ok = 1;
             if (lane == 0) {
-                ok = mbar_spin(&done[jn % S::NBUF], (uint32_t)(jn / S::NBUF) & 1u, abort_flag, dev_error,
-                               DB_DEV_ERR_TIMEOUT_EPI);
+                ok = mbar_spin_polite(&done[jn % S::NBUF], (uint32_t)(jn / S::NBUF) & 1u, abort_flag, dev_error,
+                                      DB_DEV_ERR_TIMEOUT_EPI);
                 if (ok)
-                    ok = mbar_spin(&sc_full[jn % S::SCJ], (uint32_t)(jn / S::SCJ) & 1u, abort_flag, dev_error,
-                                   DB_DEV_ERR_TIMEOUT_EPI);
+                    ok = mbar_spin_polite(&sc_full[jn % S::SCJ], (uint32_t)(jn / S::SCJ) & 1u, abort_flag,
+                                          dev_error, DB_DEV_ERR_TIMEOUT_EPI);
             }
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            __syncwarp();
+            return ok != 0;
+        };
+        // both of job jn's barriers have completed already (one test each, no waiting)
+        auto job_ready = [&](int jn) -> bool {
+            int ok = 1;
+            if (lane == 0)
+                ok = mbar_test_wait(&done[jn % S::NBUF], (uint32_t)(jn / S::NBUF) & 1u) &&
+                     mbar_test_wait(&sc_full[jn % S::SCJ], (uint32_t)(jn / S::SCJ) & 1u);
             ok = __shfl_sync(0xffffffffu, ok, 0);
             __syncwarp();
             return ok != 0;
@@ -664,7 +661,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 fold16<FUSED>(acc, *reinterpret_cast<const uint32_t(*)[16]>(&v[0]), wsc, s_a);
                 fold16<FUSED>(acc + 8, *reinterpret_cast<const uint32_t(*)[16]>(&v[16]), wsc + 64, s_a);
             };
-            // job jn's values are in flight in x (and y for 64 columns); the next job's go to z, x
+            // job jn's values are in flight in x (and y for 64 columns); the next job's go to z, x.
+            // When the next job is already complete its loads are issued before this job's fold;
+            // otherwise the fold comes first and the wait after it.
             auto step = [&](int jn, uint64_t (&acc)[COLS / 2], B32& x, B32& y, B32& z) -> bool {
                 tmem_wait_ld(x);
                 if constexpr (COLS == 64) tie32(y);
@@ -672,8 +671,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
                 for (int c = 0; c < COLS / 32; ++c) tmem_st_32x32b_x32_fill(tb + (uint32_t)(c * 32), DOT_BIAS);
                 const bool next = jn + 1 < total;
-                if (next) {
-                    if (!wait_job(jn + 1)) return false;
+                const bool early = next && job_ready(jn + 1);
+                if (early) {
                     tc_fence_after();
                     ld32(jn + 1, 0, COLS == 64 ? z : y);
                 }
@@ -682,10 +681,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 const uint32_t wsc = slot + BM * 4 + col0 * 4;
                 fold32(&acc[0], x, wsc, s_a);
                 if constexpr (COLS == 64) {
-                    if (next) ld32(jn + 1, 1, x);
+                    if (early) ld32(jn + 1, 1, x);
                     fold32(&acc[16], y, wsc + 128, s_a);
                 }
                 release_job(jn);
+                if (next && !early) {
+                    if (!wait_job(jn + 1)) return false;
+                    tc_fence_after();
+                    ld32(jn + 1, 0, COLS == 64 ? z : y);
+                    if constexpr (COLS == 64) ld32(jn + 1, 1, x);
+                }
                 return true;
             };
             if (total > 0) {

@@ -121,7 +121,7 @@ __global__ void qk_norm_rope_kernel(const float* __restrict__ qkv, int64_t ld, i
                                     const float* __restrict__ qw, const float* __restrict__ kw, float eps,
                                     const float* __restrict__ cos_t, const float* __restrict__ sin_t,
                                     __half* __restrict__ q16, __half* __restrict__ k16, __half* __restrict__ v16,
-                                    int pos0, int seq_len) {
+                                    int pos0, int seq_len, const int* __restrict__ positions) {
     pdl_wait();
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     const int heads = Hq + 2 * Hk;
@@ -133,8 +133,9 @@ __global__ void qk_norm_rope_kernel(const float* __restrict__ qkv, int64_t ld, i
     for (int u = 0; u < QK_HEADS_PER_WARP; ++u)
         if (h0 + u < heads) v[u] = *reinterpret_cast<const float4*>(qkv + (size_t)t * ld + (h0 + u) * 128 + 4 * lane);
     const int i0 = (4 * lane) & 63;
-    // rows are seq_len-token items placed one after another, each starting at position pos0
-    const size_t pos = (size_t)(pos0 + t % seq_len);
+    // rows are seq_len-token items placed one after another, each starting at position pos0, or
+    // carry their own positions (ragged sequences packed together)
+    const size_t pos = positions ? (size_t)positions[t] : (size_t)(pos0 + t % seq_len);
     const float4 cs = *reinterpret_cast<const float4*>(cos_t + pos * 64 + i0);
     const float4 sn = *reinterpret_cast<const float4*>(sin_t + pos * 64 + i0);
     const float cc[4] = {cs.x, cs.y, cs.z, cs.w}, ssn[4] = {sn.x, sn.y, sn.z, sn.w};
@@ -188,6 +189,20 @@ __global__ void mean_pool_kernel(const float* __restrict__ x, int64_t ldx, int T
     out[d] = __fdiv_rn(s, (float)T);
 }
 
+// Mean over each ragged sequence's rows (rows cu[i]..cu[i+1]-1 -> out[i]), in row order as
+// mean_pool_kernel sums a single sequence.
+__global__ void mean_pool_varlen_kernel(const float* __restrict__ x, int64_t ldx, const int* __restrict__ cu, int D,
+                                        float* __restrict__ out) {
+    pdl_wait();
+    const int d = blockIdx.x * blockDim.x + threadIdx.x, i = blockIdx.y;
+    if (d >= D) return;
+    const int t0 = cu[i], t1 = cu[i + 1];
+    float s = 0.f;
+#pragma unroll 16
+    for (int t = t0; t < t1; ++t) s = __fadd_rn(s, x[(size_t)t * ldx + d]);
+    out[(size_t)i * D + d] = __fdiv_rn(s, (float)(t1 - t0));
+}
+
 __global__ void fill_nan_if_kernel(float* __restrict__ y, int64_t n, const int* __restrict__ flag) {
     int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n && *flag) y[i] = __int_as_float(0x7fc00000);
@@ -208,14 +223,22 @@ int db_launch_rms_quantize(const float* x, int64_t ldx, const float* w, int T, i
     return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }
 
+int db_launch_mean_pool_varlen(const float* x, int64_t ldx, const int* cu_seqlens, int nseq, int D, float* out,
+                               cudaStream_t stream) {
+    if (nseq <= 0) return 0;
+    const cudaError_t e = db_launch_pdl(mean_pool_varlen_kernel, dim3((D + 127) / 128, nseq), dim3(128), 0, stream, x,
+                                        ldx, cu_seqlens, D, out);
+    return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
+}
+
 int db_launch_qk_norm_rope(const float* qkv, int64_t ld, int T, int Hq, int Hk, const float* qw, const float* kw,
                            float eps, const float* cos_t, const float* sin_t, __half* q16, __half* k16, __half* v16,
-                           cudaStream_t stream, int pos0, int seq_len) {
+                           cudaStream_t stream, int pos0, int seq_len, const int* positions) {
     if (T <= 0) return 0;
     const int64_t warps = (int64_t)T * ((Hq + 2 * Hk + QK_HEADS_PER_WARP - 1) / QK_HEADS_PER_WARP);
     const cudaError_t e = db_launch_pdl(qk_norm_rope_kernel, dim3((unsigned)((warps + 3) / 4)), dim3(128), 0, stream,
                                         qkv, ld, T, Hq, Hk, qw, kw, eps, cos_t, sin_t, q16, k16, v16, pos0,
-                                        seq_len > 0 ? seq_len : T);
+                                        seq_len > 0 ? seq_len : T, positions);
     return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }
 

@@ -8,11 +8,15 @@ int db_launch_rms_quantize(const float* x, int64_t ldx, const float* w, int T, i
                            float* normed, int64_t ldn, void* codes, int layout, int64_t ldc, float* scales,
                            int32_t* sums, int64_t lds, int* nonfinite, cudaStream_t stream, int normalize = 1);
 // Rows are items of seq_len tokens (0 = T) one after another; row t gets RoPE position
-// pos0 + t % seq_len (a continuation after a cached prefix of pos0 tokens).
+// pos0 + t % seq_len (a continuation after a cached prefix of pos0 tokens), or positions[t] when
+// positions (device, T ints) is given (ragged sequences packed together).
 int db_launch_qk_norm_rope(const float* qkv, int64_t ld, int T, int Hq, int Hk, const float* qw, const float* kw,
                            float eps, const float* cos_t, const float* sin_t, __half* q16, __half* k16, __half* v16,
-                           cudaStream_t stream, int pos0 = 0, int seq_len = 0);
+                           cudaStream_t stream, int pos0 = 0, int seq_len = 0, const int* positions = nullptr);
 int db_launch_mean_pool(const float* x, int64_t ldx, int T, int D, float* out, cudaStream_t stream);
+// Mean of each ragged sequence's rows: out [nseq, D], sequence i = rows cu_seqlens[i]..cu_seqlens[i+1]-1.
+int db_launch_mean_pool_varlen(const float* x, int64_t ldx, const int* cu_seqlens, int nseq, int D, float* out,
+                               cudaStream_t stream);
 int db_launch_fill_nan_if(float* y, int64_t n, const int* flag, cudaStream_t stream);
 
 // Non-causal GQA attention over head_dim 128: q16 [T, Hq, 128], k16/v16 [T, Hk, 128] (f16),
@@ -32,6 +36,13 @@ int db_launch_attention_quant(const __half* q16, const __half* k16, const __half
 int db_launch_attention_tc(const __half* q16, const __half* k16, const __half* v16, int B, int T, int Hq, int Hk,
                            float scale, float* out, int64_t ldo, void* codes, int64_t ldc, float* scales,
                            int64_t lds, int* nonfinite, cudaStream_t stream, int codes_i8 = 0);
+// Ragged sequences packed one after another (R rows; sequence i = rows cu_seqlens[i] ..
+// cu_seqlens[i+1]-1, a device array; max_len >= every length): non-causal attention of each
+// sequence over its own rows, outputs as db_launch_attention_tc.
+int db_launch_attention_varlen(const __half* q16, const __half* k16, const __half* v16, const int* cu_seqlens,
+                               int nseq, int max_len, int R, int Hq, int Hk, float scale, float* out, int64_t ldo,
+                               void* codes, int64_t ldc, float* scales, int64_t lds, int* nonfinite,
+                               cudaStream_t stream, int codes_i8 = 0);
 // Decoder form of the quantising attention: B items of T rows each (q16/k16/v16 and the outputs
 // hold the items one after another); every item's keys are the P cached prefix keys kp/vp
 // [P, Hk, 128] (shared by the items; P = 0: none) followed by its own T keys, which are causal

@@ -84,6 +84,7 @@ struct db_model {
     float *cos_t = nullptr, *sin_t = nullptr, *sa = nullptr, *sh = nullptr;
     __half *acodes = nullptr, *hcodes = nullptr, *q16 = nullptr, *k16 = nullptr, *v16 = nullptr;
     int32_t* ids = nullptr;
+    int32_t *cu = nullptr, *pos = nullptr;  // ragged batch: sequence boundaries, row positions
     int* flag = nullptr;
     int* dev_err = nullptr;
     // one CUDA graph per token count for the plain forward (captured on the second call for a T)
@@ -227,7 +228,8 @@ int ensure_workspace(db_model* m, int T) {
     auto& v = m->ws_allocations;
     if (m->alloc(&m->x, (size_t)T * D, v) || m->alloc(&m->qkv, (size_t)T * m->Nqkv(), v) ||
         m->alloc(&m->ctx, (size_t)T * m->Nq(), v) || m->alloc(&m->normed, (size_t)T * D, v) ||
-        m->alloc(&m->pooled, D, v) ||
+        m->alloc(&m->pooled, (size_t)T * D, v) || m->alloc(&m->cu, (size_t)T + 1, v) ||
+        m->alloc(&m->pos, (size_t)T, v) ||
         m->alloc(&m->sa, (size_t)Gmax * db_scale_stride(T), v) || m->alloc(&m->sh, (size_t)(F / 64) * db_scale_stride(T), v) ||
         m->alloc(&m->acodes, (size_t)T * Kmax, v) || m->alloc(&m->hcodes, (size_t)T * F, v) ||
         m->alloc(&m->q16, (size_t)T * m->Nq(), v) || m->alloc(&m->k16, (size_t)T * m->Nk(), v) ||
@@ -323,6 +325,12 @@ struct Pass {
     __half* const* sk = nullptr;
     __half* const* sv = nullptr;
     bool pool = true;
+    // ragged encoder batch: nseq sequences packed into T rows, sequence i = rows cu[i]..cu[i+1]-1
+    // (device arrays; pos = each row's position in its sequence), pooled into m->pooled [nseq, D]
+    const int* cu = nullptr;
+    const int* pos = nullptr;
+    int nseq = 0;
+    int max_len = 0;
 };
 
 // Enqueues the forward of ids (device, T tokens) -> m->pooled.  Host-side cancellation is polled
@@ -430,11 +438,16 @@ int enqueue_forward(db_model* m, int T, const volatile uint8_t* cancel, const Pa
             rc = timed(3, [&] {
                 // a prefix pass stores this layer's keys and values straight into the cache
                 return db_launch_qk_norm_rope(m->qkv, Nqkv, R, c.q_heads, c.kv_heads, w.q_norm, w.k_norm, c.eps,
-                                              m->cos_t, m->sin_t, m->q16, own_k(l), own_v(l), st, P, T);
+                                              m->cos_t, m->sin_t, m->q16, own_k(l), own_v(l), st, P, T,
+                                              pass ? pass->pos : nullptr);
             });
         // attention writes the context already quantised for the output projection
         if (!rc)
             rc = timed(4, [&] {
+                if (!c.causal && pass && pass->cu)
+                    return db_launch_attention_varlen(m->q16, m->k16, m->v16, pass->cu, pass->nseq, pass->max_len, R,
+                                                      c.q_heads, c.kv_heads, attn_scale, nullptr, 0, m->acodes,
+                                                      ld_codes, m->sa, lds, m->flag, st, m->i8);
                 if (!c.causal && !pass)
                     return db_launch_attention_quant(m->q16, m->k16, m->v16, T, c.q_heads, c.kv_heads, attn_scale,
                                                      m->acodes, ld_codes, m->sa, lds, m->flag, st, m->i8);
@@ -482,7 +495,10 @@ int enqueue_forward(db_model* m, int T, const volatile uint8_t* cancel, const Pa
             return db_launch_rms_quantize(m->x, D, m->final_norm, R, D, c.eps, 0, m->normed, D, nullptr, DB_CODES_TC, 0,
                                           nullptr, nullptr, 0, m->flag, st);
         });
-    if (!rc && (!pass || pass->pool)) rc = timed(10, [&] { return db_launch_mean_pool(m->normed, D, T, D, m->pooled, st); });
+    if (!rc && pass && pass->cu)
+        rc = timed(10, [&] { return db_launch_mean_pool_varlen(m->normed, D, pass->cu, pass->nseq, D, m->pooled, st); });
+    else if (!rc && (!pass || pass->pool))
+        rc = timed(10, [&] { return db_launch_mean_pool(m->normed, D, T, D, m->pooled, st); });
     return rc ? db_cuda_status(rc, "forward") : 0;
 }
 
@@ -581,6 +597,128 @@ int predict_one(db_model* m, const int32_t* ids, size_t n, const db_parameters* 
     if (cancel && *cancel) {
         fill_error(err, "CANCELLED", "Inference was cancelled");
         return -1;
+    }
+    return 0;
+}
+
+// Request checks of predict_one (the reference's codes); returns 0 or fills err.
+int validate_request(const db_model* m, const int32_t* ids, size_t n, int limit, db_error* err) {
+    if (!ids || n == 0) {
+        fill_error(err, "INVALID_REQUEST", "a nonempty token sequence is required");
+        return -1;
+    }
+    if (n > (size_t)limit) {
+        fill_error(err, "INPUT_TOO_LONG", "single question exceeds token limit: " + std::to_string(n) + " > " +
+                                              std::to_string(limit) + "; inputs are never truncated");
+        return -1;
+    }
+    for (size_t i = 0; i < n; ++i)
+        if (ids[i] < 0 || ids[i] >= m->cfg.vocab) {
+            fill_error(err, "INVALID_REQUEST", "token id " + std::to_string(ids[i]) + " outside the vocabulary");
+            return -1;
+        }
+    return 0;
+}
+
+// Model::predict_batch for an encoder (mod.rs:250-273: ordered outcomes, one per request) as packed
+// ragged passes: the valid requests' tokens are concatenated (up to kPackRows rows per pass), every
+// row-wise kernel and GEMM runs once over all rows, attention runs per sequence over its own keys
+// (cu_seqlens), and each sequence is mean-pooled.  Every kernel computes a row (or a sequence's
+// attention) exactly as the one-request forward does, so outcomes are bit-identical to predict.
+// A pass whose hidden state turns non-finite is re-run request by request, so that the failure is
+// reported for the request it belongs to.
+constexpr size_t kPackRows = 65536;
+int predict_packed(db_model* m, const int32_t* const* ids, const size_t* lens, size_t count,
+                   const db_parameters* params, const volatile uint8_t* cancel, float* outs, int32_t* status,
+                   db_error* errs) {
+    const int D = m->cfg.hidden;
+    const int limit = params ? params->max_sequence_tokens : m->cfg.max_sequence_tokens;
+    std::vector<size_t> valid;
+    for (size_t i = 0; i < count; ++i) {
+        db_error* e = errs ? &errs[i] : nullptr;
+        status[i] = -1;
+        if (cancel && *cancel) {
+            fill_error(e, "CANCELLED", "Inference was cancelled");
+        } else if (limit <= 0) {
+            fill_error(e, "INVALID_PARAMETERS", "maxSequenceTokens must be positive");
+        } else if (validate_request(m, ids[i], lens[i], limit, e) == 0) {
+            valid.push_back(i);
+        }
+    }
+    cudaSetDevice(m->device);
+    size_t next = 0;
+    while (next < valid.size()) {
+        // one pass: as many whole requests as fit kPackRows rows (and the grid's 65535 sequences)
+        size_t end = next, rows = 0;
+        while (end < valid.size() && end - next < 65535 && (end == next || rows + lens[valid[end]] <= kPackRows))
+            rows += lens[valid[end++]];
+        const int nseq = (int)(end - next), R = (int)rows;
+        auto fail_all = [&](const char* code, const std::string& msg) {
+            for (size_t k = next; k < end; ++k) fill_error(errs ? &errs[valid[k]] : nullptr, code, msg);
+        };
+        if (cancel && *cancel) {
+            fail_all("CANCELLED", "Inference was cancelled");
+            next = end;
+            continue;
+        }
+        if (ensure_workspace(m, R)) {
+            fail_all("RESOURCE_LIMIT", db_last_error_message());
+            next = end;
+            continue;
+        }
+        std::vector<int32_t> h_ids(R), h_pos(R), h_cu(nseq + 1);
+        int max_len = 0, r0 = 0;
+        for (int k = 0; k < nseq; ++k) {
+            const size_t i = valid[next + k];
+            const int n = (int)lens[i];
+            h_cu[k] = r0;
+            std::memcpy(h_ids.data() + r0, ids[i], (size_t)n * sizeof(int32_t));
+            for (int t = 0; t < n; ++t) h_pos[r0 + t] = t;
+            r0 += n;
+            max_len = std::max(max_len, n);
+        }
+        h_cu[nseq] = R;
+        cudaMemcpyAsync(m->ids, h_ids.data(), (size_t)R * 4, cudaMemcpyHostToDevice, m->stream);
+        cudaMemcpyAsync(m->pos, h_pos.data(), (size_t)R * 4, cudaMemcpyHostToDevice, m->stream);
+        cudaMemcpyAsync(m->cu, h_cu.data(), (size_t)(nseq + 1) * 4, cudaMemcpyHostToDevice, m->stream);
+        Pass pass;
+        pass.cu = m->cu;
+        pass.pos = m->pos;
+        pass.nseq = nseq;
+        pass.max_len = max_len;
+        const int rc = enqueue_forward(m, R, cancel, &pass);
+        std::vector<float> pooled((size_t)nseq * D);
+        int flag = 0;
+        if (rc == 0) {
+            cudaMemcpyAsync(&flag, m->flag, sizeof(int), cudaMemcpyDeviceToHost, m->stream);
+            cudaMemcpyAsync(pooled.data(), m->pooled, pooled.size() * 4, cudaMemcpyDeviceToHost, m->stream);
+        }
+        const cudaError_t e = cudaStreamSynchronize(m->stream);
+        if (rc == 1 || (cancel && *cancel)) {
+            fail_all("CANCELLED", "Inference was cancelled");
+        } else if (rc || e != cudaSuccess) {
+            fail_all("INFERENCE_FAILED", rc ? db_last_error_message() : cudaGetErrorString(e));
+        } else {
+            int word = 0;
+            cudaMemcpy(&word, m->dev_err, sizeof(int), cudaMemcpyDeviceToHost);
+            if (word) {
+                cudaMemset(m->dev_err, 0, sizeof(int));
+                fail_all("INFERENCE_FAILED", "device wait expired (error word " + std::to_string(word) + ")");
+            } else if (flag) {
+                for (size_t k = next; k < end; ++k) {
+                    const size_t i = valid[k];
+                    status[i] = predict_one(m, ids[i], lens[i], params, cancel, outs + i * (size_t)D,
+                                            errs ? &errs[i] : nullptr);
+                }
+            } else {
+                for (int k = 0; k < nseq; ++k) {
+                    const size_t i = valid[next + k];
+                    std::memcpy(outs + i * (size_t)D, pooled.data() + (size_t)k * D, (size_t)D * sizeof(float));
+                    status[i] = 0;
+                }
+            }
+        }
+        next = end;
     }
     return 0;
 }
@@ -848,10 +986,13 @@ int db_predict_batch(db_model* m, const int32_t* const* ids, const size_t* lens,
         fill_error(err, "CACHE_OWNER", "Cache belongs to another model instance");
         return -1;
     }
-    for (size_t i = 0; i < count; ++i)
-        status[i] = predict_one(m, ids[i], lens[i], params, cancel, outs + i * (size_t)m->cfg.hidden,
-                                errs ? &errs[i] : nullptr);
-    return 0;
+    if (m->cfg.causal || count <= 1 || m->streaming) {
+        for (size_t i = 0; i < count; ++i)
+            status[i] = predict_one(m, ids[i], lens[i], params, cancel, outs + i * (size_t)m->cfg.hidden,
+                                    errs ? &errs[i] : nullptr);
+        return 0;
+    }
+    return predict_packed(m, ids, lens, count, params, cancel, outs, status, errs);
 }
 
 int db_model_set_code_layout(db_model* m, int layout) {
