@@ -209,15 +209,16 @@ int db_gemm_g64_config(const void* a_codes, int layout, int64_t lda, const float
 
 }  // extern "C"
 
-// Tile configuration of the int8 tensor-core GEMM when none is given: the widest tile (and CTA
-// pairs) that still occupies the SMs -- each candidate is scored by the fraction of the last
-// wave of CTAs that has work, with a small preference for wide tiles (fewer re-reads of A per
-// output) and for pairs (half of the weight tile per CTA).
+// Tile configuration of the int8 tensor-core GEMM when none is given: the widest tile that still
+// occupies the SMs -- each candidate is scored by the fraction of the last wave of CTAs that has
+// work, with a small preference for wide tiles (fewer re-reads of A per output).  CTA pairs
+// measured slower than single CTAs on the C1/C2 shapes (the pair's MMA waits for both CTAs), so
+// they are scored down; the tuner still tries them.
 db_gemm_config db_gemm_i8_default_config(int64_t M, int64_t N, int epilogue) {
     const int sms = db_num_sms();
     const int cands[6][2] = {{256, 1}, {128, 1}, {64, 1}, {256, 0}, {128, 0}, {64, 0}};
     double best = -1.0;
-    db_gemm_config out{256, 0, M > 128 ? 1 : 0};
+    db_gemm_config out{256, 0, 0};
     for (const auto& c : cands) {
         const int bn = c[0], pair = c[1];
         if (pair && M <= 128) continue;
@@ -226,7 +227,7 @@ db_gemm_config db_gemm_i8_default_config(int64_t M, int64_t N, int epilogue) {
         const int64_t ctas = ((M + mt - 1) / mt) * ((N + bn - 1) / bn) * (pair ? 2 : 1);
         const int64_t waves = (ctas + sms - 1) / sms;
         const double fill = (double)ctas / (double)(waves * sms);
-        const double score = fill * (bn == 256 ? 1.0 : bn == 128 ? 0.93 : 0.85) * (pair ? 1.0 : 0.97);
+        const double score = fill * (bn == 256 ? 1.0 : bn == 128 ? 0.97 : 0.88) * (pair ? 0.85 : 1.0);
         if (score > best + 1e-9) {
             best = score;
             out = db_gemm_config{bn, 0, pair};

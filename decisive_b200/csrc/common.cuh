@@ -485,6 +485,16 @@ __device__ __forceinline__ void tmem_st_32x32b_x32_fill(uint32_t taddr, uint32_t
         "r"(v)
         : "memory");
 }
+// 32 lanes x 64 consecutive 32-bit columns, every one set to v.
+__device__ __forceinline__ void tmem_st_32x32b_x64_fill(uint32_t taddr, uint32_t v) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x64.b32 [%0], "
+        "{%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,"
+        "%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(
+            taddr),
+        "r"(v)
+        : "memory");
+}
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 __device__ __forceinline__ float warp_max(float v) {

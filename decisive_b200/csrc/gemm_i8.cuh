@@ -8,11 +8,9 @@
 //
 // The dots come from tcgen05.mma kind::i8 (signed 8-bit A and B, s32 accumulators in tensor
 // memory, K = 32 per instruction): each scale block is one job with its own TMEM accumulator
-// buffer.  A buffer does not start at zero but at DOT_BIAS = 0x4B400000, the bits of the float
-// 1.5 * 2^23: the MMAs add the integer dot to it, and because |dot| <= 64 * 127 * 127 < 2^22 the
-// result read back as a float is exactly 12582912 + dot, so one exact f32 subtraction recovers
-// float(dot) without an integer-to-float conversion.  The epilogue warps write the bias back with
-// tcgen05.st after reading a buffer, which hands it to the MMA issuer for the job NBUF later.
+// buffer.  The epilogue converts a dot exactly without an integer-to-float conversion: adding
+// DOT_BIAS = 0x4B400000 (the bits of 1.5 * 2^23) to the s32 dot gives the bits of the float
+// 12582912 + dot (|dot| <= 64 * 127 * 127 < 2^22), and subtracting 12582912 is exact.
 //
 // Layout.  A: int8 codes [M, lda] in natural k order.  W: the device layout (Q4 [N, Kp/2] bytes,
 // low nibble = even k, nibble = code + 8; Q8 [N, Kp] int8), scales f32 [GS, ldsw].  A pipeline
@@ -26,9 +24,9 @@
 //               for both CTAs of the cluster, each CTA holding 128 rows of A and BN/2 rows of W)
 //   warps 2-3   Q4 weight converters (idle for Q8)
 //   warps 4-11  epilogue (216 registers each through setmaxnreg): warp w reads TMEM lanes
-//               32 (w % 4).. and half of the tile's columns; per job: bias-subtract, scale fold
-//               in f32 (packed f32x2 operations, each an IEEE operation), bias write-back; per
-//               tile: TMA store / reduce-add of the outputs, or SwiGLU + re-quantisation
+//               32 (w % 4).. and half of the tile's columns; per job: dot conversion and scale
+//               fold in f32 (packed f32x2 operations, each an IEEE operation); per tile: TMA
+//               store / reduce-add of the outputs, or SwiGLU + re-quantisation
 // Every mbarrier wait is bounded (DB_WAIT_LIMIT_NS); on expiry the CTA records an error in the
 // device error word, stops issuing work, lets its own copies and MMAs land and frees its tensor
 // memory.  No TMA multicast.
@@ -52,9 +50,19 @@ constexpr int NUM_THREADS = 32 * (EPI_WARP0 + EPI_WARPS);  // 384
 // launch (65536 / 384, rounded down to a multiple of 8); warpgroup 0 (producer, MMA, converters)
 // drops to 64 and warpgroups 1-2 (epilogue) rise to 216: 128 * 64 + 256 * 216 <= 168 * 384.
 constexpr int REGS_LAUNCH = 65536 / NUM_THREADS / 8 * 8;
-constexpr int REGS_CONTROL = 64;
-constexpr int REGS_EPI = 216;
+#ifndef GI8_REGS_CONTROL
+#define GI8_REGS_CONTROL 64
+#endif
+constexpr int REGS_CONTROL = GI8_REGS_CONTROL;
+constexpr int REGS_EPI = (REGS_LAUNCH * NUM_THREADS - 128 * REGS_CONTROL) / 256 / 8 * 8;
 static_assert(128 * REGS_CONTROL + 256 * REGS_EPI <= REGS_LAUNCH * NUM_THREADS, "register split");
+// How the MMA issuer waits for a free accumulator buffer and the epilogue for a finished job.
+#ifndef GI8_MMA_WAIT
+#define GI8_MMA_WAIT mbar_spin
+#endif
+#ifndef GI8_EPI_WAIT
+#define GI8_EPI_WAIT mbar_spin_polite
+#endif
 constexpr uint32_t DOT_BIAS = 0x4B400000u;  // bits of 12582912.0f
 constexpr float DOT_BIAS_F = 12582912.0f;
 constexpr uint64_t DRAIN_NS = 100000000ull;
@@ -106,10 +114,13 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
     __syncwarp();
     return ok != 0;
 }
+// Warp-wide wait for the producer and the converters: one lane polls with mbarrier.test_wait and a
+// short sleep between polls.  (A thread suspended in mbarrier.try_wait was measured to resume up to
+// microseconds after the phase completed, which paced the whole pipeline at one stage per ~1 us.)
 __device__ __forceinline__ bool warp_wait_backoff(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                                   int* err, int code) {
     int ok = 1;
-    if ((threadIdx.x & 31) == 0) ok = mbar_wait_backoff(bar, parity, abort_flag, err, code);
+    if ((threadIdx.x & 31) == 0) ok = mbar_spin_polite(bar, parity, abort_flag, err, code);
     ok = __shfl_sync(0xffffffffu, ok, 0);
     __syncwarp();
     return ok != 0;
@@ -173,9 +184,25 @@ __device__ __forceinline__ void fold16(uint64_t* acc, const uint32_t (&v)[16], u
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         const uint4 w = lds128(w_addr + i * 16);
-        // (12582912 + dot) - 12582912 is exact: float(dot)
-        const uint64_t d0 = f2_add(f2_pack(v[4 * i], v[4 * i + 1]), nb2);
-        const uint64_t d1 = f2_add(f2_pack(v[4 * i + 2], v[4 * i + 3]), nb2);
+        // the s32 dot plus the bias bits, read as a float, is 12582912 + dot exactly; subtracting
+        // 12582912 is exact too: float(dot) without an integer-to-float conversion
+        const uint64_t d0 = f2_add(f2_pack(v[4 * i] + DOT_BIAS, v[4 * i + 1] + DOT_BIAS), nb2);
+        const uint64_t d1 = f2_add(f2_pack(v[4 * i + 2] + DOT_BIAS, v[4 * i + 3] + DOT_BIAS), nb2);
+#ifdef GI8_SCALAR_FOLD
+        if (FUSED) {
+            const float dd[4] = {f2_lo(d0), f2_hi(d0), f2_lo(d1), f2_hi(d1)};
+            const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+            float o[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const uint64_t a = acc[2 * i + e / 2];
+                const float prev = (e & 1) ? f2_hi(a) : f2_lo(a);
+                o[e] = __fmaf_rn(dd[e], __fmul_rn(__uint_as_float(ww[e]), s_a), prev);
+            }
+            acc[2 * i] = f2_pack(__float_as_uint(o[0]), __float_as_uint(o[1]));
+            acc[2 * i + 1] = f2_pack(__float_as_uint(o[2]), __float_as_uint(o[3]));
+        } else
+#endif
         if (FUSED) {
             acc[2 * i] = f2_fma(d0, f2_mul(f2_pack(w.x, w.y), sa2), acc[2 * i]);
             acc[2 * i + 1] = f2_fma(d1, f2_mul(f2_pack(w.z, w.w), sa2), acc[2 * i + 1]);
@@ -376,7 +403,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         const int j0 = s * 2 * SUB, j1 = min(j0 + 2 * SUB, GS);
                         for (int j = j0; j < j1; ++j, ++jn) {
                             const int b = jn % S::NBUF;
-                            if (!mbar_spin(&acc_empty[b], (uint32_t)(jn / S::NBUF) & 1u, abort_flag, dev_error,
+                            // the buffer is free and the job's scale vectors have landed (the epilogue
+                            // then needs to wait for the job's completion only)
+                            if (!GI8_MMA_WAIT(&acc_empty[b], (uint32_t)(jn / S::NBUF) & 1u, abort_flag, dev_error,
+                                              DB_DEV_ERR_TIMEOUT_MMA) ||
+                                !mbar_spin(&sc_full[jn % S::SCJ], (uint32_t)(jn / S::SCJ) & 1u, abort_flag, dev_error,
                                            DB_DEV_ERR_TIMEOUT_MMA))
                                 goto mma_end;
                             tc_fence_after();
@@ -385,8 +416,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                             for (int kk = 0; kk < KPJ; ++kk) {
                                 const uint64_t off = (uint64_t)(((j - j0) * JB + kk * 32) >> 4);
                                 // accumulate onto the bias the epilogue left in the buffer
-                                if (PAIR) umma_i8_pair(d, ad + off, bd + off, IDESC, 1u);
-                                else umma_i8(d, ad + off, bd + off, IDESC, 1u);
+                                const uint32_t acc_in = kk > 0 ? 1u : 0u;  // a job starts from zero
+                                if (PAIR) umma_i8_pair(d, ad + off, bd + off, IDESC, acc_in);
+                                else umma_i8(d, ad + off, bd + off, IDESC, acc_in);
                             }
                             if (PAIR) {
                                 umma_commit_pair(smem_u32(&done[b]));
@@ -468,53 +500,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const uint32_t tlane = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)col0;
         const uint32_t sc_base = smem_u32(smem + S::OFF_SC);
         const bool any_nonfinite = nonfinite != nullptr && *nonfinite != 0;
-        // every buffer starts at the bias
-#pragma unroll
-        for (int b = 0; b < S::NBUF; ++b)
-#pragma unroll
-            for (int c = 0; c < COLS / 32; ++c) tmem_st_32x32b_x32_fill(tlane + (uint32_t)(b * BN + c * 32), DOT_BIAS);
-        tmem_wait_st();
-        tc_fence_before();
+        // every accumulator buffer starts free
         __syncwarp();
         if (lane == 0)
             for (int b = 0; b < S::NBUF; ++b) {
                 if (PAIR) mbar_arrive_cluster(at_leader(&acc_empty[b]));
                 else mbar_arrive(&acc_empty[b]);
             }
-        // job jn's accumulators (done) and scale vectors (sc_full) are ready; false: aborted
+        // job jn's accumulators are ready (its MMAs completed; the MMA issuer waited for the job's
+        // scale vectors before issuing them, so those have landed too); false: aborted
         auto wait_job = [&](int jn) -> bool {
             int ok = 1;
-            if (lane == 0) {
-                ok = mbar_spin_polite(&done[jn % S::NBUF], (uint32_t)(jn / S::NBUF) & 1u, abort_flag, dev_error,
-                                      DB_DEV_ERR_TIMEOUT_EPI);
-                if (ok)
-                    ok = mbar_spin_polite(&sc_full[jn % S::SCJ], (uint32_t)(jn / S::SCJ) & 1u, abort_flag,
-                                          dev_error, DB_DEV_ERR_TIMEOUT_EPI);
-            }
-            ok = __shfl_sync(0xffffffffu, ok, 0);
-            __syncwarp();
-            return ok != 0;
-        };
-        // both of job jn's barriers have completed already (one test each, no waiting)
-        auto job_ready = [&](int jn) -> bool {
-            int ok = 1;
             if (lane == 0)
-                ok = mbar_test_wait(&done[jn % S::NBUF], (uint32_t)(jn / S::NBUF) & 1u) &&
-                     mbar_test_wait(&sc_full[jn % S::SCJ], (uint32_t)(jn / S::SCJ) & 1u);
+                ok = GI8_EPI_WAIT(&done[jn % S::NBUF], (uint32_t)(jn / S::NBUF) & 1u, abort_flag, dev_error,
+                                  DB_DEV_ERR_TIMEOUT_EPI);
             ok = __shfl_sync(0xffffffffu, ok, 0);
             __syncwarp();
             return ok != 0;
-        };
-        // the buffer of job jn holds the bias again and every warp is done with its scale slot
-        auto release_job = [&](int jn) {
-            tmem_wait_st();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) {
-                if (PAIR) mbar_arrive_cluster(at_leader(&acc_empty[jn % S::NBUF]));
-                else mbar_arrive(&acc_empty[jn % S::NBUF]);
-                mbar_arrive(&sc_empty[jn % S::SCJ]);
-            }
         };
         int ybuf = 0;
         // Output of a finished tile: the fused SwiGLU + re-quantisation, a TMA store / reduce-add
@@ -643,126 +645,94 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 return true;
             }
         };
-        const int my_tiles = tile0 < tiles ? (tiles - 1 - tile0) / tstride + 1 : 0;
-        const int total = my_tiles * GS;  // jobs of this CTA
-        if constexpr (COLS <= 64) {
-            // Software pipeline across jobs: while job jn is folded, the accumulators of job jn + 1
-            // are already on their way from tensor memory (the MMA issuer runs up to NBUF jobs
-            // ahead), and job jn's bias write-back completes under the fold.  Values move in
-            // 32-column register buffers: two for 64-wide tiles (the second half of the next job
-            // is loaded into the buffer whose values were just folded, so three buffers rotate),
-            // one for 32-wide (two rotate).
-            using B32 = uint32_t[32];
-            B32 rb0, rb1, rb2;
-            auto ld32 = [&](int jn, int h, B32& v) {
-                tmem_ld_32x32b_x32(tlane + (uint32_t)((jn % S::NBUF) * BN + h * 32), v);
-            };
-            auto fold32 = [&](uint64_t* acc, const B32& v, uint32_t wsc, float s_a) {
-                fold16<FUSED>(acc, *reinterpret_cast<const uint32_t(*)[16]>(&v[0]), wsc, s_a);
-                fold16<FUSED>(acc + 8, *reinterpret_cast<const uint32_t(*)[16]>(&v[16]), wsc + 64, s_a);
-            };
-            // job jn's values are in flight in x (and y for 64 columns); the next job's go to z, x.
-            // When the next job is already complete its loads are issued before this job's fold;
-            // otherwise the fold comes first and the wait after it.
-            auto step = [&](int jn, uint64_t (&acc)[COLS / 2], B32& x, B32& y, B32& z) -> bool {
-                tmem_wait_ld(x);
-                if constexpr (COLS == 64) tie32(y);
-                const uint32_t tb = tlane + (uint32_t)((jn % S::NBUF) * BN);
+        // Jobs are handled in steps of JPS = 128 / COLS (4 at 64-wide tiles, 2 at 128-wide, 1 at
+        // 256-wide): one wait for the step's last job (commits complete in issue order, so the
+        // earlier ones are done too), all of the step's accumulators loaded under one wait (128
+        // registers; 256-wide tiles in two halves of 64 columns), the buffers handed back to the MMA
+        // issuer as soon as their values are in registers, then the folds in job order and the
+        // scale slots returned.  Steps never cross a tile.
+        constexpr int JPS = COLS >= 128 ? 1 : 128 / COLS;  // jobs per step
+        constexpr int NH = COLS > 64 ? COLS / 64 : 1;       // loads per job (256-wide tiles: 2)
+        constexpr int HC = COLS / NH;                       // columns per load (32 or 64)
+        auto release_buf = [&](int jn) {
+            if (PAIR) mbar_arrive_cluster(at_leader(&acc_empty[jn % S::NBUF]));
+            else mbar_arrive(&acc_empty[jn % S::NBUF]);
+        };
+        for (int tile = tile0, jn = 0, jt = 0; tile < tiles; tile += tstride, ++jt) {
+            const int m0 = (tile % m_tiles) * MT + row_off, n0 = (tile / m_tiles) * BN;
+            uint64_t acc[COLS / 2];
 #pragma unroll
-                for (int c = 0; c < COLS / 32; ++c) tmem_st_32x32b_x32_fill(tb + (uint32_t)(c * 32), DOT_BIAS);
-                const bool next = jn + 1 < total;
-                const bool early = next && job_ready(jn + 1);
-                if (early) {
-                    tc_fence_after();
-                    ld32(jn + 1, 0, COLS == 64 ? z : y);
-                }
-                const uint32_t slot = sc_base + (jn % S::SCJ) * S::SC_SLOT;
-                const float s_a = lds_f32(slot + r * 4);
-                const uint32_t wsc = slot + BM * 4 + col0 * 4;
-                fold32(&acc[0], x, wsc, s_a);
-                if constexpr (COLS == 64) {
-                    if (early) ld32(jn + 1, 1, x);
-                    fold32(&acc[16], y, wsc + 128, s_a);
-                }
-                release_job(jn);
-                if (next && !early) {
-                    if (!wait_job(jn + 1)) return false;
-                    tc_fence_after();
-                    ld32(jn + 1, 0, COLS == 64 ? z : y);
-                    if constexpr (COLS == 64) ld32(jn + 1, 1, x);
-                }
-                return true;
-            };
-            if (total > 0) {
-                if (!wait_job(0)) goto done;
+            for (int j = 0; j < COLS / 2; ++j) acc[j] = 0ull;
+            for (int j = 0; j < GS;) {
+                // a whole step, or the tile's last jobs one at a time
+                const int nj = (JPS > 1 && GS - j >= JPS) ? JPS : 1;
+                if (!wait_job(jn + nj - 1)) goto done;
                 tc_fence_after();
-                ld32(0, 0, rb0);
-                if (COLS == 64) ld32(0, 1, rb1);
-            }
-            int jn = 0, jt = 0;
-            for (int tile = tile0; tile < tiles; tile += tstride, ++jt) {
-                const int m0 = (tile % m_tiles) * MT + row_off, n0 = (tile / m_tiles) * BN;
-                uint64_t acc[COLS / 2];
+                if (JPS > 1 && nj == JPS) {
+                    uint32_t v[JPS][COLS];
 #pragma unroll
-                for (int j = 0; j < COLS / 2; ++j) acc[j] = 0ull;
-                for (int j = 0; j < GS; ++j, ++jn) {
-                    bool ok;
-                    if constexpr (COLS == 64) {
-                        // (x, y, z) rotates (0,1,2) -> (2,0,1) -> (1,2,0)
-                        const int ph = jn % 3;
-                        ok = ph == 0 ? step(jn, acc, rb0, rb1, rb2) : ph == 1 ? step(jn, acc, rb2, rb0, rb1)
-                                                                              : step(jn, acc, rb1, rb2, rb0);
-                    } else {
-                        ok = (jn & 1) ? step(jn, acc, rb1, rb0, rb2) : step(jn, acc, rb0, rb1, rb2);
+                    for (int q = 0; q < JPS; ++q) {
+                        const uint32_t tb = tlane + (uint32_t)(((jn + q) % S::NBUF) * BN);
+#pragma unroll
+                        for (int c = 0; c < COLS / 32; ++c)
+                            tmem_ld_32x32b_x32(tb + (uint32_t)(c * 32), *reinterpret_cast<uint32_t(*)[32]>(&v[q][32 * c]));
                     }
-                    if (!ok) goto done;
-                }
-                if (!finish_tile(acc, m0, n0, jt)) goto done;
-            }
-        } else {
-            // 256-wide tiles: 128 accumulators per thread leave room for 16-column chunks only; the
-            // next chunk's load is in flight while the current one is folded
-            constexpr int NCH = COLS / 16;
-            int jn = 0, jt = 0;
-            for (int tile = tile0; tile < tiles; tile += tstride, ++jt) {
-                const int m0 = (tile % m_tiles) * MT + row_off, n0 = (tile / m_tiles) * BN;
-                uint64_t acc[COLS / 2];
+                    tmem_wait_ld();
 #pragma unroll
-                for (int j = 0; j < COLS / 2; ++j) acc[j] = 0ull;
-                for (int j = 0; j < GS; ++j, ++jn) {
-                    if (!wait_job(jn)) goto done;
-                    tc_fence_after();
+                    for (int q = 0; q < JPS; ++q)
+#pragma unroll
+                        for (int c = 0; c < COLS / 32; ++c) tie32(*reinterpret_cast<uint32_t(*)[32]>(&v[q][32 * c]));
+                    // every column of the step's jobs is in registers: their buffers are free
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0)
+                        for (int q = 0; q < JPS; ++q) release_buf(jn + q);
+#pragma unroll
+                    for (int q = 0; q < JPS; ++q) {
+                        const uint32_t slot = sc_base + ((jn + q) % S::SCJ) * S::SC_SLOT;
+                        const float s_a = lds_f32(slot + r * 4);
+                        const uint32_t wsc = slot + BM * 4 + col0 * 4;
+#pragma unroll
+                        for (int c = 0; c < COLS / 16; ++c)
+                            fold16<FUSED>(&acc[c * 8], *reinterpret_cast<const uint32_t(*)[16]>(&v[q][16 * c]),
+                                          wsc + 64 * c, s_a);
+                    }
+                } else {
+                    const uint32_t tb = tlane + (uint32_t)((jn % S::NBUF) * BN);
                     const uint32_t slot = sc_base + (jn % S::SCJ) * S::SC_SLOT;
                     const float s_a = lds_f32(slot + r * 4);
                     const uint32_t wsc = slot + BM * 4 + col0 * 4;
-                    const uint32_t tb = tlane + (uint32_t)((jn % S::NBUF) * BN);
-                    uint32_t va[16], vb[16];
-                    tmem_ld_32x32b_x16(tb, va);
 #pragma unroll
-                    for (int c = 0; c < NCH; c += 2) {
-                        tmem_wait_ld(va);
-                        if (c + 1 < NCH) tmem_ld_32x32b_x16(tb + (uint32_t)((c + 1) * 16), vb);
-                        fold16<FUSED>(&acc[c * 8], va, wsc + c * 64, s_a);
-                        if (c + 1 < NCH) {
-                            tmem_wait_ld(vb);
-                            if (c + 2 < NCH) tmem_ld_32x32b_x16(tb + (uint32_t)((c + 2) * 16), va);
-                            fold16<FUSED>(&acc[(c + 1) * 8], vb, wsc + (c + 1) * 64, s_a);
+                    for (int h = 0; h < NH; ++h) {
+                        uint32_t v[HC];
+#pragma unroll
+                        for (int c = 0; c < HC / 32; ++c)
+                            tmem_ld_32x32b_x32(tb + (uint32_t)(h * HC + 32 * c), *reinterpret_cast<uint32_t(*)[32]>(&v[32 * c]));
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int c = 0; c < HC / 32; ++c) tie32(*reinterpret_cast<uint32_t(*)[32]>(&v[32 * c]));
+                        if (h == NH - 1) {
+                            tc_fence_before();
+                            __syncwarp();
+                            if (lane == 0) release_buf(jn);
                         }
-                    }
 #pragma unroll
-                    for (int c = 0; c < COLS / 32; ++c) tmem_st_32x32b_x32_fill(tb + (uint32_t)(c * 32), DOT_BIAS);
-                    release_job(jn);
+                        for (int c = 0; c < HC / 16; ++c)
+                            fold16<FUSED>(&acc[(h * HC) / 2 + c * 8], *reinterpret_cast<const uint32_t(*)[16]>(&v[16 * c]),
+                                          wsc + (h * HC + 16 * c) * 4, s_a);
+                    }
                 }
-                if (!finish_tile(acc, m0, n0, jt)) goto done;
+                __syncwarp();  // every lane has read the step's scale slots
+                if (lane == 0)
+                    for (int q = 0; q < nj; ++q) mbar_arrive(&sc_empty[(jn + q) % S::SCJ]);
+                jn += nj;
+                j += nj;
             }
+            if (!finish_tile(acc, m0, n0, jt)) goto done;
         }
     }
 done:
-    if (warp >= EPI_WARP0) {
-        // loads and stores of tensor memory this warp issued have completed
-        tmem_wait_ld();
-        tmem_wait_st();
-    }
+    if (warp >= EPI_WARP0) tmem_wait_ld();  // tensor-memory loads this warp issued have completed
     bulk_wait_all();  // output stores issued by this thread have completed
     // Teardown through mbarriers (a hardware CTA barrier reached from the different role branches
     // was measured to release some warps before the others arrived): warp 1 frees tensor memory
