@@ -224,6 +224,189 @@ def config_json():
                   f"(L2 {L2_BYTES >> 20} MiB)"}
 
 
+# ------------------------------------------------------------------ named shapes (driver-run evidence)
+def _device_time_us(fn, reps, flush=None, sleep=200_000):
+    """Median device time of fn() over reps launches (CUDA events on the current stream), each
+    launch queued behind a short GPU sleep (no host latency timed) and, when given, an L2 flush."""
+    import torch
+    times = []
+    for _ in range(reps):
+        if flush is not None:
+            flush.zero_()
+        torch.cuda._sleep(sleep)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b) * 1e3)
+    return float(np.median(times))
+
+
+def shape_c1(db, reps=20):
+    """one W4A8 g64 GEMM, M=1024 K=1024 N=3072 (activations f16 N(0,1) seed 0,
+    weights f32 N(0,0.02) seed 1 -> bf16 -> Q4), int8 tensor-core path, L2 flushed per launch."""
+    import torch
+    from oracle import oracle
+    m, k, n = 1024, 1024, 3072
+    w = oracle.f32_to_bf16(np.random.default_rng(1).normal(0, 0.02, (n, k)).astype(np.float32))
+    x = torch.from_numpy(np.random.default_rng(0).normal(0, 1, (m, k)).astype(np.float16)).cuda()
+    codes, scales = db.pack_weights(torch.from_numpy(w.view(np.int16)).cuda(), 4)
+    a, sa, _ = db.quantize_activations(x, bits=8, layout=db.CODES_NATURAL)
+    y = torch.empty((m, n), dtype=torch.float32, device="cuda")
+    flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device="cuda")
+    fn = lambda: db.gemm(a, db.CODES_NATURAL, sa, codes, scales, m, n, k, 4, residual=y)
+    for _ in range(3):
+        fn()
+    us = _device_time_us(fn, reps, flush)
+    peak_tf, _, kind = measured_peaks()
+    tf = 2.0 * m * n * k / us / 1e6
+    return {"us": us, "tflops": tf, "frac_of_bf16_peak": tf / peak_tf, "peak_kind": kind,
+            "timing": f"device, median of {reps}, L2 flushed"}
+
+
+def shape_gemv(db, rows=(1, 4, 8), reps=20):
+    """Small-M decode GEMV on the C5 layers (hidden 2560, 32q/8kv x 128, FF 9728, Q4 g64): weight
+    (+ scale) bytes streamed from HBM per launch over the measured copy bandwidth."""
+    import torch
+    hid, ff = 2560, 9728
+    shapes = [("qkv", hid, 32 * 128 + 2 * 8 * 128), ("o", 32 * 128, hid), ("gate_up", hid, 2 * ff), ("down", ff, hid)]
+    flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device="cuda")
+    _, peak_gbs, kind = measured_peaks()
+    out = {}
+    for t, (name, k, n) in enumerate(shapes):
+        codes, scales = db.pack_weights(db.synthetic_bf16(SEED, 100 + t, (n, k), 0.02), 4)
+        wbytes = codes.numel() + (k // 64) * n * 4
+        for m in rows:
+            x = torch.randn(m, k, device="cuda")
+            a, sa, sums = db.quantize_activations(x, bits=8, layout=db.CODES_GEMV, sums=True)
+            y = torch.empty((m, n), dtype=torch.float32, device="cuda")
+            fn = lambda: db.gemm(a, db.CODES_GEMV, sa, codes, scales, m, n, k, 4, a_sums=sums, residual=y)
+            for _ in range(3):
+                fn()
+            us = _device_time_us(fn, reps, flush)
+            out[f"{name}_M{m}"] = {"us": us, "GB/s": wbytes / us / 1e3, "frac_of_hbm": wbytes / us / 1e3 / peak_gbs}
+    for m in rows:
+        fr = [v["frac_of_hbm"] for kk, v in out.items() if kk.endswith(f"_M{m}")]
+        out[f"mean_frac_M{m}"] = float(np.mean(fr))
+    out["peak_kind"] = kind
+    out["timing"] = f"device, median of {reps}, L2 flushed"
+    return out
+
+
+def shape_c3(db, rank, world, local_rank, reps=3):
+    """the C2-shaped encoder with int8 (Q8 g64) weights on a ragged batch of 64
+    sequences, lengths U(16, 1024) (seed 3), through the public predict_batch (packed passes).  At
+    N > 1 the sequences are sharded by longest-processing-time (sharding.assign_lpt) and each rank
+    runs its share; the time is the max over ranks and the outputs are gathered on rank 0."""
+    import torch
+    import torch.distributed as dist
+
+    from decisive_b200 import sharding
+    cfg = dict(CFG, weight_bits=8)
+    model = db.Model.synthetic(db.EncoderConfig(**cfg, max_sequence_tokens=1024), seed=SEED, std=0.02,
+                               device=local_rank)
+    rng = np.random.default_rng(3)
+    lens = rng.integers(16, 1025, 64)
+    reqs = [rng.integers(0, CFG["vocab"], int(L)).astype(np.int32) for L in lens]
+    mine = sharding.assign_lpt([int(L) for L in lens], world)[rank]
+    local = [reqs[i] for i in mine]
+    model.predict_batch(local)  # warm-up (workspace sized)
+    torch.cuda.synchronize()
+    best = 1e30
+    for _ in range(reps):
+        if world > 1:
+            dist.barrier()
+        t0 = time.perf_counter()
+        out = model.predict_batch(local)
+        dt = time.perf_counter() - t0
+        if world > 1:
+            t = torch.tensor([dt], dtype=torch.float64, device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            dt = float(t.item())
+        best = min(best, dt)
+    ok = all(o.status == "success" for o in out)
+    if world > 1:
+        gathered = sharding.gather_ordered({i: np.asarray(o.result.response)[:4].tolist() for i, o in zip(mine, out)}, 64)
+        ok = ok and (rank != 0 or len(gathered) == 64)
+    loads = sharding.rank_loads(sharding.assign_lpt([int(L) for L in lens], world), [int(L) for L in lens])
+    model.close()
+    tokens = int(lens.sum())
+    return {"tokens_per_s": tokens / best, "ms_per_batch": best * 1e3, "sequences": 64, "tokens": tokens,
+            "all_success": bool(ok), "lpt_max_over_mean_load": max(loads) / (sum(loads) / len(loads)),
+            "timing": "host wall clock around predict_batch (host ids in, pooled embeddings out), best of "
+                      f"{reps}, max over ranks"}
+
+
+def shape_c4(db, local_rank, requests=2):
+    """BASELINE config 4 (shape): the Decima-shaped encoder (12L, D=768, 12 heads, FF 3072, W8A8
+    blocks of 32), requests of 8 sequences of 384 + U(16..48) tokens, one predict per sequence."""
+    cfg = db.BertConfig(layers=12, hidden=768, heads=12, ffn=3072, vocab=128100, max_positions=512, block=32)
+    model = db.BertModel(cfg, seed=SEED, std=0.02, device=local_rank)
+    rng = np.random.default_rng(4)
+    seqs = [rng.integers(0, cfg.vocab, 384 + int(rng.integers(16, 49))).astype(np.int32) for _ in range(8 * requests)]
+    model.predict(seqs[0])
+    t0 = time.perf_counter()
+    for s_ in seqs:
+        model.predict(s_)
+    dt = time.perf_counter() - t0
+    model.close()
+    tokens = sum(len(s_) for s_ in seqs)
+    return {"tokens_per_s": tokens / dt, "ms_per_request": dt / requests * 1e3,
+            "timing": "host wall clock around the public call per sequence (ids in, pooled state out)"}
+
+
+def shape_c5(db, local_rank, requests=3):
+    """BASELINE config 5 (shape): the Qwen3-4B-shaped decoder (36L, D=2560, 32q/8kv, FF 9728, Q4),
+    requests of a 512-token prefix and 4 continuations of 32 tokens, through the public
+    predict_continuations; cold (new prefix) and prefix-cached."""
+    cfg = db.EncoderConfig(layers=36, hidden=2560, q_heads=32, kv_heads=8, head_dim=128, ffn=9728, vocab=151936,
+                           weight_bits=4, max_sequence_tokens=1024, causal=True)
+    model = db.Model.synthetic(cfg, seed=SEED, std=0.02, device=local_rank)
+    rng = np.random.default_rng(5)
+    prefixes = rng.integers(0, cfg.vocab, (requests + 1, 512)).astype(np.int32)
+    conts = rng.integers(0, cfg.vocab, (requests + 1, 4, 32)).astype(np.int32)
+    cache = model.create_cache(db.CacheOptions(max_bytes=256 << 20, require_prefix=True))
+    model.predict_continuations(prefixes[requests], conts[requests], cache=cache)  # warm-up
+    t0 = time.perf_counter()
+    for i in range(requests):
+        model.predict_continuations(prefixes[i], conts[i], cache=cache)
+    cold = (time.perf_counter() - t0) / requests
+    t0 = time.perf_counter()
+    for i in range(requests):
+        model.predict_continuations(prefixes[0], conts[i], cache=cache)
+    hit = (time.perf_counter() - t0) / requests
+    model.close()
+    return {"ms_per_request": cold * 1e3, "ms_per_request_prefix_cached": hit * 1e3,
+            "tokens_per_s": (512 + 128) / cold,
+            "timing": "host wall clock around the public call (ids in, hidden states out)"}
+
+
+def named_shapes(db, rank, world, local_rank):
+    """Every named BASELINE shape, short: each entry is independent (a failure is recorded, not
+    raised).  C3 runs on every rank (sharded); the others on rank 0."""
+    import torch
+    import torch.distributed as dist
+    out = {}
+
+    def run(name, fn):
+        try:
+            out[name] = fn()
+        except Exception as e:  # recorded in the line
+            out[name] = {"error": f"{type(e).__name__}: {e}"[:300]}
+
+    run("c3_ragged_int8_batch", lambda: shape_c3(db, rank, world, local_rank))
+    if rank == 0:
+        run("c1_gemm", lambda: shape_c1(db))
+        run("gemv_c5_layers", lambda: shape_gemv(db))
+        run("c4_decima_encoder", lambda: shape_c4(db, local_rank))
+        run("c5_decoder_prefix", lambda: shape_c5(db, local_rank))
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    return out
+
+
 # ------------------------------------------------------------------ GPU arm
 def run_ours(args, rank, world, local_rank):
     import torch
@@ -320,6 +503,7 @@ def run_ours(args, rank, world, local_rank):
     traffic = ncu_traffic()
     launches = sum(v[1] for v in prof.values())
 
+    extras = None if args.no_extras else named_shapes(db, rank, world, local_rank)
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
@@ -338,6 +522,8 @@ def run_ours(args, rank, world, local_rank):
                 "kernel_ms_per_step": {k: v[0] / args.steps for k, v in prof.items()},
                 "weights": "streamed: pinned host memory -> two device banks" if args.stream else "resident in HBM",
                 "tile_configs": tuning}
+        if extras is not None:
+            line["named_shapes"] = extras
         if world == 1 and not args.no_cpu:
             cpu_v, info = cpu_sample(host_cores(), layers=args.cpu_layers, full_budget_s=30.0)
             line["cpu_baseline"] = {"value": cpu_v, "unit": "tokens/s", "cores": info["cores"], "kind": "port",
@@ -558,6 +744,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-layers", type=int, default=2)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-extras", action="store_true", help="skip the named BASELINE shapes in the line")
     ap.add_argument("--no-tune", action="store_true", help="skip kernel selection (default tile configurations)")
     ap.add_argument("--stream", action="store_true",
                     help="stream layer weights from pinned host memory through two device banks")
