@@ -265,32 +265,38 @@ def shape_c1(db, reps=20):
             "timing": f"device, median of {reps}, L2 flushed"}
 
 
-def shape_gemv(db, rows=(1, 4, 8), reps=20):
-    """Small-M decode GEMV on the C5 layers (hidden 2560, 32q/8kv x 128, FF 9728, Q4 g64): weight
-    (+ scale) bytes streamed from HBM per launch over the measured copy bandwidth."""
+def shape_gemv(db, rows=(1, 4, 8), copies=16, reps=5):
+    """Small-M decode GEMV on the C5 layers (hidden 2560, 32q/8kv x 128, FF 9728, Q4 g64), as a decode
+    step runs it: `copies` distinct weight matrices of one shape (together larger than L2, so every
+    launch streams its weights from HBM) launched back to back; time per launch = device time of
+    the chain / copies (median of `reps` chains).  The roofline is the weight (+ scale) bytes per
+    launch over the measured HBM copy bandwidth."""
     import torch
     hid, ff = 2560, 9728
     shapes = [("qkv", hid, 32 * 128 + 2 * 8 * 128), ("o", 32 * 128, hid), ("gate_up", hid, 2 * ff), ("down", ff, hid)]
-    flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device="cuda")
     _, peak_gbs, kind = measured_peaks()
     out = {}
     for t, (name, k, n) in enumerate(shapes):
-        codes, scales = db.pack_weights(db.synthetic_bf16(SEED, 100 + t, (n, k), 0.02), 4)
-        wbytes = codes.numel() + (k // 64) * n * 4
+        mats = [db.pack_weights(db.synthetic_bf16(SEED, 100 + 16 * t + c, (n, k), 0.02), 4) for c in range(copies)]
+        wbytes = mats[0][0].numel() + (k // 64) * n * 4
         for m in rows:
             x = torch.randn(m, k, device="cuda")
             a, sa, sums = db.quantize_activations(x, bits=8, layout=db.CODES_GEMV, sums=True)
             y = torch.empty((m, n), dtype=torch.float32, device="cuda")
-            fn = lambda: db.gemm(a, db.CODES_GEMV, sa, codes, scales, m, n, k, 4, a_sums=sums, residual=y)
-            for _ in range(3):
-                fn()
-            us = _device_time_us(fn, reps, flush)
+
+            def chain():
+                for codes, scales in mats:
+                    db.gemm(a, db.CODES_GEMV, sa, codes, scales, m, n, k, 4, a_sums=sums, residual=y)
+            chain()
+            us = _device_time_us(chain, reps) / copies
             out[f"{name}_M{m}"] = {"us": us, "GB/s": wbytes / us / 1e3, "frac_of_hbm": wbytes / us / 1e3 / peak_gbs}
+        del mats
     for m in rows:
         fr = [v["frac_of_hbm"] for kk, v in out.items() if kk.endswith(f"_M{m}")]
         out[f"mean_frac_M{m}"] = float(np.mean(fr))
     out["peak_kind"] = kind
-    out["timing"] = f"device, median of {reps}, L2 flushed"
+    out["timing"] = (f"device time of {copies} back-to-back launches on distinct weights (> L2) / {copies}, "
+                     f"median of {reps} chains")
     return out
 
 
@@ -577,52 +583,14 @@ def run_gemm(args, local_rank):
 
 
 def run_gemv(args, local_rank):
-    """Small-M grouped GEMV (decode / scoring steps; C5-shaped layers: hidden 2560, 32q/8kv x 128,
-    FF 9728, Q4 g64): HBM-bound, so the roofline is the weight (+ scale) bytes streamed from HBM
-    per launch over the measured copy bandwidth.  L2 is flushed before every launch, so the
-    weights come from HBM; device-timed with CUDA events, K launches per shape."""
+    """Small-M grouped GEMV (decode / scoring steps) on the C5-shaped layers, chained launches on
+    distinct weights (see shape_gemv)."""
     import torch
 
     import decisive_b200 as db
-    from oracle import oracle
     torch.cuda.set_device(local_rank)
-    hid, ff = 2560, 9728
-    shapes = [("qkv", hid, 32 * 128 + 2 * 8 * 128), ("o", 32 * 128, hid), ("gate_up", hid, 2 * ff), ("down", ff, hid)]
-    rows = [int(v) for v in args.gemv_rows.split(",")]
-    flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device="cuda")
-    _, peak_gbs, kind = measured_peaks()
-    results = []
-    for name, k, n in shapes:
-        rng = np.random.default_rng(k * 7 + n)
-        w = oracle.f32_to_bf16(rng.normal(0, 0.02, (n, k)).astype(np.float32))
-        codes, scales = db.pack_weights(torch.from_numpy(w.view(np.int16)).cuda(), args.bits)
-        wbytes = codes.numel() * codes.element_size() + (k // 64) * n * 4
-        for m in rows:
-            x = torch.from_numpy(rng.normal(0, 1, (m, k)).astype(np.float32)).cuda()
-            a, sa, sums = db.quantize_activations(x, bits=8, layout=db.CODES_GEMV, sums=True)
-            y = torch.empty((m, n), dtype=torch.float32, device="cuda")
-            for _ in range(args.warmup):
-                db.gemm(a, db.CODES_GEMV, sa, codes, scales, m, n, k, args.bits, a_sums=sums, residual=y)
-            torch.cuda.synchronize()
-            times = []
-            for _ in range(args.steps):
-                flush.zero_()
-                # a few microseconds of GPU sleep so the launch below is queued before the start
-                # event fires (the host-side call must not be inside the measured interval)
-                torch.cuda._sleep(200_000)
-                s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                s.record()
-                db.gemm(a, db.CODES_GEMV, sa, codes, scales, m, n, k, args.bits, a_sums=sums, residual=y)
-                e.record()
-                torch.cuda.synchronize()
-                times.append(s.elapsed_time(e))
-            us = float(np.median(times)) * 1e3
-            gbs = wbytes / us / 1e3
-            results.append({"layer": name, "M": m, "K": k, "N": n, "weight_bytes": wbytes, "us": us,
-                            "GB/s": gbs, "frac_of_hbm": gbs / peak_gbs})
-    print(json.dumps({"workload": f"gemv Q{args.bits} g64 C5-shaped layers", "peak_hbm_gbs": peak_gbs,
-                      "peak_kind": kind, "l2": "flushed before every launch", "launches_per_case": args.steps,
-                      "cases": results}), flush=True)
+    rows = tuple(int(v) for v in args.gemv_rows.split(","))
+    print(json.dumps({"workload": f"gemv Q4 g64 C5-shaped layers", **shape_gemv(db, rows=rows)}), flush=True)
 
 
 def run_decima(args, local_rank):

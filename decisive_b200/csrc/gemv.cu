@@ -6,20 +6,26 @@
 // exact integer, who computes it does not matter: the K range is split freely across threads and
 // only the final per-(row, activation row) fold runs in group order.
 //
-// Layout: a CTA owns GEMV_ROWS output rows.  Work items are (16-byte chunk of K, block of
-// GEMV_RB rows): a thread loads the chunk's activation codes once (L1-resident, shared by every
-// CTA) and reuses them for GEMV_RB weight rows, so activation traffic per weight byte stays low
-// even at M = 8.  Partial dots of the chunks of one group are reduced across neighbouring lanes
-// and parked in shared memory; after one CTA barrier, one thread per (row, activation row) runs the
-// sequential fold from shared memory (weight and activation scales staged there first).
+// Layout: a CTA owns ROWS output rows (32 at M = 1, 16 at M <= 4, 8 at M <= 8: the parked dots
+// [ROWS][M][G] stay within shared memory).  Work items are (16-byte chunk of K, block of GEMV_RB
+// rows): a thread loads the chunk's activation codes once (L1-resident, shared by every CTA) and
+// reuses them for GEMV_RB weight rows, so activation traffic per weight byte stays low even at
+// M = 8.  Partial dots of the chunks of one group are reduced across neighbouring lanes and parked
+// in shared memory; after one CTA barrier, one thread per (row, activation row) runs the sequential
+// fold from shared memory (weight and activation scales staged there first).
+//
+// The kernel is launched with programmatic dependent launch: its first weight loads (weights are
+// never written by the kernel before it) go out before it waits for the previous kernel, so in a
+// decode chain the weight stream of one projection overlaps the tail of the one before.
 #include "common.cuh"
 #include "kernels.h"
 
 namespace db {
 
 constexpr int GEMV_MAX_ROWS = 8;      // activation rows (M) handled by this path
-constexpr int GEMV_ROWS = 8;          // output rows per CTA
 constexpr int GEMV_RB = 4;            // output rows sharing one activation load
+// output rows per CTA for MR activation rows
+__host__ __device__ constexpr int gemv_rows(int mr) { return mr == 1 ? 32 : mr <= 4 ? 16 : 8; }
 constexpr int GEMV_MAX_THREADS = 512;  // block size grows with K: items per CTA = 2 * chunks per row
 constexpr int GEMV_MAX_GROUPS = 160;  // K <= 10240
 constexpr int GEMV_BATCH = 2;         // items whose weight loads are in flight together
@@ -81,6 +87,7 @@ __global__ void __launch_bounds__(GEMV_MAX_THREADS)
                 const int* __restrict__ nonfinite) {
     // dynamic shared memory, sized by G:
     //   dots [GEMV_ROWS][MR][G] | sw_s [G][GEMV_ROWS] | sa_s [G][MR] | corr_s [G][MR]
+    constexpr int GEMV_ROWS = gemv_rows(MR);
     extern __shared__ int gemv_smem[];
     int* dots = gemv_smem;
     float* sw_s = reinterpret_cast<float*>(gemv_smem + GEMV_ROWS * MR * G);
@@ -110,10 +117,12 @@ __global__ void __launch_bounds__(GEMV_MAX_THREADS)
             }
         }
     };
-    // the first weight loads go out before anything else, so their HBM latency overlaps the
-    // staging of the scales and code sums below
+    // the first weight loads go out before anything else -- before the wait for the previous kernel
+    // (the weights are not among its outputs) -- so their HBM latency overlaps that kernel's tail
+    // and the staging of the scales and code sums below
     uint4 wv[GEMV_BATCH][GEMV_RB];
     load_batch(0, wv);
+    pdl_wait();
     for (int i = threadIdx.x; i < G * GEMV_ROWS; i += blockDim.x) {
         const int g = i / GEMV_ROWS, j = i % GEMV_ROWS;
         sw_s[i] = n0 + j < N ? __ldg(sw + (size_t)g * lds_w + n0 + j) : 0.f;
@@ -185,6 +194,7 @@ __global__ void __launch_bounds__(GEMV_MAX_THREADS)
 
 template <int BITS, int MR, bool FUSED, bool RESIDUAL>
 static int launch_mr(const DbGemvArgs& a, int G, cudaStream_t s) {
+    constexpr int GEMV_ROWS = gemv_rows(MR);
     auto kernel = gemv_kernel<BITS, MR, FUSED, RESIDUAL>;
     {
         const int max_bytes = (GEMV_ROWS * MR + GEMV_ROWS + 2 * MR) * GEMV_MAX_GROUPS * 4;
@@ -197,9 +207,9 @@ static int launch_mr(const DbGemvArgs& a, int G, cudaStream_t s) {
     const int items = (GEMV_ROWS / GEMV_RB) * G * (BITS == 4 ? 2 : 4);
     int threads = 128;
     while (threads < GEMV_MAX_THREADS && threads * GEMV_BATCH < items) threads *= 2;
-    kernel<<<grid, threads, bytes, s>>>(a.a_codes, a.lda, a.sa, a.a_sums, a.ldsa, a.w_codes, a.sw, a.M, a.N, G,
-                                             a.y, a.ldy, a.nonfinite);
-    return (int)cudaGetLastError();
+    const cudaError_t e = db_launch_pdl(kernel, grid, dim3(threads), bytes, s, a.a_codes, a.lda, a.sa, a.a_sums,
+                                        a.ldsa, a.w_codes, a.sw, a.M, a.N, G, a.y, a.ldy, a.nonfinite);
+    return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }
 
 template <int BITS, bool FUSED, bool RESIDUAL>
