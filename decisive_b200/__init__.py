@@ -597,6 +597,26 @@ class BertModel:
             raise Error._from(err)
         return (pooled, h) if hidden else pooled
 
+    HEAD_OUTPUTS = 3
+
+    def score(self, state, choices, pooled: bool = False):
+        """One cross-encoder request: logits [len(choices), 3] for the sequences state ++ choice,
+        run packed in one pass (and their pooled states [len(choices), hidden] when asked)."""
+        import numpy as np
+        state = np.ascontiguousarray(state, dtype=np.int32)
+        chs = [np.ascontiguousarray(c, dtype=np.int32) for c in choices]
+        ptrs = (C.c_void_p * max(len(chs), 1))(*[c.ctypes.data for c in chs])
+        lens = (C.c_size_t * max(len(chs), 1))(*[c.size for c in chs])
+        logits = np.empty((len(chs), self.HEAD_OUTPUTS), np.float32)
+        p = np.empty((len(chs), self.config.hidden), np.float32) if pooled else None
+        err = _lib.DbError()
+        rc = load().db_bert_score(self._h, state.ctypes.data_as(C.c_void_p), state.size, ptrs, lens, len(chs),
+                                  logits.ctypes.data_as(C.c_void_p),
+                                  p.ctypes.data_as(C.c_void_p) if p is not None else None, C.byref(err))
+        if rc:
+            raise Error._from(err)
+        return (logits, p) if pooled else logits
+
     def close(self):
         if getattr(self, "_h", None):
             load().db_bert_destroy(self._h)

@@ -95,6 +95,7 @@ SIGNATURES = [
     ("db_bert_create_synthetic", _vp, [_i32, C.POINTER(BertConfig), C.c_uint64, _f, C.POINTER(DbError)]),
     ("db_bert_destroy", None, [_vp]),
     ("db_bert_predict", _i32, [_vp, _vp, _sz, _vp, _vp, C.POINTER(DbError)]),
+    ("db_bert_score", _i32, [_vp, _vp, _sz, _vp, _vp, _sz, _vp, _vp, C.POINTER(DbError)]),
     ("db_predict_continuations", _i32, [_vp, _vp, _vp, _sz, _vp, _sz, _sz, _vp, _vp, C.POINTER(DbError)]),
     ("db_cache_stats", _i32, [_vp, _vp, _vp, _vp]),
     ("db_model_profile", _i32, [_vp, _i32]),

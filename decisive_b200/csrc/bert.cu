@@ -26,14 +26,28 @@ __global__ void bf16_to_f32_kernel(const uint16_t* __restrict__ in, int64_t n, f
         out[i] = __uint_as_float((uint32_t)in[i] << 16);
 }
 
-// x[t] = (word[id] + type[0]) + pos[t]   (decima/mod.rs:503-508)
+// x[t] = (word[id] + type[0]) + pos[p]   (decima/mod.rs:503-508); p = t, or positions[t] for
+// sequences packed one after another
 __global__ void embed_kernel(const int32_t* __restrict__ ids, const float* __restrict__ word,
-                             const float* __restrict__ type, const float* __restrict__ pos, int D,
-                             float* __restrict__ x) {
+                             const float* __restrict__ type, const float* __restrict__ pos,
+                             const int32_t* __restrict__ positions, int D, float* __restrict__ x) {
     const int t = blockIdx.x;
     const float* w = word + (size_t)ids[t] * D;
+    const size_t p = positions ? (size_t)positions[t] : (size_t)t;
     for (int i = threadIdx.x; i < D; i += blockDim.x)
-        x[(size_t)t * D + i] = __fadd_rn(__fadd_rn(w[i], type[i]), pos[(size_t)t * D + i]);
+        x[(size_t)t * D + i] = __fadd_rn(__fadd_rn(w[i], type[i]), pos[p * D + i]);
+}
+
+// Scorer head (f32 linear, sequential sums as the reference's portable f32 kernel): logits[s, o] =
+// sum_k pooled[s, k] * w[o, k] + b[o] for NO outputs; one warp per (sequence, output), lane 0
+// accumulates in index order.
+__global__ void head_kernel(const float* __restrict__ pooled, const float* __restrict__ w, const float* __restrict__ b,
+                            int nseq, int D, int NO, float* __restrict__ out) {
+    const int s = blockIdx.x, o = threadIdx.x / 32, lane = threadIdx.x & 31;
+    if (s >= nseq || o >= NO || lane != 0) return;
+    float acc = 0.f;
+    for (int k = 0; k < D; ++k) acc = __fadd_rn(acc, __fmul_rn(pooled[(size_t)s * D + k], w[(size_t)o * D + k]));
+    out[(size_t)s * NO + o] = __fadd_rn(acc, b[o]);
 }
 
 __device__ __forceinline__ float block_sum(float v, float* red) {
@@ -135,11 +149,15 @@ struct db_bert {
         float *bqkv, *bo, *b1, *b2, *ln1_w, *ln1_b, *ln2_w, *ln2_b;
     };
     std::vector<Layer> layers;
-    // workspace for cfg.max_positions tokens
+    float *head_w = nullptr, *head_b = nullptr;  // scorer head [DB_BERT_HEAD_OUTPUTS, hidden] + bias
+    // workspace for cap rows (one sequence of cfg.max_positions tokens, or a request's packed
+    // sequences: kBatchSeqs of them)
+    int cap = 0;
     float *x = nullptr, *tmp = nullptr, *qkv = nullptr, *h = nullptr, *ctx128 = nullptr, *ctx = nullptr,
-          *scales = nullptr, *pooled = nullptr;
-    __half *codes = nullptr, *q16 = nullptr, *k16 = nullptr, *v16 = nullptr;
-    int32_t* ids = nullptr;
+          *scales = nullptr, *pooled = nullptr, *logits = nullptr;
+    int8_t* codes = nullptr;
+    __half *q16 = nullptr, *k16 = nullptr, *v16 = nullptr;
+    int32_t *ids = nullptr, *positions = nullptr, *cu = nullptr;
     int* flag = nullptr;
     template <class T>
     bool alloc(T** p, size_t count) {
@@ -153,6 +171,8 @@ namespace {
 
 // synthetic tensor ids (db_synthetic_bf16 keys): word 0, pos 1, type 2; layer l: 16 + 16 l + kind
 enum { K_Q = 0, K_K, K_V, K_O, K_FF1, K_FF2, K_BQ, K_BK, K_BV, K_BO, K_B1, K_B2 };
+constexpr uint64_t K_HEAD_W = 3, K_HEAD_B = 4;  // scorer head (model-level ids, below the layers')
+constexpr int kBatchSeqs = 16;                  // sequences one packed pass holds (a request has 8)
 inline uint64_t tid(int l, int kind) { return 16 + 16ull * l + kind; }
 
 int build_synthetic(db_bert* m, uint64_t seed, float stdv) {
@@ -236,16 +256,25 @@ int build_synthetic(db_bert* m, uint64_t seed, float stdv) {
     int h = 0;
     cudaMemcpy(&h, bad, 4, cudaMemcpyDeviceToHost);  // synchronises: the staging is free to go
     if (!rc && h) rc = db_fail(DB_ERR_NONFINITE, "INVALID_WEIGHTS", "non-finite synthetic weight");
+    // scorer head (f32, like the reference's Precision::F32 score linear)
+    if (!rc && (!m->alloc(&m->head_w, (size_t)DB_BERT_HEAD_OUTPUTS * D) || !m->alloc(&m->head_b, DB_BERT_HEAD_OUTPUTS)))
+        rc = db_fail(DB_ERR_CUDA, "RESOURCE_LIMIT", "head allocation");
+    if (!rc) rc = gen(K_HEAD_W, (int64_t)DB_BERT_HEAD_OUTPUTS * D, m->head_w);
+    if (!rc) rc = gen(K_HEAD_B, DB_BERT_HEAD_OUTPUTS, m->head_b);
+    cudaStreamSynchronize(st);
     // workspace
-    const int H = c.heads, Kmax = std::max(D, F);
-    const int64_t lds = db_scale_stride(P), GSmax = (Kmax + c.block - 1) / c.block;
-    if (!rc && (!m->alloc(&m->x, (size_t)P * D) || !m->alloc(&m->tmp, (size_t)P * D) ||
-                !m->alloc(&m->qkv, (size_t)P * 3 * D) || !m->alloc(&m->h, (size_t)P * F) ||
-                !m->alloc(&m->ctx128, (size_t)P * H * 128) || !m->alloc(&m->ctx, (size_t)P * D) ||
-                !m->alloc(&m->scales, (size_t)GSmax * lds) || !m->alloc(&m->pooled, D) ||
-                !m->alloc(&m->codes, (size_t)P * ((Kmax + 63) / 64 * 64)) || !m->alloc(&m->q16, (size_t)P * H * 128) ||
-                !m->alloc(&m->k16, (size_t)P * H * 128) || !m->alloc(&m->v16, (size_t)P * H * 128) ||
-                !m->alloc(&m->ids, P) || !m->alloc(&m->flag, 4)))
+    const int H = c.heads, Kmax = std::max(D, F), R = kBatchSeqs * P;
+    m->cap = R;
+    const int64_t lds = db_scale_stride(R), GSmax = (Kmax + c.block - 1) / c.block;
+    if (!rc && (!m->alloc(&m->x, (size_t)R * D) || !m->alloc(&m->tmp, (size_t)R * D) ||
+                !m->alloc(&m->qkv, (size_t)R * 3 * D) || !m->alloc(&m->h, (size_t)R * F) ||
+                !m->alloc(&m->ctx128, (size_t)R * H * 128) || !m->alloc(&m->ctx, (size_t)R * D) ||
+                !m->alloc(&m->scales, (size_t)GSmax * lds) || !m->alloc(&m->pooled, (size_t)kBatchSeqs * D) ||
+                !m->alloc(&m->logits, (size_t)kBatchSeqs * DB_BERT_HEAD_OUTPUTS) ||
+                !m->alloc(&m->codes, (size_t)R * ((Kmax + 63) / 64 * 64)) || !m->alloc(&m->q16, (size_t)R * H * 128) ||
+                !m->alloc(&m->k16, (size_t)R * H * 128) || !m->alloc(&m->v16, (size_t)R * H * 128) ||
+                !m->alloc(&m->ids, R) || !m->alloc(&m->positions, R) || !m->alloc(&m->cu, kBatchSeqs + 1) ||
+                !m->alloc(&m->flag, 4)))
         rc = db_fail(DB_ERR_CUDA, "RESOURCE_LIMIT", "workspace exceeds device limits");
     return rc;
 }
@@ -254,8 +283,8 @@ int build_synthetic(db_bert* m, uint64_t seed, float stdv) {
 int linear(db_bert* m, const float* x, int T, int K, const uint8_t* wc, const float* ws, int N, const float* b,
            float* y) {
     const auto& c = m->cfg;
-    const int64_t Kp = (K + 63) / 64 * 64, lds = db_scale_stride(c.max_positions);
-    int rc = db_launch_decima_quantize(x, K, T, K, c.block, m->codes, DB_CODES_TC_F16, Kp, m->scales, lds, 0,
+    const int64_t Kp = (K + 63) / 64 * 64, lds = db_scale_stride(m->cap);
+    int rc = db_launch_decima_quantize(x, K, T, K, c.block, m->codes, DB_CODES_NATURAL_I8, Kp, m->scales, lds, 0,
                                        m->flag, m->stream);
     if (rc) return rc;
     DbGemmArgs a{};
@@ -278,15 +307,21 @@ int linear(db_bert* m, const float* x, int T, int K, const uint8_t* wc, const fl
     a.block = c.block;
     a.bias = b;
     a.add_bias = 1;
-    return db_launch_gemm_tc(a, m->stream);
+    const db_gemm_config d = db_gemm_i8_default_config(T, N, DB_EPI_STORE);
+    a.block_n = d.block_n;
+    a.pair_ctas = d.pair_ctas;
+    return db_launch_gemm_i8(a, m->stream);
 }
 
-int forward(db_bert* m, int T) {
+// T rows: one sequence (nseq == 0), or nseq sequences packed one after another (m->cu holds
+// their row boundaries, m->positions each row's position; attention per sequence, pooled into
+// m->pooled [nseq, D]).
+int forward(db_bert* m, int T, int nseq = 0, int max_len = 0) {
     const auto& c = m->cfg;
     const int D = c.hidden, F = c.ffn, H = c.heads, hd = D / H;
     cudaStream_t st = m->stream;
     cudaMemsetAsync(m->flag, 0, 4, st);
-    embed_kernel<<<T, 256, 0, st>>>(m->ids, m->word, m->type, m->pos, D, m->x);
+    embed_kernel<<<T, 256, 0, st>>>(m->ids, m->word, m->type, m->pos, nseq ? m->positions : nullptr, D, m->x);
     layer_norm_kernel<<<T, 128, 0, st>>>(m->x, nullptr, m->emb_ln_w, m->emb_ln_b, D, c.eps);
     int rc = (int)cudaGetLastError();
     for (int l = 0; l < c.layers && !rc; ++l) {
@@ -294,8 +329,11 @@ int forward(db_bert* m, int T) {
         rc = linear(m, m->x, T, D, w.qkv_c, w.qkv_s, 3 * D, w.bqkv, m->qkv);
         if (rc) break;
         split_heads_kernel<<<T, 256, 0, st>>>(m->qkv, T, H, hd, m->q16, m->k16, m->v16);
-        rc = db_launch_attention(m->q16, m->k16, m->v16, T, H, H, 1.f / sqrtf((float)hd), m->ctx128, (int64_t)H * 128,
-                                 st);
+        rc = nseq ? db_launch_attention_varlen(m->q16, m->k16, m->v16, m->cu, nseq, max_len, T, H, H,
+                                               1.f / sqrtf((float)hd), m->ctx128, (int64_t)H * 128, nullptr, 0,
+                                               nullptr, 0, nullptr, st)
+                  : db_launch_attention(m->q16, m->k16, m->v16, T, H, H, 1.f / sqrtf((float)hd), m->ctx128,
+                                        (int64_t)H * 128, st);
         if (rc) break;
         merge_heads_kernel<<<T, 256, 0, st>>>(m->ctx128, H, hd, m->ctx);
         rc = linear(m, m->ctx, T, D, w.o_c, w.o_s, D, w.bo, m->tmp);
@@ -309,7 +347,8 @@ int forward(db_bert* m, int T) {
         layer_norm_kernel<<<T, 128, 0, st>>>(m->x, m->tmp, w.ln2_w, w.ln2_b, D, c.eps);
         rc = (int)cudaGetLastError();
     }
-    if (!rc) rc = db_launch_mean_pool(m->x, D, T, D, m->pooled, st);
+    if (!rc) rc = nseq ? db_launch_mean_pool_varlen(m->x, D, m->cu, nseq, D, m->pooled, st)
+                       : db_launch_mean_pool(m->x, D, T, D, m->pooled, st);
     return rc;
 }
 
@@ -373,6 +412,69 @@ int db_bert_predict(db_bert* m, const int32_t* ids, size_t n, float* pooled, flo
     cudaMemcpyAsync(pooled, m->pooled, (size_t)m->cfg.hidden * 4, cudaMemcpyDeviceToHost, m->stream);
     if (hidden) cudaMemcpyAsync(hidden, m->x, n * m->cfg.hidden * 4, cudaMemcpyDeviceToHost, m->stream);
     const cudaError_t e = cudaStreamSynchronize(m->stream);
+    if (rc || e != cudaSuccess) {
+        fill_error(err, "INFERENCE_FAILED", rc ? cudaGetErrorString((cudaError_t)rc) : cudaGetErrorString(e));
+        return -1;
+    }
+    if (flag) {
+        fill_error(err, "INFERENCE_FAILED", "non-finite hidden state");
+        return -1;
+    }
+    return 0;
+}
+
+// One request of the cross-encoder: sequence i = state ++ choices[i] (positions restart at 0 for
+// every sequence), all count sequences packed into one pass; logits [count, DB_BERT_HEAD_OUTPUTS]
+// = head(mean-pooled final state) per sequence, pooled [count, hidden] when non-null.
+int db_bert_score(db_bert* m, const int32_t* state, size_t n_state, const int32_t* const* choices,
+                  const size_t* choice_lens, size_t count, float* logits, float* pooled, db_error* err) {
+    if (!m || (!state && n_state) || !choices || !choice_lens || !logits) {
+        fill_error(err, "INVALID_PARAMETERS", "null model, state, choices or output");
+        return -1;
+    }
+    if (count == 0 || count > (size_t)kBatchSeqs) {
+        fill_error(err, "INVALID_REQUEST", "a request scores 1.." + std::to_string(kBatchSeqs) + " choices");
+        return -1;
+    }
+    const auto& c = m->cfg;
+    std::vector<int32_t> ids, pos;
+    std::vector<int> cu(count + 1, 0);
+    int max_len = 0;
+    for (size_t i = 0; i < count; ++i) {
+        const size_t L = n_state + choice_lens[i];
+        if (L == 0 || L > (size_t)c.max_positions || (choice_lens[i] && !choices[i])) {
+            fill_error(err, L == 0 || L <= (size_t)c.max_positions ? "INVALID_REQUEST" : "INPUT_TOO_LONG",
+                       "each state + choice sequence takes 1.." + std::to_string(c.max_positions) + " tokens");
+            return -1;
+        }
+        for (size_t t = 0; t < L; ++t) {
+            const int32_t id = t < n_state ? state[t] : choices[i][t - n_state];
+            if (id < 0 || id >= c.vocab) {
+                fill_error(err, "INVALID_REQUEST", "token id " + std::to_string(id) + " outside the vocabulary");
+                return -1;
+            }
+            ids.push_back(id);
+            pos.push_back((int32_t)t);
+        }
+        cu[i + 1] = cu[i] + (int)L;
+        max_len = std::max(max_len, (int)L);
+    }
+    const int T = cu[count], D = c.hidden, NO = DB_BERT_HEAD_OUTPUTS;
+    cudaSetDevice(m->device);
+    cudaStream_t st = m->stream;
+    cudaMemcpyAsync(m->ids, ids.data(), (size_t)T * 4, cudaMemcpyHostToDevice, st);
+    cudaMemcpyAsync(m->positions, pos.data(), (size_t)T * 4, cudaMemcpyHostToDevice, st);
+    cudaMemcpyAsync(m->cu, cu.data(), (count + 1) * 4, cudaMemcpyHostToDevice, st);
+    int rc = forward(m, T, (int)count, max_len);
+    if (!rc) {
+        head_kernel<<<(unsigned)count, 32 * NO, 0, st>>>(m->pooled, m->head_w, m->head_b, (int)count, D, NO, m->logits);
+        rc = (int)cudaGetLastError();
+    }
+    int flag = 0;
+    cudaMemcpyAsync(&flag, m->flag, 4, cudaMemcpyDeviceToHost, st);
+    cudaMemcpyAsync(logits, m->logits, count * NO * 4, cudaMemcpyDeviceToHost, st);
+    if (pooled) cudaMemcpyAsync(pooled, m->pooled, count * D * 4, cudaMemcpyDeviceToHost, st);
+    const cudaError_t e = cudaStreamSynchronize(st);
     if (rc || e != cudaSuccess) {
         fill_error(err, "INFERENCE_FAILED", rc ? cudaGetErrorString((cudaError_t)rc) : cudaGetErrorString(e));
         return -1;

@@ -317,6 +317,16 @@ typedef struct db_bert db_bert;
 db_bert *db_bert_create_synthetic(int device, const db_bert_config *cfg, uint64_t seed, float std, db_error *err);
 void db_bert_destroy(db_bert *m);
 int db_bert_predict(db_bert *m, const int32_t *ids, size_t n, float *pooled, float *hidden, db_error *err);
+/* The cross-encoder request (one state paired with `count` choices, 1..16): sequence i is
+ * state ++ choices[i] with positions restarting at 0, every sequence of 1..max_positions tokens;
+ * the sequences run packed in one pass (per-sequence attention, segmented mean pool) and each
+ * yields DB_BERT_HEAD_OUTPUTS f32 logits from the scorer head, an f32 linear over the pooled state
+ * with sequential sums in index order (decima/mod.rs:482, 701: the `score` linear, Precision::F32,
+ * portable kernel; synthetic weights: key 3 [outputs, hidden], bias key 4).  logits
+ * [count, DB_BERT_HEAD_OUTPUTS]; pooled [count, hidden] when non-null. */
+#define DB_BERT_HEAD_OUTPUTS 3
+int db_bert_score(db_bert *m, const int32_t *state, size_t n_state, const int32_t *const *choices,
+                  const size_t *choice_lens, size_t count, float *logits, float *pooled, db_error *err);
 
 /* Prefix-state cache and continuation batching for causal models (C5; the reference's Kev prefix
  * reuse, kev/mod.rs:163-240, and per-question continuation from a clone of the prefix state,

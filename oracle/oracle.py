@@ -475,6 +475,23 @@ def gelu(x):
     return x
 
 
+def bert_score_head(pooled, w, b):
+    """The scorer head of the cross-encoder: an f32 linear over each pooled state, summed in index
+    order from 0 with a separate multiply and add per term, then the bias (decima/mod.rs:482, 701:
+    the `score` linear, Precision::F32, Kernel::Portable).  pooled [S, D], w [O, D], b [O] ->
+    [S, O]."""
+    pooled = np.asarray(pooled, np.float32)
+    w, b = np.asarray(w, np.float32), np.asarray(b, np.float32)
+    out = np.empty((pooled.shape[0], w.shape[0]), np.float32)
+    for s in range(pooled.shape[0]):
+        for o in range(w.shape[0]):
+            acc = np.float32(0)
+            for k in range(w.shape[1]):
+                acc = np.float32(acc + np.float32(pooled[s, k] * w[o, k]))
+            out[s, o] = np.float32(acc + b[o])
+    return out
+
+
 def bert_forward(cfg: dict, w: dict, ids, mode: int = 0):
     """Composed Decima (BERT-shaped, decima/mod.rs:492-556) encoder forward with W8A8 block
     projections: x = LN(word[id] + type[0] + pos[p]); per layer x = LN(x + o(attn(q, k, v)));

@@ -82,18 +82,18 @@ def test_c2_all_28_layers_match_oracle(db, oracle):
 
 
 def test_c4_full_width_matches_oracle(db):
-    from oracle import oracle
-    from test_gpu_bert import oracle_weights
+    """BASELINE config 4 dimensions (768 hidden, 12 heads, FF 3072, vocab 128100, W8A8 blocks of
+    32) on one request as the config states it: a 384-token state and 8 choices of U(16..48)
+    tokens, scored as 8 packed state+choice sequences into 3-way logits."""
+    from test_gpu_bert import check_score
     cfg = dict(layers=2, hidden=768, heads=12, ffn=3072, vocab=128100, max_positions=512, block=32, eps=1e-12)
     seed, std = 3, 0.05
     model = db.BertModel(db.BertConfig(**cfg), seed=seed, std=std)
-    ids = np.random.default_rng(4).integers(0, cfg["vocab"], 384 + 32).astype(np.int32)
-    pooled, states = model.predict(ids, hidden=True)
+    rng = np.random.default_rng(4)
+    state = rng.integers(0, cfg["vocab"], 384).astype(np.int32)
+    choices = [rng.integers(0, cfg["vocab"], int(rng.integers(16, 49))).astype(np.int32) for _ in range(8)]
+    check_score(db, model, cfg, seed, std, state, choices, oracle_seqs=(0, 5))
     model.close()
-    want_pooled, want_states = oracle.bert_forward(cfg, oracle_weights(db, cfg, seed, std), ids)
-    assert cosine(pooled, want_pooled) >= 0.9999, cosine(pooled, want_pooled)
-    per_token = [cosine(states[t], want_states[t]) for t in range(len(ids))]
-    assert min(per_token) >= 0.999, min(per_token)
 
 
 def test_c5_full_width_continuations_match_causal_oracle(db, oracle):

@@ -3,7 +3,12 @@
 LayerNorm and erf GELU of decima/cpu.rs).  The attention runs in f16 on the GPU and in f32 on the
 CPU, and CUDA's erff differs from libm's by an ulp or so, so the bar is the encoder's: mean-pooled
 state cosine >= 0.9999, every token's state >= 0.999.  Relative-position attention is not part of
-this model (the reference's Decima uses absolute positions)."""
+this model (the reference's Decima uses absolute positions).
+
+The cross-encoder request (score: one state with several choices, run as packed state+choice
+sequences) computes every row, every sequence's attention and every pool as a one-sequence predict
+does, so its pooled states equal predict's bit for bit, and its scorer head equals the oracle's
+sequential f32 linear bit for bit on the same pooled state."""
 import numpy as np
 import pytest
 
@@ -73,4 +78,63 @@ def test_c4_encoder_rejects_bad_requests(db):
     assert e.value.code == "INVALID_REQUEST"
     with pytest.raises(db.Error):
         db.BertModel(db.BertConfig(layers=1, hidden=250, heads=4, ffn=512, vocab=100, max_positions=64))
+    model.close()
+
+
+def head_weights(db, cfg, seed, std):
+    def f32(tensor, shape):
+        bits = db.synthetic_bf16(seed, tensor, shape, std).cpu().numpy().view(np.uint16).astype(np.uint32) << 16
+        return bits.view(np.float32).reshape(shape)
+    return f32(3, (3, cfg["hidden"])), f32(4, (3,))
+
+
+def check_score(db, model, cfg, seed, std, state, choices, oracle_seqs=()):
+    from oracle import oracle
+    logits, pooled = model.score(state, choices, pooled=True)
+    assert logits.shape == (len(choices), 3) and pooled.shape == (len(choices), cfg["hidden"])
+    hw, hb = head_weights(db, cfg, seed, std)
+    # the head on the GPU's pooled states: bit-exact against the sequential f32 linear
+    assert np.array_equal(logits.view(np.uint32), oracle.bert_score_head(pooled, hw, hb).view(np.uint32))
+    for i, ch in enumerate(choices):
+        single = model.predict(np.concatenate([state, ch]))
+        assert np.array_equal(pooled[i].view(np.uint32), single.view(np.uint32)), i
+    if oracle_seqs:
+        w = oracle_weights(db, cfg, seed, std)
+        for i in oracle_seqs:
+            want_pooled, _ = oracle.bert_forward(cfg, w, np.concatenate([state, choices[i]]))
+            assert cosine(pooled[i], want_pooled) >= 0.9999, (i, cosine(pooled[i], want_pooled))
+            want = oracle.bert_score_head(want_pooled[None, :], hw, hb)[0]
+            # pooled cosine >= 0.9999 puts |pooled - want| within ~0.0142 |want|, so by Cauchy-Schwarz
+            # each logit is within 0.02 |w_o| |want| of the oracle's
+            bound = 0.02 * np.linalg.norm(hw, axis=1) * np.linalg.norm(want_pooled)
+            assert np.all(np.abs(logits[i] - want) <= bound), (logits[i], want, bound)
+
+
+@pytest.mark.parametrize("block,nstate,lens", [(32, 40, (5, 17, 1, 33, 9)), (64, 1, (3,)), (32, 0, (7, 64, 2)),
+                                               (32, 60, (0, 4))])
+def test_c4_score_packed_request(db, block, nstate, lens):
+    cfg = dict(layers=2, hidden=256, heads=4, ffn=512, vocab=1000, max_positions=128, block=block, eps=1e-12)
+    seed, std = 9, 0.05
+    model = db.BertModel(db.BertConfig(**cfg), seed=seed, std=std)
+    rng = np.random.default_rng(nstate)
+    state = rng.integers(0, cfg["vocab"], nstate).astype(np.int32)
+    choices = [rng.integers(0, cfg["vocab"], n).astype(np.int32) for n in lens]
+    check_score(db, model, cfg, seed, std, state, choices, oracle_seqs=(0, len(lens) - 1))
+    model.close()
+    assert db.device_error_word() == 0
+
+
+def test_c4_score_rejects_bad_requests(db):
+    cfg = db.BertConfig(layers=1, hidden=256, heads=4, ffn=512, vocab=100, max_positions=64)
+    model = db.BertModel(cfg)
+    state = np.arange(40) % 100
+    for choices, code in (([], "INVALID_REQUEST"), ([[1]] * 17, "INVALID_REQUEST"), ([[1], [2] * 25], "INPUT_TOO_LONG"),
+                          ([[1], [100]], "INVALID_REQUEST")):
+        with pytest.raises(db.Error) as e:
+            model.score(state, choices)
+        assert e.value.code == code, choices
+    with pytest.raises(db.Error) as e:
+        model.score([], [[]])
+    assert e.value.code == "INVALID_REQUEST"
+    assert model.score(state, [[1]] * 16).shape == (16, 3)  # the model still serves
     model.close()
