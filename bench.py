@@ -373,8 +373,9 @@ def shape_c4(db, local_rank, requests=4):
 
 def shape_c5(db, local_rank, requests=3):
     """BASELINE config 5 (shape): the Qwen3-4B-shaped decoder (36L, D=2560, 32q/8kv, FF 9728, Q4),
-    requests of a 512-token prefix and 4 continuations of 32 tokens, through the public
-    predict_continuations; cold (new prefix) and prefix-cached."""
+    requests of a 512-token prefix and 4 continuations of 32 tokens scored by log-probability
+    (LM head over the 151,936-token vocabulary), through the public score_continuations; cold
+    (new prefix) and prefix-cached."""
     cfg = db.EncoderConfig(layers=36, hidden=2560, q_heads=32, kv_heads=8, head_dim=128, ffn=9728, vocab=151936,
                            weight_bits=4, max_sequence_tokens=1024, causal=True)
     model = db.Model.synthetic(cfg, seed=SEED, std=0.02, device=local_rank)
@@ -382,19 +383,19 @@ def shape_c5(db, local_rank, requests=3):
     prefixes = rng.integers(0, cfg.vocab, (requests + 1, 512)).astype(np.int32)
     conts = rng.integers(0, cfg.vocab, (requests + 1, 4, 32)).astype(np.int32)
     cache = model.create_cache(db.CacheOptions(max_bytes=256 << 20, require_prefix=True))
-    model.predict_continuations(prefixes[requests], conts[requests], cache=cache)  # warm-up
+    model.score_continuations(prefixes[requests], conts[requests], cache=cache)  # warm-up
     t0 = time.perf_counter()
     for i in range(requests):
-        model.predict_continuations(prefixes[i], conts[i], cache=cache)
+        model.score_continuations(prefixes[i], conts[i], cache=cache)
     cold = (time.perf_counter() - t0) / requests
     t0 = time.perf_counter()
     for i in range(requests):
-        model.predict_continuations(prefixes[0], conts[i], cache=cache)
+        model.score_continuations(prefixes[0], conts[i], cache=cache)
     hit = (time.perf_counter() - t0) / requests
     model.close()
     return {"ms_per_request": cold * 1e3, "ms_per_request_prefix_cached": hit * 1e3,
             "tokens_per_s": (512 + 128) / cold,
-            "timing": "host wall clock around the public call (ids in, hidden states out)"}
+            "timing": "host wall clock around the public call (ids in, 4 x 32 log-probs out)"}
 
 
 def named_shapes(db, rank, world, local_rank):
@@ -649,7 +650,8 @@ def run_c5(args, local_rank):
     """C5 (Qwen3-4B-shaped decoder: 36 layers, D=2560, 32q/8kv x 128, FF 9728, Q4 g64, synthetic
     weights): requests of a 512-token prefix and 4 continuations of 32 tokens.  Each request runs
     the causal prefix pass once (keys/values kept per layer) and the 4 continuations batched after
-    it, through the public db_predict_continuations call (host ids in, host hidden states out).
+    it, scored by log-probability through the public db_score_continuations call (host ids in,
+    host per-token log-probs out).
     Requests have distinct prefixes, so nothing is reused across them; a second timing repeats one
     prefix to show the cached path."""
     import torch
@@ -665,21 +667,21 @@ def run_c5(args, local_rank):
     conts = rng.integers(0, cfg.vocab, (n_req + args.warmup, 4, 32)).astype(np.int32)
     cache = model.create_cache(db.CacheOptions(max_bytes=256 << 20, require_prefix=True))
     for i in range(args.warmup):
-        model.predict_continuations(prefixes[n_req + i], conts[n_req + i], cache=cache)
+        model.score_continuations(prefixes[n_req + i], conts[n_req + i], cache=cache)
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     for i in range(n_req):
-        model.predict_continuations(prefixes[i], conts[i], cache=cache)
+        model.score_continuations(prefixes[i], conts[i], cache=cache)
     dt = time.perf_counter() - t0
     t1 = time.perf_counter()
     for i in range(n_req):
-        model.predict_continuations(prefixes[0], conts[i], cache=cache)  # same prefix: reused
+        model.score_continuations(prefixes[0], conts[i], cache=cache)  # same prefix: reused
     dt_hit = time.perf_counter() - t1
     tokens = 512 + 4 * 32
-    print(json.dumps({"workload": "C5 decoder Q4 (36L, D=2560, 32q/8kv, FF 9728): 512-token prefix + 4 x 32 continuations",
+    print(json.dumps({"workload": "C5 decoder Q4 (36L, D=2560, 32q/8kv, FF 9728): 512-token prefix + 4 x 32 continuations scored by log-probability",
                       "requests": n_req, "requests_per_s": n_req / dt, "tokens_per_s": n_req * tokens / dt,
                       "ms_per_request": dt / n_req * 1e3, "ms_per_request_prefix_cached": dt_hit / n_req * 1e3,
-                      "cache": cache.stats(), "timing": "host wall clock around the public call (ids in, hidden out)",
+                      "cache": cache.stats(), "timing": "host wall clock around the public call (ids in, log-probs out)",
                       "data": "synthetic (seeded N(0,0.02) bf16 weights, uniform token ids)"}), flush=True)
     model.close()
 

@@ -465,6 +465,29 @@ class Model:
             raise Error._from(err)
         return out
 
+    def score_continuations(self, prefix, continuations, cache: Cache | None = None,
+                            cancellation: Cancellation | None = None, hidden: bool = False):
+        """Causal models: per-token log-probabilities [count, tokens] of each continuation after the
+        shared prefix, from an LM head tied to the embedding matrix (the continuation's score is
+        the row sum).  With hidden=True also the LM head's input rows [1 + count*tokens, hidden]:
+        the prefix's last final-normed state, then the continuations' states."""
+        import numpy as np
+        pre = np.ascontiguousarray(prefix, dtype=np.int32)
+        cont = np.ascontiguousarray(continuations, dtype=np.int32)
+        if cont.ndim != 2:
+            raise ValueError("continuations must be equal-length token lists")
+        out = np.empty(cont.shape, dtype=np.float32)
+        h = np.empty((1 + cont.size, self.config.hidden), dtype=np.float32) if hidden else None
+        err = _lib.DbError()
+        rc = load().db_score_continuations(self._h, cache._h if cache else None, pre.ctypes.data_as(C.c_void_p),
+                                           pre.size, cont.ctypes.data_as(C.c_void_p), cont.shape[0], cont.shape[1],
+                                           cancellation.ptr if cancellation else None,
+                                           out.ctypes.data_as(C.c_void_p),
+                                           h.ctypes.data_as(C.c_void_p) if h is not None else None, C.byref(err))
+        if rc:
+            raise Error._from(err)
+        return (out, h) if hidden else out
+
     def predict_batch(self, requests, parameters: PplxParameters | None = None, cache: Cache | None = None,
                       cancellation: Cancellation | None = None) -> list[Outcome]:
         import numpy as np

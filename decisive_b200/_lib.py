@@ -97,6 +97,7 @@ SIGNATURES = [
     ("db_bert_predict", _i32, [_vp, _vp, _sz, _vp, _vp, C.POINTER(DbError)]),
     ("db_bert_score", _i32, [_vp, _vp, _sz, _vp, _vp, _sz, _vp, _vp, C.POINTER(DbError)]),
     ("db_predict_continuations", _i32, [_vp, _vp, _vp, _sz, _vp, _sz, _sz, _vp, _vp, C.POINTER(DbError)]),
+    ("db_score_continuations", _i32, [_vp, _vp, _vp, _sz, _vp, _sz, _sz, _vp, _vp, _vp, C.POINTER(DbError)]),
     ("db_cache_stats", _i32, [_vp, _vp, _vp, _vp]),
     ("db_model_profile", _i32, [_vp, _i32]),
     ("db_model_set_code_layout", _i32, [_vp, _i32]),

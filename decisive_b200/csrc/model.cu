@@ -80,6 +80,10 @@ struct db_model {
     // per-layer prefix keys/values of a continuation call whose cache cannot keep them
     std::vector<__half*> tmp_k, tmp_v;
     int tmp_cap = 0;
+    // continuation scoring: the prefix's last final-normed state [D] (when no cache keeps it), the
+    // LM head's input rows [1 + continuation rows, D] and a logits chunk [kLmRows, vocab]
+    float *prefix_last = nullptr, *lm_x = nullptr, *logits = nullptr;
+    int lm_x_rows = 0;
     float *x = nullptr, *qkv = nullptr, *ctx = nullptr, *normed = nullptr, *pooled = nullptr;
     float *cos_t = nullptr, *sin_t = nullptr, *sa = nullptr, *sh = nullptr;
     __half *acodes = nullptr, *hcodes = nullptr, *q16 = nullptr, *k16 = nullptr, *v16 = nullptr;
@@ -147,11 +151,14 @@ struct db_cache {
     std::vector<int32_t> ids;
     int cap_P = 0;
     std::vector<__half*> k, v;
+    float* last = nullptr;  // the prefix's last final-normed state [hidden] (predicts the first continuation token)
     int64_t hits = 0, reused = 0, computed = 0;
     void release() {
-        if (!k.empty()) cudaSetDevice(device);
+        if (!k.empty() || last) cudaSetDevice(device);
         for (__half* p : k) cudaFree(p);
         for (__half* p : v) cudaFree(p);
+        if (last) cudaFree(last);
+        last = nullptr;
         k.clear();
         v.clear();
         ids.clear();
@@ -909,6 +916,7 @@ void db_model_destroy(db_model* m) {
     m->free_all(m->ws_allocations);
     m->free_all(m->rope_allocations);
     m->free_all(m->allocations);
+    if (m->lm_x) cudaFree(m->lm_x);
     for (uint8_t* h : m->host_layers) cudaFreeHost(h);
     for (uint8_t* b : m->banks) cudaFree(b);
     for (int i = 0; i < 2; ++i) {
@@ -1332,13 +1340,105 @@ int ensure_kv(std::vector<__half*>& k, std::vector<__half*>& v, int& cap, int ro
 
 extern "C" {
 
-int db_predict_continuations(db_model* m, db_cache* cache, const int32_t* prefix, size_t prefix_len,
-                             const int32_t* continuations, size_t count, size_t tokens,
-                             const volatile uint8_t* cancel, float* hidden, db_error* err) {
-    if (!m || !hidden || !prefix || !continuations) {
-        fill_error(err, "INVALID_PARAMETERS", "null model, ids or output");
+}  // extern "C"
+
+namespace {
+
+// Log-probabilities of continuation tokens from LM-head logits.  Logits rows (global index gr =
+// r0 + blockIdx.x): row 0 is the prefix's last state and predicts token 0 of every continuation;
+// row 1 + b*T + j is continuation b's token j and predicts its token j + 1 (the last token of a
+// continuation predicts nothing).  out[b*T + t] = logits[row, ids[b*T + t]] - logsumexp(row), the
+// log-sum-exp kept as a running (max, scaled sum) per thread and merged across the CTA.
+__global__ void __launch_bounds__(512) lm_logprob_kernel(const float* __restrict__ logits, int V, int r0,
+                                                         const int32_t* __restrict__ ids, int B, int T,
+                                                         float* __restrict__ out) {
+    const int gr = r0 + blockIdx.x;
+    if (gr > 0 && (gr - 1) % T == T - 1) return;
+    const float* x = logits + (size_t)blockIdx.x * V;
+    float mx = -INFINITY, sum = 0.f;
+    auto add = [&](float v) {
+        if (v > mx) {
+            sum = sum * expf(mx - v) + 1.f;
+            mx = v;
+        } else {
+            sum += expf(v - mx);
+        }
+    };
+    if ((V & 3) == 0) {
+        const float4* x4 = reinterpret_cast<const float4*>(x);
+        for (int i = threadIdx.x; i < V / 4; i += blockDim.x) {
+            const float4 v = x4[i];
+            add(v.x);
+            add(v.y);
+            add(v.z);
+            add(v.w);
+        }
+    } else {
+        for (int i = threadIdx.x; i < V; i += blockDim.x) add(x[i]);
+    }
+    auto merge = [](float& m1, float& s1, float m2, float s2) {
+        const float m = fmaxf(m1, m2);
+        if (m == -INFINITY) return;
+        s1 = (m1 == -INFINITY ? 0.f : s1 * expf(m1 - m)) + (m2 == -INFINITY ? 0.f : s2 * expf(m2 - m));
+        m1 = m;
+    };
+#pragma unroll
+    for (int o = 16; o; o >>= 1) merge(mx, sum, __shfl_xor_sync(0xffffffffu, mx, o), __shfl_xor_sync(0xffffffffu, sum, o));
+    __shared__ float sm[16], ss[16];
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    if (lane == 0) {
+        sm[wid] = mx;
+        ss[wid] = sum;
+    }
+    __syncthreads();
+    if (wid == 0) {
+        const int nw = blockDim.x >> 5;
+        mx = lane < nw ? sm[lane] : -INFINITY;
+        sum = lane < nw ? ss[lane] : 0.f;
+#pragma unroll
+        for (int o = 16; o; o >>= 1)
+            merge(mx, sum, __shfl_xor_sync(0xffffffffu, mx, o), __shfl_xor_sync(0xffffffffu, sum, o));
+        const float lse = mx + logf(sum);
+        if (gr == 0) {
+            for (int b = lane; b < B; b += 32) out[(size_t)b * T] = x[ids[(size_t)b * T]] - lse;
+        } else if (lane == 0) {
+            const int b = (gr - 1) / T, j = (gr - 1) % T;
+            out[(size_t)b * T + j + 1] = x[ids[(size_t)b * T + j + 1]] - lse;
+        }
+    }
+}
+
+constexpr int kLmRows = 256;  // logits rows per LM-head chunk
+
+int finish_call(db_model* m, db_error* err) {
+    int flag = 0;
+    cudaMemcpyAsync(&flag, m->flag, sizeof(int), cudaMemcpyDeviceToHost, m->stream);
+    const cudaError_t e = cudaStreamSynchronize(m->stream);
+    if (e != cudaSuccess) {
+        fill_error(err, "INFERENCE_FAILED", cudaGetErrorString(e));
         return -1;
     }
+    int word = 0;
+    cudaMemcpy(&word, m->dev_err, sizeof(int), cudaMemcpyDeviceToHost);
+    if (word) {
+        cudaMemset(m->dev_err, 0, sizeof(int));
+        fill_error(err, "INFERENCE_FAILED", "device wait expired (error word " + std::to_string(word) + ")");
+        return -1;
+    }
+    if (flag) {
+        fill_error(err, "INFERENCE_FAILED", "non-finite hidden state");
+        return -1;
+    }
+    return 0;
+}
+
+// The shared part of predict and score: checks the request (the reference's codes), runs or reuses
+// the prefix (kev/mod.rs:186-236: its per-layer keys and values go into the cache when its byte
+// budget holds them) and then all continuations in one batched pass after it.  On success m->normed
+// holds the count*tokens final-normed continuation states and *last the prefix's last one.
+int run_continuations(db_model* m, db_cache* cache, const int32_t* prefix, size_t prefix_len,
+                      const int32_t* continuations, size_t count, size_t tokens, int extra_rows,
+                      const volatile uint8_t* cancel, const float** last, db_error* err) {
     if (!m->cfg.causal) {
         fill_error(err, "UNSUPPORTED_CACHE", "continuations need a causal (decoder) model");
         return -1;
@@ -1370,7 +1470,10 @@ int db_predict_continuations(db_model* m, db_cache* cache, const int32_t* prefix
     }
     cudaSetDevice(m->device);
     const int P = (int)prefix_len, T = (int)tokens, B = (int)count, L = m->cfg.layers, Hk = m->cfg.kv_heads;
-    if (ensure_workspace(m, std::max(P, B * T)) || ensure_rope(m, P + T)) {
+    const int D = m->cfg.hidden;
+    if (ensure_workspace(m, std::max(P, B * T + extra_rows)) || ensure_rope(m, P + T) ||
+        (!m->prefix_last && m->alloc(&m->prefix_last, D, m->allocations) &&
+         db_fail(DB_ERR_CUDA, "RESOURCE_LIMIT", "prefix state exceeds device limits"))) {
         fill_error(err, "RESOURCE_LIMIT", db_last_error_message());
         return -1;
     }
@@ -1380,26 +1483,32 @@ int db_predict_continuations(db_model* m, db_cache* cache, const int32_t* prefix
         else fill_error(err, "INFERENCE_FAILED", db_last_error_message());
         return -1;
     };
-    // the prefix state: reused from the cache, or computed by a causal pass that stores every
-    // layer's keys and values (into the cache when its byte budget holds them, kev/mod.rs:186-236)
     const bool reuse = cache && cache->prefix_cache && (int)cache->ids.size() == P &&
-                       std::equal(prefix, prefix + P, cache->ids.begin()) && (int)cache->k.size() == L;
+                       std::equal(prefix, prefix + P, cache->ids.begin()) && (int)cache->k.size() == L &&
+                       cache->last;
     std::vector<__half*>* pk = &m->tmp_k;
     std::vector<__half*>* pv = &m->tmp_v;
     if (reuse) {
         pk = &cache->k;
         pv = &cache->v;
+        *last = cache->last;
         cache->hits += 1;
         cache->reused += P;
     } else {
-        const size_t state_bytes = (size_t)L * P * Hk * 128 * 2 * 2;
+        const size_t state_bytes = (size_t)L * P * Hk * 128 * 2 * 2 + (size_t)D * 4;
         const bool keep = cache && cache->prefix_cache && state_bytes <= cache->max_bytes;
         int rc = 0;
+        float* keep_last = m->prefix_last;
         if (keep) {
             cache->ids.clear();
             rc = ensure_kv(cache->k, cache->v, cache->cap_P, P, L, Hk);
+            if (!rc && !cache->last && cudaMalloc(&cache->last, (size_t)D * 4) != cudaSuccess) {
+                cache->last = nullptr;
+                rc = db_fail(DB_ERR_CUDA, "RESOURCE_LIMIT", "prefix state exceeds device limits");
+            }
             pk = &cache->k;
             pv = &cache->v;
+            keep_last = cache->last;
         } else {
             rc = ensure_kv(m->tmp_k, m->tmp_v, m->tmp_cap, P, L, Hk);
         }
@@ -1414,10 +1523,11 @@ int db_predict_continuations(db_model* m, db_cache* cache, const int32_t* prefix
         pass.pool = false;
         rc = enqueue_forward(m, P, cancel, &pass);
         if (rc) return failed(rc);
+        cudaMemcpyAsync(keep_last, m->normed + (size_t)(P - 1) * D, (size_t)D * 4, cudaMemcpyDeviceToDevice, m->stream);
+        *last = keep_last;
         if (cache && cache->prefix_cache) cache->computed += P;
         if (keep) cache->ids.assign(prefix, prefix + P);
     }
-    // all continuations in one batched pass after the prefix
     cudaMemcpyAsync(m->ids, continuations, (size_t)B * T * sizeof(int32_t), cudaMemcpyHostToDevice, m->stream);
     Pass pass;
     pass.items = B;
@@ -1425,29 +1535,113 @@ int db_predict_continuations(db_model* m, db_cache* cache, const int32_t* prefix
     pass.pk = pk->data();
     pass.pv = pv->data();
     pass.pool = false;
-    int rc = enqueue_forward(m, T, cancel, &pass);
+    const int rc = enqueue_forward(m, T, cancel, &pass);
     if (rc) return failed(rc);
-    int flag = 0;
-    cudaMemcpyAsync(&flag, m->flag, sizeof(int), cudaMemcpyDeviceToHost, m->stream);
-    cudaMemcpyAsync(hidden, m->normed, (size_t)B * T * m->cfg.hidden * sizeof(float), cudaMemcpyDeviceToHost,
-                    m->stream);
-    const cudaError_t e = cudaStreamSynchronize(m->stream);
-    if (e != cudaSuccess) {
-        fill_error(err, "INFERENCE_FAILED", cudaGetErrorString(e));
-        return -1;
-    }
-    int word = 0;
-    cudaMemcpy(&word, m->dev_err, sizeof(int), cudaMemcpyDeviceToHost);
-    if (word) {
-        cudaMemset(m->dev_err, 0, sizeof(int));
-        fill_error(err, "INFERENCE_FAILED", "device wait expired (error word " + std::to_string(word) + ")");
-        return -1;
-    }
-    if (flag) {
-        fill_error(err, "INFERENCE_FAILED", "non-finite hidden state");
-        return -1;
-    }
     return 0;
+}
+
+// The LM head over the rows [last; the B*T continuation states] (the tied embedding matrix, the
+// model's own quantised weights) and the log-probability of every continuation token
+// (logprobs [B*T], device), in chunks of kLmRows logits rows.  Rows are quantised like every
+// projection's input (g64, 8-bit codes).
+int enqueue_lm_logprobs(db_model* m, const float* last, int B, int T, float* logprobs) {
+    const auto& c = m->cfg;
+    const int D = c.hidden, V = c.vocab, R = 1 + B * T;
+    cudaStream_t st = m->stream;
+    if (R > m->lm_x_rows) {
+        m->lm_x_rows = 0;
+        if (m->lm_x) cudaFree(m->lm_x);
+        m->lm_x = nullptr;
+        if (cudaMalloc(&m->lm_x, (size_t)R * D * 4) != cudaSuccess) {
+            m->lm_x = nullptr;
+            return db_fail(DB_ERR_CUDA, "RESOURCE_LIMIT", "LM-head rows exceed device limits");
+        }
+        m->lm_x_rows = R;
+    }
+    if (!m->logits && m->alloc(&m->logits, (size_t)kLmRows * V, m->allocations))
+        return db_fail(DB_ERR_CUDA, "RESOURCE_LIMIT", "LM-head logits exceed device limits");
+    cudaMemcpyAsync(m->lm_x, last, (size_t)D * 4, cudaMemcpyDeviceToDevice, st);
+    cudaMemcpyAsync(m->lm_x + D, m->normed, (size_t)B * T * D * 4, cudaMemcpyDeviceToDevice, st);
+    const int64_t ld_codes = m->Kmax(), lds = db_scale_stride(m->cap_T);
+    const int layout = m->i8 ? DB_CODES_NATURAL_I8 : DB_CODES_TC_F16;
+    int rc = db_launch_quantize_rows(m->lm_x, DB_F32, D, R, D, 8, m->acodes, layout, ld_codes, m->sa, nullptr, lds,
+                                     m->flag, st);
+    const uint8_t* a8 = reinterpret_cast<const uint8_t*>(m->acodes);
+    const size_t code_bytes = m->i8 ? 1 : 2;
+    for (int r0 = 0; r0 < R && !rc; r0 += kLmRows) {
+        const int rows = std::min(kLmRows, R - r0);
+        DbGemmArgs g{};
+        g.a_codes = a8 + (size_t)r0 * ld_codes * code_bytes;
+        g.lda = ld_codes;
+        g.sa = m->sa + r0;
+        g.ldsa = lds;
+        g.w_codes = m->emb_c;
+        g.sw = m->emb_s;
+        g.M = rows;
+        g.N = V;
+        g.K = D;
+        g.bits = c.weight_bits;
+        g.fused = c.fused;
+        g.epilogue = DB_EPI_STORE;
+        g.y = m->logits;
+        g.ldy = V;
+        g.nonfinite = m->flag;
+        g.dev_error = m->dev_err;
+        if (m->i8) {
+            const db_gemm_config d = db_gemm_i8_default_config(rows, V, DB_EPI_STORE);
+            g.block_n = d.block_n;
+            g.pair_ctas = d.pair_ctas;
+            rc = db_launch_gemm_i8(g, st);
+        } else {
+            rc = db_launch_gemm_tc(g, st);
+        }
+        if (rc) break;
+        lm_logprob_kernel<<<rows, 512, 0, st>>>(m->logits, V, r0, m->ids, B, T, logprobs);
+        rc = (int)cudaGetLastError();
+    }
+    return rc ? db_cuda_status(rc, "LM head") : 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+int db_predict_continuations(db_model* m, db_cache* cache, const int32_t* prefix, size_t prefix_len,
+                             const int32_t* continuations, size_t count, size_t tokens,
+                             const volatile uint8_t* cancel, float* hidden, db_error* err) {
+    if (!m || !hidden || !prefix || !continuations) {
+        fill_error(err, "INVALID_PARAMETERS", "null model, ids or output");
+        return -1;
+    }
+    const float* last = nullptr;
+    if (run_continuations(m, cache, prefix, prefix_len, continuations, count, tokens, 0, cancel, &last, err))
+        return -1;
+    cudaMemcpyAsync(hidden, m->normed, count * tokens * m->cfg.hidden * sizeof(float), cudaMemcpyDeviceToHost,
+                    m->stream);
+    return finish_call(m, err);
+}
+
+int db_score_continuations(db_model* m, db_cache* cache, const int32_t* prefix, size_t prefix_len,
+                           const int32_t* continuations, size_t count, size_t tokens,
+                           const volatile uint8_t* cancel, float* logprobs, float* hidden, db_error* err) {
+    if (!m || !logprobs || !prefix || !continuations) {
+        fill_error(err, "INVALID_PARAMETERS", "null model, ids or output");
+        return -1;
+    }
+    const float* last = nullptr;
+    if (run_continuations(m, cache, prefix, prefix_len, continuations, count, tokens, 1, cancel, &last, err))
+        return -1;
+    const int D = m->cfg.hidden, BT = (int)(count * tokens);
+    // the log-probabilities land in the spare pooled buffer (cap_T * D floats >= B*T)
+    int rc = enqueue_lm_logprobs(m, last, (int)count, (int)tokens, m->pooled);
+    if (rc) {
+        cudaStreamSynchronize(m->stream);
+        fill_error(err, "INFERENCE_FAILED", db_last_error_message());
+        return -1;
+    }
+    cudaMemcpyAsync(logprobs, m->pooled, (size_t)BT * 4, cudaMemcpyDeviceToHost, m->stream);
+    if (hidden) cudaMemcpyAsync(hidden, m->lm_x, (size_t)(1 + BT) * D * 4, cudaMemcpyDeviceToHost, m->stream);
+    return finish_call(m, err);
 }
 
 int db_cache_stats(const db_cache* c, int64_t* hits, int64_t* reused_tokens, int64_t* computed_tokens) {

@@ -335,12 +335,22 @@ int db_bert_score(db_bert *m, const int32_t *state, size_t n_state, const int32_
  * max_bytes.  db_predict_continuations runs `count` continuations of `tokens` tokens each after
  * the prefix, batched in one pass (every continuation sees the prefix and, causally, its own
  * tokens; the prefix is computed once, or reused when the cache holds the same ids), and writes
- * the final-normed hidden states [count, tokens, hidden] (the Kev query/key heads on top of them
- * are not part of this library).  prefix_len + tokens must not exceed max_sequence_tokens
- * (INPUT_TOO_LONG).  cache may be NULL (nothing is kept). */
+ * the final-normed hidden states [count, tokens, hidden].  prefix_len + tokens must not exceed
+ * max_sequence_tokens (INPUT_TOO_LONG).  cache may be NULL (nothing is kept); a kept prefix also
+ * keeps its last final-normed state. */
 int db_predict_continuations(db_model *m, db_cache *cache, const int32_t *prefix, size_t prefix_len,
                              const int32_t *continuations, size_t count, size_t tokens,
                              const volatile uint8_t *cancel, float *hidden, db_error *err);
+/* Scores the continuations by log-probability: the same pass as db_predict_continuations, then an
+ * LM head tied to the embedding matrix (logits = the model's quantised embedding rows times the
+ * final-normed state, quantised to 8-bit g64 codes like every projection input) and a log-softmax
+ * over the vocabulary.  logprobs [count, tokens]: log p(token t of continuation b | prefix and
+ * tokens 0..t-1 of b); token 0 is predicted from the prefix's last state.  hidden, when non-null,
+ * receives the LM head's input rows [1 + count*tokens, hidden] (the prefix's last state, then the
+ * continuations' states).  Errors as db_predict_continuations. */
+int db_score_continuations(db_model *m, db_cache *cache, const int32_t *prefix, size_t prefix_len,
+                           const int32_t *continuations, size_t count, size_t tokens,
+                           const volatile uint8_t *cancel, float *logprobs, float *hidden, db_error *err);
 /* hits / prefix tokens reused / prefix tokens computed (kev/mod.rs Stats) */
 int db_cache_stats(const db_cache *c, int64_t *hits, int64_t *reused_tokens, int64_t *computed_tokens);
 

@@ -429,6 +429,30 @@ def set_threads(n: int) -> None:
     lib().oracle_set_threads(n)
 
 
+def lm_logprobs(embedding_bf16, hidden_rows, continuations, weight_bits=4, mode=0):
+    """Log-probabilities of continuation tokens from an LM head tied to the embedding matrix.  The
+    reference has no LM head for this path (its Kev/Jev score through small heads on the hidden
+    state); this is the scoring the C5 configuration names: logits = int8::Matrix(embedding)
+    applied to the final-normed rows (int8.rs:166-288 numerics, activation codes of 8 bits), then a
+    float64 log-softmax.  hidden_rows [1 + B*T, D]: the prefix's last state, then continuation b's
+    token j at row 1 + b*T + j; continuations [B, T] -> [B, T]."""
+    hidden_rows = np.ascontiguousarray(hidden_rows, dtype=np.float32)
+    D = hidden_rows.shape[1]
+    emb = np.ascontiguousarray(embedding_bf16, dtype=np.uint16).reshape(-1, D)
+    V = emb.shape[0]
+    conts = np.asarray(continuations)
+    B, T = conts.shape
+    logits = Matrix(emb.reshape(-1), D, V, weight_bits, 8).apply(hidden_rows, mode=mode).astype(np.float64)
+    mx = logits.max(axis=1, keepdims=True)
+    lse = (mx + np.log(np.exp(logits - mx).sum(axis=1, keepdims=True)))[:, 0]
+    out = np.empty((B, T), np.float64)
+    for b in range(B):
+        for t in range(T):
+            row = 0 if t == 0 else 1 + b * T + t - 1
+            out[b, t] = logits[row, conts[b, t]] - lse[row]
+    return out
+
+
 # ------------------------------------------------------------------ Decima int8 (decima/int8.rs)
 def decima_quantize_rows(x, block: int):
     """[rows, cols] f32 -> (codes int8 [rows, groups*block], scales f32 [rows, groups])."""

@@ -114,10 +114,20 @@ def test_c5_full_width_continuations_match_causal_oracle(db, oracle):
     got = model.predict_continuations(prefix, conts, cache=cache)
     again = model.predict_continuations(prefix, conts, cache=cache)  # prefix reused from the cache
     assert np.array_equal(again.view(np.uint32), got.view(np.uint32))
+    # scored by log-probability over the 151,936-token vocabulary (LM head tied to the embedding)
+    lp, rows = model.score_continuations(prefix, conts, cache=cache, hidden=True)
     model.close()
+    assert np.array_equal(rows[1:].view(np.uint32), got.reshape(-1, D).view(np.uint32))
+    want = oracle.lm_logprobs(w["embedding"], rows, conts, 4, mode=2)
+    assert np.abs(lp - want).max() <= 5e-5, np.abs(lp - want).max()
     ref = oracle.Encoder(dict(cfg, causal=1), w)
     for c in range(4):
         _, h = ref.forward(np.concatenate([prefix, conts[c]]), mode=2, hidden=True)
         per_token = [cosine(got[c, t], h[512 + t]) for t in range(32)]
         assert min(per_token) >= 0.999, (c, min(per_token))
         assert cosine(got[c].mean(0), h[512:].mean(0)) >= 0.9999
+        if c == 0:
+            e2e = oracle.lm_logprobs(w["embedding"], np.concatenate([h[511:512], h[512:544]]), conts[:1], 4,
+                                     mode=2)[0]
+            err = np.abs(lp[0] - e2e)
+            assert err.max() <= 0.1 and err.mean() <= 0.03, (err.max(), err.mean())

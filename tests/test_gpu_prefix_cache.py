@@ -101,3 +101,59 @@ def test_prefix_cache_contract(db, oracle):
     model.close()
     other.close()
     enc.close()
+
+
+def lm_rows(h, prefix_len, tokens):
+    """The LM head's input rows for one continuation from a causal pass's final states h."""
+    return np.concatenate([h[prefix_len - 1:prefix_len], h[prefix_len:prefix_len + tokens]])
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("prefix_len,tokens,count", [(50, 9, 3), (1, 1, 1), (200, 33, 2)])
+def test_scored_continuations(db, oracle, bits, prefix_len, tokens, count):
+    """Log-probability scoring: the LM head (tied embedding, W*A8 g64) and the f32 log-softmax on
+    the GPU's own rows agree with the oracle's f64 log-softmax over the oracle GEMM's logits to
+    2e-5; end to end against the causal oracle, per-token log-probs agree to 0.1 (mean 0.03: the
+    states carry the f16 attention's noise, cosine >= 0.999 per token)."""
+    cfg, model, ref = decoder(db, oracle, bits)
+    w = random_weights(oracle, cfg, seed=5)
+    rng = np.random.default_rng(prefix_len + 11 * tokens)
+    prefix = rng.integers(0, cfg["vocab"], prefix_len).astype(np.int32)
+    conts = rng.integers(0, cfg["vocab"], (count, tokens)).astype(np.int32)
+    cache = model.create_cache(db.CacheOptions(max_bytes=64 << 20, require_prefix=True))
+    lp, rows = model.score_continuations(prefix, conts, cache=cache, hidden=True)
+    assert lp.shape == (count, tokens) and rows.shape == (1 + count * tokens, cfg["hidden"])
+    assert np.all(lp < 0)
+    want = oracle.lm_logprobs(w["embedding"], rows, conts, bits)
+    assert np.abs(lp - want).max() <= 2e-5, np.abs(lp - want).max()
+    # the rows after the first are the continuation states predict_continuations returns
+    states = model.predict_continuations(prefix, conts, cache=cache)
+    assert np.array_equal(rows[1:].view(np.uint32), states.reshape(-1, cfg["hidden"]).view(np.uint32))
+    for c in range(count):
+        _, h = ref.forward(np.concatenate([prefix, conts[c]]), mode=2, hidden=True)
+        e2e = oracle.lm_logprobs(w["embedding"], lm_rows(h, prefix_len, tokens), conts[c:c + 1], bits)[0]
+        err = np.abs(lp[c] - e2e)
+        assert err.max() <= 0.1 and err.mean() <= 0.03, (c, err.max(), err.mean())
+    # a reused prefix (its last state kept with its keys and values) and no cache give the same bits
+    again = model.score_continuations(prefix, conts, cache=cache)
+    assert np.array_equal(again.view(np.uint32), lp.view(np.uint32))
+    st = cache.stats()
+    assert st["hits"] == 2 and st["prefix_tokens_computed"] == prefix_len
+    alone = model.score_continuations(prefix, conts[-1:])
+    assert np.array_equal(alone[0].view(np.uint32), lp[-1].view(np.uint32))
+    model.close()
+
+
+def test_scoring_rejects_bad_requests(db, oracle):
+    cfg, model, _ = decoder(db, oracle, 4)
+    with pytest.raises(db.Error) as e:
+        model.score_continuations([1, 2], np.zeros((2, 0), np.int32))
+    assert e.value.code == "INVALID_REQUEST"
+    with pytest.raises(db.Error) as e:
+        model.score_continuations(np.arange(500) % 1000, np.zeros((1, 13), np.int32))
+    assert e.value.code == "INPUT_TOO_LONG"
+    with pytest.raises(db.Error) as e:
+        model.score_continuations([1, 2], [[3, 1000]])
+    assert e.value.code == "INVALID_REQUEST"
+    assert model.score_continuations([1, 2], [[3, 4]]).shape == (1, 2)
+    model.close()
