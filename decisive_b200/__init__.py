@@ -234,6 +234,21 @@ def attention(q16, k16, v16, q_heads: int, kv_heads: int, scale: float | None = 
     return out
 
 
+def attention_decoder(q16, k16, v16, items: int, q_heads: int, kv_heads: int, kp16=None, vp16=None,
+                      causal: bool = True, scale: float | None = None):
+    """Decoder attention: `items` items of q16.shape[0] // items rows, each after the cached prefix
+    keys kp16/vp16 [P, kv_heads, 128] (None: no prefix), causal own keys when asked."""
+    import torch
+    R = q16.shape[0]
+    out = torch.empty((R, q_heads * 128), dtype=torch.float32, device=q16.device)
+    s = (1.0 / 128 ** 0.5) if scale is None else scale
+    P = 0 if kp16 is None else kp16.shape[0]
+    check(load().db_attention_decoder(_ptr(q16), _ptr(k16), _ptr(v16), items, R // items,
+                                      _ptr(kp16) if P else None, _ptr(vp16) if P else None, P, int(causal), q_heads,
+                                      kv_heads, 128, s, _ptr(out), q_heads * 128, _stream()))
+    return out
+
+
 def synthetic_bf16(seed: int, tensor: int, shape, std: float, device="cuda"):
     import torch
     out = torch.empty(shape, dtype=torch.int16, device=device)

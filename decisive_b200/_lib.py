@@ -79,6 +79,8 @@ SIGNATURES = [
     ("db_mlp_g64_natural", _i32, [_vp, _i64, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _i32, _i32, _vp, _i64, _vp, _i64, _vp, _vp]),
     ("db_interleave_gate_up", _i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i32, _vp, _vp, _vp]),
     ("db_attention", _i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _f, _vp, _i64, _vp]),
+    ("db_attention_decoder", _i32, [_vp, _vp, _vp, _i64, _i64, _vp, _vp, _i64, C.c_int, _i64, _i64, _i64, _f, _vp,
+                                    _i64, _vp]),
     ("db_synthetic_bf16", _i32, [C.c_uint64, C.c_uint64, _i64, _f, _vp, _vp]),
     ("db_model_create", _vp, [_i32, C.POINTER(EncoderConfig), C.POINTER(EncoderWeights), C.POINTER(DbError)]),
     ("db_model_create_synthetic", _vp, [_i32, C.POINTER(EncoderConfig), C.c_uint64, _f, C.POINTER(DbError)]),

@@ -1,8 +1,15 @@
 // Non-causal GQA attention on the 5th-generation tensor cores (tcgen05 MMAs into tensor memory,
 // TMA tile loads), head_dim 128, f16 operands with f32 accumulation.  Same mathematics as the
 // reference's attention core (scale * q.k, a softmax over the keys, then P.v per head in f32:
-// backbone.rs:560-600); this kernel serves the non-causal calls without cached prefix keys (the
-// encoder forward), attention.cu the causal and prefix forms.
+// backbone.rs:560-600).  It serves every attention call: the encoder's (items of T rows, or ragged
+// sequences packed one after another, each attending to its own keys) and the decoder's (causal
+// own keys after P cached prefix keys, kev/mod.rs:163-300).
+//
+// Decoder mode: a CTA's keys are the P prefix keys (shared by every item; their own tensor maps)
+// followed by its item's own keys, causal ones only up to its query tile's diagonal; keys past the
+// prefix, past the item or (causal) past the query row score -inf.  Every CTA computes one item's
+// query tile against that item's keys alone, so a result does not depend on the other items of
+// the batch.
 //
 // One CTA = 128 queries of one query head (one query per TMEM lane); keys in tiles of 128, one
 // pass.  Key tiles alternate between two S buffers, two O accumulators and two softmax warpgroups
@@ -159,13 +166,20 @@ __device__ __forceinline__ bool warp_wait_at(uint64_t* bar, uint32_t parity, vol
     return ok != 0;
 }
 
+// Decoder-mode parameters: P prefix keys (maps tmKp/tmVp) before the item's own keys, causal.
+struct DecoderArgs {
+    int dec, P, causal;
+};
+
 template <bool QUANT>
 __global__ void __launch_bounds__(AT_THREADS, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                        const __grid_constant__ CUtensorMap tmV, int T, int Hq, int Hk, float scale_log2,
+                        const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmKp,
+                        const __grid_constant__ CUtensorMap tmVp, int T, int Hq, int Hk, float scale_log2,
                         float* __restrict__ out, int64_t ldo, void* __restrict__ codes, int64_t ldc,
                         float* __restrict__ scales, int64_t lds, int* __restrict__ nonfinite,
-                        int* __restrict__ dev_error, int codes_i8, const int* __restrict__ cu_seqlens) {
+                        int* __restrict__ dev_error, int codes_i8, const int* __restrict__ cu_seqlens,
+                        const DecoderArgs da) {
     pdl_wait();
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -187,8 +201,15 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         item = 0;
         if (q0 >= T) return;
     }
-    const int nt = (T + AT_KT - 1) / AT_KT;  // key tiles
-    const int np = (nt + 1) / 2;             // pairs of tiles (even, odd)
+    // key tiles: npre prefix tiles (decoder mode), then nown tiles of the item's own keys (causal:
+    // up to the tile holding this query tile's diagonal; AT_Q == AT_KT)
+    int npre = 0, nown = (T + AT_KT - 1) / AT_KT;
+    if (da.dec) {
+        npre = (da.P + AT_KT - 1) / AT_KT;
+        if (da.causal) nown = min(nown, q0 / AT_KT + 1);
+    }
+    const int nt = npre + nown;  // key tiles
+    const int np = (nt + 1) / 2; // pairs of tiles (even, odd)
     const uint32_t sQ = smem_u32(smem + OFF_Q), sP = smem_u32(smem + OFF_P), sKV = smem_u32(smem + OFF_KV);
 
     if (threadIdx.x == 0) {
@@ -214,6 +235,10 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         tma_prefetch_desc(&tmQ);
         tma_prefetch_desc(&tmK);
         tma_prefetch_desc(&tmV);
+        if (npre) {
+            tma_prefetch_desc(&tmKp);
+            tma_prefetch_desc(&tmVp);
+        }
     }
     if (warp == 1) {
         tmem_alloc(tmem_slot, 512);
@@ -231,14 +256,17 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
             int st = 0, issued = 0;
             uint32_t ph = 0;
             bool ok = true;
-            auto load = [&](const CUtensorMap* map, int tile) -> bool {
+            auto load = [&](bool is_v, int tile) -> bool {
                 if (!warp_wait_at(&bars[BAR_KV_EMPTY + st], ph ^ 1u, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_TMA))
                     return false;
                 if (lane == 0) {
+                    const bool pre = tile < npre;
+                    const CUtensorMap* map = pre ? (is_v ? &tmVp : &tmKp) : (is_v ? &tmV : &tmK);
+                    const int y = pre ? tile * AT_KT : row0 + (tile - npre) * AT_KT, z = pre ? 0 : item;
                     const uint32_t dst = sKV + (uint32_t)(st * AT_TILE);
                     mbar_arrive_expect_tx(&bars[BAR_KV_FULL + st], AT_TILE);
-                    tma_load_4d(dst, map, &bars[BAR_KV_FULL + st], 0, kh, row0 + tile * AT_KT, item);
-                    tma_load_4d(dst + AT_HALF, map, &bars[BAR_KV_FULL + st], 64, kh, row0 + tile * AT_KT, item);
+                    tma_load_4d(dst, map, &bars[BAR_KV_FULL + st], 0, kh, y, z);
+                    tma_load_4d(dst + AT_HALF, map, &bars[BAR_KV_FULL + st], 64, kh, y, z);
                 }
                 __syncwarp();
                 ++issued;
@@ -256,9 +284,9 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
             __syncwarp();
             for (int p = 0; p <= np && ok; ++p) {
                 if (p < np)
-                    for (int j = 2 * p; j < min(2 * p + 2, nt) && ok; ++j) ok = load(&tmK, j);
+                    for (int j = 2 * p; j < min(2 * p + 2, nt) && ok; ++j) ok = load(false, j);
                 if (p > 0)
-                    for (int j = 2 * p - 2; j < min(2 * p, nt) && ok; ++j) ok = load(&tmV, j);
+                    for (int j = 2 * p - 2; j < min(2 * p, nt) && ok; ++j) ok = load(true, j);
             }
             if (!ok && lane == 0) {
                 // after an abort: let the copies this warp issued land before the CTA winds down
@@ -385,6 +413,8 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         float m = -INFINITY, l = 0.f;  // running maximum (scaled, log2 domain) and row sum
         bool ok = true;
         uint32_t r[4][32];
+        // own keys this row may see: [0, own_end) of the item
+        const int own_end = da.dec && da.causal ? min(T, q0 + row + 1) : T;
         for (int p = 0; p < np && ok; ++p) {
             const int j = 2 * p + b;
             if (j >= nt) break;
@@ -402,22 +432,22 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(&bars[BAR_S_EMPTY + b]);
             ++su;
-            // keys past the sequence end (only in a ragged last tile) score -inf: 2^(-inf) = 0
-            const int kv0 = j * AT_KT;
-            if (kv0 + AT_KT > T) {
-                const int lim = T - kv0;
+            // keys past the prefix, past the sequence end or (causal) past the query row score
+            // -inf: 2^(-inf) = 0.  Every tile keeps at least its first key for every row.
+            const int hi_c = j < npre ? da.P - j * AT_KT : own_end - (j - npre) * AT_KT;
+            if (__any_sync(0xffffffffu, hi_c < AT_KT)) {
 #pragma unroll
                 for (int c = 0; c < 4; ++c)
 #pragma unroll
                     for (int i = 0; i < 32; ++i)
-                        if (32 * c + i >= lim) r[c][i] = __float_as_uint(-INFINITY);
+                        if (32 * c + i >= hi_c) r[c][i] = __float_as_uint(-INFINITY);
             }
             float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // four independent chains
 #pragma unroll
             for (int c = 0; c < 4; ++c)
 #pragma unroll
                 for (int i = 0; i < 32; ++i) mx[i & 3] = fmaxf(mx[i & 3], __uint_as_float(r[c][i]));
-            const float mt = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * scale_log2;  // key kv0 < T
+            const float mt = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * scale_log2;  // a key is kept
             float factor = 1.f;
             if (p == 0) {
                 m = mt;
@@ -484,7 +514,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         }
         if (ok) {
             const float m_even = xm[row], m_odd = xm[AT_Q + row];
-            const float mm = fmaxf(m_even, m_odd);  // finite: the even tiles include key 0
+            const float mm = fmaxf(m_even, m_odd);  // finite: every tile keeps a key
             const float f_even = ex2(m_even - mm);
             const float f_odd = nt > 1 ? ex2(m_odd - mm) : 0.f;
             const float inv = 1.f / (xm[2 * AT_Q + row] * f_even + xm[3 * AT_Q + row] * f_odd);
@@ -594,39 +624,59 @@ int make_head_map(DbEncodeTiledFn enc, CUtensorMap* map, const __half* base, int
 
 using namespace db;
 
-// q16 [B*T, Hq, 128], k16/v16 [B*T, Hk, 128] (f16, 16-byte aligned); either out (f32, row stride
-// ldo) or codes/scales/nonfinite (quantised for the output projection) receives the context.
-int db_launch_attention_tc(const __half* q16, const __half* k16, const __half* v16, int B, int T, int Hq, int Hk,
-                           float scale, float* out, int64_t ldo, void* codes, int64_t ldc, float* scales,
-                           int64_t lds, int* nonfinite, cudaStream_t stream, int codes_i8) {
-    if (T <= 0 || B <= 0) return 0;
+namespace {
+
+// Output checks shared by the launchers: either out (f32, row stride ldo) or codes/scales/nonfinite
+// (the context quantised for the output projection).
+int check_io(const __half* q16, const __half* k16, const __half* v16, int Hq, int Hk, float* out, int64_t ldo,
+             void* codes, int64_t ldc, float* scales, int* nonfinite, int codes_i8) {
     const bool quant = codes != nullptr;
-    if (Hk <= 0 || Hq % Hk || Hq > 65535 || B > 65535 ||
-        (quant && (!scales || !nonfinite || (ldc & (codes_i8 ? 15 : 7)))) ||
+    if (Hk <= 0 || Hq % Hk || Hq > 65535 || (quant && (!scales || !nonfinite || (ldc & (codes_i8 ? 15 : 7)))) ||
         (!quant && (!out || (ldo & 3))))
         return (int)cudaErrorInvalidValue;
     if ((reinterpret_cast<uintptr_t>(q16) | reinterpret_cast<uintptr_t>(k16) | reinterpret_cast<uintptr_t>(v16)) & 15)
         return (int)cudaErrorMisalignedAddress;
     if (!quant && (reinterpret_cast<uintptr_t>(out) & 15)) return (int)cudaErrorMisalignedAddress;
     if (quant && (reinterpret_cast<uintptr_t>(codes) & 15)) return (int)cudaErrorMisalignedAddress;
+    return 0;
+}
+
+int launch(const dim3& grid, const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUtensorMap& tmV,
+           const CUtensorMap& tmKp, const CUtensorMap& tmVp, int T, int Hq, int Hk, float scale, float* out,
+           int64_t ldo, void* codes, int64_t ldc, float* scales, int64_t lds, int* nonfinite, int codes_i8,
+           const int* cu_seqlens, const DecoderArgs& da, cudaStream_t stream) {
+    int* err = db_device_error_ptr();
+    if (!err) return (int)cudaErrorMemoryAllocation;
+    auto kernel = codes ? attention_tc_kernel<true> : attention_tc_kernel<false>;
+    {
+        const cudaError_t e = db_set_max_smem(reinterpret_cast<const void*>(kernel), AT_SMEM);
+        if (e != cudaSuccess) return (int)e;
+    }
+    const cudaError_t e = db_launch_pdl(kernel, grid, dim3(AT_THREADS), AT_SMEM, stream, tmQ, tmK, tmV, tmKp, tmVp, T,
+                                        Hq, Hk, scale * 1.4426950408889634f, out, ldo, codes, ldc, scales, lds,
+                                        nonfinite, err, codes_i8, cu_seqlens, da);
+    return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
+}
+
+}  // namespace
+
+// q16 [B*T, Hq, 128], k16/v16 [B*T, Hk, 128] (f16, 16-byte aligned); either out (f32, row stride
+// ldo) or codes/scales/nonfinite (quantised for the output projection) receives the context.
+int db_launch_attention_tc(const __half* q16, const __half* k16, const __half* v16, int B, int T, int Hq, int Hk,
+                           float scale, float* out, int64_t ldo, void* codes, int64_t ldc, float* scales,
+                           int64_t lds, int* nonfinite, cudaStream_t stream, int codes_i8) {
+    if (T <= 0 || B <= 0) return 0;
+    if (B > 65535) return (int)cudaErrorInvalidValue;
+    if (const int rc = check_io(q16, k16, v16, Hq, Hk, out, ldo, codes, ldc, scales, nonfinite, codes_i8)) return rc;
     DbEncodeTiledFn enc = db_encode_tiled();
     if (!enc) return (int)cudaErrorNotSupported;
     CUtensorMap tmQ, tmK, tmV;
     if (make_head_map(enc, &tmQ, q16, Hq, T, B) || make_head_map(enc, &tmK, k16, Hk, T, B) ||
         make_head_map(enc, &tmV, v16, Hk, T, B))
         return (int)cudaErrorInvalidValue;
-    int* err = db_device_error_ptr();
-    if (!err) return (int)cudaErrorMemoryAllocation;
-    auto kernel = quant ? attention_tc_kernel<true> : attention_tc_kernel<false>;
-    {
-        const cudaError_t e = db_set_max_smem(reinterpret_cast<const void*>(kernel), AT_SMEM);
-        if (e != cudaSuccess) return (int)e;
-    }
     const dim3 grid((unsigned)((T + AT_Q - 1) / AT_Q), (unsigned)Hq, (unsigned)B);
-    const cudaError_t e = db_launch_pdl(kernel, grid, dim3(AT_THREADS), AT_SMEM, stream, tmQ, tmK, tmV, T, Hq, Hk,
-                                        scale * 1.4426950408889634f, out, ldo, codes, ldc, scales, lds, nonfinite, err,
-                                        codes_i8, static_cast<const int*>(nullptr));
-    return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
+    return launch(grid, tmQ, tmK, tmV, tmK, tmV, T, Hq, Hk, scale, out, ldo, codes, ldc, scales, lds, nonfinite,
+                  codes_i8, nullptr, DecoderArgs{0, 0, 0}, stream);
 }
 
 // Ragged items packed one after another: R rows in total, sequence i holds rows
@@ -638,30 +688,66 @@ int db_launch_attention_varlen(const __half* q16, const __half* k16, const __hal
                                void* codes, int64_t ldc, float* scales, int64_t lds, int* nonfinite,
                                cudaStream_t stream, int codes_i8) {
     if (nseq <= 0 || R <= 0 || max_len <= 0) return 0;
-    const bool quant = codes != nullptr;
-    if (!cu_seqlens || Hk <= 0 || Hq % Hk || Hq > 65535 || nseq > 65535 ||
-        (quant && (!scales || !nonfinite || (ldc & (codes_i8 ? 15 : 7)))) || (!quant && (!out || (ldo & 3))))
-        return (int)cudaErrorInvalidValue;
-    if ((reinterpret_cast<uintptr_t>(q16) | reinterpret_cast<uintptr_t>(k16) | reinterpret_cast<uintptr_t>(v16)) & 15)
-        return (int)cudaErrorMisalignedAddress;
-    if (!quant && (reinterpret_cast<uintptr_t>(out) & 15)) return (int)cudaErrorMisalignedAddress;
-    if (quant && (reinterpret_cast<uintptr_t>(codes) & 15)) return (int)cudaErrorMisalignedAddress;
+    if (!cu_seqlens || nseq > 65535) return (int)cudaErrorInvalidValue;
+    if (const int rc = check_io(q16, k16, v16, Hq, Hk, out, ldo, codes, ldc, scales, nonfinite, codes_i8)) return rc;
     DbEncodeTiledFn enc = db_encode_tiled();
     if (!enc) return (int)cudaErrorNotSupported;
     CUtensorMap tmQ, tmK, tmV;
     if (make_head_map(enc, &tmQ, q16, Hq, R, 1) || make_head_map(enc, &tmK, k16, Hk, R, 1) ||
         make_head_map(enc, &tmV, v16, Hk, R, 1))
         return (int)cudaErrorInvalidValue;
-    int* err = db_device_error_ptr();
-    if (!err) return (int)cudaErrorMemoryAllocation;
-    auto kernel = quant ? attention_tc_kernel<true> : attention_tc_kernel<false>;
-    {
-        const cudaError_t e = db_set_max_smem(reinterpret_cast<const void*>(kernel), AT_SMEM);
-        if (e != cudaSuccess) return (int)e;
-    }
     const dim3 grid((unsigned)((max_len + AT_Q - 1) / AT_Q), (unsigned)Hq, (unsigned)nseq);
-    const cudaError_t e = db_launch_pdl(kernel, grid, dim3(AT_THREADS), AT_SMEM, stream, tmQ, tmK, tmV, max_len, Hq,
-                                        Hk, scale * 1.4426950408889634f, out, ldo, codes, ldc, scales, lds, nonfinite,
-                                        err, codes_i8, cu_seqlens);
-    return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
+    return launch(grid, tmQ, tmK, tmV, tmK, tmV, max_len, Hq, Hk, scale, out, ldo, codes, ldc, scales, lds, nonfinite,
+                  codes_i8, cu_seqlens, DecoderArgs{0, 0, 0}, stream);
+}
+
+// The decoder form: B items of T rows each (q16/k16/v16 and the outputs hold the items one after
+// another); every item's keys are the P cached prefix keys kp/vp [P, Hk, 128] (shared by the items;
+// P = 0: none) followed by its own T keys, which are causal (row i sees own keys 0..i) when
+// causal != 0.
+int db_launch_attention_decoder(const __half* q16, const __half* k16, const __half* v16, int B, int T,
+                                const __half* kp, const __half* vp, int P, int causal, int Hq, int Hk, float scale,
+                                float* out, int64_t ldo, void* codes, int64_t ldc, float* scales, int64_t lds,
+                                int* nonfinite, cudaStream_t stream, int codes_i8) {
+    if (T <= 0 || B <= 0) return 0;
+    if (P < 0 || (P > 0 && (!kp || !vp)) || B > 65535) return (int)cudaErrorInvalidValue;
+    if (const int rc = check_io(q16, k16, v16, Hq, Hk, out, ldo, codes, ldc, scales, nonfinite, codes_i8)) return rc;
+    if (P > 0 && ((reinterpret_cast<uintptr_t>(kp) | reinterpret_cast<uintptr_t>(vp)) & 15))
+        return (int)cudaErrorMisalignedAddress;
+    DbEncodeTiledFn enc = db_encode_tiled();
+    if (!enc) return (int)cudaErrorNotSupported;
+    CUtensorMap tmQ, tmK, tmV, tmKp, tmVp;
+    if (make_head_map(enc, &tmQ, q16, Hq, T, B) || make_head_map(enc, &tmK, k16, Hk, T, B) ||
+        make_head_map(enc, &tmV, v16, Hk, T, B))
+        return (int)cudaErrorInvalidValue;
+    tmKp = tmK;  // no prefix: the maps are never read
+    tmVp = tmV;
+    if (P > 0 && (make_head_map(enc, &tmKp, kp, Hk, P, 1) || make_head_map(enc, &tmVp, vp, Hk, P, 1)))
+        return (int)cudaErrorInvalidValue;
+    const dim3 grid((unsigned)((T + AT_Q - 1) / AT_Q), (unsigned)Hq, (unsigned)B);
+    return launch(grid, tmQ, tmK, tmV, tmKp, tmVp, T, Hq, Hk, scale, out, ldo, codes, ldc, scales, lds, nonfinite,
+                  codes_i8, nullptr, DecoderArgs{1, P, causal ? 1 : 0}, stream);
+}
+
+int db_launch_attention(const __half* q16, const __half* k16, const __half* v16, int T, int Hq, int Hk, float scale,
+                        float* out, int64_t ldo, cudaStream_t stream) {
+    return db_launch_attention_tc(q16, k16, v16, 1, T, Hq, Hk, scale, out, ldo, nullptr, 0, nullptr, 0, nullptr,
+                                  stream);
+}
+
+int db_launch_attention_quant(const __half* q16, const __half* k16, const __half* v16, int T, int Hq, int Hk,
+                              float scale, void* codes, int64_t ldc, float* scales, int64_t lds, int* nonfinite,
+                              cudaStream_t stream, int codes_i8) {
+    if (!codes) return (int)cudaErrorInvalidValue;
+    return db_launch_attention_tc(q16, k16, v16, 1, T, Hq, Hk, scale, nullptr, 0, codes, ldc, scales, lds, nonfinite,
+                                  stream, codes_i8);
+}
+
+int db_launch_attention_prefix_quant(const __half* q16, const __half* k16, const __half* v16, int B, int T,
+                                     const __half* kp, const __half* vp, int P, int causal, int Hq, int Hk,
+                                     float scale, void* codes, int64_t ldc, float* scales, int64_t lds,
+                                     int* nonfinite, cudaStream_t stream, int codes_i8) {
+    if (!codes) return (int)cudaErrorInvalidValue;
+    return db_launch_attention_decoder(q16, k16, v16, B, T, kp, vp, P, causal, Hq, Hk, scale, nullptr, 0, codes, ldc,
+                                       scales, lds, nonfinite, stream, codes_i8);
 }

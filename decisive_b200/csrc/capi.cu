@@ -495,6 +495,21 @@ int db_attention(const void* q16, const void* k16, const void* v16, int64_t T, i
                           "attention");
 }
 
+int db_attention_decoder(const void* q16, const void* k16, const void* v16, int64_t B, int64_t T, const void* kp,
+                         const void* vp, int64_t P, int causal, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
+                         float scale, float* out, int64_t ldo, void* stream) {
+    if (head_dim != 128 || B < 0 || T < 0 || P < 0 || B > 65535 || T > (1 << 30) || P > (1 << 30) || kv_heads <= 0 ||
+        q_heads % kv_heads || ldo < q_heads * head_dim || (P > 0 && (!kp || !vp)))
+        return db_fail(DB_ERR_UNSUPPORTED, "UNSUPPORTED",
+                       "attention: head_dim 128, Hq % Hk == 0 and prefix keys for P > 0 required");
+    return db_cuda_status(db_launch_attention_decoder(static_cast<const __half*>(q16), static_cast<const __half*>(k16),
+                                                      static_cast<const __half*>(v16), (int)B, (int)T,
+                                                      static_cast<const __half*>(kp), static_cast<const __half*>(vp),
+                                                      (int)P, causal, (int)q_heads, (int)kv_heads, scale, out, ldo,
+                                                      nullptr, 0, nullptr, 0, nullptr, S(stream)),
+                          "attention");
+}
+
 int db_synthetic_bf16(uint64_t seed, uint64_t tensor, int64_t n, float stdv, uint16_t* out, void* stream) {
     if (n < 0 || !out) return db_fail(DB_ERR_INVALID_ARGUMENT, "INVALID_ARGUMENT", "synthetic: bad size");
     if (n == 0) return DB_OK;

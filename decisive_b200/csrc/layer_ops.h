@@ -43,10 +43,15 @@ int db_launch_attention_varlen(const __half* q16, const __half* k16, const __hal
                                int nseq, int max_len, int R, int Hq, int Hk, float scale, float* out, int64_t ldo,
                                void* codes, int64_t ldc, float* scales, int64_t lds, int* nonfinite,
                                cudaStream_t stream, int codes_i8 = 0);
-// Decoder form of the quantising attention: B items of T rows each (q16/k16/v16 and the outputs
-// hold the items one after another); every item's keys are the P cached prefix keys kp/vp
-// [P, Hk, 128] (shared by the items; P = 0: none) followed by its own T keys, which are causal
-// (row i sees own keys 0..i) when causal != 0.
+// Decoder form of the attention (tcgen05, one item's query tile per CTA): B items of T
+// rows each (q16/k16/v16 and the outputs hold the items one after another); every item's keys are
+// the P cached prefix keys kp/vp [P, Hk, 128] (shared by the items; P = 0: none) followed by its
+// own T keys, which are causal (row i sees own keys 0..i) when causal != 0.  Outputs as
+// db_launch_attention_tc; db_launch_attention_prefix_quant is its quantising form.
+int db_launch_attention_decoder(const __half* q16, const __half* k16, const __half* v16, int B, int T,
+                                const __half* kp, const __half* vp, int P, int causal, int Hq, int Hk, float scale,
+                                float* out, int64_t ldo, void* codes, int64_t ldc, float* scales, int64_t lds,
+                                int* nonfinite, cudaStream_t stream, int codes_i8 = 0);
 int db_launch_attention_prefix_quant(const __half* q16, const __half* k16, const __half* v16, int B, int T,
                                      const __half* kp, const __half* vp, int P, int causal, int Hq, int Hk,
                                      float scale, void* codes, int64_t ldc, float* scales, int64_t lds,

@@ -228,6 +228,14 @@ int db_interleave_gate_up(const uint8_t *gate_codes, const float *gate_scales, c
  * k/v f16 [T, Hk, 128], out f32 [T, Hq*128] (row stride ldo); scale multiplies q.k. */
 int db_attention(const void *q16, const void *k16, const void *v16, int64_t T, int64_t q_heads, int64_t kv_heads,
                  int64_t head_dim, float scale, float *out, int64_t ldo, void *stream);
+/* The decoder form (kev/mod.rs:163-300 continuation from a cached prefix): B items of T rows one
+ * after another (q f16 [B*T, Hq, 128], k/v f16 [B*T, Hk, 128]); each item attends to the P cached
+ * prefix keys kp/vp f16 [P, Hk, 128] (shared; P = 0: none, kp/vp may be NULL) and then to its own
+ * keys, causally (row i of an item sees its own keys 0..i) when causal != 0.  out f32
+ * [B*T, Hq*128] (row stride ldo). */
+int db_attention_decoder(const void *q16, const void *k16, const void *v16, int64_t B, int64_t T, const void *kp,
+                         const void *vp, int64_t P, int causal, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
+                         float scale, float *out, int64_t ldo, void *stream);
 
 /* Deterministic synthetic bf16 tensor on the device: value_i = std * N(0,1) from a
  * counter-based generator keyed by (seed, tensor). */

@@ -354,3 +354,50 @@ def test_attention_matches_oracle(db, oracle, t, hq, hk, scale):
     r = ref.reshape(-1)
     # f16 probabilities (11-bit mantissa) into an f32 accumulator: error ~1e-3 of the output RMS
     assert np.max(np.abs(o - r)) <= 5e-3 * np.sqrt(np.mean(r ** 2)) + 1e-6
+
+
+def decoder_attention_ref(q, k, v, kp, vp, items, hq, hk, causal, scale):
+    """float64 restatement: each item's rows see the prefix keys, then their own keys (causal: up
+    to themselves); scale * q.k, softmax, P.v per head."""
+    R = q.shape[0]
+    T = R // items
+    out = np.zeros((R, hq * 128))
+    for b in range(items):
+        rows = slice(b * T, (b + 1) * T)
+        for h in range(hq):
+            kh = h // (hq // hk)
+            keys = np.concatenate([kp[:, kh], k[rows, kh]]) if kp is not None else k[rows, kh]
+            vals = np.concatenate([vp[:, kh], v[rows, kh]]) if vp is not None else v[rows, kh]
+            s = q[rows, h] @ keys.T * scale
+            if causal:
+                P = keys.shape[0] - T  # own key j sits at column P + j
+                s[(np.arange(keys.shape[0])[None, :] - P) > np.arange(T)[:, None]] = -np.inf
+            s -= s.max(axis=1, keepdims=True)
+            p = np.exp(s)
+            out[rows, h * 128:(h + 1) * 128] = (p / p.sum(axis=1, keepdims=True)) @ vals
+    return out
+
+
+# (items, T, P, causal, Hq, Hk, scale): C5-shaped continuations (4 x 32 after 512), the prefix pass
+# (causal, no prefix, many tiles), ragged prefixes and items, single-token decode steps, GQA 1/2/4.
+@pytest.mark.parametrize("items,t,p,causal,hq,hk,scale", [
+    (4, 32, 512, 1, 8, 2, None), (1, 300, 0, 1, 4, 2, None), (3, 17, 100, 1, 4, 4, 0.25), (2, 129, 1, 0, 4, 1, None),
+    (1, 1, 1, 1, 2, 1, None), (5, 1, 300, 1, 4, 2, 0.25), (1, 1000, 0, 1, 4, 2, None), (2, 200, 257, 0, 2, 2, None)])
+def test_decoder_attention_matches_reference(db, items, t, p, causal, hq, hk, scale):
+    rng = np.random.default_rng(items * 1000 + t + p)
+    q = rng.normal(0, 1, (items * t, hq, 128)).astype(np.float16)
+    k = rng.normal(0, 1, (items * t, hk, 128)).astype(np.float16)
+    v = rng.normal(0, 1, (items * t, hk, 128)).astype(np.float16)
+    kp = rng.normal(0, 1, (p, hk, 128)).astype(np.float16) if p else None
+    vp = rng.normal(0, 1, (p, hk, 128)).astype(np.float16) if p else None
+    cu = lambda a: torch.from_numpy(a).cuda() if a is not None else None
+    out = db.attention_decoder(cu(q), cu(k), cu(v), items, hq, hk, cu(kp), cu(vp), bool(causal), scale)
+    assert db.device_error_word() == 0
+    s = (1.0 / 128 ** 0.5) if scale is None else scale
+    f64 = lambda a: a.astype(np.float64) if a is not None else None
+    ref = decoder_attention_ref(f64(q), f64(k), f64(v), f64(kp), f64(vp), items, hq, hk, causal, s)
+    o = out.cpu().numpy()
+    assert np.max(np.abs(o - ref)) <= 5e-3 * np.sqrt(np.mean(ref ** 2)) + 1e-6
+    # an item's result does not depend on the other items of the batch
+    last = db.attention_decoder(cu(q[-t:]), cu(k[-t:]), cu(v[-t:]), 1, hq, hk, cu(kp), cu(vp), bool(causal), scale)
+    assert np.array_equal(last.cpu().numpy().view(np.uint32), o[-t:].view(np.uint32))
