@@ -144,6 +144,10 @@ __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity, 
 // waits here, before touching anything, until that kernel has completed and its writes are
 // visible.  Returns at once for a launch without the attribute.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Lets the next kernel of the stream (launched with programmatic dependent launch) start once every
+// CTA of this grid has passed here; it still waits (pdl_wait) for this grid's completion before it
+// reads anything this grid writes.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 // Hardware named barrier among `count` threads (a multiple of 32); barrier 0 is __syncthreads.
 __device__ __forceinline__ void named_barrier_sync(int id, int count) {

@@ -256,7 +256,7 @@ def test_tensor_core_gemm_portable_mode_bit_exact(db, oracle, m, k, n):
 
 @pytest.mark.parametrize("wb", [4, 8])
 @pytest.mark.parametrize("m", [1, 2, 3, 4, 5, 8])
-@pytest.mark.parametrize("k,n", [(64, 7), (1025, 65), (1024, 3072), (3072, 1024)])
+@pytest.mark.parametrize("k,n", [(64, 7), (1025, 65), (1024, 3072), (3072, 1024), (9728, 40), (10240, 9)])
 def test_gemv_path_bit_exact(db, oracle, wb, m, k, n):
     x = ref_x(m, k, kind="normal")
     for fused, mode in ((True, 0), (False, 1)):
