@@ -15,7 +15,9 @@
 // shared memory with the block's weight scales, and after a CTA barrier one thread per (row,
 // activation row) runs the sequential fold out of shared memory (the activation scales are staged
 // there once per launch).  The next block's weights and weight scales are loaded before that
-// barrier, so they are in flight during the fold.
+// barrier, so they are in flight during the fold; the parking space is double-buffered, so the
+// fold of one block runs while the other warps form the next block's dots (the barrier of the
+// next block orders a buffer's fold before its reuse two blocks later).
 //
 // The kernel is launched with programmatic dependent launch: its first weight loads (weights are
 // never written by the kernel before it) go out before it waits for the previous kernel, and it
@@ -90,10 +92,10 @@ __global__ void __launch_bounds__(gemv_max_threads(BITS))
                 const int32_t* __restrict__ asum, int64_t ldsa, const uint8_t* __restrict__ w,
                 const float* __restrict__ sw, int M, int N, int G, float* __restrict__ y, int64_t ldy,
                 const int* __restrict__ nonfinite) {
-    // shared memory: dots [R][MR][G] | sw_s [G][R] | sa_s [G][MR]
-    extern __shared__ int dots[];
-    float* sw_s = reinterpret_cast<float*>(dots + R * MR * G);
-    float* sa_s = sw_s + G * R;
+    // shared memory: two buffers of (dots [R][MR][G] | sw_s [G][R]), then sa_s [G][MR]
+    extern __shared__ int gemv_smem[];
+    const int buf_words = (R * MR + R) * G;
+    float* sa_s = reinterpret_cast<float*>(gemv_smem + 2 * buf_words);
     constexpr int CPG = BITS == 4 ? 2 : 4;            // 16-byte chunks per 64-code group
     // weight scales of a block per thread: R * G over >= CPG * G threads
     constexpr int SWPT = (R + CPG - 1) / CPG;
@@ -151,7 +153,9 @@ __global__ void __launch_bounds__(gemv_max_threads(BITS))
         corr[r] = (BITS == 4 && live && (c % CPG) == 0) ? 8 * __ldg(asum + (size_t)g_own * ldsa + r) : 0;
     }
     const bool poisoned = nonfinite && *nonfinite;
-    for (; blk < nblocks; blk += gridDim.x) {
+    for (int it = 0; blk < nblocks; blk += gridDim.x, ++it) {
+        int* dots = gemv_smem + (it & 1) * buf_words;
+        float* sw_s = reinterpret_cast<float*>(dots + R * MR * G);
         // chunk dots of the block's R rows, summed over the CPG chunks of a group (neighbouring
         // lanes), parked for the fold
         int part[R][MR];
@@ -193,8 +197,9 @@ __global__ void __launch_bounds__(gemv_max_threads(BITS))
         }
         __syncthreads();
         // sequential fold, one thread per (output row, activation row)
-        if (threadIdx.x < R * MR) {
-            const int j = threadIdx.x / MR, r = threadIdx.x % MR;
+        const int q = threadIdx.x;
+        if (q < R * MR) {
+            const int j = q / MR, r = q % MR;
             const int n = blk * R + j;
             if (r < M && n < N) {
                 const int* drow = dots + (j * MR + r) * G;
@@ -212,11 +217,10 @@ __global__ void __launch_bounds__(gemv_max_threads(BITS))
                 *dst = acc;
             }
         }
-        __syncthreads();  // the parked dots are read before the next block overwrites them
     }
 }
 
-static size_t gemv_smem_bytes(int R, int MR, int G) { return (size_t)(R * MR + R + MR) * G * 4; }
+static size_t gemv_smem_bytes(int R, int MR, int G) { return (size_t)(2 * (R * MR + R) + MR) * G * 4; }
 
 // Persistent grid: as many CTAs as fit on the SMs (at most one per block).  R = 8 rows per block
 // when that still gives every resident CTA a block, else 4 (more blocks for short N); MR = 8
@@ -225,11 +229,14 @@ template <int BITS, int MR, int R, bool FUSED, bool RESIDUAL>
 static int launch_r(const DbGemvArgs& a, int G, int threads, cudaStream_t s) {
     auto kernel = gemv_kernel<BITS, MR, R, FUSED, RESIDUAL>;
     const size_t smem = gemv_smem_bytes(R, MR, G);
-    int per_sm = 0;
-    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem);
+    cudaError_t e = db_set_max_smem(reinterpret_cast<const void*>(kernel), (int)gemv_smem_bytes(R, MR, GEMV_MAX_GROUPS));
     if (e != cudaSuccess) return (int)e;
-    const int nblocks = (a.N + R - 1) / R;
-    const int grid = std::max(1, std::min(nblocks, std::max(per_sm, 1) * db_num_sms()));
+    int per_sm = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem);
+    if (e != cudaSuccess) return (int)e;
+    // every CTA walks the same number of blocks
+    const int nblocks = (a.N + R - 1) / R, resident = std::max(per_sm, 1) * db_num_sms();
+    const int grid = std::max(1, std::min(nblocks, resident));
     e = db_launch_pdl(kernel, dim3(grid), dim3(threads), smem, s, a.a_codes, a.lda, a.sa, a.a_sums, a.ldsa,
                       a.w_codes, a.sw, a.M, a.N, G, a.y, a.ldy, a.nonfinite);
     return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
@@ -238,6 +245,9 @@ static int launch_r(const DbGemvArgs& a, int G, int threads, cudaStream_t s) {
 // Whether blocks of R rows give every CTA that fits on the SMs at least one block.
 template <int BITS, int MR, int R, bool FUSED, bool RESIDUAL>
 static bool fills(const DbGemvArgs& a, int G, int threads) {
+    if (db_set_max_smem(reinterpret_cast<const void*>(gemv_kernel<BITS, MR, R, FUSED, RESIDUAL>),
+                        (int)gemv_smem_bytes(R, MR, GEMV_MAX_GROUPS)) != cudaSuccess)
+        return false;
     int per_sm = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_kernel<BITS, MR, R, FUSED, RESIDUAL>, threads,
                                                       gemv_smem_bytes(R, MR, G)) != cudaSuccess)
