@@ -56,7 +56,7 @@ def measured_peaks():
 
 def ncu_traffic():
     """DRAM bytes per GEMM launch from the committed ncu summary (profiles/), or None."""
-    p = os.path.join(ROOT, "profiles", "gemm_tc_c2_encoder.md")
+    p = os.path.join(ROOT, "profiles", "gemm_i8_c2_encoder.md")
     if not os.path.exists(p):
         return None
     m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", open(p).read())
@@ -533,7 +533,7 @@ def run_ours(args, rank, world, local_rank):
                 "gpu_launches": launches,
                 "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
                              "frac": achieved / peak_tf, "traffic": traffic,
-                             "kernel": "gemm_tc_kernel (all projection launches)",
+                             "kernel": "gemm_i8_kernel (all projection launches)",
                              "peak_kind": f"{peak_kind} bf16 dense burst",
                              "launches": gemm_launches, "avg_launch_us": gemm_ms / gemm_launches * 1e3,
                              "flops_per_launch": gemm_flops / gemm_launches},
