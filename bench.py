@@ -696,7 +696,8 @@ def run_c4(args, local_rank):
 
     import decisive_b200 as db
     torch.cuda.set_device(local_rank)
-    cfg = db.BertConfig(layers=12, hidden=768, heads=12, ffn=3072, vocab=128100, max_positions=512, block=32)
+    cfg = db.BertConfig(layers=12, hidden=768, heads=12, ffn=3072, vocab=128100, max_positions=512, block=32,
+                        mode=args.c4_mode)
     model = db.BertModel(cfg, seed=SEED, std=0.02, device=local_rank)
     n = max(args.steps, 1)
     reqs = c4_requests(cfg.vocab, n)
@@ -708,7 +709,8 @@ def run_c4(args, local_rank):
         model.score(state, choices)
     dt = time.perf_counter() - t0
     tokens = sum(8 * len(st) + sum(len(c) for c in ch) for st, ch in reqs)
-    print(json.dumps({"workload": "C4 Decima-shaped cross-encoder (12L, D=768, FF 3072), W8A8 block 32, "
+    print(json.dumps({"workload": "C4 Decima-shaped cross-encoder (12L, D=768, FF 3072), "
+                                  f"{'W8A32' if args.c4_mode else 'W8A8'} block 32, "
                                   "requests of a 384-token state + 8 choices of U(16..48) tokens -> 8 x 3 logits",
                       "requests": n, "tokens_per_s": tokens / dt, "requests_per_s": n / dt,
                       "ms_per_request": dt / n * 1e3,
@@ -736,6 +738,7 @@ def main():
     ap.add_argument("--layout", default="i8", choices=["i8", "tc"],
                     help="activation codes of --workload gemm: int8 (kind::i8 kernel) or f16 (kind::f16 kernel)")
     ap.add_argument("--gemm-config", default="", help="block_n,max_ctas,pair_ctas for --workload gemm")
+    ap.add_argument("--c4-mode", type=int, default=0, choices=[0, 1], help="--workload c4: 0 W8A8, 1 W8A32")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))

@@ -152,6 +152,18 @@ def decima_linear(x, w_codes, w_scales, N: int, block: int = 32, fused: bool = T
     return y
 
 
+def decima_linear_w8a32(x, w_codes, w_scales, N: int, block: int = 32, fused: bool = True, bias=None):
+    """decima Matrix::apply_with_rows, Weights mode: y [M, N] = f32 x times the int8 weight codes
+    (decoded with their block scales) + bias."""
+    import torch
+    M, K = x.shape
+    flag = torch.zeros(1, dtype=torch.int32, device=x.device)
+    y = torch.empty((M, N), dtype=torch.float32, device=x.device)
+    check(load().db_decima_linear_w8a32(_ptr(x), M, K, _ptr(w_codes), _ptr(w_scales), N, block, int(fused),
+                                        _ptr(bias), _ptr(y), _ptr(flag), _stream()))
+    return y
+
+
 EPILOGUE_STORE, EPILOGUE_RESIDUAL, EPILOGUE_SWIGLU = 0, 1, 2
 
 
@@ -605,10 +617,11 @@ class BertConfig:
     block: int = 32
     eps: float = 1e-12
     fused: bool = True
+    mode: int = 0  # 0: W8A8 (WeightsActivations), 1: W8A32 (Weights)
 
     def c(self) -> _lib.BertConfig:
         return _lib.BertConfig(self.layers, self.hidden, self.heads, self.ffn, self.vocab, self.max_positions,
-                               self.block, self.eps, int(self.fused))
+                               self.block, self.eps, int(self.fused), int(self.mode))
 
 
 class BertModel:

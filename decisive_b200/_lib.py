@@ -29,7 +29,7 @@ class EncoderConfig(C.Structure):
 class BertConfig(C.Structure):
     _fields_ = [("layers", C.c_int32), ("hidden", C.c_int32), ("heads", C.c_int32), ("ffn", C.c_int32),
                 ("vocab", C.c_int32), ("max_positions", C.c_int32), ("block", C.c_int32), ("eps", C.c_float),
-                ("fused", C.c_int32)]
+                ("fused", C.c_int32), ("mode", C.c_int32)]
 
 
 class Parameters(C.Structure):
@@ -68,6 +68,7 @@ SIGNATURES = [
     ("db_decima_quantize_activations", _i32, [_vp, _i64, _i64, _i32, _vp, _i32, _i64, _vp, _i64, _vp, _vp]),
     ("db_decima_workspace_bytes", _sz, [_i64, _i64, _i32]),
     ("db_decima_linear", _i32, [_vp, _i64, _i64, _vp, _vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp]),
+    ("db_decima_linear_w8a32", _i32, [_vp, _i64, _i64, _vp, _vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp]),
     ("db_gemm_tune", _i32, [_i64, _i64, _i64, _i32, _i32, C.c_char_p, _vp, C.c_char_p, _sz]),
     ("db_linear_workspace_bytes", _sz, [_i64, _i64]),
     ("db_linear_g64", _i32, [_vp, _i64, _i64, _vp, _vp, _i64, _i32, _i32, _i32, _vp, _vp, _vp]),

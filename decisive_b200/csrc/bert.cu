@@ -279,10 +279,13 @@ int build_synthetic(db_bert* m, uint64_t seed, float stdv) {
     return rc;
 }
 
-// y [T, N] = W8A8(x [T, K]) + bias (codes of x are quantised first)
+// y [T, N] = W8A8(x [T, K]) + bias (codes of x are quantised first), or W8A32 (x as f32)
 int linear(db_bert* m, const float* x, int T, int K, const uint8_t* wc, const float* ws, int N, const float* b,
            float* y) {
     const auto& c = m->cfg;
+    if (c.mode == 1)
+        return db_launch_decima_w8a32(x, K, T, K, wc, (K + 63) / 64 * 64, ws, db_scale_stride(N), N, c.block, c.fused,
+                                      b, y, N, m->flag, m->stream);
     const int64_t Kp = (K + 63) / 64 * 64, lds = db_scale_stride(m->cap);
     int rc = db_launch_decima_quantize(x, K, T, K, c.block, m->codes, DB_CODES_NATURAL_I8, Kp, m->scales, lds, 0,
                                        m->flag, m->stream);
@@ -360,7 +363,7 @@ db_bert* db_bert_create_synthetic(int device, const db_bert_config* cfg, uint64_
     if (!cfg || cfg->layers <= 0 || cfg->hidden <= 0 || cfg->heads <= 0 || cfg->hidden % cfg->heads ||
         cfg->hidden / cfg->heads > 128 || cfg->hidden > 1024 || cfg->ffn <= 0 || cfg->vocab <= 0 ||
         cfg->max_positions <= 0 || cfg->max_positions > 4096 || (cfg->block != 32 && cfg->block != 64) ||
-        !(cfg->eps > 0.f)) {
+        !(cfg->eps > 0.f) || (cfg->mode != 0 && cfg->mode != 1)) {
         fill_error(err, "INVALID_PARAMETERS", "unsupported Decima encoder configuration");
         return nullptr;
     }

@@ -355,6 +355,22 @@ int db_decima_linear(const float* x, int64_t M, int64_t K, const uint8_t* w_code
     return db_cuda_status(db_launch_gemm_tc(a, S(stream)), "decima gemm");
 }
 
+int db_decima_linear_w8a32(const float* x, int64_t M, int64_t K, const uint8_t* w_codes, const float* sw, int64_t N,
+                           int block, int fused, const float* bias, float* y, int* nonfinite, void* stream) {
+    if (M < 0 || K <= 0 || N <= 0 || !decima_block_ok(block) || !w_codes || !sw || !y || !nonfinite ||
+        (M > 0 && !x))
+        return db_fail(DB_ERR_INVALID_ARGUMENT, "INVALID_ARGUMENT", "decima linear: bad shape");
+    if (block == 16)
+        return db_fail(DB_ERR_UNSUPPORTED, "UNSUPPORTED", "decima W8A32: the GPU kernel takes blocks of 32, 64 or 128");
+    if (M == 0) return DB_OK;
+    cudaMemsetAsync(nonfinite, 0, sizeof(int), S(stream));
+    int rc = db_launch_decima_w8a32(x, K, (int)M, (int)K, w_codes, groups_of(K) * DB_GROUP, sw, db_scale_stride(N),
+                                    (int)N, block, fused, bias, y, N, nonfinite, S(stream));
+    if (rc) return db_cuda_status(rc, "decima w8a32");
+    // a non-finite x gives all-NaN y (decima/int8.rs:183-187)
+    return db_cuda_status(db_launch_fill_nan_if(y, M * N, nonfinite, S(stream)), "decima w8a32");
+}
+
 int db_project_packed(const float* x, int64_t K, const uint8_t* w_codes, const float* sw, int64_t outputs, int bits,
                       float* y, void* workspace, void* stream) {
     if (K <= 0 || K % DB_GROUP || outputs <= 0 || !workspace)

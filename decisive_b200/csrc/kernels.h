@@ -21,6 +21,11 @@ int db_launch_quantize_rows(const void* x, int dtype, int64_t ldx, int M, int K,
 // Decima int8 quantiser (blocks of 16/32/64/128, round half away from zero of x / scale).  Weights
 // use it with layout DB_CODES_NATURAL_I8 into the Q8 device layout and group-major scales
 // [G, lds]; activations with DB_CODES_TC_F16.  row_major_scales = 1 writes scales [M, lds].
+// Decima Weights mode (W8A32): y [M, ldy] = x [M, ldx] (f32) times int8 weight codes [N, ldw] in
+// blocks of 32/64/128 with group-major scales [ceil(K/block), ldsw], + bias; fused = the AVX2 order.
+int db_launch_decima_w8a32(const float* x, int64_t ldx, int M, int K, const uint8_t* w_codes, int64_t ldw,
+                           const float* sw, int64_t ldsw, int N, int block, int fused, const float* bias, float* y,
+                           int64_t ldy, int* nonfinite, cudaStream_t stream);
 int db_launch_decima_quantize(const float* x, int64_t ldx, int M, int K, int block, void* codes, int layout,
                               int64_t ldc, float* scales, int64_t lds, int row_major_scales, int* nonfinite,
                               cudaStream_t stream);

@@ -200,6 +200,14 @@ int db_decima_quantize_activations(const float *x, int64_t M, int64_t K, int blo
  * portable sum += float(dot) * (sw*sa) (int8.rs:380-420).  A non-finite x gives all-NaN y.
  * workspace: device bytes from db_decima_workspace_bytes(M, K, block). */
 size_t db_decima_workspace_bytes(int64_t M, int64_t K, int block);
+/* Matrix::apply_with_rows in Weights mode (W8A32: the same int8 weight codes and scales, f32
+ * activations), blocks of 32, 64 or 128 (16 gives DB_ERR_UNSUPPORTED).  fused = 1 follows the AVX2
+ * kernel (decima/int8/weights_x86.rs:51-113): weights decoded to the f32 product code * scale, one
+ * fma chain over k per output; 0 the portable kernel (int8.rs:384-407): per block dot += x * code,
+ * sum += dot * scale.  y [M, N] = sum + bias[n] (bias NULL: + 0); a non-finite x gives all-NaN y.
+ * nonfinite: one device int the call uses as its flag (no allocation). */
+int db_decima_linear_w8a32(const float *x, int64_t M, int64_t K, const uint8_t *w_codes, const float *sw, int64_t N,
+                           int block, int fused, const float *bias, float *y, int *nonfinite, void *stream);
 int db_decima_linear(const float *x, int64_t M, int64_t K, const uint8_t *w_codes, const float *sw, int64_t N,
                      int block, int fused, const float *bias, float *y, void *workspace, void *stream);
 
@@ -311,7 +319,7 @@ int db_predict_batch(db_model *m, const int32_t *const *ids, const size_t *lens,
 /* ---- C4: the Decima-shaped (BERT) encoder on the Decima int8 kernels (decima/mod.rs:492-556):
  * x = LN(word[id] + type[0] + pos[p]); per layer x = LN(x + Wo attn(qkv) + bo),
  * x = LN(x + W2 gelu(W1 x + b1) + b2); every projection W8A8 in blocks of `block` (32 or 64) with
- * the Decima quantiser; heads of hidden/heads <= 128 dims, non-causal attention scaled by
+ * the Decima quantiser, or W8A32 with mode = 1; heads of hidden/heads <= 128 dims, non-causal attention scaled by
  * 1/sqrt(head dim); erf GELU; LayerNorm eps `eps`.  Synthetic weights (db_synthetic_bf16 keys:
  * word 0, pos 1, type 2; layer l: 16 + 16 l + {q 0, k 1, v 2, o 3, ff1 4, ff2 5, bq 6, bk 7, bv 8,
  * bo 9, b1 10, b2 11}; LayerNorm weights 1, biases 0).  db_bert_predict writes the mean-pooled
@@ -320,6 +328,8 @@ typedef struct {
     int32_t layers, hidden, heads, ffn, vocab, max_positions, block;
     float eps;
     int32_t fused; /* 1 = AVX2 accumulation order (default), 0 = portable */
+    int32_t mode;  /* 0 = W8A8 (WeightsActivations, the int8 tensor-core GEMM), 1 = W8A32 (Weights:
+                      f32 activations, db_decima_linear_w8a32's kernel) */
 } db_bert_config;
 typedef struct db_bert db_bert;
 db_bert *db_bert_create_synthetic(int device, const db_bert_config *cfg, uint64_t seed, float std, db_error *err);

@@ -988,6 +988,46 @@ void oracle_decima_apply_w8a8(const int8_t *w_codes, const float *w_scales, size
     free(sa);
 }
 
+/* Matrix::apply_with_rows in Weights mode (W8A32: int8 weights, f32 activations).
+ * mode 0, the AVX2 kernel (decima/int8/weights_x86.rs:51-113): every weight is decoded to the f32
+ *   product code * scale (:63-76), then each output is one fma chain over k = 0..cols-1 from 0
+ *   (:86-100), plus the bias (:104-109);
+ * mode 1, the portable kernel (decima/int8.rs:384-407): per block a dot of x * code (a multiply
+ *   and an add per term), then sum += dot * scale, then the bias.
+ * A non-finite x gives all-NaN y (int8.rs:183-187).  codes [rows, groups*block], scales
+ * [rows, groups]. */
+void oracle_decima_apply_w8a32(const int8_t *w_codes, const float *w_scales, size_t rows, size_t cols,
+                               size_t block, const float *x, size_t m, const float *bias, int mode, float *y) {
+    const size_t groups = (cols + block - 1) / block;
+    for (size_t i = 0; i < m * cols; ++i)
+        if (!isfinite(x[i])) {
+            for (size_t j = 0; j < m * rows; ++j) y[j] = NAN;
+            return;
+        }
+#pragma omp parallel for schedule(static)
+    for (long long i = 0; i < (long long)m; ++i) {
+        const float *xi = x + (size_t)i * cols;
+        for (size_t n = 0; n < rows; ++n) {
+            const int8_t *qw = w_codes + n * groups * block;
+            float sum = 0.f;
+            if (mode == 0) {
+                for (size_t k = 0; k < cols; ++k) {
+                    const float wf = (float)qw[k] * w_scales[n * groups + k / block];
+                    sum = fmaf(xi[k], wf, sum);
+                }
+            } else {
+                for (size_t g = 0; g < groups; ++g) {
+                    float dot = 0.f;
+                    const size_t k1 = (g + 1) * block < cols ? (g + 1) * block : cols;
+                    for (size_t k = g * block; k < k1; ++k) dot = dot + xi[k] * (float)qw[k];
+                    sum = sum + dot * w_scales[n * groups + g];
+                }
+            }
+            y[(size_t)i * rows + n] = sum + (bias ? bias[n] : 0.f);
+        }
+    }
+}
+
 void oracle_layer_norm(float *x, size_t rows, size_t d, const float *w, const float *b, float eps) {
     for (size_t r = 0; r < rows; ++r) {
         float *row = x + r * d;

@@ -135,6 +135,8 @@ void oracle_decima_quantize_rows(const float *x, size_t rows, size_t cols, size_
  * then y = sum + (bias ? bias[n] : 0).  A non-finite x gives all-NaN y (int8.rs:186-190). */
 void oracle_decima_apply_w8a8(const int8_t *w_codes, const float *w_scales, size_t rows, size_t cols,
                               size_t block, const float *x, size_t m, const float *bias, int mode, float *y);
+void oracle_decima_apply_w8a32(const int8_t *w_codes, const float *w_scales, size_t rows, size_t cols,
+                               size_t block, const float *x, size_t m, const float *bias, int mode, float *y);
 
 /* Decima encoder pieces (decima/cpu.rs): LayerNorm with sequential f32 sums (:529-539) and the
  * erf GELU (:542-556); the composed C4 forward lives in oracle.py (bert_forward). */

@@ -94,6 +94,7 @@ def _declare(l):
     l.oracle_decima_quantize.argtypes = [C.c_float, C.c_float]
     l.oracle_decima_quantize_rows.argtypes = [_f, _sz, _sz, _sz, _i8, _f]
     l.oracle_decima_apply_w8a8.argtypes = [_i8, _f, _sz, _sz, _sz, _f, _sz, _f, C.c_int, _f]
+    l.oracle_decima_apply_w8a32.argtypes = [_i8, _f, _sz, _sz, _sz, _f, _sz, _f, C.c_int, _f]
     l.oracle_layer_norm.argtypes = [_f, _sz, _sz, _f, _f, C.c_float]
     l.oracle_gelu.argtypes = [_f, _sz]
     l.oracle_num_threads.restype = C.c_int
@@ -466,9 +467,11 @@ def decima_quantize_rows(x, block: int):
 
 
 class DecimaMatrix:
-    """decima::int8::Matrix in WeightsActivations mode (W8A8), weights f32 [rows, cols]."""
+    """decima::int8::Matrix, weights f32 [rows, cols]: WeightsActivations mode (W8A8) by default,
+    Weights mode (W8A32: f32 activations) with weights_only=True."""
 
-    def __init__(self, weights, block: int):
+    def __init__(self, weights, block: int, weights_only: bool = False):
+        self.weights_only = weights_only
         w = np.ascontiguousarray(weights, dtype=np.float32)
         if block not in (16, 32, 64, 128) or not np.all(np.isfinite(w)):
             raise ValueError("INT8 block must be 16, 32, 64 or 128 and weights finite")
@@ -480,8 +483,9 @@ class DecimaMatrix:
         x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, self.cols)
         y = np.zeros((x.shape[0], self.rows), np.float32)
         b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
-        lib().oracle_decima_apply_w8a8(_p(self.codes, _i8), _p(self.scales, _f), self.rows, self.cols,
-                                       self.block, _p(x, _f), x.shape[0], _p(b, _f), mode, _p(y, _f))
+        fn = lib().oracle_decima_apply_w8a32 if self.weights_only else lib().oracle_decima_apply_w8a8
+        fn(_p(self.codes, _i8), _p(self.scales, _f), self.rows, self.cols, self.block, _p(x, _f), x.shape[0],
+           _p(b, _f), mode, _p(y, _f))
         return y
 
 
@@ -519,8 +523,10 @@ def bert_score_head(pooled, w, b):
 def bert_forward(cfg: dict, w: dict, ids, mode: int = 0):
     """Composed Decima (BERT-shaped, decima/mod.rs:492-556) encoder forward with W8A8 block
     projections: x = LN(word[id] + type[0] + pos[p]); per layer x = LN(x + o(attn(q, k, v)));
-    x = LN(x + ff2(gelu(ff1(x)))).  Returns (mean-pooled, hidden [T, D])."""
+    x = LN(x + ff2(gelu(ff1(x)))).  cfg["mode"] = 1 runs the projections in Weights mode (W8A32).
+    Returns (mean-pooled, hidden [T, D])."""
     D, H, block, eps = cfg["hidden"], cfg["heads"], cfg["block"], cfg["eps"]
+    wo = bool(cfg.get("mode", 0))  # 1: Weights mode (W8A32)
     hd = D // H
     ids = np.asarray(ids)
     T = ids.size
@@ -528,13 +534,13 @@ def bert_forward(cfg: dict, w: dict, ids, mode: int = 0):
     x = layer_norm(x, w["emb_ln_w"], w["emb_ln_b"], eps)
     for l in range(cfg["layers"]):
         L = w["layers"][l]
-        q = DecimaMatrix(L["q"], block).apply(x, bias=L["bq"], mode=mode)
-        k = DecimaMatrix(L["k"], block).apply(x, bias=L["bk"], mode=mode)
-        v = DecimaMatrix(L["v"], block).apply(x, bias=L["bv"], mode=mode)
+        q = DecimaMatrix(L["q"], block, wo).apply(x, bias=L["bq"], mode=mode)
+        k = DecimaMatrix(L["k"], block, wo).apply(x, bias=L["bk"], mode=mode)
+        v = DecimaMatrix(L["v"], block, wo).apply(x, bias=L["bv"], mode=mode)
         ctx = attention(q, k, v, H, H, hd, scale=1.0 / np.sqrt(hd))
-        o = DecimaMatrix(L["o"], block).apply(ctx, bias=L["bo"], mode=mode)
+        o = DecimaMatrix(L["o"], block, wo).apply(ctx, bias=L["bo"], mode=mode)
         x = layer_norm((x + o).astype(np.float32), L["ln1_w"], L["ln1_b"], eps)
-        h = gelu(DecimaMatrix(L["ff1"], block).apply(x, bias=L["b1"], mode=mode))
-        o2 = DecimaMatrix(L["ff2"], block).apply(h, bias=L["b2"], mode=mode)
+        h = gelu(DecimaMatrix(L["ff1"], block, wo).apply(x, bias=L["b1"], mode=mode))
+        o2 = DecimaMatrix(L["ff2"], block, wo).apply(h, bias=L["b2"], mode=mode)
         x = layer_norm((x + o2).astype(np.float32), L["ln2_w"], L["ln2_b"], eps)
     return x.mean(axis=0, dtype=np.float32), x

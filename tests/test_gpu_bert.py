@@ -67,6 +67,29 @@ def test_c4_encoder_matches_composed_oracle(db, hidden, heads, block, tokens):
     assert db.device_error_word() == 0
 
 
+@pytest.mark.parametrize("fused", [True, False])
+def test_c4_encoder_weights_mode_matches_oracle(db, fused):
+    """The same encoder with Weights-mode (W8A32) projections: f32 activations against the int8
+    weight codes (decima/int8.rs:166-283, weights_x86.rs), in either accumulation order."""
+    from oracle import oracle
+    cfg = dict(layers=2, hidden=256, heads=4, ffn=512, vocab=1000, max_positions=128, block=32, eps=1e-12)
+    seed, std = 11, 0.05
+    model = db.BertModel(db.BertConfig(**cfg, fused=fused, mode=1), seed=seed, std=std)
+    ids = np.random.default_rng(5).integers(0, cfg["vocab"], 90).astype(np.int32)
+    pooled, states = model.predict(ids, hidden=True)
+    want_pooled, want_states = oracle.bert_forward(dict(cfg, mode=1), oracle_weights(db, cfg, seed, std), ids,
+                                                   mode=0 if fused else 1)
+    assert cosine(pooled, want_pooled) >= 0.9999, cosine(pooled, want_pooled)
+    assert min(cosine(states[t], want_states[t]) for t in range(len(ids))) >= 0.999
+    # W8A32 keeps the activations in f32: closer to the oracle than the W8A8 model is
+    w8a8 = db.BertModel(db.BertConfig(**cfg, fused=fused), seed=seed, std=std)
+    assert cosine(pooled, want_pooled) >= cosine(w8a8.predict(ids), want_pooled)
+    logits = model.score(ids[:40], [ids[40:50], ids[50:52]])
+    assert logits.shape == (2, 3) and np.all(np.isfinite(logits))
+    model.close()
+    w8a8.close()
+
+
 def test_c4_encoder_rejects_bad_requests(db):
     cfg = db.BertConfig(layers=1, hidden=256, heads=4, ffn=512, vocab=100, max_positions=64)
     model = db.BertModel(cfg)

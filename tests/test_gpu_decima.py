@@ -97,3 +97,37 @@ def test_decima_nonfinite_input_gives_nan_and_bias_only(db):
         db.decima_quantize_weights(torch.tensor([[float("nan")]], device="cuda"), 32)
     with pytest.raises(Exception):
         db.decima_linear(torch.zeros((1, 1), device="cuda"), codes, scales, 1, 16)  # GEMM takes 32 or 64
+
+
+# ------------------------------------------------------------------ Weights mode (W8A32)
+@pytest.mark.parametrize("block", [32, 64, 128])
+@pytest.mark.parametrize("m,n,k", [(1, 9, 33), (7, 17, 127), (65, 70, 96), (200, 300, 768), (130, 768, 3072)])
+def test_decima_w8a32_bit_exact(db, oracle, block, m, n, k):
+    """Matrix::apply_with_rows in Weights mode: f32 activations against the int8 weight codes, in
+    the AVX2 order (decoded weights, one fma chain over k: decima/int8/weights_x86.rs) and the
+    portable order (per-block dot, then sum += dot * scale: decima/int8.rs:384-407)."""
+    x = x_pattern(m, k)
+    v = (np.random.default_rng(k + n).normal(0, 0.05, (n, k))).astype(np.float32)
+    bias = np.random.default_rng(n).normal(0, 1, n).astype(np.float32)
+    ref = oracle.DecimaMatrix(v, block, weights_only=True)
+    codes, scales = db.decima_quantize_weights(torch.from_numpy(v).cuda(), block)
+    xd = torch.from_numpy(x).cuda()
+    bd = torch.from_numpy(bias).cuda()
+    for fused, mode in ((True, 0), (False, 1)):
+        y = db.decima_linear_w8a32(xd, codes, scales, n, block, fused, bd).cpu().numpy()
+        want = ref.apply(x, bias=bias, mode=mode)
+        assert bits_equal(y, want), (fused, np.max(np.abs(y - want)))
+        y0 = db.decima_linear_w8a32(xd, codes, scales, n, block, fused, None).cpu().numpy()
+        assert bits_equal(y0, ref.apply(x, mode=mode))
+
+
+def test_decima_w8a32_nonfinite_and_blocks(db):
+    codes, scales = db.decima_quantize_weights(torch.ones((3, 40), device="cuda"), 32)
+    x = torch.ones((2, 40), device="cuda")
+    x[1, 7] = float("nan")
+    assert torch.isnan(db.decima_linear_w8a32(x, codes, scales, 3, 32)).all()
+    y = db.decima_linear_w8a32(torch.ones((2, 40), device="cuda"), codes, scales, 3, 32)
+    assert torch.equal(y, torch.full((2, 3), 40.0, device="cuda"))
+    c16, s16 = db.decima_quantize_weights(torch.ones((3, 40), device="cuda"), 16)
+    with pytest.raises(Exception):
+        db.decima_linear_w8a32(torch.ones((2, 40), device="cuda"), c16, s16, 3, 16)
