@@ -158,7 +158,8 @@ int db_gemm_g64_config(const void* a_codes, int layout, int64_t lda, const float
                        int64_t ldsa, const uint8_t* w_codes, const float* sw, int64_t M, int64_t N, int64_t K,
                        int bits, int fused, int residual, float* y, int64_t ldy, const int* nonfinite,
                        const db_gemm_config* config, void* stream) {
-    if (config && ((config->block_n != 0 && config->block_n != 64 && config->block_n != 128 && config->block_n != 256) ||
+    if (config && ((config->block_n != 0 && config->block_n != 64 && config->block_n != 128 && config->block_n != 256 &&
+                    !(config->block_n == 32 && layout == DB_CODES_NATURAL)) ||
                    config->max_ctas < 0 ||
                    (config->pair_ctas != 0 && config->pair_ctas != 1)))
         return db_fail(DB_ERR_INVALID_ARGUMENT, "INVALID_ARGUMENT", "gemm: bad tile configuration");

@@ -24,9 +24,9 @@ int db_launch_gemm_i8(const DbGemmArgs& a, cudaStream_t stream) {
             (a.ldoc & 15) || a.ldoc < a.N / 2 || a.ldos < db_scale_stride(a.M))
             return (int)cudaErrorInvalidValue;
     }
-    if (bn != 64 && bn != 128 && bn != 256) return (int)cudaErrorInvalidValue;
-    // CTA pairs (M = 256 MMAs) when asked for and there are rows for both CTAs
-    const bool pair = a.pair_ctas && a.M > BM;
+    if (bn != 32 && bn != 64 && bn != 128 && bn != 256) return (int)cudaErrorInvalidValue;
+    // CTA pairs (M = 256 MMAs) when asked for and there are rows for both CTAs (not at 32-wide tiles)
+    const bool pair = a.pair_ctas && a.M > BM && bn != 32;
     if ((reinterpret_cast<uintptr_t>(a.a_codes) & 15) || (a.lda & 15) || a.lda < Kp ||
         (reinterpret_cast<uintptr_t>(a.w_codes) & 15) || (reinterpret_cast<uintptr_t>(a.sa) & 15) ||
         (reinterpret_cast<uintptr_t>(a.sw) & 15) || a.ldsa < db_scale_stride(a.M) || (a.ldsa & 3))

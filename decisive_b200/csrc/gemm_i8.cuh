@@ -18,6 +18,8 @@
 // tile, loaded by TMA as-is for Q8 (128B swizzle) or as raw nibbles for Q4, which two converter
 // warps turn into the swizzled int8 tile.
 //
+// Tiles are 128 x BN with BN = 32, 64, 128 or 256 (32: single CTAs, store / residual epilogues; it
+// serves small M, where wider tiles leave most SMs without a tile).
 // Roles (384 threads, one CTA per SM, persistent over MT x BN output tiles):
 //   warp 0      TMA producer
 //   warp 1      TMEM owner + MMA issuer (lane 0; in pair mode the even CTA issues M = 256 MMAs
@@ -63,6 +65,9 @@ static_assert(128 * REGS_CONTROL + 256 * REGS_EPI <= REGS_LAUNCH * NUM_THREADS, 
 #ifndef GI8_EPI_WAIT
 #define GI8_EPI_WAIT mbar_spin_polite
 #endif
+#ifndef GI8_PROD_WAIT
+#define GI8_PROD_WAIT mbar_spin_polite
+#endif
 constexpr uint32_t DOT_BIAS = 0x4B400000u;  // bits of 12582912.0f
 constexpr float DOT_BIAS_F = 12582912.0f;
 constexpr uint64_t DRAIN_NS = 100000000ull;
@@ -70,14 +75,14 @@ constexpr uint64_t DRAIN_NS = 100000000ull;
 template <int BN, int BITS, int EPI, bool PAIR>
 struct Smem {
     static constexpr int WR = PAIR ? BN / 2 : BN;               // weight rows held by this CTA
-    static constexpr int NBUF = 512 / BN > 8 ? 8 : 512 / BN;    // TMEM accumulator buffers
+    static constexpr int NBUF = 512 / BN > 16 ? 16 : 512 / BN;  // TMEM accumulator buffers
     static constexpr int A_BYTES = BM * KS;                     // 16 KB
     static constexpr int B_BYTES = WR * KS;                     // int8 weight tile of a stage
     static constexpr int RAW_BYTES = BITS == 4 ? WR * KS / 2 : 0;
     static constexpr int STAGE_BYTES = A_BYTES + (BITS == 8 ? B_BYTES : RAW_BYTES);
     static constexpr int CB_BYTES = BITS == 4 ? B_BYTES : 0;    // converted Q4 tile of a stage
     static constexpr int COLS = BN / 2;                         // accumulator columns per epilogue thread
-    static constexpr int SCJ = 16;                              // scale ring: jobs loaded ahead of the epilogue
+    static constexpr int SCJ = BN <= 32 ? 32 : 16;              // scale ring: jobs loaded ahead of the epilogue
     static constexpr int SC_SLOT = (BM + BN) * 4;               // sa of this CTA's 128 rows + sw of the tile's columns
     static constexpr int SC_BYTES = SCJ * SC_SLOT;
     static constexpr int Y_CHUNK = 32 * 16 * 4;                 // 32 rows x 16 f32 columns
@@ -144,6 +149,32 @@ __device__ __forceinline__ void tie32(uint32_t (&r)[32]) {
                    "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
                    "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
                    "+r"(r[29]), "+r"(r[30]), "+r"(r[31]));
+}
+
+__device__ __forceinline__ void tie16(uint32_t (&r)[16]) {
+    asm volatile(""
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                   "+r"(r[15]));
+}
+// One job's HC columns of this warp's lanes: 32-column loads, or one 16-column load at 32-wide tiles.
+template <int HC>
+__device__ __forceinline__ void load_cols(uint32_t taddr, uint32_t* v) {
+    if constexpr (HC == 16) {
+        tmem_ld_32x32b_x16(taddr, *reinterpret_cast<uint32_t(*)[16]>(v));
+    } else {
+#pragma unroll
+        for (int c = 0; c < HC / 32; ++c) tmem_ld_32x32b_x32(taddr + (uint32_t)(c * 32), *reinterpret_cast<uint32_t(*)[32]>(v + 32 * c));
+    }
+}
+template <int HC>
+__device__ __forceinline__ void tie_cols(uint32_t* v) {
+    if constexpr (HC == 16) {
+        tie16(*reinterpret_cast<uint32_t(*)[16]>(v));
+    } else {
+#pragma unroll
+        for (int c = 0; c < HC / 32; ++c) tie32(*reinterpret_cast<uint32_t(*)[32]>(v + 32 * c));
+    }
 }
 
 // 16 * Q16 values h (pairs in v) -> int8 codes clamp(rint(h * inv), +-127), natural order, as
@@ -310,63 +341,58 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             // ------------------------------------------------------------ TMA producer
             // Per stage: the activation and weight tiles; per job (scale block): this CTA's 128
             // activation scales and the tile's BN weight scales into the scale ring, clipped to
-            // the padded scale rows (ldsa, ldsw; 16-byte multiples).
-            int st = 0, issued = 0, jn = 0, sc_issued = 0;
-            uint32_t ps = 0;
-            for (int tile = tile0; tile < tiles; tile += tstride) {
-                const int m0 = (tile % m_tiles) * MT + row_off, n0 = (tile / m_tiles) * BN + wrow_off;
-                const int ncol0 = (tile / m_tiles) * BN;
-                const int sa_rows = (int)min((int64_t)BM, ldsa - m0), sw_cols = (int)min((int64_t)BN, ldsw - ncol0);
-                const uint32_t sc_bytes = (uint32_t)(max(sa_rows, 0) + max(sw_cols, 0)) * 4u;
-                for (int s = 0; s < NS; ++s) {
-                    if (!warp_wait_backoff(&empty[st], ps ^ 1u, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_TMA))
-                        goto drain;
-                    if (lane == 0) {
-                        uint8_t* sp = smem + S::OFF_STAGE + st * S::STAGE_BYTES;
-                        // full boxes are counted, also where they reach past K or M (zero fill)
-                        constexpr uint32_t TX = S::A_BYTES + (BITS == 8 ? S::B_BYTES : 0);
-                        if (PAIR) {
-                            mbar_arrive_expect_tx_cluster(at_leader(&full[st]), TX);
-                            tma_load_2d_pair(sp, &tmA, at_leader(&full[st]), s * KS, m0);
-                            if (BITS == 8) {
-                                tma_load_2d_pair(sp + S::A_BYTES, &tmW, at_leader(&full[st]), s * KS, n0);
+            // the padded scale rows (ldsa, ldsw; 16-byte multiples).  Lane 0 alone runs the loop:
+            // a warp-wide handshake per wait and per issue (shuffle + syncwarp) was measured to
+            // cost ~250 cycles each, which paced the whole pipeline at ~2,000 cycles per stage.
+            if (lane == 0) {
+                int st = 0, issued = 0, jn = 0, sc_issued = 0;
+                uint32_t ps = 0;
+                for (int tile = tile0; tile < tiles; tile += tstride) {
+                    const int m0 = (tile % m_tiles) * MT + row_off, n0 = (tile / m_tiles) * BN + wrow_off;
+                    const int ncol0 = (tile / m_tiles) * BN;
+                    const int sa_rows = (int)min((int64_t)BM, ldsa - m0), sw_cols = (int)min((int64_t)BN, ldsw - ncol0);
+                    const uint32_t sc_bytes = (uint32_t)(max(sa_rows, 0) + max(sw_cols, 0)) * 4u;
+                    for (int s = 0; s < NS; ++s) {
+                        if (!GI8_PROD_WAIT(&empty[st], ps ^ 1u, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_TMA)) goto drain;
+                        {
+                            uint8_t* sp = smem + S::OFF_STAGE + st * S::STAGE_BYTES;
+                            // full boxes are counted, also where they reach past K or M (zero fill)
+                            constexpr uint32_t TX = S::A_BYTES + (BITS == 8 ? S::B_BYTES : 0);
+                            if (PAIR) {
+                                mbar_arrive_expect_tx_cluster(at_leader(&full[st]), TX);
+                                tma_load_2d_pair(sp, &tmA, at_leader(&full[st]), s * KS, m0);
+                                if (BITS == 8) tma_load_2d_pair(sp + S::A_BYTES, &tmW, at_leader(&full[st]), s * KS, n0);
+                            } else {
+                                mbar_arrive_expect_tx(&full[st], TX);
+                                tma_load_2d(sp, &tmA, &full[st], s * KS, m0);
+                                if (BITS == 8) tma_load_2d(sp + S::A_BYTES, &tmW, &full[st], s * KS, n0);
                             }
-                        } else {
-                            mbar_arrive_expect_tx(&full[st], TX);
-                            tma_load_2d(sp, &tmA, &full[st], s * KS, m0);
-                            if (BITS == 8) tma_load_2d(sp + S::A_BYTES, &tmW, &full[st], s * KS, n0);
+                            if (BITS == 4) {
+                                mbar_arrive_expect_tx(&wfull[st], S::RAW_BYTES);
+                                tma_load_2d(sp + S::A_BYTES, &tmW, &wfull[st], s * (KS / 2), n0);
+                            }
                         }
-                        if (BITS == 4) {
-                            mbar_arrive_expect_tx(&wfull[st], S::RAW_BYTES);
-                            tma_load_2d(sp + S::A_BYTES, &tmW, &wfull[st], s * (KS / 2), n0);
-                        }
-                    }
-                    __syncwarp();
-                    ++issued;
-                    if (++st == S::STAGES) { st = 0; ps ^= 1u; }
-                    const int j1 = min((s + 1) * 2 * SUB, GS);
-                    for (int j = s * 2 * SUB; j < j1; ++j, ++jn) {
-                        const int slot = jn % S::SCJ;
-                        if (!warp_wait_backoff(&sc_empty[slot], ((uint32_t)(jn / S::SCJ) & 1u) ^ 1u, abort_flag, dev_error,
+                        ++issued;
+                        if (++st == S::STAGES) { st = 0; ps ^= 1u; }
+                        const int j1 = min((s + 1) * 2 * SUB, GS);
+                        for (int j = s * 2 * SUB; j < j1; ++j, ++jn) {
+                            const int slot = jn % S::SCJ;
+                            if (!GI8_PROD_WAIT(&sc_empty[slot], ((uint32_t)(jn / S::SCJ) & 1u) ^ 1u, abort_flag, dev_error,
                                                DB_DEV_ERR_TIMEOUT_TMA))
-                            goto drain;
-                        if (lane == 0) {
+                                goto drain;
                             uint8_t* dst = smem + S::OFF_SC + slot * S::SC_SLOT;
                             mbar_arrive_expect_tx(&sc_full[slot], sc_bytes);
                             if (sa_rows > 0) bulk_load(dst, sa + (int64_t)j * ldsa + m0, (uint32_t)sa_rows * 4u, &sc_full[slot]);
                             if (sw_cols > 0)
                                 bulk_load(dst + BM * 4, sw + (int64_t)j * ldsw + ncol0, (uint32_t)sw_cols * 4u, &sc_full[slot]);
+                            ++sc_issued;
                         }
-                        __syncwarp();
-                        ++sc_issued;
                     }
                 }
-            }
-            goto ctl_done;
-        drain:
-            // after an abort: let the stages and scale slots this warp issued land before the CTA
-            // winds down
-            if (lane == 0) {
+                goto prod_done;
+            drain:
+                // after an abort: let the stages and scale slots this lane issued land before the CTA
+                // winds down
                 for (int k = 0; k < issued && k < S::STAGES; ++k) {
                     if (st == 0) { st = S::STAGES - 1; ps ^= 1u; } else --st;
                     if (BITS == 4) mbar_wait_drain(&wfull[st], ps, DRAIN_NS);
@@ -376,6 +402,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     const int jj = jn - 1 - k;
                     mbar_wait_drain(&sc_full[jj % S::SCJ], (uint32_t)(jj / S::SCJ) & 1u, DRAIN_NS);
                 }
+            prod_done:;
             }
             __syncwarp();
         } else if (warp == 1) {
@@ -671,17 +698,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 if (JPS > 1 && nj == JPS) {
                     uint32_t v[JPS][COLS];
 #pragma unroll
-                    for (int q = 0; q < JPS; ++q) {
-                        const uint32_t tb = tlane + (uint32_t)(((jn + q) % S::NBUF) * BN);
-#pragma unroll
-                        for (int c = 0; c < COLS / 32; ++c)
-                            tmem_ld_32x32b_x32(tb + (uint32_t)(c * 32), *reinterpret_cast<uint32_t(*)[32]>(&v[q][32 * c]));
-                    }
+                    for (int q = 0; q < JPS; ++q)
+                        load_cols<COLS>(tlane + (uint32_t)(((jn + q) % S::NBUF) * BN), v[q]);
                     tmem_wait_ld();
 #pragma unroll
-                    for (int q = 0; q < JPS; ++q)
-#pragma unroll
-                        for (int c = 0; c < COLS / 32; ++c) tie32(*reinterpret_cast<uint32_t(*)[32]>(&v[q][32 * c]));
+                    for (int q = 0; q < JPS; ++q) tie_cols<COLS>(v[q]);
                     // every column of the step's jobs is in registers: their buffers are free
                     tc_fence_before();
                     __syncwarp();
@@ -705,12 +726,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
                     for (int h = 0; h < NH; ++h) {
                         uint32_t v[HC];
-#pragma unroll
-                        for (int c = 0; c < HC / 32; ++c)
-                            tmem_ld_32x32b_x32(tb + (uint32_t)(h * HC + 32 * c), *reinterpret_cast<uint32_t(*)[32]>(&v[32 * c]));
+                        load_cols<HC>(tb + (uint32_t)(h * HC), v);
                         tmem_wait_ld();
-#pragma unroll
-                        for (int c = 0; c < HC / 32; ++c) tie32(*reinterpret_cast<uint32_t(*)[32]>(&v[32 * c]));
+                        tie_cols<HC>(v);
                         if (h == NH - 1) {
                             tc_fence_before();
                             __syncwarp();
@@ -812,6 +830,7 @@ int launch_bn(const DbGemmArgs& a, int bn, bool pair, const Maps& mp, cudaStream
         return pair ? launch<256, BITS, EPI, FUSED, true, SUB>(a, mp.a, mp.w, mp.y, mp.y_tma, mp.G, s)
                     : launch<256, BITS, EPI, FUSED, false, SUB>(a, mp.a, mp.w, mp.y, mp.y_tma, mp.G, s);
     } else {
+        if (bn == 32) return launch<32, BITS, EPI, FUSED, false, SUB>(a, mp.a, mp.w, mp.y, mp.y_tma, mp.G, s);
         if (bn == 64)
             return pair ? launch<64, BITS, EPI, FUSED, true, SUB>(a, mp.a, mp.w, mp.y, mp.y_tma, mp.G, s)
                         : launch<64, BITS, EPI, FUSED, false, SUB>(a, mp.a, mp.w, mp.y, mp.y_tma, mp.G, s);

@@ -68,7 +68,7 @@ bool cache_lookup(const char* path, const std::string& key, db_gemm_config* out)
     db_gemm_config c{};
     bool found = false;
     while (f >> k >> c.block_n >> c.max_ctas >> c.pair_ctas)
-        if (k == key && (c.block_n == 0 || c.block_n == 64 || c.block_n == 128 || c.block_n == 256) && c.max_ctas >= 0 &&
+        if (k == key && (c.block_n == 0 || c.block_n == 32 || c.block_n == 64 || c.block_n == 128 || c.block_n == 256) && c.max_ctas >= 0 &&
             (c.pair_ctas == 0 || c.pair_ctas == 1)) {  // malformed entries are ignored
             *out = c;
             found = true;  // the last entry for a key wins
@@ -238,9 +238,9 @@ int db_tune_gemm_shape(int64_t M, int64_t N, int64_t K, int bits, int epilogue, 
     std::vector<db_gemm_config> cands;  // baseline first
     if (i8) {
         cands.push_back(db_gemm_i8_default_config(M, N, epilogue));
-        for (int bn : {256, 128, 64})
+        for (int bn : {256, 128, 64, 32})
             for (int pair : {1, 0}) {
-                if ((pair && M <= 128) || (swiglu && bn == 64)) continue;
+                if ((pair && (M <= 128 || bn == 32)) || (swiglu && bn < 128)) continue;
                 if (bn == cands[0].block_n && pair == cands[0].pair_ctas) continue;
                 cands.push_back({bn, 0, pair});
             }

@@ -189,11 +189,11 @@ def test_tensor_core_gemm_bit_exact(db, oracle, wb, ab, m, k, n, path):
 
 
 I8_CONFIGS = [(256, 0, 1), (256, 0, 0), (128, 0, 1), (128, 0, 0), (64, 0, 1), (64, 0, 0), (256, 5, 1), (64, 3, 0),
-              (128, 7, 1)]
+              (128, 7, 1), (32, 0, 0), (32, 5, 0), (32, 0, 1)]
 
 
 @pytest.mark.parametrize("m,k,n", [(200, 1000, 300), (1024, 1024, 3072), (257, 130, 129), (384, 2048, 256),
-                                   (300, 64, 64), (129, 3072, 1024)])
+                                   (300, 64, 64), (129, 3072, 1024), (128, 4096, 2560), (37, 200, 70)])
 @pytest.mark.parametrize("wb", [4, 8])
 def test_i8_tile_configurations_are_bitwise_equal(db, oracle, m, k, n, wb):
     """kind::i8 path: every tile width / pairing / grid cap gives the oracle's bits, for the store

@@ -21,7 +21,7 @@ def test_tune_gemm_candidates_equal_and_cached(tmp_path, M, N, K, bits, epi):
     cands = rep["candidates"]
     # the baseline is the int8 path's default configuration for the shape
     base_cfg = cands[0]["config"]
-    assert base_cfg[0] in (64, 128, 256) and base_cfg[1] == 0 and base_cfg[2] in (0, 1)
+    assert base_cfg[0] in (32, 64, 128, 256) and base_cfg[1] == 0 and base_cfg[2] in (0, 1)
     assert len(cands) == len({tuple(c["config"]) for c in cands}) >= (1 if epi == db.EPILOGUE_SWIGLU else 3)
     assert all(c["equal"] for c in cands)  # every tile configuration is bitwise equal by design
     assert all(c["ms"] > 0 for c in cands)
@@ -41,7 +41,7 @@ def test_tune_cache_ignores_malformed_entries(tmp_path):
     with open(cache, "a") as f:
         f.write(f"{rep['key']} 96 0 0\n")  # not a valid tile width
     choice, rep2 = db.tune_gemm(512, 1024, 512, 4, db.EPILOGUE_STORE, str(cache))
-    assert rep2["cached"] is True and rep2["choice"] in [[bn, 0, p] for bn in (64, 128, 256) for p in (0, 1)]
+    assert rep2["cached"] is True and rep2["choice"] in [[bn, 0, p] for bn in (32, 64, 128, 256) for p in (0, 1)]
     cache.write_text(f"{rep['key']} 96 0 0\n")  # only a malformed entry: tuned again
     _, rep3 = db.tune_gemm(512, 1024, 512, 4, db.EPILOGUE_STORE, str(cache))
     assert rep3["cached"] is False
