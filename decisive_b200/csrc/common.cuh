@@ -89,6 +89,80 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     }
 }
 
+// Tests two mbarrier phases with both tests in flight at once (one asm block: the second test does
+// not wait for the first one's result); bit 0 / bit 1 of the return value: phase of a / b done.
+__device__ __forceinline__ uint32_t mbar_test_wait2(uint64_t* a, uint32_t pa, uint64_t* b, uint32_t pb) {
+    uint32_t ra, rb;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%2], %3;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 q, [%4], %5;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t"
+        "selp.u32 %1, 2, 0, q;\n\t}"
+        : "=r"(ra), "=r"(rb)
+        : "r"(smem_u32(a)), "r"(pa), "r"(smem_u32(b)), "r"(pb)
+        : "memory");
+    return ra | rb;
+}
+// Four phases tested with all four tests in flight; bits 0-3 of the return value.
+__device__ __forceinline__ uint32_t mbar_test_wait4(uint64_t* a, uint32_t pa, uint64_t* b, uint32_t pb, uint64_t* c,
+                                                    uint32_t pc, uint64_t* d, uint32_t pd) {
+    uint32_t ra, rb, rc, rd;
+    asm volatile(
+        "{\n\t.reg .pred p, q, r, s;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%4], %5;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 q, [%6], %7;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 r, [%8], %9;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 s, [%10], %11;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t"
+        "selp.u32 %1, 2, 0, q;\n\t"
+        "selp.u32 %2, 4, 0, r;\n\t"
+        "selp.u32 %3, 8, 0, s;\n\t}"
+        : "=r"(ra), "=r"(rb), "=r"(rc), "=r"(rd)
+        : "r"(smem_u32(a)), "r"(pa), "r"(smem_u32(b)), "r"(pb), "r"(smem_u32(c)), "r"(pc), "r"(smem_u32(d)), "r"(pd)
+        : "memory");
+    return ra | rb | rc | rd;
+}
+// Bounded waits for two or four phases (as mbar_spin, for every barrier given); a phase seen
+// complete stays counted.
+__device__ __forceinline__ bool mbar_spin2(uint64_t* a, uint32_t pa, uint64_t* b, uint32_t pb,
+                                           volatile int* abort_flag, int* err, int code) {
+    uint32_t done = mbar_test_wait2(a, pa, b, pb);
+    if (done == 3u) return true;
+    const uint64_t start = globaltimer();
+    for (uint32_t i = 1;; ++i) {
+        done |= mbar_test_wait2(a, pa, b, pb);
+        if (done == 3u) return true;
+        if ((i & 63u) == 0) {
+            if (*abort_flag) return false;
+            if (globaltimer() - start > DB_WAIT_LIMIT_NS) {
+                *abort_flag = 1;
+                atomicOr(err, code);
+                return false;
+            }
+        }
+    }
+}
+__device__ __forceinline__ bool mbar_spin4(uint64_t* a, uint32_t pa, uint64_t* b, uint32_t pb, uint64_t* c,
+                                           uint32_t pc, uint64_t* d, uint32_t pd, volatile int* abort_flag, int* err,
+                                           int code) {
+    uint32_t done = mbar_test_wait4(a, pa, b, pb, c, pc, d, pd);
+    if (done == 15u) return true;
+    const uint64_t start = globaltimer();
+    for (uint32_t i = 1;; ++i) {
+        done |= mbar_test_wait4(a, pa, b, pb, c, pc, d, pd);
+        if (done == 15u) return true;
+        if ((i & 63u) == 0) {
+            if (*abort_flag) return false;
+            if (globaltimer() - start > DB_WAIT_LIMIT_NS) {
+                *abort_flag = 1;
+                atomicOr(err, code);
+                return false;
+            }
+        }
+    }
+}
+
 // Bounded wait that never suspends the thread (mbarrier.test_wait in a loop): for waits on the
 // critical path, where a thread suspended in try_wait was measured to resume 0.3-1.4 us after the
 // phase completed.  Poll from one lane per warp.

@@ -58,10 +58,7 @@ constexpr int REGS_LAUNCH = 65536 / NUM_THREADS / 8 * 8;
 constexpr int REGS_CONTROL = GI8_REGS_CONTROL;
 constexpr int REGS_EPI = (REGS_LAUNCH * NUM_THREADS - 128 * REGS_CONTROL) / 256 / 8 * 8;
 static_assert(128 * REGS_CONTROL + 256 * REGS_EPI <= REGS_LAUNCH * NUM_THREADS, "register split");
-// How the MMA issuer waits for a free accumulator buffer and the epilogue for a finished job.
-#ifndef GI8_MMA_WAIT
-#define GI8_MMA_WAIT mbar_spin
-#endif
+// How the epilogue waits for a finished job and the producer for free ring slots.
 #ifndef GI8_EPI_WAIT
 #define GI8_EPI_WAIT mbar_spin_polite
 #endif
@@ -339,70 +336,76 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REGS_CONTROL));
         if (warp == 0) {
             // ------------------------------------------------------------ TMA producer
-            // Per stage: the activation and weight tiles; per job (scale block): this CTA's 128
-            // activation scales and the tile's BN weight scales into the scale ring, clipped to
-            // the padded scale rows (ldsa, ldsw; 16-byte multiples).  Lane 0 alone runs the loop:
-            // a warp-wide handshake per wait and per issue (shuffle + syncwarp) was measured to
-            // cost ~250 cycles each, which paced the whole pipeline at ~2,000 cycles per stage.
+            // Two independent issue chains: lane 0 loads the stages (activation and weight tiles),
+            // lane 1 the scale ring (per job: this CTA's 128 activation scales and the tile's BN
+            // weight scales, clipped to the padded scale rows ldsa, ldsw; 16-byte multiples).  An
+            // mbarrier test costs ~200-300 cycles before its result can be used and a copy issue
+            // ~100-150, so one chain of ~14 operations per stage took ~1,900 cycles and paced the
+            // pipeline; the two diverged lanes interleave and hide each other's latency.  No
+            // warp-wide handshake inside the loops.
             if (lane == 0) {
-                int st = 0, issued = 0, jn = 0, sc_issued = 0;
+                int st = 0, issued = 0;
                 uint32_t ps = 0;
                 for (int tile = tile0; tile < tiles; tile += tstride) {
                     const int m0 = (tile % m_tiles) * MT + row_off, n0 = (tile / m_tiles) * BN + wrow_off;
-                    const int ncol0 = (tile / m_tiles) * BN;
-                    const int sa_rows = (int)min((int64_t)BM, ldsa - m0), sw_cols = (int)min((int64_t)BN, ldsw - ncol0);
-                    const uint32_t sc_bytes = (uint32_t)(max(sa_rows, 0) + max(sw_cols, 0)) * 4u;
                     for (int s = 0; s < NS; ++s) {
-                        if (!GI8_PROD_WAIT(&empty[st], ps ^ 1u, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_TMA)) goto drain;
-                        {
-                            uint8_t* sp = smem + S::OFF_STAGE + st * S::STAGE_BYTES;
-                            // full boxes are counted, also where they reach past K or M (zero fill)
-                            constexpr uint32_t TX = S::A_BYTES + (BITS == 8 ? S::B_BYTES : 0);
-                            if (PAIR) {
-                                mbar_arrive_expect_tx_cluster(at_leader(&full[st]), TX);
-                                tma_load_2d_pair(sp, &tmA, at_leader(&full[st]), s * KS, m0);
-                                if (BITS == 8) tma_load_2d_pair(sp + S::A_BYTES, &tmW, at_leader(&full[st]), s * KS, n0);
-                            } else {
-                                mbar_arrive_expect_tx(&full[st], TX);
-                                tma_load_2d(sp, &tmA, &full[st], s * KS, m0);
-                                if (BITS == 8) tma_load_2d(sp + S::A_BYTES, &tmW, &full[st], s * KS, n0);
-                            }
-                            if (BITS == 4) {
-                                mbar_arrive_expect_tx(&wfull[st], S::RAW_BYTES);
-                                tma_load_2d(sp + S::A_BYTES, &tmW, &wfull[st], s * (KS / 2), n0);
-                            }
+                        if (!GI8_PROD_WAIT(&empty[st], ps ^ 1u, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_TMA)) goto stage_drain;
+                        uint8_t* sp = smem + S::OFF_STAGE + st * S::STAGE_BYTES;
+                        // full boxes are counted, also where they reach past K or M (zero fill)
+                        constexpr uint32_t TX = S::A_BYTES + (BITS == 8 ? S::B_BYTES : 0);
+                        if (PAIR) {
+                            mbar_arrive_expect_tx_cluster(at_leader(&full[st]), TX);
+                            tma_load_2d_pair(sp, &tmA, at_leader(&full[st]), s * KS, m0);
+                            if (BITS == 8) tma_load_2d_pair(sp + S::A_BYTES, &tmW, at_leader(&full[st]), s * KS, n0);
+                        } else {
+                            mbar_arrive_expect_tx(&full[st], TX);
+                            tma_load_2d(sp, &tmA, &full[st], s * KS, m0);
+                            if (BITS == 8) tma_load_2d(sp + S::A_BYTES, &tmW, &full[st], s * KS, n0);
+                        }
+                        if (BITS == 4) {
+                            mbar_arrive_expect_tx(&wfull[st], S::RAW_BYTES);
+                            tma_load_2d(sp + S::A_BYTES, &tmW, &wfull[st], s * (KS / 2), n0);
                         }
                         ++issued;
                         if (++st == S::STAGES) { st = 0; ps ^= 1u; }
-                        const int j1 = min((s + 1) * 2 * SUB, GS);
-                        for (int j = s * 2 * SUB; j < j1; ++j, ++jn) {
-                            const int slot = jn % S::SCJ;
-                            if (!GI8_PROD_WAIT(&sc_empty[slot], ((uint32_t)(jn / S::SCJ) & 1u) ^ 1u, abort_flag, dev_error,
-                                               DB_DEV_ERR_TIMEOUT_TMA))
-                                goto drain;
-                            uint8_t* dst = smem + S::OFF_SC + slot * S::SC_SLOT;
-                            mbar_arrive_expect_tx(&sc_full[slot], sc_bytes);
-                            if (sa_rows > 0) bulk_load(dst, sa + (int64_t)j * ldsa + m0, (uint32_t)sa_rows * 4u, &sc_full[slot]);
-                            if (sw_cols > 0)
-                                bulk_load(dst + BM * 4, sw + (int64_t)j * ldsw + ncol0, (uint32_t)sw_cols * 4u, &sc_full[slot]);
-                            ++sc_issued;
-                        }
                     }
                 }
-                goto prod_done;
-            drain:
-                // after an abort: let the stages and scale slots this lane issued land before the CTA
-                // winds down
+                goto stage_done;
+            stage_drain:
+                // after an abort: let the stages this lane issued land before the CTA winds down
                 for (int k = 0; k < issued && k < S::STAGES; ++k) {
                     if (st == 0) { st = S::STAGES - 1; ps ^= 1u; } else --st;
                     if (BITS == 4) mbar_wait_drain(&wfull[st], ps, DRAIN_NS);
                     if (leader) mbar_wait_drain(&full[st], ps, DRAIN_NS);
                 }
+            stage_done:;
+            } else if (lane == 1) {
+                int jn = 0, sc_issued = 0;
+                for (int tile = tile0; tile < tiles; tile += tstride) {
+                    const int m0 = (tile % m_tiles) * MT + row_off, ncol0 = (tile / m_tiles) * BN;
+                    const int sa_rows = (int)min((int64_t)BM, ldsa - m0), sw_cols = (int)min((int64_t)BN, ldsw - ncol0);
+                    const uint32_t sc_bytes = (uint32_t)(max(sa_rows, 0) + max(sw_cols, 0)) * 4u;
+                    for (int j = 0; j < GS; ++j, ++jn) {
+                        const int slot = jn % S::SCJ;
+                        if (!GI8_PROD_WAIT(&sc_empty[slot], ((uint32_t)(jn / S::SCJ) & 1u) ^ 1u, abort_flag, dev_error,
+                                           DB_DEV_ERR_TIMEOUT_TMA))
+                            goto scale_drain;
+                        uint8_t* dst = smem + S::OFF_SC + slot * S::SC_SLOT;
+                        mbar_arrive_expect_tx(&sc_full[slot], sc_bytes);
+                        if (sa_rows > 0) bulk_load(dst, sa + (int64_t)j * ldsa + m0, (uint32_t)sa_rows * 4u, &sc_full[slot]);
+                        if (sw_cols > 0)
+                            bulk_load(dst + BM * 4, sw + (int64_t)j * ldsw + ncol0, (uint32_t)sw_cols * 4u, &sc_full[slot]);
+                        ++sc_issued;
+                    }
+                }
+                goto scale_done;
+            scale_drain:
+                // after an abort: let the scale slots this lane issued land before the CTA winds down
                 for (int k = 0; k < sc_issued && k < S::SCJ; ++k) {
                     const int jj = jn - 1 - k;
                     mbar_wait_drain(&sc_full[jj % S::SCJ], (uint32_t)(jj / S::SCJ) & 1u, DRAIN_NS);
                 }
-            prod_done:;
+            scale_done:;
             }
             __syncwarp();
         } else if (warp == 1) {
@@ -411,6 +414,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             // built once and advanced by the stage / k offsets (start address field, in 16-byte
             // units: shared memory is below 256 KB, so the 14-bit field never carries).
             constexpr uint32_t IDESC = idesc_s8_s32(MT, BN);
+            // the epilogue's steps (jobs per completion wait); with GS a multiple of JPS_E (and
+            // NBUF a multiple of JPS_E) every buffer is always either the last of a step or never
+            // waited on, so only the last jobs of steps need a completion commit
+            constexpr int JPS_E = S::COLS >= 128 ? 1 : 128 / S::COLS;
+            static_assert(S::NBUF % JPS_E == 0, "steps of jobs fall on whole buffer groups");
+            const bool SPARSE_DONE = JPS_E > 1 && GS % JPS_E == 0;
             constexpr int KPJ = 2 / SUB;  // K = 32 MMAs per job
             constexpr int JB = 64 / SUB;  // k bytes per job
             if (leader && lane == 0) {
@@ -422,36 +431,60 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 uint32_t ps = 0;
                 for (int tile = tile0; tile < tiles; tile += tstride) {
                     for (int s = 0; s < NS; ++s) {
-                        if (!mbar_spin(&full[st], ps, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_MMA)) goto mma_end;
-                        if (BITS == 4 && !mbar_spin(&cbf[st], ps, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_MMA))
+                        // the stage's tiles (and, Q4, its converted weights): both tests in flight
+                        if (BITS == 4 ? !mbar_spin2(&full[st], ps, &cbf[st], ps, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_MMA)
+                                      : !mbar_spin(&full[st], ps, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_MMA))
                             goto mma_end;
                         const uint64_t ad = a_desc0 + (uint64_t)((st * S::STAGE_BYTES) >> 4);
                         const uint64_t bd = b_desc0 + (uint64_t)((st * B_STRIDE) >> 4);
                         const int j0 = s * 2 * SUB, j1 = min(j0 + 2 * SUB, GS);
+                        // Each job's buffer must be free and its scale vectors landed (the epilogue
+                        // then needs to wait for the job's completion only).  With four or more
+                        // buffers the stage's jobs are checked together (two jobs' four barriers per
+                        // test); with two (256-wide tiles) the next job's buffer is the one the
+                        // epilogue is reading, so each job waits for its own just before its MMAs.
+                        if (S::NBUF >= 4) {
+                            for (int q = 0; q < j1 - j0; q += 2) {
+                                const int ja = jn + q, jb = ja + 1;
+                                const bool ok =
+                                    q + 1 < j1 - j0
+                                        ? mbar_spin4(&acc_empty[ja % S::NBUF], (uint32_t)(ja / S::NBUF) & 1u,
+                                                     &sc_full[ja % S::SCJ], (uint32_t)(ja / S::SCJ) & 1u,
+                                                     &acc_empty[jb % S::NBUF], (uint32_t)(jb / S::NBUF) & 1u,
+                                                     &sc_full[jb % S::SCJ], (uint32_t)(jb / S::SCJ) & 1u, abort_flag,
+                                                     dev_error, DB_DEV_ERR_TIMEOUT_MMA)
+                                        : mbar_spin2(&acc_empty[ja % S::NBUF], (uint32_t)(ja / S::NBUF) & 1u,
+                                                     &sc_full[ja % S::SCJ], (uint32_t)(ja / S::SCJ) & 1u, abort_flag,
+                                                     dev_error, DB_DEV_ERR_TIMEOUT_MMA);
+                                if (!ok) goto mma_end;
+                            }
+                            tc_fence_after();
+                        }
                         for (int j = j0; j < j1; ++j, ++jn) {
                             const int b = jn % S::NBUF;
-                            // the buffer is free and the job's scale vectors have landed (the epilogue
-                            // then needs to wait for the job's completion only)
-                            if (!GI8_MMA_WAIT(&acc_empty[b], (uint32_t)(jn / S::NBUF) & 1u, abort_flag, dev_error,
-                                              DB_DEV_ERR_TIMEOUT_MMA) ||
-                                !mbar_spin(&sc_full[jn % S::SCJ], (uint32_t)(jn / S::SCJ) & 1u, abort_flag, dev_error,
-                                           DB_DEV_ERR_TIMEOUT_MMA))
-                                goto mma_end;
-                            tc_fence_after();
+                            if (S::NBUF < 4) {
+                                if (!mbar_spin2(&acc_empty[b], (uint32_t)(jn / S::NBUF) & 1u, &sc_full[jn % S::SCJ],
+                                                (uint32_t)(jn / S::SCJ) & 1u, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_MMA))
+                                    goto mma_end;
+                                tc_fence_after();
+                            }
                             const uint32_t d = tmem_base + (uint32_t)(b * BN);
 #pragma unroll
                             for (int kk = 0; kk < KPJ; ++kk) {
                                 const uint64_t off = (uint64_t)(((j - j0) * JB + kk * 32) >> 4);
-                                // accumulate onto the bias the epilogue left in the buffer
                                 const uint32_t acc_in = kk > 0 ? 1u : 0u;  // a job starts from zero
                                 if (PAIR) umma_i8_pair(d, ad + off, bd + off, IDESC, acc_in);
                                 else umma_i8(d, ad + off, bd + off, IDESC, acc_in);
                             }
-                            if (PAIR) {
-                                umma_commit_pair(smem_u32(&done[b]));
-                                umma_commit_pair(at_peer(&done[b]));
-                            } else {
-                                umma_commit(&done[b]);
+                            // completion is signalled where the epilogue waits: every job, or (steps
+                            // of JPS_E jobs dividing the tile) the last job of each step
+                            if (!SPARSE_DONE || jn % JPS_E == JPS_E - 1) {
+                                if (PAIR) {
+                                    umma_commit_pair(smem_u32(&done[b]));
+                                    umma_commit_pair(at_peer(&done[b]));
+                                } else {
+                                    umma_commit(&done[b]);
+                                }
                             }
                         }
                         if (PAIR) {
