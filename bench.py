@@ -566,7 +566,7 @@ def run_gemm(args, local_rank):
     x = np.random.default_rng(0).normal(0, 1, (m, k)).astype(np.float16)
     codes, scales = db.pack_weights(torch.from_numpy(w.view(np.int16)).cuda(), args.bits)
     xt = torch.from_numpy(x).cuda()
-    layout = db.CODES_TC if args.layout == "tc" else db.CODES_NATURAL
+    layout = {"tc": db.CODES_TC, "dq": db.CODES_DQ}.get(args.layout, db.CODES_NATURAL)
     a, sa, _ = db.quantize_activations(xt, bits=8, layout=layout)
     y = torch.empty((m, n), dtype=torch.float32, device="cuda")
     flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device="cuda")
@@ -735,8 +735,9 @@ def main():
     ap.add_argument("--gemv-rows", default="1,4,8", help="activation rows (M) for --workload gemv")
     ap.add_argument("--gemm-shape", default="1024,1024,3072", help="M,K,N for --workload gemm")
     ap.add_argument("--bits", type=int, default=4)
-    ap.add_argument("--layout", default="i8", choices=["i8", "tc"],
-                    help="activation codes of --workload gemm: int8 (kind::i8 kernel) or f16 (kind::f16 kernel)")
+    ap.add_argument("--layout", default="i8", choices=["i8", "tc", "dq"],
+                    help="activation codes of --workload gemm: int8 (kind::i8 kernel), f16 codes (kind::f16 "
+                         "kernel) or dequantised f16 (kind::f16 full-K kernel)")
     ap.add_argument("--gemm-config", default="", help="block_n,max_ctas,pair_ctas for --workload gemm")
     ap.add_argument("--c4-mode", type=int, default=0, choices=[0, 1], help="--workload c4: 0 W8A8, 1 W8A32")
     args = ap.parse_args()

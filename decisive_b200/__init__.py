@@ -19,7 +19,7 @@ from . import _lib
 from ._lib import CudaError, check, load
 
 GROUP = 64
-CODES_NATURAL, CODES_GEMV, CODES_TC = 0, 1, 2
+CODES_NATURAL, CODES_GEMV, CODES_TC, CODES_DQ = 0, 1, 2, 3
 DTYPES = {"float32": 0, "float16": 1, "bfloat16": 2}
 
 
@@ -50,7 +50,7 @@ def quantize_activations(x, bits: int = 8, layout: int = CODES_TC, sums: bool = 
     M, K = x.shape
     Kp = padded(K)
     G = Kp // GROUP
-    dt = torch.float16 if layout == CODES_TC else torch.int8
+    dt = torch.float16 if layout in (CODES_TC, CODES_DQ) else torch.int8
     codes = torch.zeros((M, Kp), dtype=dt, device=x.device)
     lds = scale_stride(max(M, 1))
     scales = torch.zeros((G, lds), dtype=torch.float32, device=x.device)
@@ -105,11 +105,13 @@ class GemmConfig(C.Structure):
 def gemm(a_codes, layout, sa, w_codes, sw, M, N, K, bits, fused=True, a_sums=None, residual=None, nonfinite=None,
          config=None):
     """Matrix::apply_prepared (int8.rs:229-288) on prepared activations -> y f32 [M, N].
-    config: optional GemmConfig (tile configuration of the tensor-core path)."""
+    config: optional GemmConfig (tile configuration of the tensor-core path).  CODES_DQ: a_codes are
+    the dequantised f16 activations (sa may be None); the kind::f16 full-K GEMM (tolerance numerics)."""
     import torch
     y = residual if residual is not None else torch.empty((M, N), dtype=torch.float32, device=w_codes.device)
     cfg = C.byref(config) if config is not None else None
-    check(load().db_gemm_g64_config(_ptr(a_codes), layout, a_codes.stride(0), _ptr(sa), _ptr(a_sums), sa.stride(0),
+    check(load().db_gemm_g64_config(_ptr(a_codes), layout, a_codes.stride(0), _ptr(sa), _ptr(a_sums),
+                                    sa.stride(0) if sa is not None else 0,
                                     _ptr(w_codes), _ptr(sw), M, N, K, bits, int(fused), int(residual is not None),
                                     _ptr(y), N, _ptr(nonfinite), cfg, _stream()))
     return y

@@ -16,7 +16,7 @@ CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libdecisive_b200.so")
 SOURCES = ["gemm_i8_q4.cu", "gemm_i8_q8.cu", "gemm_i8_swiglu.cu", "gemm_i8.cu", "quant.cu", "gemm_tc.cu", "gemv.cu", "layer_ops.cu", "attention_tc.cu", "capi.cu", "model.cu", "noalloc.cu",
-           "tuner.cu", "packed_io.cu", "bert.cu", "decima_w8a32.cu"]
+           "tuner.cu", "packed_io.cu", "bert.cu", "decima_w8a32.cu", "gemm_dq.cu"]
 HEADERS = ["gemm_i8.cuh", "common.cuh", "kernels.h", "layer_ops.h", "capi_internal.h", "packed_io.h"]
 PUBLIC_HEADER = os.path.join(os.path.dirname(HERE), "include", "decisive_b200.h")
 

@@ -82,7 +82,7 @@ static inline int64_t groups_of(int64_t K) { return (K + DB_GROUP - 1) / DB_GROU
 int db_quantize_activations_g64(const void* x, int dtype, int64_t ldx, int64_t M, int64_t K, int bits, void* codes,
                                 int layout, int64_t ldc, float* scales, int32_t* sums, int64_t lds, int* nonfinite,
                                 void* stream) {
-    if (M < 0 || K <= 0 || (bits != 4 && bits != 8) || dtype < 0 || dtype > 2 || layout < 0 || layout > 2)
+    if (M < 0 || K <= 0 || (bits != 4 && bits != 8) || dtype < 0 || dtype > 2 || layout < 0 || layout > DB_CODES_DQ)
         return db_fail(DB_ERR_INVALID_ARGUMENT, "INVALID_ARGUMENT", "quantize: bad shape, bits, dtype or layout");
     if (ldx < K || ldc < groups_of(K) * DB_GROUP || lds < M || !x || !codes || !scales)
         return db_fail(DB_ERR_INVALID_ARGUMENT, "INVALID_ARGUMENT", "quantize: bad strides or null pointer");
@@ -161,9 +161,10 @@ int db_gemm_g64_config(const void* a_codes, int layout, int64_t lda, const float
     if (config && ((config->block_n != 0 && config->block_n != 64 && config->block_n != 128 && config->block_n != 256 &&
                     !(config->block_n == 32 && layout == DB_CODES_NATURAL)) ||
                    config->max_ctas < 0 ||
-                   (config->pair_ctas != 0 && config->pair_ctas != 1)))
+                   (config->pair_ctas != 0 && config->pair_ctas != 1) ||
+                   (config->pair_ctas && layout == DB_CODES_DQ)))
         return db_fail(DB_ERR_INVALID_ARGUMENT, "INVALID_ARGUMENT", "gemm: bad tile configuration");
-    if (M < 0 || N <= 0 || K <= 0 || (bits != 4 && bits != 8) || ldy < N || ldsa < M)
+    if (M < 0 || N <= 0 || K <= 0 || (bits != 4 && bits != 8) || ldy < N || (layout != DB_CODES_DQ && ldsa < M))
         return db_fail(DB_ERR_INVALID_ARGUMENT, "INVALID_ARGUMENT", "gemm: bad shape");
     if (M == 0) return DB_OK;
     if (layout == DB_CODES_GEMV) {
@@ -173,7 +174,7 @@ int db_gemm_g64_config(const void* a_codes, int layout, int64_t lda, const float
                      bits, fused, residual, y, ldy, nonfinite};
         return db_cuda_status(db_launch_gemv(g, S(stream)), "gemv");
     }
-    if (layout != DB_CODES_TC && layout != DB_CODES_NATURAL)
+    if (layout != DB_CODES_TC && layout != DB_CODES_NATURAL && layout != DB_CODES_DQ)
         return db_fail(DB_ERR_INVALID_ARGUMENT, "INVALID_ARGUMENT", "gemm: unknown code layout");
     DbGemmArgs a{};
     a.a_codes = a_codes;
@@ -197,6 +198,7 @@ int db_gemm_g64_config(const void* a_codes, int layout, int64_t lda, const float
         a.max_ctas = config->max_ctas;
         a.pair_ctas = config->pair_ctas;
     }
+    if (layout == DB_CODES_DQ) return db_cuda_status(db_launch_gemm_dq(a, S(stream)), "gemm");
     if (layout == DB_CODES_NATURAL) {
         if (!config) {
             const db_gemm_config d = db_gemm_i8_default_config(M, N, a.epilogue);

@@ -11,7 +11,9 @@ __host__ __device__ inline int64_t db_scale_stride(int64_t n) { return (n + 127)
 // element types of activation inputs
 enum { DB_F32 = 0, DB_F16 = 1, DB_BF16 = 2 };
 // activation code layouts
-enum { DB_CODES_NATURAL_I8 = 0, DB_CODES_GEMV_I8 = 1, DB_CODES_TC_F16 = 2 };
+// DB_CODES_DQ_F16: f16 [M, Kp], natural k order, each value f16(code * group scale) (the
+// dequantised activations of the kind::f16 full-K GEMM, gemm_dq.cu)
+enum { DB_CODES_NATURAL_I8 = 0, DB_CODES_GEMV_I8 = 1, DB_CODES_TC_F16 = 2, DB_CODES_DQ_F16 = 3 };
 // GEMM epilogues
 enum { DB_EPI_STORE = 0, DB_EPI_RESIDUAL = 1, DB_EPI_SWIGLU_QUANT = 2 };
 
@@ -70,6 +72,7 @@ struct DbGemmArgs {
     int block;             // K values per scale group: 0 or 64 (group 64), 32 (Decima int8 blocks, Q8 only)
     const float* bias;     // add_bias = 1: y = acc + bias[n] (bias == nullptr: y = acc + 0)
     int add_bias;
+    void* w_scratch;       // dequantised GEMM: f16 [N, Kp] for the unpacked weights (null: cached buffer)
 };
 int db_launch_gemm_tc(const DbGemmArgs& args, cudaStream_t stream);
 // The same GEMM on int8 activation codes in natural order (DB_CODES_NATURAL_I8, a_codes [M, lda]
@@ -77,6 +80,13 @@ int db_launch_gemm_tc(const DbGemmArgs& args, cudaStream_t stream);
 // (default 256; the SwiGLU epilogue always 256, writing int8 natural codes to out_codes),
 // optional CTA pairs (M = 256 MMAs), scale blocks of 64 or (Q8 only) 32.
 int db_launch_gemm_i8(const DbGemmArgs& args, cudaStream_t stream);
+// The GEMM on dequantised operands (gemm_dq.cu): a_codes f16 [M, lda] in DB_CODES_DQ_F16
+// (sa unused); an unpack pass writes the weights as f16(code * scale) [N, Kp] into w_scratch
+// (db_gemm_dq_scratch_bytes; null: a library buffer cached per device and stream), then tcgen05 kind::f16
+// with f32 accumulation over the whole K; store or residual epilogue, tile widths 64/128/256.
+int db_launch_gemm_dq(const DbGemmArgs& args, cudaStream_t stream);
+int db_gemm_dq_default_block_n(int64_t M, int64_t N);
+size_t db_gemm_dq_scratch_bytes(int64_t N, int64_t K);
 
 // Small-M path: int8 A codes (GEMV order) [M, lda] + sums [G, ldsa], sa [G, ldsa].
 struct DbGemvArgs {

@@ -1,6 +1,6 @@
 // Elementwise / row kernels around the projections of one encoder layer:
 //   rms_quantize   RMSNorm (cpu.rs:310-333) fused with the group-64 activation quantiser
-//                  (int8.rs:178-202), writing tensor-core or GEMV code layouts
+//                  (int8.rs:178-202), writing tensor-core, GEMV, natural or dequantised layouts
 //   qk_norm_rope   per-head RMSNorm of q and k (backbone.rs:519-520) + rotate-half RoPE
 //                  (backbone.rs:471-483) from a host-computed cos/sin table, f16 outputs
 //   mean_pool      sequential mean over tokens of the final hidden rows
@@ -94,6 +94,14 @@ __global__ void rms_quantize_kernel(const float* __restrict__ x, int64_t ldx, co
         pk.x = *reinterpret_cast<uint32_t*>(&h0);
         pk.y = *reinterpret_cast<uint32_t*>(&h1);
         *reinterpret_cast<uint2*>(static_cast<__half*>(codes) + (size_t)t * ldc + b8 + (odd ? 4 : 0)) = pk;
+    } else if (layout == DB_CODES_DQ_F16) {
+        // dequantised, natural order: f16(code * group scale) of k = c..c+3
+        const __half2 h0 = __halves2half2(__float2half_rn(__fmul_rn((float)q[0], gs)), __float2half_rn(__fmul_rn((float)q[1], gs)));
+        const __half2 h1 = __halves2half2(__float2half_rn(__fmul_rn((float)q[2], gs)), __float2half_rn(__fmul_rn((float)q[3], gs)));
+        uint2 pk;
+        pk.x = *reinterpret_cast<const uint32_t*>(&h0);
+        pk.y = *reinterpret_cast<const uint32_t*>(&h1);
+        *reinterpret_cast<uint2*>(static_cast<__half*>(codes) + (size_t)t * ldc + c) = pk;
     } else if (layout == DB_CODES_GEMV_I8) {
         // stored order k0,k2,k4,k6 | k1,k3,k5,k7
         const int e = odd ? 1 : 0;

@@ -10,6 +10,7 @@
 //                 the stored order is k = 0,4,1,5,2,6,3,7 (matches the nibble extraction of the GEMM)
 //   activation codes, GEMV order: int8 [M, Kp]; inside every 8 consecutive k: 0,2,4,6,1,3,5,7
 //   activation codes, natural order: int8 [M, Kp] (reference Scratch::values, int8.rs:7-11)
+//   dequantised activations: f16 [M, Kp], natural order, f16(code * group scale)
 //   activation scales f32 [G, lds] and code sums int32 [G, lds]; the tensor-core GEMM needs
 //                 lds >= roundup(M, 128) and lds % 4 == 0 (bulk-copied per 128-row tile)
 // Kp = ceil(K/64)*64; padding codes are 0 (nibble 8).
@@ -67,6 +68,11 @@ __global__ void quantize_rows_kernel(const void* __restrict__ x, int dtype, int6
         __half* out = static_cast<__half*>(codes) + (size_t)m * ldc;
         out[code_position(layout, k0)] = __float2half_rn(c0);
         out[code_position(layout, k0 + 1)] = __float2half_rn(c1);
+    } else if (layout == DB_CODES_DQ_F16) {
+        // dequantised: each code times its group scale, rounded to f16 (natural order)
+        __half* out = static_cast<__half*>(codes) + (size_t)m * ldc;
+        out[k0] = __float2half_rn(__fmul_rn((float)(int)c0, scale));  // a zero code is +0
+        out[k0 + 1] = __float2half_rn(__fmul_rn((float)(int)c1, scale));
     } else {
         int8_t* out = static_cast<int8_t*>(codes) + (size_t)m * ldc;
         out[code_position(layout, k0)] = (int8_t)(int)c0;

@@ -48,6 +48,8 @@ extern "C" {
  *   DB_CODES_NATURAL  int8 [M, Kp], k in order (reference Scratch::values, int8.rs:7-11)
  *   DB_CODES_GEMV     int8 [M, Kp], inside each 8 consecutive k stored as k0,k2,k4,k6,k1,k3,k5,k7
  *   DB_CODES_TC       f16  [M, Kp] integer-valued, inside each 8 stored as k0,k4,k1,k5,k2,k6,k3,k7
+ *   DB_CODES_DQ       f16  [M, Kp] dequantised values f16(code * group scale), k in order: the
+ *                     operand of the dequantised-operand GEMM (no grouped fold; see db_gemm_g64)
  * Kp = ceil(K/64)*64; activation scales f32 [G, lds], sums int32 [G, lds], G = Kp/64.
  * DB_LAYOUT: weight codes Q4 [N, Kp/2] bytes (low nibble = even k, nibble = code+8, i.e. the
  * code bytes of packed.rs:22-28), Q8 [N, Kp] int8; weight scales f32 [G, Ns] with
@@ -56,6 +58,7 @@ extern "C" {
 #define DB_CODES_NATURAL 0
 #define DB_CODES_GEMV 1
 #define DB_CODES_TC 2
+#define DB_CODES_DQ 3
 
 int db_abi_version(void);
 /* row stride (elements) of a scale array with n columns: roundup(n, 128) */
@@ -104,7 +107,15 @@ int db_dequant_rows_g64(const uint8_t *codes, const float *scales, int64_t N, in
  * M <= db_gemv_max_rows();
  * a_sums is required by the GEMV layout with Q4 weights.  fused: 1 = AVX2 numerics (fma),
  * 0 = portable numerics.  residual: 1 adds into y.  nonfinite (optional): when *nonfinite != 0
- * every output is NaN (int8.rs:170-173). */
+ * every output is NaN (int8.rs:170-173).
+ * DB_CODES_DQ (dequantised mode, the numerics of the reference's WGSL GEMMs, which dequantise the
+ * weights and accumulate in f32): a_codes f16 [M, lda] from the quantiser's DB_CODES_DQ layout
+ * (lda % 8 == 0; sa, ldsa and fused unused); the weights are unpacked to f16(code * scale) into
+ * a library scratch buffer (N x Kp f16, kept per device and stream and grown when a call needs
+ * more; growing is refused while the stream is being captured) and y = the tcgen05 kind::f16 sum
+ * over all K in f32.  Not bit-exact against the grouped fold: within ~1.5e-3 of the output RMS
+ * (the contract is 2e-3); every tile configuration gives the same bits.  Single CTAs only
+ * (pair_ctas 0). */
 int db_gemm_g64(const void *a_codes, int layout, int64_t lda, const float *sa, const int32_t *a_sums, int64_t ldsa,
                 const uint8_t *w_codes, const float *sw, int64_t M, int64_t N, int64_t K, int bits, int fused,
                 int residual, float *y, int64_t ldy, const int *nonfinite, void *stream);
