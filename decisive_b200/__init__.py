@@ -548,8 +548,9 @@ class Model:
         check(load().db_model_use_graphs(self._h, int(enable)))
 
     def set_code_layout(self, layout: int):
-        """CODES_NATURAL (int8 codes, kind::i8 GEMM; default) or CODES_TC (f16 codes, kind::f16 GEMM);
-        bit-identical outputs either way."""
+        """CODES_NATURAL (int8 codes, kind::i8 GEMM; default) or CODES_TC (f16 codes, kind::f16 GEMM),
+        bit-identical outputs either way; or CODES_DQ (dequantised f16 operands, full-K f32
+        accumulation: within the contract's tolerance, not bit-identical)."""
         check(load().db_model_set_code_layout(self._h, int(layout)))
 
     def profile(self, enable: bool = True):

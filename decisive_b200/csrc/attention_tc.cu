@@ -547,7 +547,21 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
                     }
                     const float scale = fmaxf(__fdiv_rn(amax, 127.f), FLT_MIN);
                     const float rinv = __fdiv_rn(1.f, scale);
-                    if (codes_i8) {
+                    if (codes_i8 == 2) {
+                        // dequantised: f16(code * scale) in natural order (a zero code is +0)
+                        __half* dst = static_cast<__half*>(codes) + orow * ldc + h * AT_D + 64 * b;
+#pragma unroll
+                        for (int g8 = 0; g8 < 8; ++g8) {
+                            uint32_t hw[4];
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                const float c0 = fminf(fmaxf(rintf(__fmul_rn(v[8 * g8 + 2 * e], rinv)), -127.f), 127.f);
+                                const float c1 = fminf(fmaxf(rintf(__fmul_rn(v[8 * g8 + 2 * e + 1], rinv)), -127.f), 127.f);
+                                hw[e] = pack_f16x2(__fmul_rn((float)(int)c0, scale), __fmul_rn((float)(int)c1, scale));
+                            }
+                            *reinterpret_cast<uint4*>(dst + 8 * g8) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+                        }
+                    } else if (codes_i8) {
                         // int8 codes in natural order
                         int8_t* dst = static_cast<int8_t*>(codes) + orow * ldc + h * AT_D + 64 * b;
 #pragma unroll
@@ -631,7 +645,8 @@ namespace {
 int check_io(const __half* q16, const __half* k16, const __half* v16, int Hq, int Hk, float* out, int64_t ldo,
              void* codes, int64_t ldc, float* scales, int* nonfinite, int codes_i8) {
     const bool quant = codes != nullptr;
-    if (Hk <= 0 || Hq % Hk || Hq > 65535 || (quant && (!scales || !nonfinite || (ldc & (codes_i8 ? 15 : 7)))) ||
+    if (Hk <= 0 || Hq % Hk || Hq > 65535 || codes_i8 < 0 || codes_i8 > 2 ||
+        (quant && (!scales || !nonfinite || (ldc & (codes_i8 == 1 ? 15 : 7)))) ||
         (!quant && (!out || (ldo & 3))))
         return (int)cudaErrorInvalidValue;
     if ((reinterpret_cast<uintptr_t>(q16) | reinterpret_cast<uintptr_t>(k16) | reinterpret_cast<uintptr_t>(v16)) & 15)

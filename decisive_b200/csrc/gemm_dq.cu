@@ -13,8 +13,8 @@
 // configurations are bitwise equal to each other.
 //
 // Two kernels per call:
-//   unpack   Q4 / Q8 device codes + f32 group scales -> w' f16 [N, Kp] (natural k order), one
-//            coalesced 16-byte load of codes per thread; the weights stay 4 / 8 bits in HBM and
+//   unpack   Q4 / Q8 device codes + f32 group scales -> w' f16 [N, Kp] (natural k order), with
+//            coalesced loads and 16-byte stores; the weights stay 4 / 8 bits in HBM and
 //            w' (at most tens of MB) is written to, and re-read from, the 126 MB L2.  Each weight
 //            is unpacked once per call: a converter inside the GEMM would redo it for every row
 //            tile (8 times at M = 1024), and clock64 traces of such a kernel (converter warps
@@ -122,31 +122,27 @@ __device__ __forceinline__ uint4 q8_words_to_f16(uint32_t w0, uint32_t w1, Scale
     return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
-// Unpack pass: thread i handles 16 bytes of codes of one weight row (32 Q4 or 16 Q8 weights, inside
-// one scale group), consecutive threads consecutive bytes of the row.  w' [N, Kp] f16.
+// Unpack pass: thread i writes the 16 bytes (8 weights) of one 8-k chunk of a weight row,
+// consecutive threads consecutive chunks, so a warp reads 128 (Q4) or 256 (Q8) contiguous bytes of
+// codes and writes 512 contiguous bytes of w' [N, Kp] f16.
 template <int BITS>
 __global__ void __launch_bounds__(256) unpack_weights_kernel(const uint8_t* __restrict__ codes,
                                                              const float* __restrict__ sw, int64_t ldsw, int N,
                                                              int Kp, __half* __restrict__ out) {
     pdl_wait();
-    const int row_bytes = Kp * BITS / 8, per_row = row_bytes / 16;
+    const int per_row = Kp / 8;
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i < (int64_t)N * per_row) {
         const int n = (int)(i / per_row), c = (int)(i % per_row);
-        constexpr int KPT = 16 * 8 / BITS;  // weights per thread: 32 (Q4) or 16 (Q8)
-        const int k0 = c * KPT;
-        const uint4 v = __ldg(reinterpret_cast<const uint4*>(codes + (size_t)n * row_bytes) + c);
-        const Scale2 s = split_scale(__ldg(sw + (int64_t)(k0 / 64) * ldsw + n));
-        uint4* dst = reinterpret_cast<uint4*>(out + (size_t)n * Kp + k0);
+        const Scale2 s = split_scale(__ldg(sw + (int64_t)(c / 8) * ldsw + n));
+        uint4 o;
         if (BITS == 4) {
-            dst[0] = q4_word_to_f16(v.x, s);
-            dst[1] = q4_word_to_f16(v.y, s);
-            dst[2] = q4_word_to_f16(v.z, s);
-            dst[3] = q4_word_to_f16(v.w, s);
+            o = q4_word_to_f16(__ldg(reinterpret_cast<const uint32_t*>(codes + (size_t)n * (Kp / 2)) + c), s);
         } else {
-            dst[0] = q8_words_to_f16(v.x, v.y, s);
-            dst[1] = q8_words_to_f16(v.z, v.w, s);
+            const uint2 v = __ldg(reinterpret_cast<const uint2*>(codes + (size_t)n * Kp) + c);
+            o = q8_words_to_f16(v.x, v.y, s);
         }
+        reinterpret_cast<uint4*>(out + (size_t)n * Kp)[c] = o;
     }
     pdl_trigger();
 }
@@ -415,25 +411,16 @@ int launch_bn(const DbGemmArgs& a, int bn, const CUtensorMap& tmA, const CUtenso
 }  // namespace gdq
 }  // namespace db
 
-// Tile width of the dequantised GEMM when none is given: the widest tile that still occupies the
-// SMs (each candidate scored by the fill of its last wave of CTAs, with a small preference for
-// wide tiles, which re-read A less and issue fewer MMAs per output).
+// Tile width of the dequantised GEMM when none is given: the widest tile that still gives at
+// least 96 tiles (two thirds of the SMs); persistent CTAs overlap a tile's epilogue with the next
+// tile's MMAs, so a partial last wave costs less than narrower tiles do (measured on the C2
+// projections: 256 for N = 3072, 4096, 6144 at M = 1024, 64 for N = 1024).
 int db_gemm_dq_default_block_n(int64_t M, int64_t N) {
-    const int sms = db_num_sms();
-    const int cands[3] = {256, 128, 64};
-    double best = -1.0;
-    int out = 256;
-    for (int bn : cands) {
-        const int64_t ctas = ((M + 127) / 128) * ((N + bn - 1) / bn);
-        const int64_t waves = (ctas + sms - 1) / sms;
-        const double fill = (double)ctas / (double)(waves * sms);
-        const double score = fill * (bn == 256 ? 1.0 : bn == 128 ? 0.97 : 0.88);
-        if (score > best + 1e-9) {
-            best = score;
-            out = bn;
-        }
+    const int64_t mt = (M + 127) / 128;
+    for (int bn : {256, 128}) {
+        if (mt * ((N + bn - 1) / bn) >= 96) return bn;
     }
-    return out;
+    return 64;
 }
 
 size_t db_gemm_dq_scratch_bytes(int64_t N, int64_t K) { return (size_t)N * ((K + 63) / 64 * 64) * 2; }
@@ -490,7 +477,7 @@ int db_launch_gemm_dq(const DbGemmArgs& a, cudaStream_t stream) {
     __half* wq = static_cast<__half*>(scratch);
     int rc = 0;
     {
-        const int64_t threads = (int64_t)a.N * (Kp * a.bits / 8 / 16);
+        const int64_t threads = (int64_t)a.N * (Kp / 8);
         const dim3 grid((unsigned)((threads + 255) / 256));
         const cudaError_t e = a.bits == 4
                                   ? db_launch_pdl(unpack_weights_kernel<4>, grid, dim3(256), 0, stream, a.w_codes, a.sw,

@@ -18,13 +18,18 @@ int db_launch_mean_pool(const float* x, int64_t ldx, int T, int D, float* out, c
 int db_launch_mean_pool_varlen(const float* x, int64_t ldx, const int* cu_seqlens, int nseq, int D, float* out,
                                cudaStream_t stream);
 int db_launch_fill_nan_if(float* y, int64_t n, const int* flag, cudaStream_t stream);
+// SwiGLU + group-64 re-quantisation of a gate/up projection stored as f32 [R, 2F] (blocks of 64
+// gate then 64 up columns) into dequantised f16 activations [R, ldo] (DB_CODES_DQ_F16).
+int db_launch_swiglu_quantize_dq(const float* gu, int64_t ld, int R, int F, __half* out, int64_t ldo, int* nonfinite,
+                                 cudaStream_t stream);
 
 // Non-causal GQA attention over head_dim 128: q16 [T, Hq, 128], k16/v16 [T, Hk, 128] (f16),
 // out f32 [T, Hq*128] with row stride ldo.  scale multiplies q.k before the softmax.
 int db_launch_attention(const __half* q16, const __half* k16, const __half* v16, int T, int Hq, int Hk, float scale,
                         float* out, int64_t ldo, cudaStream_t stream);
 // Same attention, writing the context already quantised for the output projection: f16 codes in
-// tensor-core order [T, ldc], or with codes_i8 int8 codes in natural order [T, ldc] (ldc % 16 == 0)
+// tensor-core order [T, ldc], or with codes_i8 = 1 int8 codes in natural order [T, ldc] (ldc % 16 == 0),
+// or with codes_i8 = 2 dequantised f16 values f16(code * scale) in natural order (DB_CODES_DQ_F16)
 // (head h occupies features 128h..128h+127), per-64 scales [2*Hq, lds]; *nonfinite is raised
 // when a context value is not finite.
 int db_launch_attention_quant(const __half* q16, const __half* k16, const __half* v16, int T, int Hq, int Hk,

@@ -105,6 +105,12 @@ struct db_model {
     // activation codes of the projections: int8 natural order through the kind::i8 GEMM (default),
     // or f16 codes through the kind::f16 GEMM (db_model_set_code_layout)
     bool i8 = true;
+    // dequantised mode (DB_CODES_DQ): the layers' projections take f16(code * scale) activations
+    // through the full-K kind::f16 GEMM (gemm_dq.cu); dq_w holds the unpacked weights of one
+    // projection, gu32 the f32 gate/up output before the SwiGLU re-quantisation
+    bool dq = false;
+    void* dq_w = nullptr;
+    float* gu32 = nullptr;
     // per-launch CUDA-event profiling (mirror of the reference's projection_ms accounting,
     // cpu.rs:8-16 / native.rs:229-258), enabled by db_model_profile
     bool profile = false;
@@ -240,7 +246,8 @@ int ensure_workspace(db_model* m, int T) {
         m->alloc(&m->sa, (size_t)Gmax * db_scale_stride(T), v) || m->alloc(&m->sh, (size_t)(F / 64) * db_scale_stride(T), v) ||
         m->alloc(&m->acodes, (size_t)T * Kmax, v) || m->alloc(&m->hcodes, (size_t)T * F, v) ||
         m->alloc(&m->q16, (size_t)T * m->Nq(), v) || m->alloc(&m->k16, (size_t)T * m->Nk(), v) ||
-        m->alloc(&m->v16, (size_t)T * m->Nk(), v) || m->alloc(&m->ids, T, v) || m->alloc(&m->flag, 4, v))
+        m->alloc(&m->v16, (size_t)T * m->Nk(), v) || m->alloc(&m->ids, T, v) || m->alloc(&m->flag, 4, v) ||
+        (m->dq && m->alloc(&m->gu32, (size_t)T * 2 * F, v)))
         return db_fail(DB_ERR_CUDA, "RESOURCE_LIMIT", "workspace exceeds device limits");
     m->cap_T = T;
     return ensure_rope(m, T);
@@ -364,9 +371,14 @@ int enqueue_forward(db_model* m, int T, const volatile uint8_t* cancel, const Pa
     rc = timed(0, [&] {
         return db_launch_dequant_rows(m->emb_c, m->emb_s, c.vocab, D, bits, m->ids, R, m->x, D, m->flag, st);
     });
-    const int code_layout = m->i8 ? DB_CODES_NATURAL_I8 : DB_CODES_TC_F16;
+    const int code_layout = m->dq ? DB_CODES_DQ_F16 : m->i8 ? DB_CODES_NATURAL_I8 : DB_CODES_TC_F16;
+    const int attn_codes = m->dq ? 2 : m->i8 ? 1 : 0;  // the attention's quantised output layout
     // one projection; the tuned tile configuration, else the i8 path's default for the shape
     auto launch = [&](int proj, DbGemmArgs& g) {
+        if (m->dq) {
+            g.w_scratch = m->dq_w;
+            return db_launch_gemm_dq(g, st);
+        }
         g.block_n = m->tuned[proj].block_n;
         g.max_ctas = m->tuned[proj].max_ctas;
         g.pair_ctas = m->tuned[proj].pair_ctas;
@@ -454,15 +466,15 @@ int enqueue_forward(db_model* m, int T, const volatile uint8_t* cancel, const Pa
                 if (!c.causal && pass && pass->cu)
                     return db_launch_attention_varlen(m->q16, m->k16, m->v16, pass->cu, pass->nseq, pass->max_len, R,
                                                       c.q_heads, c.kv_heads, attn_scale, nullptr, 0, m->acodes,
-                                                      ld_codes, m->sa, lds, m->flag, st, m->i8);
+                                                      ld_codes, m->sa, lds, m->flag, st, attn_codes);
                 if (!c.causal && !pass)
                     return db_launch_attention_quant(m->q16, m->k16, m->v16, T, c.q_heads, c.kv_heads, attn_scale,
-                                                     m->acodes, ld_codes, m->sa, lds, m->flag, st, m->i8);
+                                                     m->acodes, ld_codes, m->sa, lds, m->flag, st, attn_codes);
                 return db_launch_attention_prefix_quant(m->q16, own_k(l), own_v(l), items, T,
                                                         pass && pass->pk ? pass->pk[l] : nullptr,
                                                         pass && pass->pv ? pass->pv[l] : nullptr, P, c.causal,
                                                         c.q_heads, c.kv_heads, attn_scale,
-                                                        m->acodes, ld_codes, m->sa, lds, m->flag, st, m->i8);
+                                                        m->acodes, ld_codes, m->sa, lds, m->flag, st, attn_codes);
             });
         if (!rc) rc = timed(6, [&] { return gemm(1, m->acodes, w.o_c, w.o_s, m->sa, D, Nq, DB_EPI_RESIDUAL, m->x, D); });
         if (!rc)
@@ -470,8 +482,13 @@ int enqueue_forward(db_model* m, int T, const volatile uint8_t* cancel, const Pa
                 return db_launch_rms_quantize(m->x, D, w.post_norm, R, D, c.eps, 0, nullptr, 0, m->acodes, code_layout,
                                               ld_codes, m->sa, nullptr, lds, m->flag, st);
             });
-        if (!rc)
+        if (!rc && m->dq) {
+            // dequantised mode: the gate/up projection in f32, then SwiGLU + re-quantisation
+            rc = timed(7, [&] { return gemm(2, m->acodes, w.gu_c, w.gu_s, m->sa, 2 * F, D, DB_EPI_STORE, m->gu32, 2 * F); });
+            if (!rc) rc = timed(1, [&] { return db_launch_swiglu_quantize_dq(m->gu32, 2 * F, R, F, m->hcodes, F, m->flag, st); });
+        } else if (!rc) {
             rc = timed(7, [&] { return gemm(2, m->acodes, w.gu_c, w.gu_s, m->sa, 2 * F, D, DB_EPI_SWIGLU_QUANT, nullptr, 0); });
+        }
         if (!rc) rc = timed(8, [&] {
             DbGemmArgs g{};
             g.a_codes = m->hcodes;
@@ -1004,12 +1021,33 @@ int db_predict_batch(db_model* m, const int32_t* const* ids, const size_t* lens,
 }
 
 int db_model_set_code_layout(db_model* m, int layout) {
-    if (!m || (layout != DB_CODES_NATURAL && layout != DB_CODES_TC)) return DB_ERR_INVALID_ARGUMENT;
+    if (!m || (layout != DB_CODES_NATURAL && layout != DB_CODES_TC && layout != DB_CODES_DQ))
+        return DB_ERR_INVALID_ARGUMENT;
     cudaSetDevice(m->device);
     cudaStreamSynchronize(m->stream);
     m->drop_graphs();
     for (auto& t : m->tuned) t = db_gemm_config{0, 0, 0};  // tile choices belong to one kernel
-    m->i8 = layout == DB_CODES_NATURAL;
+    const bool dq = layout == DB_CODES_DQ;
+    if (dq && !m->dq_w) {
+        // the unpacked weights of the largest projection of a layer
+        const int D = m->D(), F = m->F();
+        const size_t bytes = std::max({db_gemm_dq_scratch_bytes(m->Nqkv(), D), db_gemm_dq_scratch_bytes(D, m->Nq()),
+                                       db_gemm_dq_scratch_bytes(2 * F, D), db_gemm_dq_scratch_bytes(D, F)});
+        if (cudaMalloc(&m->dq_w, bytes) != cudaSuccess) {
+            m->dq_w = nullptr;
+            return db_fail(DB_ERR_CUDA, "RESOURCE_LIMIT", "dequantised weight scratch exceeds device limits");
+        }
+        m->allocations.push_back(m->dq_w);
+    }
+    if (dq != m->dq) {
+        // the workspace holds the f32 gate/up buffer in dequantised mode only
+        m->free_all(m->ws_allocations);
+        m->cap_T = 0;
+        m->gu32 = nullptr;
+    }
+    m->dq = dq;
+    // the LM head and the int8 paths outside the layers keep int8 codes in dequantised mode
+    m->i8 = layout != DB_CODES_TC;
     return DB_OK;
 }
 
@@ -1059,6 +1097,11 @@ int db_model_tune(db_model* m, int64_t tokens, const char* cache_path, char* rep
         return DB_ERR_INVALID_ARGUMENT;
     }
     cudaSetDevice(m->device);
+    if (m->dq) {
+        // the dequantised GEMM has one configuration per shape (no candidates to select among)
+        if (report_json && cap) std::snprintf(report_json, cap, "{\"dequantised\": true}");
+        return DB_OK;
+    }
     const int D = m->D(), F = m->F();
     // the four projections of a layer: {N, K, epilogue}
     const int64_t shapes[4][3] = {{m->Nqkv(), D, DB_EPI_STORE},

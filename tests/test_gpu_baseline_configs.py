@@ -6,7 +6,8 @@ C1  the single W4A8 GEMM on config 1's exact inputs: activations f16 N(0,1) from
     output bitwise equal to the oracle (int8.rs:526-585 numerics) and, as the north-star bound,
     within 2e-3 x RMS of it.
 C2  all 28 layers of the Pplx-shaped encoder at 1024 tokens against the composed oracle:
-    pooled cosine >= 0.9999 (the north-star bound for final embeddings).
+    pooled cosine >= 0.9999 (the north-star bound for final embeddings), with the exact grouped
+    GEMMs and with the dequantised ones (DB_CODES_DQ).
 C4  the Decima-shaped encoder at its real width (hidden 768, 12 heads, FFN 3072, vocab 128100,
     blocks of 32), 2 layers, one 384 + 32-token sequence: pooled cosine >= 0.9999.
 C5  the Qwen3-4B-shaped decoder at its real width (hidden 2560, 32q/8kv x 128, FFN 9728), 2
@@ -62,9 +63,13 @@ def test_c1_exact_inputs(db, oracle):
     assert float(np.max(np.abs(y.astype(np.float64) - ref))) <= 2e-3 * rms
 
 
-def test_c2_all_28_layers_match_oracle(db, oracle):
-    cfg = dict(layers=28, hidden=1024, q_heads=16, kv_heads=8, head_dim=128, ffn=3072, vocab=151936, weight_bits=4)
-    model = db.Model.synthetic(db.EncoderConfig(**cfg), seed=11)
+C2_CFG = dict(layers=28, hidden=1024, q_heads=16, kv_heads=8, head_dim=128, ffn=3072, vocab=151936, weight_bits=4)
+
+
+@pytest.fixture(scope="module")
+def c2_oracle(db, oracle):
+    """The synthetic C2 weights, 1024 token ids and the composed oracle's pooled embedding."""
+    model = db.Model.synthetic(db.EncoderConfig(**C2_CFG), seed=11)
     D, F, L = 1024, 3072, 28
     shapes = {"q": (2048, D), "k": (1024, D), "v": (1024, D), "o": (D, 2048), "gate": (F, D), "up": (F, D),
               "down": (D, F)}
@@ -74,10 +79,30 @@ def test_c2_all_28_layers_match_oracle(db, oracle):
     for name, size in (("input_norm", D), ("post_norm", D), ("q_norm", 128), ("k_norm", 128)):
         w[name] = [np.ones(size, np.float32) for _ in range(L)]
     w["final_norm"] = np.ones(D, np.float32)
-    ids = np.random.default_rng(2).integers(0, cfg["vocab"], 1024).astype(np.int32)
+    model.close()
+    ids = np.random.default_rng(2).integers(0, C2_CFG["vocab"], 1024).astype(np.int32)
+    return ids, oracle.Encoder(C2_CFG, w).forward(ids, mode=2)
+
+
+def test_c2_all_28_layers_match_oracle(db, c2_oracle):
+    ids, want = c2_oracle
+    model = db.Model.synthetic(db.EncoderConfig(**C2_CFG), seed=11)
     got = model.predict(ids).response
     model.close()
-    want = oracle.Encoder(cfg, w).forward(ids, mode=2)
+    assert cosine(got, want) >= 0.9999, cosine(got, want)
+
+
+def test_c2_dequantised_mode_matches_oracle(db, c2_oracle):
+    """The same 28 layers with the dequantised projections (f16(code * scale) operands, full-K f32
+    accumulation, separate SwiGLU re-quantisation): pooled cosine >= 0.9999 against the oracle's
+    exact grouped fold, and repeatable bit for bit."""
+    ids, want = c2_oracle
+    model = db.Model.synthetic(db.EncoderConfig(**C2_CFG), seed=11)
+    model.set_code_layout(db.CODES_DQ)
+    got = model.predict(ids).response
+    again = model.predict(ids).response
+    model.close()
+    assert np.array_equal(got.view(np.uint32), again.view(np.uint32))
     assert cosine(got, want) >= 0.9999, cosine(got, want)
 
 

@@ -61,6 +61,26 @@ def test_c3_packed_batch_matches_oracle_and_single_requests(db, oracle):
     assert db.device_error_word() == 0
 
 
+def test_c3_packed_batch_dequantised_mode(db, oracle):
+    """The packed pass with the dequantised projections (DB_CODES_DQ): every request equals its own
+    single pass bit for bit (each output row is its own full-K sum) and the oracle within cosine
+    >= 0.9999."""
+    cfg = dict(C2, layers=2, weight_bits=8)
+    model = db.Model.synthetic(db.EncoderConfig(**cfg, max_sequence_tokens=1024), seed=21)
+    model.set_code_layout(db.CODES_DQ)
+    reqs = c3_requests()[:16]
+    out = model.predict_batch(reqs)
+    assert all(o.status == "success" for o in out)
+    ref = oracle.Encoder(cfg, synthetic_oracle_weights(model, cfg))
+    for i, r in enumerate(reqs):
+        got = np.asarray(out[i].result.response)
+        single = np.asarray(model.predict(r).response)
+        assert np.array_equal(got.view(np.uint32), single.view(np.uint32)), i
+        assert cosine(got, ref.forward(r, mode=2)) >= 0.9999, i
+    model.close()
+    assert db.device_error_word() == 0
+
+
 def test_c3_full_depth_packed_equals_single(db):
     cfg = dict(C2, layers=28, weight_bits=8)
     model = db.Model.synthetic(db.EncoderConfig(**cfg, max_sequence_tokens=1024), seed=22)

@@ -196,3 +196,20 @@ def test_code_layouts_are_bit_identical(db, oracle, bits):
     c = np.asarray(model.predict(ids).response)
     assert np.array_equal(a.view(np.uint32), b.view(np.uint32)) and np.array_equal(a.view(np.uint32), c.view(np.uint32))
     model.close()
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("tokens", [1, 37, 300])
+def test_dequantised_mode_matches_composed_oracle(db, oracle, bits, tokens):
+    """DB_CODES_DQ (f16(code * scale) operands, full-K f32 accumulation, separate SwiGLU
+    re-quantisation): final embeddings within cosine >= 0.9999 of the oracle's exact grouped fold."""
+    cfg = dict(SMALL, weight_bits=bits)
+    w = random_weights(oracle, cfg, seed=bits)
+    model = db.Model.from_weights(db.EncoderConfig(**cfg, max_sequence_tokens=512), w)
+    model.set_code_layout(db.CODES_DQ)
+    ids = np.random.default_rng(tokens).integers(0, cfg["vocab"], tokens).astype(np.int32)
+    got = model.predict(ids).response
+    want = oracle.Encoder(cfg, w).forward(ids, mode=2)
+    assert cosine(got, want) >= 0.9999, cosine(got, want)
+    model.close()
+    assert db.device_error_word() == 0
