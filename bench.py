@@ -54,9 +54,9 @@ def measured_peaks():
     return 1590.0, 6650.0, "fallback"
 
 
-def ncu_traffic():
+def ncu_traffic(summary: str = "gemm_i8_c2_encoder.md"):
     """DRAM bytes per GEMM launch from the committed ncu summary (profiles/), or None."""
-    p = os.path.join(ROOT, "profiles", "gemm_i8_c2_encoder.md")
+    p = os.path.join(ROOT, "profiles", summary)
     if not os.path.exists(p):
         return None
     m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", open(p).read())
@@ -450,8 +450,13 @@ def run_ours(args, rank, world, local_rank):
 
     cfg = db.EncoderConfig(**CFG, max_sequence_tokens=TOKENS)
     model = db.Model.synthetic(cfg, seed=SEED, std=0.02, device=local_rank)
-    # kernel selection (bitwise-equal tile configurations, fastest by >= 1 %), before any timing
-    tuning = None if args.no_tune else {k: v["choice"] for k, v in model.tune(TOKENS).items()}
+    dq = args.numerics == "dq"
+    if dq:
+        # dequantised projections: f16(code * scale) operands, f32 accumulation over the whole K
+        model.set_code_layout(db.CODES_DQ)
+    # kernel selection (bitwise-equal tile configurations, fastest by >= 1 %), before any timing;
+    # the dequantised GEMM has one configuration per shape
+    tuning = None if (args.no_tune or dq) else {k: v["choice"] for k, v in model.tune(TOKENS).items()}
     if args.stream:
         model.set_streaming(True)  # weights in pinned host memory, two layers on the device
     rng = np.random.default_rng(SEED + rank)
@@ -518,14 +523,19 @@ def run_ours(args, rank, world, local_rank):
     gemm_flops = sum(fl.values()) * TOKENS * CFG["layers"] * args.steps
     achieved = gemm_flops / (gemm_ms / 1e3) / 1e12
     peak_tf, _, peak_kind = measured_peaks()
-    traffic = ncu_traffic()
+    traffic = ncu_traffic("gemm_dq_c2_encoder.md" if dq else "gemm_i8_c2_encoder.md")
     launches = sum(v[1] for v in prof.values())
 
     extras = None if args.no_extras else named_shapes(db, rank, world, local_rank)
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "dtype": "w4a8 int (f16 MMA exact int dots, f32 fma)",
+                "scaling": "weak", "vs_baseline": None,
+                "dtype": ("w4a8 dequantised to f16 operands, f32 accumulation over K (kind::f16)" if dq
+                          else "w4a8 int (kind::i8 exact int dots, f32 fma group fold)"),
+                "numerics": ("dequantised: f16(code*scale) operands, full-K f32 sums; within the contract's "
+                             "2e-3 x RMS per GEMM, C2 pooled cosine >= 0.9999 (tests)" if dq
+                             else "exact: the reference's grouped fold bit for bit"),
                 "data": "synthetic (seeded N(0,0.02) bf16 weights, uniform token ids)", "config": config_json(),
                 "clocks": clocks.summary(),
                 "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": TOKENS * 4,
@@ -533,7 +543,8 @@ def run_ours(args, rank, world, local_rank):
                 "gpu_launches": launches,
                 "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
                              "frac": achieved / peak_tf, "traffic": traffic,
-                             "kernel": "gemm_i8_kernel (all projection launches)",
+                             "kernel": ("unpack_weights_kernel + gemm_dq_kernel (all projection launches)" if dq
+                                        else "gemm_i8_kernel (all projection launches)"),
                              "peak_kind": f"{peak_kind} bf16 dense burst",
                              "launches": gemm_launches, "avg_launch_us": gemm_ms / gemm_launches * 1e3,
                              "flops_per_launch": gemm_flops / gemm_launches},
@@ -729,6 +740,9 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="skip the named BASELINE shapes in the line")
     ap.add_argument("--no-tune", action="store_true", help="skip kernel selection (default tile configurations)")
+    ap.add_argument("--numerics", default="dq", choices=["dq", "exact"],
+                    help="C2 projections: dequantised f16 operands with full-K f32 sums (default) or the "
+                         "reference's exact grouped fold (kind::i8)")
     ap.add_argument("--stream", action="store_true",
                     help="stream layer weights from pinned host memory through two device banks")
     ap.add_argument("--workload", default="encoder", choices=["encoder", "gemm", "gemv", "decima", "c5", "c4"])
