@@ -20,7 +20,7 @@
 //            tile (8 times at M = 1024), and clock64 traces of such a kernel (converter warps
 //            writing the swizzled tile in shared memory) showed the conversion and its per-stage
 //            hand-over pacing the tensor core at ~2,400 cycles per 64-k stage (MMA: 512).
-//   GEMM     one CTA per SM, persistent over 128 x BN output tiles (BN = 64, 128, 256), 192
+//   GEMM     one CTA per SM, persistent over 128 x BN output tiles (BN = 64, 128, 256), 320
 //            threads:
 //     warp 0      TMA producer (lane 0): per stage (64 k) the A box (128 x 64 f16) and the w' box
 //                 (BN x 64 f16), both with the 128-byte swizzle (UMMA K-major operands as-is)
@@ -28,12 +28,15 @@
 //                 accumulator (two buffers of BN columns, alternating by tile, so a tile's epilogue
 //                 overlaps the next tile's MMAs); one commit per stage frees the stage, one per
 //                 tile hands the accumulator to the epilogue
-//     warps 2-5   epilogue: warp w reads TMEM lanes 32 (w % 4).., all BN columns, 32 at a time,
-//                 and hands them to the TMA through shared memory (store, or reduce-add into y),
-//                 or stores them itself where y's rows are not 16-byte aligned
+//     warps 2-9   epilogue, two warps per TMEM lane quadrant: warp w reads lanes 32 (w % 4).. and
+//                 half of the tile's columns, 32 at a time, and hands them to the TMA through shared
+//                 memory (store, or reduce-add into y), or stores them itself where y's rows are not
+//                 16-byte aligned; or (gate/up) the SwiGLU + re-quantisation of whole 64 + 64 column
+//                 blocks into f16(code * scale), one block per warp
 // Every mbarrier wait is bounded (DB_WAIT_LIMIT_NS); on expiry the CTA records an error in the
 // device error word, stops issuing work, lets its own copies and MMAs land and frees its tensor
 // memory.  No TMA multicast.
+#include <float.h>
 #include <string.h>
 
 #include <map>
@@ -49,8 +52,8 @@ namespace gdq {
 constexpr int BM = 128;  // tile rows
 constexpr int KS = 64;   // k per pipeline stage (one scale group)
 constexpr int EPI_WARP0 = 2;
-constexpr int EPI_WARPS = 4;
-constexpr int NUM_THREADS = 32 * (EPI_WARP0 + EPI_WARPS);  // 192
+constexpr int EPI_WARPS = 8;
+constexpr int NUM_THREADS = 32 * (EPI_WARP0 + EPI_WARPS);  // 320
 constexpr uint64_t DRAIN_NS = 100000000ull;
 
 template <int BN>
@@ -169,10 +172,12 @@ template <int BN, int EPI>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_dq_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                    const __grid_constant__ CUtensorMap tmY, int y_tma, float* __restrict__ y, int64_t ldy, int M,
-                   int N, int G, const int* __restrict__ nonfinite, int* __restrict__ dev_error) {
+                   int N, int G, __half* __restrict__ out_codes, int64_t ldoc, const int* __restrict__ nonfinite,
+                   int* __restrict__ dev_error) {
     using S = Smem<BN>;
     static_assert(BN == 64 || BN == 128 || BN == 256, "tile width");
-    static_assert(EPI == DB_EPI_STORE || EPI == DB_EPI_RESIDUAL, "store or residual epilogue");
+    static_assert(EPI == DB_EPI_STORE || EPI == DB_EPI_RESIDUAL || (EPI == DB_EPI_SWIGLU_QUANT && BN >= 128),
+                  "store, residual, or SwiGLU on whole 64 + 64 blocks");
     pdl_wait();
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -286,6 +291,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     } else {
         // ---------------------------------------------------------------- epilogue
         const int q = warp & 3;  // TMEM lane quadrant this warp may access: rows 32q..
+        const int half = (warp - EPI_WARP0) >> 2;  // which half of the tile's columns (or blocks)
         const uint32_t tlane = tmem_base + ((uint32_t)(q * 32) << 16);
         const bool any_nonfinite = nonfinite != nullptr && *nonfinite != 0;
         const uint32_t ystage = smem_u32(smem + S::OFF_Y) + (warp - EPI_WARP0) * S::Y_BUFS * S::Y_CHUNK;
@@ -302,13 +308,73 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             if (!warp_wait_polite(&done[b], (uint32_t)(t >> 1) & 1u, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_EPI))
                 goto epi_done;
             tc_fence_after();
+            if constexpr (EPI == DB_EPI_SWIGLU_QUANT) {
+                // The columns are blocks of 64 gate rows followed by the 64 matching up rows
+                // (db_interleave_gate_up), so a thread holds whole blocks of its row: h = silu(gate) *
+                // up for the block's 64 features (cpu.rs:513-518, the correctly rounded quotient),
+                // the group scale max(max|h| / 127, MIN_POSITIVE), codes clamp(rint(h / scale))
+                // (int8.rs:178-202, the operations of the int8 GEMM's SwiGLU epilogue), and the
+                // dequantised f16(code * scale) stored for the down projection.
+                const int m = m0 + q * 32 + lane;
 #pragma unroll 1
-            for (int c = 0; c < BN / 32; ++c) {
+                for (int blk = half; blk < BN / 128; blk += 2) {
+                    uint32_t gv[2][32], uv[2][32];
+                    const uint32_t base = tlane + (uint32_t)(b * BN + blk * 128);
+                    tmem_ld_32x32b_x32(base, gv[0]);
+                    tmem_ld_32x32b_x32(base + 32, gv[1]);
+                    tmem_ld_32x32b_x32(base + 64, uv[0]);
+                    tmem_ld_32x32b_x32(base + 96, uv[1]);
+                    tmem_wait_ld();
+                    tie32(gv[0]);
+                    tie32(gv[1]);
+                    tie32(uv[0]);
+                    tie32(uv[1]);
+                    float amax = 0.f;
+#pragma unroll
+                    for (int h = 0; h < 2; ++h)
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            const float g = __uint_as_float(gv[h][i]);
+                            const float s = __fmul_rn(g, __frcp_rn(__fadd_rn(1.f, expf(-g))));
+                            const float hv = __fmul_rn(s, __uint_as_float(uv[h][i]));
+                            gv[h][i] = __float_as_uint(hv);
+                            amax = fmaxf(amax, fabsf(hv));
+                        }
+                    const float scale = fmaxf(__fdiv_rn(amax, 127.f), FLT_MIN);
+                    const float inv = __fdiv_rn(1.f, scale);
+                    const int fblk = (n0 + blk * 128) / 128;  // 64-feature block of the output
+                    if (m < M && fblk * 128 < N) {
+                        uint4* dst = reinterpret_cast<uint4*>(out_codes + (size_t)m * ldoc + (size_t)fblk * 64);
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            uint32_t w[4];
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                const int f = 8 * j + 2 * e;
+                                const float c0 = fminf(fmaxf(rintf(__fmul_rn(__uint_as_float(gv[f >> 5][f & 31]), inv)), -127.f), 127.f);
+                                const float c1 = fminf(fmaxf(rintf(__fmul_rn(__uint_as_float(gv[(f + 1) >> 5][(f + 1) & 31]), inv)), -127.f), 127.f);
+                                const __half2 o = __floats2half2_rn(__fmul_rn((float)(int)c0, scale), __fmul_rn((float)(int)c1, scale));
+                                w[e] = *reinterpret_cast<const uint32_t*>(&o);
+                            }
+                            dst[j] = make_uint4(w[0], w[1], w[2], w[3]);
+                        }
+                    }
+                }
+                // this warp's columns are in registers (at BN = 128 the second warp of the quadrant
+                // has none): hand the buffer back
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&acc_empty[b]);
+                continue;
+            }
+            constexpr int CPW = BN / 64;  // 32-column chunks per warp (half of the tile's columns)
+#pragma unroll 1
+            for (int c = half * CPW; c < (half + 1) * CPW; ++c) {
                 uint32_t v[32];
                 tmem_ld_32x32b_x32(tlane + (uint32_t)(b * BN + c * 32), v);
                 tmem_wait_ld();
                 tie32(v);
-                if (c == BN / 32 - 1) {
+                if (c == (half + 1) * CPW - 1) {
                     // every column of the buffer is in registers: hand it back to the MMA issuer
                     tc_fence_before();
                     __syncwarp();
@@ -395,17 +461,22 @@ int launch(const DbGemmArgs& a, const CUtensorMap& tmA, const CUtensorMap& tmW, 
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    const cudaError_t e =
-        cudaLaunchKernelEx(&cfg, kernel, tmA, tmW, tmY, y_tma, a.y, a.ldy, a.M, a.N, G, a.nonfinite, a.dev_error);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, tmA, tmW, tmY, y_tma, a.y, a.ldy, a.M, a.N, G,
+                                             static_cast<__half*>(a.out_codes), a.ldoc, a.nonfinite, a.dev_error);
     return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }
 
 template <int EPI>
 int launch_bn(const DbGemmArgs& a, int bn, const CUtensorMap& tmA, const CUtensorMap& tmW, const CUtensorMap& tmY,
               int y_tma, int G, cudaStream_t s) {
-    if (bn == 64) return launch<64, EPI>(a, tmA, tmW, tmY, y_tma, G, s);
-    if (bn == 128) return launch<128, EPI>(a, tmA, tmW, tmY, y_tma, G, s);
-    return launch<256, EPI>(a, tmA, tmW, tmY, y_tma, G, s);
+    if constexpr (EPI == DB_EPI_SWIGLU_QUANT) {
+        if (bn == 128) return launch<128, EPI>(a, tmA, tmW, tmY, y_tma, G, s);
+        return launch<256, EPI>(a, tmA, tmW, tmY, y_tma, G, s);
+    } else {
+        if (bn == 64) return launch<64, EPI>(a, tmA, tmW, tmY, y_tma, G, s);
+        if (bn == 128) return launch<128, EPI>(a, tmA, tmW, tmY, y_tma, G, s);
+        return launch<256, EPI>(a, tmA, tmW, tmY, y_tma, G, s);
+    }
 }
 
 }  // namespace gdq
@@ -455,18 +526,26 @@ static int dq_cached_scratch(cudaStream_t stream, size_t bytes, void** out) {
 int db_launch_gemm_dq(const DbGemmArgs& a, cudaStream_t stream) {
     using namespace db::gdq;
     if (a.M <= 0 || a.N <= 0) return 0;
+    const bool swiglu = a.epilogue == DB_EPI_SWIGLU_QUANT;
     if (a.K <= 0 || (a.bits != 4 && a.bits != 8) || (a.block != 0 && a.block != 64) ||
-        (a.epilogue != DB_EPI_STORE && a.epilogue != DB_EPI_RESIDUAL) || a.pair_ctas)
+        (a.epilogue != DB_EPI_STORE && a.epilogue != DB_EPI_RESIDUAL && !swiglu) || a.pair_ctas)
         return (int)cudaErrorInvalidValue;
     DbEncodeTiledFn enc = db_encode_tiled();
     if (!enc) return (int)cudaErrorNotSupported;
     const int G = (a.K + 63) / 64, Kp = G * 64;
-    const int bn = a.block_n ? a.block_n : db_gemm_dq_default_block_n(a.M, a.N);
+    int bn = a.block_n ? a.block_n : db_gemm_dq_default_block_n(a.M, a.N);
     if (bn != 64 && bn != 128 && bn != 256) return (int)cudaErrorInvalidValue;
+    if (swiglu) {
+        // SwiGLU: whole blocks of 64 gate + 64 up columns per tile; out_codes f16 [M, ldoc]
+        if (bn == 64) bn = 128;
+        if (a.N % 128 || !a.out_codes || (reinterpret_cast<uintptr_t>(a.out_codes) & 15) || (a.ldoc & 7) ||
+            a.ldoc < a.N / 2)
+            return (int)cudaErrorInvalidValue;
+    }
     // A rows are TMA boxes of f16 (16-byte aligned rows); codes rows are read 16 bytes at a time
     if ((reinterpret_cast<uintptr_t>(a.a_codes) & 15) || (a.lda & 7) || a.lda < Kp ||
-        (reinterpret_cast<uintptr_t>(a.w_codes) & 15) || (reinterpret_cast<uintptr_t>(a.sw) & 3) || !a.y ||
-        a.ldy < a.N || (reinterpret_cast<uintptr_t>(a.w_scratch) & 15))
+        (reinterpret_cast<uintptr_t>(a.w_codes) & 15) || (reinterpret_cast<uintptr_t>(a.sw) & 3) ||
+        (!swiglu && (!a.y || a.ldy < a.N)) || (reinterpret_cast<uintptr_t>(a.w_scratch) & 15))
         return (int)cudaErrorMisalignedAddress;
     // w' [N, Kp] f16: the caller's scratch, or the cached buffer of this device and stream
     void* scratch = a.w_scratch;
@@ -510,7 +589,7 @@ int db_launch_gemm_dq(const DbGemmArgs& a, cudaStream_t stream) {
             rc = (int)cudaErrorInvalidValue;
     }
     // output tensor map for the TMA store / reduce-add (16-byte aligned rows; else plain stores)
-    if (!rc && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0 && (a.ldy & 3) == 0) {
+    if (!rc && !swiglu && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0 && (a.ldy & 3) == 0) {
         cuuint64_t dims[2] = {(cuuint64_t)a.N, (cuuint64_t)a.M};
         cuuint64_t strides[1] = {(cuuint64_t)a.ldy * 4};
         cuuint32_t box[2] = {16, 32};
@@ -520,7 +599,8 @@ int db_launch_gemm_dq(const DbGemmArgs& a, cudaStream_t stream) {
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
     }
     if (!rc)
-        rc = a.epilogue == DB_EPI_RESIDUAL ? launch_bn<DB_EPI_RESIDUAL>(a, bn, tmA, tmW, tmY, y_tma, G, stream)
-                                           : launch_bn<DB_EPI_STORE>(a, bn, tmA, tmW, tmY, y_tma, G, stream);
+        rc = swiglu ? launch_bn<DB_EPI_SWIGLU_QUANT>(a, bn, tmA, tmW, tmY, y_tma, G, stream)
+             : a.epilogue == DB_EPI_RESIDUAL ? launch_bn<DB_EPI_RESIDUAL>(a, bn, tmA, tmW, tmY, y_tma, G, stream)
+                                             : launch_bn<DB_EPI_STORE>(a, bn, tmA, tmW, tmY, y_tma, G, stream);
     return rc;
 }

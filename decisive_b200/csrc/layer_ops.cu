@@ -216,36 +216,6 @@ __global__ void fill_nan_if_kernel(float* __restrict__ y, int64_t n, const int* 
     if (i < n && *flag) y[i] = __int_as_float(0x7fc00000);
 }
 
-// SwiGLU + group-64 re-quantisation for the dequantised GEMM path: gu f32 [R, 2F] holds the gate/up
-// projection with its columns in blocks of 64 gate then the matching 64 up features
-// (db_interleave_gate_up); one warp per (row, block) computes h = silu(gate) * up
-// (cpu.rs:513-518 with the correctly rounded quotient), the block's scale
-// max(max|h| / 127, MIN_POSITIVE) and codes clamp(rint(h / scale)) (int8.rs:178-202, the same
-// operations as the int8 GEMM's fused SwiGLU epilogue) and writes f16(code * scale), natural order.
-__global__ void swiglu_quantize_dq_kernel(const float* __restrict__ gu, int64_t ld, int R, int F,
-                                          __half* __restrict__ out, int64_t ldo, int* __restrict__ nonfinite) {
-    pdl_wait();
-    const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    const int lane = threadIdx.x & 31, blocks = F / 64;
-    if (warp < (int64_t)R * blocks) {
-        const int r = (int)(warp / blocks), b = (int)(warp % blocks);
-        const float* row = gu + (size_t)r * ld + 128 * b;
-        const float2 g = *reinterpret_cast<const float2*>(row + 2 * lane);
-        const float2 u = *reinterpret_cast<const float2*>(row + 64 + 2 * lane);
-        auto silu = [](float x) { return __fmul_rn(x, __frcp_rn(__fadd_rn(1.f, expf(-x)))); };
-        const float h0 = __fmul_rn(silu(g.x), u.x), h1 = __fmul_rn(silu(g.y), u.y);
-        if (__any_sync(0xffffffffu, !(isfinite(h0) && isfinite(h1))) && lane == 0 && nonfinite) atomicOr(nonfinite, 1);
-        const float amax = warp_max(fmaxf(fabsf(h0), fabsf(h1)));
-        const float scale = fmaxf(__fdiv_rn(amax, 127.f), FLT_MIN);
-        const float inv = __fdiv_rn(1.f, scale);
-        const float c0 = fminf(fmaxf(rintf(__fmul_rn(h0, inv)), -127.f), 127.f);
-        const float c1 = fminf(fmaxf(rintf(__fmul_rn(h1, inv)), -127.f), 127.f);
-        const __half2 o = __floats2half2_rn(__fmul_rn((float)(int)c0, scale), __fmul_rn((float)(int)c1, scale));
-        *reinterpret_cast<__half2*>(out + (size_t)r * ldo + 64 * b + 2 * lane) = o;
-    }
-    pdl_trigger();
-}
-
 }  // namespace db
 
 using namespace db;
@@ -282,16 +252,6 @@ int db_launch_qk_norm_rope(const float* qkv, int64_t ld, int T, int Hq, int Hk, 
 
 int db_launch_mean_pool(const float* x, int64_t ldx, int T, int D, float* out, cudaStream_t stream) {
     const cudaError_t e = db_launch_pdl(mean_pool_kernel, dim3((D + 127) / 128), dim3(128), 0, stream, x, ldx, T, D, out);
-    return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
-}
-
-int db_launch_swiglu_quantize_dq(const float* gu, int64_t ld, int R, int F, __half* out, int64_t ldo, int* nonfinite,
-                                 cudaStream_t stream) {
-    if (R <= 0) return 0;
-    if (F % 64 || (ld & 1) || (ldo & 1)) return (int)cudaErrorInvalidValue;
-    const int64_t threads = (int64_t)R * (F / 64) * 32;
-    const cudaError_t e = db_launch_pdl(swiglu_quantize_dq_kernel, dim3((unsigned)((threads + 255) / 256)), dim3(256), 0,
-                                        stream, gu, ld, R, F, out, ldo, nonfinite);
     return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }
 

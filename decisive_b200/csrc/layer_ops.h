@@ -18,10 +18,6 @@ int db_launch_mean_pool(const float* x, int64_t ldx, int T, int D, float* out, c
 int db_launch_mean_pool_varlen(const float* x, int64_t ldx, const int* cu_seqlens, int nseq, int D, float* out,
                                cudaStream_t stream);
 int db_launch_fill_nan_if(float* y, int64_t n, const int* flag, cudaStream_t stream);
-// SwiGLU + group-64 re-quantisation of a gate/up projection stored as f32 [R, 2F] (blocks of 64
-// gate then 64 up columns) into dequantised f16 activations [R, ldo] (DB_CODES_DQ_F16).
-int db_launch_swiglu_quantize_dq(const float* gu, int64_t ld, int R, int F, __half* out, int64_t ldo, int* nonfinite,
-                                 cudaStream_t stream);
 
 // Non-causal GQA attention over head_dim 128: q16 [T, Hq, 128], k16/v16 [T, Hk, 128] (f16),
 // out f32 [T, Hq*128] with row stride ldo.  scale multiplies q.k before the softmax.

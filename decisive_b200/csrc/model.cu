@@ -107,10 +107,9 @@ struct db_model {
     bool i8 = true;
     // dequantised mode (DB_CODES_DQ): the layers' projections take f16(code * scale) activations
     // through the full-K kind::f16 GEMM (gemm_dq.cu); dq_w holds the unpacked weights of one
-    // projection, gu32 the f32 gate/up output before the SwiGLU re-quantisation
+    // projection
     bool dq = false;
     void* dq_w = nullptr;
-    float* gu32 = nullptr;
     // per-launch CUDA-event profiling (mirror of the reference's projection_ms accounting,
     // cpu.rs:8-16 / native.rs:229-258), enabled by db_model_profile
     bool profile = false;
@@ -246,8 +245,7 @@ int ensure_workspace(db_model* m, int T) {
         m->alloc(&m->sa, (size_t)Gmax * db_scale_stride(T), v) || m->alloc(&m->sh, (size_t)(F / 64) * db_scale_stride(T), v) ||
         m->alloc(&m->acodes, (size_t)T * Kmax, v) || m->alloc(&m->hcodes, (size_t)T * F, v) ||
         m->alloc(&m->q16, (size_t)T * m->Nq(), v) || m->alloc(&m->k16, (size_t)T * m->Nk(), v) ||
-        m->alloc(&m->v16, (size_t)T * m->Nk(), v) || m->alloc(&m->ids, T, v) || m->alloc(&m->flag, 4, v) ||
-        (m->dq && m->alloc(&m->gu32, (size_t)T * 2 * F, v)))
+        m->alloc(&m->v16, (size_t)T * m->Nk(), v) || m->alloc(&m->ids, T, v) || m->alloc(&m->flag, 4, v))
         return db_fail(DB_ERR_CUDA, "RESOURCE_LIMIT", "workspace exceeds device limits");
     m->cap_T = T;
     return ensure_rope(m, T);
@@ -482,13 +480,8 @@ int enqueue_forward(db_model* m, int T, const volatile uint8_t* cancel, const Pa
                 return db_launch_rms_quantize(m->x, D, w.post_norm, R, D, c.eps, 0, nullptr, 0, m->acodes, code_layout,
                                               ld_codes, m->sa, nullptr, lds, m->flag, st);
             });
-        if (!rc && m->dq) {
-            // dequantised mode: the gate/up projection in f32, then SwiGLU + re-quantisation
-            rc = timed(7, [&] { return gemm(2, m->acodes, w.gu_c, w.gu_s, m->sa, 2 * F, D, DB_EPI_STORE, m->gu32, 2 * F); });
-            if (!rc) rc = timed(1, [&] { return db_launch_swiglu_quantize_dq(m->gu32, 2 * F, R, F, m->hcodes, F, m->flag, st); });
-        } else if (!rc) {
+        if (!rc)
             rc = timed(7, [&] { return gemm(2, m->acodes, w.gu_c, w.gu_s, m->sa, 2 * F, D, DB_EPI_SWIGLU_QUANT, nullptr, 0); });
-        }
         if (!rc) rc = timed(8, [&] {
             DbGemmArgs g{};
             g.a_codes = m->hcodes;
@@ -1038,12 +1031,6 @@ int db_model_set_code_layout(db_model* m, int layout) {
             return db_fail(DB_ERR_CUDA, "RESOURCE_LIMIT", "dequantised weight scratch exceeds device limits");
         }
         m->allocations.push_back(m->dq_w);
-    }
-    if (dq != m->dq) {
-        // the workspace holds the f32 gate/up buffer in dequantised mode only
-        m->free_all(m->ws_allocations);
-        m->cap_T = 0;
-        m->gu32 = nullptr;
     }
     m->dq = dq;
     // the LM head and the int8 paths outside the layers keep int8 codes in dequantised mode

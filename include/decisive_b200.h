@@ -398,9 +398,8 @@ int db_model_use_graphs(db_model *m, int enable);
  * the same per-group integer dots and fold them in the same order, so outputs are bit-identical;
  * only speed differs.  DB_CODES_DQ switches the layers' projections to the dequantised numerics
  * (f16(code * scale) operands, f32 accumulation over the whole K: the reference's WGSL GEMM
- * numerics, within the contract's tolerance of the grouped fold, not bit-identical); the gate/up
- * projection is then stored in f32 and re-quantised by a separate SwiGLU kernel, and the model
- * keeps an unpacked-weight scratch of its largest projection.  Resets tuned tile choices (they
+ * numerics, within the contract's tolerance of the grouped fold, not bit-identical), and the
+ * model keeps an unpacked-weight scratch of its largest projection.  Resets tuned tile choices (they
  * belong to one kernel); db_model_tune has nothing to select in dequantised mode. */
 int db_model_set_code_layout(db_model *m, int layout);
 
