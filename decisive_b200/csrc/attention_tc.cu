@@ -181,6 +181,9 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
                         int* __restrict__ dev_error, int codes_i8, const int* __restrict__ cu_seqlens,
                         const DecoderArgs da) {
     pdl_wait();
+    // dequantised output: the next kernel is the output projection's weight unpack, which reads
+    // nothing this kernel writes; let it start while this one runs
+    if (codes_i8 == 2) pdl_trigger();
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);

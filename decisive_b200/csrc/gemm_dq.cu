@@ -127,12 +127,16 @@ __device__ __forceinline__ uint4 q8_words_to_f16(uint32_t w0, uint32_t w1, Scale
 
 // Unpack pass: thread i writes the 16 bytes (8 weights) of one 8-k chunk of a weight row,
 // consecutive threads consecutive chunks, so a warp reads 128 (Q4) or 256 (Q8) contiguous bytes of
-// codes and writes 512 contiguous bytes of w' [N, Kp] f16.
+// codes and writes 512 contiguous bytes of w' [N, Kp] f16.  overlap = 1 (the caller guarantees that
+// no kernel still running reads `out`, e.g. by alternating two buffers): the pass reads only the
+// weights, so it runs while the previous kernel in the stream finishes and waits for that kernel
+// only before it exits (its completion still implies the previous kernel's, so the kernels after
+// it keep their ordering).
 template <int BITS>
 __global__ void __launch_bounds__(256) unpack_weights_kernel(const uint8_t* __restrict__ codes,
                                                              const float* __restrict__ sw, int64_t ldsw, int N,
-                                                             int Kp, __half* __restrict__ out) {
-    pdl_wait();
+                                                             int Kp, __half* __restrict__ out, int overlap) {
+    if (!overlap) pdl_wait();
     const int per_row = Kp / 8;
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i < (int64_t)N * per_row) {
@@ -147,6 +151,7 @@ __global__ void __launch_bounds__(256) unpack_weights_kernel(const uint8_t* __re
         }
         reinterpret_cast<uint4*>(out + (size_t)n * Kp)[c] = o;
     }
+    if (overlap) pdl_wait();
     pdl_trigger();
 }
 
@@ -225,6 +230,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
     const uint32_t st_base = smem_u32(smem + S::OFF_STAGE);
+    // the next kernel may be scheduled now: it waits for this grid's completion before it reads
+    // anything this kernel writes (an overlapped unpack pass writes a buffer no running GEMM reads)
+    pdl_trigger();
 
     if (warp == 0) {
         // ---------------------------------------------------------------- TMA producer (lane 0)
@@ -424,7 +432,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tmem_wait_ld();
     }
     bulk_wait_all();  // output stores issued by this thread have completed
-    pdl_trigger();
     // Teardown through mbarriers: warp 1 frees tensor memory once every warp has arrived.  Every
     // wait above is bounded, so all warps get here.
     tc_fence_before();
@@ -549,6 +556,7 @@ int db_launch_gemm_dq(const DbGemmArgs& a, cudaStream_t stream) {
         return (int)cudaErrorMisalignedAddress;
     // w' [N, Kp] f16: the caller's scratch, or the cached buffer of this device and stream
     void* scratch = a.w_scratch;
+    if (!scratch && a.overlap_unpack) return (int)cudaErrorInvalidValue;  // overlap needs the caller's buffers
     if (!scratch) {
         const int e = dq_cached_scratch(stream, db_gemm_dq_scratch_bytes(a.N, a.K), &scratch);
         if (e) return e;
@@ -560,9 +568,9 @@ int db_launch_gemm_dq(const DbGemmArgs& a, cudaStream_t stream) {
         const dim3 grid((unsigned)((threads + 255) / 256));
         const cudaError_t e = a.bits == 4
                                   ? db_launch_pdl(unpack_weights_kernel<4>, grid, dim3(256), 0, stream, a.w_codes, a.sw,
-                                                  (int64_t)db_scale_stride(a.N), a.N, Kp, wq)
+                                                  (int64_t)db_scale_stride(a.N), a.N, Kp, wq, a.overlap_unpack)
                                   : db_launch_pdl(unpack_weights_kernel<8>, grid, dim3(256), 0, stream, a.w_codes, a.sw,
-                                                  (int64_t)db_scale_stride(a.N), a.N, Kp, wq);
+                                                  (int64_t)db_scale_stride(a.N), a.N, Kp, wq, a.overlap_unpack);
         rc = e != cudaSuccess ? (int)e : (int)cudaGetLastError();
     }
     CUtensorMap tmA, tmW, tmY;

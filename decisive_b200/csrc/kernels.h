@@ -73,6 +73,7 @@ struct DbGemmArgs {
     const float* bias;     // add_bias = 1: y = acc + bias[n] (bias == nullptr: y = acc + 0)
     int add_bias;
     void* w_scratch;       // dequantised GEMM: f16 [N, Kp] for the unpacked weights (null: cached buffer)
+    int overlap_unpack;    // 1: no running kernel reads w_scratch, so the unpack overlaps the previous kernel
 };
 int db_launch_gemm_tc(const DbGemmArgs& args, cudaStream_t stream);
 // The same GEMM on int8 activation codes in natural order (DB_CODES_NATURAL_I8, a_codes [M, lda]

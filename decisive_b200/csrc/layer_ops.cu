@@ -35,6 +35,9 @@ __global__ void rms_quantize_kernel(const float* __restrict__ x, int64_t ldx, co
                                     int* __restrict__ nonfinite) {
     __shared__ float partial[32];
     pdl_wait();
+    // dequantised layout: the next kernel is the projection's weight unpack, which reads nothing
+    // this kernel writes; let it start while this one runs
+    if (layout == DB_CODES_DQ_F16) pdl_trigger();
     const int t = blockIdx.x, lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     const int c = 4 * threadIdx.x;
     const float4 v = *reinterpret_cast<const float4*>(x + (size_t)t * ldx + c);

@@ -106,10 +106,11 @@ struct db_model {
     // or f16 codes through the kind::f16 GEMM (db_model_set_code_layout)
     bool i8 = true;
     // dequantised mode (DB_CODES_DQ): the layers' projections take f16(code * scale) activations
-    // through the full-K kind::f16 GEMM (gemm_dq.cu); dq_w holds the unpacked weights of one
-    // projection
+    // through the full-K kind::f16 GEMM (gemm_dq.cu); dq_w[2] hold the unpacked weights of
+    // consecutive projections (alternating, so one projection's unpack overlaps the kernel before it
+    // while the previous GEMM may still read the other buffer)
     bool dq = false;
-    void* dq_w = nullptr;
+    void* dq_w[2] = {nullptr, nullptr};
     // per-launch CUDA-event profiling (mirror of the reference's projection_ms accounting,
     // cpu.rs:8-16 / native.rs:229-258), enabled by db_model_profile
     bool profile = false;
@@ -374,7 +375,8 @@ int enqueue_forward(db_model* m, int T, const volatile uint8_t* cancel, const Pa
     // one projection; the tuned tile configuration, else the i8 path's default for the shape
     auto launch = [&](int proj, DbGemmArgs& g) {
         if (m->dq) {
-            g.w_scratch = m->dq_w;
+            g.w_scratch = m->dq_w[proj & 1];  // qkv, gate/up: 0; o, down: 1
+            g.overlap_unpack = 1;
             return db_launch_gemm_dq(g, st);
         }
         g.block_n = m->tuned[proj].block_n;
@@ -1021,16 +1023,18 @@ int db_model_set_code_layout(db_model* m, int layout) {
     m->drop_graphs();
     for (auto& t : m->tuned) t = db_gemm_config{0, 0, 0};  // tile choices belong to one kernel
     const bool dq = layout == DB_CODES_DQ;
-    if (dq && !m->dq_w) {
-        // the unpacked weights of the largest projection of a layer
+    if (dq && !m->dq_w[0]) {
+        // the unpacked weights of the largest projection of a layer, twice
         const int D = m->D(), F = m->F();
         const size_t bytes = std::max({db_gemm_dq_scratch_bytes(m->Nqkv(), D), db_gemm_dq_scratch_bytes(D, m->Nq()),
                                        db_gemm_dq_scratch_bytes(2 * F, D), db_gemm_dq_scratch_bytes(D, F)});
-        if (cudaMalloc(&m->dq_w, bytes) != cudaSuccess) {
-            m->dq_w = nullptr;
-            return db_fail(DB_ERR_CUDA, "RESOURCE_LIMIT", "dequantised weight scratch exceeds device limits");
+        for (int i = 0; i < 2; ++i) {
+            if (cudaMalloc(&m->dq_w[i], bytes) != cudaSuccess) {
+                m->dq_w[i] = nullptr;
+                return db_fail(DB_ERR_CUDA, "RESOURCE_LIMIT", "dequantised weight scratch exceeds device limits");
+            }
+            m->allocations.push_back(m->dq_w[i]);
         }
-        m->allocations.push_back(m->dq_w);
     }
     m->dq = dq;
     // the LM head and the int8 paths outside the layers keep int8 codes in dequantised mode
