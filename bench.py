@@ -243,19 +243,21 @@ def _device_time_us(fn, reps, flush=None, sleep=200_000):
     return float(np.median(times))
 
 
-def shape_c1(db, reps=20):
+def shape_c1(db, reps=20, layout=None):
     """one W4A8 g64 GEMM, M=1024 K=1024 N=3072 (activations f16 N(0,1) seed 0,
-    weights f32 N(0,0.02) seed 1 -> bf16 -> Q4), int8 tensor-core path, L2 flushed per launch."""
+    weights f32 N(0,0.02) seed 1 -> bf16 -> Q4), the exact int8 tensor-core path (or the given
+    activation layout, e.g. the dequantised one, unpack pass included), L2 flushed per launch."""
     import torch
     from oracle import oracle
     m, k, n = 1024, 1024, 3072
     w = oracle.f32_to_bf16(np.random.default_rng(1).normal(0, 0.02, (n, k)).astype(np.float32))
     x = torch.from_numpy(np.random.default_rng(0).normal(0, 1, (m, k)).astype(np.float16)).cuda()
     codes, scales = db.pack_weights(torch.from_numpy(w.view(np.int16)).cuda(), 4)
-    a, sa, _ = db.quantize_activations(x, bits=8, layout=db.CODES_NATURAL)
+    layout = db.CODES_NATURAL if layout is None else layout
+    a, sa, _ = db.quantize_activations(x, bits=8, layout=layout)
     y = torch.empty((m, n), dtype=torch.float32, device="cuda")
     flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device="cuda")
-    fn = lambda: db.gemm(a, db.CODES_NATURAL, sa, codes, scales, m, n, k, 4, residual=y)
+    fn = lambda: db.gemm(a, layout, sa, codes, scales, m, n, k, 4, residual=y)
     for _ in range(3):
         fn()
     us = _device_time_us(fn, reps, flush)
@@ -302,7 +304,7 @@ def shape_gemv(db, rows=(1, 4, 8), copies=16, reps=5):
     return out
 
 
-def shape_c3(db, rank, world, local_rank, reps=3):
+def shape_c3(db, rank, world, local_rank, reps=3, dq=False):
     """the C2-shaped encoder with int8 (Q8 g64) weights on a ragged batch of 64
     sequences, lengths U(16, 1024) (seed 3), through the public predict_batch (packed passes).  At
     N > 1 the sequences are sharded by longest-processing-time (sharding.assign_lpt) and each rank
@@ -314,6 +316,8 @@ def shape_c3(db, rank, world, local_rank, reps=3):
     cfg = dict(CFG, weight_bits=8)
     model = db.Model.synthetic(db.EncoderConfig(**cfg, max_sequence_tokens=1024), seed=SEED, std=0.02,
                                device=local_rank)
+    if dq:
+        model.set_code_layout(db.CODES_DQ)
     rng = np.random.default_rng(3)
     lens = rng.integers(16, 1025, 64)
     reqs = [rng.integers(0, CFG["vocab"], int(L)).astype(np.int32) for L in lens]
@@ -341,6 +345,7 @@ def shape_c3(db, rank, world, local_rank, reps=3):
     model.close()
     tokens = int(lens.sum())
     return {"tokens_per_s": tokens / best, "ms_per_batch": best * 1e3, "sequences": 64, "tokens": tokens,
+            "numerics": "dequantised" if dq else "exact",
             "all_success": bool(ok), "lpt_max_over_mean_load": max(loads) / (sum(loads) / len(loads)),
             "timing": "host wall clock around predict_batch (host ids in, pooled embeddings out), best of "
                       f"{reps}, max over ranks"}
@@ -400,7 +405,7 @@ def shape_c5(db, local_rank, requests=3):
             "timing": "host wall clock around the public call (ids in, 4 x 32 log-probs out)"}
 
 
-def named_shapes(db, rank, world, local_rank):
+def named_shapes(db, rank, world, local_rank, dq=False):
     """Every named BASELINE shape, short: each entry is independent (a failure is recorded, not
     raised).  C3 runs on every rank (sharded); the others on rank 0."""
     import torch
@@ -413,9 +418,11 @@ def named_shapes(db, rank, world, local_rank):
         except Exception as e:  # recorded in the line
             out[name] = {"error": f"{type(e).__name__}: {e}"[:300]}
 
-    run("c3_ragged_int8_batch", lambda: shape_c3(db, rank, world, local_rank))
+    run("c3_ragged_int8_batch", lambda: shape_c3(db, rank, world, local_rank, dq=dq))
     if rank == 0:
         run("c1_gemm", lambda: shape_c1(db))
+        if dq:
+            run("c1_gemm_dequantised", lambda: shape_c1(db, layout=db.CODES_DQ))
         run("gemv_c5_layers", lambda: shape_gemv(db))
         run("c4_decima_encoder", lambda: shape_c4(db, local_rank))
         run("c5_decoder_prefix", lambda: shape_c5(db, local_rank))
@@ -523,10 +530,11 @@ def run_ours(args, rank, world, local_rank):
     gemm_flops = sum(fl.values()) * TOKENS * CFG["layers"] * args.steps
     achieved = gemm_flops / (gemm_ms / 1e3) / 1e12
     peak_tf, _, peak_kind = measured_peaks()
-    traffic = ncu_traffic("gemm_dq_c2_encoder.md" if dq else "gemm_i8_c2_encoder.md")
-    launches = sum(v[1] for v in prof.values())
+    traffic = ncu_traffic("gemm_dq_c2.md" if dq else "gemm_i8_c2_encoder.md")
+    # profiled regions; in dequantised mode each projection's region holds two kernels (unpack, GEMM)
+    launches = sum(v[1] for v in prof.values()) + (gemm_launches if dq else 0)
 
-    extras = None if args.no_extras else named_shapes(db, rank, world, local_rank)
+    extras = None if args.no_extras else named_shapes(db, rank, world, local_rank, dq=dq)
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,

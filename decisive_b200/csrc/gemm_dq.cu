@@ -55,6 +55,7 @@ constexpr int EPI_WARP0 = 2;
 constexpr int EPI_WARPS = 8;
 constexpr int NUM_THREADS = 32 * (EPI_WARP0 + EPI_WARPS);  // 320
 constexpr uint64_t DRAIN_NS = 100000000ull;
+constexpr int UNPACK_CHUNKS = 4;  // 8-k chunks per thread of the unpack pass
 
 template <int BN>
 struct Smem {
@@ -125,9 +126,10 @@ __device__ __forceinline__ uint4 q8_words_to_f16(uint32_t w0, uint32_t w1, Scale
     return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
-// Unpack pass: thread i writes the 16 bytes (8 weights) of one 8-k chunk of a weight row,
-// consecutive threads consecutive chunks, so a warp reads 128 (Q4) or 256 (Q8) contiguous bytes of
-// codes and writes 512 contiguous bytes of w' [N, Kp] f16.  overlap = 1 (the caller guarantees that
+// Unpack pass: a thread converts UNPACK_CHUNKS 8-k chunks of weights (16 bytes of w' each), the
+// chunks UNPACK_CHUNKS x the grid's threads apart, consecutive threads consecutive chunks, so each
+// round of a warp reads 128 (Q4) or 256 (Q8) contiguous bytes of codes and writes 512 contiguous
+// bytes of w' [N, Kp] f16; all of a thread's loads are issued before its first conversion.  overlap = 1 (the caller guarantees that
 // no kernel still running reads `out`, e.g. by alternating two buffers): the pass reads only the
 // weights, so it runs while the previous kernel in the stream finishes and waits for that kernel
 // only before it exits (its completion still implies the previous kernel's, so the kernels after
@@ -138,18 +140,30 @@ __global__ void __launch_bounds__(256) unpack_weights_kernel(const uint8_t* __re
                                                              int Kp, __half* __restrict__ out, int overlap) {
     if (!overlap) pdl_wait();
     const int per_row = Kp / 8;
-    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < (int64_t)N * per_row) {
-        const int n = (int)(i / per_row), c = (int)(i % per_row);
-        const Scale2 s = split_scale(__ldg(sw + (int64_t)(c / 8) * ldsw + n));
-        uint4 o;
-        if (BITS == 4) {
-            o = q4_word_to_f16(__ldg(reinterpret_cast<const uint32_t*>(codes + (size_t)n * (Kp / 2)) + c), s);
-        } else {
-            const uint2 v = __ldg(reinterpret_cast<const uint2*>(codes + (size_t)n * Kp) + c);
-            o = q8_words_to_f16(v.x, v.y, s);
+    const int64_t total = (int64_t)N * per_row;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    const int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    uint2 v[UNPACK_CHUNKS];
+    float sc[UNPACK_CHUNKS];
+#pragma unroll
+    for (int u = 0; u < UNPACK_CHUNKS; ++u) {
+        const int64_t i = i0 + u * stride;
+        v[u] = make_uint2(0u, 0u);
+        sc[u] = 0.f;
+        if (i < total) {
+            const int n = (int)(i / per_row), c = (int)(i % per_row);
+            sc[u] = __ldg(sw + (int64_t)(c / 8) * ldsw + n);
+            if (BITS == 4) v[u].x = __ldg(reinterpret_cast<const uint32_t*>(codes + (size_t)n * (Kp / 2)) + c);
+            else v[u] = __ldg(reinterpret_cast<const uint2*>(codes + (size_t)n * Kp) + c);
         }
-        reinterpret_cast<uint4*>(out + (size_t)n * Kp)[c] = o;
+    }
+#pragma unroll
+    for (int u = 0; u < UNPACK_CHUNKS; ++u) {
+        const int64_t i = i0 + u * stride;
+        if (i < total) {
+            const Scale2 s = split_scale(sc[u]);
+            reinterpret_cast<uint4*>(out)[i] = BITS == 4 ? q4_word_to_f16(v[u].x, s) : q8_words_to_f16(v[u].x, v[u].y, s);
+        }
     }
     if (overlap) pdl_wait();
     pdl_trigger();
@@ -564,7 +578,7 @@ int db_launch_gemm_dq(const DbGemmArgs& a, cudaStream_t stream) {
     __half* wq = static_cast<__half*>(scratch);
     int rc = 0;
     {
-        const int64_t threads = (int64_t)a.N * (Kp / 8);
+        const int64_t threads = ((int64_t)a.N * (Kp / 8) + UNPACK_CHUNKS - 1) / UNPACK_CHUNKS;
         const dim3 grid((unsigned)((threads + 255) / 256));
         const cudaError_t e = a.bits == 4
                                   ? db_launch_pdl(unpack_weights_kernel<4>, grid, dim3(256), 0, stream, a.w_codes, a.sw,
