@@ -161,8 +161,7 @@ int db_gemm_g64_config(const void* a_codes, int layout, int64_t lda, const float
     if (config && ((config->block_n != 0 && config->block_n != 64 && config->block_n != 128 && config->block_n != 256 &&
                     !(config->block_n == 32 && layout == DB_CODES_NATURAL)) ||
                    config->max_ctas < 0 ||
-                   (config->pair_ctas != 0 && config->pair_ctas != 1) ||
-                   (config->pair_ctas && layout == DB_CODES_DQ)))
+                   (config->pair_ctas != 0 && config->pair_ctas != 1)))
         return db_fail(DB_ERR_INVALID_ARGUMENT, "INVALID_ARGUMENT", "gemm: bad tile configuration");
     if (M < 0 || N <= 0 || K <= 0 || (bits != 4 && bits != 8) || ldy < N || (layout != DB_CODES_DQ && ldsa < M))
         return db_fail(DB_ERR_INVALID_ARGUMENT, "INVALID_ARGUMENT", "gemm: bad shape");

@@ -20,8 +20,9 @@
 //            tile (8 times at M = 1024), and clock64 traces of such a kernel (converter warps
 //            writing the swizzled tile in shared memory) showed the conversion and its per-stage
 //            hand-over pacing the tensor core at ~2,400 cycles per 64-k stage (MMA: 512).
-//   GEMM     one CTA per SM, persistent over 128 x BN output tiles (BN = 64, 128, 256), 320
-//            threads:
+//   GEMM     one CTA per SM, persistent over 128 x BN output tiles (BN = 64, 128, 256), or over
+//            256 x BN tiles with CTA pairs (cta_group::2: each CTA holds 128 rows of A and BN/2
+//            rows of w', the even CTA issues M = 256 MMAs; no multicast), 320 threads:
 //     warp 0      TMA producer (lane 0): per stage (64 k) the A box (128 x 64 f16) and the w' box
 //                 (BN x 64 f16), both with the 128-byte swizzle (UMMA K-major operands as-is)
 //     warp 1      TMEM owner + MMA issuer (lane 0): four K = 16 MMAs per stage into the tile's
@@ -57,10 +58,11 @@ constexpr int NUM_THREADS = 32 * (EPI_WARP0 + EPI_WARPS);  // 320
 constexpr uint64_t DRAIN_NS = 100000000ull;
 constexpr int UNPACK_CHUNKS = 4;  // 8-k chunks per thread of the unpack pass
 
-template <int BN>
+template <int BN, bool PAIR>
 struct Smem {
+    static constexpr int WR = PAIR ? BN / 2 : BN;           // weight rows held by this CTA
     static constexpr int A_BYTES = BM * KS * 2;             // 16 KB f16 activation box
-    static constexpr int B_BYTES = BN * KS * 2;             // f16 weight box
+    static constexpr int B_BYTES = WR * KS * 2;             // f16 weight box (this CTA's rows)
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int Y_CHUNK = 32 * 16 * 4;             // 32 rows x 16 f32 columns
     static constexpr int Y_BUFS = 2;
@@ -187,13 +189,13 @@ __device__ __forceinline__ bool warp_wait_polite(uint64_t* bar, uint32_t parity,
     return ok != 0;
 }
 
-template <int BN, int EPI>
+template <int BN, int EPI, bool PAIR>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_dq_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                    const __grid_constant__ CUtensorMap tmY, int y_tma, float* __restrict__ y, int64_t ldy, int M,
                    int N, int G, __half* __restrict__ out_codes, int64_t ldoc, const int* __restrict__ nonfinite,
                    int* __restrict__ dev_error) {
-    using S = Smem<BN>;
+    using S = Smem<BN, PAIR>;
     static_assert(BN == 64 || BN == 128 || BN == 256, "tile width");
     static_assert(EPI == DB_EPI_STORE || EPI == DB_EPI_RESIDUAL || (EPI == DB_EPI_SWIGLU_QUANT && BN >= 128),
                   "store, residual, or SwiGLU on whole 64 + 64 blocks");
@@ -211,18 +213,30 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + S::OFF_MISC + 4);
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
-    const int m_tiles = (M + BM - 1) / BM, n_tiles = (N + BN - 1) / BN;
+    // Pair mode: a cluster of two CTAs computes 256 x BN tiles; CTA `rank` holds rows 128*rank.. of
+    // the tile (its A box, its TMEM lanes) and weight rows (BN/2)*rank.. of it, and the even CTA
+    // issues the M = 256 MMAs for both (B is read from both CTAs' shared memory; no multicast).
+    const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+    const bool leader = rank == 0;
+    constexpr int MT = PAIR ? 2 * BM : BM;  // tile rows
+    const int m_tiles = (M + MT - 1) / MT, n_tiles = (N + BN - 1) / BN;
     const int tiles = m_tiles * n_tiles;
-    const int tile0 = (int)blockIdx.x, tstride = (int)gridDim.x;
+    const int tile0 = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+    const int tstride = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+    const int row_off = (int)rank * BM, wrow_off = (int)rank * S::WR;
+    // barrier addresses as the pair sees them (the leader's copies count both CTAs)
+    auto at_leader = [&](uint64_t* b) { return PAIR ? mapa_shared(smem_u32(b), 0) : smem_u32(b); };
+    auto at_peer = [&](uint64_t* b) { return mapa_shared(smem_u32(b), 1); };
 
     if (threadIdx.x == 0) {
+        constexpr int NC = PAIR ? 2 : 1;
         for (int i = 0; i < S::STAGES; ++i) {
-            mbar_init(&full[i], 1);
+            mbar_init(&full[i], NC);
             mbar_init(&empty[i], 1);
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&done[i], 1);
-            mbar_init(&acc_empty[i], EPI_WARPS);
+            mbar_init(&acc_empty[i], NC * EPI_WARPS);
         }
         mbar_init(mma_done, 1);
         mbar_init(end_bar(0), NUM_THREADS / 32);
@@ -236,11 +250,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (y_tma) tma_prefetch_desc(&tmY);
     }
     if (warp == 1) {
-        tmem_alloc(tmem_slot, 2 * BN);
-        tmem_relinquish();
+        if (PAIR) {
+            tmem_alloc_pair(tmem_slot, 2 * BN);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(tmem_slot, 2 * BN);
+            tmem_relinquish();
+        }
     }
     tc_fence_before();
     __syncthreads();
+    if (PAIR) cluster_sync_all();  // the peer's barriers are initialised before any remote arrive
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
     const uint32_t st_base = smem_u32(smem + S::OFF_STAGE);
@@ -254,14 +274,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             int st = 0, issued = 0;
             uint32_t ps = 0;
             for (int tile = tile0; tile < tiles; tile += tstride) {
-                const int m0 = (tile % m_tiles) * BM, n0 = (tile / m_tiles) * BN;
+                const int m0 = (tile % m_tiles) * MT + row_off, n0 = (tile / m_tiles) * BN + wrow_off;
                 for (int g = 0; g < G; ++g) {
                     if (!mbar_spin_polite(&empty[st], ps ^ 1u, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_TMA)) goto drain;
                     uint8_t* sp = smem + S::OFF_STAGE + st * S::STAGE_BYTES;
-                    // full boxes are counted, also where they reach past M or N (zero fill)
-                    mbar_arrive_expect_tx(&full[st], S::STAGE_BYTES);
-                    tma_load_2d(sp, &tmA, &full[st], g * KS, m0);
-                    tma_load_2d(sp + S::A_BYTES, &tmW, &full[st], g * KS, n0);
+                    // full boxes are counted, also where they reach past M or N (zero fill); in pair
+                    // mode both CTAs' bytes count on the leader's barrier
+                    if (PAIR) {
+                        mbar_arrive_expect_tx_cluster(at_leader(&full[st]), S::STAGE_BYTES);
+                        tma_load_2d_pair(sp, &tmA, at_leader(&full[st]), g * KS, m0);
+                        tma_load_2d_pair(sp + S::A_BYTES, &tmW, at_leader(&full[st]), g * KS, n0);
+                    } else {
+                        mbar_arrive_expect_tx(&full[st], S::STAGE_BYTES);
+                        tma_load_2d(sp, &tmA, &full[st], g * KS, m0);
+                        tma_load_2d(sp + S::A_BYTES, &tmW, &full[st], g * KS, n0);
+                    }
                     ++issued;
                     if (++st == S::STAGES) { st = 0; ps ^= 1u; }
                 }
@@ -271,7 +298,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             // after an abort: let the stages this lane issued land before the CTA winds down
             for (int k = 0; k < issued && k < S::STAGES; ++k) {
                 if (st == 0) { st = S::STAGES - 1; ps ^= 1u; } else --st;
-                mbar_wait_drain(&full[st], ps, DRAIN_NS);
+                if (leader) mbar_wait_drain(&full[st], ps, DRAIN_NS);
             }
         prod_done:;
         }
@@ -280,8 +307,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         // ---------------------------------------------------------------- MMA issuer (lane 0)
         // Descriptors are built once and advanced by the stage / k offsets (start address field in
         // 16-byte units; shared memory is below 256 KB, so the 14-bit field never carries).
-        constexpr uint32_t IDESC = idesc_f16_f32(BM, BN);
-        if (lane == 0) {
+        constexpr uint32_t IDESC = idesc_f16_f32(MT, BN);
+        if (leader && lane == 0) {
             const uint64_t a_desc0 = sw128_desc(st_base), b_desc0 = sw128_desc(st_base + S::A_BYTES);
             int st = 0, t = 0;
             uint32_t ps = 0;
@@ -296,18 +323,39 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     tc_fence_after();
                     const uint64_t off = (uint64_t)((st * S::STAGE_BYTES) >> 4);
 #pragma unroll
-                    for (int kk = 0; kk < KS / 16; ++kk)  // K = 16 per MMA: 32 bytes along the row
-                        umma_f16(d, a_desc0 + off + (uint64_t)(kk * 2), b_desc0 + off + (uint64_t)(kk * 2), IDESC,
-                                 (g | kk) != 0 ? 1u : 0u);
-                    umma_commit(&empty[st]);
+                    for (int kk = 0; kk < KS / 16; ++kk) {  // K = 16 per MMA: 32 bytes along the row
+                        const uint64_t ad = a_desc0 + off + (uint64_t)(kk * 2), bd = b_desc0 + off + (uint64_t)(kk * 2);
+                        if (PAIR) umma_f16_pair(d, ad, bd, IDESC, (g | kk) != 0 ? 1u : 0u);
+                        else umma_f16(d, ad, bd, IDESC, (g | kk) != 0 ? 1u : 0u);
+                    }
+                    if (PAIR) {
+                        umma_commit_pair(smem_u32(&empty[st]));
+                        umma_commit_pair(at_peer(&empty[st]));
+                    } else {
+                        umma_commit(&empty[st]);
+                    }
                     if (++st == S::STAGES) { st = 0; ps ^= 1u; }
                 }
-                umma_commit(&done[b]);
+                if (PAIR) {
+                    umma_commit_pair(smem_u32(&done[b]));
+                    umma_commit_pair(at_peer(&done[b]));
+                } else {
+                    umma_commit(&done[b]);
+                }
             }
         mma_end:
             // every MMA this thread issued has completed before the CTA releases tensor memory
-            umma_commit(mma_done);
+            if (PAIR) {
+                umma_commit_pair(smem_u32(mma_done));
+                umma_commit_pair(at_peer(mma_done));
+            } else {
+                umma_commit(mma_done);
+            }
             mbar_wait_drain(mma_done, 0, DRAIN_NS);
+        } else if (!leader && lane == 0) {
+            // the peer CTA's tensor memory is written by the leader's MMAs: wait for their last
+            // commit (a wait as long as the whole launch, so bounded by the launch-wide limit)
+            mbar_wait_drain(mma_done, 0, DB_WAIT_LIMIT_NS);
         }
         __syncwarp();
     } else {
@@ -319,14 +367,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const uint32_t ystage = smem_u32(smem + S::OFF_Y) + (warp - EPI_WARP0) * S::Y_BUFS * S::Y_CHUNK;
         const uint32_t nanv = 0x7fc00000u;
         int ybuf = 0, t = 0;
-        // both accumulator buffers start free
+        // both accumulator buffers start free (the leader's barriers count both CTAs' warps)
+        auto release = [&](int b) {
+            if (PAIR) mbar_arrive_cluster(at_leader(&acc_empty[b]));
+            else mbar_arrive(&acc_empty[b]);
+        };
         if (lane == 0) {
-            mbar_arrive(&acc_empty[0]);
-            mbar_arrive(&acc_empty[1]);
+            release(0);
+            release(1);
         }
         for (int tile = tile0; tile < tiles; tile += tstride, ++t) {
             const int b = t & 1;
-            const int m0 = (tile % m_tiles) * BM, n0 = (tile / m_tiles) * BN;
+            const int m0 = (tile % m_tiles) * MT + row_off, n0 = (tile / m_tiles) * BN;
             if (!warp_wait_polite(&done[b], (uint32_t)(t >> 1) & 1u, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_EPI))
                 goto epi_done;
             tc_fence_after();
@@ -386,7 +438,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 // has none): hand the buffer back
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&acc_empty[b]);
+                if (lane == 0) release(b);
                 continue;
             }
             constexpr int CPW = BN / 64;  // 32-column chunks per warp (half of the tile's columns)
@@ -400,7 +452,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     // every column of the buffer is in registers: hand it back to the MMA issuer
                     tc_fence_before();
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&acc_empty[b]);
+                    if (lane == 0) release(b);
                 }
                 if (!y_tma) {
                     // rows whose stride is not a 16-byte multiple: plain stores of this thread's row
@@ -452,52 +504,73 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     __syncwarp();
     if (lane == 0) mbar_arrive(end_bar(0));
     if (warp == 1) {
-        if (lane == 0) mbar_wait_drain(end_bar(0), 0, DB_WAIT_LIMIT_NS);
+        if (lane == 0) {
+            mbar_wait_drain(end_bar(0), 0, DB_WAIT_LIMIT_NS);
+            if (PAIR) {
+                // neither CTA leaves while the other may still arrive on its barriers or have its
+                // shared memory read by the pair's MMAs
+                mbar_arrive_cluster(mapa_shared(smem_u32(end_bar(1)), rank ^ 1u));
+                mbar_wait_drain(end_bar(1), 0, DB_WAIT_LIMIT_NS);
+            }
+        }
         __syncwarp();
         tc_fence_after();
-        tmem_dealloc(tmem_base, 2 * BN);
+        if (PAIR) tmem_dealloc_pair(tmem_base, 2 * BN);
+        else tmem_dealloc(tmem_base, 2 * BN);
     }
 }
 
-template <int BN, int EPI>
+template <int BN, int EPI, bool PAIR>
 int launch(const DbGemmArgs& a, const CUtensorMap& tmA, const CUtensorMap& tmW, const CUtensorMap& tmY, int y_tma,
            int G, cudaStream_t stream) {
-    using S = Smem<BN>;
-    auto kernel = gemm_dq_kernel<BN, EPI>;
+    using S = Smem<BN, PAIR>;
+    auto kernel = gemm_dq_kernel<BN, EPI, PAIR>;
     {
         const cudaError_t e = db_set_max_smem(reinterpret_cast<const void*>(kernel), S::BYTES);
         if (e != cudaSuccess) return (int)e;
     }
-    const int tiles = ((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN);
+    constexpr int MT = PAIR ? 2 * BM : BM;
+    const int tiles = ((a.M + MT - 1) / MT) * ((a.N + BN - 1) / BN);
     int units = a.max_ctas > 0 ? a.max_ctas : db_num_sms();
+    if (PAIR) units /= 2;
     if (units > tiles) units = tiles;
     if (units < 1) units = 1;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)units);
+    cfg.gridDim = dim3((unsigned)(PAIR ? 2 * units : units));
     cfg.blockDim = dim3(NUM_THREADS);
     cfg.dynamicSmemBytes = S::BYTES;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = PAIR ? 2 : 1;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, tmA, tmW, tmY, y_tma, a.y, a.ldy, a.M, a.N, G,
                                              static_cast<__half*>(a.out_codes), a.ldoc, a.nonfinite, a.dev_error);
     return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }
 
-template <int EPI>
+template <int EPI, bool PAIR>
 int launch_bn(const DbGemmArgs& a, int bn, const CUtensorMap& tmA, const CUtensorMap& tmW, const CUtensorMap& tmY,
               int y_tma, int G, cudaStream_t s) {
     if constexpr (EPI == DB_EPI_SWIGLU_QUANT) {
-        if (bn == 128) return launch<128, EPI>(a, tmA, tmW, tmY, y_tma, G, s);
-        return launch<256, EPI>(a, tmA, tmW, tmY, y_tma, G, s);
+        if (bn == 128) return launch<128, EPI, PAIR>(a, tmA, tmW, tmY, y_tma, G, s);
+        return launch<256, EPI, PAIR>(a, tmA, tmW, tmY, y_tma, G, s);
     } else {
-        if (bn == 64) return launch<64, EPI>(a, tmA, tmW, tmY, y_tma, G, s);
-        if (bn == 128) return launch<128, EPI>(a, tmA, tmW, tmY, y_tma, G, s);
-        return launch<256, EPI>(a, tmA, tmW, tmY, y_tma, G, s);
+        if (bn == 64) return launch<64, EPI, PAIR>(a, tmA, tmW, tmY, y_tma, G, s);
+        if (bn == 128) return launch<128, EPI, PAIR>(a, tmA, tmW, tmY, y_tma, G, s);
+        return launch<256, EPI, PAIR>(a, tmA, tmW, tmY, y_tma, G, s);
     }
+}
+template <int EPI>
+int launch_pair(const DbGemmArgs& a, int bn, bool pair, const CUtensorMap& tmA, const CUtensorMap& tmW,
+                const CUtensorMap& tmY, int y_tma, int G, cudaStream_t s) {
+    return pair ? launch_bn<EPI, true>(a, bn, tmA, tmW, tmY, y_tma, G, s)
+                : launch_bn<EPI, false>(a, bn, tmA, tmW, tmY, y_tma, G, s);
 }
 
 }  // namespace gdq
@@ -549,13 +622,15 @@ int db_launch_gemm_dq(const DbGemmArgs& a, cudaStream_t stream) {
     if (a.M <= 0 || a.N <= 0) return 0;
     const bool swiglu = a.epilogue == DB_EPI_SWIGLU_QUANT;
     if (a.K <= 0 || (a.bits != 4 && a.bits != 8) || (a.block != 0 && a.block != 64) ||
-        (a.epilogue != DB_EPI_STORE && a.epilogue != DB_EPI_RESIDUAL && !swiglu) || a.pair_ctas)
+        (a.epilogue != DB_EPI_STORE && a.epilogue != DB_EPI_RESIDUAL && !swiglu))
         return (int)cudaErrorInvalidValue;
     DbEncodeTiledFn enc = db_encode_tiled();
     if (!enc) return (int)cudaErrorNotSupported;
     const int G = (a.K + 63) / 64, Kp = G * 64;
     int bn = a.block_n ? a.block_n : db_gemm_dq_default_block_n(a.M, a.N);
     if (bn != 64 && bn != 128 && bn != 256) return (int)cudaErrorInvalidValue;
+    // CTA pairs (M = 256 MMAs) when asked for and there are rows for both CTAs
+    const bool pair = a.pair_ctas && a.M > BM;
     if (swiglu) {
         // SwiGLU: whole blocks of 64 gate + 64 up columns per tile; out_codes f16 [M, ldoc]
         if (bn == 64) bn = 128;
@@ -603,7 +678,7 @@ int db_launch_gemm_dq(const DbGemmArgs& a, cudaStream_t stream) {
     if (!rc) {
         cuuint64_t dims[2] = {(cuuint64_t)Kp, (cuuint64_t)a.N};
         cuuint64_t strides[1] = {(cuuint64_t)Kp * 2};
-        cuuint32_t box[2] = {KS, (cuuint32_t)bn};
+        cuuint32_t box[2] = {KS, (cuuint32_t)(pair ? bn / 2 : bn)};  // this CTA's weight rows
         cuuint32_t estr[2] = {1, 1};
         if (enc(&tmW, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, wq, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                 CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -621,8 +696,8 @@ int db_launch_gemm_dq(const DbGemmArgs& a, cudaStream_t stream) {
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
     }
     if (!rc)
-        rc = swiglu ? launch_bn<DB_EPI_SWIGLU_QUANT>(a, bn, tmA, tmW, tmY, y_tma, G, stream)
-             : a.epilogue == DB_EPI_RESIDUAL ? launch_bn<DB_EPI_RESIDUAL>(a, bn, tmA, tmW, tmY, y_tma, G, stream)
-                                             : launch_bn<DB_EPI_STORE>(a, bn, tmA, tmW, tmY, y_tma, G, stream);
+        rc = swiglu ? launch_pair<DB_EPI_SWIGLU_QUANT>(a, bn, pair, tmA, tmW, tmY, y_tma, G, stream)
+             : a.epilogue == DB_EPI_RESIDUAL ? launch_pair<DB_EPI_RESIDUAL>(a, bn, pair, tmA, tmW, tmY, y_tma, G, stream)
+                                             : launch_pair<DB_EPI_STORE>(a, bn, pair, tmA, tmW, tmY, y_tma, G, stream);
     return rc;
 }

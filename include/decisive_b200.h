@@ -114,8 +114,7 @@ int db_dequant_rows_g64(const uint8_t *codes, const float *scales, int64_t N, in
  * a library scratch buffer (N x Kp f16, kept per device and stream and grown when a call needs
  * more; growing is refused while the stream is being captured) and y = the tcgen05 kind::f16 sum
  * over all K in f32.  Not bit-exact against the grouped fold: within ~1.5e-3 of the output RMS
- * (the contract is 2e-3); every tile configuration gives the same bits.  Single CTAs only
- * (pair_ctas 0). */
+ * (the contract is 2e-3); every tile configuration gives the same bits. */
 int db_gemm_g64(const void *a_codes, int layout, int64_t lda, const float *sa, const int32_t *a_sums, int64_t ldsa,
                 const uint8_t *w_codes, const float *sw, int64_t M, int64_t N, int64_t K, int bits, int fused,
                 int residual, float *y, int64_t ldy, const int *nonfinite, void *stream);

@@ -101,22 +101,23 @@ def test_dq_activation_layout_is_dequantised_oracle_codes(db, oracle, m, k):
     assert np.array_equal(a.cpu().numpy().view(np.uint16), expect.view(np.uint16))
 
 
-DQ_CONFIGS = [(0, 0), (256, 0), (128, 0), (64, 0), (256, 5), (128, 7), (64, 3), (64, 1)]
+DQ_CONFIGS = [(0, 0, 0), (256, 0, 0), (128, 0, 0), (64, 0, 0), (256, 5, 0), (128, 7, 0), (64, 3, 0), (64, 1, 0),
+              (256, 0, 1), (128, 0, 1), (64, 0, 1), (256, 6, 1), (64, 3, 1)]
 
 
 @pytest.mark.parametrize("m,k,n", [(200, 1000, 300), (1024, 1024, 3072), (257, 130, 129), (129, 3072, 1024),
                                    (37, 200, 70)])
 @pytest.mark.parametrize("wb", [4, 8])
 def test_dq_tile_configurations_are_bitwise_equal(db, oracle, m, k, n, wb):
-    """Every tile width and grid cap gives the same bits, for the store and the residual (TMA
-    reduce-add: y = base + acc, one f32 rounding) epilogues."""
+    """Every tile width, grid cap and CTA pairing (M = 256 MMAs over two CTAs) gives the same bits,
+    for the store and the residual (TMA reduce-add: y = base + acc, one f32 rounding) epilogues."""
     x, bf = _inputs(oracle, m, k, n, seed=1)
     codes, scales = db.pack_weights(torch.from_numpy(bf.view(np.int16)).cuda(), wb)
     a, _, _ = db.quantize_activations(torch.from_numpy(x).cuda(), bits=8, layout=db.CODES_DQ)
     base = torch.randn(m, n, device="cuda")
     first = None
-    for bn, cap in DQ_CONFIGS:
-        cfg = db.GemmConfig(bn, cap, 0)
+    for bn, cap, pair in DQ_CONFIGS:
+        cfg = db.GemmConfig(bn, cap, pair)
         y = db.gemm(a, db.CODES_DQ, None, codes, scales, m, n, k, wb, config=cfg)
         r = db.gemm(a, db.CODES_DQ, None, codes, scales, m, n, k, wb, residual=base.clone(), config=cfg)
         torch.cuda.synchronize()
@@ -124,8 +125,8 @@ def test_dq_tile_configurations_are_bitwise_equal(db, oracle, m, k, n, wb):
         y, r = y.cpu().numpy(), r.cpu().numpy()
         if first is None:
             first = y
-        assert bits_equal(y, first), f"store epilogue differs for config {(bn, cap)}"
-        assert bits_equal(r, (base.cpu().numpy() + y).astype(np.float32)), f"residual differs for {(bn, cap)}"
+        assert bits_equal(y, first), f"store epilogue differs for config {(bn, cap, pair)}"
+        assert bits_equal(r, (base.cpu().numpy() + y).astype(np.float32)), f"residual differs for {(bn, cap, pair)}"
 
 
 def test_dq_nonfinite_input_gives_nan(db, oracle):
@@ -137,11 +138,3 @@ def test_dq_nonfinite_input_gives_nan(db, oracle):
     y = db.gemm(a, db.CODES_DQ, None, codes, scales, 64, 128, 256, 4, nonfinite=flag)
     torch.cuda.synchronize()
     assert int(flag.item()) == 1 and bool(torch.isnan(y).all())
-
-
-def test_dq_rejects_cta_pairs(db):
-    a = torch.zeros((256, 64), dtype=torch.float16, device="cuda")
-    codes = torch.zeros((128, 32), dtype=torch.uint8, device="cuda")
-    scales = torch.zeros((1, 128), dtype=torch.float32, device="cuda")
-    with pytest.raises(Exception):
-        db.gemm(a, db.CODES_DQ, None, codes, scales, 256, 128, 64, 4, config=db.GemmConfig(128, 0, 1))
