@@ -193,8 +193,8 @@ template <int BN, int EPI, bool PAIR>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_dq_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                    const __grid_constant__ CUtensorMap tmY, int y_tma, float* __restrict__ y, int64_t ldy, int M,
-                   int N, int G, __half* __restrict__ out_codes, int64_t ldoc, const int* __restrict__ nonfinite,
-                   int* __restrict__ dev_error) {
+                   int N, int G, int ksplit, __half* __restrict__ out_codes, int64_t ldoc,
+                   const int* __restrict__ nonfinite, int* __restrict__ dev_error) {
     using S = Smem<BN, PAIR>;
     static_assert(BN == 64 || BN == 128 || BN == 256, "tile width");
     static_assert(EPI == DB_EPI_STORE || EPI == DB_EPI_RESIDUAL || (EPI == DB_EPI_SWIGLU_QUANT && BN >= 128),
@@ -220,7 +220,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const bool leader = rank == 0;
     constexpr int MT = PAIR ? 2 * BM : BM;  // tile rows
     const int m_tiles = (M + MT - 1) / MT, n_tiles = (N + BN - 1) / BN;
-    const int tiles = m_tiles * n_tiles;
+    // Work units: a tile, or with ksplit = 2 one half of a tile's K range (its partial sum goes to
+    // its own output buffer, rows s*M.., and the consumer adds the halves in a fixed order)
+    const int units = m_tiles * n_tiles * ksplit;
+    const int gsplit = (G + ksplit - 1) / ksplit;
     const int tile0 = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
     const int tstride = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
     const int row_off = (int)rank * BM, wrow_off = (int)rank * S::WR;
@@ -273,9 +276,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (lane == 0) {
             int st = 0, issued = 0;
             uint32_t ps = 0;
-            for (int tile = tile0; tile < tiles; tile += tstride) {
+            for (int unit = tile0; unit < units; unit += tstride) {
+                const int tile = unit / ksplit, gb = (unit % ksplit) * gsplit, ge = min(G, gb + gsplit);
                 const int m0 = (tile % m_tiles) * MT + row_off, n0 = (tile / m_tiles) * BN + wrow_off;
-                for (int g = 0; g < G; ++g) {
+                for (int g = gb; g < ge; ++g) {
                     if (!mbar_spin_polite(&empty[st], ps ^ 1u, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_TMA)) goto drain;
                     uint8_t* sp = smem + S::OFF_STAGE + st * S::STAGE_BYTES;
                     // full boxes are counted, also where they reach past M or N (zero fill); in pair
@@ -312,21 +316,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const uint64_t a_desc0 = sw128_desc(st_base), b_desc0 = sw128_desc(st_base + S::A_BYTES);
             int st = 0, t = 0;
             uint32_t ps = 0;
-            for (int tile = tile0; tile < tiles; tile += tstride, ++t) {
+            for (int unit = tile0; unit < units; unit += tstride, ++t) {
                 const int b = t & 1;
+                const int gb = (unit % ksplit) * gsplit, ge = min(G, gb + gsplit);
                 if (!mbar_spin(&acc_empty[b], (uint32_t)(t >> 1) & 1u, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_MMA))
                     goto mma_end;
                 tc_fence_after();
                 const uint32_t d = tmem_base + (uint32_t)(b * BN);
-                for (int g = 0; g < G; ++g) {
+                for (int g = gb; g < ge; ++g) {
                     if (!mbar_spin(&full[st], ps, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_MMA)) goto mma_end;
                     tc_fence_after();
                     const uint64_t off = (uint64_t)((st * S::STAGE_BYTES) >> 4);
 #pragma unroll
                     for (int kk = 0; kk < KS / 16; ++kk) {  // K = 16 per MMA: 32 bytes along the row
                         const uint64_t ad = a_desc0 + off + (uint64_t)(kk * 2), bd = b_desc0 + off + (uint64_t)(kk * 2);
-                        if (PAIR) umma_f16_pair(d, ad, bd, IDESC, (g | kk) != 0 ? 1u : 0u);
-                        else umma_f16(d, ad, bd, IDESC, (g | kk) != 0 ? 1u : 0u);
+                        const uint32_t acc_in = (g != gb || kk != 0) ? 1u : 0u;  // a unit starts from zero
+                        if (PAIR) umma_f16_pair(d, ad, bd, IDESC, acc_in);
+                        else umma_f16(d, ad, bd, IDESC, acc_in);
                     }
                     if (PAIR) {
                         umma_commit_pair(smem_u32(&empty[st]));
@@ -376,8 +382,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             release(0);
             release(1);
         }
-        for (int tile = tile0; tile < tiles; tile += tstride, ++t) {
+        for (int unit = tile0; unit < units; unit += tstride, ++t) {
             const int b = t & 1;
+            const int tile = unit / ksplit, split = unit % ksplit;
             const int m0 = (tile % m_tiles) * MT + row_off, n0 = (tile / m_tiles) * BN;
             if (!warp_wait_polite(&done[b], (uint32_t)(t >> 1) & 1u, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_EPI))
                 goto epi_done;
@@ -455,16 +462,27 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     if (lane == 0) release(b);
                 }
                 if (!y_tma) {
-                    // rows whose stride is not a 16-byte multiple: plain stores of this thread's row
+                    // plain stores of this thread's row: rows whose stride is not a 16-byte multiple,
+                    // or the partial sums of split units (split s writes rows s*M..)
                     const int m = m0 + q * 32 + lane;
                     if (m < M) {
-                        float* dst = y + (size_t)m * ldy;
+                        float* dst = y + ((size_t)split * M + m) * ldy;
+                        const int nb = n0 + c * 32;
+                        if (EPI == DB_EPI_STORE && nb + 32 <= N && ((reinterpret_cast<uintptr_t>(dst + nb) & 15) == 0)) {
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) {
-                            const int n = n0 + c * 32 + j;
-                            if (n < N) {
-                                const float o = any_nonfinite ? __uint_as_float(nanv) : __uint_as_float(v[j]);
-                                dst[n] = EPI == DB_EPI_RESIDUAL ? __fadd_rn(dst[n], o) : o;
+                            for (int j = 0; j < 8; ++j) {
+                                uint4 o = make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                                if (any_nonfinite) o = make_uint4(nanv, nanv, nanv, nanv);
+                                reinterpret_cast<uint4*>(dst + nb)[j] = o;
+                            }
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) {
+                                const int n = nb + j;
+                                if (n < N) {
+                                    const float o = any_nonfinite ? __uint_as_float(nanv) : __uint_as_float(v[j]);
+                                    dst[n] = EPI == DB_EPI_RESIDUAL ? __fadd_rn(dst[n], o) : o;
+                                }
                             }
                         }
                     }
@@ -530,7 +548,8 @@ int launch(const DbGemmArgs& a, const CUtensorMap& tmA, const CUtensorMap& tmW, 
         if (e != cudaSuccess) return (int)e;
     }
     constexpr int MT = PAIR ? 2 * BM : BM;
-    const int tiles = ((a.M + MT - 1) / MT) * ((a.N + BN - 1) / BN);
+    const int ksplit = a.k_splits > 1 ? a.k_splits : 1;
+    const int tiles = ((a.M + MT - 1) / MT) * ((a.N + BN - 1) / BN) * ksplit;
     int units = a.max_ctas > 0 ? a.max_ctas : db_num_sms();
     if (PAIR) units /= 2;
     if (units > tiles) units = tiles;
@@ -549,7 +568,7 @@ int launch(const DbGemmArgs& a, const CUtensorMap& tmA, const CUtensorMap& tmW, 
     attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, tmA, tmW, tmY, y_tma, a.y, a.ldy, a.M, a.N, G,
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, tmA, tmW, tmY, y_tma, a.y, a.ldy, a.M, a.N, G, ksplit,
                                              static_cast<__half*>(a.out_codes), a.ldoc, a.nonfinite, a.dev_error);
     return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }
@@ -580,10 +599,10 @@ int launch_pair(const DbGemmArgs& a, int bn, bool pair, const CUtensorMap& tmA, 
 // least 96 tiles (two thirds of the SMs); persistent CTAs overlap a tile's epilogue with the next
 // tile's MMAs, so a partial last wave costs less than narrower tiles do (measured on the C2
 // projections: 256 for N = 3072, 4096, 6144 at M = 1024, 64 for N = 1024).
-int db_gemm_dq_default_block_n(int64_t M, int64_t N) {
-    const int64_t mt = (M + 127) / 128;
+int db_gemm_dq_default_block_n(int64_t M, int64_t N, int k_splits) {
+    const int64_t mt = (M + 127) / 128, ks = k_splits > 1 ? k_splits : 1;
     for (int bn : {256, 128}) {
-        if (mt * ((N + bn - 1) / bn) >= 96) return bn;
+        if (mt * ((N + bn - 1) / bn) * ks >= 96) return bn;
     }
     return 64;
 }
@@ -627,10 +646,15 @@ int db_launch_gemm_dq(const DbGemmArgs& a, cudaStream_t stream) {
     DbEncodeTiledFn enc = db_encode_tiled();
     if (!enc) return (int)cudaErrorNotSupported;
     const int G = (a.K + 63) / 64, Kp = G * 64;
-    int bn = a.block_n ? a.block_n : db_gemm_dq_default_block_n(a.M, a.N);
+    int bn = a.block_n ? a.block_n : db_gemm_dq_default_block_n(a.M, a.N, a.k_splits);
     if (bn != 64 && bn != 128 && bn != 256) return (int)cudaErrorInvalidValue;
     // CTA pairs (M = 256 MMAs) when asked for and there are rows for both CTAs
     const bool pair = a.pair_ctas && a.M > BM;
+    // split K: two halves of every tile's K range, their partial sums stored to y rows 0..M-1 and
+    // M..2M-1 (store epilogue only; y holds 2M rows)
+    const bool split = a.k_splits > 1;
+    if (a.k_splits < 0 || a.k_splits > 2 || (split && (a.epilogue != DB_EPI_STORE || pair || G < 2)))
+        return (int)cudaErrorInvalidValue;
     if (swiglu) {
         // SwiGLU: whole blocks of 64 gate + 64 up columns per tile; out_codes f16 [M, ldoc]
         if (bn == 64) bn = 128;
@@ -686,7 +710,7 @@ int db_launch_gemm_dq(const DbGemmArgs& a, cudaStream_t stream) {
             rc = (int)cudaErrorInvalidValue;
     }
     // output tensor map for the TMA store / reduce-add (16-byte aligned rows; else plain stores)
-    if (!rc && !swiglu && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0 && (a.ldy & 3) == 0) {
+    if (!rc && !swiglu && !split && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0 && (a.ldy & 3) == 0) {
         cuuint64_t dims[2] = {(cuuint64_t)a.N, (cuuint64_t)a.M};
         cuuint64_t strides[1] = {(cuuint64_t)a.ldy * 4};
         cuuint32_t box[2] = {16, 32};

@@ -74,6 +74,7 @@ struct DbGemmArgs {
     int add_bias;
     void* w_scratch;       // dequantised GEMM: f16 [N, Kp] for the unpacked weights (null: cached buffer)
     int overlap_unpack;    // 1: no running kernel reads w_scratch, so the unpack overlaps the previous kernel
+    int k_splits;          // dequantised GEMM, store epilogue: 2 = two K halves into y rows 0..M-1, M..2M-1
 };
 int db_launch_gemm_tc(const DbGemmArgs& args, cudaStream_t stream);
 // The same GEMM on int8 activation codes in natural order (DB_CODES_NATURAL_I8, a_codes [M, lda]
@@ -86,7 +87,7 @@ int db_launch_gemm_i8(const DbGemmArgs& args, cudaStream_t stream);
 // (db_gemm_dq_scratch_bytes; null: a library buffer cached per device and stream), then tcgen05 kind::f16
 // with f32 accumulation over the whole K; store or residual epilogue, tile widths 64/128/256.
 int db_launch_gemm_dq(const DbGemmArgs& args, cudaStream_t stream);
-int db_gemm_dq_default_block_n(int64_t M, int64_t N);
+int db_gemm_dq_default_block_n(int64_t M, int64_t N, int k_splits = 1);
 size_t db_gemm_dq_scratch_bytes(int64_t N, int64_t K);
 
 // Small-M path: int8 A codes (GEMV order) [M, lda] + sums [G, ldsa], sa [G, ldsa].

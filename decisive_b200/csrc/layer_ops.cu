@@ -28,11 +28,15 @@ __device__ __forceinline__ int gemv_pos(int k) {
 // 2b+1 hold the two halves (k0..k3, k4..k7) of one 8-code block; they swap halves with one
 // shuffle so each lane writes its part of the block's stored order with a single 8-byte
 // (tensor-core f16 order) or 4-byte (GEMV int8 order) store.
-__global__ void rms_quantize_kernel(const float* __restrict__ x, int64_t ldx, const float* __restrict__ w, int T,
+// add0 / add1 (optional, [T, D] with row stride D): the two K-half partial sums of the projection
+// that feeds the residual stream (dequantised mode); x = (x + add0) + add1 is written back to x
+// first, then normalised as usual.
+__global__ void rms_quantize_kernel(float* __restrict__ x, int64_t ldx, const float* __restrict__ w, int T,
                                     int D, float eps, int zero_centered, int normalize, float* __restrict__ normed,
                                     int64_t ldn, void* __restrict__ codes, int layout, int64_t ldc,
                                     float* __restrict__ scales, int32_t* __restrict__ sums, int64_t lds,
-                                    int* __restrict__ nonfinite) {
+                                    int* __restrict__ nonfinite, const float* __restrict__ add0,
+                                    const float* __restrict__ add1) {
     __shared__ float partial[32];
     pdl_wait();
     // dequantised layout: the next kernel is the projection's weight unpack, which reads nothing
@@ -40,7 +44,14 @@ __global__ void rms_quantize_kernel(const float* __restrict__ x, int64_t ldx, co
     if (layout == DB_CODES_DQ_F16) pdl_trigger();
     const int t = blockIdx.x, lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     const int c = 4 * threadIdx.x;
-    const float4 v = *reinterpret_cast<const float4*>(x + (size_t)t * ldx + c);
+    float4 v = *reinterpret_cast<const float4*>(x + (size_t)t * ldx + c);
+    if (add0) {
+        const float4 p = *reinterpret_cast<const float4*>(add0 + (size_t)t * D + c);
+        const float4 q = *reinterpret_cast<const float4*>(add1 + (size_t)t * D + c);
+        v = make_float4(__fadd_rn(__fadd_rn(v.x, p.x), q.x), __fadd_rn(__fadd_rn(v.y, p.y), q.y),
+                        __fadd_rn(__fadd_rn(v.z, p.z), q.z), __fadd_rn(__fadd_rn(v.w, p.w), q.w));
+        *reinterpret_cast<float4*>(x + (size_t)t * ldx + c) = v;
+    }
     const bool bad = !(isfinite(v.x) && isfinite(v.y) && isfinite(v.z) && isfinite(v.w));
     if (__any_sync(0xffffffffu, bad) && lane == 0 && nonfinite) atomicOr(nonfinite, 1);
     float scale = 1.f;
@@ -225,12 +236,14 @@ using namespace db;
 
 int db_launch_rms_quantize(const float* x, int64_t ldx, const float* w, int T, int D, float eps, int zero_centered,
                            float* normed, int64_t ldn, void* codes, int layout, int64_t ldc, float* scales,
-                           int32_t* sums, int64_t lds, int* nonfinite, cudaStream_t stream, int normalize) {
+                           int32_t* sums, int64_t lds, int* nonfinite, cudaStream_t stream, int normalize,
+                           const float* add0, const float* add1) {
     if (T <= 0) return 0;
-    if (D % 128 || D > 4096) return (int)cudaErrorInvalidValue;
-    const cudaError_t e = db_launch_pdl(rms_quantize_kernel, dim3(T), dim3(D / 4), 0, stream, x, ldx, w, T, D, eps,
-                                        zero_centered, normalize, normed, ldn, codes, layout, ldc, scales, sums, lds,
-                                        nonfinite);
+    if (D % 128 || D > 4096 || (add0 == nullptr) != (add1 == nullptr)) return (int)cudaErrorInvalidValue;
+    // with add0 / add1 the kernel updates x in place (x is the caller's writable residual stream)
+    const cudaError_t e = db_launch_pdl(rms_quantize_kernel, dim3(T), dim3(D / 4), 0, stream, const_cast<float*>(x), ldx,
+                                        w, T, D, eps, zero_centered, normalize, normed, ldn, codes, layout, ldc, scales,
+                                        sums, lds, nonfinite, add0, add1);
     return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }
 

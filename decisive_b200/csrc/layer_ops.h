@@ -6,7 +6,8 @@
 
 int db_launch_rms_quantize(const float* x, int64_t ldx, const float* w, int T, int D, float eps, int zero_centered,
                            float* normed, int64_t ldn, void* codes, int layout, int64_t ldc, float* scales,
-                           int32_t* sums, int64_t lds, int* nonfinite, cudaStream_t stream, int normalize = 1);
+                           int32_t* sums, int64_t lds, int* nonfinite, cudaStream_t stream, int normalize = 1,
+                           const float* add0 = nullptr, const float* add1 = nullptr);
 // Rows are items of seq_len tokens (0 = T) one after another; row t gets RoPE position
 // pos0 + t % seq_len (a continuation after a cached prefix of pos0 tokens), or positions[t] when
 // positions (device, T ints) is given (ragged sequences packed together).

@@ -111,6 +111,9 @@ struct db_model {
     // while the previous GEMM may still read the other buffer)
     bool dq = false;
     void* dq_w[2] = {nullptr, nullptr};
+    // dequantised mode: the o and down projections split K in two; their partial sums ([2, T, D])
+    // are added to the residual stream by the next RMSNorm kernel
+    float* dq_part = nullptr;
     // per-launch CUDA-event profiling (mirror of the reference's projection_ms accounting,
     // cpu.rs:8-16 / native.rs:229-258), enabled by db_model_profile
     bool profile = false;
@@ -246,7 +249,8 @@ int ensure_workspace(db_model* m, int T) {
         m->alloc(&m->sa, (size_t)Gmax * db_scale_stride(T), v) || m->alloc(&m->sh, (size_t)(F / 64) * db_scale_stride(T), v) ||
         m->alloc(&m->acodes, (size_t)T * Kmax, v) || m->alloc(&m->hcodes, (size_t)T * F, v) ||
         m->alloc(&m->q16, (size_t)T * m->Nq(), v) || m->alloc(&m->k16, (size_t)T * m->Nk(), v) ||
-        m->alloc(&m->v16, (size_t)T * m->Nk(), v) || m->alloc(&m->ids, T, v) || m->alloc(&m->flag, 4, v))
+        m->alloc(&m->v16, (size_t)T * m->Nk(), v) || m->alloc(&m->ids, T, v) || m->alloc(&m->flag, 4, v) ||
+        (m->dq && m->alloc(&m->dq_part, (size_t)2 * T * D, v)))
         return db_fail(DB_ERR_CUDA, "RESOURCE_LIMIT", "workspace exceeds device limits");
     m->cap_T = T;
     return ensure_rope(m, T);
@@ -391,8 +395,9 @@ int enqueue_forward(db_model* m, int T, const volatile uint8_t* cancel, const Pa
         return db_launch_gemm_i8(g, st);
     };
     auto gemm = [&](int proj, const void* a, const uint8_t* wc, const float* ws, const float* sa, int N, int K, int epi,
-                    float* y, int64_t ldy) {
+                    float* y, int64_t ldy, int ksplit = 0) {
         DbGemmArgs g{};
+        g.k_splits = ksplit;
         g.a_codes = a;
         g.lda = ld_codes;
         g.sa = sa;
@@ -444,14 +449,22 @@ int enqueue_forward(db_model* m, int T, const volatile uint8_t* cancel, const Pa
         upload(0);
         if (c.layers > 1) upload(1);
     }
+    // dequantised mode: the o and down projections store two K-half partial sums (dq_part); the next
+    // RMSNorm kernel adds them to the residual stream, (x + p0) + p1, in that order
+    const float* pend = nullptr;
+    auto take = [&](int i) -> const float* {
+        if (!pend) return nullptr;
+        return i == 0 ? pend : pend + (size_t)R * D;
+    };
     for (int l = 0; l < c.layers && !rc; ++l) {
         if (cancel && *cancel) return 1;
         if (m->streaming) cudaStreamWaitEvent(st, m->uploaded[l & 1], 0);
         const LayerW w = m->streaming ? bank_layer(l) : m->layers[l];
         rc = timed(1, [&] {
             return db_launch_rms_quantize(m->x, D, w.in_norm, R, D, c.eps, 0, nullptr, 0, m->acodes, code_layout,
-                                          ld_codes, m->sa, nullptr, lds, m->flag, st);
+                                          ld_codes, m->sa, nullptr, lds, m->flag, st, 1, take(0), take(1));
         });
+        pend = nullptr;
         if (!rc) rc = timed(2, [&] { return gemm(0, m->acodes, w.qkv_c, w.qkv_s, m->sa, Nqkv, D, DB_EPI_STORE, m->qkv, Nqkv); });
         if (!rc)
             rc = timed(3, [&] {
@@ -476,12 +489,18 @@ int enqueue_forward(db_model* m, int T, const volatile uint8_t* cancel, const Pa
                                                         c.q_heads, c.kv_heads, attn_scale,
                                                         m->acodes, ld_codes, m->sa, lds, m->flag, st, attn_codes);
             });
-        if (!rc) rc = timed(6, [&] { return gemm(1, m->acodes, w.o_c, w.o_s, m->sa, D, Nq, DB_EPI_RESIDUAL, m->x, D); });
+        if (!rc && m->dq) {
+            rc = timed(6, [&] { return gemm(1, m->acodes, w.o_c, w.o_s, m->sa, D, Nq, DB_EPI_STORE, m->dq_part, D, 2); });
+            pend = m->dq_part;
+        } else if (!rc) {
+            rc = timed(6, [&] { return gemm(1, m->acodes, w.o_c, w.o_s, m->sa, D, Nq, DB_EPI_RESIDUAL, m->x, D); });
+        }
         if (!rc)
             rc = timed(1, [&] {
                 return db_launch_rms_quantize(m->x, D, w.post_norm, R, D, c.eps, 0, nullptr, 0, m->acodes, code_layout,
-                                              ld_codes, m->sa, nullptr, lds, m->flag, st);
+                                              ld_codes, m->sa, nullptr, lds, m->flag, st, 1, take(0), take(1));
             });
+        pend = nullptr;
         if (!rc)
             rc = timed(7, [&] { return gemm(2, m->acodes, w.gu_c, w.gu_s, m->sa, 2 * F, D, DB_EPI_SWIGLU_QUANT, nullptr, 0); });
         if (!rc) rc = timed(8, [&] {
@@ -500,10 +519,16 @@ int enqueue_forward(db_model* m, int T, const volatile uint8_t* cancel, const Pa
             g.epilogue = DB_EPI_RESIDUAL;
             g.y = m->x;
             g.ldy = D;
+            if (m->dq) {
+                g.epilogue = DB_EPI_STORE;  // two K-half partial sums, added by the next RMSNorm
+                g.y = m->dq_part;
+                g.k_splits = 2;
+            }
             g.nonfinite = m->flag;
             g.dev_error = m->dev_err;
             return launch(3, g);
         });
+        if (!rc && m->dq) pend = m->dq_part;
         if (m->streaming) {
             cudaEventRecord(m->consumed[l & 1], st);
             if (l + 2 < c.layers) upload(l + 2);
@@ -512,7 +537,7 @@ int enqueue_forward(db_model* m, int T, const volatile uint8_t* cancel, const Pa
     if (!rc)
         rc = timed(9, [&] {
             return db_launch_rms_quantize(m->x, D, m->final_norm, R, D, c.eps, 0, m->normed, D, nullptr, DB_CODES_TC, 0,
-                                          nullptr, nullptr, 0, m->flag, st);
+                                          nullptr, nullptr, 0, m->flag, st, 1, take(0), take(1));
         });
     if (!rc && pass && pass->cu)
         rc = timed(10, [&] { return db_launch_mean_pool_varlen(m->normed, D, pass->cu, pass->nseq, D, m->pooled, st); });
@@ -1035,6 +1060,12 @@ int db_model_set_code_layout(db_model* m, int layout) {
             }
             m->allocations.push_back(m->dq_w[i]);
         }
+    }
+    if (dq != m->dq) {
+        // the workspace holds the split-K partial sums in dequantised mode only
+        m->free_all(m->ws_allocations);
+        m->cap_T = 0;
+        m->dq_part = nullptr;
     }
     m->dq = dq;
     // the LM head and the int8 paths outside the layers keep int8 codes in dequantised mode
