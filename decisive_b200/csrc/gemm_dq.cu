@@ -180,6 +180,34 @@ __device__ __forceinline__ void tie32(uint32_t (&r)[32]) {
                    "+r"(r[29]), "+r"(r[30]), "+r"(r[31]));
 }
 
+// One stage of the MMA issuer in one asm block: the test of the NEXT stage's full barrier goes out
+// first, then the stage's four K = 16 MMAs (the first with accumulate = acc_first) and its commit,
+// and only then is the test's result read, so the ~250-cycle mbarrier round trip overlaps the
+// issue of the MMAs instead of preceding it (warps issue in order: a read of the result right
+// after the test would stall the MMAs behind it).  Returns the next stage's test result.
+__device__ __forceinline__ uint32_t umma4_f16_commit_test(uint32_t d, uint64_t a0, uint64_t a1, uint64_t a2,
+                                                         uint64_t a3, uint64_t b0, uint64_t b1, uint64_t b2,
+                                                         uint64_t b3, uint32_t idesc, uint32_t acc_first,
+                                                         uint32_t commit_bar, uint32_t test_bar, uint32_t test_parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p, t, q;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 q, [%13], %14;\n\t"
+        "setp.ne.b32 p, %11, 0;\n\t"
+        "setp.eq.u32 t, 0, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%1], %2, %6, %10, p;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%1], %3, %7, %10, t;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%1], %4, %8, %10, t;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%1], %5, %9, %10, t;\n\t"
+        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%12];\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(ok)
+        : "r"(d), "l"(a0), "l"(a1), "l"(a2), "l"(a3), "l"(b0), "l"(b1), "l"(b2), "l"(b3), "r"(idesc), "r"(acc_first),
+          "r"(commit_bar), "r"(test_bar), "r"(test_parity)
+        : "memory");
+    return ok;
+}
+
 __device__ __forceinline__ bool warp_wait_polite(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err,
                                                  int code) {
     int ok = 1;
@@ -315,7 +343,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (leader && lane == 0) {
             const uint64_t a_desc0 = sw128_desc(st_base), b_desc0 = sw128_desc(st_base + S::A_BYTES);
             int st = 0, t = 0;
-            uint32_t ps = 0;
+            uint32_t ps = 0, ready = 0;  // ready: the result of the current stage's early test
             for (int unit = tile0; unit < units; unit += tstride, ++t) {
                 const int b = t & 1;
                 const int gb = (unit % ksplit) * gsplit, ge = min(G, gb + gsplit);
@@ -324,9 +352,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 tc_fence_after();
                 const uint32_t d = tmem_base + (uint32_t)(b * BN);
                 for (int g = gb; g < ge; ++g) {
-                    if (!mbar_spin(&full[st], ps, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_MMA)) goto mma_end;
+                    if (!ready && !mbar_spin(&full[st], ps, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_MMA)) goto mma_end;
                     tc_fence_after();
                     const uint64_t off = (uint64_t)((st * S::STAGE_BYTES) >> 4);
+                    if constexpr (!PAIR) {
+                        const int st2 = st + 1 == S::STAGES ? 0 : st + 1;
+                        const uint32_t ps2 = st + 1 == S::STAGES ? ps ^ 1u : ps;
+                        const uint64_t ad = a_desc0 + off, bd = b_desc0 + off;
+                        ready = umma4_f16_commit_test(d, ad, ad + 2, ad + 4, ad + 6, bd, bd + 2, bd + 4, bd + 6, IDESC,
+                                                      g != gb ? 1u : 0u, smem_u32(&empty[st]), smem_u32(&full[st2]), ps2);
+                        st = st2;
+                        ps = ps2;
+                        continue;
+                    }
+                    ready = 0;
 #pragma unroll
                     for (int kk = 0; kk < KS / 16; ++kk) {  // K = 16 per MMA: 32 bytes along the row
                         const uint64_t ad = a_desc0 + off + (uint64_t)(kk * 2), bd = b_desc0 + off + (uint64_t)(kk * 2);
@@ -710,6 +749,9 @@ int db_launch_gemm_dq(const DbGemmArgs& a, cudaStream_t stream) {
             rc = (int)cudaErrorInvalidValue;
     }
     // output tensor map for the TMA store / reduce-add (16-byte aligned rows; else plain stores)
+    // output tensor map for the TMA store / reduce-add (16-byte aligned rows; else plain stores;
+    // direct 16-byte stores from registers were measured slower for the store epilogue, 0.66 against
+    // 0.60 ms of qkv per C2 step)
     if (!rc && !swiglu && !split && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0 && (a.ldy & 3) == 0) {
         cuuint64_t dims[2] = {(cuuint64_t)a.N, (cuuint64_t)a.M};
         cuuint64_t strides[1] = {(cuuint64_t)a.ldy * 4};
