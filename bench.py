@@ -378,7 +378,7 @@ def shape_c4(db, local_rank, requests=4):
                       "8 x 3 logits out)"}
 
 
-def shape_c5(db, local_rank, requests=3):
+def shape_c5(db, local_rank, requests=3, dq=False):
     """BASELINE config 5 (shape): the Qwen3-4B-shaped decoder (36L, D=2560, 32q/8kv, FF 9728, Q4),
     requests of a 512-token prefix and 4 continuations of 32 tokens scored by log-probability
     (LM head over the 151,936-token vocabulary), through the public score_continuations; cold
@@ -386,6 +386,8 @@ def shape_c5(db, local_rank, requests=3):
     cfg = db.EncoderConfig(layers=36, hidden=2560, q_heads=32, kv_heads=8, head_dim=128, ffn=9728, vocab=151936,
                            weight_bits=4, max_sequence_tokens=1024, causal=True)
     model = db.Model.synthetic(cfg, seed=SEED, std=0.02, device=local_rank)
+    if dq:
+        model.set_code_layout(db.CODES_DQ)
     rng = np.random.default_rng(5)
     prefixes = rng.integers(0, cfg.vocab, (requests + 1, 512)).astype(np.int32)
     conts = rng.integers(0, cfg.vocab, (requests + 1, 4, 32)).astype(np.int32)
@@ -401,7 +403,7 @@ def shape_c5(db, local_rank, requests=3):
     hit = (time.perf_counter() - t0) / requests
     model.close()
     return {"ms_per_request": cold * 1e3, "ms_per_request_prefix_cached": hit * 1e3,
-            "tokens_per_s": (512 + 128) / cold,
+            "tokens_per_s": (512 + 128) / cold, "numerics": "dequantised" if dq else "exact",
             "timing": "host wall clock around the public call (ids in, 4 x 32 log-probs out)"}
 
 
@@ -425,7 +427,7 @@ def named_shapes(db, rank, world, local_rank, dq=False):
             run("c1_gemm_dequantised", lambda: shape_c1(db, layout=db.CODES_DQ))
         run("gemv_c5_layers", lambda: shape_gemv(db))
         run("c4_decima_encoder", lambda: shape_c4(db, local_rank))
-        run("c5_decoder_prefix", lambda: shape_c5(db, local_rank))
+        run("c5_decoder_prefix", lambda: shape_c5(db, local_rank, dq=dq))
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -682,6 +684,8 @@ def run_c5(args, local_rank):
     cfg = db.EncoderConfig(layers=36, hidden=2560, q_heads=32, kv_heads=8, head_dim=128, ffn=9728, vocab=151936,
                            weight_bits=4, max_sequence_tokens=1024, causal=True)
     model = db.Model.synthetic(cfg, seed=SEED, std=0.02, device=local_rank)
+    if args.numerics == "dq":
+        model.set_code_layout(db.CODES_DQ)
     rng = np.random.default_rng(5)
     n_req = max(args.steps, 1)
     prefixes = rng.integers(0, cfg.vocab, (n_req + args.warmup, 512)).astype(np.int32)

@@ -12,7 +12,8 @@ C4  the Decima-shaped encoder at its real width (hidden 768, 12 heads, FFN 3072,
     blocks of 32), 2 layers, one 384 + 32-token sequence: pooled cosine >= 0.9999.
 C5  the Qwen3-4B-shaped decoder at its real width (hidden 2560, 32q/8kv x 128, FFN 9728), 2
     layers, a 512-token prefix and 4 continuations of 32 tokens: per-token cosine >= 0.999 and
-    continuation-mean cosine >= 0.9999 against one causal oracle pass over prefix + continuation.
+    continuation-mean cosine >= 0.9999 against one causal oracle pass over prefix + continuation,
+    with the exact and with the dequantised projections.
 """
 import numpy as np
 import pytest
@@ -121,9 +122,12 @@ def test_c4_full_width_matches_oracle(db):
     model.close()
 
 
-def test_c5_full_width_continuations_match_causal_oracle(db, oracle):
+@pytest.mark.parametrize("numerics", ["exact", "dequantised"])
+def test_c5_full_width_continuations_match_causal_oracle(db, oracle, numerics):
     cfg = dict(layers=2, hidden=2560, q_heads=32, kv_heads=8, head_dim=128, ffn=9728, vocab=151936, weight_bits=4)
     model = db.Model.synthetic(db.EncoderConfig(**cfg, max_sequence_tokens=1024, causal=True), seed=5)
+    if numerics == "dequantised":
+        model.set_code_layout(db.CODES_DQ)
     D, F, L, Nq, Nk = 2560, 9728, 2, 4096, 1024
     shapes = {"q": (Nq, D), "k": (Nk, D), "v": (Nk, D), "o": (D, Nq), "gate": (F, D), "up": (F, D), "down": (D, F)}
     w = {"embedding": model.synthetic_weight("embedding")}
