@@ -51,7 +51,7 @@ namespace db {
 namespace gdq {
 
 constexpr int BM = 128;  // tile rows
-constexpr int KS = 64;   // k per pipeline stage (one scale group)
+constexpr int KS = 64;   // k per pipeline stage (one scale group): four K = 16 MMAs
 constexpr int EPI_WARP0 = 2;
 constexpr int EPI_WARPS = 8;
 constexpr int NUM_THREADS = 32 * (EPI_WARP0 + EPI_WARPS);  // 320
@@ -208,6 +208,33 @@ __device__ __forceinline__ uint32_t umma4_f16_commit_test(uint32_t d, uint64_t a
     return ok;
 }
 
+// The same for a CTA pair: four M = 256 MMAs, then one commit that arrives on the barrier at the
+// same offset in both CTAs of the pair (tcgen05.commit with a CTA mask; no TMA multicast).
+__device__ __forceinline__ uint32_t umma4_f16_pair_commit_test(uint32_t d, uint64_t a0, uint64_t a1, uint64_t a2,
+                                                              uint64_t a3, uint64_t b0, uint64_t b1, uint64_t b2,
+                                                              uint64_t b3, uint32_t idesc, uint32_t acc_first,
+                                                              uint32_t commit_bar, uint32_t test_bar,
+                                                              uint32_t test_parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p, t, q;\n\t.reg .b16 mask;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 q, [%13], %14;\n\t"
+        "setp.ne.b32 p, %11, 0;\n\t"
+        "setp.eq.u32 t, 0, 0;\n\t"
+        "mov.b16 mask, 3;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%1], %2, %6, %10, p;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%1], %3, %7, %10, t;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%1], %4, %8, %10, t;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%1], %5, %9, %10, t;\n\t"
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%12], mask;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(ok)
+        : "r"(d), "l"(a0), "l"(a1), "l"(a2), "l"(a3), "l"(b0), "l"(b1), "l"(b2), "l"(b3), "r"(idesc), "r"(acc_first),
+          "r"(commit_bar), "r"(test_bar), "r"(test_parity)
+        : "memory");
+    return ok;
+}
+
 __device__ __forceinline__ bool warp_wait_polite(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err,
                                                  int code) {
     int ok = 1;
@@ -262,7 +289,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (threadIdx.x == 0) {
         constexpr int NC = PAIR ? 2 : 1;
         for (int i = 0; i < S::STAGES; ++i) {
-            mbar_init(&full[i], NC);
+            mbar_init(&full[i], 1);  // the leader's arrive (pair: armed with both CTAs' bytes)
             mbar_init(&empty[i], 1);
         }
         for (int i = 0; i < 2; ++i) {
@@ -310,10 +337,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 for (int g = gb; g < ge; ++g) {
                     if (!mbar_spin_polite(&empty[st], ps ^ 1u, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_TMA)) goto drain;
                     uint8_t* sp = smem + S::OFF_STAGE + st * S::STAGE_BYTES;
-                    // full boxes are counted, also where they reach past M or N (zero fill); in pair
-                    // mode both CTAs' bytes count on the leader's barrier
+                    // full boxes are counted, also where they reach past M or N (zero fill).  Pair mode:
+                    // both CTAs' loads complete on the leader's barrier, which the leader alone arms
+                    // with both CTAs' bytes by a local arrive (an arrive of each CTA at cluster scope
+                    // cost ~1,000 cycles per stage in clock64 traces and paced the pair).  A peer's
+                    // bytes may land before the leader arms the phase: the phase still waits for the
+                    // leader's arrive, and the peer loads a stage only after the MMAs of its previous
+                    // use completed, so the bytes always belong to the current phase.
                     if (PAIR) {
-                        mbar_arrive_expect_tx_cluster(at_leader(&full[st]), S::STAGE_BYTES);
+                        if (leader) mbar_arrive_expect_tx(&full[st], 2 * S::STAGE_BYTES);
                         tma_load_2d_pair(sp, &tmA, at_leader(&full[st]), g * KS, m0);
                         tma_load_2d_pair(sp + S::A_BYTES, &tmW, at_leader(&full[st]), g * KS, n0);
                     } else {
@@ -355,31 +387,22 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     if (!ready && !mbar_spin(&full[st], ps, abort_flag, dev_error, DB_DEV_ERR_TIMEOUT_MMA)) goto mma_end;
                     tc_fence_after();
                     const uint64_t off = (uint64_t)((st * S::STAGE_BYTES) >> 4);
-                    if constexpr (!PAIR) {
-                        const int st2 = st + 1 == S::STAGES ? 0 : st + 1;
-                        const uint32_t ps2 = st + 1 == S::STAGES ? ps ^ 1u : ps;
-                        const uint64_t ad = a_desc0 + off, bd = b_desc0 + off;
+                    // the stage's four K = 16 MMAs (32 bytes along the row each; a unit's first MMA
+                    // starts from zero) and the commit that frees the stage (pair: in both CTAs),
+                    // with the next stage's test issued ahead of them
+                    const int st2 = st + 1 == S::STAGES ? 0 : st + 1;
+                    const uint32_t ps2 = st + 1 == S::STAGES ? ps ^ 1u : ps;
+                    const uint64_t ad = a_desc0 + off, bd = b_desc0 + off;
+                    if constexpr (PAIR)
+                        ready = umma4_f16_pair_commit_test(d, ad, ad + 2, ad + 4, ad + 6, bd, bd + 2, bd + 4, bd + 6,
+                                                           IDESC, g != gb ? 1u : 0u, smem_u32(&empty[st]),
+                                                           smem_u32(&full[st2]), ps2);
+                    else
                         ready = umma4_f16_commit_test(d, ad, ad + 2, ad + 4, ad + 6, bd, bd + 2, bd + 4, bd + 6, IDESC,
-                                                      g != gb ? 1u : 0u, smem_u32(&empty[st]), smem_u32(&full[st2]), ps2);
-                        st = st2;
-                        ps = ps2;
-                        continue;
-                    }
-                    ready = 0;
-#pragma unroll
-                    for (int kk = 0; kk < KS / 16; ++kk) {  // K = 16 per MMA: 32 bytes along the row
-                        const uint64_t ad = a_desc0 + off + (uint64_t)(kk * 2), bd = b_desc0 + off + (uint64_t)(kk * 2);
-                        const uint32_t acc_in = (g != gb || kk != 0) ? 1u : 0u;  // a unit starts from zero
-                        if (PAIR) umma_f16_pair(d, ad, bd, IDESC, acc_in);
-                        else umma_f16(d, ad, bd, IDESC, acc_in);
-                    }
-                    if (PAIR) {
-                        umma_commit_pair(smem_u32(&empty[st]));
-                        umma_commit_pair(at_peer(&empty[st]));
-                    } else {
-                        umma_commit(&empty[st]);
-                    }
-                    if (++st == S::STAGES) { st = 0; ps ^= 1u; }
+                                                      g != gb ? 1u : 0u, smem_u32(&empty[st]), smem_u32(&full[st2]),
+                                                      ps2);
+                    st = st2;
+                    ps = ps2;
                 }
                 if (PAIR) {
                     umma_commit_pair(smem_u32(&done[b]));
