@@ -208,29 +208,29 @@ __device__ __forceinline__ uint32_t umma4_f16_commit_test(uint32_t d, uint64_t a
     return ok;
 }
 
-// The same for a CTA pair: four M = 256 MMAs, then one commit that arrives on the barrier at the
-// same offset in both CTAs of the pair (tcgen05.commit with a CTA mask; no TMA multicast).
+// The same for a CTA pair: four M = 256 MMAs, then a commit to this CTA's barrier and one to the
+// peer CTA's barrier at the same offset (cluster address).
 __device__ __forceinline__ uint32_t umma4_f16_pair_commit_test(uint32_t d, uint64_t a0, uint64_t a1, uint64_t a2,
                                                               uint64_t a3, uint64_t b0, uint64_t b1, uint64_t b2,
                                                               uint64_t b3, uint32_t idesc, uint32_t acc_first,
                                                               uint32_t commit_bar, uint32_t test_bar,
-                                                              uint32_t test_parity) {
+                                                              uint32_t test_parity, uint32_t peer_commit_bar) {
     uint32_t ok;
     asm volatile(
-        "{\n\t.reg .pred p, t, q;\n\t.reg .b16 mask;\n\t"
+        "{\n\t.reg .pred p, t, q;\n\t"
         "mbarrier.test_wait.parity.shared::cta.b64 q, [%13], %14;\n\t"
         "setp.ne.b32 p, %11, 0;\n\t"
         "setp.eq.u32 t, 0, 0;\n\t"
-        "mov.b16 mask, 3;\n\t"
         "tcgen05.mma.cta_group::2.kind::f16 [%1], %2, %6, %10, p;\n\t"
         "tcgen05.mma.cta_group::2.kind::f16 [%1], %3, %7, %10, t;\n\t"
         "tcgen05.mma.cta_group::2.kind::f16 [%1], %4, %8, %10, t;\n\t"
         "tcgen05.mma.cta_group::2.kind::f16 [%1], %5, %9, %10, t;\n\t"
-        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%12], mask;\n\t"
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%12];\n\t"
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%15];\n\t"
         "selp.u32 %0, 1, 0, q;\n\t}"
         : "=r"(ok)
         : "r"(d), "l"(a0), "l"(a1), "l"(a2), "l"(a3), "l"(b0), "l"(b1), "l"(b2), "l"(b3), "r"(idesc), "r"(acc_first),
-          "r"(commit_bar), "r"(test_bar), "r"(test_parity)
+          "r"(commit_bar), "r"(test_bar), "r"(test_parity), "r"(peer_commit_bar)
         : "memory");
     return ok;
 }
@@ -396,7 +396,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     if constexpr (PAIR)
                         ready = umma4_f16_pair_commit_test(d, ad, ad + 2, ad + 4, ad + 6, bd, bd + 2, bd + 4, bd + 6,
                                                            IDESC, g != gb ? 1u : 0u, smem_u32(&empty[st]),
-                                                           smem_u32(&full[st2]), ps2);
+                                                           smem_u32(&full[st2]), ps2, at_peer(&empty[st]));
                     else
                         ready = umma4_f16_commit_test(d, ad, ad + 2, ad + 4, ad + 6, bd, bd + 2, bd + 4, bd + 6, IDESC,
                                                       g != gb ? 1u : 0u, smem_u32(&empty[st]), smem_u32(&full[st2]),
