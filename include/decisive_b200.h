@@ -122,10 +122,12 @@ int db_gemm_g64(const void *a_codes, int layout, int64_t lda, const float *sa, c
 /* Tile configuration of the tensor-core GEMM: the candidate space of the kernel-selection tuner
  * (checkpoint.rs:279-294, 428-563 select among kernel variants; a candidate is accepted only when
  * its output is bitwise equal to the baseline's).  Every configuration computes the same
- * per-group fold in the same order, so all are bitwise equal by construction.
- *   block_n    output columns per tile: 0 (default: 128 for DB_CODES_TC, 256 for DB_CODES_NATURAL),
- *              64, 128 or 256, or 32 on DB_CODES_NATURAL (single CTAs; store and residual epilogues:
- *              small M) (the SwiGLU epilogue takes 128 or 256)
+ * per-group fold in the same order (DB_CODES_DQ: the same MMAs over the same K steps), so all are
+ * bitwise equal by construction.
+ *   block_n    output columns per tile: 0 (default: 128 for DB_CODES_TC, 256 for DB_CODES_NATURAL,
+ *              for DB_CODES_DQ the widest tile giving >= 96 tiles), 64, 128 or 256, or 32 on
+ *              DB_CODES_NATURAL (single CTAs; store and residual epilogues: small M) (the SwiGLU
+ *              epilogue takes 128 or 256)
  *   max_ctas   persistent grid cap: 0 = one CTA per SM
  *   pair_ctas  1 = clusters of two CTAs issue M = 256 MMAs (M > 128; DB_CODES_TC: 128-wide tiles
  *              only); 0 = off
