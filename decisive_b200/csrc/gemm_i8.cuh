@@ -294,7 +294,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (threadIdx.x == 0) {
         constexpr int NC = PAIR ? 2 : 1;
         for (int i = 0; i < S::STAGES; ++i) {
-            mbar_init(&full[i], NC);
+            mbar_init(&full[i], 1);  // the leader's arrive (pair: armed with both CTAs' bytes)
             mbar_init(&empty[i], 1);
             mbar_init(&wfull[i], 1);
             mbar_init(&cbf[i], NC * CONV_WARPS);
@@ -354,7 +354,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         // full boxes are counted, also where they reach past K or M (zero fill)
                         constexpr uint32_t TX = S::A_BYTES + (BITS == 8 ? S::B_BYTES : 0);
                         if (PAIR) {
-                            mbar_arrive_expect_tx_cluster(at_leader(&full[st]), TX);
+                            // both CTAs' loads complete on the leader's barrier, which the leader
+                            // alone arms with both CTAs' bytes by a local arrive (in the dequantised
+                            // GEMM's pairs a cluster-scope arrive from each CTA measured ~1,000
+                            // cycles per stage); a peer's bytes may land first, but the phase waits
+                            // for the leader's arrive and a stage is reloaded only after its
+                            // previous MMAs completed
+                            if (leader) mbar_arrive_expect_tx(&full[st], 2 * TX);
                             tma_load_2d_pair(sp, &tmA, at_leader(&full[st]), s * KS, m0);
                             if (BITS == 8) tma_load_2d_pair(sp + S::A_BYTES, &tmW, at_leader(&full[st]), s * KS, n0);
                         } else {
