@@ -489,7 +489,8 @@ int enqueue_forward(db_model* m, int T, const volatile uint8_t* cancel, const Pa
                                                         c.q_heads, c.kv_heads, attn_scale,
                                                         m->acodes, ld_codes, m->sa, lds, m->flag, st, attn_codes);
             });
-        if (!rc && m->dq) {
+        // (a split needs at least two 64-groups of K)
+        if (!rc && m->dq && Nq >= 128) {
             rc = timed(6, [&] { return gemm(1, m->acodes, w.o_c, w.o_s, m->sa, D, Nq, DB_EPI_STORE, m->dq_part, D, 2); });
             pend = m->dq_part;
         } else if (!rc) {
@@ -519,7 +520,7 @@ int enqueue_forward(db_model* m, int T, const volatile uint8_t* cancel, const Pa
             g.epilogue = DB_EPI_RESIDUAL;
             g.y = m->x;
             g.ldy = D;
-            if (m->dq) {
+            if (m->dq && F >= 128) {
                 g.epilogue = DB_EPI_STORE;  // two K-half partial sums, added by the next RMSNorm
                 g.y = m->dq_part;
                 g.k_splits = 2;
@@ -528,7 +529,7 @@ int enqueue_forward(db_model* m, int T, const volatile uint8_t* cancel, const Pa
             g.dev_error = m->dev_err;
             return launch(3, g);
         });
-        if (!rc && m->dq) pend = m->dq_part;
+        if (!rc && m->dq && F >= 128) pend = m->dq_part;
         if (m->streaming) {
             cudaEventRecord(m->consumed[l & 1], st);
             if (l + 2 < c.layers) upload(l + 2);
