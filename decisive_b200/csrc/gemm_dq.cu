@@ -27,13 +27,17 @@
 //                 (BN x 64 f16), both with the 128-byte swizzle (UMMA K-major operands as-is)
 //     warp 1      TMEM owner + MMA issuer (lane 0): four K = 16 MMAs per stage into the tile's
 //                 accumulator (two buffers of BN columns, alternating by tile, so a tile's epilogue
-//                 overlaps the next tile's MMAs); one commit per stage frees the stage, one per
-//                 tile hands the accumulator to the epilogue
+//                 overlaps the next tile's MMAs), issued in one asm block with the stage's commit and
+//                 the next stage's barrier test; one commit per tile hands the accumulator to the
+//                 epilogue
 //     warps 2-9   epilogue, two warps per TMEM lane quadrant: warp w reads lanes 32 (w % 4).. and
 //                 half of the tile's columns, 32 at a time, and hands them to the TMA through shared
 //                 memory (store, or reduce-add into y), or stores them itself where y's rows are not
 //                 16-byte aligned; or (gate/up) the SwiGLU + re-quantisation of whole 64 + 64 column
 //                 blocks into f16(code * scale), one block per warp
+// Work units are tiles, or with k_splits = 2 (store epilogue) the two halves of each tile's K range,
+// each storing its partial sum to its own [M, N] buffer; the model's RMSNorm adds them to the
+// residual stream in a fixed order (deterministic, independent of the tiling).
 // Every mbarrier wait is bounded (DB_WAIT_LIMIT_NS); on expiry the CTA records an error in the
 // device error word, stops issuing work, lets its own copies and MMAs land and frees its tensor
 // memory.  No TMA multicast.
