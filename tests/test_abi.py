@@ -55,6 +55,21 @@ def test_abi_version_and_argument_validation_without_gpu(lib):
     assert rc == -5 and lib.db_last_error_code().decode() == "UNSUPPORTED"
 
 
+def test_code_layout_constants_match_the_header(lib):
+    """The activation layouts the header defines (DB_CODES_*) are the binding's constants; a layout
+    past the last one is refused on the host."""
+    import decisive_b200 as db
+    text = open(HEADER).read()
+    defined = {k: int(v) for k, v in re.findall(r"#define DB_CODES_([A-Z]+) (\d+)", text)}
+    assert defined == {"NATURAL": db.CODES_NATURAL, "GEMV": db.CODES_GEMV, "TC": db.CODES_TC, "DQ": db.CODES_DQ}
+    rc = lib.db_quantize_activations_g64(None, 0, 64, 1, 64, 8, None, max(defined.values()) + 1, 64, None, None, 128,
+                                         None, None)
+    assert rc == -1 and lib.db_last_error_code().decode() == "INVALID_ARGUMENT"
+    # the dequantised GEMM validates its shape before any device work as well
+    rc = lib.db_gemm_g64(None, db.CODES_DQ, 64, None, None, 0, None, None, 1, 0, 64, 4, 1, 0, None, 0, None, None)
+    assert rc == -1
+
+
 def test_model_creation_without_device_reports_gpu_unavailable(lib):
     import decisive_b200 as db
     if lib.db_device_count() > 0:
